@@ -1,0 +1,431 @@
+"""Generate golden vectors by running the pbg reference on CPU.
+
+Usage::
+
+    python tests/golden/make_golden.py --reference <pbg checkout> [--out tests/golden]
+
+The reference (pbustillo05/ai-game-learning) is GPU-only by design: its state
+containers refuse non-accelerator tensors.  The pure functions below those
+checks are device-agnostic torch, so this script installs three test-only
+shims before calling them:
+
+* ``PokerState.validate`` keeps the reference's shape/dtype/range and chip
+  conservation checks but accepts CPU tensors (hooks.py:268-326);
+* ``PokerLegality.__post_init__`` keeps the legality checks without the
+  device test (policy.py:34-52);
+* ``PokerStateMachine.initial_roots`` is re-compiled from the reference's own
+  source with only its device-type guard removed (hooks.py:369-371).
+
+Everything else runs unmodified.  The fixtures are small ``.npz`` files that
+the ``-m "not gpu"`` tests use to pin the oracle and the ``-m gpu`` tests use
+to pin the CUDA library.
+"""
+
+from __future__ import annotations
+
+import argparse
+import inspect
+import math
+import os
+import sys
+import textwrap
+from types import MappingProxyType
+
+import numpy as np
+
+
+def _install_shims():
+    import torch
+    from pbg.games.poker.queued import hooks, policy
+
+    def validate(self, geometry):  # hooks.py:268-326 without the device test
+        batch, players = self.rows, geometry.players
+        expect = {
+            "board_cards": (torch.uint8, (batch, 5)), "combo_ids": (torch.int32, (batch, players)),
+            "button": (torch.int32, (batch,)), "street": (torch.int32, (batch,)),
+            "to_act": (torch.int32, (batch,)), "stacks": (torch.float32, (batch, players)),
+            "committed": (torch.float32, (batch, players)),
+            "committed_street": (torch.float32, (batch, players)),
+            "status": (torch.int8, (batch, players)), "current_bet": (torch.float32, (batch,)),
+            "last_full_raise": (torch.float32, (batch,)), "pending": (torch.bool, (batch, players)),
+            "can_raise": (torch.bool, (batch, players)), "terminal": (torch.bool, (batch,)),
+        }
+        for name, (dtype, shape) in expect.items():
+            value = getattr(self, name)
+            assert value.dtype == dtype and tuple(value.shape) == shape, name
+        assert bool((self.stacks >= 0).all())
+        total = (self.stacks + self.committed).sum(-1)
+        assert bool(((total - players * geometry.stack_bb).abs() <= 1e-5).all())
+
+    hooks.PokerState.validate = validate
+
+    def legality_post_init(self):  # policy.py:34-52 without the device test
+        assert self.event_ids.ndim == 2 and self.mask.shape == self.event_ids.shape
+        assert bool(self.mask.any(-1).all())
+
+    policy.PokerLegality.__post_init__ = legality_post_init
+
+    source = textwrap.dedent(inspect.getsource(hooks.PokerStateMachine.initial_roots))
+    guard = 'if device.type not in ("cuda", "mps"):'
+    assert guard in source, "reference initial_roots changed shape"
+    source = source.replace(guard, "if False:")
+    namespace: dict = {}
+    exec(compile(source, hooks.__file__, "exec"), hooks.__dict__, namespace)
+    hooks.PokerStateMachine.initial_roots = namespace["initial_roots"]
+
+
+STATE_FIELDS = ("board_cards", "combo_ids", "button", "street", "to_act", "stacks", "committed",
+                "committed_street", "status", "current_bet", "last_full_raise", "pending",
+                "can_raise", "terminal")
+HISTORY_FIELDS = ("actor", "street", "action", "amount", "pot_before", "call_amount",
+                  "current_bet", "min_raise_to", "max_raise_to", "mask")
+
+GEOMETRIES = [(2, 8.0, 4), (3, 8.0, 4), (6, 8.0, 13), (2, 100.0, 13), (6, 100.0, 13),
+              (6, 50.0, 13), (4, 20.5, 9)]
+
+
+def _np(t):
+    return t.detach().cpu().numpy().copy()
+
+
+def gen_rng(out):
+    import torch
+    from pbg.core.rollout import (DrawPurpose, child_path_keys, logical_categorical,
+                                  logical_rng_keys, logical_uniform)
+
+    rng = np.random.default_rng(20261201)
+    n = 64
+    cases = []
+    for case in range(24):
+        seed = int(rng.integers(-2**40, 2**62)) if case % 3 else case
+        iteration = int(rng.integers(0, 2**20))
+        purpose = int(1 + case % 8)
+        root = rng.integers(0, 2**62, n) if case % 2 else rng.integers(0, 4096, n)
+        path = np.where(rng.random(n) < 0.3, 0, rng.integers(-2**63, 2**63 - 1, n, dtype=np.int64))
+        draw = rng.integers(0, 4096, n)
+        lane = rng.integers(0, 8, n)
+        epoch = rng.integers(0, 4, n)
+        active = rng.random(n) < 0.8
+        keys = logical_rng_keys(seed=seed, iteration=iteration, root=torch.from_numpy(root),
+                                path=torch.from_numpy(path), draw=torch.from_numpy(draw),
+                                purpose=purpose, lane=torch.from_numpy(lane),
+                                retry_epoch=torch.from_numpy(epoch),
+                                active=torch.from_numpy(active))
+        cases.append((seed, iteration, purpose, root, path, draw, lane, epoch, active, _np(keys)))
+    out["rng_scalars"] = np.array([[c[0], c[1], c[2]] for c in cases], dtype=np.int64)
+    for i, name in enumerate(("root", "path", "draw", "lane", "epoch")):
+        out[f"rng_{name}"] = np.stack([c[3 + i] for c in cases]).astype(np.int64)
+    out["rng_active"] = np.stack([c[8] for c in cases]).astype(np.uint8)
+    out["rng_keys"] = np.stack([c[9] for c in cases])
+    ords = rng.integers(1, 1 << 20, (24, n))
+    out["rng_child_ordinal"] = ords.astype(np.int64)
+    out["rng_child"] = np.stack([
+        _np(child_path_keys(torch.from_numpy(out["rng_path"][i]), torch.from_numpy(ords[i])))
+        for i in range(24)])
+    flat = out["rng_keys"].reshape(-1)
+    extra = np.array([0, ((1 << 24) - 1) << 39, (1 << 39) - 1, 1 << 39, 2**63 - 1], dtype=np.int64)
+    ukeys = np.concatenate([flat, extra])
+    out["rng_uniform_keys"] = ukeys
+    out["rng_uniform"] = _np(logical_uniform(torch.from_numpy(ukeys)))
+    probs = rng.random((256, 12)).astype(np.float32) * (rng.random((256, 12)) < 0.6)
+    probs[:, 3] += 1e-3
+    probs = probs / probs.sum(1, keepdims=True)
+    ckeys = flat[:256]
+    out["cat_prob"] = probs.astype(np.float32)
+    out["cat_keys"] = ckeys
+    out["cat_selected"] = _np(logical_categorical(torch.from_numpy(probs.astype(np.float32)),
+                                                  torch.from_numpy(ckeys)))
+    assert DrawPurpose.ACTION == 4
+
+
+def _state_np(state):
+    return {name: _np(getattr(state, name)) for name in STATE_FIELDS}
+
+
+def _state_from(cols, rows=None):
+    import torch
+    from pbg.games.poker.queued.hooks import PokerState
+    sel = (lambda v: v) if rows is None else (lambda v: v[rows])
+    return PokerState(*(torch.from_numpy(np.ascontiguousarray(sel(cols[n]))) for n in STATE_FIELDS))
+
+
+def gen_poker(out):
+    import torch
+    from pbg.core.rollout import child_path_keys
+    from pbg.games.poker.queued.hooks import NLHEGeometry, PokerHistory, PokerStateMachine
+
+    rng = np.random.default_rng(7)
+    for gi, (players, stack, ranks) in enumerate(GEOMETRIES):
+        geometry = NLHEGeometry(players, stack, ranks)
+        machine = PokerStateMachine(geometry)
+        tag = f"g{gi}"
+        # roots: two calls with distinct addresses
+        seed, iteration, retry, base, lane = 1000 + gi, 3 + gi, gi % 3, 17 * gi, gi % 2
+        B = 16 if players == 6 and stack >= 50 else 24
+        state = machine.initial_roots(B, seed=seed, iteration=iteration, retry_epoch=retry,
+                                      logical_base=base, lane=lane, device="cpu")
+        out[f"{tag}_geometry"] = np.array([players, stack, ranks], dtype=np.float64)
+        out[f"{tag}_root_args"] = np.array([seed, iteration, retry, base, lane, B], dtype=np.int64)
+        for k, v in _state_np(state).items():
+            out[f"{tag}_root_{k}"] = v
+        # trajectory with random legal actions and keyed chance at (root, path)
+        cols = _state_np(state)
+        history = machine.empty_history(B, torch.device("cpu"))
+        hist = {n: _np(getattr(history, n)) for n in HISTORY_FIELDS}
+        path = np.zeros(B, dtype=np.int64)
+        root = np.arange(base, base + B, dtype=np.int64)
+        actions, masks, posts = [], [], []
+        step = 0
+        while not cols["terminal"].all():
+            active = ~cols["terminal"]
+            rows = np.nonzero(active)[0]
+            sub = _state_from(cols, rows)
+            legality = machine.legality(sub)
+            mask = _np(legality.mask)
+            chosen = np.full(B, -1, dtype=np.int32)
+            for i, r in enumerate(rows):
+                legal = np.nonzero(mask[i])[0]
+                u = rng.random()
+                if u < 0.15 and mask[i, 0]:
+                    pick = 0
+                elif u < 0.55:
+                    pick = 1
+                else:
+                    raises = legal[legal >= 2]
+                    pick = int(rng.choice(raises)) if raises.size else 1
+                chosen[r] = pick
+            full_mask = np.zeros((B, geometry.stack_ticks + 2), dtype=bool)
+            full_mask[rows] = mask
+            action = torch.from_numpy(chosen[rows])
+            sub_hist = PokerHistory(*(torch.from_numpy(np.ascontiguousarray(hist[n][rows])) for n in HISTORY_FIELDS))
+            sub_hist = machine.append_player_history(sub, action, sub_hist)
+            nxt = machine.step_player(sub, action)
+            sub_root = torch.from_numpy(root[rows])
+            sub_path = torch.from_numpy(path[rows])
+            for generation in range(3):
+                chance_active = machine.needs_chance(nxt)
+                sub_hist = machine.append_chance_history(nxt, chance_active, sub_hist)
+                nxt = machine.deal_next_street_keyed(nxt, seed=seed, iteration=iteration, root=sub_root,
+                                                     path=sub_path, draw=generation,
+                                                     retry_epoch=retry, lane=lane)
+            new = _state_np(nxt)
+            for n in STATE_FIELDS:
+                cols[n][rows] = new[n]
+            for n in HISTORY_FIELDS:
+                hist[n][rows] = _np(getattr(sub_hist, n))
+            path[rows] = _np(child_path_keys(sub_path, 1))
+            actions.append(chosen)
+            masks.append(full_mask)
+            posts.append({n: cols[n].copy() for n in STATE_FIELDS})
+            step += 1
+            assert step < 400
+        out[f"{tag}_actions"] = np.stack(actions)
+        out[f"{tag}_masks"] = np.packbits(np.stack(masks), axis=-1)
+        out[f"{tag}_mask_events"] = np.array([geometry.stack_ticks + 2])
+        for n in STATE_FIELDS:
+            out[f"{tag}_post_{n}"] = np.stack([p[n] for p in posts])
+        for n in HISTORY_FIELDS:
+            out[f"{tag}_history_{n}"] = hist[n].astype(np.float32 if hist[n].dtype.kind == "f" else np.int16)
+        out[f"{tag}_final_path"] = path
+        leaf = machine.sampled_leaf(_state_from(cols))
+        for k, v in leaf.items():
+            out[f"{tag}_leaf_{k}"] = _np(v)
+        out[f"{tag}_combo_class"] = _np(machine._combo_class(torch.device("cpu"))).astype(np.int32)
+
+
+def gen_known_answers(out):
+    """Literal expected states from the reference's own tests, re-derived."""
+
+    import torch
+    from pbg.games.poker.queued.hooks import NLHEGeometry, PokerStateMachine
+
+    machine = PokerStateMachine(NLHEGeometry(3, 8.0, 4))
+    state = machine.initial_roots(1, seed=71, iteration=0, retry_epoch=0, device="cpu")
+    for a in (13, 1, 17):
+        state = machine.step_player(state, torch.tensor([a], dtype=torch.int32))
+    out["ka_repend_committed_street"] = _np(state.committed_street)
+    out["ka_repend_pending"] = _np(state.pending)
+    out["ka_repend_can_raise"] = _np(state.can_raise)
+    out["ka_repend_to_act"] = _np(state.to_act)
+    out["ka_repend_mask"] = _np(machine.legality(state).mask)
+
+
+def _raw(rng, batch, hands, mixture):
+    import torch
+    g = torch.Generator().manual_seed(int(rng.integers(0, 2**31)))
+    return {
+        "type_logits": torch.randn(batch, hands, 3, generator=g) * 1.5,
+        "omega": torch.softmax(torch.randn(batch, hands, mixture, generator=g), -1),
+        "mu": torch.sigmoid(torch.randn(batch, hands, mixture, generator=g)),
+        "s": torch.nn.functional.softplus(torch.randn(batch, hands, mixture, generator=g)) + 0.02,
+        "iota": torch.sigmoid(torch.randn(batch, hands, generator=g)),
+    }
+
+
+def gen_policy(out, poker):
+    import torch
+    from pbg.games.poker.queued.policy import PokerLegality, PokerPolicyOperator
+
+    rng = np.random.default_rng(11)
+    op = PokerPolicyOperator()
+    cases = [("small", 0, 10, 3, 5), ("hu8", 0, 18, 2, 4), ("hu100", 3, 202, 2, 3), ("six50", 5, 102, 2, 3)]
+    for name, gi, E, M, H in cases:
+        if name == "small":
+            B = 6
+            mask = rng.random((B, E)) < 0.6
+            mask[:, 1] = True
+            mask[1] = False
+            mask[1, 1] = True
+        else:
+            packed = poker[f"g{gi}_masks"]
+            masks = np.unpackbits(packed, axis=-1)[..., :E].astype(bool).reshape(-1, E)
+            masks = masks[masks.any(1)]
+            B = min(48, masks.shape[0])
+            mask = masks[rng.choice(masks.shape[0], B, replace=False)]
+        raw = _raw(rng, B, H, M)
+        ids = torch.arange(E, dtype=torch.int32)[None].expand(B, -1).contiguous()
+        legality = PokerLegality(ids, torch.from_numpy(mask))
+        prob = op.probabilities(raw, legality)
+        out[f"pol_{name}_mask"] = mask.astype(np.uint8)
+        for k, v in raw.items():
+            out[f"pol_{name}_{k}"] = _np(v)
+        out[f"pol_{name}_prob"] = _np(prob)
+        hand = torch.from_numpy(rng.integers(0, H, B).astype(np.int32))
+        keys = torch.from_numpy(rng.integers(0, 2**63 - 1, B, dtype=np.int64))
+        sample = op.sample_actor(raw, legality, hand, keys)
+        out[f"pol_{name}_hand"] = _np(hand)
+        out[f"pol_{name}_keys"] = _np(keys)
+        out[f"pol_{name}_action"] = _np(sample.action)
+        out[f"pol_{name}_selected"] = _np(sample.selected_log_policy)
+        out[f"pol_{name}_selected_all"] = _np(op.selected_log_pi(raw, legality, sample.action))
+        entropy, kl = op.policy_reductions(raw, legality, None)
+        out[f"pol_{name}_entropy"] = _np(entropy)
+
+
+def gen_loss(out):
+    import torch
+    from pbg.config import EntropyLossConfig, LossConfig, ValueLossConfig
+    from pbg.core.contracts import mode_schema
+    from pbg.core.learner import LearnerOperation, ModelEvaluation, PolicyEvaluation, SequentialLearnerBatch
+
+    from categorical_policy_fixture import CategoricalPolicyAdapter, PolicyOutput
+
+    adapter = CategoricalPolicyAdapter()
+    ids = torch.arange(8)[None]
+    rng = np.random.default_rng(5)
+    N, A = 160, 8
+    logits = rng.standard_normal((N, A)).astype(np.float32)
+    mask = rng.random((N, A)) < 0.7
+    empty = ~mask.any(1)
+    mask[empty, 0] = True
+    action = np.array([rng.choice(np.nonzero(m)[0]) for m in mask], dtype=np.int32)
+    # old log pi: perturbed logits; spread wide enough that some rows clip
+    pert = logits + rng.standard_normal((N, A)).astype(np.float32) * np.float32(0.1)
+    pert[: N // 4] += rng.standard_normal((N // 4, A)).astype(np.float32) * np.float32(1.5)
+    masked = np.where(mask, pert, -np.inf)
+    lse = np.log(np.exp(masked - masked.max(1, keepdims=True)).sum(1)) + masked.max(1)
+    old = (masked[np.arange(N), action] - lse).astype(np.float32)
+    adv = rng.standard_normal(N).astype(np.float32)
+    weight = rng.uniform(0.05, 1.0, N).astype(np.float32)
+    caps = [None, 1.5]
+    for ci, cap in enumerate(caps):
+        per_total = np.zeros(N, dtype=np.float64)
+        grads = np.zeros((N, A), dtype=np.float32)
+        cfg = LossConfig(policy_clip=0.2, negative_advantage_ratio_cap=cap,
+                         value=ValueLossConfig(coefficient=0.0),
+                         entropy=EntropyLossConfig(coefficient=0.01))
+        for r in range(N):
+            x = torch.tensor(logits[r : r + 1], requires_grad=True)
+            mrow = torch.from_numpy(mask[r : r + 1])
+
+            def model(input_type, model_input, private, owner, x=x):
+                return ModelEvaluation({"logits": x[:, None, :]}, torch.zeros(1, 1))
+
+            def policy(name, mi, raw, act, private, owner, ref, mrow=mrow):
+                # the reference's game-neutral categorical fixture
+                # (tests/categorical_policy_fixture.py:19-57)
+                pout = PolicyOutput(raw["logits"].reshape(1, 1, A).float(), None)
+                sel = adapter.log_prob(pout, act.long(), ids, mrow).reshape(1)
+                ent = adapter.entropy(pout, ids, mrow).reshape(1)
+                return PolicyEvaluation(sel, ent, torch.zeros_like(sel))
+
+            fields = MappingProxyType({
+                "model_input": torch.zeros(1, 1), "owner": torch.zeros(1, dtype=torch.int32),
+                "sampled_private_state": torch.zeros(1, 2, dtype=torch.int32),
+                "action": torch.tensor(action[r : r + 1]),
+                "old_log_policy": torch.tensor(old[r : r + 1, None]),
+                "old_value": torch.zeros(1, 1), "value_target": torch.zeros(1, 1),
+                "advantage_target": torch.tensor(adv[r : r + 1, None]),
+            })
+            op = LearnerOperation(mode_schema("self_play", "sequential", "sampled"), cfg, model, policy)
+            res = op.forward_loss_backward(SequentialLearnerBatch("pre", torch.zeros(1, dtype=torch.int64), fields),
+                                           iteration=0, objective_weight=float(weight[r]))
+            per_total[r] = float(res.total)
+            grads[r] = _np(x.grad)[0]
+        out[f"loss{ci}_row_total"] = per_total
+        out[f"loss{ci}_grad"] = grads
+        out[f"loss{ci}_cap"] = np.array([np.inf if cap is None else math.log(cap)], dtype=np.float64)
+    out["loss_logits"] = logits
+    out["loss_mask"] = mask.astype(np.uint8)
+    out["loss_action"] = action
+    out["loss_old"] = old
+    out["loss_adv"] = adv
+    out["loss_weight"] = weight
+
+
+def gen_adam(out):
+    import torch
+    from pbg.core.optimization import adam_transition
+
+    rng = np.random.default_rng(3)
+    n = 4096
+    master = torch.from_numpy(rng.standard_normal((1, n)).astype(np.float32))
+    first = torch.zeros(1, n)
+    second = torch.zeros(1, n)
+    controls = torch.tensor([[1e-3, 0.9, 0.999, 1e-8, 0.01, 1.0, 128.0, 2.0, 0.5, 2000.0]])
+    steps = torch.zeros(1, dtype=torch.int64)
+    trackers = torch.zeros(1, dtype=torch.int64)
+    out["adam_master0"] = _np(master).copy()
+    out["adam_controls"] = _np(controls).copy()
+    grads_in, masters, firsts, seconds, grads_out = [], [], [], [], []
+    for s in range(3):
+        g = torch.from_numpy((rng.standard_normal((1, n)) * (0.05 if s != 1 else 3.0) * 128.0).astype(np.float32))
+        grads_in.append(_np(g).copy())
+        adam_transition(master, g, first, second, controls, steps, trackers,
+                        torch.tensor([False]), torch.tensor([True]), torch.tensor([True]), torch.tensor([False]))
+        masters.append(_np(master).copy())
+        firsts.append(_np(first).copy())
+        seconds.append(_np(second).copy())
+        grads_out.append(_np(g).copy())
+    out["adam_grad_in"] = np.stack(grads_in)
+    out["adam_master"] = np.stack(masters)
+    out["adam_first"] = np.stack(firsts)
+    out["adam_second"] = np.stack(seconds)
+    out["adam_grad_out"] = np.stack(grads_out)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", required=True, help="root of a pbg checkout")
+    parser.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    args = parser.parse_args()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    sys.path.insert(0, os.path.join(os.path.abspath(args.reference), "tests"))
+    import torch
+    torch.manual_seed(0)
+    _install_shims()
+    rng_out, poker_out, policy_out, loss_out, adam_out, ka_out = {}, {}, {}, {}, {}, {}
+    gen_rng(rng_out)
+    gen_poker(poker_out)
+    gen_known_answers(ka_out)
+    gen_policy(policy_out, poker_out)
+    gen_loss(loss_out)
+    gen_adam(adam_out)
+    for name, data in (("rng", rng_out), ("poker", poker_out), ("known_answers", ka_out),
+                       ("policy", policy_out), ("loss", loss_out), ("adam", adam_out)):
+        np.savez_compressed(os.path.join(args.out, f"{name}.npz"), **data)
+        print(name, len(data), os.path.getsize(os.path.join(args.out, f"{name}.npz")))
+
+
+if __name__ == "__main__":
+    main()
