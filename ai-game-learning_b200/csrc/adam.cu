@@ -1,0 +1,140 @@
+// Fused flat-buffer Adam/AdamW step for one optimizer lane.
+//
+// Restates pbg/core/optimization.py:182-233 (adam_transition) for K = 1:
+// unscale by the loss scale, global 2-norm and finiteness, norm clipping,
+// coupled or decoupled weight decay, bias-corrected moments, and the
+// all-or-nothing rule (a non-finite gradient leaves masters and moments
+// untouched and zeroes the gradient rows).  Three stream-ordered launches:
+// per-block sum of squares -> one-block finalise of the scalars -> apply.
+// The dynamic fp16 loss-scale update (growth/backoff trackers) is not part
+// of this step: the scale is read from controls[6] as given.
+#include "pbg_common.cuh"
+
+namespace pbg {
+
+constexpr int ADAM_BLOCK = 256;
+
+__global__ void __launch_bounds__(ADAM_BLOCK) adam_norm_kernel(int64_t n, const float4* __restrict__ grad4,
+                                                                const float* __restrict__ grad,
+                                                                const float* controls, double* partials) {
+    float inv_scale = 1.0f / controls[6];
+    float ss = 0.0f;
+    float bad = 0.0f;
+    int64_t n4 = n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n4; i += (int64_t)gridDim.x * ADAM_BLOCK) {
+        float4 g = __ldcs(grad4 + i);
+        float a = g.x * inv_scale, b = g.y * inv_scale, c = g.z * inv_scale, d = g.w * inv_scale;
+        ss += a * a + b * b + c * c + d * d;
+        bad += (isfinite(a) && isfinite(b) && isfinite(c) && isfinite(d)) ? 0.0f : 1.0f;
+    }
+    for (int64_t i = 4 * n4 + (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n; i += (int64_t)gridDim.x * ADAM_BLOCK) {
+        float a = grad[i] * inv_scale;
+        ss += a * a;
+        bad += isfinite(a) ? 0.0f : 1.0f;
+    }
+    __shared__ float red[2][ADAM_BLOCK / 32];
+    float s1 = warp_sum(ss), s2 = warp_sum(bad);
+    if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = s1; red[1][threadIdx.x >> 5] = s2; }
+    __syncthreads();
+    if (threadIdx.x < 2) {
+        double acc = 0.0;
+        for (int w = 0; w < ADAM_BLOCK / 32; ++w) acc += (double)red[threadIdx.x][w];
+        partials[2 * (int64_t)blockIdx.x + threadIdx.x] = acc;
+    }
+}
+
+// report: [applied, finite, norm, clip_scale, step_after, c1, c2, unused]
+__global__ void adam_finalize_kernel(int blocks, const double* partials, const float* controls, int64_t* step,
+                                     double* report) {
+    __shared__ double red[2][ADAM_BLOCK];
+    double ss = 0.0, bad = 0.0;
+    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
+        ss += partials[2 * (int64_t)b];
+        bad += partials[2 * (int64_t)b + 1];
+    }
+    red[0][threadIdx.x] = ss;
+    red[1][threadIdx.x] = bad;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+        if (threadIdx.x < o) {
+            red[0][threadIdx.x] += red[0][threadIdx.x + o];
+            red[1][threadIdx.x] += red[1][threadIdx.x + o];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        double norm = sqrt(red[0][0]);
+        bool finite = red[1][0] == 0.0 && isfinite(norm);
+        double clip = controls[5];
+        double scale = fmin(clip / fmax(norm, 1.0e-12), 1.0);
+        if (!finite) scale = 0.0;
+        int64_t t = step[0] + (finite ? 1 : 0);
+        double b1 = controls[1], b2 = controls[2];
+        report[0] = finite ? 1.0 : 0.0;
+        report[1] = finite ? 1.0 : 0.0;
+        report[2] = finite ? norm : INFINITY;
+        report[3] = scale;
+        report[4] = (double)t;
+        report[5] = fmax(1.0 - pow(b1, (double)t), 1.0e-30);
+        report[6] = fmax(1.0 - pow(b2, (double)t), 1.0e-30);
+        report[7] = 0.0;
+        step[0] = t;
+    }
+}
+
+__global__ void __launch_bounds__(ADAM_BLOCK) adam_apply_kernel(int64_t n, float* __restrict__ master,
+                                                                 float* __restrict__ grad, float* __restrict__ first,
+                                                                 float* __restrict__ second, const float* controls,
+                                                                 int decoupled, const double* report) {
+    bool applied = report[0] != 0.0;
+    float lr = controls[0], b1 = controls[1], b2 = controls[2], eps = controls[3], decay = controls[4];
+    float inv_scale = 1.0f / controls[6];
+    float clipping = (float)report[3];
+    float coupled = decoupled ? 0.0f : decay;
+    float inv_c1 = (float)(1.0 / report[5]);
+    float inv_sqrt_c2 = (float)(1.0 / sqrt(report[6]));
+    float shrink = 1.0f - lr * (decoupled ? decay : 0.0f);
+    for (int64_t i = (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n; i += (int64_t)gridDim.x * ADAM_BLOCK) {
+        if (!applied) { grad[i] = 0.0f; continue; }
+        float w = master[i];
+        float g = grad[i] * inv_scale * clipping + coupled * w;
+        float m = b1 * first[i] + (1.0f - b1) * g;
+        float v = b2 * second[i] + (1.0f - b2) * g * g;
+        float den = sqrtf(v) * inv_sqrt_c2 + eps;
+        float dir = m * inv_c1 / den;
+        master[i] = w * shrink - lr * dir;
+        first[i] = m;
+        second[i] = v;
+        grad[i] = g;
+    }
+}
+
+int adam_grid(int64_t n) { return stride_grid((n + 3) / 4, ADAM_BLOCK, 4); }
+
+}  // namespace pbg
+
+using namespace pbg;
+
+extern "C" {
+
+int64_t pbg_adam_partials_size(int64_t n) { return 2 * (int64_t)adam_grid(n > 0 ? n : 1); }
+
+int pbg_adam_step(int64_t n, float* master, float* grad, float* first, float* second, const float* controls,
+                  int64_t* step, int32_t decoupled, double* partials, double* report, void* stream) {
+    PBG_REQUIRE(n >= 0 && master && grad && first && second && controls && step && partials && report,
+                "adam_step: null argument");
+    PBG_REQUIRE(((uintptr_t)grad % 16) == 0, "adam_step: grad must be 16-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    int grid = adam_grid(n > 0 ? n : 1);
+    adam_norm_kernel<<<grid, ADAM_BLOCK, 0, s>>>(n, (const float4*)grad, grad, controls, partials);
+    int rc = launch_status("adam_norm");
+    if (rc) return rc;
+    adam_finalize_kernel<<<1, ADAM_BLOCK, 0, s>>>(grid, partials, controls, step, report);
+    rc = launch_status("adam_finalize");
+    if (rc) return rc;
+    if (n > 0) adam_apply_kernel<<<stride_grid(n, ADAM_BLOCK, 4), ADAM_BLOCK, 0, s>>>(n, master, grad, first, second,
+                                                                                    controls, decoupled, report);
+    return launch_status("adam_apply");
+}
+
+}  // extern "C"

@@ -1,0 +1,919 @@
+// NLHE public state machine, chance, settlement inputs and the fused
+// sampled rollout step (sm_100a).
+//
+// The per-hand transition restates pbg/games/poker/queued/hooks.py:
+//   initial_roots      :357-454      legality          :464-510
+//   step_player        :883-979      needs_chance      :981-987
+//   deal_next_street   :989-1126     history appends   :708-810
+//   sampled_leaf       :1145-1216    combo_cards/class :1128-1143, :655-674
+// Chip amounts are half big blinds, exact in fp32, so every state column is
+// bit-exact against the reference.  A hand's state lives in registers
+// (seat loops unrolled for the compile-time player count P) and is written
+// back once per call.
+#include "pbg_common.cuh"
+#include "policy.cuh"
+
+namespace pbg {
+
+template <int P>
+struct Hand {
+    uint8_t board[5];
+    int combo[P];
+    int button, street, to_act;
+    float stacks[P], committed[P], cs[P];
+    int status[P];
+    float bet, lfr;
+    bool pending[P], can[P];
+    bool terminal;
+
+    __device__ void load(const pbg_state& s, int64_t b) {
+        #pragma unroll
+        for (int i = 0; i < 5; ++i) board[i] = s.board[b * 5 + i];
+        #pragma unroll
+        for (int p = 0; p < P; ++p) {
+            combo[p] = s.combo[b * P + p];
+            stacks[p] = s.stacks[b * P + p];
+            committed[p] = s.committed[b * P + p];
+            cs[p] = s.committed_street[b * P + p];
+            status[p] = s.status[b * P + p];
+            pending[p] = s.pending[b * P + p] != 0;
+            can[p] = s.can_raise[b * P + p] != 0;
+        }
+        button = s.button[b];
+        street = s.street[b];
+        to_act = s.to_act[b];
+        bet = s.current_bet[b];
+        lfr = s.last_full_raise[b];
+        terminal = s.terminal[b] != 0;
+    }
+
+    __device__ void store(const pbg_state& s, int64_t b) const {
+        #pragma unroll
+        for (int i = 0; i < 5; ++i) s.board[b * 5 + i] = board[i];
+        #pragma unroll
+        for (int p = 0; p < P; ++p) {
+            s.combo[b * P + p] = combo[p];
+            s.stacks[b * P + p] = stacks[p];
+            s.committed[b * P + p] = committed[p];
+            s.committed_street[b * P + p] = cs[p];
+            s.status[b * P + p] = (int8_t)status[p];
+            s.pending[b * P + p] = pending[p];
+            s.can_raise[b * P + p] = can[p];
+        }
+        s.button[b] = button;
+        s.street[b] = street;
+        s.to_act[b] = to_act;
+        s.current_bet[b] = bet;
+        s.last_full_raise[b] = lfr;
+        s.terminal[b] = terminal;
+    }
+
+    // seat-indexed reads without local memory
+    __device__ float get(const float (&v)[P], int a) const {
+        float r = 0.0f;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) if (p == a) r = v[p];
+        return r;
+    }
+    __device__ int get(const int (&v)[P], int a) const {
+        int r = 0;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) if (p == a) r = v[p];
+        return r;
+    }
+    __device__ bool get(const bool (&v)[P], int a) const {
+        bool r = false;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) if (p == a) r = v[p];
+        return r;
+    }
+
+    __device__ int live_count() const {
+        int n = 0;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) n += status[p] == LIVE;
+        return n;
+    }
+
+    __device__ float pot() const {
+        float s = 0.0f;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) s = __fadd_rn(s, committed[p]);
+        return s;
+    }
+
+    // hooks.py:342-348 (_next_seat) over LIVE seats.
+    __device__ int next_live(int after) const {
+        int found = -1;
+        #pragma unroll
+        for (int o = P; o >= 1; --o) {
+            int c = (after + o) % P;
+            if (get(status, c) == LIVE) found = c;
+        }
+        return found >= 0 ? found : (after + 1) % P;
+    }
+
+    // hooks.py:464-510 as a summary: call bit and contiguous raise ticks.
+    __device__ LegalSummary legality(int T) const {
+        LegalSummary L;
+        int a = to_act;
+        float stack = get(stacks, a), street_c = get(cs, a);
+        float call = fmaxf(__fsub_rn(bet, street_c), 0.0f);
+        float maximum = __fadd_rn(street_c, stack);
+        float minimum = __fadd_rn(bet, lfr);
+        bool raising = live_count() > 1 && get(can, a);
+        L.alive = !terminal;
+        L.call_legal = call > 0.0f;
+        L.lo = 1;
+        L.hi = 0;
+        if (raising) {
+            // tick k has target (k+1)/2; twice a half-integer is an integer
+            int max2 = (int)__fmul_rn(maximum, 2.0f);
+            int min2 = (int)ceilf(__fmul_rn(minimum, 2.0f));
+            int hi = min(max2 - 1, T - 1);
+            if (min2 <= max2) {
+                L.lo = max(min2 - 1, 0);
+                L.hi = hi;
+            } else if (maximum > bet && max2 - 1 >= 0 && max2 - 1 <= T - 1) {
+                L.lo = max2 - 1;
+                L.hi = max2 - 1;
+            }
+        }
+        return L;
+    }
+
+    // hooks.py:883-979 (step_player); the action is legal by contract.
+    __device__ void step(int action) {
+        int a = to_act;
+        bool fold = action == FOLD, call_action = action == CHECK_CALL, raise_action = action >= RAISE_OFFSET;
+        float ac = get(cs, a), astack = get(stacks, a);
+        float call = fmaxf(__fsub_rn(bet, ac), 0.0f);
+        float paid_call = fminf(call, astack);
+        float paid = call_action ? paid_call : 0.0f;
+        float raise_to = __fmul_rn(__fadd_rn(__fsub_rn((float)action, 2.0f), 1.0f), 0.5f);
+        float paid_raise = fmaxf(__fsub_rn(raise_to, ac), 0.0f);
+        if (raise_action) paid = paid_raise;
+        if (fold) paid = 0.0f;
+        float next_stack = __fsub_rn(astack, paid);
+        #pragma unroll
+        for (int p = 0; p < P; ++p) {
+            if (p != a) continue;
+            if (fold) status[p] = FOLDED;
+            pending[p] = false;
+            stacks[p] = next_stack;
+            committed[p] = __fadd_rn(committed[p], paid);
+            cs[p] = __fadd_rn(cs[p], paid);
+            if (next_stack == 0.0f && !fold) status[p] = ALL_IN;
+        }
+        float old_bet = bet;
+        if (raise_action) bet = raise_to;
+        float raise_size = __fsub_rn(raise_to, old_bet);
+        bool full = raise_action && raise_size >= lfr;
+        if (full) lfr = raise_size;
+        bool any_outstanding = false;
+        int contenders = 0;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) {
+            bool active = status[p] == LIVE;
+            if (full && active) { can[p] = true; pending[p] = true; }
+            if (p == a) can[p] = false;
+            if (active && cs[p] < bet) pending[p] = true;
+            if (p == a) pending[p] = false;
+            contenders += status[p] != FOLDED;
+            any_outstanding |= pending[p] && active;
+        }
+        terminal = contenders <= 1 || (!any_outstanding && street == 3);
+        to_act = next_live(a);
+    }
+
+    __device__ bool needs_chance() const {
+        bool outstanding = false;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) outstanding |= pending[p] && status[p] == LIVE;
+        return !terminal && !outstanding && street < 3;
+    }
+
+    // 64-bit set of compact deck cards held privately or on the board.
+    __device__ uint64_t used_cards(int D, int first) const {
+        uint64_t used = 0;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) {
+            int c0, c1;
+            combo_cards(D, first, combo[p], c0, c1);
+            used |= 1ULL << (c0 - first);
+            used |= 1ULL << (c1 - first);
+        }
+        #pragma unroll
+        for (int i = 0; i < 5; ++i)
+            if (board[i] != PAD_CARD) used |= 1ULL << (board[i] - first);
+        return used;
+    }
+
+    // hooks.py:989-1074 given the three smallest (key, card) unused cards.
+    __device__ void apply_deal(bool needs, const int (&dealt)[3], int first) {
+        if (needs) {
+            if (street == 0) { board[0] = (uint8_t)(first + dealt[0]); board[1] = (uint8_t)(first + dealt[1]); board[2] = (uint8_t)(first + dealt[2]); }
+            else if (street == 1) board[3] = (uint8_t)(first + dealt[0]);
+            else if (street == 2) board[4] = (uint8_t)(first + dealt[0]);
+        }
+        street += needs ? 1 : 0;
+        int live = live_count();
+        if (needs) {
+            #pragma unroll
+            for (int p = 0; p < P; ++p) {
+                bool np = status[p] == LIVE && live > 1;
+                pending[p] = np;
+                can[p] = np;
+                cs[p] = 0.0f;
+            }
+            to_act = next_live(button);
+            bet = 0.0f;
+            lfr = 1.0f;
+        }
+        bool outstanding = false;
+        #pragma unroll
+        for (int p = 0; p < P; ++p) outstanding |= pending[p] && status[p] == LIVE;
+        if (street == 3 && !outstanding) terminal = true;
+    }
+};
+
+// Three smallest (key, index) among unused cards, one thread.
+__device__ __forceinline__ void smallest3(const int64_t* key, uint64_t used, int D, int (&out)[3]) {
+    int64_t bk[3] = {INT64_MAX, INT64_MAX, INT64_MAX};
+    int bi[3] = {D, D, D};
+    for (int c = 0; c < D; ++c) {
+        int64_t k = ((used >> c) & 1ULL) ? INT64_MAX : key[c];
+        // insert (k, c) keeping ascending (key, index) order
+        if (k < bk[2] || (k == bk[2] && c < bi[2])) {
+            bk[2] = k; bi[2] = c;
+            if (bk[2] < bk[1] || (bk[2] == bk[1] && bi[2] < bi[1])) {
+                int64_t tk = bk[1]; int ti = bi[1]; bk[1] = bk[2]; bi[1] = bi[2]; bk[2] = tk; bi[2] = ti;
+                if (bk[1] < bk[0] || (bk[1] == bk[0] && bi[1] < bi[0])) {
+                    tk = bk[0]; ti = bi[0]; bk[0] = bk[1]; bi[0] = bi[1]; bk[1] = tk; bi[1] = ti;
+                }
+            }
+        }
+    }
+    out[0] = bi[0]; out[1] = bi[1]; out[2] = bi[2];
+}
+
+// Warp version: lane holds cards lane and lane+32; three argmin rounds.
+__device__ __forceinline__ void warp_smallest3(uint64_t ns, int64_t root, int64_t path, int64_t draw_base,
+                                               int64_t lane_id, int64_t epoch, uint64_t used, int D,
+                                               int (&out)[3]) {
+    const int lane = threadIdx.x & 31;
+    int64_t k0 = INT64_MAX, k1 = INT64_MAX;
+    int c0 = lane, c1 = lane + 32;
+    if (c0 < D && !((used >> c0) & 1ULL)) k0 = rng_key(ns, root, path, draw_base + c0, lane_id, epoch);
+    if (c1 < D && !((used >> c1) & 1ULL)) k1 = rng_key(ns, root, path, draw_base + c1, lane_id, epoch);
+    if (c0 >= D) c0 = 64;
+    if (c1 >= D) c1 = 64;
+    #pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        bool first_is_min = (k0 < k1) || (k0 == k1 && c0 < c1);
+        int64_t bk = first_is_min ? k0 : k1;
+        int bc = first_is_min ? c0 : c1;
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            int64_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+            int oc = __shfl_xor_sync(0xffffffffu, bc, o);
+            if (ok < bk || (ok == bk && oc < bc)) { bk = ok; bc = oc; }
+        }
+        out[r] = bc;
+        if (bc == c0) { k0 = INT64_MAX; c0 = 64; }
+        if (bc == c1) { k1 = INT64_MAX; c1 = 64; }
+    }
+}
+
+// History slot writes ------------------------------------------------------
+struct HistoryToken {
+    int64_t actor, street, action;
+    float amount, pot, call, bet, lo, hi;
+};
+
+__device__ __forceinline__ void write_token(const pbg_history& h, int64_t b, int pos, const HistoryToken& t) {
+    int64_t i = b * h.tokens + pos;
+    h.actor[i] = t.actor; h.street[i] = t.street; h.action[i] = t.action;
+    h.amount[i] = t.amount; h.pot_before[i] = t.pot; h.call_amount[i] = t.call;
+    h.current_bet[i] = t.bet; h.min_raise_to[i] = t.lo; h.max_raise_to[i] = t.hi;
+    h.mask[i] = 1;
+}
+
+__device__ __forceinline__ int history_length(const pbg_history& h, int64_t b) {
+    int n = 0;
+    for (int t = 0; t < h.tokens; ++t) n += h.mask[b * h.tokens + t] != 0;
+    return n;
+}
+
+__device__ __forceinline__ int warp_history_length(const pbg_history& h, int64_t b) {
+    const int lane = threadIdx.x & 31;
+    int n = 0;
+    for (int t = lane; t < h.tokens; t += 32) n += h.mask[b * h.tokens + t] != 0;
+    return __reduce_add_sync(0xffffffffu, n);
+}
+
+template <int P>
+__device__ HistoryToken player_token(const Hand<P>& s, int action, int T) {
+    LegalSummary L = s.legality(T);
+    HistoryToken t;
+    bool has = L.alive && L.lo <= L.hi;
+    t.lo = has ? __fmul_rn((float)(L.lo + 1), 0.5f) : 0.0f;
+    t.hi = has ? __fmul_rn((float)(L.hi + 1), 0.5f) : 0.0f;
+    int a = s.to_act;
+    float stack = s.get(s.stacks, a), ac = s.get(s.cs, a);
+    float call = fmaxf(__fsub_rn(s.bet, ac), 0.0f);
+    float paid_call = fminf(call, stack);
+    float raise_to = __fmul_rn(__fadd_rn(__fsub_rn((float)action, 2.0f), 1.0f), 0.5f);
+    bool raised = action >= RAISE_OFFSET, called = action == CHECK_CALL;
+    t.amount = raised ? raise_to : (called ? paid_call : 0.0f);
+    t.action = raised ? 2 : (called ? 1 : 0);
+    t.actor = a;
+    t.street = s.street;
+    t.pot = s.pot();
+    t.call = call;
+    t.bet = s.bet;
+    return t;
+}
+
+template <int P>
+__device__ HistoryToken chance_token(const Hand<P>& s) {
+    HistoryToken t;
+    t.actor = -1; t.street = s.street + 1; t.action = 3;
+    t.amount = 0.0f; t.pot = s.pot(); t.call = 0.0f; t.bet = s.bet; t.lo = 0.0f; t.hi = 0.0f;
+    return t;
+}
+
+// hooks.py:1145-1216 for one hand (one thread).
+template <int P>
+__device__ void write_leaf(const Hand<P>& s, int D, int first, const pbg_leaf& leaf, int64_t b) {
+    int contenders = 0;
+    #pragma unroll
+    for (int p = 0; p < P; ++p) contenders += s.status[p] != FOLDED;
+    bool early = contenders == 1;
+    float pot = s.pot();
+    #pragma unroll
+    for (int p = 0; p < P; ++p) {
+        bool contender = s.status[p] != FOLDED;
+        float base = -s.committed[p];
+        if (early) base = __fadd_rn(base, __fmul_rn(contender ? 1.0f : 0.0f, pot));
+        leaf.baseline[b * P + p] = base;
+        leaf.amount[b * P + p] = (!early && p == 0) ? pot : 0.0f;
+        leaf.level[b * P + p] = (!early && contender) ? 0 : -1;
+        leaf.combo[b * P + p] = (!early && contender) ? s.combo[p] : -1;
+    }
+    uint64_t free_cards = ~s.used_cards(D, first) & (D == 64 ? ~0ULL : ((1ULL << D) - 1));
+    #pragma unroll
+    for (int i = 0; i < 5; ++i) {
+        uint8_t c = s.board[i];
+        if (early && c == PAD_CARD) {
+            int low = __ffsll((long long)free_cards) - 1;
+            free_cards &= free_cards - 1;
+            c = (uint8_t)(first + low);
+        }
+        leaf.board[b * 5 + i] = c;
+    }
+}
+
+// ----------------------------------------------------------------- kernels
+
+template <int P>
+__global__ void roots_kernel(Geo d, int64_t rows, uint64_t ns, int64_t epoch, int64_t base, int64_t lane_id,
+                             const int32_t* buttons, float stack_bb, pbg_state st) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < rows; b += (int64_t)gridDim.x * blockDim.x) {
+        int64_t root = base + b;
+        int64_t key[MAXD];
+        for (int c = 0; c < d.D; ++c) key[c] = rng_key(ns, root, 0, c, lane_id, epoch);
+        // 2P smallest keys in stable order: repeated selection
+        uint64_t taken = 0;
+        int order[2 * MAXP];
+        for (int r = 0; r < 2 * P; ++r) {
+            int best = -1;
+            for (int c = 0; c < d.D; ++c) {
+                if ((taken >> c) & 1ULL) continue;
+                if (best < 0 || key[c] < key[best]) best = c;
+            }
+            taken |= 1ULL << best;
+            order[r] = best;
+        }
+        Hand<P> h;
+        #pragma unroll
+        for (int i = 0; i < 5; ++i) h.board[i] = PAD_CARD;
+        int button = buttons ? buttons[b] : (int)(root % P);
+        int sb, bb, first_actor;
+        if (P == 2) { sb = button; bb = (button + 1) % 2; first_actor = button; }
+        else { sb = (button + 1) % P; bb = (button + 2) % P; first_actor = (button + 3) % P; }
+        #pragma unroll
+        for (int p = 0; p < P; ++p) {
+            h.combo[p] = combo_id(d.D, d.first, d.first + order[2 * p], d.first + order[2 * p + 1]);
+            float c = p == bb ? 1.0f : (p == sb ? 0.5f : 0.0f);
+            h.committed[p] = c;
+            h.cs[p] = c;
+            h.stacks[p] = __fsub_rn(stack_bb, c);
+            h.status[p] = LIVE;
+            h.pending[p] = true;
+            h.can[p] = true;
+        }
+        h.button = button;
+        h.street = 0;
+        h.to_act = first_actor;
+        h.bet = 1.0f;
+        h.lfr = 1.0f;
+        h.terminal = false;
+        h.store(st, b);
+    }
+}
+
+template <int P>
+__global__ void legality_kernel(Geo d, int64_t B, pbg_state st, uint8_t* mask) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        Hand<P> h;
+        h.load(st, b);
+        LegalSummary L = h.legality(d.T);
+        for (int e = 0; e < d.E; ++e) mask[b * d.E + e] = L(e) ? 1 : 0;
+    }
+}
+
+template <int P>
+__global__ void input_type_kernel(int64_t B, pbg_state st, int32_t* out) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        int contenders = 0;
+        for (int p = 0; p < P; ++p) contenders += st.status[b * P + p] != FOLDED;
+        out[b] = st.street[b] == 0 ? 0 : contenders - 1;
+    }
+}
+
+template <int P>
+__global__ void step_kernel(int64_t B, pbg_state st, const int32_t* action) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        Hand<P> h;
+        h.load(st, b);
+        h.step(action[b]);
+        h.store(st, b);
+    }
+}
+
+template <int P>
+__global__ void needs_chance_kernel(int64_t B, pbg_state st, uint8_t* out) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        Hand<P> h;
+        h.load(st, b);
+        out[b] = h.needs_chance();
+    }
+}
+
+// keys: explicit [B,D] (keyed == false) or CHANCE keys derived in-kernel.
+template <int P>
+__global__ void deal_kernel(Geo d, int64_t B, pbg_state st, const int64_t* keys, const uint8_t* active,
+                            bool keyed, uint64_t ns, const int64_t* root, const int64_t* path, int64_t draw,
+                            const int64_t* retry, const int64_t* lane) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        Hand<P> h;
+        h.load(st, b);
+        bool needs = h.needs_chance() && (active ? active[b] != 0 : true);
+        int dealt[3] = {0, 1, 2};
+        uint64_t used = h.used_cards(d.D, d.first);
+        int64_t k[MAXD];
+        for (int c = 0; c < d.D; ++c) {
+            if (keyed) k[c] = needs ? rng_key(ns, root[b], path[b], draw * d.D + c, lane[b], retry[b]) : 0;
+            else k[c] = keys[b * d.D + c];
+        }
+        smallest3(k, used, d.D, dealt);
+        h.apply_deal(needs, dealt, d.first);
+        h.store(st, b);
+    }
+}
+
+template <int P>
+__global__ void history_kernel(Geo d, int64_t B, pbg_state st, const int32_t* action, const uint8_t* active,
+                               pbg_history hist) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        Hand<P> h;
+        h.load(st, b);
+        bool on;
+        HistoryToken t;
+        if (action) { on = !h.terminal; t = player_token(h, action[b], d.T); }
+        else { on = active[b] != 0; t = chance_token(h); }
+        if (!on) continue;
+        int len = history_length(hist, b);
+        if (len < hist.tokens) write_token(hist, b, len, t);
+    }
+}
+
+template <int P>
+__global__ void leaf_kernel(Geo d, int64_t B, pbg_state st, pbg_leaf leaf) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        Hand<P> h;
+        h.load(st, b);
+        write_leaf(h, d.D, d.first, leaf, b);
+    }
+}
+
+__global__ void combo_cards_kernel(Geo d, int64_t n, const int32_t* ids, int64_t* out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int a, b;
+        combo_cards(d.D, d.first, ids[i], a, b);
+        out[2 * i] = a;
+        out[2 * i + 1] = b;
+    }
+}
+
+__global__ void combo_class_kernel(Geo d, int32_t* out) {
+    for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < d.H; h += gridDim.x * blockDim.x) {
+        int a, b;
+        combo_cards(d.D, d.first, h, a, b);
+        out[h] = combo_class(d.R, a, b);
+    }
+}
+
+// Fused sampled rollout step: one warp per hand ----------------------------
+struct StepArgs {
+    Geo d;
+    int64_t B;
+    pbg_state st;
+    pbg_history hist;
+    int64_t* root_path;
+    const int64_t* lane;
+    const int64_t* retry;
+    uint64_t ns_action, ns_chance;
+    pbg_policy pol;
+    int32_t* action;
+    float* selected;
+    int32_t* decision;
+    uint8_t* new_leaf;
+    pbg_leaf leaf;
+};
+
+template <int P>
+__global__ void __launch_bounds__(256) rollout_step_kernel(StepArgs A) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const Geo& d = A.d;
+    const int C = (d.E + 31) / 32;
+    for (int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; b < A.B; b += warps) {
+        Hand<P> h;
+        h.load(A.st, b);
+        if (h.terminal) {
+            if (lane == 0) {
+                A.action[b] = -1;
+                A.selected[b] = 0.0f;
+                if (A.new_leaf) A.new_leaf[b] = 0;
+                if (A.decision) { A.decision[4 * b] = -1; A.decision[4 * b + 1] = -1; A.decision[4 * b + 2] = 1; A.decision[4 * b + 3] = 0; }
+            }
+            continue;
+        }
+        int64_t root = A.root_path[2 * b], path = A.root_path[2 * b + 1];
+        int64_t rl = A.lane ? A.lane[b] : 0, re = A.retry ? A.retry[b] : 0;
+        // sample at the owner's private row (rollout.py:1604-1621, hooks.py:1489-1541)
+        LegalSummary L = h.legality(d.T);
+        int a = h.to_act;
+        int combo = h.get(h.combo, a);
+        int64_t row = 0;
+        if (A.pol.rows > 1) {
+            if (h.street == 0) {
+                int c0, c1;
+                combo_cards(d.D, d.first, combo, c0, c1);
+                row = combo_class(d.R, c0, c1);
+            } else {
+                row = combo;
+            }
+        }
+        RawRow raw = raw_row(A.pol, b * A.pol.rows + row);
+        float p[CHUNK_MAX];
+        float mass = warp_policy_row(raw, L, d.T, d.E, C, p);
+        int64_t key = rng_key(A.ns_action, root, path, 0, rl, re);
+        int act = warp_sample(p, d.E, C, mass, key);
+        float psel = warp_fetch(p, act, C);
+        float logp = logf(fmaxf(psel, POLICY_EPS));
+        // transition (hooks.py:1656-1700)
+        int len = A.hist.tokens > 0 ? warp_history_length(A.hist, b) : 0;
+        HistoryToken tok = player_token(h, act, d.T);
+        if (lane == 0 && A.hist.tokens > 0 && len < A.hist.tokens) write_token(A.hist, b, len, tok);
+        ++len;
+        int street_before = h.street;
+        h.step(act);
+        for (int gen = 0; gen < 3; ++gen) {
+            bool needs = h.needs_chance();
+            if (needs) {
+                if (lane == 0 && A.hist.tokens > 0 && len < A.hist.tokens) write_token(A.hist, b, len, chance_token(h));
+                ++len;
+            }
+            int dealt[3] = {0, 1, 2};
+            if (needs) {
+                uint64_t used = h.used_cards(d.D, d.first);
+                warp_smallest3(A.ns_chance, root, path, (int64_t)gen * d.D, rl, re, used, d.D, dealt);
+            }
+            h.apply_deal(needs, dealt, d.first);
+        }
+        if (lane == 0) {
+            h.store(A.st, b);
+            A.action[b] = act;
+            A.selected[b] = logp;
+            A.root_path[2 * b + 1] = child_path(path, 1);
+            if (A.decision) {
+                A.decision[4 * b] = a;
+                A.decision[4 * b + 1] = street_before;
+                A.decision[4 * b + 2] = L.lo;
+                A.decision[4 * b + 3] = (L.hi & 0xffff) | ((L.call_legal ? 1 : 0) << 16);
+            }
+            if (A.new_leaf) A.new_leaf[b] = h.terminal;
+            if (h.terminal) write_leaf(h, d.D, d.first, A.leaf, b);
+        }
+    }
+}
+
+// Reach update: block per hand, thread per private row --------------------
+template <int P>
+__global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, const int32_t* action,
+                             const int32_t* decision, float* log_reach) {
+    extern __shared__ float sel[];  // [H]
+    for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+        int a = decision[4 * b];
+        if (a < 0) continue;  // hand was already terminal
+        int street_before = decision[4 * b + 1];
+        LegalSummary L;
+        L.alive = true;
+        L.lo = decision[4 * b + 2];
+        L.hi = (int16_t)(decision[4 * b + 3] & 0xffff);
+        L.call_legal = (decision[4 * b + 3] >> 16) & 1;
+        int act = action[b];
+        int rows = street_before == 0 ? d.K : d.H;
+        for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+            RawRow raw = raw_row(pol, b * pol.rows + r);
+            // full composite probability of one row, sequential over events
+            float mixk = 0.0f, mass = 0.0f;
+            int count = 0, top = -1;
+            for (int k = 0; k < d.T; ++k) if (L(k + 2)) { ++count; top = k; }
+            float l0 = raw.logits[0], l1 = raw.logits[1], l2 = raw.logits[2];
+            // two passes: masses then the softmax over legal events
+            float S[8], norm[8];
+            for (int m = 0; m < raw.M; ++m) {
+                float loc = raw.mu[m], sc = raw.scale[m];
+                float z0 = __fdiv_rn(__fsub_rn(0.0f, loc), sc);
+                float zT = __fdiv_rn(__fsub_rn(edge_of(d.T, d.T), loc), sc);
+                norm[m] = fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(zT), sigmoid_f(-z0)), -expm1f(__fsub_rn(z0, zT))), FLT_TINY);
+                float s = 0.0f;
+                for (int k = 0; k < d.T; ++k) {
+                    float lo = __fdiv_rn(__fsub_rn(edge_of(k, d.T), loc), sc);
+                    float hi = __fdiv_rn(__fsub_rn(edge_of(k + 1, d.T), loc), sc);
+                    float v = fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(hi), sigmoid_f(-lo)), -expm1f(__fsub_rn(lo, hi))), 0.0f);
+                    s = __fadd_rn(s, __fdiv_rn(v, norm[m]));
+                }
+                S[m] = fmaxf(s, FLT_TINY);
+            }
+            // mixture per tick (recomputed) -> mass, then logits
+            auto mixture = [&](int k) {
+                float acc = 0.0f;
+                for (int m = 0; m < raw.M; ++m) {
+                    float loc = raw.mu[m], sc = raw.scale[m];
+                    float lo = __fdiv_rn(__fsub_rn(edge_of(k, d.T), loc), sc);
+                    float hi = __fdiv_rn(__fsub_rn(edge_of(k + 1, d.T), loc), sc);
+                    float v = fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(hi), sigmoid_f(-lo)), -expm1f(__fsub_rn(lo, hi))), 0.0f);
+                    acc = __fadd_rn(acc, __fmul_rn(raw.omega[m], __fdiv_rn(__fdiv_rn(v, norm[m]), S[m])));
+                }
+                return acc;
+            };
+            for (int k = L.lo; k <= L.hi && k < d.T; ++k) mass = __fadd_rn(mass, mixture(k));
+            float io = raw.iota;
+            auto logit_of = [&](int e) {
+                if (e == 0) return l0;
+                if (e == 1) return L.call_legal ? l1 : l0;
+                int k = e - 2;
+                float mk = mixture(k);
+                float cond = mass > 0.0f ? __fdiv_rn(mk, fmaxf(mass, POLICY_EPS)) : __fdiv_rn(1.0f, (float)max(count, 1));
+                float rp = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, io), cond), __fmul_rn(io, k == top ? 1.0f : 0.0f));
+                return rp > 0.0f ? __fadd_rn(l2, logf(fmaxf(rp, POLICY_EPS))) : -INFINITY;
+            };
+            // max and denominator over legal events (one pass each)
+            float mx = -INFINITY;
+            float lg_cache_sel = -INFINITY;
+            for (int e = 0; e < d.E; ++e) {
+                if (!L(e)) continue;
+                float v = logit_of(e);
+                if (e == act) lg_cache_sel = v;
+                mx = fmaxf(mx, v);
+            }
+            float den = 0.0f;
+            for (int e = 0; e < d.E; ++e) if (L(e)) den = __fadd_rn(den, expf(__fsub_rn(logit_of(e), mx)));
+            float psel = __fdiv_rn(expf(__fsub_rn(lg_cache_sel, mx)), den);
+            sel[r] = logf(fmaxf(psel, POLICY_EPS));
+            (void)mixk;
+        }
+        __syncthreads();
+        // board after the chance closure
+        uint64_t board_cards = 0;
+        for (int i = 0; i < 5; ++i) {
+            int c = st.board[b * 5 + i];
+            if (c != PAD_CARD) board_cards |= 1ULL << (c - d.first);
+        }
+        float* reach = log_reach + (int64_t)b * P * d.H;
+        for (int hnd = threadIdx.x; hnd < d.H; hnd += blockDim.x) {
+            int c0, c1;
+            combo_cards(d.D, d.first, hnd, c0, c1);
+            int r = street_before == 0 ? combo_class(d.R, c0, c1) : hnd;
+            bool conflict = ((board_cards >> (c0 - d.first)) & 1ULL) || ((board_cards >> (c1 - d.first)) & 1ULL);
+            #pragma unroll
+            for (int p = 0; p < P; ++p) {
+                float v = reach[p * d.H + hnd];
+                if (p == a) v = __fadd_rn(v, sel[r]);
+                if (conflict) v = -INFINITY;
+                reach[p * d.H + hnd] = v;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace pbg
+
+// ====================================================================== ABI
+using namespace pbg;
+
+#define PBG_DISPATCH_P(P, ...)                                           \
+    switch (P) {                                                         \
+        case 2: { constexpr int PP = 2; __VA_ARGS__; break; }            \
+        case 3: { constexpr int PP = 3; __VA_ARGS__; break; }            \
+        case 4: { constexpr int PP = 4; __VA_ARGS__; break; }            \
+        case 5: { constexpr int PP = 5; __VA_ARGS__; break; }            \
+        case 6: { constexpr int PP = 6; __VA_ARGS__; break; }            \
+        default: set_error("players must be in [2,6]"); return PBG_EINVAL; \
+    }
+
+static bool state_ok(const pbg_state& s) {
+    return s.board && s.combo && s.button && s.street && s.to_act && s.stacks && s.committed &&
+           s.committed_street && s.status && s.current_bet && s.last_full_raise && s.pending &&
+           s.can_raise && s.terminal;
+}
+
+extern "C" {
+
+int pbg_initial_roots(pbg_geometry g, int64_t rows, int64_t seed, int64_t iteration, int64_t retry_epoch,
+                      int64_t logical_base, int64_t lane, const int32_t* buttons, pbg_state st, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(rows >= 0 && state_ok(st), "initial_roots: bad rows or state");
+    if (rows == 0) return PBG_OK;
+    Geo d = derive(g);
+    uint64_t ns = rng_namespace(seed, iteration, PRIVATE);
+    float stack_bb = 0.5f * (float)g.stack_ticks;
+    PBG_DISPATCH_P(g.players, roots_kernel<PP><<<stride_grid(rows, 128), 128, 0, as_stream(stream)>>>(
+        d, rows, ns, retry_epoch, logical_base, lane, buttons, stack_bb, st));
+    return launch_status("initial_roots");
+}
+
+int pbg_legality(pbg_geometry g, int64_t B, pbg_state st, uint8_t* mask, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && mask, "legality: bad arguments");
+    if (B == 0) return PBG_OK;
+    Geo d = derive(g);
+    PBG_DISPATCH_P(g.players, legality_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(d, B, st, mask));
+    return launch_status("legality");
+}
+
+int pbg_input_type(pbg_geometry g, int64_t B, pbg_state st, int32_t* out, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && out, "input_type: bad arguments");
+    if (B == 0) return PBG_OK;
+    PBG_DISPATCH_P(g.players, input_type_kernel<PP><<<stride_grid(B, 256), 256, 0, as_stream(stream)>>>(B, st, out));
+    return launch_status("input_type");
+}
+
+int pbg_step_player(pbg_geometry g, int64_t B, pbg_state st, const int32_t* action, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && action, "step_player: bad arguments");
+    if (B == 0) return PBG_OK;
+    PBG_DISPATCH_P(g.players, step_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(B, st, action));
+    return launch_status("step_player");
+}
+
+int pbg_needs_chance(pbg_geometry g, int64_t B, pbg_state st, uint8_t* out, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && out, "needs_chance: bad arguments");
+    if (B == 0) return PBG_OK;
+    PBG_DISPATCH_P(g.players, needs_chance_kernel<PP><<<stride_grid(B, 256), 256, 0, as_stream(stream)>>>(B, st, out));
+    return launch_status("needs_chance");
+}
+
+int pbg_deal_next_street(pbg_geometry g, int64_t B, pbg_state st, const int64_t* keys, const uint8_t* active,
+                         void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && keys, "deal_next_street: bad arguments");
+    if (B == 0) return PBG_OK;
+    Geo d = derive(g);
+    PBG_DISPATCH_P(g.players, deal_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(
+        d, B, st, keys, active, false, 0, nullptr, nullptr, 0, nullptr, nullptr));
+    return launch_status("deal_next_street");
+}
+
+int pbg_deal_next_street_keyed(pbg_geometry g, int64_t B, pbg_state st, int64_t seed, int64_t iteration,
+                               const int64_t* root, const int64_t* path, int64_t draw, const int64_t* retry,
+                               const int64_t* lane, const uint8_t* active, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && root && path && retry && lane, "deal_next_street_keyed: bad arguments");
+    if (B == 0) return PBG_OK;
+    Geo d = derive(g);
+    uint64_t ns = rng_namespace(seed, iteration, CHANCE);
+    PBG_DISPATCH_P(g.players, deal_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(
+        d, B, st, nullptr, active, true, ns, root, path, draw, retry, lane));
+    return launch_status("deal_next_street_keyed");
+}
+
+int pbg_append_player_history(pbg_geometry g, int64_t B, pbg_state st, const int32_t* action, pbg_history h,
+                              void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && action && h.mask && h.tokens > 0, "append_player_history: bad arguments");
+    if (B == 0) return PBG_OK;
+    Geo d = derive(g);
+    PBG_DISPATCH_P(g.players, history_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(
+        d, B, st, action, nullptr, h));
+    return launch_status("append_player_history");
+}
+
+int pbg_append_chance_history(pbg_geometry g, int64_t B, pbg_state st, const uint8_t* active, pbg_history h,
+                              void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && active && h.mask && h.tokens > 0, "append_chance_history: bad arguments");
+    if (B == 0) return PBG_OK;
+    Geo d = derive(g);
+    PBG_DISPATCH_P(g.players, history_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(
+        d, B, st, nullptr, active, h));
+    return launch_status("append_chance_history");
+}
+
+int pbg_sampled_leaf(pbg_geometry g, int64_t B, pbg_state st, pbg_leaf leaf, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(B >= 0 && state_ok(st) && leaf.board && leaf.combo && leaf.level && leaf.baseline && leaf.amount,
+                "sampled_leaf: bad arguments");
+    if (B == 0) return PBG_OK;
+    Geo d = derive(g);
+    PBG_DISPATCH_P(g.players, leaf_kernel<PP><<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(d, B, st, leaf));
+    return launch_status("sampled_leaf");
+}
+
+int pbg_combo_cards(pbg_geometry g, int64_t n, const int32_t* ids, int64_t* out, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(n >= 0 && ids && out, "combo_cards: bad arguments");
+    if (n == 0) return PBG_OK;
+    combo_cards_kernel<<<stride_grid(n, 256), 256, 0, as_stream(stream)>>>(derive(g), n, ids, out);
+    return launch_status("combo_cards");
+}
+
+int pbg_combo_class(pbg_geometry g, int32_t* out, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    PBG_REQUIRE(out, "combo_class: null output");
+    Geo d = derive(g);
+    combo_class_kernel<<<stride_grid(d.H, 256), 256, 0, as_stream(stream)>>>(d, out);
+    return launch_status("combo_class");
+}
+
+int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, int64_t* root_path,
+                     const int64_t* lane, const int64_t* retry_epoch, int64_t seed, int64_t iteration,
+                     pbg_policy pol, int32_t* action, float* selected_log, int32_t* decision, uint8_t* new_leaf,
+                     pbg_leaf leaf, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    Geo d = derive(g);
+    PBG_REQUIRE(B >= 0 && state_ok(st) && root_path && action && selected_log, "rollout_step: bad arguments");
+    PBG_REQUIRE(pol.type_logits && pol.omega && pol.mu && pol.scale && pol.iota, "rollout_step: null policy field");
+    PBG_REQUIRE(pol.mixtures >= 1 && pol.mixtures <= 8, "rollout_step: mixtures must be in [1,8]");
+    PBG_REQUIRE(pol.rows == 1 || pol.rows >= d.H, "rollout_step: policy rows must be 1 or >= H (%d)", d.H);
+    PBG_REQUIRE(leaf.board && leaf.combo && leaf.level && leaf.baseline && leaf.amount, "rollout_step: null leaf column");
+    PBG_REQUIRE(hist.tokens == 0 || hist.mask, "rollout_step: history without mask");
+    if (B == 0) return PBG_OK;
+    StepArgs A;
+    A.d = d; A.B = B; A.st = st; A.hist = hist; A.root_path = root_path; A.lane = lane; A.retry = retry_epoch;
+    A.ns_action = rng_namespace(seed, iteration, ACTION);
+    A.ns_chance = rng_namespace(seed, iteration, CHANCE);
+    A.pol = pol; A.action = action; A.selected = selected_log; A.decision = decision; A.new_leaf = new_leaf;
+    A.leaf = leaf;
+    const int block = 256;
+    int64_t threads = B * 32;
+    PBG_DISPATCH_P(g.players, rollout_step_kernel<PP><<<stride_grid(threads, block, 8), block, 0, as_stream(stream)>>>(A));
+    return launch_status("rollout_step");
+}
+
+int pbg_reach_update(pbg_geometry g, int64_t B, pbg_state st, pbg_policy pol, const int32_t* action,
+                     const int32_t* decision, float* log_reach, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    Geo d = derive(g);
+    PBG_REQUIRE(B >= 0 && state_ok(st) && action && decision && log_reach, "reach_update: bad arguments");
+    PBG_REQUIRE(pol.rows >= d.H && pol.mixtures >= 1 && pol.mixtures <= 8, "reach_update: policy rows must be >= H");
+    if (B == 0) return PBG_OK;
+    int blocks = stride_grid(B * 256, 256, 8);
+    PBG_DISPATCH_P(g.players, reach_kernel<PP><<<blocks, 256, d.H * sizeof(float), as_stream(stream)>>>(
+        d, B, st, pol, action, decision, log_reach));
+    return launch_status("reach_update");
+}
+
+}  // extern "C"

@@ -1,0 +1,234 @@
+// Sampled-settlement showdown behind the contract-v2 evaluate_showdowns
+// signature (called at pbg/games/poker/queued/hooks.py:2277-2295).
+//
+// The reference delegates ranking to the external poker_gpu_evaluator; this
+// kernel ranks 7-card hands directly from rank counts and suit masks.  The
+// category order of each deck is the rarity-consistent order of
+// pbg/games/poker/cards.py:37-74 (category_profile): categories sorted by
+// their exact five-card counts, equal counts in conventional order.  Within
+// a category the usual kicker order applies; tied winners share equally.
+#include "pbg_common.cuh"
+
+namespace pbg {
+
+enum Cat { HIGH_CARD, PAIR, TWO_PAIR, TRIPS, STRAIGHT, FLUSH, FULL_HOUSE, QUADS, STRAIGHT_FLUSH, N_CAT };
+
+struct Strength {
+    int s[N_CAT];
+};
+
+static double comb_d(int n, int k) {
+    if (k < 0 || k > n) return 0.0;
+    double r = 1.0;
+    for (int i = 1; i <= k; ++i) r = r * (n - k + i) / i;
+    return r;
+}
+
+// Strength index of every category for a deck of R ranks (0 = weakest).
+static Strength category_strength(int R) {
+    double total = comb_d(4 * R, 5);
+    int seq = (R - 4 > 0 ? R - 4 : 0) + (R == 13 ? 1 : 0);
+    double cr5 = R >= 5 ? comb_d(R, 5) : 0.0;
+    double cnt[N_CAT];
+    cnt[HIGH_CARD] = total;
+    cnt[PAIR] = total - 1024.0 * cr5;
+    cnt[TWO_PAIR] = 144.0 * (R - 2) * comb_d(R, 2) + 24.0 * R * (R - 1);
+    cnt[TRIPS] = 64.0 * R * comb_d(R - 1, 2) + 28.0 * R * (R - 1);
+    cnt[STRAIGHT] = 1024.0 * seq;
+    cnt[FLUSH] = 4.0 * cr5;
+    cnt[FULL_HOUSE] = 24.0 * R * (R - 1);
+    cnt[QUADS] = 4.0 * R * (R - 1);
+    cnt[STRAIGHT_FLUSH] = 4.0 * seq;
+    Strength st;
+    for (int c = 0; c < N_CAT; ++c) {
+        int weaker = 0;
+        for (int o = 0; o < N_CAT; ++o) {
+            if (o == c || cnt[o] <= 0) continue;
+            if (cnt[o] > cnt[c] || (cnt[o] == cnt[c] && o < c)) ++weaker;
+        }
+        st.s[c] = cnt[c] > 0 ? weaker : -1;
+    }
+    return st;
+}
+
+__device__ __forceinline__ int top_straight(unsigned mask, int R) {
+    for (int top = 12; top >= 4; --top)
+        if (((mask >> (top - 4)) & 0x1Fu) == 0x1Fu) return top;
+    if (R == 13 && (mask & 0x100Fu) == 0x100Fu) return 3;  // A-2-3-4-5
+    return -1;
+}
+
+__device__ __forceinline__ int64_t pack(int strength, int t0, int t1, int t2, int t3, int t4) {
+    return ((((((int64_t)strength * 16 + t0) * 16 + t1) * 16 + t2) * 16 + t3) * 16) + t4;
+}
+
+// Highest set rank of mask below `below` (exclusive), or 0 when none.
+__device__ __forceinline__ int next_rank(unsigned mask, int& cursor) {
+    while (cursor >= 0 && !((mask >> cursor) & 1u)) --cursor;
+    int r = cursor >= 0 ? cursor : 0;
+    --cursor;
+    return r;
+}
+
+__device__ int64_t hand_value7(const int* cards, const Strength& S, int R) {
+    int rc[13];
+    #pragma unroll
+    for (int r = 0; r < 13; ++r) rc[r] = 0;
+    unsigned suit[4] = {0, 0, 0, 0};
+    unsigned ranks = 0;
+    #pragma unroll
+    for (int i = 0; i < 7; ++i) {
+        int r = cards[i] >> 2, s = cards[i] & 3;
+        rc[r]++;
+        suit[s] |= 1u << r;
+        ranks |= 1u << r;
+    }
+    unsigned ge2 = 0, ge3 = 0, ge4 = 0;
+    #pragma unroll
+    for (int r = 0; r < 13; ++r) {
+        if (rc[r] >= 2) ge2 |= 1u << r;
+        if (rc[r] >= 3) ge3 |= 1u << r;
+        if (rc[r] >= 4) ge4 |= 1u << r;
+    }
+    int64_t best = -1;
+    int flush_suit = -1;
+    for (int s = 0; s < 4; ++s) if (__popc(suit[s]) >= 5) flush_suit = s;
+    if (flush_suit >= 0 && S.s[STRAIGHT_FLUSH] >= 0) {
+        int top = top_straight(suit[flush_suit], R);
+        if (top >= 0) best = max(best, pack(S.s[STRAIGHT_FLUSH], top, 0, 0, 0, 0));
+    }
+    if (ge4) {
+        int q = 31 - __clz(ge4);
+        unsigned rest = ranks & ~(1u << q);
+        int k = rest ? 31 - __clz(rest) : 0;
+        best = max(best, pack(S.s[QUADS], q, k, 0, 0, 0));
+    }
+    if (ge3) {
+        int t = 31 - __clz(ge3);
+        unsigned pairs = ge2 & ~(1u << t);
+        if (pairs) best = max(best, pack(S.s[FULL_HOUSE], t, 31 - __clz(pairs), 0, 0, 0));
+    }
+    if (flush_suit >= 0 && S.s[FLUSH] >= 0) {
+        int cur = 12;
+        unsigned m = suit[flush_suit];
+        int a = next_rank(m, cur), b = next_rank(m, cur), c = next_rank(m, cur), d = next_rank(m, cur), e = next_rank(m, cur);
+        best = max(best, pack(S.s[FLUSH], a, b, c, d, e));
+    }
+    if (S.s[STRAIGHT] >= 0) {
+        int top = top_straight(ranks, R);
+        if (top >= 0) best = max(best, pack(S.s[STRAIGHT], top, 0, 0, 0, 0));
+    }
+    if (ge3) {
+        int t = 31 - __clz(ge3);
+        unsigned rest = ranks & ~(1u << t);
+        int cur = 12;
+        int a = next_rank(rest, cur), b = next_rank(rest, cur);
+        best = max(best, pack(S.s[TRIPS], t, a, b, 0, 0));
+    }
+    if (__popc(ge2) >= 2) {
+        int p1 = 31 - __clz(ge2);
+        unsigned others = ge2 & ~(1u << p1);
+        int p2 = 31 - __clz(others);
+        unsigned rest = ranks & ~(1u << p1) & ~(1u << p2);
+        int k = rest ? 31 - __clz(rest) : 0;
+        best = max(best, pack(S.s[TWO_PAIR], p1, p2, k, 0, 0));
+    }
+    if (ge2) {
+        int p = 31 - __clz(ge2);
+        unsigned rest = ranks & ~(1u << p);
+        int cur = 12;
+        int a = next_rank(rest, cur), b = next_rank(rest, cur), c = next_rank(rest, cur);
+        best = max(best, pack(S.s[PAIR], p, a, b, c, 0));
+    }
+    {
+        int cur = 12;
+        int a = next_rank(ranks, cur), b = next_rank(ranks, cur), c = next_rank(ranks, cur), d = next_rank(ranks, cur),
+            e = next_rank(ranks, cur);
+        best = max(best, pack(S.s[HIGH_CARD], a, b, c, d, e));
+    }
+    return best;
+}
+
+__global__ void showdown_kernel(Strength S, int R, int D, int first, int64_t B, int P, int strata,
+                                const uint8_t* board, const int32_t* combo, const int32_t* level,
+                                const float* baseline, const float* amount, float* out) {
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
+        int64_t value[MAXP];
+        int lev[MAXP];
+        int cards[7];
+        bool board_ok = true;
+        #pragma unroll
+        for (int i = 0; i < 5; ++i) {
+            cards[i] = board[b * 5 + i];
+            board_ok &= cards[i] >= first && cards[i] < 52;
+        }
+        const int H = D * (D - 1) / 2;
+        for (int p = 0; p < P; ++p) {
+            value[p] = -1;
+            lev[p] = level[b * P + p];
+            int id = combo[b * P + p];
+            // seats without a valid private combo or board take no share
+            if (board_ok && id >= 0 && id < H && lev[p] >= 0) {
+                combo_cards(D, first, id, cards[5], cards[6]);
+                value[p] = hand_value7(cards, S, R);
+            }
+        }
+        float acc[MAXP];
+        for (int p = 0; p < P; ++p) acc[p] = baseline[b * P + p];
+        for (int k = 0; k < strata; ++k) {
+            float amt = amount[b * strata + k];
+            if (!(amt > 0.0f)) continue;
+            int64_t best = -1;
+            for (int p = 0; p < P; ++p) if (value[p] >= 0 && lev[p] >= k && value[p] > best) best = value[p];
+            if (best < 0) continue;
+            int winners = 0;
+            for (int p = 0; p < P; ++p) winners += value[p] == best && lev[p] >= k;
+            float share = __fdiv_rn(amt, (float)winners);
+            for (int p = 0; p < P; ++p) if (value[p] == best && lev[p] >= k) acc[p] = __fadd_rn(acc[p], share);
+        }
+        for (int p = 0; p < P; ++p) out[b * P + p] = acc[p];
+    }
+}
+
+__global__ void hand_values_kernel(Strength S, int R, int64_t n, const int32_t* cards, int64_t* out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int c[7];
+        bool ok = true;
+        #pragma unroll
+        for (int j = 0; j < 7; ++j) {
+            c[j] = cards[i * 7 + j];
+            ok &= c[j] >= 0 && c[j] < 52;
+        }
+        out[i] = ok ? hand_value7(c, S, R) : -1;
+    }
+}
+
+}  // namespace pbg
+
+using namespace pbg;
+
+extern "C" {
+
+int pbg_evaluate_showdowns(int32_t rank_count, int64_t B, int32_t P, int32_t strata, const uint8_t* board,
+                           const int32_t* combo, const int32_t* level, const float* baseline, const float* amount,
+                           float* out, void* stream) {
+    PBG_REQUIRE(rank_count >= 4 && rank_count <= 13, "evaluate_showdowns: rank_count must be in [4,13]");
+    PBG_REQUIRE(P >= 2 && P <= MAXP && strata >= 1 && B >= 0, "evaluate_showdowns: bad shape");
+    PBG_REQUIRE(board && combo && level && baseline && amount && out, "evaluate_showdowns: null argument");
+    if (B == 0) return PBG_OK;
+    int D = 4 * rank_count;
+    showdown_kernel<<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(category_strength(rank_count), rank_count, D,
+                                                                        52 - D, B, P, strata, board, combo, level,
+                                                                        baseline, amount, out);
+    return launch_status("evaluate_showdowns");
+}
+
+int pbg_hand_values(int32_t rank_count, int64_t n, const int32_t* cards, int64_t* out, void* stream) {
+    PBG_REQUIRE(rank_count >= 4 && rank_count <= 13 && n >= 0 && cards && out, "hand_values: bad arguments");
+    if (n == 0) return PBG_OK;
+    hand_values_kernel<<<stride_grid(n, 128), 128, 0, as_stream(stream)>>>(category_strength(rank_count), rank_count,
+                                                                           n, cards, out);
+    return launch_status("hand_values");
+}
+
+}  // extern "C"

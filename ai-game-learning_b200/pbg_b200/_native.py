@@ -1,0 +1,134 @@
+"""ctypes binding of libpbgb200.so (the C ABI declared in include/pbgb200.h).
+
+The library is built in-tree by ``ai-game-learning_b200/build.py``.  There is
+no fallback: if the library is missing, or a tensor handed to it is not a
+CUDA tensor, the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpbgb200.so")
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+
+
+class NativeError(RuntimeError):
+    """A libpbgb200 entry point returned a failure status."""
+
+
+class Geometry(ctypes.Structure):
+    _fields_ = [("players", _I32), ("stack_ticks", _I32), ("rank_count", _I32)]
+
+
+class State(ctypes.Structure):
+    _fields_ = [(n, _P) for n in (
+        "board", "combo", "button", "street", "to_act", "stacks", "committed", "committed_street",
+        "status", "current_bet", "last_full_raise", "pending", "can_raise", "terminal")]
+
+
+class History(ctypes.Structure):
+    _fields_ = [(n, _P) for n in (
+        "actor", "street", "action", "amount", "pot_before", "call_amount", "current_bet",
+        "min_raise_to", "max_raise_to", "mask")] + [("tokens", _I32)]
+
+
+class Leaf(ctypes.Structure):
+    _fields_ = [(n, _P) for n in ("board", "combo", "level", "baseline", "amount")]
+
+
+class Policy(ctypes.Structure):
+    _fields_ = [(n, _P) for n in ("type_logits", "omega", "mu", "scale", "iota")] + [
+        ("rows", _I32), ("mixtures", _I32)]
+
+
+G, S, Hs, L, Pol = Geometry, State, History, Leaf, Policy
+
+SIGNATURES: dict[str, tuple] = {
+    "pbg_last_error": (ctypes.c_char_p, []),
+    "pbg_abi_version": (_I32, []),
+    "pbg_rng_keys": (_I32, [_I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_child_path": (_I32, [_I64, _P, _P, _P, _P]),
+    "pbg_logical_uniform": (_I32, [_I64, _P, _P, _P]),
+    "pbg_logical_categorical": (_I32, [_I64, _I32, _P, _P, _P, _P, _P]),
+    "pbg_initial_roots": (_I32, [G, _I64, _I64, _I64, _I64, _I64, _I64, _P, S, _P]),
+    "pbg_legality": (_I32, [G, _I64, S, _P, _P]),
+    "pbg_input_type": (_I32, [G, _I64, S, _P, _P]),
+    "pbg_step_player": (_I32, [G, _I64, S, _P, _P]),
+    "pbg_needs_chance": (_I32, [G, _I64, S, _P, _P]),
+    "pbg_deal_next_street": (_I32, [G, _I64, S, _P, _P, _P]),
+    "pbg_deal_next_street_keyed": (_I32, [G, _I64, S, _I64, _I64, _P, _P, _I64, _P, _P, _P, _P]),
+    "pbg_append_player_history": (_I32, [G, _I64, S, _P, Hs, _P]),
+    "pbg_append_chance_history": (_I32, [G, _I64, S, _P, Hs, _P]),
+    "pbg_sampled_leaf": (_I32, [G, _I64, S, L, _P]),
+    "pbg_combo_cards": (_I32, [G, _I64, _P, _P, _P]),
+    "pbg_combo_class": (_I32, [G, _P, _P]),
+    "pbg_evaluate_showdowns": (_I32, [_I32, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_hand_values": (_I32, [_I32, _I64, _P, _P, _P]),
+    "pbg_policy_probabilities": (_I32, [_I64, _I32, Pol, _P, _P, _P]),
+    "pbg_policy_selected_log_pi": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P]),
+    "pbg_policy_entropy": (_I32, [_I64, _I32, Pol, _P, _P, _P]),
+    "pbg_policy_sample_actor": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P, _P, _P]),
+    "pbg_rollout_step": (_I32, [G, _I64, S, Hs, _P, _P, _P, _I64, _I64, Pol, _P, _P, _P, _P, L, _P]),
+    "pbg_reach_update": (_I32, [G, _I64, S, Pol, _P, _P, _P, _P]),
+    "pbg_ppo_partials_size": (_I64, [_I64, _I32]),
+    "pbg_ppo_categorical_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_adam_partials_size": (_I64, [_I64]),
+    "pbg_adam_step": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load libpbgb200.so once; raise if it was not built."""
+
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise NativeError(
+                        f"{LIB_PATH} is missing: build it with `python ai-game-learning_b200/build.py`")
+                handle = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().pbg_last_error().decode(errors="replace")
+        raise NativeError(f"{what} failed ({rc}): {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def ptr(t: torch.Tensor | None):
+    """Device pointer of a contiguous CUDA tensor (None -> NULL)."""
+
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise NativeError("libpbgb200 operates on CUDA tensors only")
+    if not t.is_contiguous():
+        raise NativeError("libpbgb200 requires contiguous tensors")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream(device: torch.device | None = None):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)

@@ -1,0 +1,79 @@
+"""Fused PPO loss backward for categorical decision rows.
+
+``fused_ppo_backward`` is one HBM pass computing the learner objective of
+pbg/core/learner.py:2021-2077 (clipped ratio, negative-advantage log cap,
+entropy bonus) for the game-neutral categorical policy
+(tests/categorical_policy_fixture.py:33-57), scaled per row by its
+decision-mass weight, and writing d total / d logits.  The total is
+
+    total = scale * sum_r w_r * (policy_row_r - c_ent * entropy_r) * inv_count
+
+with ``inv_count = 1/N`` (the reference's lane mean, its local decision-mass
+normalisation) or ``1/sum_global(w)`` when ``global_mass=True`` (the global
+Z_{g,m}/Z scaling of the theory; the all-reduce of sum(w) happens before the
+kernel on the caller's process group).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import math
+
+import torch
+from torch import Tensor
+
+from ._native import call, lib, ptr, stream
+
+STATS = ("total", "policy", "entropy", "approximate_kl", "clip_count", "negative_cap_count", "weight_sum", "rows")
+
+
+@dataclass(frozen=True)
+class LossConfig:
+    policy_clip: float = 0.2
+    negative_advantage_ratio_cap: float | None = None
+    entropy_coefficient: float = 0.01
+
+
+class FusedPPOBackward:
+    """Owns the small device buffers a call needs (controls, partials, stats)."""
+
+    def __init__(self, rows: int, actions: int, device, config: LossConfig = LossConfig()) -> None:
+        self.rows, self.actions = int(rows), int(actions)
+        self.device = torch.device(device)
+        self.config = config
+        n = int(lib().pbg_ppo_partials_size(self.rows, self.actions))
+        self.partials = torch.zeros(n, dtype=torch.float64, device=self.device)
+        self.stats = torch.zeros(8, dtype=torch.float64, device=self.device)
+        self.controls = torch.zeros(5, dtype=torch.float32, device=self.device)
+        self.set_controls()
+
+    def set_controls(self, *, scale: float = 1.0, inv_count: float | None = None) -> None:
+        cap = self.config.negative_advantage_ratio_cap
+        log_cap = math.inf if cap is None else math.log(cap)
+        inv = 1.0 / self.rows if inv_count is None else inv_count
+        self.controls.copy_(torch.tensor([self.config.policy_clip, log_cap, self.config.entropy_coefficient,
+                                          scale, inv], dtype=torch.float32))
+
+    def __call__(self, logits: Tensor, mask: Tensor, action: Tensor, old_logp: Tensor, advantage: Tensor,
+                 weight: Tensor, dlogits: Tensor | None = None) -> tuple[Tensor, Tensor]:
+        N, A = logits.shape
+        if (N, A) != (self.rows, self.actions):
+            raise ValueError("loss rows/actions differ from the admitted shape")
+        if logits.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("logits must be fp32 or bf16")
+        if dlogits is None:
+            dlogits = torch.empty_like(logits)
+        call("pbg_ppo_categorical_backward", N, A, 1 if logits.dtype == torch.bfloat16 else 0, ptr(logits),
+             ptr(mask.view(torch.uint8) if mask.dtype == torch.bool else mask), ptr(action), ptr(old_logp),
+             ptr(advantage), ptr(weight), ptr(self.controls), ptr(dlogits), ptr(self.partials), ptr(self.stats),
+             stream(logits.device))
+        return dlogits, self.stats
+
+
+def fused_ppo_backward(logits, mask, action, old_logp, advantage, weight, config: LossConfig = LossConfig(), *,
+                       scale: float = 1.0, inv_count: float | None = None):
+    op = FusedPPOBackward(logits.shape[0], logits.shape[1], logits.device, config)
+    op.set_controls(scale=scale, inv_count=inv_count)
+    d, stats = op(logits, mask, action, old_logp, advantage, weight)
+    return d, stats.clone()

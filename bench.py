@@ -1,0 +1,375 @@
+"""Benchmark: learner decisions/s of the fused PPO loss backward (+ gradient SUM).
+
+Workload (the configuration the headline metric is quoted
+on): per rank 4,194,304 synthetic decisions x 8 actions, generated on the
+device with seed 0 + rank -- logits bf16 N(0,1), legal masks Bernoulli(0.7)
+with the lowest index forced legal in empty rows, the taken action drawn
+from the legal set with the counter RNG (LEARNER purpose), old log pi from
+logits + N(0,0.1), advantages N(0,1), decision-mass weights U(0,1).  One
+step = the fused masked log-softmax / clipped-ratio / entropy / dlogits
+kernel over all rows, then (N > 1) the SUM all-reduce of a flat fp32
+gradient buffer of --params parameters over NCCL.  Weak scaling: each rank
+owns its own rows.
+
+``--impl reference`` times the CPU restatement of the same loss (the
+reference has no CPU path) on all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ai-game-learning_b200"))
+
+METRIC = "learner decisions/sec (fused PPO loss backward + flat-gradient SUM all-reduce)"
+UNIT = "decisions/s"
+BYTES_PER_ROW = lambda A: 5 * A + 16  # bf16 logits in + u8 mask + i32 action + 3 f32 + bf16 dlogits out
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--rows", type=int, default=4_194_304)
+    p.add_argument("--actions", type=int, default=8)
+    p.add_argument("--params", type=int, default=4_194_304)
+    p.add_argument("--e2e-steps", type=int, default=10)
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------- inputs
+
+
+def make_inputs(rows, A, seed, device):
+    import torch
+    from pbg_b200.rng import DrawPurpose, logical_categorical, logical_rng_keys
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    logits = torch.randn((rows, A), generator=g, device=device).to(torch.bfloat16)
+    mask = torch.rand((rows, A), generator=g, device=device) < 0.7
+    empty = ~mask.any(1)
+    mask[:, 0] |= empty
+    uniform = mask.float()
+    keys = logical_rng_keys(seed=seed, iteration=0, root=torch.arange(rows, device=device),
+                            path=torch.zeros(rows, dtype=torch.int64, device=device), draw=0,
+                            purpose=DrawPurpose.LEARNER)
+    action = logical_categorical(uniform, keys).to(torch.int32)
+    pert = logits.float() + 0.1 * torch.randn((rows, A), generator=g, device=device)
+    old = torch.log_softmax(pert.masked_fill(~mask, -torch.inf), -1).gather(1, action.long()[:, None])[:, 0]
+    adv = torch.randn(rows, generator=g, device=device)
+    weight = torch.rand(rows, generator=g, device=device)
+    del uniform, keys, pert
+    return logits.contiguous(), mask.contiguous(), action.contiguous(), old.contiguous(), adv, weight
+
+
+# ----------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during timing."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------- peaks
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic(rows):
+    """DRAM bytes per launch of the loss kernel from the committed ncu summary."""
+
+    path = os.path.join(ROOT, "profiles", "ppo_bf16x8_loss_4M.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_row:"):
+                    return float(line.split(":")[1]) * rows
+    except OSError:
+        pass
+    return None
+
+
+# ----------------------------------------------------------- CPU legs
+
+
+def cpu_loss_rate(inputs_host, seconds=3.0, threads=None):
+    """Oracle loss passes over host rows on all threads for ~`seconds` wall."""
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+
+    logits, mask, action, old, adv, weight = inputs_host
+    N = logits.shape[0]
+    threads = threads or os.cpu_count() or 1
+    chunks = np.array_split(np.arange(N), threads)
+    O.lib()
+
+    def run(idx):
+        lo, hi = int(idx[0]), int(idx[-1]) + 1
+        O.ppo_categorical(logits[lo:hi], mask[lo:hi], action[lo:hi], old[lo:hi], adv[lo:hi], weight[lo:hi],
+                          inv_count=1.0 / N)
+        return hi - lo
+
+    rows = 0
+    start = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as pool:
+        while True:
+            rows += sum(pool.map(run, chunks))
+            if time.perf_counter() - start >= seconds:
+                break
+    wall = time.perf_counter() - start
+    return rows / wall, threads, rows, wall
+
+
+def host_sample(rows, A, seed):
+    """A CPU copy of the device workload generator's distribution (numpy)."""
+
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    logits = rng.standard_normal((rows, A)).astype(np.float32)
+    # bf16 rounding, as the device inputs carry
+    logits = (logits.view(np.uint32) + 0x8000 & 0xFFFF0000).view(np.float32)
+    mask = rng.random((rows, A)) < 0.7
+    mask[~mask.any(1), 0] = True
+    cum = np.cumsum(mask, 1)
+    pick = (rng.random(rows) * cum[:, -1]).astype(np.int64)
+    action = (cum <= pick[:, None]).sum(1).astype(np.int32)
+    pert = np.where(mask, logits + 0.1 * rng.standard_normal((rows, A)).astype(np.float32), -np.inf)
+    mx = pert.max(1)
+    lse = np.log(np.exp(pert - mx[:, None]).sum(1)) + mx
+    old = (pert[np.arange(rows), action] - lse).astype(np.float32)
+    adv = rng.standard_normal(rows).astype(np.float32)
+    weight = rng.random(rows).astype(np.float32)
+    return logits, mask.astype(np.uint8), action, old, adv, weight
+
+
+def reference_arm(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    sample = host_sample(min(args.rows, 1 << 21), args.actions, 0)
+    for _ in range(args.warmup):
+        cpu_loss_rate(sample, seconds=0.0)
+    rates = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        rate, threads, rows, wall = cpu_loss_rate(sample, seconds=0.0)
+        rates.append(rate)
+    elapsed = time.perf_counter() - t0
+    value = args.steps * sample[0].shape[0] / elapsed
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * elapsed / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": "cfg5 loss microbench, CPU restatement (oracle port)", "rows_per_step": sample[0].shape[0],
+                   "actions": args.actions},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample[0].shape[0]} rows x {args.actions} actions per step, all host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------- device arm
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from pbg_b200.loss import FusedPPOBackward, LossConfig
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    N, A = args.rows, args.actions
+    inputs = make_inputs(N, A, seed=rank, device=device)
+    logits, mask, action, old, adv, weight = inputs
+    op = FusedPPOBackward(N, A, device, LossConfig(policy_clip=0.2, negative_advantage_ratio_cap=None,
+                                                   entropy_coefficient=0.01))
+    dlogits = torch.empty_like(logits)
+    grad = torch.randn(args.params, device=device) * 1e-3
+    stream = torch.cuda.current_stream(device)
+
+    def step(events=None):
+        if events is not None:
+            events[0].record(stream)
+        op(logits, mask, action, old, adv, weight, dlogits)
+        if events is not None:
+            events[1].record(stream)
+        if world > 1:
+            dist.all_reduce(grad, op=dist.ReduceOp.SUM)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    kernel_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                     for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for i in range(args.steps):
+            step(kernel_events[i])
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kernel_events) / args.steps
+    if world > 1:
+        t = torch.tensor([elapsed_ms, kernel_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, kernel_ms = float(t[0]), float(t[1])
+    ms_per_step = elapsed_ms / args.steps
+    value = world * N / (ms_per_step / 1000.0)
+
+    # end to end through the public API: pinned host inputs -> device -> loss -> stats back
+    host = [t.cpu().pin_memory() for t in inputs]
+    stats_host = torch.empty(8, dtype=torch.float64).pin_memory()
+    dev_in = [torch.empty_like(t) for t in inputs]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = stats_host.numel() * stats_host.element_size()
+
+    def e2e_step():
+        for d, h in zip(dev_in, host):
+            d.copy_(h, non_blocking=True)
+        _, stats = op(*dev_in, dlogits)
+        if world > 1:
+            dist.all_reduce(grad, op=dist.ReduceOp.SUM)
+        stats_host.copy_(stats, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    e2e_value = world * N / (e2e_ms / 1000.0)
+
+    peak, peak_kind = measured_peak()
+    algo_bytes = BYTES_PER_ROW(A) * N
+    achieved = algo_bytes / (kernel_ms / 1000.0) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg5 loss microbench: 4,194,304 decisions x 8 actions per rank, fused PPO "
+                               "loss backward + flat fp32 gradient SUM all-reduce",
+                   "rows_per_rank": N, "actions": A, "grad_params": args.params,
+                   "allreduce": "NCCL SUM" if world > 1 else "none (single rank)",
+                   "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": committed_traffic(N),
+                     "kernel": "ppo_bf16x8_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,
+                     "algorithmic_bytes": algo_bytes},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1:
+        sample = host_sample(1 << 21, A, 0)
+        rate, threads, rows, wall = cpu_loss_rate(sample, seconds=3.0)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": f"{rows} rows ({rows // sample[0].shape[0]} passes over a "
+                                          f"{sample[0].shape[0]}-row sample) in {wall:.1f} s on {threads} threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,269 @@
+/*
+ * pbgb200.h -- C ABI of libpbgb200.so, the B200 (sm_100a) hot path of pbg.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer owned by the caller (torch tensors in
+ *     the Python host layer).  No entry point allocates device memory unless
+ *     its comment says so; scratch buffers are passed in by the caller.
+ *   - `stream` is a cudaStream_t passed as void*; work is stream-ordered and
+ *     asynchronous.  No entry point synchronises the host.
+ *   - Every entry point returns 0 on success or a negative PBG_E* code; the
+ *     message of the last failure on the calling thread is pbg_last_error().
+ *     No exception crosses the ABI; no device code traps.
+ *   - Dtypes mirror the reference's tensors: bool columns are uint8 (0/1),
+ *     int8 status, int32 ids, fp32 chips, int64 logical keys.
+ *
+ * Reference interfaces are cited as path:line inside the pbg project
+ * (pbustillo05/ai-game-learning).
+ */
+#ifndef PBGB200_H
+#define PBGB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PBG_OK 0
+#define PBG_EINVAL (-1)   /* bad argument (shape, geometry, null pointer) */
+#define PBG_ECUDA (-2)    /* a CUDA runtime call failed */
+#define PBG_ERANGE (-3)   /* a size exceeds a documented maximum */
+
+/* NLHE geometry: hooks.py:72-192 (NLHEGeometry).  stack_ticks = 2*stack_bb. */
+typedef struct {
+    int32_t players;     /* P in [2,6] */
+    int32_t stack_ticks; /* T in [16,256]; events E = T + 2 */
+    int32_t rank_count;  /* R in [4,13]; deck D = 4R cards 52-D..51 */
+} pbg_geometry;
+
+/* Public state of B hands, hooks.py:250-326 (PokerState), SoA columns. */
+typedef struct {
+    uint8_t *board;            /* [B,5], PAD 255 */
+    int32_t *combo;            /* [B,P] compact combo ids */
+    int32_t *button;           /* [B] */
+    int32_t *street;           /* [B] 0..3 */
+    int32_t *to_act;           /* [B] */
+    float *stacks;             /* [B,P] */
+    float *committed;          /* [B,P] */
+    float *committed_street;   /* [B,P] */
+    int8_t *status;            /* [B,P] LIVE 0, FOLDED 1, ALL_IN 2 */
+    float *current_bet;        /* [B] */
+    float *last_full_raise;    /* [B] */
+    uint8_t *pending;          /* [B,P] */
+    uint8_t *can_raise;        /* [B,P] */
+    uint8_t *terminal;         /* [B] */
+} pbg_state;
+
+/* Public action history, hooks.py:329-339 (PokerHistory), [B,tokens]. */
+typedef struct {
+    int64_t *actor;
+    int64_t *street;
+    int64_t *action;
+    float *amount;
+    float *pot_before;
+    float *call_amount;
+    float *current_bet;
+    float *min_raise_to;
+    float *max_raise_to;
+    uint8_t *mask;
+    int32_t tokens; /* capacity/models/capacity.py:22-25 bound */
+} pbg_history;
+
+/* Sampled settlement inputs, hooks.py:1145-1216 (sampled_leaf) output. */
+typedef struct {
+    uint8_t *board;       /* [B,5] leaf_public_state */
+    int32_t *combo;       /* [B,P] leaf_private_profile */
+    int32_t *level;       /* [B,P] stratum_level */
+    float *baseline;      /* [B,P] payoff_baseline */
+    float *amount;        /* [B,P] stratum_amount (K_strata = P) */
+} pbg_leaf;
+
+/* Raw composite-policy fields, policy.py:113-204, laid out [B, rows, ...]. */
+typedef struct {
+    const float *type_logits; /* [B,rows,3] */
+    const float *omega;       /* [B,rows,M] */
+    const float *mu;          /* [B,rows,M] */
+    const float *scale;       /* [B,rows,M]  ("s") */
+    const float *iota;        /* [B,rows] */
+    int32_t rows;             /* 1 = already selected at the actor's row */
+    int32_t mixtures;         /* M in [1,8] */
+} pbg_policy;
+
+const char *pbg_last_error(void);
+int32_t pbg_abi_version(void);
+
+/* ---------------------------------------------------------------- RNG */
+
+/* rollout.py:122-181 (logical_rng_keys): out[i] = key of the address
+ * (root[i], path[i], draw[i], lane[i], epoch[i]) in the (seed, iteration,
+ * purpose) namespace; 0 where active[i]==0 (active may be NULL). */
+int pbg_rng_keys(int64_t seed, int64_t iteration, int64_t purpose, int64_t n,
+                 const int64_t *root, const int64_t *path, const int64_t *draw,
+                 const int64_t *lane, const int64_t *epoch, const uint8_t *active,
+                 int64_t *out, void *stream);
+
+/* rollout.py:184-202 (child_path_keys). */
+int pbg_child_path(int64_t n, const int64_t *path, const int64_t *ordinal, int64_t *out,
+                   void *stream);
+
+/* rollout.py:205-234 (logical_uniform). */
+int pbg_logical_uniform(int64_t n, const int64_t *keys, float *out, void *stream);
+
+/* rollout.py:237-267 (logical_categorical): p [B,E] fp32, mass [B] or NULL. */
+int pbg_logical_categorical(int64_t B, int32_t E, const float *p, const int64_t *keys,
+                            const float *mass, int64_t *out, void *stream);
+
+/* ------------------------------------------------------- state machine */
+
+/* hooks.py:357-454 (PokerStateMachine.initial_roots); buttons may be NULL. */
+int pbg_initial_roots(pbg_geometry g, int64_t rows, int64_t seed, int64_t iteration,
+                      int64_t retry_epoch, int64_t logical_base, int64_t lane,
+                      const int32_t *buttons, pbg_state st, void *stream);
+
+/* hooks.py:464-510 (legality): mask [B,E] uint8. */
+int pbg_legality(pbg_geometry g, int64_t B, pbg_state st, uint8_t *mask, void *stream);
+
+/* hooks.py:456-462 (input_type): pre=0, post_A=A-1. */
+int pbg_input_type(pbg_geometry g, int64_t B, pbg_state st, int32_t *out, void *stream);
+
+/* hooks.py:883-979 (step_player), in place. */
+int pbg_step_player(pbg_geometry g, int64_t B, pbg_state st, const int32_t *action,
+                    void *stream);
+
+/* hooks.py:981-987 (needs_chance). */
+int pbg_needs_chance(pbg_geometry g, int64_t B, pbg_state st, uint8_t *out, void *stream);
+
+/* hooks.py:989-1074 (deal_next_street) with explicit keys [B,D]; active may
+ * be NULL. In place. */
+int pbg_deal_next_street(pbg_geometry g, int64_t B, pbg_state st, const int64_t *keys,
+                         const uint8_t *active, void *stream);
+
+/* hooks.py:1076-1126 (deal_next_street_keyed): CHANCE keys at (root, path)
+ * with draw*D + card ordinal.  retry/lane are [B]. */
+int pbg_deal_next_street_keyed(pbg_geometry g, int64_t B, pbg_state st, int64_t seed,
+                               int64_t iteration, const int64_t *root, const int64_t *path,
+                               int64_t draw, const int64_t *retry, const int64_t *lane,
+                               const uint8_t *active, void *stream);
+
+/* hooks.py:733-785 (append_player_history), from the pre-action state. */
+int pbg_append_player_history(pbg_geometry g, int64_t B, pbg_state st, const int32_t *action,
+                              pbg_history h, void *stream);
+
+/* hooks.py:787-810 (append_chance_history). */
+int pbg_append_chance_history(pbg_geometry g, int64_t B, pbg_state st, const uint8_t *active,
+                              pbg_history h, void *stream);
+
+/* hooks.py:1145-1216 (sampled_leaf) of every row treated as terminal. */
+int pbg_sampled_leaf(pbg_geometry g, int64_t B, pbg_state st, pbg_leaf leaf, void *stream);
+
+/* hooks.py:1128-1143 (combo_cards): out [n,2] int64. */
+int pbg_combo_cards(pbg_geometry g, int64_t n, const int32_t *ids, int64_t *out, void *stream);
+
+/* hooks.py:655-674 (_combo_class): out [H] int32. */
+int pbg_combo_class(pbg_geometry g, int32_t *out, void *stream);
+
+/* ----------------------------------------------------------- showdown */
+
+/* Contract-v2 evaluate_showdowns of the external poker_gpu_evaluator, as
+ * called at hooks.py:2277-2295: payoff[b,p] = baseline[b,p] + equal shares
+ * of amount[b,k] among the best 7-card hands of seats with level >= k.
+ * Category order per deck follows cards.py:37-74 (category_profile). */
+int pbg_evaluate_showdowns(int32_t rank_count, int64_t B, int32_t P, int32_t strata,
+                           const uint8_t *board, const int32_t *combo, const int32_t *level,
+                           const float *baseline, const float *amount, float *out,
+                           void *stream);
+
+/* Best 7-card hand values (strength-major) for n hands: cards [n,7] int32. */
+int pbg_hand_values(int32_t rank_count, int64_t n, const int32_t *cards, int64_t *out,
+                    void *stream);
+
+/* ------------------------------------------------------------- policy */
+
+/* policy.py:113-204 (PokerPolicyOperator.probabilities): out [B*rows,E];
+ * mask [B,E] is shared by the `rows` policy rows of each hand. */
+int pbg_policy_probabilities(int64_t B, int32_t E, pbg_policy pol, const uint8_t *mask,
+                             float *out, void *stream);
+
+/* policy.py:206-233 (selected_log_pi) for every policy row: out [B*rows]. */
+int pbg_policy_selected_log_pi(int64_t B, int32_t E, pbg_policy pol, const uint8_t *mask,
+                               const int32_t *action, float *out, void *stream);
+
+/* policy.py:235-244 (policy_reductions) without reference: entropy [B*rows]. */
+int pbg_policy_entropy(int64_t B, int32_t E, pbg_policy pol, const uint8_t *mask,
+                       float *out, void *stream);
+
+/* policy.py:246-282 (sample_actor): hand [B] selects the row of each hand. */
+int pbg_policy_sample_actor(int64_t B, int32_t E, pbg_policy pol, const uint8_t *mask,
+                            const int32_t *hand, const int64_t *keys, int32_t *action,
+                            float *selected_log, void *stream);
+
+/* ------------------------------------------------------ fused rollout */
+
+/* One fused sampled rollout step for B independent hands (warp per hand),
+ * composing rollout.py:1604-1621 (ACTION key at draw 0), hooks.py:1489-1541
+ * (sample at the owner's private row), hooks.py:1656-1700 (history,
+ * step_player, three keyed chance generations), hooks.py:1145-1216 (leaf
+ * payload of rows that became terminal) and hooks.py:1870 (child path).
+ *
+ * root_path [B,2] holds (root, path); path is replaced by its child for
+ * every row that acted.  Rows whose terminal flag is already set are left
+ * untouched and emit action -1.  pol rows: 1 = raw already at the actor's
+ * row; otherwise rows >= H and the row is the actor's preflop class
+ * (street 0, row < K) or compact combo (later streets).
+ *
+ * decision [B,4] int32 (may be NULL) receives (actor, street_before,
+ * raise_lo_tick, raise_hi_tick | call_legal<<16) for pbg_reach_update.
+ * leaf columns are written only for rows that became terminal; new_leaf[B]
+ * flags them. */
+int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist,
+                     int64_t *root_path, const int64_t *lane, const int64_t *retry_epoch,
+                     int64_t seed, int64_t iteration, pbg_policy pol, int32_t *action,
+                     float *selected_log, int32_t *decision, uint8_t *new_leaf, pbg_leaf leaf,
+                     void *stream);
+
+/* hooks.py:1641-1656 and 1688-1703: add the selected action's log policy of
+ * every private hand to the actor's log-reach row, then mask hands whose
+ * cards meet the (post-chance) board with -inf for every seat.
+ * log_reach [B,P,H]; pol has rows >= H (class rows used preflop). */
+int pbg_reach_update(pbg_geometry g, int64_t B, pbg_state st, pbg_policy pol,
+                     const int32_t *action, const int32_t *decision, float *log_reach,
+                     void *stream);
+
+/* ---------------------------------------------------------------- loss */
+
+/* Fused categorical PPO loss backward (masked log-softmax, clipped /
+ * negative-advantage-capped ratio, entropy bonus, per-row decision-mass
+ * weight, dlogits) in one HBM pass: pbg/core/learner.py:2021-2077 with the
+ * categorical policy of tests/categorical_policy_fixture.py:33-57.
+ *
+ * logits [N,A] (dtype 0=fp32, 1=bf16), mask [N,A] uint8, action [N] int32,
+ * old_logp/adv/weight [N] fp32.  dlogits [N,A] in the logits dtype.
+ * controls (device fp32[5]): clip, log_cap, ent_coef, scale, inv_count.
+ * partials: caller scratch of pbg_ppo_partials_size(N) doubles; stats
+ * (device double[8]) receives total, sum w*policy, sum w*entropy,
+ * sum w*approx_kl, clip count, neg-cap count, sum w, rows. A in [1,32]. */
+int64_t pbg_ppo_partials_size(int64_t N, int32_t A);
+int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void *logits,
+                                 const uint8_t *mask, const int32_t *action,
+                                 const float *old_logp, const float *adv, const float *weight,
+                                 const float *controls, void *dlogits, double *partials,
+                                 double *stats, void *stream);
+
+/* ---------------------------------------------------------------- Adam */
+
+/* optimization.py:182-233 (adam_transition) for one lane of a flat fp32
+ * master/grad/moment set of n parameters.  controls (device fp32[10]):
+ * lr, beta1, beta2, eps, decay, clip, scale, growth, backoff, interval;
+ * decoupled selects AdamW.  step (device int64[1]) advances when applied.
+ * partials: caller scratch of pbg_adam_partials_size(n) doubles.
+ * report (device double[4]): applied, finite, norm, clip scale. */
+int64_t pbg_adam_partials_size(int64_t n);
+int pbg_adam_step(int64_t n, float *master, float *grad, float *first, float *second,
+                  const float *controls, int64_t *step, int32_t decoupled, double *partials,
+                  double *report, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PBGB200_H */

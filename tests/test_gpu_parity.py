@@ -1,0 +1,521 @@
+"""GPU parity: libpbgb200 (through its C ABI) against the oracle and golden vectors.
+
+Bars: bit-exact for keys, cards, legal masks, chip columns, history and
+leaf payloads; sampled actions equal except at documented near-ties (the
+threshold within 1e-5 of the row mass of a CDF edge, where a different fp32
+summation order legitimately flips the bin -- counted and bounded here);
+policy probabilities within the reference's own 1e-6 / 1e-5; fp32 loss
+gradients within rtol 1e-5 and bf16 within 2e-2.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def cuda(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.to(DEV)
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+# ------------------------------------------------------------------ RNG
+
+
+def test_rng_matches_reference_golden(gold):
+    from pbg_b200 import rng
+
+    g = gold("rng")
+    for i, (seed, iteration, purpose) in enumerate(g["rng_scalars"]):
+        keys = rng.logical_rng_keys(seed=int(seed), iteration=int(iteration), purpose=int(purpose),
+                                    root=cuda(g["rng_root"][i]), path=cuda(g["rng_path"][i]),
+                                    draw=cuda(g["rng_draw"][i]), lane=cuda(g["rng_lane"][i]),
+                                    retry_epoch=cuda(g["rng_epoch"][i]),
+                                    active=cuda(g["rng_active"][i]).bool())
+        np.testing.assert_array_equal(host(keys), g["rng_keys"][i])
+        child = rng.child_path_keys(cuda(g["rng_path"][i]), cuda(g["rng_child_ordinal"][i]))
+        np.testing.assert_array_equal(host(child), g["rng_child"][i])
+    np.testing.assert_array_equal(host(rng.logical_uniform(cuda(g["rng_uniform_keys"]))), g["rng_uniform"])
+    sel = host(rng.logical_categorical(cuda(g["cat_prob"]), cuda(g["cat_keys"])))
+    ref, margin = O.categorical(g["cat_prob"], g["cat_keys"], with_margin=True)
+    np.testing.assert_array_equal(sel, ref)
+    endpoint = torch.tensor([((1 << 24) - 1) << 39], dtype=torch.int64, device=DEV)
+    assert float(rng.logical_uniform(endpoint)[0]) < 1.0
+    assert int(rng.logical_categorical(torch.tensor([[1.0, 0.0]], device=DEV), endpoint)[0]) == 0
+
+
+def test_rng_is_invariant_to_order_and_subdivision():
+    """test_rollout_transactions.py:548-620 properties."""
+
+    from pbg_b200 import rng
+
+    root = torch.tensor([3, 5, 8, 13, 21, 34], dtype=torch.int64, device=DEV)
+    path = torch.arange(6, dtype=torch.int64, device=DEV)
+    lane = torch.tensor([2, 0, 1, 2, 0, 1], dtype=torch.int64, device=DEV)
+    keys = rng.logical_rng_keys(seed=91, iteration=7, root=root, path=path, draw=4, purpose=4, lane=lane)
+    order = torch.tensor([4, 1, 5, 0, 3, 2], device=DEV)
+    perm = rng.logical_rng_keys(seed=91, iteration=7, root=root[order], path=path[order], draw=4, purpose=4,
+                                lane=lane[order])
+    rebuilt = torch.empty_like(keys)
+    rebuilt[order] = perm
+    assert torch.equal(keys, rebuilt)
+    split = torch.cat([rng.logical_rng_keys(seed=91, iteration=7, root=root[s], path=path[s], draw=4, purpose=4,
+                                            lane=lane[s]) for s in (slice(0, 2), slice(2, 6))])
+    assert torch.equal(keys, split)
+    assert not torch.equal(keys, rng.logical_rng_keys(seed=91, iteration=7, root=root, path=path, draw=4,
+                                                      purpose=5, lane=lane))
+
+
+# ------------------------------------------------------- state machine
+
+STATE_MAP = {"board_cards": "board", "combo_ids": "combo", "button": "button", "street": "street",
+             "to_act": "to_act", "stacks": "stacks", "committed": "committed",
+             "committed_street": "committed_street", "status": "status", "current_bet": "current_bet",
+             "last_full_raise": "last_full_raise", "pending": "pending", "can_raise": "can_raise",
+             "terminal": "terminal"}
+
+
+def _dev_state(cols, rows=None):
+    from pbg_b200.poker import PokerState
+
+    dtypes = {"board_cards": torch.uint8, "combo_ids": torch.int32, "button": torch.int32, "street": torch.int32,
+              "to_act": torch.int32, "stacks": torch.float32, "committed": torch.float32,
+              "committed_street": torch.float32, "status": torch.int8, "current_bet": torch.float32,
+              "last_full_raise": torch.float32, "pending": torch.bool, "can_raise": torch.bool,
+              "terminal": torch.bool}
+    sel = (lambda v: v) if rows is None else (lambda v: v[rows])
+    return PokerState(*(cuda(sel(cols[n])).to(dtypes[n]) for n in STATE_MAP))
+
+
+@pytest.mark.parametrize("gi", range(7))
+def test_state_machine_replays_reference_trajectories(gold, gi):
+    from pbg_b200.poker import HISTORY_FIELDS, NLHEGeometry, PokerHistory, PokerStateMachine
+    from pbg_b200.rng import child_path_keys
+
+    g = gold("poker")
+    tag = f"g{gi}"
+    players, stack, ranks = g[f"{tag}_geometry"]
+    geometry = NLHEGeometry(int(players), float(stack), int(ranks))
+    m = PokerStateMachine(geometry)
+    seed, iteration, retry, base, lane, B = (int(x) for x in g[f"{tag}_root_args"])
+    s = m.initial_roots(B, seed=seed, iteration=iteration, retry_epoch=retry, logical_base=base, lane=lane,
+                        device=DEV)
+    for ref, mine in STATE_MAP.items():
+        np.testing.assert_array_equal(host(getattr(s, ref)).astype(np.float64),
+                                      g[f"{tag}_root_{ref}"].astype(np.float64), err_msg=ref)
+    np.testing.assert_array_equal(host(m._combo_class(DEV)), g[f"{tag}_combo_class"])
+    cols = {n: g[f"{tag}_root_{n}"].copy() for n in STATE_MAP}
+    h = m.empty_history(B, DEV)
+    hist = {n: host(getattr(h, n)).copy() for n in HISTORY_FIELDS}
+    path = np.zeros(B, dtype=np.int64)
+    root = np.arange(base, base + B, dtype=np.int64)
+    E = int(g[f"{tag}_mask_events"][0])
+    masks = np.unpackbits(g[f"{tag}_masks"], axis=-1)[..., :E].astype(bool)
+    for t, action in enumerate(g[f"{tag}_actions"]):
+        rows = np.nonzero(action >= 0)[0]
+        sub = _dev_state(cols, rows)
+        np.testing.assert_array_equal(host(m.legality(sub).mask), masks[t][rows])
+        sub_h = PokerHistory(*(cuda(hist[n][rows]) for n in HISTORY_FIELDS))
+        act = cuda(action[rows])
+        sub_h = m.append_player_history(sub, act, sub_h)
+        nxt = m.step_player(sub, act)
+        r, p = cuda(root[rows]), cuda(path[rows])
+        for generation in range(3):
+            active = m.needs_chance(nxt)
+            sub_h = m.append_chance_history(nxt, active, sub_h)
+            nxt = m.deal_next_street_keyed(nxt, seed=seed, iteration=iteration, root=r, path=p, draw=generation,
+                                           retry_epoch=retry, lane=lane)
+        for n in STATE_MAP:
+            cols[n][rows] = host(getattr(nxt, n))
+            np.testing.assert_array_equal(cols[n].astype(np.float64), g[f"{tag}_post_{n}"][t].astype(np.float64),
+                                          err_msg=f"step {t} {n}")
+        for n in HISTORY_FIELDS:
+            hist[n][rows] = host(getattr(sub_h, n))
+        path[rows] = host(child_path_keys(p, 1))
+    for n in HISTORY_FIELDS:
+        np.testing.assert_array_equal(hist[n].astype(np.float64), g[f"{tag}_history_{n}"].astype(np.float64),
+                                      err_msg=n)
+    leaf = m.sampled_leaf(_dev_state(cols))
+    for k, v in leaf.items():
+        np.testing.assert_array_equal(host(v), g[f"{tag}_leaf_{k}"], err_msg=k)
+
+
+def test_explicit_key_deal_and_combo_cards():
+    from pbg_b200.poker import NLHEGeometry, PokerStateMachine
+
+    geometry = NLHEGeometry(2, 8.0, 13)
+    m = PokerStateMachine(geometry)
+    om = O.Machine(O.Geometry(2, 8.0, 13))
+    s = m.initial_roots(64, seed=209559, iteration=1, retry_epoch=0, device=DEV)
+    os_ = om.initial_roots(64, seed=209559, iteration=1, retry_epoch=0)
+    gen = 0
+    while not bool(s.terminal.all()):
+        if bool(m.needs_chance(s).all()):
+            keys = torch.arange(52, dtype=torch.int64, device=DEV)[None].expand(64, -1) + gen * 52 + 1
+            s = m.deal_next_street(s, keys.contiguous())
+            os_ = om.deal_next_street(os_, host(keys))
+            gen += 1
+        else:
+            a = torch.full((64,), 1, dtype=torch.int32, device=DEV)
+            s = m.step_player(s, a)
+            os_ = om.step_player(os_, host(a))
+    assert gen == 3
+    for ref, mine in STATE_MAP.items():
+        np.testing.assert_array_equal(host(getattr(s, ref)).astype(np.float64),
+                                      getattr(os_, mine).astype(np.float64), err_msg=ref)
+    ids = torch.arange(geometry.private_hands, dtype=torch.int32, device=DEV)
+    np.testing.assert_array_equal(host(m.combo_cards(ids)), om.combo_cards(host(ids)))
+
+
+# ------------------------------------------------------------- policy
+
+
+@pytest.mark.parametrize("name", ["small", "hu8", "hu100", "six50"])
+def test_policy_matches_reference_golden(gold, name):
+    from pbg_b200.poker import PokerLegality
+    from pbg_b200.policy import PokerPolicyOperator
+
+    g = gold("policy")
+    raw = {k: cuda(g[f"pol_{name}_{k}"]) for k in ("type_logits", "omega", "mu", "s", "iota")}
+    mask = cuda(g[f"pol_{name}_mask"]).bool()
+    B, E = mask.shape
+    legality = PokerLegality(torch.arange(E, dtype=torch.int32, device=DEV)[None].expand(B, -1).contiguous(), mask)
+    op = PokerPolicyOperator()
+    prob = host(op.probabilities(raw, legality))
+    np.testing.assert_allclose(prob, g[f"pol_{name}_prob"], atol=1e-6, rtol=1e-5)
+    sample = op.sample_actor(raw, legality, cuda(g[f"pol_{name}_hand"]), cuda(g[f"pol_{name}_keys"]))
+    action = host(sample.action)
+    _, _, margin = O.sample_actor({k: g[f"pol_{name}_{k}"] for k in ("type_logits", "omega", "mu", "s", "iota")},
+                                  g[f"pol_{name}_mask"], g[f"pol_{name}_hand"], g[f"pol_{name}_keys"],
+                                  with_margin=True)
+    same = action == g[f"pol_{name}_action"]
+    assert np.all(margin[~same] < 1e-5)
+    np.testing.assert_allclose(host(sample.selected_log_policy)[same], g[f"pol_{name}_selected"][same],
+                               atol=1e-5, rtol=1e-5)
+    sel_all = host(op.selected_log_pi(raw, legality, cuda(g[f"pol_{name}_action"])))
+    np.testing.assert_allclose(sel_all, g[f"pol_{name}_selected_all"], atol=1e-5, rtol=1e-5)
+    entropy, kl = op.policy_reductions(raw, legality, raw)
+    np.testing.assert_allclose(host(entropy), g[f"pol_{name}_entropy"], atol=2e-6, rtol=2e-5)
+    np.testing.assert_allclose(host(kl), 0.0, atol=2e-7)
+
+
+# ----------------------------------------------------------- showdown
+
+
+@pytest.mark.parametrize("ranks,players", [(13, 2), (13, 6), (8, 3), (5, 2), (4, 2), (9, 4)])
+def test_showdown_matches_oracle(ranks, players):
+    import poker_gpu_evaluator as poker
+
+    rng = np.random.default_rng(ranks * 10 + players)
+    B = 3000
+    D = 4 * ranks
+    first = 52 - D
+    geom = O.Geometry(players, 8.0, ranks)
+    m = O.Machine(geom)
+    deal = np.argsort(rng.random((B, D)), axis=1)[:, : 5 + 2 * players] + first
+    board = deal[:, :5].astype(np.uint8)
+    hole = deal[:, 5:].reshape(B, players, 2)
+    combo = m.combo_id(hole[..., 0], hole[..., 1])
+    level = np.where(rng.random((B, players)) < 0.2, -1, 0).astype(np.int32)
+    level[:, 0] = 0
+    base = -rng.integers(1, 16, (B, players)).astype(np.float32)
+    amount = np.zeros((B, players), np.float32)
+    amount[:, 0] = -base.sum(1)
+    ref = O.evaluate_showdowns(ranks, board, combo, level, base, amount)
+    ev = poker.bind(ranks)
+    out = ev.evaluate_showdowns(board_cards=cuda(board), combo_ids=cuda(combo), stratum_level=cuda(level),
+                                payoff_baseline=cuda(base), stratum_amount=cuda(amount))
+    np.testing.assert_array_equal(host(out), ref)
+    np.testing.assert_allclose(host(out).sum(1), 0.0, atol=1e-3)
+    # hand values directly: every 7-card hand against the brute-force oracle
+    from pbg_b200._native import call, ptr, stream
+    cards = np.concatenate([board.astype(np.int32), hole[:, 0, :].astype(np.int32)], 1)
+    got = torch.empty(B, dtype=torch.int64, device=DEV)
+    call("pbg_hand_values", ranks, B, ptr(cuda(cards)), ptr(got), stream())
+    want = np.array([O.hand_value7(ranks, c) for c in cards])
+    np.testing.assert_array_equal(host(got), want)
+
+
+# ------------------------------------------------------ fused rollout
+
+
+def _random_raw(gen, rows_shape, M):
+    t = lambda *s: torch.randn(*s, generator=gen)
+    return {
+        "type_logits": t(*rows_shape, 3) * 1.5,
+        "omega": torch.softmax(t(*rows_shape, M), -1),
+        "mu": torch.sigmoid(t(*rows_shape, M)),
+        "s": torch.nn.functional.softplus(t(*rows_shape, M)) + 0.02,
+        "iota": torch.sigmoid(t(*rows_shape)),
+    }
+
+
+@pytest.mark.parametrize("players,stack,ranks,full_rows", [(2, 8.0, 4, False), (3, 8.0, 4, True),
+                                                           (2, 100.0, 13, False), (6, 20.0, 13, True),
+                                                           (6, 100.0, 13, False)])
+def test_fused_rollout_step_matches_oracle(players, stack, ranks, full_rows):
+    from pbg_b200.poker import HISTORY_FIELDS, NLHEGeometry
+    from pbg_b200.rollout import RolloutStep
+
+    geometry = NLHEGeometry(players, stack, ranks)
+    B = 96 if full_rows and ranks == 13 else (192 if players == 6 else 384)
+    seed, iteration, M = 4242 + players, 5, 2
+    stepper = RolloutStep(geometry, seed=seed, iteration=iteration)
+    arena = stepper.roots(B, device=DEV, retry_epoch=1, logical_base=1000, lane=1)
+    om = O.Machine(O.Geometry(players, stack, ranks))
+    os_ = om.initial_roots(B, seed=seed, iteration=iteration, retry_epoch=1, logical_base=1000, lane=1)
+    oh = om.empty_history(B)
+    path = np.zeros(B, np.int64)
+    root = np.arange(1000, 1000 + B, dtype=np.int64)
+    H = geometry.private_hands
+    cls = om.combo_class()
+    log_reach = torch.zeros((B, players, H), device=DEV)
+    oracle_reach = np.zeros((B, players, H), np.float32)
+    gen = torch.Generator().manual_seed(players * 100 + ranks)
+    near_ties = 0
+    decisions = 0
+    for step in range(400):
+        active = ~os_.terminal.astype(bool)
+        if not active.any():
+            break
+        rows_shape = (B, H) if full_rows else (B, 1)
+        raw = _random_raw(gen, rows_shape, M)
+        stepper.step(arena, {k: v.to(DEV) for k, v in raw.items()})
+        if full_rows:
+            stepper.reach_update(arena, {k: v.to(DEV) for k, v in raw.items()}, log_reach)
+        g_action = host(arena.action)
+        rows = np.nonzero(active)[0]
+        sub = O.State(**{n: np.ascontiguousarray(getattr(os_, n)[rows]) for n in STATE_MAP.values()})
+        mask = om.legality(sub)
+        actor = sub.to_act
+        combo = sub.combo[np.arange(rows.size), actor]
+        if full_rows:
+            hand = np.where(sub.street == 0, cls[combo], combo)
+        else:
+            hand = np.zeros(rows.size, np.int64)
+        keys = O.rng_keys(seed=seed, iteration=iteration, purpose=O.ACTION, root=root[rows], path=path[rows],
+                          draw=0, lane=1, retry_epoch=1)
+        raw_np = {k: v.numpy()[rows] for k, v in raw.items()}
+        o_action, o_logp, margin = O.sample_actor(raw_np, mask, hand, keys, with_margin=True)
+        mismatch = o_action != g_action[rows]
+        assert np.all(margin[mismatch] < 1e-5), f"step {step}: non-tie action mismatch"
+        near_ties += int(mismatch.sum())
+        decisions += rows.size
+        action = g_action[rows].astype(np.int32)  # follow the device on near-ties
+        assert np.all(g_action[~active] == -1)
+        same = ~mismatch
+        np.testing.assert_allclose(host(arena.selected_log)[rows][same], o_logp[same], rtol=1e-5, atol=1e-5)
+        if full_rows:
+            # hooks.py:1641-1703: the actor's reach row gains log pi(action) of every hand
+            probs = O.policy_probabilities(raw_np, mask)
+            sel = np.log(np.maximum(probs[np.arange(rows.size)[:, None], np.arange(H)[None], action[:, None]],
+                                    np.float32(1e-12)))
+            pre = sub.street == 0
+            sel_hand = np.where(pre[:, None], sel[:, cls], sel)
+            oracle_reach[rows, actor] += sel_hand
+        sub_h = O.History(**{n: np.ascontiguousarray(getattr(oh, n)[rows]) for n in O.History.NAMES})
+        nxt, sub_h, child = O.rollout_transition(om, sub, sub_h, action, seed=seed, iteration=iteration,
+                                                 root=root[rows], path=path[rows], retry_epoch=1, lane=1)
+        for n in STATE_MAP.values():
+            getattr(os_, n)[rows] = getattr(nxt, n)
+        for n in O.History.NAMES:
+            getattr(oh, n)[rows] = getattr(sub_h, n)
+        path[rows] = child
+        for ref, mine in STATE_MAP.items():
+            np.testing.assert_array_equal(host(getattr(arena.state, ref)).astype(np.float64),
+                                          getattr(os_, mine).astype(np.float64), err_msg=f"step {step} {ref}")
+        np.testing.assert_array_equal(host(arena.root_path[:, 1]), path)
+        if full_rows:
+            board = os_.board
+            cards = om.combo_cards(np.arange(H))
+            conflict = ((board[:, None, :, None] != 255) & (board[:, None, :, None] == cards[None, :, None, :])).any((2, 3))
+            oracle_reach = np.where(conflict[:, None, :], -np.inf, oracle_reach).astype(np.float32)
+            got = host(log_reach)
+            np.testing.assert_array_equal(np.isinf(got), np.isinf(oracle_reach))
+            finite = np.isfinite(oracle_reach)
+            np.testing.assert_allclose(got[finite], oracle_reach[finite], rtol=1e-5, atol=1e-4)
+        new = host(arena.new_leaf).astype(bool)
+        ended = new & active
+        assert np.array_equal(new[active], os_.terminal[active].astype(bool))
+        if ended.any():
+            oleaf = om.sampled_leaf(O.State(**{n: np.ascontiguousarray(getattr(os_, n)[ended]) for n in STATE_MAP.values()}))
+            for k, v in arena.leaf.items():
+                np.testing.assert_array_equal(host(v)[ended], oleaf[k], err_msg=k)
+    assert os_.terminal.all()
+    for n in HISTORY_FIELDS:
+        np.testing.assert_array_equal(host(getattr(arena.history, n)).astype(np.float64),
+                                      getattr(oh, n).astype(np.float64), err_msg=n)
+    # near-ties are rare; report the rate through the assertion message
+    assert near_ties <= max(2, decisions // 1000), f"{near_ties} near-tie flips in {decisions} decisions"
+
+
+def test_rollout_is_independent_of_batching():
+    """Hands addressed by (root, path) evolve identically alone or in a batch."""
+
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.rollout import RolloutStep
+
+    geometry = NLHEGeometry(2, 8.0, 4)
+    stepper = RolloutStep(geometry, seed=7, iteration=2)
+    full = stepper.roots(64, device=DEV, logical_base=0)
+    part = stepper.roots(16, device=DEV, logical_base=32)
+    gen = torch.Generator().manual_seed(3)
+    for _ in range(40):
+        raw = _random_raw(gen, (64, 1), 2)
+        stepper.step(full, {k: v.to(DEV) for k, v in raw.items()})
+        stepper.step(part, {k: v[32:48].to(DEV) for k, v in raw.items()})
+    for ref in STATE_MAP:
+        assert torch.equal(getattr(full.state, ref)[32:48], getattr(part.state, ref)), ref
+
+
+# --------------------------------------------------------------- loss
+
+
+def _loss_inputs(N, A, seed, cap_rows=True):
+    rng = np.random.default_rng(seed)
+    logits = rng.standard_normal((N, A)).astype(np.float32)
+    mask = rng.random((N, A)) < 0.7
+    mask[~mask.any(1), 0] = True
+    if N > 4:
+        mask[1] = False
+        mask[1, A - 1] = True  # single legal action
+        mask[2] = True
+    action = np.array([rng.choice(np.nonzero(m)[0]) for m in mask], dtype=np.int32)
+    pert = logits + rng.standard_normal((N, A)).astype(np.float32) * np.float32(0.1)
+    if cap_rows:
+        pert[: N // 4] += rng.standard_normal((N // 4, A)).astype(np.float32) * np.float32(1.5)
+    masked = np.where(mask, pert, -np.inf)
+    mx = masked.max(1, keepdims=True)
+    lse = np.log(np.exp(masked - mx).sum(1)) + mx[:, 0]
+    old = (masked[np.arange(N), action] - lse).astype(np.float32)
+    adv = rng.standard_normal(N).astype(np.float32)
+    weight = rng.uniform(0.0, 1.0, N).astype(np.float32)
+    return logits, mask, action, old, adv, weight
+
+
+@pytest.mark.parametrize("A,cap", [(8, None), (8, 1.5), (3, None), (17, 2.0), (1, None)])
+def test_fp32_loss_backward_matches_oracle(A, cap):
+    from pbg_b200.loss import LossConfig, fused_ppo_backward
+
+    N = 5000
+    logits, mask, action, old, adv, weight = _loss_inputs(N, A, 11 + A)
+    cfg = LossConfig(0.2, cap, 0.01)
+    d, stats = fused_ppo_backward(cuda(logits), cuda(mask), cuda(action), cuda(old), cuda(adv), cuda(weight), cfg)
+    ref_d, ref_s = O.ppo_categorical(logits, mask, action, old, adv, weight,
+                                     log_cap=math.inf if cap is None else math.log(cap))
+    scale = np.abs(ref_d).max() + 1e-30
+    np.testing.assert_allclose(host(d), ref_d, rtol=1e-5, atol=1e-5 * scale)
+    np.testing.assert_allclose(host(stats)[[0, 1, 2, 3, 6, 7]], ref_s[[0, 1, 2, 3, 6, 7]], rtol=1e-5, atol=1e-6)
+    assert abs(host(stats)[4] - ref_s[4]) <= 2 and abs(host(stats)[5] - ref_s[5]) <= 2
+
+
+def test_loss_matches_reference_autograd_golden(gold):
+    from pbg_b200.loss import LossConfig, fused_ppo_backward
+
+    g = gold("loss")
+    N = g["loss_logits"].shape[0]
+    for ci in (0, 1):
+        cap = float(g[f"loss{ci}_cap"][0])
+        cfg = LossConfig(0.2, None if math.isinf(cap) else math.exp(cap), 0.01)
+        d, stats = fused_ppo_backward(cuda(g["loss_logits"]), cuda(g["loss_mask"]), cuda(g["loss_action"]),
+                                      cuda(g["loss_old"]), cuda(g["loss_adv"]), cuda(g["loss_weight"]), cfg)
+        np.testing.assert_allclose(host(d) * N, g[f"loss{ci}_grad"], rtol=1e-5, atol=1e-7)
+        w = g["loss_weight"].astype(np.float64)
+        np.testing.assert_allclose(host(stats)[0], (w * g[f"loss{ci}_row_total"]).sum() / N, rtol=1e-5)
+
+
+def test_bf16_vector_path_matches_torch_fp32_autograd():
+    """The A=8 bf16 kernel against a plain PyTorch fp32 autograd restatement."""
+
+    from pbg_b200.loss import LossConfig, fused_ppo_backward
+
+    N, A = 1 << 16, 8
+    logits, mask, action, old, adv, weight = _loss_inputs(N, A, 99)
+    x16 = cuda(logits).to(torch.bfloat16)
+    d, stats = fused_ppo_backward(x16, cuda(mask), cuda(action), cuda(old), cuda(adv), cuda(weight),
+                                  LossConfig(0.2, 2.0, 0.01))
+    x = x16.float().clone().requires_grad_()
+    m = cuda(mask)
+    z = x.masked_fill(~m, -torch.inf)
+    lp = torch.log_softmax(z, -1)
+    sel = lp.gather(1, cuda(action).long()[:, None])[:, 0]
+    p = torch.softmax(z, -1)
+    ent = -(torch.where(m, p * lp, torch.zeros_like(p))).sum(-1)
+    lr = sel - cuda(old)
+    ratio = lr.exp()
+    clipped = ratio.clamp(0.8, 1.2)
+    a = cuda(adv)
+    neg = torch.minimum(lr, torch.full_like(lr, math.log(2.0))).exp()
+    pr = torch.where(a < 0, neg, ratio)
+    prow = -torch.minimum(pr * a, clipped * a)
+    total = (cuda(weight) * (prow - 0.01 * ent)).sum() / N
+    total.backward()
+    ref = x.grad
+    got = d.float()
+    scale = ref.abs().max()
+    torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-2 * float(scale))
+    torch.testing.assert_close(torch.tensor(float(stats[0])), total.detach().cpu().double().float(), rtol=1e-4,
+                               atol=1e-6)
+
+
+def test_loss_edge_shapes():
+    from pbg_b200.loss import LossConfig, fused_ppo_backward
+
+    # empty batch: stats are zero, nothing is written
+    z = torch.zeros((0, 8), dtype=torch.bfloat16, device=DEV)
+    e = torch.zeros(0, device=DEV)
+    d, stats = fused_ppo_backward(z, torch.zeros((0, 8), dtype=torch.bool, device=DEV),
+                                  torch.zeros(0, dtype=torch.int32, device=DEV), e, e, e, LossConfig(), inv_count=1.0)
+    assert float(stats.abs().sum()) == 0.0
+    # unaligned rows fall back to the scalar path with identical results
+    N = 1001
+    logits, mask, action, old, adv, weight = _loss_inputs(N + 1, 8, 5)
+    base = cuda(logits).to(torch.bfloat16)
+    d_aligned, _ = fused_ppo_backward(base[1:].contiguous(), cuda(mask[1:]), cuda(action[1:]), cuda(old[1:]),
+                                      cuda(adv[1:]), cuda(weight[1:]))
+    flat = torch.empty((N + 1) * 8 + 1, dtype=torch.bfloat16, device=DEV)
+    view = flat[1:1 + N * 8].view(N, 8)
+    view.copy_(base[1:])
+    d_unaligned, _ = fused_ppo_backward(view, cuda(mask[1:]), cuda(action[1:]), cuda(old[1:]), cuda(adv[1:]),
+                                        cuda(weight[1:]))
+    assert torch.equal(d_aligned, d_unaligned)
+
+
+# --------------------------------------------------------------- Adam
+
+
+def test_adam_matches_reference_golden(gold):
+    from pbg_b200.optim import FlatAdam
+
+    g = gold("adam")
+    c = g["adam_controls"][0]
+    opt = FlatAdam(cuda(g["adam_master0"][0]).clone(), lr=float(c[0]), beta1=float(c[1]), beta2=float(c[2]),
+                   epsilon=float(c[3]), decay=float(c[4]), clip=float(c[5]), scale=float(c[6]))
+    for s in range(3):
+        opt.grad.copy_(cuda(g["adam_grad_in"][s][0]))
+        report = host(opt.step())
+        assert report[0] == 1.0
+        np.testing.assert_allclose(host(opt.master), g["adam_master"][s][0], rtol=1e-5, atol=1e-7)
+        np.testing.assert_allclose(host(opt.first), g["adam_first"][s][0], rtol=1e-5, atol=1e-9)
+        np.testing.assert_allclose(host(opt.second), g["adam_second"][s][0], rtol=1e-4, atol=1e-12)
+        np.testing.assert_allclose(host(opt.grad), g["adam_grad_out"][s][0], rtol=1e-5, atol=1e-9)
+    # a non-finite gradient leaves the state untouched and zeroes the gradient
+    before = opt.master.clone()
+    opt.grad.fill_(1.0)
+    opt.grad[7] = float("nan")
+    report = host(opt.step())
+    assert report[0] == 0.0 and torch.equal(opt.master, before) and float(opt.grad.abs().sum()) == 0.0
+    assert int(opt.step_count[0]) == 3
