@@ -8,12 +8,24 @@
 // bounds are restated exactly, so the gradient is the reference's autograd
 // gradient, not an approximation of it.
 //
+// Algebra used to keep the row cheap (x logits, legal set L, e_j =
+// exp(x_j - max) on L and 0 off L, s = sum e, lse = max + log s,
+// p_j = e_j / s):
+//   entropy       H      = lse - sum_j p_j x_j
+//   d lp_a / d x_j       = [j == a] - p_j
+//   d H / d x_j          = -p_j (x_j - lse + H)
+//   d total / d x_j      = coef * ( g [j == a] + p_j (c x_j + c (H - lse) - g) )
+// with g = d policy_row / d log_ratio and c the entropy coefficient; illegal
+// entries vanish through e_j = 0.  Exponentials and logarithms run base 2 on
+// the special-function unit (exp2f, __log2f: documented CUDA functions with a
+// few-ulp error), about 1e-6 relative on the gradient.
+//
 // Layout: logits/dlogits [N,A] (bf16 or fp32), mask [N,A] u8, action [N]
-// i32, old_logp/adv/weight [N] f32.  For A == 8 with 16-byte aligned rows
-// one thread moves a whole row with 16/8/16-byte vector accesses (56 B per
-// row with bf16 logits); other shapes take a scalar path.  Per-block loss
-// statistics go to a caller scratch array and are summed in a fixed order by
-// a one-block finalise kernel, so results are deterministic.
+// i32, old_logp/adv/weight [N] f32.  For A == 8 with aligned rows one thread
+// moves a whole row with 16/8/16-byte accesses (56 B per row with bf16
+// logits) and prefetches the next row before computing the current one.
+// Per-block statistics go to caller scratch; the last block to finish sums
+// them in block order (deterministic) and clears the arrival counter.
 #include <cuda_bf16.h>
 
 #include "pbg_common.cuh"
@@ -23,15 +35,18 @@ namespace pbg {
 constexpr int LOSS_BLOCK = 256;
 constexpr int LOSS_STATS = 8;
 constexpr int LOSS_MAX_A = 32;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
 
 struct LossControls {
-    float clip, cap, cent, coef_scale;  // coef_scale = scale * inv_count
+    float clip, cap, exp_cap, cent, coef_scale;  // coef_scale = scale * inv_count
 };
 
 __device__ __forceinline__ LossControls load_controls(const float* c) {
     LossControls k;
     k.clip = c[0];
     k.cap = c[1];
+    k.exp_cap = expf(c[1]);
     k.cent = c[2];
     k.coef_scale = c[3] * c[4];
     return k;
@@ -45,14 +60,16 @@ struct RowStats {
     }
 };
 
-// d(policy_row)/d(log_ratio) and the row's policy loss (learner.py:2021-2047).
+// Row objective pieces from the log ratio (learner.py:2021-2047): returns
+// g = d policy_row / d log_ratio and writes policy_row and the ratio.
 __device__ __forceinline__ float ratio_terms(float lr, float adv, const LossControls& k, float& prow,
                                              float& ratio_out) {
-    float ratio = expf(lr);
+    float ratio = exp2f(lr * LOG2E);
     float lo = 1.0f - k.clip, hi = 1.0f + k.clip;
     float clipped = fminf(fmaxf(ratio, lo), hi);
     bool negative = adv < 0.0f;
-    float neg_ratio = expf(fminf(lr, k.cap));
+    // exp(min(lr, cap)) without a second exponential
+    float neg_ratio = lr <= k.cap ? ratio : k.exp_cap;
     float pr = negative ? neg_ratio : ratio;
     float f1 = pr * adv, f2 = clipped * adv;
     prow = -fminf(f1, f2);
@@ -76,46 +93,55 @@ __device__ __forceinline__ void accumulate(RowStats& s, float coef, float w, flo
     s.v[7] += 1.0f;
 }
 
-// One row held in registers: x[j] logits, legal bitmask.
-template <int A>
-__device__ __forceinline__ void row_backward(float (&x)[A], unsigned legal, int act, float old, float adv, float w,
-                                             const LossControls& k, RowStats& s) {
-    float mx = -INFINITY;
+// One row in registers: x[j] logits (overwritten with dlogits), legal(j) flags.
+template <int A, class Legal>
+__device__ __forceinline__ void row_backward(float (&x)[A], const Legal& legal, int act, float old, float adv,
+                                             float w, const LossControls& k, RowStats& s) {
+    float my = -INFINITY;
     #pragma unroll
-    for (int j = 0; j < A; ++j) if ((legal >> j) & 1u) mx = fmaxf(mx, x[j]);
+    for (int j = 0; j < A; ++j) if (legal(j)) my = fmaxf(my, x[j] * LOG2E);
     float e[A];
-    float se = 0.0f;
+    float se = 0.0f, sx = 0.0f, xa = 0.0f;
     #pragma unroll
     for (int j = 0; j < A; ++j) {
-        e[j] = ((legal >> j) & 1u) ? expf(x[j] - mx) : 0.0f;
+        bool on = legal(j);
+        e[j] = on ? exp2f(fmaf(x[j], LOG2E, -my)) : 0.0f;
         se += e[j];
+        sx = on ? fmaf(e[j], x[j], sx) : sx;  // masked logits may be -inf
+        xa = j == act ? x[j] : xa;
     }
-    float lse = mx + logf(se);
     float inv = __frcp_rn(se);
-    float ent = 0.0f, lpa = 0.0f;
-    #pragma unroll
-    for (int j = 0; j < A; ++j) {
-        float lp = x[j] - lse;
-        if ((legal >> j) & 1u) ent -= e[j] * inv * lp;
-        if (j == act) lpa = lp;
-        x[j] = lp;  // reuse as log-probability
-    }
-    float lr = lpa - old;
+    float lse = (my + __log2f(se)) * LN2;
+    float ent = lse - sx * inv;
+    float lr = (xa - lse) - old;
     float prow, ratio;
-    float dprow = ratio_terms(lr, adv, k, prow, ratio);
+    float g = ratio_terms(lr, adv, k, prow, ratio);
     float coef = k.coef_scale * w;
+    float pscale = inv * coef;
+    float K = k.cent * (ent - lse) - g;
+    float ga = coef * g;
     #pragma unroll
     for (int j = 0; j < A; ++j) {
-        float p = e[j] * inv;
-        float g = dprow * ((j == act ? 1.0f : 0.0f) - p) + k.cent * p * (x[j] + ent);
-        x[j] = ((legal >> j) & 1u) ? coef * g : 0.0f;  // reuse as dlogit
+        float d = legal(j) ? (e[j] * pscale) * fmaf(k.cent, x[j], K) : 0.0f;
+        x[j] = j == act ? d + ga : d;
     }
     accumulate(s, coef, w, prow, ent, ratio, lr, k, adv);
 }
 
-// Block reduction of the 8 statistics into partials[block*8 + i].
-__device__ __forceinline__ void block_stats(RowStats& s, double* partials) {
+struct Legal8 {  // 8 bool bytes (0/1) packed in a uint2
+    uint2 m;
+    __device__ bool operator()(int j) const { return ((j < 4 ? m.x >> (8 * j) : m.y >> (8 * (j - 4))) & 0xffu) != 0; }
+};
+
+struct LegalBits {
+    unsigned bits;
+    __device__ bool operator()(int j) const { return (bits >> j) & 1u; }
+};
+
+// Per-block sums -> partials[block*8+i]; the last block reduces all blocks.
+__device__ __forceinline__ void block_stats(RowStats& s, double* partials, double* stats) {
     __shared__ float red[LOSS_BLOCK / 32][LOSS_STATS];
+    __shared__ bool last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     #pragma unroll
     for (int i = 0; i < LOSS_STATS; ++i) {
@@ -123,11 +149,24 @@ __device__ __forceinline__ void block_stats(RowStats& s, double* partials) {
         if (lane == 0) red[warp][i] = v;
     }
     __syncthreads();
+    unsigned int* arrivals = reinterpret_cast<unsigned int*>(partials + (int64_t)gridDim.x * LOSS_STATS);
     if (threadIdx.x < LOSS_STATS) {
         double acc = 0.0;
         for (int w = 0; w < LOSS_BLOCK / 32; ++w) acc += (double)red[w][threadIdx.x];
         partials[(int64_t)blockIdx.x * LOSS_STATS + threadIdx.x] = acc;
+        __threadfence();
     }
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(arrivals, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x < LOSS_STATS) {
+        double acc = 0.0;
+        for (unsigned b = 0; b < gridDim.x; ++b) acc += __ldcg(partials + (int64_t)b * LOSS_STATS + threadIdx.x);
+        stats[threadIdx.x] = acc;
+    }
+    if (threadIdx.x == 0) *arrivals = 0u;  // ready for the next launch on this scratch
 }
 
 __device__ __forceinline__ void bf16x8_to_float(const uint4& v, float (&x)[8]) {
@@ -148,56 +187,54 @@ __device__ __forceinline__ uint4 float8_to_bf16(const float (&x)[8]) {
     return v;
 }
 
-__device__ __forceinline__ unsigned mask8(const uint2& m) {
-    unsigned bits = 0;
-    #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        bits |= (((m.x >> (8 * j)) & 0xffu) != 0 ? 1u : 0u) << j;
-        bits |= (((m.y >> (8 * j)) & 0xffu) != 0 ? 1u : 0u) << (j + 4);
-    }
-    return bits;
+struct Row8 {
+    uint4 logits;
+    uint2 mask;
+    int act;
+    float old, adv, w;
+};
+
+__device__ __forceinline__ Row8 load_row8(int64_t r, const uint4* logits, const uint2* mask, const int32_t* action,
+                                          const float* old_logp, const float* adv, const float* weight) {
+    Row8 v;
+    v.logits = __ldcs(logits + r);
+    v.mask = __ldcs(mask + r);
+    v.act = __ldcs(action + r);
+    v.old = __ldcs(old_logp + r);
+    v.adv = __ldcs(adv + r);
+    v.w = __ldcs(weight + r);
+    return v;
 }
 
-// A == 8, bf16: a row is one uint4 of logits, one uint2 of mask.
-__global__ void __launch_bounds__(LOSS_BLOCK) ppo_bf16x8_kernel(int64_t N, const uint4* __restrict__ logits,
+// A == 8, bf16: software-pipelined, one row per thread per step.
+__global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, const uint4* __restrict__ logits,
                                                                  const uint2* __restrict__ mask,
                                                                  const int32_t* __restrict__ action,
                                                                  const float* __restrict__ old_logp,
                                                                  const float* __restrict__ adv,
                                                                  const float* __restrict__ weight,
                                                                  const float* __restrict__ controls,
-                                                                 uint4* __restrict__ dlogits, double* partials) {
+                                                                 uint4* __restrict__ dlogits, double* partials,
+                                                                 double* stats) {
     LossControls k = load_controls(controls);
     RowStats s;
     s.zero();
     const int64_t stride = (int64_t)gridDim.x * LOSS_BLOCK;
     int64_t r = (int64_t)blockIdx.x * LOSS_BLOCK + threadIdx.x;
-    // two rows in flight per thread
-    for (; r + stride < N; r += 2 * stride) {
-        uint4 v0 = __ldcs(logits + r), v1 = __ldcs(logits + r + stride);
-        uint2 m0 = __ldcs(mask + r), m1 = __ldcs(mask + r + stride);
-        int a0 = __ldcs(action + r), a1 = __ldcs(action + r + stride);
-        float o0 = __ldcs(old_logp + r), o1 = __ldcs(old_logp + r + stride);
-        float d0 = __ldcs(adv + r), d1 = __ldcs(adv + r + stride);
-        float w0 = __ldcs(weight + r), w1 = __ldcs(weight + r + stride);
-        float x0[8], x1[8];
-        bf16x8_to_float(v0, x0);
-        bf16x8_to_float(v1, x1);
-        row_backward<8>(x0, mask8(m0), a0, o0, d0, w0, k, s);
-        row_backward<8>(x1, mask8(m1), a1, o1, d1, w1, k, s);
-        __stcs(dlogits + r, float8_to_bf16(x0));
-        __stcs(dlogits + r + stride, float8_to_bf16(x1));
+    Row8 cur;
+    if (r < N) cur = load_row8(r, logits, mask, action, old_logp, adv, weight);
+    while (r < N) {
+        int64_t nr = r + stride;
+        Row8 nxt;
+        if (nr < N) nxt = load_row8(nr, logits, mask, action, old_logp, adv, weight);
+        float x[8];
+        bf16x8_to_float(cur.logits, x);
+        row_backward<8>(x, Legal8{cur.mask}, cur.act, cur.old, cur.adv, cur.w, k, s);
+        __stcs(dlogits + r, float8_to_bf16(x));
+        cur = nxt;
+        r = nr;
     }
-    if (r < N) {
-        uint4 v0 = __ldcs(logits + r);
-        uint2 m0 = __ldcs(mask + r);
-        float x0[8];
-        bf16x8_to_float(v0, x0);
-        row_backward<8>(x0, mask8(m0), __ldcs(action + r), __ldcs(old_logp + r), __ldcs(adv + r),
-                        __ldcs(weight + r), k, s);
-        __stcs(dlogits + r, float8_to_bf16(x0));
-    }
-    block_stats(s, partials);
+    block_stats(s, partials, stats);
 }
 
 // Generic rows (A <= 32, fp32 or bf16, any alignment).
@@ -222,7 +259,8 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
                                                                   const float* __restrict__ adv,
                                                                   const float* __restrict__ weight,
                                                                   const float* __restrict__ controls,
-                                                                  T* __restrict__ dlogits, double* partials) {
+                                                                  T* __restrict__ dlogits, double* partials,
+                                                                  double* stats) {
     LossControls k = load_controls(controls);
     RowStats s;
     s.zero();
@@ -237,34 +275,27 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
                 legal |= (mask[r * A + j] != 0 ? 1u : 0u) << j;
             }
         }
-        row_backward<LOSS_MAX_A>(x, legal, action[r], old_logp[r], adv[r], weight[r], k, s);
+        row_backward<LOSS_MAX_A>(x, LegalBits{legal}, action[r], old_logp[r], adv[r], weight[r], k, s);
         #pragma unroll
         for (int j = 0; j < LOSS_MAX_A; ++j)
             if (j < A) dlogits[r * A + j] = from_f<T>(x[j]);
     }
-    block_stats(s, partials);
+    block_stats(s, partials, stats);
 }
 
-// Fixed-order sum of per-block statistics.
-__global__ void ppo_finalize_kernel(int blocks, const double* partials, double* stats) {
-    __shared__ double red[LOSS_BLOCK];
-    for (int i = 0; i < LOSS_STATS; ++i) {
-        double acc = 0.0;
-        for (int b = threadIdx.x; b < blocks; b += blockDim.x) acc += partials[(int64_t)b * LOSS_STATS + i];
-        red[threadIdx.x] = acc;
-        __syncthreads();
-        for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-            if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
-            __syncthreads();
-        }
-        if (threadIdx.x == 0) stats[i] = red[0];
-        __syncthreads();
-    }
-}
-
+// One wave of resident blocks (occupancy of the vector kernel), grid-stride beyond.
 int ppo_grid(int64_t N) {
-    // enough rows in flight to cover HBM latency: 8 resident blocks per SM
-    return stride_grid(N, LOSS_BLOCK, 8);
+    static int per_sm[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int slot = dev >= 0 && dev < 64 ? dev : 0;
+    if (per_sm[slot] == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, ppo_bf16x8_kernel, LOSS_BLOCK, 0) != cudaSuccess || n <= 0)
+            n = 4;
+        per_sm[slot] = n;
+    }
+    return stride_grid(N, LOSS_BLOCK, per_sm[slot]);
 }
 
 }  // namespace pbg
@@ -275,7 +306,8 @@ extern "C" {
 
 int64_t pbg_ppo_partials_size(int64_t N, int32_t A) {
     (void)A;
-    return (int64_t)ppo_grid(N > 0 ? N : 1) * LOSS_STATS;
+    // per-block statistics plus one slot holding the arrival counter
+    return (int64_t)ppo_grid(N > 0 ? N : 1) * LOSS_STATS + 1;
 }
 
 int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void* logits, const uint8_t* mask,
@@ -284,27 +316,24 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
                                  double* stats, void* stream) {
     PBG_REQUIRE(N >= 0 && A >= 1 && A <= LOSS_MAX_A, "ppo: need N >= 0 and A in [1,32]");
     PBG_REQUIRE(dtype == 0 || dtype == 1, "ppo: dtype must be 0 (fp32) or 1 (bf16)");
-    PBG_REQUIRE(logits && mask && action && old_logp && adv && weight && controls && dlogits && partials && stats,
-                "ppo: null argument");
+    PBG_REQUIRE(controls && partials && stats, "ppo: null controls or scratch");
+    PBG_REQUIRE(N == 0 || (logits && mask && action && old_logp && adv && weight && dlogits), "ppo: null argument");
     cudaStream_t s = as_stream(stream);
     int grid = ppo_grid(N > 0 ? N : 1);
     bool vec = dtype == 1 && A == 8 && ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dlogits % 16 == 0) &&
                ((uintptr_t)mask % 8 == 0);
     if (vec) {
         ppo_bf16x8_kernel<<<grid, LOSS_BLOCK, 0, s>>>(N, (const uint4*)logits, (const uint2*)mask, action, old_logp,
-                                                      adv, weight, controls, (uint4*)dlogits, partials);
+                                                      adv, weight, controls, (uint4*)dlogits, partials, stats);
     } else if (dtype == 1) {
         ppo_generic_kernel<__nv_bfloat16><<<grid, LOSS_BLOCK, 0, s>>>(
             N, A, (const __nv_bfloat16*)logits, mask, action, old_logp, adv, weight, controls,
-            (__nv_bfloat16*)dlogits, partials);
+            (__nv_bfloat16*)dlogits, partials, stats);
     } else {
         ppo_generic_kernel<float><<<grid, LOSS_BLOCK, 0, s>>>(N, A, (const float*)logits, mask, action, old_logp, adv,
-                                                              weight, controls, (float*)dlogits, partials);
+                                                              weight, controls, (float*)dlogits, partials, stats);
     }
-    int rc = launch_status("ppo_categorical_backward");
-    if (rc) return rc;
-    ppo_finalize_kernel<<<1, LOSS_BLOCK, 0, s>>>(grid, partials, stats);
-    return launch_status("ppo_finalize");
+    return launch_status("ppo_categorical_backward");
 }
 
 }  // extern "C"

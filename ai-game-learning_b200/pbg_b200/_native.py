@@ -114,12 +114,25 @@ def check(rc: int, what: str) -> None:
         raise NativeError(f"{what} failed ({rc}): {msg}")
 
 
+_keep = threading.local()
+
+
 def call(name: str, *args) -> None:
-    check(getattr(lib(), name)(*args), name)
+    """Invoke an entry point; tensors passed through ptr() stay alive until it returns.
+
+    Without this, two temporaries built in one argument list (for example two
+    ``torch.full_like`` columns) could share one caching-allocator block: the
+    first is freed as soon as ptr() returns and the second reuses it.
+    """
+
+    try:
+        check(getattr(lib(), name)(*args), name)
+    finally:
+        _keep.items = []
 
 
 def ptr(t: torch.Tensor | None):
-    """Device pointer of a contiguous CUDA tensor (None -> NULL)."""
+    """Device pointer of a contiguous CUDA tensor (None -> NULL), kept alive for call()."""
 
     if t is None:
         return None
@@ -127,6 +140,10 @@ def ptr(t: torch.Tensor | None):
         raise NativeError("libpbgb200 operates on CUDA tensors only")
     if not t.is_contiguous():
         raise NativeError("libpbgb200 requires contiguous tensors")
+    items = getattr(_keep, "items", None)
+    if items is None:
+        items = _keep.items = []
+    items.append(t)
     return ctypes.c_void_p(t.data_ptr())
 
 

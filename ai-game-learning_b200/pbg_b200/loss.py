@@ -51,7 +51,7 @@ class FusedPPOBackward:
     def set_controls(self, *, scale: float = 1.0, inv_count: float | None = None) -> None:
         cap = self.config.negative_advantage_ratio_cap
         log_cap = math.inf if cap is None else math.log(cap)
-        inv = 1.0 / self.rows if inv_count is None else inv_count
+        inv = (1.0 / self.rows if self.rows else 0.0) if inv_count is None else inv_count
         self.controls.copy_(torch.tensor([self.config.policy_clip, log_cap, self.config.entropy_coefficient,
                                           scale, inv], dtype=torch.float32))
 

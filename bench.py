@@ -356,7 +356,7 @@ def main():
                      "kernel": "ppo_bf16x8_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,
                      "algorithmic_bytes": algo_bytes},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1:

@@ -452,8 +452,12 @@ def test_bf16_vector_path_matches_torch_fp32_autograd():
     z = x.masked_fill(~m, -torch.inf)
     lp = torch.log_softmax(z, -1)
     sel = lp.gather(1, cuda(action).long()[:, None])[:, 0]
-    p = torch.softmax(z, -1)
-    ent = -(torch.where(m, p * lp, torch.zeros_like(p))).sum(-1)
+    # entropy as the categorical fixture writes it (finite logits off the mask)
+    finite = torch.where(m, x, torch.zeros_like(x))
+    mx = torch.where(m, finite, torch.full_like(x, -torch.inf)).amax(-1, keepdim=True)
+    un = torch.where(m, torch.exp(finite - mx), torch.zeros_like(x))
+    nz = un.sum(-1, keepdim=True)
+    ent = -((un / nz) * torch.where(m, finite - mx - torch.log(nz), torch.zeros_like(x))).sum(-1)
     lr = sel - cuda(old)
     ratio = lr.exp()
     clipped = ratio.clamp(0.8, 1.2)
