@@ -5,7 +5,7 @@
 Sources whose results must follow the reference's operation order one
 rounding at a time (state machine, policy composition, RNG, showdown) are
 compiled with ``-fmad=false``; the HBM-bound loss and optimizer kernels keep
-fused multiply-adds.
+fused multiply-adds, and the loss flushes denormals (``-ftz=true``).
 """
 
 from __future__ import annotations
@@ -54,6 +54,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
                  "-I", os.path.join(ROOT, "include"), "-I", CSRC, "-c", src, "-o", obj]
         if name in EXACT:
             flags.insert(5, "-fmad=false")
+        if name == "loss.cu":
+            flags.insert(5, "-ftz=true")
         if verbose:
             flags.insert(5, "-Xptxas=-v")
         subprocess.run(flags, check=True)

@@ -20,10 +20,12 @@
 // the special-function unit (exp2f, __log2f: documented CUDA functions with a
 // few-ulp error), about 1e-6 relative on the gradient.
 //
-// Layout: logits/dlogits [N,A] (bf16 or fp32), mask [N,A] u8, action [N]
-// i32, old_logp/adv/weight [N] f32.  For A == 8 with aligned rows one thread
-// moves a whole row with 16/8/16-byte accesses (56 B per row with bf16
-// logits) and prefetches the next row before computing the current one.
+// Layout: logits/dlogits [N,A] (bf16 or fp32), mask [N,A] u8 (0/1), action
+// [N] i32, old_logp/adv/weight [N] f32.  For A == 8 with aligned rows one
+// thread moves a whole row with 16/8/16-byte accesses (56 B per row with bf16
+// logits), prefetches the next row before computing the current one, and
+// does the elementwise work on bf16/f32 pairs.  Compiled with -ftz=true:
+// denormal probabilities flush to zero.
 // Per-block statistics go to caller scratch; the last block to finish sums
 // them in block order (deterministic) and clears the arrival counter.
 #include <cuda_bf16.h>
@@ -128,11 +130,6 @@ __device__ __forceinline__ void row_backward(float (&x)[A], const Legal& legal, 
     accumulate(s, coef, w, prow, ent, ratio, lr, k, adv);
 }
 
-struct Legal8 {  // 8 bool bytes (0/1) packed in a uint2
-    uint2 m;
-    __device__ bool operator()(int j) const { return ((j < 4 ? m.x >> (8 * j) : m.y >> (8 * (j - 4))) & 0xffu) != 0; }
-};
-
 struct LegalBits {
     unsigned bits;
     __device__ bool operator()(int j) const { return (bits >> j) & 1u; }
@@ -169,24 +166,6 @@ __device__ __forceinline__ void block_stats(RowStats& s, double* partials, doubl
     if (threadIdx.x == 0) *arrivals = 0u;  // ready for the next launch on this scratch
 }
 
-__device__ __forceinline__ void bf16x8_to_float(const uint4& v, float (&x)[8]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-    #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float2 f = __bfloat1622float2(h[i]);
-        x[2 * i] = f.x;
-        x[2 * i + 1] = f.y;
-    }
-}
-
-__device__ __forceinline__ uint4 float8_to_bf16(const float (&x)[8]) {
-    uint4 v;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
-    #pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
-    return v;
-}
-
 struct Row8 {
     uint4 logits;
     uint2 mask;
@@ -206,16 +185,82 @@ __device__ __forceinline__ Row8 load_row8(int64_t r, const uint4* logits, const 
     return v;
 }
 
+// A == 8, bf16 rows as four bf16x2 pairs ----------------------------------
+//
+// Mask bytes are 0/1 (torch.bool).  A pair's two bytes become a 32-bit lane
+// mask w (0xFFFF per legal element) with one byte permute and one multiply;
+// then x & w is the logit pair with illegal entries zeroed and
+// (x & w) | (-inf & ~w) the pair with illegal entries at -inf (one LOP3).
+// Elementwise arithmetic runs on float2 with the packed FP32 instructions.
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
+__device__ __forceinline__ void row8_backward(const Row8& row, const LossControls& k, RowStats& s, uint4& out) {
+    const uint32_t v[4] = {row.logits.x, row.logits.y, row.logits.z, row.logits.w};
+    const uint32_t mw[4] = {__byte_perm(row.mask.x, 0u, 0x1100) * 0xffu, __byte_perm(row.mask.x, 0u, 0x3322) * 0xffu,
+                            __byte_perm(row.mask.y, 0u, 0x1100) * 0xffu, __byte_perm(row.mask.y, 0u, 0x3322) * 0xffu};
+    uint32_t xm[4], ym[4];
+    #pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        xm[p] = v[p] & mw[p];
+        ym[p] = xm[p] | (0xff80ff80u & ~mw[p]);
+    }
+    // masked max in bf16 (exact)
+    __nv_bfloat162 m01 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&ym[0]),
+                                 *reinterpret_cast<const __nv_bfloat162*>(&ym[1]));
+    __nv_bfloat162 m23 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&ym[2]),
+                                 *reinterpret_cast<const __nv_bfloat162*>(&ym[3]));
+    __nv_bfloat162 mm = __hmax2(m01, m23);
+    float my = fmaxf(__low2float(mm), __high2float(mm)) * LOG2E;
+    const float2 L2 = make_float2(LOG2E, LOG2E), NMY = make_float2(-my, -my);
+    float2 X[4], E[4];
+    #pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        X[p] = bf2_to_f2(xm[p]);
+        float2 t = __ffma2_rn(bf2_to_f2(ym[p]), L2, NMY);
+        E[p] = make_float2(exp2f(t.x), exp2f(t.y));
+    }
+    float2 S = __fadd2_rn(__fadd2_rn(E[0], E[1]), __fadd2_rn(E[2], E[3]));
+    float2 SX = __ffma2_rn(E[3], X[3], __ffma2_rn(E[2], X[2], __ffma2_rn(E[1], X[1], __fmul2_rn(E[0], X[0]))));
+    float se = S.x + S.y, sx = SX.x + SX.y;
+    const int act = row.act, ka = act >> 1;
+    float2 Xa = ka == 0 ? X[0] : ka == 1 ? X[1] : ka == 2 ? X[2] : X[3];
+    float xa = (act & 1) ? Xa.y : Xa.x;
+    float inv = __fdividef(1.0f, se);
+    float lse = (my + __log2f(se)) * LN2;
+    float ent = lse - sx * inv;
+    float lr = (xa - lse) - row.old;
+    float prow, ratio;
+    float g = ratio_terms(lr, row.adv, k, prow, ratio);
+    float coef = k.coef_scale * row.w;
+    float pscale = inv * coef;
+    float K = k.cent * (ent - lse) - g;
+    float ga = coef * g;
+    const float2 PS = make_float2(pscale, pscale), C2 = make_float2(k.cent, k.cent), K2 = make_float2(K, K);
+    const float2 GA = (act & 1) ? make_float2(0.0f, ga) : make_float2(ga, 0.0f);
+    uint32_t o[4];
+    #pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        float2 d = __fmul2_rn(__fmul2_rn(E[p], PS), __ffma2_rn(C2, X[p], K2));
+        if (p == ka) d = __fadd2_rn(d, GA);
+        __nv_bfloat162 h = __floats2bfloat162_rn(d.x, d.y);
+        o[p] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    out = make_uint4(o[0], o[1], o[2], o[3]);
+    accumulate(s, coef, row.w, prow, ent, ratio, lr, k, row.adv);
+}
+
 // A == 8, bf16: software-pipelined, one row per thread per step.
 __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, const uint4* __restrict__ logits,
-                                                                 const uint2* __restrict__ mask,
-                                                                 const int32_t* __restrict__ action,
-                                                                 const float* __restrict__ old_logp,
-                                                                 const float* __restrict__ adv,
-                                                                 const float* __restrict__ weight,
-                                                                 const float* __restrict__ controls,
-                                                                 uint4* __restrict__ dlogits, double* partials,
-                                                                 double* stats) {
+                                                                    const uint2* __restrict__ mask,
+                                                                    const int32_t* __restrict__ action,
+                                                                    const float* __restrict__ old_logp,
+                                                                    const float* __restrict__ adv,
+                                                                    const float* __restrict__ weight,
+                                                                    const float* __restrict__ controls,
+                                                                    uint4* __restrict__ dlogits, double* partials,
+                                                                    double* stats) {
     LossControls k = load_controls(controls);
     RowStats s;
     s.zero();
@@ -227,10 +272,9 @@ __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, co
         int64_t nr = r + stride;
         Row8 nxt;
         if (nr < N) nxt = load_row8(nr, logits, mask, action, old_logp, adv, weight);
-        float x[8];
-        bf16x8_to_float(cur.logits, x);
-        row_backward<8>(x, Legal8{cur.mask}, cur.act, cur.old, cur.adv, cur.w, k, s);
-        __stcs(dlogits + r, float8_to_bf16(x));
+        uint4 out;
+        row8_backward(cur, k, s, out);
+        __stcs(dlogits + r, out);
         cur = nxt;
         r = nr;
     }
