@@ -381,3 +381,68 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
 }
 
 }  // extern "C"
+
+// ===================================================== allocation-free variant
+//
+// Some callers cannot call cudaMalloc: host applications that hand all
+// device memory to their own pool and forbid allocations once training
+// starts, plugins whose binding has no way to pass a scratch buffer, and code
+// that must not stall on the allocator in the middle of a step.  For them
+// the per-block loss statistics live in a fixed array compiled into this
+// library instead of in caller scratch.  Every GPU that loads the library
+// holds the array (about 128 KiB) until the process exits.
+#include <mutex>
+
+namespace pbg {
+
+constexpr int NOALLOC_MAX_BLOCKS = 2048;  // statistics of at most 2048 thread blocks
+static __device__ __align__(256) double g_ppo_noalloc_scratch[NOALLOC_MAX_BLOCKS * LOSS_STATS + 1];
+
+static std::mutex g_noalloc_mutex;
+static double* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the array on the current device.  The array's name is
+// only a host-side stand-in, so the address is looked up once per device,
+// with that device current, and cached.
+static int noalloc_scratch(double** out) {
+    int dev = 0;
+    int rc = cuda_status(cudaGetDevice(&dev), "ppo_noalloc: cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) {
+        set_error("ppo_noalloc: device ordinal %d is beyond the 64 supported", dev);
+        return PBG_ERANGE;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        rc = cuda_status(cudaGetSymbolAddress(&p, g_ppo_noalloc_scratch), "ppo_noalloc: cudaGetSymbolAddress");
+        if (rc) return rc;
+        g_noalloc_ptr[dev] = static_cast<double*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return PBG_OK;
+}
+
+}  // namespace pbg
+
+extern "C" int pbg_ppo_categorical_backward_noalloc(int64_t N, int32_t A, int32_t dtype, const void* logits,
+                                                    const uint8_t* mask, const int32_t* action,
+                                                    const float* old_logp, const float* adv, const float* weight,
+                                                    const float* controls, void* dlogits, double* stats,
+                                                    void* stream) {
+    int grid = ppo_grid(N > 0 ? N : 1);
+    if (grid > NOALLOC_MAX_BLOCKS) {
+        set_error("ppo_noalloc: this launch needs statistics for %d blocks; the built-in scratch holds %d "
+                  "(use pbg_ppo_categorical_backward with caller scratch)", grid, NOALLOC_MAX_BLOCKS);
+        return PBG_ERANGE;
+    }
+    double* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // The arrival counter must start at zero; clear it in stream order.
+    rc = cuda_status(cudaMemsetAsync(scratch + (int64_t)grid * LOSS_STATS, 0, sizeof(double), as_stream(stream)),
+                     "ppo_noalloc: clearing the arrival counter");
+    if (rc) return rc;
+    return pbg_ppo_categorical_backward(N, A, dtype, logits, mask, action, old_logp, adv, weight, controls, dlogits,
+                                        scratch, stats, stream);
+}

@@ -250,6 +250,25 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
                                  const float *controls, void *dlogits, double *partials,
                                  double *stats, void *stream);
 
+/* Allocation-free variant of pbg_ppo_categorical_backward (no counterpart
+ * in the reference).  For callers that cannot allocate device memory --
+ * hosts that own all device memory through their own pool, bindings with no
+ * way to pass scratch -- the per-block statistics live in a fixed array
+ * inside this library (statistics of at most 2048 thread blocks, about 128
+ * KiB, held by every GPU that loads the library until exit).  Returns
+ * PBG_ERANGE if a launch would need more blocks than that.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU (concurrent streams, or several host
+ * threads on one device) race and must be serialised by the caller.  No
+ * allocation happens; arguments and results are as for the entry point
+ * above, minus `partials`. */
+int pbg_ppo_categorical_backward_noalloc(int64_t N, int32_t A, int32_t dtype, const void *logits,
+                                         const uint8_t *mask, const int32_t *action,
+                                         const float *old_logp, const float *adv,
+                                         const float *weight, const float *controls, void *dlogits,
+                                         double *stats, void *stream);
+
 /* ---------------------------------------------------------------- Adam */
 
 /* optimization.py:182-233 (adam_transition) for one lane of a flat fp32
