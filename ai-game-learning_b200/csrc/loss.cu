@@ -26,8 +26,11 @@
 // logits), prefetches the next row before computing the current one, and
 // does the elementwise work on bf16/f32 pairs.  Compiled with -ftz=true:
 // denormal probabilities flush to zero.
-// Per-block statistics go to caller scratch; the last block to finish sums
-// them in block order (deterministic) and clears the arrival counter.
+// When every stream is 16-byte aligned and at least one 1024-row tile exists,
+// the rows are staged through shared memory by bulk-async copies (see
+// ppo_bf16x8_bulk_kernel).  Per-block statistics go to caller scratch; the
+// last block to finish sums them in block order (deterministic) and clears
+// the arrival counter.
 #include <cuda_bf16.h>
 
 #include "pbg_common.cuh"
@@ -135,9 +138,14 @@ struct LegalBits {
     __device__ bool operator()(int j) const { return (bits >> j) & 1u; }
 };
 
-// Per-block sums -> partials[block*8+i]; the last block reduces all blocks.
-__device__ __forceinline__ void block_stats(RowStats& s, double* partials, double* stats) {
-    __shared__ float red[LOSS_BLOCK / 32][LOSS_STATS];
+// Scratch layout: slot 0 holds the arrival counter (low 32 bits) and an
+// error word (high 32 bits); block b's sums are slots 1 + 8b .. 8 + 8b.  The
+// fixed counter slot lets launches with different grids share one buffer.
+// The last block to arrive sums all blocks in block order (deterministic),
+// publishes stats (rows = -1 if any block reported an error) and clears slot 0.
+template <int BLOCK>
+__device__ __forceinline__ void block_stats(RowStats& s, double* partials, double* stats, bool failed = false) {
+    __shared__ float red[BLOCK / 32][LOSS_STATS];
     __shared__ bool last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     #pragma unroll
@@ -146,24 +154,27 @@ __device__ __forceinline__ void block_stats(RowStats& s, double* partials, doubl
         if (lane == 0) red[warp][i] = v;
     }
     __syncthreads();
-    unsigned int* arrivals = reinterpret_cast<unsigned int*>(partials + (int64_t)gridDim.x * LOSS_STATS);
+    unsigned int* word = reinterpret_cast<unsigned int*>(partials);  // [0] counter, [1] error
     if (threadIdx.x < LOSS_STATS) {
         double acc = 0.0;
-        for (int w = 0; w < LOSS_BLOCK / 32; ++w) acc += (double)red[w][threadIdx.x];
-        partials[(int64_t)blockIdx.x * LOSS_STATS + threadIdx.x] = acc;
-        __threadfence();
+        for (int w = 0; w < BLOCK / 32; ++w) acc += (double)red[w][threadIdx.x];
+        partials[1 + (int64_t)blockIdx.x * LOSS_STATS + threadIdx.x] = acc;
     }
+    if (threadIdx.x == 0 && failed) atomicOr(word + 1, 1u);
+    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(arrivals, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) last = atomicAdd(word, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
     if (threadIdx.x < LOSS_STATS) {
         double acc = 0.0;
-        for (unsigned b = 0; b < gridDim.x; ++b) acc += __ldcg(partials + (int64_t)b * LOSS_STATS + threadIdx.x);
-        stats[threadIdx.x] = acc;
+        for (unsigned b = 0; b < gridDim.x; ++b) acc += __ldcg(partials + 1 + (int64_t)b * LOSS_STATS + threadIdx.x);
+        bool bad = __ldcg(reinterpret_cast<const unsigned long long*>(partials)) >> 32;
+        stats[threadIdx.x] = (bad && threadIdx.x == LOSS_STATS - 1) ? -1.0 : acc;
     }
-    if (threadIdx.x == 0) *arrivals = 0u;  // ready for the next launch on this scratch
+    __syncthreads();
+    if (threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(partials) = 0ull;  // ready for the next launch
 }
 
 struct Row8 {
@@ -278,7 +289,164 @@ __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, co
         cur = nxt;
         r = nr;
     }
-    block_stats(s, partials, stats);
+    block_stats<LOSS_BLOCK>(s, partials, stats);
+}
+
+// A == 8, bf16, bulk-async staged ----------------------------------------
+//
+// One persistent CTA per SM streams tiles of BULK_T rows through a ring of
+// BULK_STAGES shared-memory stages.  Thread 0 fills a stage with six plain
+// 1D bulk copies (cp.async.bulk global -> shared, no tensor map, no
+// multicast) that complete on the stage's mbarrier; all threads wait on the
+// barrier, compute their rows from shared memory, store dlogits straight to
+// global memory, and after a block barrier thread 0 refills the stage with
+// the tile STAGES ahead.  Bytes in flight are set by the ring (up to three
+// 40 KB tiles per SM), not by registers.  Every wait is bounded: a stage that
+// does not complete within the bound marks the launch failed (stats rows =
+// -1), the CTA waits (bounded again) for its own copies still in flight, and
+// the launch finishes normally.
+constexpr int BULK_T = 1024;
+constexpr int BULK_STAGES = 4;
+constexpr int BULK_THREADS = 512;
+constexpr uint32_t BULK_OFF_MASK = BULK_T * 16;
+constexpr uint32_t BULK_OFF_ACT = BULK_OFF_MASK + BULK_T * 8;
+constexpr uint32_t BULK_OFF_OLD = BULK_OFF_ACT + BULK_T * 4;
+constexpr uint32_t BULK_OFF_ADV = BULK_OFF_OLD + BULK_T * 4;
+constexpr uint32_t BULK_OFF_W = BULK_OFF_ADV + BULK_T * 4;
+constexpr uint32_t BULK_TILE_BYTES = BULK_OFF_W + BULK_T * 4;  // 40 KB
+constexpr size_t BULK_SMEM = (size_t)BULK_STAGES * BULK_TILE_BYTES;
+constexpr uint32_t BULK_WAIT_TRIES = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < BULK_WAIT_TRIES; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+struct BulkArgs {
+    int64_t N;
+    const uint4* logits;
+    const uint2* mask;
+    const int32_t* action;
+    const float* old_logp;
+    const float* adv;
+    const float* weight;
+    const float* controls;
+    uint4* dlogits;
+    double* partials;
+    double* stats;
+};
+
+// Fill stage `st` with tile `tile` (thread 0 only).
+__device__ __forceinline__ void bulk_issue(const BulkArgs& a, unsigned char* ring, uint64_t* bars, int st,
+                                           int64_t tile) {
+    uint32_t bar = smem_u32(&bars[st]);
+    uint32_t dst = smem_u32(ring + (size_t)st * BULK_TILE_BYTES);
+    int64_t r0 = tile * BULK_T;
+    mbar_expect_tx(bar, BULK_TILE_BYTES);
+    bulk_g2s(dst, a.logits + r0, BULK_T * 16, bar);
+    bulk_g2s(dst + BULK_OFF_MASK, a.mask + r0, BULK_T * 8, bar);
+    bulk_g2s(dst + BULK_OFF_ACT, a.action + r0, BULK_T * 4, bar);
+    bulk_g2s(dst + BULK_OFF_OLD, a.old_logp + r0, BULK_T * 4, bar);
+    bulk_g2s(dst + BULK_OFF_ADV, a.adv + r0, BULK_T * 4, bar);
+    bulk_g2s(dst + BULK_OFF_W, a.weight + r0, BULK_T * 4, bar);
+}
+
+__global__ void __launch_bounds__(BULK_THREADS, 1) ppo_bf16x8_bulk_kernel(BulkArgs a) {
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(8) uint64_t bars[BULK_STAGES];
+    LossControls k = load_controls(a.controls);
+    RowStats s;
+    s.zero();
+    const int64_t ntiles = a.N / BULK_T;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < BULK_STAGES; ++st) mbar_init(smem_u32(&bars[st]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int st = 0; st < BULK_STAGES; ++st) {
+            int64_t t = blockIdx.x + (int64_t)st * gridDim.x;
+            if (t < ntiles) bulk_issue(a, ring, bars, st, t);
+        }
+    }
+    __syncthreads();
+    bool failed = false;
+    int64_t i = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
+        const int st = (int)(i % BULK_STAGES);
+        const uint32_t parity = (uint32_t)((i / BULK_STAGES) & 1);
+        bool ok = mbar_wait_bounded(smem_u32(&bars[st]), parity);
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        const unsigned char* base = ring + (size_t)st * BULK_TILE_BYTES;
+        #pragma unroll 2
+        for (int rr = threadIdx.x; rr < BULK_T; rr += BULK_THREADS) {
+            Row8 row;
+            row.logits = reinterpret_cast<const uint4*>(base)[rr];
+            row.mask = reinterpret_cast<const uint2*>(base + BULK_OFF_MASK)[rr];
+            row.act = reinterpret_cast<const int32_t*>(base + BULK_OFF_ACT)[rr];
+            row.old = reinterpret_cast<const float*>(base + BULK_OFF_OLD)[rr];
+            row.adv = reinterpret_cast<const float*>(base + BULK_OFF_ADV)[rr];
+            row.w = reinterpret_cast<const float*>(base + BULK_OFF_W)[rr];
+            uint4 out;
+            row8_backward(row, k, s, out);
+            __stcs(a.dlogits + tile * BULK_T + rr, out);
+        }
+        __syncthreads();  // stage fully read before it is refilled
+        if (threadIdx.x == 0) {
+            int64_t next = tile + (int64_t)BULK_STAGES * gridDim.x;
+            if (next < ntiles) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                bulk_issue(a, ring, bars, st, next);
+            }
+        }
+    }
+    if (failed && threadIdx.x == 0) {
+        // wait (bounded) for this CTA's copies still in flight before shared memory is released
+        for (int64_t m = i; m < i + BULK_STAGES; ++m) {
+            int64_t t = blockIdx.x + m * gridDim.x;
+            if (t < ntiles) mbar_wait_bounded(smem_u32(&bars[m % BULK_STAGES]), (uint32_t)((m / BULK_STAGES) & 1));
+        }
+    }
+    // rows after the last full tile: direct loads
+    if (!failed) {
+        for (int64_t r = ntiles * BULK_T + (int64_t)blockIdx.x * BULK_THREADS + threadIdx.x; r < a.N;
+             r += (int64_t)gridDim.x * BULK_THREADS) {
+            Row8 row = load_row8(r, a.logits, a.mask, a.action, a.old_logp, a.adv, a.weight);
+            uint4 out;
+            row8_backward(row, k, s, out);
+            __stcs(a.dlogits + r, out);
+        }
+    }
+    block_stats<BULK_THREADS>(s, a.partials, a.stats, failed);
 }
 
 // Generic rows (A <= 32, fp32 or bf16, any alignment).
@@ -324,7 +492,7 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
         for (int j = 0; j < LOSS_MAX_A; ++j)
             if (j < A) dlogits[r * A + j] = from_f<T>(x[j]);
     }
-    block_stats(s, partials, stats);
+    block_stats<LOSS_BLOCK>(s, partials, stats);
 }
 
 // One wave of resident blocks (occupancy of the vector kernel), grid-stride beyond.
@@ -350,8 +518,8 @@ extern "C" {
 
 int64_t pbg_ppo_partials_size(int64_t N, int32_t A) {
     (void)A;
-    // per-block statistics plus one slot holding the arrival counter
-    return (int64_t)ppo_grid(N > 0 ? N : 1) * LOSS_STATS + 1;
+    // one counter/error slot plus per-block statistics of the widest launch
+    return 1 + (int64_t)ppo_grid(N > 0 ? N : 1) * LOSS_STATS;
 }
 
 int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void* logits, const uint8_t* mask,
@@ -366,7 +534,26 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
     int grid = ppo_grid(N > 0 ? N : 1);
     bool vec = dtype == 1 && A == 8 && ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dlogits % 16 == 0) &&
                ((uintptr_t)mask % 8 == 0);
-    if (vec) {
+    bool bulk = vec && N >= BULK_T && ((uintptr_t)mask % 16 == 0) && ((uintptr_t)action % 16 == 0) &&
+                ((uintptr_t)old_logp % 16 == 0) && ((uintptr_t)adv % 16 == 0) && ((uintptr_t)weight % 16 == 0);
+    if (bulk) {
+        static bool smem_ready[64] = {false};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64) dev = 0;
+        if (!smem_ready[dev]) {
+            int rc = cuda_status(cudaFuncSetAttribute(ppo_bf16x8_bulk_kernel,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BULK_SMEM),
+                                 "ppo: shared-memory opt-in");
+            if (rc) return rc;
+            smem_ready[dev] = true;
+        }
+        int64_t tiles = N / BULK_T;
+        int bgrid = (int)(tiles < sm_count() ? tiles : sm_count());
+        BulkArgs a{N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
+                   (uint4*)dlogits, partials, stats};
+        ppo_bf16x8_bulk_kernel<<<bgrid, BULK_THREADS, BULK_SMEM, s>>>(a);
+    } else if (vec) {
         ppo_bf16x8_kernel<<<grid, LOSS_BLOCK, 0, s>>>(N, (const uint4*)logits, (const uint2*)mask, action, old_logp,
                                                       adv, weight, controls, (uint4*)dlogits, partials, stats);
     } else if (dtype == 1) {
@@ -439,8 +626,8 @@ extern "C" int pbg_ppo_categorical_backward_noalloc(int64_t N, int32_t A, int32_
     double* scratch = nullptr;
     int rc = noalloc_scratch(&scratch);
     if (rc) return rc;
-    // The arrival counter must start at zero; clear it in stream order.
-    rc = cuda_status(cudaMemsetAsync(scratch + (int64_t)grid * LOSS_STATS, 0, sizeof(double), as_stream(stream)),
+    // The arrival counter and error word (slot 0) must start at zero; clear them in stream order.
+    rc = cuda_status(cudaMemsetAsync(scratch, 0, sizeof(double), as_stream(stream)),
                      "ppo_noalloc: clearing the arrival counter");
     if (rc) return rc;
     return pbg_ppo_categorical_backward(N, A, dtype, logits, mask, action, old_logp, adv, weight, controls, dlogits,

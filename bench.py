@@ -297,6 +297,8 @@ def main():
         torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
+    if float(op.stats[7]) != N:
+        raise RuntimeError("loss kernel reported a failed launch (stats rows != N)")
     elapsed_ms = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kernel_events) / args.steps
     if world > 1:

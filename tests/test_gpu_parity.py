@@ -529,3 +529,21 @@ def test_adam_matches_reference_golden(gold):
     report = host(opt.step())
     assert report[0] == 0.0 and torch.equal(opt.master, before) and float(opt.grad.abs().sum()) == 0.0
     assert int(opt.step_count[0]) == 3
+
+
+def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
+    """717,133 rows: 700 full 1024-row tiles (several passes of the 4-stage ring per CTA) + 333 tail rows."""
+
+    from pbg_b200.loss import LossConfig, fused_ppo_backward
+
+    N, A = 1024 * 700 + 333, 8
+    logits, mask, action, old, adv, weight = _loss_inputs(N, A, 17)
+    x16 = cuda(logits).to(torch.bfloat16)
+    for step in range(2):  # the scratch counter must reset between launches
+        d, stats = fused_ppo_backward(x16, cuda(mask), cuda(action), cuda(old), cuda(adv), cuda(weight),
+                                      LossConfig(0.2, 2.0, 0.01))
+        assert float(stats[7]) == N, "a bulk stage wait timed out"
+    ref, ref_s = O.ppo_categorical(host(x16.float()), mask, action, old, adv, weight, log_cap=math.log(2.0))
+    scale = float(np.abs(ref).max())
+    np.testing.assert_allclose(host(d.float()), ref, rtol=2e-2, atol=2e-2 * scale)
+    np.testing.assert_allclose(host(stats)[[0, 1, 2, 3, 6]], ref_s[[0, 1, 2, 3, 6]], rtol=1e-4, atol=1e-9 * N)
