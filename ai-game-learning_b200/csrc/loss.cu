@@ -26,7 +26,7 @@
 // logits), prefetches the next row before computing the current one, and
 // does the elementwise work on bf16/f32 pairs.  Compiled with -ftz=true:
 // denormal probabilities flush to zero.
-// When every stream is 16-byte aligned and at least one 1024-row tile exists,
+// When every stream is 16-byte aligned and at least one 992-row tile exists,
 // the rows are staged through shared memory by bulk-async copies (see
 // ppo_bf16x8_bulk_kernel).  Per-block statistics go to caller scratch; the
 // last block to finish sums them in block order (deterministic) and clears
@@ -292,28 +292,29 @@ __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, co
     block_stats<LOSS_BLOCK>(s, partials, stats);
 }
 
-// A == 8, bf16, bulk-async staged ----------------------------------------
+// A == 8, bf16, bulk-async staged, warp-specialised -----------------------
 //
-// One persistent CTA per SM streams tiles of BULK_T rows through a ring of
-// BULK_STAGES shared-memory stages.  Thread 0 fills a stage with six plain
-// 1D bulk copies (cp.async.bulk global -> shared, no tensor map, no
-// multicast) that complete on the stage's mbarrier; all threads wait on the
-// barrier, compute their rows from shared memory, store dlogits straight to
-// global memory, and after a block barrier thread 0 refills the stage with
-// the tile STAGES ahead.  Bytes in flight are set by the ring (up to three
-// 40 KB tiles per SM), not by registers.  Every wait is bounded: a stage that
-// does not complete within the bound marks the launch failed (stats rows =
-// -1), the CTA waits (bounded again) for its own copies still in flight, and
-// the launch finishes normally.
-constexpr int BULK_T = 1024;
+// One persistent CTA per SM (1024 threads): warp 31 is the producer, warps
+// 0..30 consume.  Tiles of BULK_T = 992 rows (one row per consumer thread)
+// stream through a ring of BULK_STAGES shared-memory stages.  The producer's
+// lane 0 fills a stage with six plain 1D bulk copies (cp.async.bulk global ->
+// shared, no tensor map, no multicast) completing on the stage's "full"
+// mbarrier; each consumer warp waits on it, computes its 32 rows, stores
+// dlogits straight to global memory and arrives on the stage's "empty"
+// mbarrier; the producer refills a stage once all 31 warps have released it.
+// No warp waits on another warp's compute.  Every wait is bounded: a wait
+// that runs out marks the launch failed (stats rows = -1), the producer
+// waits (bounded again) for its copies still in flight, and the launch ends.
+constexpr int BULK_CONSUMER_WARPS = 31;
+constexpr int BULK_THREADS = 32 * (BULK_CONSUMER_WARPS + 1);
+constexpr int BULK_T = 32 * BULK_CONSUMER_WARPS;  // 992 rows
 constexpr int BULK_STAGES = 4;
-constexpr int BULK_THREADS = 512;
 constexpr uint32_t BULK_OFF_MASK = BULK_T * 16;
 constexpr uint32_t BULK_OFF_ACT = BULK_OFF_MASK + BULK_T * 8;
 constexpr uint32_t BULK_OFF_OLD = BULK_OFF_ACT + BULK_T * 4;
 constexpr uint32_t BULK_OFF_ADV = BULK_OFF_OLD + BULK_T * 4;
 constexpr uint32_t BULK_OFF_W = BULK_OFF_ADV + BULK_T * 4;
-constexpr uint32_t BULK_TILE_BYTES = BULK_OFF_W + BULK_T * 4;  // 40 KB
+constexpr uint32_t BULK_TILE_BYTES = BULK_OFF_W + BULK_T * 4;  // 39,680 B, every offset a multiple of 16
 constexpr size_t BULK_SMEM = (size_t)BULK_STAGES * BULK_TILE_BYTES;
 constexpr uint32_t BULK_WAIT_TRIES = 1u << 22;
 
@@ -325,6 +326,10 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -365,50 +370,68 @@ struct BulkArgs {
     double* stats;
 };
 
-// Fill stage `st` with tile `tile` (thread 0 only).
-__device__ __forceinline__ void bulk_issue(const BulkArgs& a, unsigned char* ring, uint64_t* bars, int st,
+__device__ __forceinline__ void bulk_issue(const BulkArgs& a, unsigned char* ring, uint32_t full_bar, int st,
                                            int64_t tile) {
-    uint32_t bar = smem_u32(&bars[st]);
     uint32_t dst = smem_u32(ring + (size_t)st * BULK_TILE_BYTES);
     int64_t r0 = tile * BULK_T;
-    mbar_expect_tx(bar, BULK_TILE_BYTES);
-    bulk_g2s(dst, a.logits + r0, BULK_T * 16, bar);
-    bulk_g2s(dst + BULK_OFF_MASK, a.mask + r0, BULK_T * 8, bar);
-    bulk_g2s(dst + BULK_OFF_ACT, a.action + r0, BULK_T * 4, bar);
-    bulk_g2s(dst + BULK_OFF_OLD, a.old_logp + r0, BULK_T * 4, bar);
-    bulk_g2s(dst + BULK_OFF_ADV, a.adv + r0, BULK_T * 4, bar);
-    bulk_g2s(dst + BULK_OFF_W, a.weight + r0, BULK_T * 4, bar);
+    mbar_expect_tx(full_bar, BULK_TILE_BYTES);
+    bulk_g2s(dst, a.logits + r0, BULK_T * 16, full_bar);
+    bulk_g2s(dst + BULK_OFF_MASK, a.mask + r0, BULK_T * 8, full_bar);
+    bulk_g2s(dst + BULK_OFF_ACT, a.action + r0, BULK_T * 4, full_bar);
+    bulk_g2s(dst + BULK_OFF_OLD, a.old_logp + r0, BULK_T * 4, full_bar);
+    bulk_g2s(dst + BULK_OFF_ADV, a.adv + r0, BULK_T * 4, full_bar);
+    bulk_g2s(dst + BULK_OFF_W, a.weight + r0, BULK_T * 4, full_bar);
 }
 
 __global__ void __launch_bounds__(BULK_THREADS, 1) ppo_bf16x8_bulk_kernel(BulkArgs a) {
     extern __shared__ __align__(128) unsigned char ring[];
-    __shared__ __align__(8) uint64_t bars[BULK_STAGES];
+    __shared__ __align__(8) uint64_t full[BULK_STAGES], empty[BULK_STAGES];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     LossControls k = load_controls(a.controls);
     RowStats s;
     s.zero();
     const int64_t ntiles = a.N / BULK_T;
     if (threadIdx.x == 0) {
-        for (int st = 0; st < BULK_STAGES; ++st) mbar_init(smem_u32(&bars[st]), 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         for (int st = 0; st < BULK_STAGES; ++st) {
-            int64_t t = blockIdx.x + (int64_t)st * gridDim.x;
-            if (t < ntiles) bulk_issue(a, ring, bars, st, t);
+            mbar_init(smem_u32(&full[st]), 1);
+            mbar_init(smem_u32(&empty[st]), BULK_CONSUMER_WARPS);
         }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     bool failed = false;
-    int64_t i = 0;
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
-        const int st = (int)(i % BULK_STAGES);
-        const uint32_t parity = (uint32_t)((i / BULK_STAGES) & 1);
-        bool ok = mbar_wait_bounded(smem_u32(&bars[st]), parity);
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
+    if (warp == BULK_CONSUMER_WARPS) {
+        // producer
+        if (lane == 0) {
+            int64_t issued = 0;
+            for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++issued) {
+                const int st = (int)(issued % BULK_STAGES);
+                if (issued >= BULK_STAGES &&
+                    !mbar_wait_bounded(smem_u32(&empty[st]), (uint32_t)((issued / BULK_STAGES - 1) & 1))) {
+                    failed = true;
+                    break;
+                }
+                bulk_issue(a, ring, smem_u32(&full[st]), st, tile);
+            }
+            if (failed) {
+                // copies of the last BULK_STAGES issued tiles may still be in flight
+                int64_t first = issued > BULK_STAGES ? issued - BULK_STAGES : 0;
+                for (int64_t m = first; m < issued; ++m)
+                    mbar_wait_bounded(smem_u32(&full[m % BULK_STAGES]), (uint32_t)((m / BULK_STAGES) & 1));
+            }
         }
-        const unsigned char* base = ring + (size_t)st * BULK_TILE_BYTES;
-        #pragma unroll 2
-        for (int rr = threadIdx.x; rr < BULK_T; rr += BULK_THREADS) {
+    } else {
+        // consumers: one row per thread per tile
+        int64_t used = 0;
+        for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++used) {
+            const int st = (int)(used % BULK_STAGES);
+            bool ok = mbar_wait_bounded(smem_u32(&full[st]), (uint32_t)((used / BULK_STAGES) & 1));
+            if (!__all_sync(0xffffffffu, ok)) {
+                failed = true;
+                break;
+            }
+            const unsigned char* base = ring + (size_t)st * BULK_TILE_BYTES;
+            const int rr = threadIdx.x;  // warp * 32 + lane < BULK_T
             Row8 row;
             row.logits = reinterpret_cast<const uint4*>(base)[rr];
             row.mask = reinterpret_cast<const uint2*>(base + BULK_OFF_MASK)[rr];
@@ -416,37 +439,24 @@ __global__ void __launch_bounds__(BULK_THREADS, 1) ppo_bf16x8_bulk_kernel(BulkAr
             row.old = reinterpret_cast<const float*>(base + BULK_OFF_OLD)[rr];
             row.adv = reinterpret_cast<const float*>(base + BULK_OFF_ADV)[rr];
             row.w = reinterpret_cast<const float*>(base + BULK_OFF_W)[rr];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty[st]));  // this warp's rows are in registers
             uint4 out;
             row8_backward(row, k, s, out);
             __stcs(a.dlogits + tile * BULK_T + rr, out);
         }
-        __syncthreads();  // stage fully read before it is refilled
-        if (threadIdx.x == 0) {
-            int64_t next = tile + (int64_t)BULK_STAGES * gridDim.x;
-            if (next < ntiles) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                bulk_issue(a, ring, bars, st, next);
+        // rows after the last full tile: direct loads
+        if (!failed) {
+            for (int64_t r = ntiles * BULK_T + (int64_t)blockIdx.x * BULK_T + threadIdx.x; r < a.N;
+                 r += (int64_t)gridDim.x * BULK_T) {
+                Row8 row = load_row8(r, a.logits, a.mask, a.action, a.old_logp, a.adv, a.weight);
+                uint4 out;
+                row8_backward(row, k, s, out);
+                __stcs(a.dlogits + r, out);
             }
         }
     }
-    if (failed && threadIdx.x == 0) {
-        // wait (bounded) for this CTA's copies still in flight before shared memory is released
-        for (int64_t m = i; m < i + BULK_STAGES; ++m) {
-            int64_t t = blockIdx.x + m * gridDim.x;
-            if (t < ntiles) mbar_wait_bounded(smem_u32(&bars[m % BULK_STAGES]), (uint32_t)((m / BULK_STAGES) & 1));
-        }
-    }
-    // rows after the last full tile: direct loads
-    if (!failed) {
-        for (int64_t r = ntiles * BULK_T + (int64_t)blockIdx.x * BULK_THREADS + threadIdx.x; r < a.N;
-             r += (int64_t)gridDim.x * BULK_THREADS) {
-            Row8 row = load_row8(r, a.logits, a.mask, a.action, a.old_logp, a.adv, a.weight);
-            uint4 out;
-            row8_backward(row, k, s, out);
-            __stcs(a.dlogits + r, out);
-        }
-    }
-    block_stats<BULK_THREADS>(s, a.partials, a.stats, failed);
+    block_stats<BULK_THREADS>(s, a.partials, a.stats, __syncthreads_or(failed));
 }
 
 // Generic rows (A <= 32, fp32 or bf16, any alignment).
