@@ -45,6 +45,7 @@ constexpr float LN2 = 0.6931471805599453f;
 
 struct LossControls {
     float clip, cap, exp_cap, cent, coef_scale;  // coef_scale = scale * inv_count
+    float lo, hi;                                // 1 - clip, 1 + clip
 };
 
 __device__ __forceinline__ LossControls load_controls(const float* c) {
@@ -54,11 +55,13 @@ __device__ __forceinline__ LossControls load_controls(const float* c) {
     k.exp_cap = expf(c[1]);
     k.cent = c[2];
     k.coef_scale = c[3] * c[4];
+    k.lo = 1.0f - c[0];
+    k.hi = 1.0f + c[0];
     return k;
 }
 
 struct RowStats {
-    float v[LOSS_STATS];
+    float v[LOSS_STATS];  // v[7] (rows) is added once per thread by the kernel, not per row
     __device__ void zero() {
         #pragma unroll
         for (int i = 0; i < LOSS_STATS; ++i) v[i] = 0.0f;
@@ -67,23 +70,24 @@ struct RowStats {
 
 // Row objective pieces from the log ratio (learner.py:2021-2047): returns
 // g = d policy_row / d log_ratio and writes policy_row and the ratio.
+// policy_row = -min(f1, f2) with f1 = (capped) ratio * A, f2 = clip(ratio) * A;
+// torch.minimum sends the gradient to the smaller operand and half to each
+// at a tie; torch.clamp passes it inside [lo, hi] inclusive.
 __device__ __forceinline__ float ratio_terms(float lr, float adv, const LossControls& k, float& prow,
                                              float& ratio_out) {
     float ratio = exp2f(lr * LOG2E);
-    float lo = 1.0f - k.clip, hi = 1.0f + k.clip;
-    float clipped = fminf(fmaxf(ratio, lo), hi);
+    float clipped = fminf(fmaxf(ratio, k.lo), k.hi);
     bool negative = adv < 0.0f;
     // exp(min(lr, cap)) without a second exponential
     float neg_ratio = lr <= k.cap ? ratio : k.exp_cap;
     float pr = negative ? neg_ratio : ratio;
     float f1 = pr * adv, f2 = clipped * adv;
     prow = -fminf(f1, f2);
-    float g1 = f1 < f2 ? 1.0f : (f1 == f2 ? 0.5f : 0.0f);
-    float g2 = f2 < f1 ? 1.0f : (f1 == f2 ? 0.5f : 0.0f);
-    float dpr = negative ? neg_ratio * (lr < k.cap ? 1.0f : (lr == k.cap ? 0.5f : 0.0f)) : ratio;
-    float dcl = (ratio >= lo && ratio <= hi) ? ratio : 0.0f;
+    float dpr = negative ? (lr < k.cap ? neg_ratio : (lr == k.cap ? 0.5f * neg_ratio : 0.0f)) : ratio;
+    float dcl = (ratio >= k.lo && ratio <= k.hi) ? ratio : 0.0f;
+    float d = f1 < f2 ? dpr : (f2 < f1 ? dcl : 0.5f * (dpr + dcl));
     ratio_out = ratio;
-    return -(g1 * adv * dpr + g2 * adv * dcl);
+    return -adv * d;
 }
 
 __device__ __forceinline__ void accumulate(RowStats& s, float coef, float w, float prow, float ent, float ratio,
@@ -95,7 +99,6 @@ __device__ __forceinline__ void accumulate(RowStats& s, float coef, float w, flo
     s.v[4] += fabsf(ratio - 1.0f) > k.clip ? 1.0f : 0.0f;
     s.v[5] += (adv < 0.0f && lr > k.cap) ? 1.0f : 0.0f;
     s.v[6] += w;
-    s.v[7] += 1.0f;
 }
 
 // One row in registers: x[j] logits (overwritten with dlogits), legal(j) flags.
@@ -177,6 +180,11 @@ __device__ __forceinline__ void block_stats(RowStats& s, double* partials, doubl
     if (threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(partials) = 0ull;  // ready for the next launch
 }
 
+// Rows a grid-stride loop starting at r0 with step `stride` visits below N.
+__device__ __forceinline__ float strided_rows(int64_t r0, int64_t stride, int64_t N) {
+    return r0 < N ? (float)((N - 1 - r0) / stride + 1) : 0.0f;
+}
+
 struct Row8 {
     uint4 logits;
     uint2 mask;
@@ -200,8 +208,8 @@ __device__ __forceinline__ Row8 load_row8(int64_t r, const uint4* logits, const 
 //
 // Mask bytes are 0/1 (torch.bool).  A pair's two bytes become a 32-bit lane
 // mask w (0xFFFF per legal element) with one byte permute and one multiply;
-// then x & w is the logit pair with illegal entries zeroed and
-// (x & w) | (-inf & ~w) the pair with illegal entries at -inf (one LOP3).
+// (x & w) | (-2^100 & ~w) is the logit pair with illegal entries at -2^100
+// (one LOP3).
 // Elementwise arithmetic runs on float2 with the packed FP32 instructions.
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t v) {
     return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
@@ -211,17 +219,16 @@ __device__ __forceinline__ void row8_backward(const Row8& row, const LossControl
     const uint32_t v[4] = {row.logits.x, row.logits.y, row.logits.z, row.logits.w};
     const uint32_t mw[4] = {__byte_perm(row.mask.x, 0u, 0x1100) * 0xffu, __byte_perm(row.mask.x, 0u, 0x3322) * 0xffu,
                             __byte_perm(row.mask.y, 0u, 0x1100) * 0xffu, __byte_perm(row.mask.y, 0u, 0x3322) * 0xffu};
-    uint32_t xm[4], ym[4];
+    // illegal entries become -2^100: exp underflows to exactly 0 and every product with
+    // that 0 stays finite, so they drop out of the sums and get a zero gradient
+    uint32_t xm[4];
     #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        xm[p] = v[p] & mw[p];
-        ym[p] = xm[p] | (0xff80ff80u & ~mw[p]);
-    }
+    for (int p = 0; p < 4; ++p) xm[p] = (v[p] & mw[p]) | (0xf180f180u & ~mw[p]);
     // masked max in bf16 (exact)
-    __nv_bfloat162 m01 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&ym[0]),
-                                 *reinterpret_cast<const __nv_bfloat162*>(&ym[1]));
-    __nv_bfloat162 m23 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&ym[2]),
-                                 *reinterpret_cast<const __nv_bfloat162*>(&ym[3]));
+    __nv_bfloat162 m01 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&xm[0]),
+                                 *reinterpret_cast<const __nv_bfloat162*>(&xm[1]));
+    __nv_bfloat162 m23 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&xm[2]),
+                                 *reinterpret_cast<const __nv_bfloat162*>(&xm[3]));
     __nv_bfloat162 mm = __hmax2(m01, m23);
     float my = fmaxf(__low2float(mm), __high2float(mm)) * LOG2E;
     const float2 L2 = make_float2(LOG2E, LOG2E), NMY = make_float2(-my, -my);
@@ -229,7 +236,7 @@ __device__ __forceinline__ void row8_backward(const Row8& row, const LossControl
     #pragma unroll
     for (int p = 0; p < 4; ++p) {
         X[p] = bf2_to_f2(xm[p]);
-        float2 t = __ffma2_rn(bf2_to_f2(ym[p]), L2, NMY);
+        float2 t = __ffma2_rn(X[p], L2, NMY);
         E[p] = make_float2(exp2f(t.x), exp2f(t.y));
     }
     float2 S = __fadd2_rn(__fadd2_rn(E[0], E[1]), __fadd2_rn(E[2], E[3]));
@@ -289,6 +296,7 @@ __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, co
         cur = nxt;
         r = nr;
     }
+    s.v[7] = strided_rows((int64_t)blockIdx.x * LOSS_BLOCK + threadIdx.x, stride, N);
     block_stats<LOSS_BLOCK>(s, partials, stats);
 }
 
@@ -447,8 +455,9 @@ __global__ void __launch_bounds__(BULK_THREADS, 1) ppo_bf16x8_bulk_kernel(BulkAr
         }
         // rows after the last full tile: direct loads
         if (!failed) {
-            for (int64_t r = ntiles * BULK_T + (int64_t)blockIdx.x * BULK_T + threadIdx.x; r < a.N;
-                 r += (int64_t)gridDim.x * BULK_T) {
+            const int64_t t0 = ntiles * BULK_T + (int64_t)blockIdx.x * BULK_T + threadIdx.x;
+            s.v[7] = (float)used + strided_rows(t0, (int64_t)gridDim.x * BULK_T, a.N);
+            for (int64_t r = t0; r < a.N; r += (int64_t)gridDim.x * BULK_T) {
                 Row8 row = load_row8(r, a.logits, a.mask, a.action, a.old_logp, a.adv, a.weight);
                 uint4 out;
                 row8_backward(row, k, s, out);
@@ -502,6 +511,7 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
         for (int j = 0; j < LOSS_MAX_A; ++j)
             if (j < A) dlogits[r * A + j] = from_f<T>(x[j]);
     }
+    s.v[7] = strided_rows((int64_t)blockIdx.x * LOSS_BLOCK + threadIdx.x, (int64_t)gridDim.x * LOSS_BLOCK, N);
     block_stats<LOSS_BLOCK>(s, partials, stats);
 }
 
