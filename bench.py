@@ -243,6 +243,65 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------- rollout component
+
+
+ROLLOUT_BYTES_HU = 64 * 2 + 40 + 16 + 8 + 16 + 25 + 110 + 100  # state r+w, raw row, address, outputs, history
+
+
+def rollout_component(device, hands=65_536, seed=0):
+    """Fused rollout step over a full self-play rollout (HU 100bb, 13 ranks, cfg2's 65,536 hands).
+
+    A fixed seeded raw policy row per hand (the model is not on this path yet) drives every step.
+    The same rollout runs once untimed to count the decisions each step makes (it is deterministic),
+    then again timed with CUDA events around every step launch.
+    """
+
+    import torch
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.rollout import RolloutStep
+
+    geometry = NLHEGeometry(2, 100.0, 13)
+    stepper = RolloutStep(geometry, seed=seed, iteration=0)
+    g = torch.Generator(device=device).manual_seed(seed + 7)
+    raw = {"type_logits": torch.randn((hands, 1, 3), generator=g, device=device),
+           "omega": torch.softmax(torch.randn((hands, 1, 2), generator=g, device=device), -1),
+           "mu": torch.rand((hands, 1, 2), generator=g, device=device),
+           "s": torch.rand((hands, 1, 2), generator=g, device=device) * 0.3 + 0.02,
+           "iota": torch.rand((hands, 1), generator=g, device=device) * 0.2}
+    counts = []
+    arena = stepper.roots(hands, device=device)
+    for _ in range(400):
+        active = int((~arena.state.terminal).sum())
+        if active == 0:
+            break
+        counts.append(active)
+        stepper.step(arena, raw)
+    arena = stepper.roots(hands, device=device)
+    stream = torch.cuda.current_stream(device)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in counts]
+    torch.cuda.synchronize(device)
+    for a, b in events:
+        a.record(stream)
+        stepper.step(arena, raw)
+        b.record(stream)
+    torch.cuda.synchronize(device)
+    assert bool(arena.state.terminal.all())
+    times = [a.elapsed_time(b) for a, b in events]
+    total_ms = sum(times)
+    decisions = sum(counts)
+    peak, _ = measured_peak()
+    achieved = ROLLOUT_BYTES_HU * decisions / (total_ms / 1000.0) / 1e9
+    return {"workload": "fused rollout step, HU 100bb R13, 65,536 hands to terminal, raw policy at the actor row",
+            "decisions": decisions, "steps": len(counts), "ms": total_ms,
+            "decisions_per_s": decisions / (total_ms / 1000.0),
+            "first_step_us": 1000.0 * times[0],
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "bytes_per_decision": ROLLOUT_BYTES_HU,
+                         "kernel": "rollout_step_kernel"},
+            "gpu_launches": len(counts)}
+
+
 # ----------------------------------------------------------- device arm
 
 
@@ -361,6 +420,8 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
+    if rank == 0:
+        line["components"] = {"rollout_step": rollout_component(device)}
     if rank == 0 and world == 1:
         sample = host_sample(1 << 21, A, 0)
         rate, threads, rows, wall = cpu_loss_rate(sample, seconds=3.0)
