@@ -621,6 +621,74 @@ __global__ void __launch_bounds__(256) rollout_step_kernel(StepArgs A) {
     }
 }
 
+// log pi(act) of one composite-policy row, one thread (hooks.py:1641-1645 via
+// policy.py:113-233).  Pass 1 sums each mixture component over all ticks and
+// over the legal raise range (so the masked mass needs no extra pass); pass 2
+// runs an online softmax over the legal events.
+__device__ float selected_log_row(const RawRow& raw, const LegalSummary& L, int T, int act) {
+    constexpr int MMAX = 8;
+    MixtureEdges me[MMAX];
+    float S[MMAX], Ls[MMAX];
+    const bool any_raise = L.lo <= L.hi;
+    for (int m = 0; m < raw.M; ++m) {
+        me[m] = mixture_edges(raw.mu[m], raw.scale[m], T);
+        float sig, sm_prev;
+        edge_sigmoids(me[m], 0, T, sig, sm_prev);
+        float full = 0.0f, legal = 0.0f;
+        for (int k = 0; k < T; ++k) {
+            float sig_next, sm_next;
+            edge_sigmoids(me[m], k + 1, T, sig_next, sm_next);
+            float v = __fmul_rn(fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev), me[m].width), 0.0f), me[m].inv_norm);
+            full = __fadd_rn(full, v);
+            if (k >= L.lo && k <= L.hi) legal = __fadd_rn(legal, v);
+            sm_prev = sm_next;
+        }
+        S[m] = fmaxf(full, FLT_TINY);
+        Ls[m] = legal;
+    }
+    float mass = 0.0f;
+    for (int m = 0; m < raw.M; ++m) mass = __fadd_rn(mass, __fmul_rn(raw.omega[m], __fdiv_rn(Ls[m], S[m])));
+    const int count = any_raise ? L.hi - L.lo + 1 : 0;
+    const float l0 = raw.logits[0], l1 = raw.logits[1], l2 = raw.logits[2], io = raw.iota;
+    // online softmax over legal events
+    float mx = -INFINITY, sum = 0.0f, la = -INFINITY;
+    auto push = [&](float v, bool is_act) {
+        if (is_act) la = v;
+        if (v == -INFINITY) return;
+        if (v > mx) {
+            sum = __fadd_rn(__fmul_rn(sum, expf(__fsub_rn(mx, v))), 1.0f);
+            mx = v;
+        } else {
+            sum = __fadd_rn(sum, expf(__fsub_rn(v, mx)));
+        }
+    };
+    if (L.call_legal) push(l0, act == 0);
+    push(L.call_legal ? l1 : l0, act == 1);
+    if (any_raise) {
+        float sm_prev[MMAX];
+        for (int m = 0; m < raw.M; ++m) {
+            float sig;
+            edge_sigmoids(me[m], L.lo, T, sig, sm_prev[m]);
+        }
+        for (int k = L.lo; k <= L.hi; ++k) {
+            float mixk = 0.0f;
+            for (int m = 0; m < raw.M; ++m) {
+                float sig_next, sm_next;
+                edge_sigmoids(me[m], k + 1, T, sig_next, sm_next);
+                float v = __fmul_rn(fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev[m]), me[m].width), 0.0f),
+                                    me[m].inv_norm);
+                mixk = __fadd_rn(mixk, __fmul_rn(raw.omega[m], __fdiv_rn(v, S[m])));
+                sm_prev[m] = sm_next;
+            }
+            float cond = mass > 0.0f ? __fdiv_rn(mixk, fmaxf(mass, POLICY_EPS)) : __fdiv_rn(1.0f, (float)count);
+            float rp = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, io), cond), __fmul_rn(io, k == L.hi ? 1.0f : 0.0f));
+            push(rp > 0.0f ? __fadd_rn(l2, logf(fmaxf(rp, POLICY_EPS))) : -INFINITY, act == k + 2);
+        }
+    }
+    float psel = la == -INFINITY ? 0.0f : __fdiv_rn(expf(__fsub_rn(la, mx)), sum);
+    return logf(fmaxf(psel, POLICY_EPS));
+}
+
 // Reach update: block per hand, thread per private row --------------------
 template <int P>
 __global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, const int32_t* action,
@@ -638,65 +706,7 @@ __global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, con
         int act = action[b];
         int rows = street_before == 0 ? d.K : d.H;
         for (int r = threadIdx.x; r < rows; r += blockDim.x) {
-            RawRow raw = raw_row(pol, b * pol.rows + r);
-            // full composite probability of one row, sequential over events
-            float mixk = 0.0f, mass = 0.0f;
-            int count = 0, top = -1;
-            for (int k = 0; k < d.T; ++k) if (L(k + 2)) { ++count; top = k; }
-            float l0 = raw.logits[0], l1 = raw.logits[1], l2 = raw.logits[2];
-            // two passes: masses then the softmax over legal events
-            float S[8], norm[8];
-            for (int m = 0; m < raw.M; ++m) {
-                float loc = raw.mu[m], sc = raw.scale[m];
-                float z0 = __fdiv_rn(__fsub_rn(0.0f, loc), sc);
-                float zT = __fdiv_rn(__fsub_rn(edge_of(d.T, d.T), loc), sc);
-                norm[m] = fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(zT), sigmoid_f(-z0)), -expm1f(__fsub_rn(z0, zT))), FLT_TINY);
-                float s = 0.0f;
-                for (int k = 0; k < d.T; ++k) {
-                    float lo = __fdiv_rn(__fsub_rn(edge_of(k, d.T), loc), sc);
-                    float hi = __fdiv_rn(__fsub_rn(edge_of(k + 1, d.T), loc), sc);
-                    float v = fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(hi), sigmoid_f(-lo)), -expm1f(__fsub_rn(lo, hi))), 0.0f);
-                    s = __fadd_rn(s, __fdiv_rn(v, norm[m]));
-                }
-                S[m] = fmaxf(s, FLT_TINY);
-            }
-            // mixture per tick (recomputed) -> mass, then logits
-            auto mixture = [&](int k) {
-                float acc = 0.0f;
-                for (int m = 0; m < raw.M; ++m) {
-                    float loc = raw.mu[m], sc = raw.scale[m];
-                    float lo = __fdiv_rn(__fsub_rn(edge_of(k, d.T), loc), sc);
-                    float hi = __fdiv_rn(__fsub_rn(edge_of(k + 1, d.T), loc), sc);
-                    float v = fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(hi), sigmoid_f(-lo)), -expm1f(__fsub_rn(lo, hi))), 0.0f);
-                    acc = __fadd_rn(acc, __fmul_rn(raw.omega[m], __fdiv_rn(__fdiv_rn(v, norm[m]), S[m])));
-                }
-                return acc;
-            };
-            for (int k = L.lo; k <= L.hi && k < d.T; ++k) mass = __fadd_rn(mass, mixture(k));
-            float io = raw.iota;
-            auto logit_of = [&](int e) {
-                if (e == 0) return l0;
-                if (e == 1) return L.call_legal ? l1 : l0;
-                int k = e - 2;
-                float mk = mixture(k);
-                float cond = mass > 0.0f ? __fdiv_rn(mk, fmaxf(mass, POLICY_EPS)) : __fdiv_rn(1.0f, (float)max(count, 1));
-                float rp = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, io), cond), __fmul_rn(io, k == top ? 1.0f : 0.0f));
-                return rp > 0.0f ? __fadd_rn(l2, logf(fmaxf(rp, POLICY_EPS))) : -INFINITY;
-            };
-            // max and denominator over legal events (one pass each)
-            float mx = -INFINITY;
-            float lg_cache_sel = -INFINITY;
-            for (int e = 0; e < d.E; ++e) {
-                if (!L(e)) continue;
-                float v = logit_of(e);
-                if (e == act) lg_cache_sel = v;
-                mx = fmaxf(mx, v);
-            }
-            float den = 0.0f;
-            for (int e = 0; e < d.E; ++e) if (L(e)) den = __fadd_rn(den, expf(__fsub_rn(logit_of(e), mx)));
-            float psel = __fdiv_rn(expf(__fsub_rn(lg_cache_sel, mx)), den);
-            sel[r] = logf(fmaxf(psel, POLICY_EPS));
-            (void)mixk;
+            sel[r] = selected_log_row(raw_row(pol, b * pol.rows + r), L, d.T, act);
         }
         __syncthreads();
         // board after the chance closure

@@ -28,6 +28,37 @@ __device__ __forceinline__ float sigmoid_f(float x) {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
 }
 
+// One mixture component of the discretised logistic over T ticks: edges
+// x_i = linspace(0, 1, T+1)[i], z_i = (x_i - mu) / s.  Tick k has mass
+// sigma(z_{k+1}) * sigma(-z_k) * (-expm1(z_k - z_{k+1})); the edges are equally
+// spaced, so the last factor is one constant per component, and each edge's
+// sigmoid pair costs one exponential and one reciprocal:
+//   sigma(z) = 1 / (1 + e^{-z}),  sigma(-z) = e^{-z} sigma(z)  (1 when e^{-z} overflows).
+// The normaliser sigma(z_T) sigma(-z_0) (-expm1(z_0 - z_T)) keeps the
+// reference's form.
+struct MixtureEdges {
+    float loc, inv_scale, width, inv_norm;
+};
+
+__device__ __forceinline__ MixtureEdges mixture_edges(float loc, float sc, int T) {
+    MixtureEdges m;
+    m.loc = loc;
+    m.inv_scale = __fdiv_rn(1.0f, sc);
+    float z0 = __fdiv_rn(__fsub_rn(0.0f, loc), sc);
+    float zT = __fdiv_rn(__fsub_rn(edge_of(T, T), loc), sc);
+    float norm = __fmul_rn(__fmul_rn(sigmoid_f(zT), sigmoid_f(-z0)), -expm1f(__fsub_rn(z0, zT)));
+    m.inv_norm = __fdiv_rn(1.0f, fmaxf(norm, FLT_TINY));
+    m.width = -expm1f(-__fmul_rn(__fdiv_rn(1.0f, (float)T), m.inv_scale));
+    return m;
+}
+
+__device__ __forceinline__ void edge_sigmoids(const MixtureEdges& m, int i, int T, float& sig, float& sm) {
+    float z = __fmul_rn(__fsub_rn(edge_of(i, T), m.loc), m.inv_scale);
+    float ex = expf(-z);
+    sig = __fdividef(1.0f, __fadd_rn(1.0f, ex));
+    sm = isinf(ex) ? 1.0f : __fmul_rn(ex, sig);
+}
+
 // Legal-event sources ------------------------------------------------------
 struct MaskRow {           // a materialised [E] uint8 row
     const uint8_t* m;
@@ -77,25 +108,25 @@ __device__ float warp_policy_row(const RawRow& raw, const Legal& legal, int T, i
     #pragma unroll
     for (int j = 0; j < CHUNK_MAX; ++j) mix[j] = 0.0f;
     for (int m = 0; m < raw.M; ++m) {
-        float loc = raw.mu[m], sc = raw.scale[m];
-        float z0 = __fdiv_rn(__fsub_rn(0.0f, loc), sc);
-        float zT = __fdiv_rn(__fsub_rn(edge_of(T, T), loc), sc);
-        float norm = __fmul_rn(__fmul_rn(sigmoid_f(zT), sigmoid_f(-z0)), -expm1f(__fsub_rn(z0, zT)));
-        norm = fmaxf(norm, FLT_TINY);
+        MixtureEdges mx_m = mixture_edges(raw.mu[m], raw.scale[m], T);
         float tick[CHUNK_MAX];
         float part = 0.0f;
+        // ticks of this lane's chunk: tick k needs sigma(-z_k) and sigma(z_{k+1})
+        const int k0 = e0 - 2;
+        float sig_unused, sm_prev;
+        edge_sigmoids(mx_m, k0 > 0 ? k0 : 0, T, sig_unused, sm_prev);
         #pragma unroll
         for (int j = 0; j < CHUNK_MAX; ++j) {
             tick[j] = 0.0f;
             int e = e0 + j;
-            if (j < C && e >= 2 && e < E) {
-                int k = e - 2;
-                float lo = __fdiv_rn(__fsub_rn(edge_of(k, T), loc), sc);
-                float hi = __fdiv_rn(__fsub_rn(edge_of(k + 1, T), loc), sc);
-                float v = __fmul_rn(__fmul_rn(sigmoid_f(hi), sigmoid_f(-lo)), -expm1f(__fsub_rn(lo, hi)));
-                v = fmaxf(v, 0.0f);
-                tick[j] = __fdiv_rn(v, norm);
+            int k = e - 2;
+            if (j < C && k >= 0 && e < E) {
+                float sig_next, sm_next;
+                edge_sigmoids(mx_m, k + 1, T, sig_next, sm_next);
+                float v = fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev), mx_m.width), 0.0f);
+                tick[j] = __fmul_rn(v, mx_m.inv_norm);
                 part = __fadd_rn(part, tick[j]);
+                sm_prev = sm_next;
             }
         }
         float total = fmaxf(warp_sum(part), FLT_TINY);

@@ -532,11 +532,11 @@ def test_adam_matches_reference_golden(gold):
 
 
 def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
-    """694,733 rows: 700 full 992-row tiles (several passes of the 4-stage ring per CTA) + 333 tail rows."""
+    """1,389,133 rows: 700 full 1984-row tiles (several passes of the 2-stage ring per CTA) + 333 tail rows."""
 
     from pbg_b200.loss import LossConfig, fused_ppo_backward
 
-    N, A = 992 * 700 + 333, 8
+    N, A = 1984 * 700 + 333, 8
     logits, mask, action, old, adv, weight = _loss_inputs(N, A, 17)
     x16 = cuda(logits).to(torch.bfloat16)
     for step in range(2):  # the scratch counter must reset between launches
