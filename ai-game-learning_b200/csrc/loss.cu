@@ -26,7 +26,7 @@
 // logits), prefetches the next row before computing the current one, and
 // does the elementwise work on bf16/f32 pairs.  Compiled with -ftz=true:
 // denormal probabilities flush to zero.
-// When every stream is 16-byte aligned and at least one 1984-row tile exists,
+// When every stream is 16-byte aligned and at least one 992-row tile exists,
 // the rows are staged through shared memory by bulk-async copies (see
 // ppo_bf16x8_bulk_kernel).  Per-block statistics go to caller scratch; the
 // last block to finish sums them in block order (deterministic) and clears
@@ -303,8 +303,8 @@ __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, co
 // A == 8, bf16, bulk-async staged, warp-specialised -----------------------
 //
 // One persistent CTA per SM (1024 threads): warp 31 is the producer, warps
-// 0..30 consume.  Tiles of BULK_T = 1984 rows (two rows per consumer thread)
-// stream through a ring of BULK_STAGES = 2 shared-memory stages.  The producer's
+// 0..30 consume.  Tiles of BULK_T = 992 rows (one row per consumer thread)
+// stream through a ring of BULK_STAGES shared-memory stages.  The producer's
 // lane 0 fills a stage with six plain 1D bulk copies (cp.async.bulk global ->
 // shared, no tensor map, no multicast) completing on the stage's "full"
 // mbarrier; each consumer warp waits on it, computes its 32 rows, stores
@@ -315,15 +315,14 @@ __global__ void __launch_bounds__(LOSS_BLOCK, 4) ppo_bf16x8_kernel(int64_t N, co
 // waits (bounded again) for its copies still in flight, and the launch ends.
 constexpr int BULK_CONSUMER_WARPS = 31;
 constexpr int BULK_THREADS = 32 * (BULK_CONSUMER_WARPS + 1);
-constexpr int BULK_ROWS_PER_THREAD = 2;
-constexpr int BULK_T = 32 * BULK_CONSUMER_WARPS * BULK_ROWS_PER_THREAD;  // 1984 rows
-constexpr int BULK_STAGES = 2;
+constexpr int BULK_T = 32 * BULK_CONSUMER_WARPS;  // 992 rows
+constexpr int BULK_STAGES = 4;
 constexpr uint32_t BULK_OFF_MASK = BULK_T * 16;
 constexpr uint32_t BULK_OFF_ACT = BULK_OFF_MASK + BULK_T * 8;
 constexpr uint32_t BULK_OFF_OLD = BULK_OFF_ACT + BULK_T * 4;
 constexpr uint32_t BULK_OFF_ADV = BULK_OFF_OLD + BULK_T * 4;
 constexpr uint32_t BULK_OFF_W = BULK_OFF_ADV + BULK_T * 4;
-constexpr uint32_t BULK_TILE_BYTES = BULK_OFF_W + BULK_T * 4;  // 79,360 B, every offset a multiple of 16
+constexpr uint32_t BULK_TILE_BYTES = BULK_OFF_W + BULK_T * 4;  // 39,680 B, every offset a multiple of 16
 constexpr size_t BULK_SMEM = (size_t)BULK_STAGES * BULK_TILE_BYTES;
 constexpr uint32_t BULK_WAIT_TRIES = 1u << 22;
 
@@ -440,32 +439,25 @@ __global__ void __launch_bounds__(BULK_THREADS, 1) ppo_bf16x8_bulk_kernel(BulkAr
                 break;
             }
             const unsigned char* base = ring + (size_t)st * BULK_TILE_BYTES;
-            Row8 row[BULK_ROWS_PER_THREAD];
-            #pragma unroll
-            for (int j = 0; j < BULK_ROWS_PER_THREAD; ++j) {
-                const int rr = threadIdx.x + j * 32 * BULK_CONSUMER_WARPS;
-                row[j].logits = reinterpret_cast<const uint4*>(base)[rr];
-                row[j].mask = reinterpret_cast<const uint2*>(base + BULK_OFF_MASK)[rr];
-                row[j].act = reinterpret_cast<const int32_t*>(base + BULK_OFF_ACT)[rr];
-                row[j].old = reinterpret_cast<const float*>(base + BULK_OFF_OLD)[rr];
-                row[j].adv = reinterpret_cast<const float*>(base + BULK_OFF_ADV)[rr];
-                row[j].w = reinterpret_cast<const float*>(base + BULK_OFF_W)[rr];
-            }
+            const int rr = threadIdx.x;  // warp * 32 + lane < BULK_T
+            Row8 row;
+            row.logits = reinterpret_cast<const uint4*>(base)[rr];
+            row.mask = reinterpret_cast<const uint2*>(base + BULK_OFF_MASK)[rr];
+            row.act = reinterpret_cast<const int32_t*>(base + BULK_OFF_ACT)[rr];
+            row.old = reinterpret_cast<const float*>(base + BULK_OFF_OLD)[rr];
+            row.adv = reinterpret_cast<const float*>(base + BULK_OFF_ADV)[rr];
+            row.w = reinterpret_cast<const float*>(base + BULK_OFF_W)[rr];
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty[st]));  // this warp's rows are in registers
-            #pragma unroll
-            for (int j = 0; j < BULK_ROWS_PER_THREAD; ++j) {
-                uint4 out;
-                row8_backward(row[j], k, s, out);
-                __stcs(a.dlogits + tile * BULK_T + threadIdx.x + j * 32 * BULK_CONSUMER_WARPS, out);
-            }
+            uint4 out;
+            row8_backward(row, k, s, out);
+            __stcs(a.dlogits + tile * BULK_T + rr, out);
         }
         // rows after the last full tile: direct loads
         if (!failed) {
-            const int64_t t0 = ntiles * BULK_T + (int64_t)blockIdx.x * (32 * BULK_CONSUMER_WARPS) + threadIdx.x;
-            const int64_t step = (int64_t)gridDim.x * (32 * BULK_CONSUMER_WARPS);
-            s.v[7] = (float)(used * BULK_ROWS_PER_THREAD) + strided_rows(t0, step, a.N);
-            for (int64_t r = t0; r < a.N; r += step) {
+            const int64_t t0 = ntiles * BULK_T + (int64_t)blockIdx.x * BULK_T + threadIdx.x;
+            s.v[7] = (float)used + strided_rows(t0, (int64_t)gridDim.x * BULK_T, a.N);
+            for (int64_t r = t0; r < a.N; r += (int64_t)gridDim.x * BULK_T) {
                 Row8 row = load_row8(r, a.logits, a.mask, a.action, a.old_logp, a.adv, a.weight);
                 uint4 out;
                 row8_backward(row, k, s, out);

@@ -406,6 +406,31 @@ def _loss_inputs(N, A, seed, cap_rows=True):
     return logits, mask, action, old, adv, weight
 
 
+def _boundary_rows(logits, mask, action, old, clip=0.2, log_cap=math.inf, tol=1e-5):
+    """Rows whose importance ratio is within `tol` of 1 +- clip or whose log ratio is within `tol` of the cap.
+
+    The clipped objective's gradient jumps there, so an fp32 evaluation and the double-precision oracle can
+    land on opposite sides of the edge; those rows are the only ones allowed to differ beyond tolerance.
+    """
+
+    x = np.where(mask, logits.astype(np.float64), -np.inf)
+    mx = x.max(1, keepdims=True)
+    lse = np.log(np.exp(x - mx).sum(1)) + mx[:, 0]
+    lr = x[np.arange(len(x)), action] - lse - old.astype(np.float64)
+    ratio = np.exp(lr)
+    near = (np.abs(ratio - (1 - clip)) < tol) | (np.abs(ratio - (1 + clip)) < tol)
+    if math.isfinite(log_cap):
+        near |= np.abs(lr - log_cap) < tol
+    return near
+
+
+def _assert_close_except_boundary(got, ref, rows_near, rtol, atol):
+    bad = ~np.isclose(got, ref, rtol=rtol, atol=atol)
+    bad_rows = bad.any(1) if bad.ndim == 2 else bad
+    assert np.all(rows_near[bad_rows]), f"{int((bad_rows & ~rows_near).sum())} rows differ away from a clip edge"
+    assert bad_rows.sum() <= max(2, len(bad_rows) // 100000)
+
+
 @pytest.mark.parametrize("A,cap", [(8, None), (8, 1.5), (3, None), (17, 2.0), (1, None)])
 def test_fp32_loss_backward_matches_oracle(A, cap):
     from pbg_b200.loss import LossConfig, fused_ppo_backward
@@ -418,7 +443,8 @@ def test_fp32_loss_backward_matches_oracle(A, cap):
                                      log_cap=math.inf if cap is None else math.log(cap))
     # absolute floor: the size of one row's gradient terms (coef * |adv| * ratio)
     scale = max(np.abs(ref_d).max(), np.abs(adv).max() / N)
-    np.testing.assert_allclose(host(d), ref_d, rtol=1e-5, atol=1e-5 * scale)
+    near = _boundary_rows(logits, mask, action, old, 0.2, math.inf if cap is None else math.log(cap))
+    _assert_close_except_boundary(host(d), ref_d, near, rtol=1e-5, atol=1e-5 * scale)
     # sums over N rows: absolute floor of 1e-9 per row
     np.testing.assert_allclose(host(stats)[[0, 1, 2, 3, 6, 7]], ref_s[[0, 1, 2, 3, 6, 7]], rtol=1e-5, atol=1e-9 * N)
     assert abs(host(stats)[4] - ref_s[4]) <= 2 and abs(host(stats)[5] - ref_s[5]) <= 2
@@ -472,7 +498,8 @@ def test_bf16_vector_path_matches_torch_fp32_autograd():
     ref = x.grad
     got = d.float()
     scale = ref.abs().max()
-    torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-2 * float(scale))
+    near = _boundary_rows(host(x16.float()), mask, action, old, 0.2, math.log(2.0))
+    _assert_close_except_boundary(host(got), host(ref), near, rtol=2e-2, atol=2e-2 * float(scale))
     torch.testing.assert_close(torch.tensor(float(stats[0])), total.detach().cpu().double().float(), rtol=1e-4,
                                atol=1e-6)
 
@@ -532,11 +559,11 @@ def test_adam_matches_reference_golden(gold):
 
 
 def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
-    """1,389,133 rows: 700 full 1984-row tiles (several passes of the 2-stage ring per CTA) + 333 tail rows."""
+    """694,733 rows: 700 full 992-row tiles (several passes of the 4-stage ring per CTA) + 333 tail rows."""
 
     from pbg_b200.loss import LossConfig, fused_ppo_backward
 
-    N, A = 1984 * 700 + 333, 8
+    N, A = 992 * 700 + 333, 8
     logits, mask, action, old, adv, weight = _loss_inputs(N, A, 17)
     x16 = cuda(logits).to(torch.bfloat16)
     for step in range(2):  # the scratch counter must reset between launches
@@ -545,5 +572,6 @@ def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
         assert float(stats[7]) == N, "a bulk stage wait timed out"
     ref, ref_s = O.ppo_categorical(host(x16.float()), mask, action, old, adv, weight, log_cap=math.log(2.0))
     scale = float(np.abs(ref).max())
-    np.testing.assert_allclose(host(d.float()), ref, rtol=2e-2, atol=2e-2 * scale)
+    near = _boundary_rows(host(x16.float()), mask, action, old, 0.2, math.log(2.0))
+    _assert_close_except_boundary(host(d.float()), ref, near, rtol=2e-2, atol=2e-2 * scale)
     np.testing.assert_allclose(host(stats)[[0, 1, 2, 3, 6]], ref_s[[0, 1, 2, 3, 6]], rtol=1e-4, atol=1e-9 * N)
