@@ -257,34 +257,6 @@ __device__ __forceinline__ void smallest3(const int64_t* key, uint64_t used, int
     out[0] = bi[0]; out[1] = bi[1]; out[2] = bi[2];
 }
 
-// Warp version: lane holds cards lane and lane+32; three argmin rounds.
-__device__ __forceinline__ void warp_smallest3(uint64_t ns, int64_t root, int64_t path, int64_t draw_base,
-                                               int64_t lane_id, int64_t epoch, uint64_t used, int D,
-                                               int (&out)[3]) {
-    const int lane = threadIdx.x & 31;
-    int64_t k0 = INT64_MAX, k1 = INT64_MAX;
-    int c0 = lane, c1 = lane + 32;
-    if (c0 < D && !((used >> c0) & 1ULL)) k0 = rng_key(ns, root, path, draw_base + c0, lane_id, epoch);
-    if (c1 < D && !((used >> c1) & 1ULL)) k1 = rng_key(ns, root, path, draw_base + c1, lane_id, epoch);
-    if (c0 >= D) c0 = 64;
-    if (c1 >= D) c1 = 64;
-    #pragma unroll
-    for (int r = 0; r < 3; ++r) {
-        bool first_is_min = (k0 < k1) || (k0 == k1 && c0 < c1);
-        int64_t bk = first_is_min ? k0 : k1;
-        int bc = first_is_min ? c0 : c1;
-        #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            int64_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
-            int oc = __shfl_xor_sync(0xffffffffu, bc, o);
-            if (ok < bk || (ok == bk && oc < bc)) { bk = ok; bc = oc; }
-        }
-        out[r] = bc;
-        if (bc == c0) { k0 = INT64_MAX; c0 = 64; }
-        if (bc == c1) { k1 = INT64_MAX; c1 = 64; }
-    }
-}
-
 // History slot writes ------------------------------------------------------
 struct HistoryToken {
     int64_t actor, street, action;
@@ -303,13 +275,6 @@ __device__ __forceinline__ int history_length(const pbg_history& h, int64_t b) {
     int n = 0;
     for (int t = 0; t < h.tokens; ++t) n += h.mask[b * h.tokens + t] != 0;
     return n;
-}
-
-__device__ __forceinline__ int warp_history_length(const pbg_history& h, int64_t b) {
-    const int lane = threadIdx.x & 31;
-    int n = 0;
-    for (int t = lane; t < h.tokens; t += 32) n += h.mask[b * h.tokens + t] != 0;
-    return __reduce_add_sync(0xffffffffu, n);
 }
 
 template <int P>
@@ -494,8 +459,9 @@ __global__ void history_kernel(Geo d, int64_t B, pbg_state st, const int32_t* ac
         if (action) { on = !h.terminal; t = player_token(h, action[b], d.T); }
         else { on = active[b] != 0; t = chance_token(h); }
         if (!on) continue;
-        int len = history_length(hist, b);
+        int len = hist.length ? hist.length[b] : history_length(hist, b);
         if (len < hist.tokens) write_token(hist, b, len, t);
+        if (hist.length) hist.length[b] = len + 1 < hist.tokens ? len + 1 : hist.tokens;
     }
 }
 
@@ -543,32 +509,53 @@ struct StepArgs {
     pbg_leaf leaf;
 };
 
+// Three smallest (key, card) CHANCE keys among unused cards, one thread,
+// keys computed on the fly (hooks.py:1064-1075 order: stable by card index).
+__device__ __forceinline__ void chance_smallest3(uint64_t ns, int64_t root, int64_t path, int64_t draw_base,
+                                                 int64_t lane_id, int64_t epoch, uint64_t used, int D, int (&out)[3]) {
+    int64_t bk[3] = {INT64_MAX, INT64_MAX, INT64_MAX};
+    int bi[3] = {D, D, D};
+    for (int c = 0; c < D; ++c) {
+        if ((used >> c) & 1ULL) continue;
+        int64_t k = rng_key(ns, root, path, draw_base + c, lane_id, epoch);
+        if (k < bk[2] || (k == bk[2] && c < bi[2])) {
+            bk[2] = k; bi[2] = c;
+            if (bk[2] < bk[1] || (bk[2] == bk[1] && bi[2] < bi[1])) {
+                int64_t tk = bk[1]; int ti = bi[1]; bk[1] = bk[2]; bi[1] = bi[2]; bk[2] = tk; bi[2] = ti;
+                if (bk[1] < bk[0] || (bk[1] == bk[0] && bi[1] < bi[0])) {
+                    tk = bk[0]; ti = bi[0]; bk[0] = bk[1]; bi[0] = bi[1]; bk[1] = tk; bi[1] = ti;
+                }
+            }
+        }
+    }
+    out[0] = bi[0]; out[1] = bi[1]; out[2] = bi[2];
+}
+
+// Fused sampled rollout step: one thread per hand.  Consecutive threads own
+// consecutive hands, so every state column is read and written coalesced.
 template <int P>
-__global__ void __launch_bounds__(256) rollout_step_kernel(StepArgs A) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+__global__ void __launch_bounds__(128) rollout_step_kernel(StepArgs A) {
     const Geo& d = A.d;
-    const int C = (d.E + 31) / 32;
-    for (int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; b < A.B; b += warps) {
-        Hand<P> h;
-        h.load(A.st, b);
-        if (h.terminal) {
-            if (lane == 0) {
-                A.action[b] = -1;
-                A.selected[b] = 0.0f;
-                if (A.new_leaf) A.new_leaf[b] = 0;
-                if (A.decision) { A.decision[4 * b] = -1; A.decision[4 * b + 1] = -1; A.decision[4 * b + 2] = 1; A.decision[4 * b + 3] = 0; }
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < A.B; b += (int64_t)gridDim.x * blockDim.x) {
+        if (A.st.terminal[b]) {
+            A.action[b] = -1;
+            A.selected[b] = 0.0f;
+            if (A.new_leaf) A.new_leaf[b] = 0;
+            if (A.decision) {
+                A.decision[4 * b] = -1; A.decision[4 * b + 1] = -1; A.decision[4 * b + 2] = 1; A.decision[4 * b + 3] = 0;
             }
             continue;
         }
-        int64_t root = A.root_path[2 * b], path = A.root_path[2 * b + 1];
-        int64_t rl = A.lane ? A.lane[b] : 0, re = A.retry ? A.retry[b] : 0;
+        Hand<P> h;
+        h.load(A.st, b);
+        const int64_t root = A.root_path[2 * b], path = A.root_path[2 * b + 1];
+        const int64_t rl = A.lane ? A.lane[b] : 0, re = A.retry ? A.retry[b] : 0;
         // sample at the owner's private row (rollout.py:1604-1621, hooks.py:1489-1541)
         LegalSummary L = h.legality(d.T);
-        int a = h.to_act;
-        int combo = h.get(h.combo, a);
+        const int a = h.to_act;
         int64_t row = 0;
         if (A.pol.rows > 1) {
+            int combo = h.get(h.combo, a);
             if (h.street == 0) {
                 int c0, c1;
                 combo_cards(d.D, d.first, combo, c0, c1);
@@ -577,116 +564,52 @@ __global__ void __launch_bounds__(256) rollout_step_kernel(StepArgs A) {
                 row = combo;
             }
         }
-        RawRow raw = raw_row(A.pol, b * A.pol.rows + row);
-        float p[CHUNK_MAX];
-        float mass = warp_policy_row(raw, L, d.T, d.E, C, p);
-        int64_t key = rng_key(A.ns_action, root, path, 0, rl, re);
-        int act = warp_sample(p, d.E, C, mass, key);
-        float psel = warp_fetch(p, act, C);
-        float logp = logf(fmaxf(psel, POLICY_EPS));
+        ClosedPolicy pol;
+        pol.init(raw_row(A.pol, b * A.pol.rows + row), L, d.T);
+        const int64_t key = rng_key(A.ns_action, root, path, 0, rl, re);
+        const int act = pol.sample(key_uniform(key));
+        const float logp = logf(fmaxf(pol.prob(act), POLICY_EPS));
         // transition (hooks.py:1656-1700)
-        int len = A.hist.tokens > 0 ? warp_history_length(A.hist, b) : 0;
-        HistoryToken tok = player_token(h, act, d.T);
-        if (lane == 0 && A.hist.tokens > 0 && len < A.hist.tokens) write_token(A.hist, b, len, tok);
+        const bool with_history = A.hist.tokens > 0;
+        int len = 0;
+        if (with_history) len = A.hist.length ? A.hist.length[b] : history_length(A.hist, b);
+        if (with_history && len < A.hist.tokens) write_token(A.hist, b, len, player_token(h, act, d.T));
         ++len;
-        int street_before = h.street;
+        const int street_before = h.street;
         h.step(act);
         for (int gen = 0; gen < 3; ++gen) {
             bool needs = h.needs_chance();
-            if (needs) {
-                if (lane == 0 && A.hist.tokens > 0 && len < A.hist.tokens) write_token(A.hist, b, len, chance_token(h));
-                ++len;
-            }
             int dealt[3] = {0, 1, 2};
             if (needs) {
-                uint64_t used = h.used_cards(d.D, d.first);
-                warp_smallest3(A.ns_chance, root, path, (int64_t)gen * d.D, rl, re, used, d.D, dealt);
+                if (with_history && len < A.hist.tokens) write_token(A.hist, b, len, chance_token(h));
+                ++len;
+                chance_smallest3(A.ns_chance, root, path, (int64_t)gen * d.D, rl, re, h.used_cards(d.D, d.first), d.D,
+                                 dealt);
             }
             h.apply_deal(needs, dealt, d.first);
         }
-        if (lane == 0) {
-            h.store(A.st, b);
-            A.action[b] = act;
-            A.selected[b] = logp;
-            A.root_path[2 * b + 1] = child_path(path, 1);
-            if (A.decision) {
-                A.decision[4 * b] = a;
-                A.decision[4 * b + 1] = street_before;
-                A.decision[4 * b + 2] = L.lo;
-                A.decision[4 * b + 3] = (L.hi & 0xffff) | ((L.call_legal ? 1 : 0) << 16);
-            }
-            if (A.new_leaf) A.new_leaf[b] = h.terminal;
-            if (h.terminal) write_leaf(h, d.D, d.first, A.leaf, b);
+        if (with_history && A.hist.length) A.hist.length[b] = len < A.hist.tokens ? len : A.hist.tokens;
+        h.store(A.st, b);
+        A.action[b] = act;
+        A.selected[b] = logp;
+        A.root_path[2 * b + 1] = child_path(path, 1);
+        if (A.decision) {
+            A.decision[4 * b] = a;
+            A.decision[4 * b + 1] = street_before;
+            A.decision[4 * b + 2] = L.lo;
+            A.decision[4 * b + 3] = (L.hi & 0xffff) | ((L.call_legal ? 1 : 0) << 16);
         }
+        if (A.new_leaf) A.new_leaf[b] = h.terminal;
+        if (h.terminal) write_leaf(h, d.D, d.first, A.leaf, b);
     }
 }
 
 // log pi(act) of one composite-policy row, one thread (hooks.py:1641-1645 via
-// policy.py:113-233).  Pass 1 sums each mixture component over all ticks and
-// over the legal raise range (so the masked mass needs no extra pass); pass 2
-// runs an online softmax over the legal events.
-__device__ float selected_log_row(const RawRow& raw, const LegalSummary& L, int T, int act) {
-    constexpr int MMAX = 8;
-    MixtureEdges me[MMAX];
-    float S[MMAX], Ls[MMAX];
-    const bool any_raise = L.lo <= L.hi;
-    for (int m = 0; m < raw.M; ++m) {
-        me[m] = mixture_edges(raw.mu[m], raw.scale[m], T);
-        float sig, sm_prev;
-        edge_sigmoids(me[m], 0, T, sig, sm_prev);
-        float full = 0.0f, legal = 0.0f;
-        for (int k = 0; k < T; ++k) {
-            float sig_next, sm_next;
-            edge_sigmoids(me[m], k + 1, T, sig_next, sm_next);
-            float v = __fmul_rn(fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev), me[m].width), 0.0f), me[m].inv_norm);
-            full = __fadd_rn(full, v);
-            if (k >= L.lo && k <= L.hi) legal = __fadd_rn(legal, v);
-            sm_prev = sm_next;
-        }
-        S[m] = fmaxf(full, FLT_TINY);
-        Ls[m] = legal;
-    }
-    float mass = 0.0f;
-    for (int m = 0; m < raw.M; ++m) mass = __fadd_rn(mass, __fmul_rn(raw.omega[m], __fdiv_rn(Ls[m], S[m])));
-    const int count = any_raise ? L.hi - L.lo + 1 : 0;
-    const float l0 = raw.logits[0], l1 = raw.logits[1], l2 = raw.logits[2], io = raw.iota;
-    // online softmax over legal events
-    float mx = -INFINITY, sum = 0.0f, la = -INFINITY;
-    auto push = [&](float v, bool is_act) {
-        if (is_act) la = v;
-        if (v == -INFINITY) return;
-        if (v > mx) {
-            sum = __fadd_rn(__fmul_rn(sum, expf(__fsub_rn(mx, v))), 1.0f);
-            mx = v;
-        } else {
-            sum = __fadd_rn(sum, expf(__fsub_rn(v, mx)));
-        }
-    };
-    if (L.call_legal) push(l0, act == 0);
-    push(L.call_legal ? l1 : l0, act == 1);
-    if (any_raise) {
-        float sm_prev[MMAX];
-        for (int m = 0; m < raw.M; ++m) {
-            float sig;
-            edge_sigmoids(me[m], L.lo, T, sig, sm_prev[m]);
-        }
-        for (int k = L.lo; k <= L.hi; ++k) {
-            float mixk = 0.0f;
-            for (int m = 0; m < raw.M; ++m) {
-                float sig_next, sm_next;
-                edge_sigmoids(me[m], k + 1, T, sig_next, sm_next);
-                float v = __fmul_rn(fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev[m]), me[m].width), 0.0f),
-                                    me[m].inv_norm);
-                mixk = __fadd_rn(mixk, __fmul_rn(raw.omega[m], __fdiv_rn(v, S[m])));
-                sm_prev[m] = sm_next;
-            }
-            float cond = mass > 0.0f ? __fdiv_rn(mixk, fmaxf(mass, POLICY_EPS)) : __fdiv_rn(1.0f, (float)count);
-            float rp = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, io), cond), __fmul_rn(io, k == L.hi ? 1.0f : 0.0f));
-            push(rp > 0.0f ? __fadd_rn(l2, logf(fmaxf(rp, POLICY_EPS))) : -INFINITY, act == k + 2);
-        }
-    }
-    float psel = la == -INFINITY ? 0.0f : __fdiv_rn(expf(__fsub_rn(la, mx)), sum);
-    return logf(fmaxf(psel, POLICY_EPS));
+// policy.py:113-233), through the closed-form composition.
+__device__ __forceinline__ float selected_log_row(const RawRow& raw, const LegalSummary& L, int T, int act) {
+    ClosedPolicy pol;
+    pol.init(raw, L, T);
+    return logf(fmaxf(pol.prob(act), POLICY_EPS));
 }
 
 // Reach update: block per hand, thread per private row --------------------
@@ -906,9 +829,8 @@ int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, 
     A.ns_chance = rng_namespace(seed, iteration, CHANCE);
     A.pol = pol; A.action = action; A.selected = selected_log; A.decision = decision; A.new_leaf = new_leaf;
     A.leaf = leaf;
-    const int block = 256;
-    int64_t threads = B * 32;
-    PBG_DISPATCH_P(g.players, rollout_step_kernel<PP><<<stride_grid(threads, block, 8), block, 0, as_stream(stream)>>>(A));
+    const int block = 128;
+    PBG_DISPATCH_P(g.players, rollout_step_kernel<PP><<<stride_grid(B, block, 16), block, 0, as_stream(stream)>>>(A));
     return launch_status("rollout_step");
 }
 

@@ -238,3 +238,124 @@ __device__ __forceinline__ float warp_fetch(const float (&p)[CHUNK_MAX], int e, 
 }
 
 }  // namespace pbg
+
+namespace pbg {
+
+// ---------------------------------------------------------------------------
+// Closed-form composite policy of one row, one thread.
+//
+// For one logistic component with edges z_i = (x_i - mu) / s, the tick mass
+// sigma(z_{k+1}) sigma(-z_k) (1 - e^{z_k - z_{k+1}}) equals
+// sigma(z_{k+1}) - sigma(z_k), so the mass of any tick range [a, b) is the
+// same product form with (a, b) in place of (k, k+1):
+//     R(a, b) = sigma(z_b) sigma(-z_a) (-expm1(-(x_b - x_a) / s)),
+// accurate in both tails because no difference of nearly equal sigmoids is
+// taken and the edge gap is computed from the edges, not from rounded z's.
+// Consequences used here (policy.py:113-204 is the per-tick definition):
+//   * the legal raise mass needs one R per component, not one per tick;
+//   * the conditional raise probabilities rp_k over the legal ticks sum to 1
+//     ((1 - iota) mix/mass + iota at the all-in tick), so the softmax
+//     denominator is e^{l0} [fold legal] + e^{l1'} + e^{l2} [raise legal];
+//   * the CDF at any tick is O(M), so sampling is a binary search over ticks.
+// Results equal the per-tick composition up to rounding.
+struct ClosedPolicy {
+    static constexpr int MMAX = 8;
+    float loc[MMAX], inv_s[MMAX], wnorm[MMAX];  // wnorm = omega / normaliser
+    int M, T;
+    LegalSummary L;
+    float mass, iota, pf, pc, pr;  // fold, check/call and total raise probability
+    bool raise;
+
+    __device__ float range(int m, int a, int b) const {
+        if (b <= a) return 0.0f;
+        float xa = edge_of(a, T), xb = edge_of(b, T);
+        float za = __fmul_rn(__fsub_rn(xa, loc[m]), inv_s[m]);
+        float zb = __fmul_rn(__fsub_rn(xb, loc[m]), inv_s[m]);
+        float w = -expm1f(-__fmul_rn(__fsub_rn(xb, xa), inv_s[m]));
+        return fmaxf(__fmul_rn(__fmul_rn(sigmoid_f(zb), sigmoid_f(-za)), w), 0.0f);
+    }
+
+    // normalised mixture mass of ticks [a, b)
+    __device__ float mix(int a, int b) const {
+        float acc = 0.0f;
+        for (int m = 0; m < M; ++m) acc = __fadd_rn(acc, __fmul_rn(wnorm[m], range(m, a, b)));
+        return acc;
+    }
+
+    __device__ void init(const RawRow& raw, const LegalSummary& legal, int ticks) {
+        M = raw.M;
+        T = ticks;
+        L = legal;
+        iota = raw.iota;
+        raise = L.alive && L.lo <= L.hi;
+        for (int m = 0; m < M; ++m) {
+            loc[m] = raw.mu[m];
+            inv_s[m] = __fdiv_rn(1.0f, raw.scale[m]);
+            wnorm[m] = 1.0f;
+            float norm = range(m, 0, T);
+            wnorm[m] = __fdiv_rn(raw.omega[m], fmaxf(norm, FLT_TINY));
+        }
+        mass = raise ? mix(L.lo, L.hi + 1) : 0.0f;
+        float l0 = raw.logits[0], l1 = L.call_legal ? raw.logits[1] : raw.logits[0], l2 = raw.logits[2];
+        float mx = l1;
+        if (L.call_legal) mx = fmaxf(mx, l0);
+        if (raise) mx = fmaxf(mx, l2);
+        float ef = L.call_legal ? expf(__fsub_rn(l0, mx)) : 0.0f;
+        float ec = expf(__fsub_rn(l1, mx));
+        float er = raise ? expf(__fsub_rn(l2, mx)) : 0.0f;
+        float d = __fadd_rn(__fadd_rn(ef, ec), er);
+        pf = __fdiv_rn(ef, d);
+        pc = __fdiv_rn(ec, d);
+        pr = __fdiv_rn(er, d);
+    }
+
+    // conditional raise probability of tick k (legal, lo <= k <= hi)
+    __device__ float rp(int k) const {
+        int count = L.hi - L.lo + 1;
+        float cond = mass > 0.0f ? __fdiv_rn(mix(k, k + 1), fmaxf(mass, POLICY_EPS)) : __fdiv_rn(1.0f, (float)count);
+        return __fadd_rn(__fmul_rn(__fsub_rn(1.0f, iota), cond), k == L.hi ? iota : 0.0f);
+    }
+
+    // conditional raise probability of ticks lo..k
+    __device__ float rp_cum(int k) const {
+        int count = L.hi - L.lo + 1;
+        float cond = mass > 0.0f ? fminf(__fdiv_rn(mix(L.lo, k + 1), fmaxf(mass, POLICY_EPS)), 1.0f)
+                                 : __fdiv_rn((float)(k - L.lo + 1), (float)count);
+        return __fadd_rn(__fmul_rn(__fsub_rn(1.0f, iota), cond), k == L.hi ? iota : 0.0f);
+    }
+
+    // probability of event e (legal by contract)
+    __device__ float prob(int e) const {
+        if (e == 0) return L.call_legal ? pf : 0.0f;
+        if (e == 1) return pc;
+        int k = e - 2;
+        if (!raise || k < L.lo || k > L.hi) return 0.0f;
+        float r = rp(k);
+        return r > 0.0f ? __fmul_rn(pr, fmaxf(r, POLICY_EPS)) : 0.0f;
+    }
+
+    // inverse-CDF draw at uniform u over the event order fold, call, ticks
+    // (rollout.py:237-267): first event whose cumulative probability reaches
+    // min(u * total, nextafter(total, 0)); a threshold beyond the last
+    // legal event (rounding) takes the last legal event.
+    __device__ int sample(float u) const {
+        float total = __fadd_rn(__fadd_rn(L.call_legal ? pf : 0.0f, pc), pr);
+        float thr = __fmul_rn(u, total);
+        float cap = nextafterf(total, 0.0f);
+        thr = thr < cap ? thr : cap;
+        float c0 = L.call_legal ? pf : 0.0f;
+        if (L.call_legal && c0 >= thr) return 0;
+        float c1 = __fadd_rn(c0, pc);
+        if (c1 >= thr || !raise) return 1;
+        int lo = L.lo, hi = L.hi;
+        if (__fadd_rn(c1, __fmul_rn(pr, rp_cum(hi))) < thr) return hi + 2;
+        while (lo < hi) {  // smallest k with c1 + pr * rp_cum(k) >= thr
+            int mid = (lo + hi) >> 1;
+            if (__fadd_rn(c1, __fmul_rn(pr, rp_cum(mid))) >= thr) hi = mid;
+            else lo = mid + 1;
+        }
+        return lo + 2;
+    }
+};
+
+}  // namespace pbg

@@ -38,7 +38,7 @@ class State(ctypes.Structure):
 class History(ctypes.Structure):
     _fields_ = [(n, _P) for n in (
         "actor", "street", "action", "amount", "pot_before", "call_amount", "current_bet",
-        "min_raise_to", "max_raise_to", "mask")] + [("tokens", _I32)]
+        "min_raise_to", "max_raise_to", "mask")] + [("tokens", _I32), ("length", _P)]
 
 
 class Leaf(ctypes.Structure):

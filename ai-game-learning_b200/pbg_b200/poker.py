@@ -181,8 +181,10 @@ class PokerHistory:
     def clone(self) -> "PokerHistory":
         return PokerHistory(*(getattr(self, n).clone() for n in HISTORY_FIELDS))
 
-    def c(self) -> N.History:
-        return N.History(*(ptr(getattr(self, n)) for n in HISTORY_FIELDS), self.mask.shape[1])
+    def c(self, length: Tensor | None = None) -> N.History:
+        """ABI view; `length` ([B] int32 tokens used) lets appends skip counting the mask."""
+
+        return N.History(*(ptr(getattr(self, n)) for n in HISTORY_FIELDS), self.mask.shape[1], ptr(length))
 
 
 @dataclass(frozen=True)

@@ -41,6 +41,7 @@ class RolloutArena:
     decision: Tensor       # [B,4] int32
     new_leaf: Tensor       # [B] bool
     leaf: dict             # sampled_leaf columns
+    history_length: Tensor  # [B] int32 tokens used (kept by the kernel)
 
     @property
     def rows(self) -> int:
@@ -70,13 +71,14 @@ class RolloutStep:
             torch.zeros(rows, dtype=torch.float32, device=device),
             torch.zeros((rows, 4), dtype=torch.int32, device=device),
             torch.zeros(rows, dtype=torch.bool, device=device),
-            self.machine._leaf_tensors(rows, device))
+            self.machine._leaf_tensors(rows, device),
+            torch.zeros(rows, dtype=torch.int32, device=device))
 
     def step(self, arena: RolloutArena, raw) -> None:
         """Advance every non-terminal hand by one player decision (in place)."""
 
         pol, keep, rows = policy_struct(raw)
-        hist = arena.history.c() if self.with_history else N.History(*([None] * 10), 0)
+        hist = arena.history.c(arena.history_length) if self.with_history else N.History(*([None] * 10), 0, None)
         leaf = N.Leaf(*(ptr(v) for v in arena.leaf.values()))
         call("pbg_rollout_step", self.geometry.c, arena.rows, arena.state.c(), hist, ptr(arena.root_path),
              ptr(arena.lane), ptr(arena.retry_epoch), self.seed, self.iteration, pol, ptr(arena.action),

@@ -67,7 +67,8 @@ typedef struct {
     float *min_raise_to;
     float *max_raise_to;
     uint8_t *mask;
-    int32_t tokens; /* capacity/models/capacity.py:22-25 bound */
+    int32_t tokens;  /* model/capacity.py:22-25 bound */
+    int32_t *length; /* [B] tokens used, kept current by every append; NULL = count the mask */
 } pbg_history;
 
 /* Sampled settlement inputs, hooks.py:1145-1216 (sampled_leaf) output. */
@@ -200,7 +201,7 @@ int pbg_policy_sample_actor(int64_t B, int32_t E, pbg_policy pol, const uint8_t 
 
 /* ------------------------------------------------------ fused rollout */
 
-/* One fused sampled rollout step for B independent hands (warp per hand),
+/* One fused sampled rollout step for B independent hands (thread per hand),
  * composing rollout.py:1604-1621 (ACTION key at draw 0), hooks.py:1489-1541
  * (sample at the owner's private row), hooks.py:1656-1700 (history,
  * step_player, three keyed chance generations), hooks.py:1145-1216 (leaf
