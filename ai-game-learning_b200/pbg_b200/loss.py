@@ -23,7 +23,9 @@ import math
 import torch
 from torch import Tensor
 
-from ._native import call, lib, ptr, stream
+import ctypes
+
+from ._native import call, check, lib, ptr, stream
 
 STATS = ("total", "policy", "entropy", "approximate_kl", "clip_count", "negative_cap_count", "weight_sum", "rows")
 
@@ -69,6 +71,40 @@ class FusedPPOBackward:
              ptr(advantage), ptr(weight), ptr(self.controls), ptr(dlogits), ptr(self.partials), ptr(self.stats),
              stream(logits.device))
         return dlogits, self.stats
+
+    def bind(self, logits, mask, action, old_logp, advantage, weight, dlogits) -> BoundPPOBackward:
+        if tuple(logits.shape) != (self.rows, self.actions) or dlogits.shape != logits.shape:
+            raise ValueError("loss rows/actions differ from the admitted shape")
+        return BoundPPOBackward(self, logits, mask, action, old_logp, advantage, weight, dlogits)
+
+
+class BoundPPOBackward:
+    """A loss launch with its device pointers resolved once.
+
+    Repeated steps over the same buffers (a learner's admitted batch slots)
+    re-launch from cached arguments, so the host adds only the ctypes call;
+    the launch also records cleanly into a CUDA graph (warm it up once first
+    so one-time device set-up happens outside the capture).
+    """
+
+    def __init__(self, op: "FusedPPOBackward", logits, mask, action, old_logp, advantage, weight, dlogits):
+        N, A = logits.shape
+        tensors = (logits, mask.view(torch.uint8) if mask.dtype == torch.bool else mask, action, old_logp,
+                   advantage, weight, op.controls, dlogits, op.partials, op.stats)
+        for t in tensors:
+            if not (t.is_cuda and t.is_contiguous()):
+                raise ValueError("bound loss buffers must be contiguous CUDA tensors")
+        self._keep = tensors
+        self._fn = lib().pbg_ppo_categorical_backward
+        self._args = (N, A, 1 if logits.dtype == torch.bfloat16 else 0, *(ctypes.c_void_p(t.data_ptr()) for t in tensors))
+        self.stats = op.stats
+        self.dlogits = dlogits
+
+    def launch(self, stream=None) -> None:
+        s = torch.cuda.current_stream() if stream is None else stream
+        rc = self._fn(*self._args, ctypes.c_void_p(s.cuda_stream))
+        if rc != 0:
+            check(rc, "pbg_ppo_categorical_backward")
 
 
 def fused_ppo_backward(logits, mask, action, old_logp, advantage, weight, config: LossConfig = LossConfig(), *,

@@ -254,7 +254,7 @@ def rollout_component(device, hands=65_536, seed=0):
 
     A fixed seeded raw policy row per hand (the model is not on this path yet) drives every step.
     The same rollout runs once untimed to count the decisions each step makes (it is deterministic),
-    then again timed with CUDA events around every step launch.
+    then again timed with CUDA events around every step, each step replayed from a CUDA graph.
     """
 
     import torch
@@ -281,9 +281,14 @@ def rollout_component(device, hands=65_536, seed=0):
     stream = torch.cuda.current_stream(device)
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in counts]
     torch.cuda.synchronize(device)
+    # one step over fixed arena buffers, replayed from a CUDA graph (no host gaps between steps)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        stepper.step(arena, raw)
+    torch.cuda.synchronize(device)
     for a, b in events:
         a.record(stream)
-        stepper.step(arena, raw)
+        graph.replay()
         b.record(stream)
     torch.cuda.synchronize(device)
     assert bool(arena.state.terminal.all())
@@ -328,11 +333,25 @@ def main():
     dlogits = torch.empty_like(logits)
     grad = torch.randn(args.params, device=device) * 1e-3
     stream = torch.cuda.current_stream(device)
+    bound = op.bind(logits, mask, action, old, adv, weight, dlogits)
+    bound.launch(stream)  # one-time device set-up happens outside any capture
+    torch.cuda.synchronize(device)
+    graph = None
+    if world == 1:
+        # the single-rank step is one kernel: replay it from a CUDA graph so host launch
+        # cost never gaps the device (multi-rank steps keep NCCL eager)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            bound.launch()
+        torch.cuda.synchronize(device)
 
     def step(events=None):
         if events is not None:
             events[0].record(stream)
-        op(logits, mask, action, old, adv, weight, dlogits)
+        if graph is not None:
+            graph.replay()
+        else:
+            bound.launch(stream)
         if events is not None:
             events[1].record(stream)
         if world > 1:
@@ -374,13 +393,15 @@ def main():
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = stats_host.numel() * stats_host.element_size()
 
+    e2e_bound = op.bind(*dev_in, dlogits)
+
     def e2e_step():
         for d, h in zip(dev_in, host):
             d.copy_(h, non_blocking=True)
-        _, stats = op(*dev_in, dlogits)
+        e2e_bound.launch(stream)
         if world > 1:
             dist.all_reduce(grad, op=dist.ReduceOp.SUM)
-        stats_host.copy_(stats, non_blocking=True)
+        stats_host.copy_(op.stats, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -411,7 +432,8 @@ def main():
                                "loss backward + flat fp32 gradient SUM all-reduce",
                    "rows_per_rank": N, "actions": A, "grad_params": args.params,
                    "allreduce": "NCCL SUM" if world > 1 else "none (single rank)",
-                   "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}"},
+                   "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}",
+                   "launch": "CUDA graph replay (one kernel per step)" if world == 1 else "eager (kernel + NCCL)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": committed_traffic(N),
                      "kernel": "ppo_bf16x8_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,

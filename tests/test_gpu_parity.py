@@ -575,3 +575,28 @@ def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
     near = _boundary_rows(host(x16.float()), mask, action, old, 0.2, math.log(2.0))
     _assert_close_except_boundary(host(d.float()), ref, near, rtol=2e-2, atol=2e-2 * scale)
     np.testing.assert_allclose(host(stats)[[0, 1, 2, 3, 6]], ref_s[[0, 1, 2, 3, 6]], rtol=1e-4, atol=1e-9 * N)
+
+
+def test_bound_loss_launch_and_graph_replay_match_the_call():
+    from pbg_b200.loss import FusedPPOBackward, LossConfig
+
+    N, A = 992 * 40 + 7, 8
+    logits, mask, action, old, adv, weight = _loss_inputs(N, A, 23)
+    args = [cuda(logits).to(torch.bfloat16), cuda(mask), cuda(action), cuda(old), cuda(adv), cuda(weight)]
+    op = FusedPPOBackward(N, A, DEV, LossConfig(0.2, None, 0.01))
+    ref_d, ref_s = op(*args)
+    ref_d, ref_s = ref_d.clone(), ref_s.clone()
+    out = torch.empty_like(args[0])
+    bound = op.bind(*args, out)
+    bound.launch()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_d) and torch.equal(op.stats, ref_s)
+    out.zero_()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        bound.launch()
+    for _ in range(2):
+        op.stats.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref_d) and torch.equal(op.stats, ref_s)
