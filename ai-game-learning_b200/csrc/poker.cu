@@ -656,6 +656,137 @@ __global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, con
     }
 }
 
+
+// Model-input rows (hooks.py:531-612 direct_model_input, hooks.py:630-648
+// _compact_preflop_reach): one block per hand.  Layout: public 8+10P |
+// log-reach P*K (preflop, class-compact) or P*H | 10 history columns of
+// `tokens` | zeros for the folded summary of post rows when P > 2.
+__device__ __forceinline__ float public_column(const pbg_state& st, int64_t b, int t, int P, const Geo& d,
+                                               float scale) {
+    if (t == 0) return __fdiv_rn((float)st.street[b], 3.0f);
+    t -= 1;
+    if (t < 5) {
+        int c = st.board[b * 5 + t];
+        return c == PAD_CARD ? -1.0f : __fdiv_rn(__fsub_rn((float)c, (float)d.first), (float)max(1, d.D - 1));
+    }
+    t -= 5;
+    if (t < P) return st.to_act[b] == t ? 1.0f : 0.0f;
+    t -= P;
+    if (t < P) return st.button[b] == t ? 1.0f : 0.0f;
+    t -= P;
+    if (t < P) return __fdiv_rn(st.stacks[b * P + t], scale);
+    t -= P;
+    if (t < P) return __fdiv_rn(st.committed[b * P + t], scale);
+    t -= P;
+    if (t < P) return __fdiv_rn(st.committed_street[b * P + t], scale);
+    t -= P;
+    if (t < 3 * P) return st.status[b * P + t / 3] == t % 3 ? 1.0f : 0.0f;
+    t -= 3 * P;
+    if (t < P) return st.pending[b * P + t] ? 1.0f : 0.0f;
+    t -= P;
+    if (t == 0) return __fdiv_rn(st.current_bet[b], scale);
+    if (t == 1) return __fdiv_rn(st.last_full_raise[b], scale);
+    t -= 2;
+    return st.can_raise[b * P + t] ? 1.0f : 0.0f;
+}
+
+// Compact combo ids of preflop class k (class matrix of hooks.py:655-674):
+// pair (6 combos), suited (4) or offsuit (12).
+__device__ __forceinline__ int class_members(const Geo& d, int k, int (&ids)[12]) {
+    const int R = d.R, i = k / R, j = k % R, shift = 13 - R;
+    int n = 0;
+    if (i == j) {
+        int r = R - 1 - i + shift;
+        for (int s1 = 0; s1 < 4; ++s1)
+            for (int s2 = s1 + 1; s2 < 4; ++s2) ids[n++] = combo_id(d.D, d.first, 4 * r + s1, 4 * r + s2);
+    } else if (i < j) {
+        int hi = R - 1 - i + shift, lo = R - 1 - j + shift;
+        for (int s = 0; s < 4; ++s) ids[n++] = combo_id(d.D, d.first, 4 * hi + s, 4 * lo + s);
+    } else {
+        int hi = R - 1 - j + shift, lo = R - 1 - i + shift;
+        for (int s1 = 0; s1 < 4; ++s1)
+            for (int s2 = 0; s2 < 4; ++s2)
+                if (s1 != s2) ids[n++] = combo_id(d.D, d.first, 4 * hi + s1, 4 * lo + s2);
+    }
+    return n;
+}
+
+template <int P>
+__global__ void model_input_kernel(Geo d, int64_t B, pbg_state st, int pre, const float* reach, pbg_history hist,
+                                   int tokens, float* out, int64_t width, float scale) {
+    __shared__ float gauge[MAXP];
+    __shared__ float red[32];
+    const int nt = blockDim.x;
+    for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+        float* row = out + b * width;
+        const int npub = 8 + 10 * P;
+        for (int t = threadIdx.x; t < npub; t += nt) row[t] = public_column(st, b, t, P, d, scale);
+        int64_t off = npub;
+        if (pre) {
+            if (reach) {
+                // per-seat gauge: max of the finite exact reaches
+                for (int p = 0; p < P; ++p) {
+                    float m = -INFINITY;
+                    for (int h = threadIdx.x; h < d.H; h += nt) {
+                        float v = reach[(b * P + p) * d.H + h];
+                        if (isfinite(v)) m = fmaxf(m, v);
+                    }
+                    m = warp_max(m);
+                    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+                    __syncthreads();
+                    if (threadIdx.x == 0) {
+                        float g = -INFINITY;
+                        for (int w = 0; w < (nt + 31) / 32; ++w) g = fmaxf(g, red[w]);
+                        gauge[p] = isfinite(g) ? g : 0.0f;
+                    }
+                    __syncthreads();
+                }
+            }
+            for (int i = threadIdx.x; i < P * d.K; i += nt) {
+                int p = i / d.K, k = i % d.K;
+                int ids[12];
+                int n = class_members(d, k, ids);
+                float v;
+                if (!reach) {
+                    v = logf((float)n);
+                } else {
+                    float sum = 0.0f, g = gauge[p];
+                    for (int m = 0; m < n; ++m) {
+                        float x = reach[(b * P + p) * d.H + ids[m]];
+                        if (isfinite(x)) sum = __fadd_rn(sum, expf(__fsub_rn(x, g)));
+                    }
+                    v = sum > 0.0f ? __fadd_rn(logf(fmaxf(sum, FLT_TINY)), g) : -INFINITY;
+                }
+                row[off + i] = v;
+            }
+            off += (int64_t)P * d.K;
+        } else {
+            for (int i = threadIdx.x; i < P * d.H; i += nt) row[off + i] = reach ? reach[b * P * d.H + i] : 0.0f;
+            off += (int64_t)P * d.H;
+        }
+        for (int i = threadIdx.x; i < 10 * tokens; i += nt) {
+            int c = i / tokens, t = i % tokens;
+            int64_t at = b * tokens + t;
+            float v;
+            if (!hist.mask) v = c < 3 ? -1.0f : 0.0f;
+            else if (c == 0) v = (float)hist.actor[at];
+            else if (c == 1) v = (float)hist.street[at];
+            else if (c == 2) v = (float)hist.action[at];
+            else if (c == 3) v = hist.amount[at];
+            else if (c == 4) v = hist.pot_before[at];
+            else if (c == 5) v = hist.call_amount[at];
+            else if (c == 6) v = hist.current_bet[at];
+            else if (c == 7) v = hist.min_raise_to[at];
+            else if (c == 8) v = hist.max_raise_to[at];
+            else v = hist.mask[at] ? 1.0f : 0.0f;
+            row[off + i] = v;
+        }
+        off += 10 * (int64_t)tokens;
+        for (int64_t i = off + threadIdx.x; i < width; i += nt) row[i] = 0.0f;  // folded summary
+        __syncthreads();
+    }
+}
+
 }  // namespace pbg
 
 // ====================================================================== ABI
@@ -847,5 +978,25 @@ int pbg_reach_update(pbg_geometry g, int64_t B, pbg_state st, pbg_policy pol, co
         d, B, st, pol, action, decision, log_reach));
     return launch_status("reach_update");
 }
+
+int pbg_direct_model_input(pbg_geometry g, int64_t B, pbg_state st, int32_t input_type, const float* log_reach,
+                           pbg_history hist, float* out, int64_t width, void* stream) {
+    int rc = check_geometry(g);
+    if (rc) return rc;
+    Geo d = derive(g);
+    PBG_REQUIRE(B >= 0 && state_ok(st) && out && (input_type == 0 || input_type == 1), "direct_model_input: bad arguments");
+    PBG_REQUIRE(hist.tokens > 0, "direct_model_input: history token capacity required");
+    const int P = g.players;
+    int64_t folded = (input_type == 1 && P > 2) ? (int64_t)d.H + d.D + d.D * d.D + P + P * d.D + 2 : 0;
+    int64_t expect = 8 + 10 * P + (int64_t)P * (input_type == 0 ? d.K : d.H) + 10 * (int64_t)hist.tokens + folded;
+    PBG_REQUIRE(width == expect, "direct_model_input: width %lld, the layout needs %lld", (long long)width,
+                (long long)expect);
+    if (B == 0) return PBG_OK;
+    float scale = 0.5f * (float)g.stack_ticks;
+    PBG_DISPATCH_P(g.players, model_input_kernel<PP><<<stride_grid(B * 256, 256, 8), 256, 0, as_stream(stream)>>>(
+        d, B, st, input_type == 0, log_reach, hist, hist.tokens, out, width, scale));
+    return launch_status("direct_model_input");
+}
+
 
 }  // extern "C"

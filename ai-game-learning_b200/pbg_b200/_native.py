@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_sampled_leaf": (_I32, [G, _I64, S, L, _P]),
     "pbg_combo_cards": (_I32, [G, _I64, _P, _P, _P]),
     "pbg_combo_class": (_I32, [G, _P, _P]),
+    "pbg_direct_model_input": (_I32, [G, _I64, S, _I32, _P, Hs, _P, _I64, _P]),
     "pbg_evaluate_showdowns": (_I32, [_I32, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_hand_values": (_I32, [_I32, _I64, _P, _P, _P]),
     "pbg_policy_probabilities": (_I32, [_I64, _I32, Pol, _P, _P, _P]),

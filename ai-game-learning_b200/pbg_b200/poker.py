@@ -304,6 +304,35 @@ class PokerStateMachine:
              N.Leaf(*(ptr(v) for v in leaf.values())), stream(state.device))
         return MappingProxyType(leaf)
 
+    def model_input_width(self, input_type: str) -> int:
+        """hooks.py:138-169: retained row width of a partition."""
+
+        g = self.geometry
+        P, D, H, K = g.players, g.deck_cards, g.private_hands, g.private_classes
+        base = 8 + 10 * P + 10 * g.history_tokens
+        if input_type == "pre":
+            return base + P * K
+        if input_type.startswith("post_") and input_type[5:].isdigit():
+            folded = 0 if P == 2 else H + D + D * D + P + P * D + 2
+            return base + P * H + folded
+        raise ValueError(f"unknown poker input partition {input_type!r}")
+
+    def direct_model_input(self, input_type: str, state: PokerState, log_reach: Tensor | None = None,
+                           history: PokerHistory | None = None) -> Tensor:
+        """hooks.py:531-612: the retained public, reach and history model row."""
+
+        width = self.model_input_width(input_type)
+        pre = input_type == "pre"
+        if log_reach is not None and log_reach.shape != (state.rows, self.geometry.players,
+                                                          self.geometry.private_hands):
+            raise QueuedPokerError("device model input takes the exact [B,P,H] reach")
+        out = torch.empty((state.rows, width), dtype=torch.float32, device=state.device)
+        hist = history.c() if history is not None else N.History(*([None] * 10), self.geometry.history_tokens, None)
+        call("pbg_direct_model_input", self.geometry.c, state.rows, state.c(), 0 if pre else 1,
+             ptr(None if log_reach is None else log_reach.float().contiguous()), hist, ptr(out), width,
+             stream(state.device))
+        return out
+
     def combo_cards(self, combo_ids: Tensor) -> Tensor:
         ids = combo_ids.to(torch.int32).contiguous()
         out = torch.empty(ids.shape + (2,), dtype=torch.int64, device=ids.device)

@@ -164,6 +164,16 @@ int pbg_combo_cards(pbg_geometry g, int64_t n, const int32_t *ids, int64_t *out,
 /* hooks.py:655-674 (_combo_class): out [H] int32. */
 int pbg_combo_class(pbg_geometry g, int32_t *out, void *stream);
 
+/* hooks.py:531-612 (direct_model_input) with hooks.py:630-648
+ * (_compact_preflop_reach): out [B,width] fp32 rows.  input_type 0 = "pre"
+ * (class-compact reach), 1 = "post_*" (exact reach, folded-summary zeros
+ * when P > 2).  log_reach is the exact [B,P,H] reach or NULL (class counts
+ * preflop, zeros after); hist.mask NULL means an empty history of
+ * hist.tokens slots.  width must equal the reference's row width. */
+int pbg_direct_model_input(pbg_geometry g, int64_t B, pbg_state st, int32_t input_type,
+                           const float *log_reach, pbg_history hist, float *out, int64_t width,
+                           void *stream);
+
 /* ----------------------------------------------------------- showdown */
 
 /* Contract-v2 evaluate_showdowns of the external poker_gpu_evaluator, as

@@ -530,3 +530,54 @@ def rollout_transition(machine: Machine, s: State, h: History, action, *, seed, 
         s = machine.deal_next_street_keyed(s, seed=seed, iteration=iteration, root=root, path=path,
                                            draw=generation, retry_epoch=retry_epoch, lane=lane)
     return s, h, child_path(path, 1)
+
+
+# ------------------------------------------------------ model input
+
+
+def direct_model_input(machine: Machine, input_type: str, s: State, log_reach=None, history: History | None = None):
+    """hooks.py:531-612 (direct_model_input), with hooks.py:630-648 (_compact_preflop_reach).
+
+    Row layout: public 8+10P | log-reach P*K (pre, class-compact) or P*H (post) | 10 history columns
+    of `tokens` | folded summary zeros (post rows of P > 2 tables).
+    """
+
+    g = machine.g
+    P, D, H, K, first = g.players, g.deck_cards, g.private_hands, g.private_classes, g.first_card
+    B = s.rows
+    scale = np.float32(g.stack_bb)
+    board = s.board.astype(np.float32)
+    board = np.where(s.board == PAD_CARD, np.float32(-1.0), (board - np.float32(first)) / np.float32(max(1, D - 1)))
+    eye = np.eye(P, dtype=np.float32)
+    status = np.eye(3, dtype=np.float32)[s.status.astype(np.int64)].reshape(B, 3 * P)
+    public = np.concatenate([
+        (s.street.astype(np.float32) / np.float32(3.0))[:, None], board, eye[s.to_act], eye[s.button],
+        s.stacks / scale, s.committed / scale, s.committed_street / scale, status,
+        s.pending.astype(np.float32), (s.current_bet / scale)[:, None], (s.last_full_raise / scale)[:, None],
+        s.can_raise.astype(np.float32)], 1).astype(np.float32)
+    cls = machine.combo_class()
+    counts = np.bincount(cls, minlength=K).astype(np.float32)
+    pre = input_type == "pre"
+    if log_reach is None:
+        reach = np.broadcast_to(np.log(counts)[None, None], (B, P, K)) if pre else np.zeros((B, P, H), np.float32)
+    elif pre:
+        exact = np.asarray(log_reach, dtype=np.float32)
+        finite = np.isfinite(exact)
+        gauge = np.where(finite, exact, -np.inf).max(-1, keepdims=True)
+        safe = np.where(np.isfinite(gauge), gauge, np.float32(0.0))
+        weight = np.where(finite, np.exp(exact - safe), np.float32(0.0)).astype(np.float32)
+        compact = np.zeros((B, P, K), np.float32)
+        for k in range(K):
+            compact[..., k] = weight[..., cls == k].sum(-1)
+        tiny = np.finfo(np.float32).tiny
+        reach = np.where(compact > 0, np.log(np.maximum(compact, tiny)) + safe, -np.inf).astype(np.float32)
+    else:
+        reach = np.asarray(log_reach, dtype=np.float32)
+    if history is None:
+        history = History.empty(B, g.history_tokens)
+    hist = [getattr(history, n).astype(np.float32) for n in History.NAMES]
+    parts = [public, reach.reshape(B, -1), *hist]
+    if not pre and P > 2:
+        width = H + D + D * D + P + P * D + 2
+        parts.append(np.zeros((B, width), np.float32))
+    return np.concatenate(parts, 1).astype(np.float32)

@@ -404,6 +404,42 @@ def gen_adam(out):
     out["adam_grad_out"] = np.stack(grads_out)
 
 
+def gen_model_input(out, poker):
+    """hooks.py:531-612 (direct_model_input) on trajectory states, with and without reach/history."""
+
+    import torch
+    from pbg.games.poker.queued.hooks import NLHEGeometry, PokerHistory, PokerStateMachine
+
+    rng = np.random.default_rng(13)
+    for gi in (0, 1, 3, 6):
+        players, stack, ranks = poker[f"g{gi}_geometry"]
+        geometry = NLHEGeometry(int(players), float(stack), int(ranks))
+        machine = PokerStateMachine(geometry)
+        tag = f"mi{gi}"
+        steps = poker[f"g{gi}_post_board_cards"].shape[0]
+        t = min(2, steps - 1)
+        cols = {n: poker[f"g{gi}_post_{n}"][t][:8] for n in STATE_FIELDS}
+        cols["terminal"] = np.zeros_like(cols["terminal"])
+        state = _state_from(cols)
+        B, P, H = state.rows, geometry.players, geometry.private_hands
+        reach = rng.standard_normal((B, P, H)).astype(np.float32) * 3.0
+        reach[rng.random((B, P, H)) < 0.2] = -np.inf
+        reach[0, 0, :] = -np.inf  # a seat with no finite reach
+        hist = {n: poker[f"g{gi}_history_{n}"][:8] for n in HISTORY_FIELDS}
+        history = PokerHistory(*(torch.from_numpy(np.ascontiguousarray(
+            hist[n].astype(np.int64) if n in ("actor", "street", "action") else
+            (hist[n].astype(bool) if n == "mask" else hist[n].astype(np.float32)))) for n in HISTORY_FIELDS))
+        for k, v in cols.items():
+            out[f"{tag}_state_{k}"] = v
+        out[f"{tag}_geometry"] = np.array([players, stack, ranks])
+        out[f"{tag}_reach"] = reach
+        out[f"{tag}_pre_plain"] = _np(machine.direct_model_input("pre", state))
+        out[f"{tag}_pre_full"] = _np(machine.direct_model_input("pre", state, torch.from_numpy(reach), history))
+        post = f"post_{P}"
+        out[f"{tag}_post_plain"] = _np(machine.direct_model_input(post, state))
+        out[f"{tag}_post_full"] = _np(machine.direct_model_input(post, state, torch.from_numpy(reach), history))
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="root of a pbg checkout")
@@ -421,8 +457,10 @@ def main() -> None:
     gen_policy(policy_out, poker_out)
     gen_loss(loss_out)
     gen_adam(adam_out)
+    mi_out = {}
+    gen_model_input(mi_out, poker_out)
     for name, data in (("rng", rng_out), ("poker", poker_out), ("known_answers", ka_out),
-                       ("policy", policy_out), ("loss", loss_out), ("adam", adam_out)):
+                       ("policy", policy_out), ("loss", loss_out), ("adam", adam_out), ("model_input", mi_out)):
         np.savez_compressed(os.path.join(args.out, f"{name}.npz"), **data)
         print(name, len(data), os.path.getsize(os.path.join(args.out, f"{name}.npz")))
 

@@ -600,3 +600,30 @@ def test_bound_loss_launch_and_graph_replay_match_the_call():
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, ref_d) and torch.equal(op.stats, ref_s)
+
+
+@pytest.mark.parametrize("gi", [0, 1, 3, 6])
+def test_direct_model_input_matches_reference_golden(gold, gi):
+    """hooks.py:531-612 rows: public and history columns exact, the compact preflop reach within 1e-5."""
+
+    from pbg_b200.poker import HISTORY_FIELDS, NLHEGeometry, PokerHistory, PokerStateMachine
+
+    g = gold("model_input")
+    p = gold("poker")
+    tag = f"mi{gi}"
+    players, stack, ranks = g[f"{tag}_geometry"]
+    m = PokerStateMachine(NLHEGeometry(int(players), float(stack), int(ranks)))
+    cols = {n: g[f"{tag}_state_{n}"] for n in STATE_MAP}
+    s = _dev_state(cols)
+    B = s.rows
+    dtypes = {"actor": torch.int64, "street": torch.int64, "action": torch.int64, "mask": torch.bool}
+    h = PokerHistory(*(cuda(p[f"g{gi}_history_{n}"][:B]).to(dtypes.get(n, torch.float32)) for n in HISTORY_FIELDS))
+    reach = cuda(g[f"{tag}_reach"])
+    post = f"post_{int(players)}"
+    np.testing.assert_array_equal(host(m.direct_model_input(post, s)), g[f"{tag}_post_plain"])
+    np.testing.assert_array_equal(host(m.direct_model_input(post, s, reach, h)), g[f"{tag}_post_full"])
+    for got, want in ((host(m.direct_model_input("pre", s)), g[f"{tag}_pre_plain"]),
+                      (host(m.direct_model_input("pre", s, reach, h)), g[f"{tag}_pre_full"])):
+        np.testing.assert_array_equal(np.isinf(got), np.isinf(want))
+        fin = np.isfinite(want)
+        np.testing.assert_allclose(got[fin], want[fin], rtol=1e-5, atol=1e-6)
