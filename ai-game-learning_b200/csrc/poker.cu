@@ -509,85 +509,120 @@ struct StepArgs {
     pbg_leaf leaf;
 };
 
-// Three smallest (key, card) CHANCE keys among unused cards, one thread,
-// keys computed on the fly (hooks.py:1064-1075 order: stable by card index).
-__device__ __forceinline__ void chance_smallest3(uint64_t ns, int64_t root, int64_t path, int64_t draw_base,
-                                                 int64_t lane_id, int64_t epoch, uint64_t used, int D, int (&out)[3]) {
-    int64_t bk[3] = {INT64_MAX, INT64_MAX, INT64_MAX};
-    int bi[3] = {D, D, D};
-    for (int c = 0; c < D; ++c) {
-        if ((used >> c) & 1ULL) continue;
-        int64_t k = rng_key(ns, root, path, draw_base + c, lane_id, epoch);
-        if (k < bk[2] || (k == bk[2] && c < bi[2])) {
-            bk[2] = k; bi[2] = c;
-            if (bk[2] < bk[1] || (bk[2] == bk[1] && bi[2] < bi[1])) {
-                int64_t tk = bk[1]; int ti = bi[1]; bk[1] = bk[2]; bi[1] = bi[2]; bk[2] = tk; bi[2] = ti;
-                if (bk[1] < bk[0] || (bk[1] == bk[0] && bi[1] < bi[0])) {
-                    tk = bk[0]; ti = bi[0]; bk[0] = bk[1]; bi[0] = bi[1]; bk[1] = tk; bi[1] = ti;
-                }
-            }
+// Three smallest (key, card) CHANCE keys among one hand's unused cards,
+// computed by a whole warp: lane l keys cards l and l+32, then three
+// shuffle-argmin rounds over (key, card) pairs (stable by card index).
+__device__ __forceinline__ void warp_smallest3(uint64_t ns, int64_t root, int64_t path, int64_t draw_base,
+                                               int64_t lane_id, int64_t epoch, uint64_t used, int D,
+                                               int (&out)[3]) {
+    const int lane = threadIdx.x & 31;
+    int64_t k0 = INT64_MAX, k1 = INT64_MAX;
+    int c0 = lane, c1 = lane + 32;
+    if (c0 < D && !((used >> c0) & 1ULL)) k0 = rng_key(ns, root, path, draw_base + c0, lane_id, epoch);
+    if (c1 < D && !((used >> c1) & 1ULL)) k1 = rng_key(ns, root, path, draw_base + c1, lane_id, epoch);
+    if (c0 >= D) c0 = 64;
+    if (c1 >= D) c1 = 64;
+    #pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        bool first_is_min = (k0 < k1) || (k0 == k1 && c0 < c1);
+        int64_t bk = first_is_min ? k0 : k1;
+        int bc = first_is_min ? c0 : c1;
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            int64_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+            int oc = __shfl_xor_sync(0xffffffffu, bc, o);
+            if (ok < bk || (ok == bk && oc < bc)) { bk = ok; bc = oc; }
         }
+        out[r] = bc;
+        if (bc == c0) { k0 = INT64_MAX; c0 = 64; }
+        if (bc == c1) { k1 = INT64_MAX; c1 = 64; }
     }
-    out[0] = bi[0]; out[1] = bi[1]; out[2] = bi[2];
 }
 
 // Fused sampled rollout step: one thread per hand.  Consecutive threads own
 // consecutive hands, so every state column is read and written coalesced.
+// The loop is warp-uniform: hands that must deal a street are dealt by the
+// whole warp (warp_smallest3), one hand at a time.
 template <int P>
 __global__ void __launch_bounds__(128) rollout_step_kernel(StepArgs A) {
     const Geo& d = A.d;
-    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < A.B; b += (int64_t)gridDim.x * blockDim.x) {
-        if (A.st.terminal[b]) {
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); base < A.B; base += stride) {
+        const int64_t b = base + lane;
+        const bool valid = b < A.B;
+        const bool live = valid && !A.st.terminal[b];
+        if (valid && !live) {
             A.action[b] = -1;
             A.selected[b] = 0.0f;
             if (A.new_leaf) A.new_leaf[b] = 0;
             if (A.decision) {
                 A.decision[4 * b] = -1; A.decision[4 * b + 1] = -1; A.decision[4 * b + 2] = 1; A.decision[4 * b + 3] = 0;
             }
-            continue;
         }
+        if (__ballot_sync(0xffffffffu, live) == 0u) continue;
         Hand<P> h;
-        h.load(A.st, b);
-        const int64_t root = A.root_path[2 * b], path = A.root_path[2 * b + 1];
-        const int64_t rl = A.lane ? A.lane[b] : 0, re = A.retry ? A.retry[b] : 0;
-        // sample at the owner's private row (rollout.py:1604-1621, hooks.py:1489-1541)
-        LegalSummary L = h.legality(d.T);
-        const int a = h.to_act;
-        int64_t row = 0;
-        if (A.pol.rows > 1) {
-            int combo = h.get(h.combo, a);
-            if (h.street == 0) {
-                int c0, c1;
-                combo_cards(d.D, d.first, combo, c0, c1);
-                row = combo_class(d.R, c0, c1);
-            } else {
-                row = combo;
-            }
-        }
-        ClosedPolicy pol;
-        pol.init(raw_row(A.pol, b * A.pol.rows + row), L, d.T);
-        const int64_t key = rng_key(A.ns_action, root, path, 0, rl, re);
-        const int act = pol.sample(key_uniform(key));
-        const float logp = logf(fmaxf(pol.prob(act), POLICY_EPS));
-        // transition (hooks.py:1656-1700)
+        int64_t root = 0, path = 0, rl = 0, re = 0;
+        int act = 1, a = 0, street_before = 0, len = 0;
+        float logp = 0.0f;
+        LegalSummary L;
+        L.alive = false; L.call_legal = false; L.lo = 1; L.hi = 0;
         const bool with_history = A.hist.tokens > 0;
-        int len = 0;
-        if (with_history) len = A.hist.length ? A.hist.length[b] : history_length(A.hist, b);
-        if (with_history && len < A.hist.tokens) write_token(A.hist, b, len, player_token(h, act, d.T));
-        ++len;
-        const int street_before = h.street;
-        h.step(act);
+        if (live) {
+            h.load(A.st, b);
+            root = A.root_path[2 * b];
+            path = A.root_path[2 * b + 1];
+            rl = A.lane ? A.lane[b] : 0;
+            re = A.retry ? A.retry[b] : 0;
+            // sample at the owner's private row (rollout.py:1604-1621, hooks.py:1489-1541)
+            L = h.legality(d.T);
+            a = h.to_act;
+            int64_t row = 0;
+            if (A.pol.rows > 1) {
+                int combo = h.get(h.combo, a);
+                if (h.street == 0) {
+                    int c0, c1;
+                    combo_cards(d.D, d.first, combo, c0, c1);
+                    row = combo_class(d.R, c0, c1);
+                } else {
+                    row = combo;
+                }
+            }
+            ClosedPolicy pol;
+            pol.init(raw_row(A.pol, b * A.pol.rows + row), L, d.T);
+            const int64_t key = rng_key(A.ns_action, root, path, 0, rl, re);
+            act = pol.sample(key_uniform(key));
+            logp = logf(fmaxf(pol.prob(act), POLICY_EPS));
+            // transition (hooks.py:1656-1700)
+            if (with_history) len = A.hist.length ? A.hist.length[b] : history_length(A.hist, b);
+            if (with_history && len < A.hist.tokens) write_token(A.hist, b, len, player_token(h, act, d.T));
+            ++len;
+            street_before = h.street;
+            h.step(act);
+        }
         for (int gen = 0; gen < 3; ++gen) {
-            bool needs = h.needs_chance();
-            int dealt[3] = {0, 1, 2};
+            const bool needs = live && h.needs_chance();
+            unsigned pending = __ballot_sync(0xffffffffu, needs);
+            if (pending == 0u) continue;
+            uint64_t used = 0;
             if (needs) {
                 if (with_history && len < A.hist.tokens) write_token(A.hist, b, len, chance_token(h));
                 ++len;
-                chance_smallest3(A.ns_chance, root, path, (int64_t)gen * d.D, rl, re, h.used_cards(d.D, d.first), d.D,
-                                 dealt);
+                used = h.used_cards(d.D, d.first);
             }
-            h.apply_deal(needs, dealt, d.first);
+            int dealt[3] = {0, 1, 2};
+            while (pending) {
+                const int src = __ffs(pending) - 1;
+                pending &= pending - 1;
+                int out3[3];
+                warp_smallest3(A.ns_chance, __shfl_sync(0xffffffffu, root, src), __shfl_sync(0xffffffffu, path, src),
+                               (int64_t)gen * d.D, __shfl_sync(0xffffffffu, rl, src), __shfl_sync(0xffffffffu, re, src),
+                               __shfl_sync(0xffffffffu, used, src), d.D, out3);
+                if (lane == src) { dealt[0] = out3[0]; dealt[1] = out3[1]; dealt[2] = out3[2]; }
+            }
+            if (live) h.apply_deal(needs, dealt, d.first);
         }
+        if (!live) continue;
         if (with_history && A.hist.length) A.hist.length[b] = len < A.hist.tokens ? len : A.hist.tokens;
         h.store(A.st, b);
         A.action[b] = act;
