@@ -65,3 +65,67 @@ class DistributedSUM:
         out = value.clone()
         dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
         return out
+
+
+class NVLSFlatSum:
+    """A flat fp32 gradient buffer summed across ranks through NVLink SHARP.
+
+    The buffer lives in torch symmetric memory bound to a multicast object;
+    ``sum_()`` launches libpbgb200's multimem all-reduce (each rank reduces
+    its 1/world slice in the switch and multicasts the result), replacing the
+    NCCL SUM of replica.py:352-362 for this buffer.  Raises if the fabric has
+    no multicast support; every rank must call ``sum_()`` in the same order.
+    """
+
+    def __init__(self, numel: int, device, group=None) -> None:
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm
+
+        from ._native import lib
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if numel % (4 * self.world):
+            raise ValueError("NVLS SUM needs numel to be a multiple of 4 * world_size")
+        self.buffer = symm.empty(numel, dtype=torch.float32, device=device)
+        self.buffer.zero_()
+        self.handle = symm.rendezvous(self.buffer, self.group)
+        if int(self.handle.multicast_ptr) == 0:
+            raise RuntimeError("this fabric exposes no NVLS multicast object")
+        if int(self.handle.signal_pad_size) < int(lib().pbg_nvls_signal_bytes()):
+            raise RuntimeError("symmetric-memory signal pad is smaller than the NVLS barrier needs")
+        base = int(self.handle.buffer_ptrs[self.rank])
+        self.multicast = ctypes.c_void_p(int(self.handle.multicast_ptr) + (self.buffer.data_ptr() - base))
+        self.pads = ctypes.c_void_p(int(self.handle.signal_pad_ptrs_dev))
+        self.error = torch.zeros(1, dtype=torch.int32, device=device)
+        self.numel = numel
+        # the barrier slots must start at zero on every rank before the first call
+        slots = int(lib().pbg_nvls_signal_bytes()) // 4
+        pad = self.handle.get_signal_pad(self.rank, (slots,), dtype=torch.int32)
+        pad.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+
+    def sum_(self, stream=None) -> torch.Tensor:
+        """In-place SUM of ``buffer`` over all ranks (stream-ordered, no host sync)."""
+
+        from ._native import call, ptr
+
+        s = torch.cuda.current_stream() if stream is None else stream
+        call("pbg_nvls_allreduce_sum_f32", self.numel, self.multicast, self.pads, self.rank, self.world,
+             ptr(self.error), ctypes_stream(s))
+        return self.buffer
+
+    def check(self) -> None:
+        """Raise if any barrier wait of an earlier sum_() ran out (synchronises)."""
+
+        if int(self.error.item()) != 0:
+            raise RuntimeError("an NVLS all-reduce barrier timed out on this rank")
+
+
+def ctypes_stream(s):
+    import ctypes
+
+    return ctypes.c_void_p(s.cuda_stream)
