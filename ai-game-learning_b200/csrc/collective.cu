@@ -21,7 +21,7 @@
 namespace pbg {
 
 constexpr int NVLS_THREADS = 512;
-constexpr int NVLS_MAX_BLOCKS = 32;
+constexpr int NVLS_MAX_BLOCKS = 160;
 constexpr int NVLS_MAX_WORLD = 8;
 constexpr uint32_t NVLS_WAIT_TRIES = 1u << 22;
 
@@ -117,9 +117,12 @@ int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pa
     PBG_REQUIRE(n > 0 && n % (4 * world) == 0, "nvls_sum: n must be a positive multiple of 4*world");
     PBG_REQUIRE(multicast && signal_pads && error, "nvls_sum: null argument");
     PBG_REQUIRE(((uintptr_t)multicast % 16) == 0, "nvls_sum: multicast address must be 16-byte aligned");
+    // enough CTAs to keep several MB of multimem loads in flight: one per SM at most,
+    // each CTA covering at least 4 float4 per thread
     int64_t vn = n / world / 4;
-    int blocks = (int)((vn + NVLS_THREADS - 1) / NVLS_THREADS);
-    if (blocks > 16) blocks = 16;
+    int64_t want = (vn + 4 * NVLS_THREADS - 1) / (4 * NVLS_THREADS);
+    int cap = sm_count() < NVLS_MAX_BLOCKS ? sm_count() : NVLS_MAX_BLOCKS;
+    int blocks = (int)(want < cap ? want : cap);
     if (blocks < 1) blocks = 1;
     nvls_sum_kernel<<<blocks, NVLS_THREADS, 0, as_stream(stream)>>>(n, (float*)multicast, (uint32_t* const*)signal_pads,
                                                                     rank, world, error);

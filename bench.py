@@ -331,8 +331,24 @@ def main():
     op = FusedPPOBackward(N, A, device, LossConfig(policy_clip=0.2, negative_advantage_ratio_cap=None,
                                                    entropy_coefficient=0.01))
     dlogits = torch.empty_like(logits)
-    grad = torch.randn(args.params, device=device) * 1e-3
     stream = torch.cuda.current_stream(device)
+    flat = None
+    allreduce_kind = "none (single rank)"
+    if world > 1:
+        # the flat gradient lives in symmetric memory and is summed through NVLink SHARP by
+        # libpbgb200's multimem kernel; NCCL only if the fabric exposes no multicast object
+        from pbg_b200.distributed import NVLSFlatSum
+
+        try:
+            flat = NVLSFlatSum(args.params, device)
+            grad = flat.buffer
+            allreduce_kind = "NVLS multimem SUM (libpbgb200)"
+        except RuntimeError:
+            grad = torch.empty(args.params, device=device)
+            allreduce_kind = "NCCL SUM"
+        grad.copy_(torch.randn(args.params, device=device) * 1e-3)
+    else:
+        grad = torch.randn(args.params, device=device) * 1e-3
     bound = op.bind(logits, mask, action, old, adv, weight, dlogits)
     bound.launch(stream)  # one-time device set-up happens outside any capture
     torch.cuda.synchronize(device)
@@ -355,7 +371,10 @@ def main():
         if events is not None:
             events[1].record(stream)
         if world > 1:
-            dist.all_reduce(grad, op=dist.ReduceOp.SUM)
+            if flat is not None:
+                flat.sum_(stream)
+            else:
+                dist.all_reduce(grad, op=dist.ReduceOp.SUM)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -377,6 +396,8 @@ def main():
         dist.barrier()
     if float(op.stats[7]) != N:
         raise RuntimeError("loss kernel reported a failed launch (stats rows != N)")
+    if flat is not None:
+        flat.check()
     elapsed_ms = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kernel_events) / args.steps
     if world > 1:
@@ -400,7 +421,10 @@ def main():
             d.copy_(h, non_blocking=True)
         e2e_bound.launch(stream)
         if world > 1:
-            dist.all_reduce(grad, op=dist.ReduceOp.SUM)
+            if flat is not None:
+                flat.sum_(stream)
+            else:
+                dist.all_reduce(grad, op=dist.ReduceOp.SUM)
         stats_host.copy_(op.stats, non_blocking=True)
 
     for _ in range(2):
@@ -431,7 +455,7 @@ def main():
         "config": {"workload": "cfg5 loss microbench: 4,194,304 decisions x 8 actions per rank, fused PPO "
                                "loss backward + flat fp32 gradient SUM all-reduce",
                    "rows_per_rank": N, "actions": A, "grad_params": args.params,
-                   "allreduce": "NCCL SUM" if world > 1 else "none (single rank)",
+                   "allreduce": allreduce_kind,
                    "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}",
                    "launch": "CUDA graph replay (one kernel per step)" if world == 1 else "eager (kernel + NCCL)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
