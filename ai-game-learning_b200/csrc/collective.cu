@@ -10,8 +10,9 @@
 // makes every rank's multicast stores complete before anyone uses the sum.
 //
 // Barrier protocol: CTA c of rank r signals peer p by a release store of 1
-// into p's signal pad at slot (phase, c, r), then waits (acquire) for its own
-// slots (phase, c, p) of every peer and clears them.  Barrier 1 and barrier 2
+// into p's signal pad at slot ((phase * grid + c) * world + r), then waits
+// (acquire) for its own slots ((phase * grid + c) * world + p) of every peer
+// and clears them.  The host caps the grid to what the pad holds.  Barrier 1 and barrier 2
 // use disjoint slot ranges, which is enough for back-to-back calls: a peer can
 // only signal a slot again after this rank has cleared it (the intervening
 // barrier orders it).  Every wait is bounded; a wait that runs out sets
@@ -40,7 +41,7 @@ __device__ bool rank_barrier(uint32_t* const* pads, int rank, int world, int pha
     __shared__ int ok_shared;
     if (threadIdx.x == 0) ok_shared = 1;
     __syncthreads();
-    const int slot_base = (phase * NVLS_MAX_BLOCKS + blockIdx.x) * NVLS_MAX_WORLD;
+    const int slot_base = (phase * (int)gridDim.x + (int)blockIdx.x) * world;
     if (threadIdx.x < world) {
         const int peer = threadIdx.x;
         __threadfence_system();
@@ -107,12 +108,11 @@ using namespace pbg;
 
 extern "C" {
 
-int64_t pbg_nvls_signal_bytes(void) {
-    return (int64_t)2 * NVLS_MAX_BLOCKS * NVLS_MAX_WORLD * sizeof(uint32_t);
-}
+// Signal-pad bytes one CTA needs per rank of the group (two barrier phases).
+int64_t pbg_nvls_signal_bytes(void) { return (int64_t)2 * NVLS_MAX_WORLD * sizeof(uint32_t); }
 
-int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pads, int32_t rank, int32_t world,
-                               uint32_t* error, void* stream) {
+int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pads, int64_t pad_bytes, int32_t rank,
+                               int32_t world, uint32_t* error, void* stream) {
     PBG_REQUIRE(world >= 2 && world <= NVLS_MAX_WORLD && rank >= 0 && rank < world, "nvls_sum: bad rank/world");
     PBG_REQUIRE(n > 0 && n % (4 * world) == 0, "nvls_sum: n must be a positive multiple of 4*world");
     PBG_REQUIRE(multicast && signal_pads && error, "nvls_sum: null argument");
@@ -122,6 +122,9 @@ int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pa
     int64_t vn = n / world / 4;
     int64_t want = (vn + 4 * NVLS_THREADS - 1) / (4 * NVLS_THREADS);
     int cap = sm_count() < NVLS_MAX_BLOCKS ? sm_count() : NVLS_MAX_BLOCKS;
+    int64_t fit = pad_bytes / (2 * (int64_t)world * (int64_t)sizeof(uint32_t));  // barrier slots the pad holds
+    PBG_REQUIRE(fit >= 1, "nvls_sum: signal pad of %lld bytes is too small", (long long)pad_bytes);
+    if (fit < cap) cap = (int)fit;
     int blocks = (int)(want < cap ? want : cap);
     if (blocks < 1) blocks = 1;
     nvls_sum_kernel<<<blocks, NVLS_THREADS, 0, as_stream(stream)>>>(n, (float*)multicast, (uint32_t* const*)signal_pads,

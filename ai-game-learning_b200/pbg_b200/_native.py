@@ -84,7 +84,7 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_ppo_categorical_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_ppo_categorical_backward_noalloc": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_nvls_signal_bytes": (_I64, []),
-    "pbg_nvls_allreduce_sum_f32": (_I32, [_I64, _P, _P, _I32, _I32, _P, _P]),
+    "pbg_nvls_allreduce_sum_f32": (_I32, [_I64, _P, _P, _I64, _I32, _I32, _P, _P]),
     "pbg_adam_partials_size": (_I64, [_I64]),
     "pbg_adam_step": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P]),
 }

@@ -94,7 +94,8 @@ class NVLSFlatSum:
         self.handle = symm.rendezvous(self.buffer, self.group)
         if int(self.handle.multicast_ptr) == 0:
             raise RuntimeError("this fabric exposes no NVLS multicast object")
-        if int(self.handle.signal_pad_size) < int(lib().pbg_nvls_signal_bytes()):
+        self.pad_bytes = int(self.handle.signal_pad_size)
+        if self.pad_bytes < int(lib().pbg_nvls_signal_bytes()):
             raise RuntimeError("symmetric-memory signal pad is smaller than the NVLS barrier needs")
         base = int(self.handle.buffer_ptrs[self.rank])
         self.multicast = ctypes.c_void_p(int(self.handle.multicast_ptr) + (self.buffer.data_ptr() - base))
@@ -102,8 +103,7 @@ class NVLSFlatSum:
         self.error = torch.zeros(1, dtype=torch.int32, device=device)
         self.numel = numel
         # the barrier slots must start at zero on every rank before the first call
-        slots = int(lib().pbg_nvls_signal_bytes()) // 4
-        pad = self.handle.get_signal_pad(self.rank, (slots,), dtype=torch.int32)
+        pad = self.handle.get_signal_pad(self.rank, (self.pad_bytes // 4,), dtype=torch.int32)
         pad.zero_()
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
@@ -114,8 +114,8 @@ class NVLSFlatSum:
         from ._native import call, ptr
 
         s = torch.cuda.current_stream() if stream is None else stream
-        call("pbg_nvls_allreduce_sum_f32", self.numel, self.multicast, self.pads, self.rank, self.world,
-             ptr(self.error), ctypes_stream(s))
+        call("pbg_nvls_allreduce_sum_f32", self.numel, self.multicast, self.pads, self.pad_bytes, self.rank,
+             self.world, ptr(self.error), ctypes_stream(s))
         return self.buffer
 
     def check(self) -> None:

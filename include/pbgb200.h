@@ -298,14 +298,15 @@ int pbg_adam_step(int64_t n, float *master, float *grad, float *first, float *se
 /* replica.py:352-362 (all_reduce SUM of the flat fp32 gradient) over NVLink
  * SHARP: `multicast` is the multicast address of a symmetric-memory buffer
  * of n floats (n a multiple of 4*world), `signal_pads` a device array of the
- * world ranks' signal-pad pointers (each pad at least pbg_nvls_signal_bytes()
- * bytes, zero before first use).  Each rank sums its 1/world slice in the
+ * world ranks' signal-pad pointers (pads of pad_bytes bytes, zero before
+ * first use; the launch uses at most pad_bytes / pbg_nvls_signal_bytes() CTAs).  Each rank sums its 1/world slice in the
  * switch (multimem.ld_reduce) and stores it to every rank (multimem.st),
  * between two bounded cross-rank barriers; *error (device) becomes nonzero if
  * a barrier wait runs out.  Every rank must make the same call. */
-int64_t pbg_nvls_signal_bytes(void);
-int pbg_nvls_allreduce_sum_f32(int64_t n, void *multicast, const void *signal_pads, int32_t rank,
-                               int32_t world, uint32_t *error, void *stream);
+int64_t pbg_nvls_signal_bytes(void); /* pad bytes one CTA uses per group of up to 8 ranks */
+int pbg_nvls_allreduce_sum_f32(int64_t n, void *multicast, const void *signal_pads,
+                               int64_t pad_bytes, int32_t rank, int32_t world, uint32_t *error,
+                               void *stream);
 
 #ifdef __cplusplus
 }
