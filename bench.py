@@ -8,8 +8,9 @@ from the legal set with the counter RNG (LEARNER purpose), old log pi from
 logits + N(0,0.1), advantages N(0,1), decision-mass weights U(0,1).  One
 step = the fused masked log-softmax / clipped-ratio / entropy / dlogits
 kernel over all rows, then (N > 1) the SUM all-reduce of a flat fp32
-gradient buffer of --params parameters over NCCL.  Weak scaling: each rank
-owns its own rows.
+gradient buffer of --params parameters (libpbgb200's NVLS multimem kernel on
+symmetric memory; NCCL when the fabric has no multicast).  Weak scaling: each
+rank owns its own rows.
 
 ``--impl reference`` times the CPU restatement of the same loss (the
 reference has no CPU path) on all host threads.
@@ -352,27 +353,30 @@ def main():
     bound = op.bind(logits, mask, action, old, adv, weight, dlogits)
     bound.launch(stream)  # one-time device set-up happens outside any capture
     torch.cuda.synchronize(device)
-    graph = None
-    if world == 1:
-        # the single-rank step is one kernel: replay it from a CUDA graph so host launch
-        # cost never gaps the device (multi-rank steps keep NCCL eager)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            bound.launch()
+    # Steps are replayed from CUDA graphs over fixed buffers so host launch cost never gaps the
+    # device: one graph for the loss kernel and, at N > 1 with NVLS, one for the gradient SUM
+    # (NCCL, when used, stays eager).
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        bound.launch()
+    sum_graph = None
+    if flat is not None:
+        flat.sum_(stream)  # warm once outside capture
         torch.cuda.synchronize(device)
+        sum_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(sum_graph):
+            flat.sum_()
+    torch.cuda.synchronize(device)
 
     def step(events=None):
         if events is not None:
             events[0].record(stream)
-        if graph is not None:
-            graph.replay()
-        else:
-            bound.launch(stream)
+        graph.replay()
         if events is not None:
             events[1].record(stream)
         if world > 1:
-            if flat is not None:
-                flat.sum_(stream)
+            if sum_graph is not None:
+                sum_graph.replay()
             else:
                 dist.all_reduce(grad, op=dist.ReduceOp.SUM)
 
@@ -457,7 +461,8 @@ def main():
                    "rows_per_rank": N, "actions": A, "grad_params": args.params,
                    "allreduce": allreduce_kind,
                    "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}",
-                   "launch": "CUDA graph replay (one kernel per step)" if world == 1 else "eager (kernel + NCCL)"},
+                   "launch": "CUDA graph replay" + (" (loss kernel, then NVLS SUM kernel)" if flat is not None else
+                                                     " (loss kernel)" + (", NCCL eager" if world > 1 else ""))},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": committed_traffic(N),
                      "kernel": "ppo_bf16x8_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,
@@ -477,6 +482,9 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        del sum_graph, flat, grad
+        torch.cuda.synchronize(device)
+        dist.barrier()
         dist.destroy_process_group()
 
 
