@@ -411,6 +411,34 @@ def main():
     ms_per_step = elapsed_ms / args.steps
     value = world * N / (ms_per_step / 1000.0)
 
+    # the gradient SUM alone, NVLS kernel vs NCCL on the same bytes (max over ranks)
+    allreduce = None
+    if world > 1:
+        def time_reduce(fn, reps=20):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(device)
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                fn()
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            t = torch.tensor([a.elapsed_time(b) / reps], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t[0]) * 1000.0
+
+        nbytes = 4 * args.params
+        bus = lambda us: 2.0 * (world - 1) / world * nbytes / (us * 1e-6) / 1e9
+        scratch = torch.zeros(args.params, device=device)
+        nccl_us = time_reduce(lambda: dist.all_reduce(scratch, op=dist.ReduceOp.SUM))
+        allreduce = {"bytes": nbytes, "nccl_us": nccl_us, "nccl_busbw_gbs": bus(nccl_us)}
+        if sum_graph is not None:
+            nvls_us = time_reduce(sum_graph.replay)
+            allreduce.update({"nvls_us": nvls_us, "nvls_busbw_gbs": bus(nvls_us)})
+        del scratch
+
     # end to end through the public API: pinned host inputs -> device -> loss -> stats back
     host = [t.cpu().pin_memory() for t in inputs]
     stats_host = torch.empty(8, dtype=torch.float64).pin_memory()
@@ -473,6 +501,8 @@ def main():
     }
     if rank == 0:
         line["components"] = {"rollout_step": rollout_component(device)}
+        if allreduce is not None:
+            line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:
         sample = host_sample(1 << 21, A, 0)
         rate, threads, rows, wall = cpu_loss_rate(sample, seconds=3.0)
