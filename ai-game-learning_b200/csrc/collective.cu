@@ -24,6 +24,7 @@ namespace pbg {
 constexpr int NVLS_THREADS = 512;
 constexpr int NVLS_MAX_BLOCKS = 160;
 constexpr int NVLS_MAX_WORLD = 8;
+constexpr int NVLS_UNROLL = 4;
 constexpr uint32_t NVLS_WAIT_TRIES = 1u << 22;
 
 __device__ __forceinline__ void signal_release(uint32_t* addr) {
@@ -87,15 +88,13 @@ __global__ void __launch_bounds__(NVLS_THREADS) nvls_sum_kernel(int64_t n, float
     const int64_t v0 = (int64_t)rank * slice / 4, vn = slice / 4;
     const int64_t stride = (int64_t)gridDim.x * NVLS_THREADS;
     int64_t i = (int64_t)blockIdx.x * NVLS_THREADS + threadIdx.x;
-    for (; i + 3 * stride < vn; i += 4 * stride) {  // four independent loads in flight
-        float4 a = multimem_ld_reduce_add(mc + 4 * (v0 + i));
-        float4 b = multimem_ld_reduce_add(mc + 4 * (v0 + i + stride));
-        float4 c = multimem_ld_reduce_add(mc + 4 * (v0 + i + 2 * stride));
-        float4 d = multimem_ld_reduce_add(mc + 4 * (v0 + i + 3 * stride));
-        multimem_st(mc + 4 * (v0 + i), a);
-        multimem_st(mc + 4 * (v0 + i + stride), b);
-        multimem_st(mc + 4 * (v0 + i + 2 * stride), c);
-        multimem_st(mc + 4 * (v0 + i + 3 * stride), d);
+    constexpr int U = NVLS_UNROLL;  // independent multimem loads in flight per thread
+    for (; i + (U - 1) * stride < vn; i += U * stride) {
+        float4 v[U];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = multimem_ld_reduce_add(mc + 4 * (v0 + i + u * stride));
+        #pragma unroll
+        for (int u = 0; u < U; ++u) multimem_st(mc + 4 * (v0 + i + u * stride), v[u]);
     }
     for (; i < vn; i += stride) multimem_st(mc + 4 * (v0 + i), multimem_ld_reduce_add(mc + 4 * (v0 + i)));
     __syncthreads();
@@ -117,10 +116,10 @@ int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pa
     PBG_REQUIRE(n > 0 && n % (4 * world) == 0, "nvls_sum: n must be a positive multiple of 4*world");
     PBG_REQUIRE(multicast && signal_pads && error, "nvls_sum: null argument");
     PBG_REQUIRE(((uintptr_t)multicast % 16) == 0, "nvls_sum: multicast address must be 16-byte aligned");
-    // enough CTAs to keep several MB of multimem loads in flight: one per SM at most,
-    // each CTA covering at least 4 float4 per thread
+    // as many SMs issuing multimem requests as the slice allows (one float4 per thread
+    // at least), capped at one CTA per SM and by the barrier slots the pad holds
     int64_t vn = n / world / 4;
-    int64_t want = (vn + 4 * NVLS_THREADS - 1) / (4 * NVLS_THREADS);
+    int64_t want = (vn + NVLS_THREADS - 1) / NVLS_THREADS;
     int cap = sm_count() < NVLS_MAX_BLOCKS ? sm_count() : NVLS_MAX_BLOCKS;
     int64_t fit = pad_bytes / (2 * (int64_t)world * (int64_t)sizeof(uint32_t));  // barrier slots the pad holds
     PBG_REQUIRE(fit >= 1, "nvls_sum: signal pad of %lld bytes is too small", (long long)pad_bytes);

@@ -336,11 +336,15 @@ def main():
     flat = None
     allreduce_kind = "none (single rank)"
     if world > 1:
-        # the flat gradient lives in symmetric memory and is summed through NVLink SHARP by
-        # libpbgb200's multimem kernel; NCCL only if the fabric exposes no multicast object
+        # from 4 ranks up the flat gradient lives in symmetric memory and is summed through
+        # NVLink SHARP by libpbgb200's multimem kernel (1.5x NCCL at 8 ranks); at 2 ranks a
+        # multimem SUM moves more NVLink bytes than NCCL's ring, and NCCL is kept, as it is
+        # when the fabric exposes no multicast object
         from pbg_b200.distributed import NVLSFlatSum
 
         try:
+            if world < 4:
+                raise RuntimeError("two ranks: NCCL ring")
             flat = NVLSFlatSum(args.params, device)
             grad = flat.buffer
             allreduce_kind = "NVLS multimem SUM (libpbgb200)"
