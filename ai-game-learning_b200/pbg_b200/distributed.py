@@ -15,11 +15,12 @@ from torch import Tensor
 
 
 class DistributedSUM:
-    def __init__(self, group=None) -> None:
+    def __init__(self, group=None, nvls: "NVLSFlatSum | None" = None) -> None:
         if not dist.is_initialized():
             raise RuntimeError("DistributedSUM requires an initialised process group")
         self.group = group
         self.world_size = dist.get_world_size(group)
+        self.nvls = nvls  # gradients living in this buffer are summed by the NVLS kernel
 
     def agree_active(self, active: Tensor) -> Tensor:
         """replica.py:332-345: lanes active on every rank; raise on disagreement."""
@@ -46,7 +47,11 @@ class DistributedSUM:
             raise ValueError("gradient SUM requires fp32 [K,N]")
         agreed = self.agree_active(active)
         gradients.mul_(agreed.to(gradients.dtype)[:, None])
-        dist.all_reduce(gradients, op=dist.ReduceOp.SUM, group=self.group)
+        if self.nvls is not None and gradients.data_ptr() == self.nvls.buffer.data_ptr() \
+                and gradients.numel() == self.nvls.numel:
+            self.nvls.sum_()
+        else:
+            dist.all_reduce(gradients, op=dist.ReduceOp.SUM, group=self.group)
         return gradients
 
     def barrier(self) -> None:
