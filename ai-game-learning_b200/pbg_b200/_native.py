@@ -50,6 +50,22 @@ class Policy(ctypes.Structure):
         ("rows", _I32), ("mixtures", _I32)]
 
 
+class TargetTables(ctypes.Structure):
+    _fields_ = [(n, _P) for n in (
+        "work0", "work1", "trace", "cost", "delta", "head_v", "head_t", "head_c", "sigma_v", "sigma_t", "sigma_c",
+        "action_p", "action_a", "work_cap", "head_cap", "width", "conversion")]
+
+
+class TargetNodes(ctypes.Structure):
+    _fields_ = [(n, _P) for n in (
+        "replica", "child_begin", "child_count", "destination_row", "input_type", "output_type", "owner_slot",
+        "nominal_degree", "target_degree", "sigma_head_row", "sigma_target_row", "action_begin")]
+
+
+class TargetChildren(ctypes.Structure):
+    _fields_ = [(n, _P) for n in ("source_row", "source_type", "path", "multiplier")]
+
+
 G, S, Hs, L, Pol = Geometry, State, History, Leaf, Policy
 
 SIGNATURES: dict[str, tuple] = {
@@ -83,6 +99,8 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_ppo_partials_size": (_I64, [_I64, _I32]),
     "pbg_ppo_categorical_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_ppo_categorical_backward_noalloc": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_layered_targets": (_I32, [_P, _I32, TargetNodes, TargetChildren, TargetTables, _I32, _I32, _I32, _I32,
+                                   _I32, _I32, ctypes.c_float, _I32, _I32, _P, _P, _P]),
     "pbg_nvls_signal_bytes": (_I64, []),
     "pbg_nvls_allreduce_sum_f32": (_I32, [_I64, _P, _P, _I64, _I32, _I32, _P, _P]),
     "pbg_adam_partials_size": (_I64, [_I64]),

@@ -1,0 +1,195 @@
+"""Layered lambda-return targets over a topology forest.
+
+``run_layers`` has the argument list and result of the reference's queued
+layer operator (pbg/core/csrc/layered_targets.cu:311-411, loaded by
+pbg/core/cuda_layer.py:13 and called from pbg/core/targets.py:640): node and
+child column tensors, per-partition arena tensors, the conversion table and
+the scalar shape arguments in, the per-lane ``failure_min`` (int32,
+INT32_MAX = lane published) out.  The difference is the launch: every layer
+runs inside ONE cooperative kernel with a grid barrier between layers,
+instead of one kernel per layer queued from a host loop.
+
+``LayeredTargets.bind`` builds the device pointer tables once; ``launch``
+then enqueues the single kernel with no allocation or host copy, so a
+caller can replay it (or capture it) per iteration.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Sequence
+
+import torch
+from torch import Tensor
+
+from ._native import NativeError, TargetChildren, TargetNodes, TargetTables, call, stream
+
+INT32_MAX = 2**31 - 1
+BARRIER_TIMEOUT = -2  # failure_min value of every lane when a grid barrier wait ran out
+
+NODE_COLUMNS = ("replica", "child_begin", "child_count", "destination_row", "input_type", "output_type",
+                "owner_slot", "nominal_degree", "target_degree", "sigma_head_row", "sigma_target_row",
+                "action_begin")
+CHILD_COLUMNS = ("source_row", "source_type", "path", "multiplier")
+
+
+class TargetError(RuntimeError):
+    """Invalid layered-target arguments (pbg/core/targets.py:40)."""
+
+
+def _lambda(value: float) -> float:
+    result = float(value)
+    if not math.isfinite(result) or not 0.0 <= result <= 1.0:
+        raise TargetError("lambda must be finite and lie in [0, 1]")
+    return result
+
+
+def _address(t: Tensor | None, device: torch.device) -> int:
+    if t is None or t.numel() == 0:
+        return 0
+    if t.device != device or t.dtype != torch.float32 or not t.is_contiguous():
+        raise TargetError("arena tensors must be contiguous float32 on the plan's device")
+    return t.data_ptr()
+
+
+def conversion_table(widths: Sequence[int], maps: dict[tuple[int, int], Sequence[int]]) -> Tensor:
+    """[outputs, outputs, max_width] int32 source component -> destination component (-1 none).
+
+    ``maps[(source, destination)][h]`` names the destination class of source
+    component h (pbg/core/targets.py:88-94 ConversionMap.destination_index);
+    identity rows are filled for source == destination, as
+    pbg/core/targets.py:609-626 does.
+    """
+
+    n = len(widths)
+    width = max(widths)
+    table = torch.full((n, n, width), -1, dtype=torch.int32)
+    for s in range(n):
+        table[s, s, : widths[s]] = torch.arange(widths[s], dtype=torch.int32)
+    for (s, d), index in maps.items():
+        if len(index) != widths[s]:
+            raise TargetError("conversion map does not cover its source width")
+        if any(i < 0 or i >= widths[d] for i in index):
+            raise TargetError("conversion destination index is out of range")
+        table[s, d, : widths[s]] = torch.tensor(list(index), dtype=torch.int32)
+    return table
+
+
+class LayeredTargets:
+    """One bound forest: pointer tables and columns resident on the device."""
+
+    def __init__(self, layer_ptr: Tensor, nodes: Sequence[Tensor], children: Sequence[Tensor],
+                 work0, work1, trace, cost, delta, head_v, head_t, head_c, sigma_v, sigma_t, sigma_c,
+                 action_p, action_a, conversion: Tensor, work_cap: Sequence[int], head_cap: Sequence[int],
+                 width: Sequence[int], n_replica: int, input_count: int, output_count: int,
+                 action_partition_count: int, p_train: int, max_width: int, lambda_: float, sampled: bool,
+                 branched: bool) -> None:
+        if len(nodes) != len(NODE_COLUMNS) or len(children) != len(CHILD_COLUMNS):
+            raise TargetError("node/child column count differs from the layer-plan schema")
+        device = nodes[0].device
+        if device.type != "cuda":
+            raise TargetError("queued targets require CUDA")
+        self.device = device
+        for t in list(nodes) + list(children[:3]):
+            if t.device != device or t.dtype != torch.int32 or not t.is_contiguous():
+                raise TargetError("layer-plan columns must be contiguous int32 on one CUDA device")
+        if children[3].dtype != torch.float32 or children[3].device != device:
+            raise TargetError("cost multipliers must be float32 on the plan's device")
+        self.lambda_ = _lambda(lambda_)
+        counts = dict(output_count=(work0, work1, trace, cost, delta), input_count=(head_v, head_t, head_c))
+        for name, groups in counts.items():
+            n = output_count if name == "output_count" else input_count
+            for g in groups:
+                if len(g) != n:
+                    raise TargetError(f"arena table length differs from {name}")
+        for g in (sigma_v, sigma_t, sigma_c):
+            if len(g) != n_replica * input_count:
+                raise TargetError("sigma tables must hold n_replica * input_count entries")
+        for g in (action_p, action_a):
+            if len(g) != n_replica * action_partition_count:
+                raise TargetError("action tables must hold n_replica * action_partition_count entries")
+        if not (len(work_cap) == len(width) == output_count and len(head_cap) == input_count):
+            raise TargetError("capacity/width lists differ from the partition counts")
+        if max_width != max(width) or conversion.numel() != output_count * output_count * max_width:
+            raise TargetError("conversion table shape differs from [outputs, outputs, max_width]")
+
+        def table(group) -> Tensor:
+            return torch.tensor([_address(t, device) for t in group], dtype=torch.int64, device=device)
+
+        def ints(values) -> Tensor:
+            return torch.tensor([int(v) for v in values], dtype=torch.int32, device=device)
+
+        self._arenas = [list(g) for g in (work0, work1, trace, cost, delta, head_v, head_t, head_c, sigma_v,
+                                          sigma_t, sigma_c, action_p, action_a)]  # keep the arenas alive
+        self._tables = [table(g) for g in self._arenas]
+        self._ints = [ints(work_cap), ints(head_cap), ints(width),
+                      conversion.to(device=device, dtype=torch.int32).contiguous().flatten()]
+        self.layer_ptr = layer_ptr.to(device=device, dtype=torch.int32).contiguous()
+        self.layers = int(self.layer_ptr.numel()) - 1
+        if self.layers < 0:
+            raise TargetError("layer_ptr must hold layers + 1 offsets")
+        self.nodes = [t.contiguous() for t in nodes]
+        self.children = [t.contiguous() for t in children]
+        self.failure_min = torch.full((n_replica,), INT32_MAX, dtype=torch.int32, device=device)
+        self.sync = torch.zeros(2, dtype=torch.int32, device=device)
+        self.shape = (int(n_replica), int(input_count), int(output_count), int(action_partition_count),
+                      int(p_train), int(max_width))
+        self.sampled, self.branched = bool(sampled), bool(branched)
+        self._args = self._bind()
+
+    def _bind(self) -> tuple:
+        addr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        nd = TargetNodes(*[addr(t) for t in self.nodes])
+        ch = TargetChildren(*[addr(t) for t in self.children])
+        tb = TargetTables(*[addr(t) for t in self._tables], *[addr(t) for t in self._ints])
+        n_replica, input_count, output_count, action_count, p_train, max_width = self.shape
+        return (addr(self.layer_ptr), self.layers, nd, ch, tb, n_replica, input_count, output_count, action_count,
+                p_train, max_width, ctypes.c_float(self.lambda_), int(self.sampled), int(self.branched),
+                addr(self.failure_min), addr(self.sync))
+
+    def launch(self, cuda_stream=None) -> Tensor:
+        """Enqueue the single cooperative launch; returns ``failure_min`` (device)."""
+
+        s = stream(self.device) if cuda_stream is None else ctypes.c_void_p(cuda_stream)
+        call("pbg_layered_targets", *self._args, s)
+        return self.failure_min
+
+    def reset_barrier(self) -> None:
+        """Clear the grid-barrier words after a launch that reported BARRIER_TIMEOUT."""
+
+        self.sync.zero_()
+
+
+def run_layers(layer_ptr_cpu: Tensor, nodes: Sequence[Tensor], children: Sequence[Tensor], work0, work1, trace,
+               cost, delta, head_v, head_t, head_c, sigma_v, sigma_t, sigma_c, action_p, action_a,
+               conversion: Tensor, work_cap, head_cap, width, n_replica: int, input_count: int, output_count: int,
+               action_partition_count: int, p_train: int, max_width: int, lambda_: float, sampled: bool,
+               branched: bool) -> Tensor:
+    """pbg/core/csrc/layered_targets.cu:311 run_layers: the same arguments, the same ``failure_min`` result."""
+
+    if layer_ptr_cpu.device.type != "cpu":
+        raise TargetError("layer_ptr must be CPU")
+    bound = LayeredTargets(layer_ptr_cpu, nodes, children, work0, work1, trace, cost, delta, head_v, head_t,
+                           head_c, sigma_v, sigma_t, sigma_c, action_p, action_a, conversion, work_cap, head_cap,
+                           width, n_replica, input_count, output_count, action_partition_count, p_train, max_width,
+                           lambda_, sampled, branched)
+    return bound.launch()
+
+
+class _Extension:
+    """Module-like handle with the reference extension's one entry point."""
+
+    run_layers = staticmethod(run_layers)
+
+
+def layered_target_cuda() -> _Extension:
+    """pbg/core/cuda_layer.py:13: the layer operator, here from the prebuilt libpbgb200.so."""
+
+    if not torch.cuda.is_available():
+        raise NativeError("layered targets require CUDA")
+    return _Extension()
+
+
+__all__ = ["BARRIER_TIMEOUT", "INT32_MAX", "LayeredTargets", "TargetError", "conversion_table",
+           "layered_target_cuda", "run_layers"]

@@ -293,6 +293,56 @@ int pbg_adam_step(int64_t n, float *master, float *grad, float *first, float *se
                   const float *controls, int64_t *step, int32_t decoupled, double *partials,
                   double *report, void *stream);
 
+/* ------------------------------------------------------- layered targets */
+
+/* Device tables of per-partition arena pointers (int64 device addresses, 0 =
+ * absent), the layout pbg/core/csrc/layered_targets.cu:14-32 binds:
+ * work0/work1/trace/cost/delta [output_count], head_v/head_t/head_c
+ * [input_count], sigma_v/sigma_t/sigma_c [n_replica*input_count],
+ * action_p/action_a [n_replica*action_partition_count]; work_cap/width
+ * [output_count], head_cap [input_count] int32; conversion
+ * [output_count, output_count, max_width] int32 (source component ->
+ * destination component, -1 = none). */
+typedef struct {
+    const int64_t *work0, *work1, *trace, *cost, *delta;
+    const int64_t *head_v, *head_t, *head_c;
+    const int64_t *sigma_v, *sigma_t, *sigma_c;
+    const int64_t *action_p, *action_a;
+    const int32_t *work_cap, *head_cap, *width, *conversion;
+} pbg_target_tables;
+
+/* Topology nodes in reverse-layer order, int32 [node_count] columns
+ * (targets.py:640 run_layers node tensors). */
+typedef struct {
+    const int32_t *replica, *child_begin, *child_count, *destination_row, *input_type, *output_type;
+    const int32_t *owner_slot, *nominal_degree, *target_degree, *sigma_head_row, *sigma_target_row;
+    const int32_t *action_begin;
+} pbg_target_nodes;
+
+/* Child edges: encoded source row (r >= 0 arena 0 row r; r < 0 arena 1 row
+ * -r-1), source output partition, unit path cost, cost multiplier. */
+typedef struct {
+    const int32_t *source_row, *source_type, *path;
+    const float *multiplier;
+} pbg_target_children;
+
+/* pbg/core/csrc/layered_targets.cu:117-411 (layered_target_kernel +
+ * run_layers): lambda-returns, sigma targets and per-action advantages of
+ * every topology node, layer by layer, in ONE cooperative launch.
+ * layer_ptr [layers+1] (device) bounds each layer's nodes; layer l writes
+ * work arena (l+1)&1.  failure_min [n_replica] (device) receives INT_MAX or
+ * the first failing node of each lane, or -2 in every lane when a grid
+ * barrier wait ran out (bounded wait; the kernel then returns early).
+ * sync [2] (device uint32: arrival counter, generation) must hold a zero
+ * counter before the call; a completed call leaves it zero again, a timed-out
+ * one does not (zero it before the next call).  No reference counterpart for
+ * sync: the reference's host loop launches one kernel per layer instead. */
+int pbg_layered_targets(const int32_t *layer_ptr, int32_t layers, pbg_target_nodes nodes,
+                        pbg_target_children children, pbg_target_tables tables, int32_t n_replica,
+                        int32_t input_count, int32_t output_count, int32_t action_partition_count,
+                        int32_t p_train, int32_t max_width, float lambda, int32_t sampled,
+                        int32_t branched, int32_t *failure_min, uint32_t *sync, void *stream);
+
 /* ---------------------------------------------------------- collective */
 
 /* replica.py:352-362 (all_reduce SUM of the flat fp32 gradient) over NVLink

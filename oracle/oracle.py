@@ -102,6 +102,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_policy_probabilities": (None, [_I64, _I32, _I32, _I64, _P, _P, _P, _P, _P, _P, _P]),
         "orc_ppo_categorical": (None, [_I64, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
         "orc_adam": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P]),
+        "orc_layered_targets": (None, [_P, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32,
+                                       _I32, _I32, _I32, ctypes.c_float, _I32, _I32, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -581,3 +583,51 @@ def direct_model_input(machine: Machine, input_type: str, s: State, log_reach=No
         width = H + D + D * D + P + P * D + 2
         parts.append(np.zeros((B, width), np.float32))
     return np.concatenate(parts, 1).astype(np.float32)
+
+
+TARGET_GROUPS = ("work0", "work1", "trace", "cost", "delta", "head_v", "head_t", "head_c",
+                 "sigma_v", "sigma_t", "sigma_c", "action_p", "action_a")
+
+
+def layered_targets(layer_ptr, nodes, children, arenas: dict, conversion, work_cap, head_cap, width, *,
+                    n_replica, input_count, output_count, action_partitions, p_train, lam, sampled, branched):
+    """pbg/core/csrc/layered_targets.cu:117-411 on host arrays (updated in place).
+
+    ``nodes``: the 12 int32 node columns, ``children``: source_row,
+    source_type, path (int32) and multiplier (float32); ``arenas`` maps each
+    name of TARGET_GROUPS to a list of float32 arrays (None = absent).
+    Returns failure_min (int32 [n_replica]).
+    """
+
+    keep = []
+
+    def col(a, dt):
+        a = np.ascontiguousarray(a, dtype=dt)
+        keep.append(a)
+        return a
+
+    lp = col(layer_ptr, np.int32)
+    node_cols = [col(a, np.int32) for a in nodes]
+    node_tab = col(np.array([a.ctypes.data for a in node_cols], dtype=np.uint64), np.uint64)
+    src_row, src_type, path = (col(a, np.int32) for a in children[:3])
+    mult = col(children[3], np.float32)
+    tables = []
+    for name in TARGET_GROUPS:
+        group = arenas.get(name) or []
+        addresses = []
+        for a in group:
+            if a is None or a.size == 0:
+                addresses.append(0)
+            else:
+                assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"], name
+                addresses.append(a.ctypes.data)
+        tables.append(col(np.array(addresses or [0], dtype=np.int64), np.int64))
+    table_tab = col(np.array([t.ctypes.data for t in tables], dtype=np.uint64), np.uint64)
+    wc, hc, wd = col(work_cap, np.int32), col(head_cap if len(head_cap) else [0], np.int32), col(width, np.int32)
+    conv = col(conversion, np.int32)
+    failure = np.zeros(n_replica, dtype=np.int32)
+    lib().orc_layered_targets(_ptr(lp), len(lp) - 1, _ptr(node_tab), _ptr(src_row), _ptr(src_type), _ptr(path),
+                              _ptr(mult), _ptr(table_tab), _ptr(wc), _ptr(hc), _ptr(wd), _ptr(conv), n_replica,
+                              input_count, output_count, action_partitions, p_train, int(max(width)),
+                              float(lam), int(sampled), int(branched), _ptr(failure))
+    return failure

@@ -923,3 +923,178 @@ int32_t orc_adam(int64_t n, float *master, float *grad, float *first, float *sec
     *step = t;
     return 1;
 }
+
+/* ------------------------------------------------------- layered targets */
+
+/*
+ * pbg/core/csrc/layered_targets.cu:117-411 (layered_target_kernel, run_layers):
+ * lambda-return targets over a topology forest, one node after another in
+ * layer order.  Tables hold HOST addresses (int64, 0 = absent) in the layout
+ * the CUDA entry point binds: t[0..4] = work0, work1, trace, cost, delta per
+ * output; t[5..7] = head_v, head_t, head_c per input; t[8..10] = sigma_v,
+ * sigma_t, sigma_c per (lane, input); t[11..12] = action_p, action_a per
+ * (lane, action partition).  node columns n[0..11] and child columns follow
+ * pbg/core/targets.py:272-282.  Float order follows the reference kernel.
+ */
+typedef struct {
+    const int64_t *tab[13];
+    const int32_t *work_cap, *head_cap, *width, *conversion;
+    int32_t output_count, input_count, action_partitions, p_train, max_width;
+} orc_tables;
+
+static float *tab_f(const int64_t *table, int index) { return (float *)(intptr_t)table[index]; }
+
+static float orc_work(const orc_tables *T, const int64_t *table, int part, int lane, int enc, int p, int d) {
+    if (!table || !table[part]) return 0.0f;
+    int arena = enc < 0 ? 1 : 0, row = enc < 0 ? -enc - 1 : enc;
+    int64_t i = ((((int64_t)lane * T->work_cap[part] + row) * 2 + arena) * T->p_train + p) * T->width[part] + d;
+    return tab_f(table, part)[i];
+}
+
+static float orc_convert(const orc_tables *T, const int64_t *table, int src, int dst, int lane, int enc, int p, int d) {
+    if (src == dst) return orc_work(T, table, src, lane, enc, p, d);
+    const int32_t *map = T->conversion + ((int64_t)src * T->output_count + dst) * T->max_width;
+    float s = 0.0f;
+    for (int h = 0; h < T->width[src]; ++h)
+        if (map[h] == d) s += orc_work(T, table, src, lane, enc, p, h);
+    return s;
+}
+
+static float orc_scalar(const orc_tables *T, const int64_t *table, int part, int lane, int enc) {
+    if (!table || !table[part]) return 0.0f;
+    int arena = enc < 0 ? 1 : 0, row = enc < 0 ? -enc - 1 : enc;
+    return tab_f(table, part)[((int64_t)lane * T->work_cap[part] + row) * 2 + arena];
+}
+
+static float orc_trace(const orc_tables *T, int part, int lane, int enc, int p) {
+    int arena = enc < 0 ? 1 : 0, row = enc < 0 ? -enc - 1 : enc;
+    return tab_f(T->tab[2], part)[(((int64_t)lane * T->work_cap[part] + row) * 2 + arena) * T->p_train + p];
+}
+
+static int rb_invalid(float mass, float moment) {
+    return !isfinite(moment) || mass < 0.0f || (mass == 0.0f && fabsf(moment) > 1.0e-7f);
+}
+
+void orc_layered_targets(const int32_t *layer_ptr, int32_t layers, const int32_t *const *n,
+                         const int32_t *src_row, const int32_t *src_type, const int32_t *path,
+                         const float *multiplier, const int64_t *const *tables, const int32_t *work_cap,
+                         const int32_t *head_cap, const int32_t *width, const int32_t *conversion,
+                         int32_t n_replica, int32_t input_count, int32_t output_count,
+                         int32_t action_partitions, int32_t p_train, int32_t max_width, float lambda,
+                         int32_t sampled, int32_t branched, int32_t *failure_min) {
+    orc_tables T;
+    for (int i = 0; i < 13; ++i) T.tab[i] = tables[i];
+    T.work_cap = work_cap; T.head_cap = head_cap; T.width = width; T.conversion = conversion;
+    T.output_count = output_count; T.input_count = input_count; T.action_partitions = action_partitions;
+    T.p_train = p_train; T.max_width = max_width;
+    const int64_t *W0 = T.tab[0], *W1 = T.tab[1];
+    for (int l = 0; l < n_replica; ++l) failure_min[l] = INT32_MAX;
+    for (int layer = 0; layer < layers; ++layer) {
+        const int arena = (layer + 1) & 1;
+        for (int node = layer_ptr[layer]; node < layer_ptr[layer + 1]; ++node) {
+            const int lane = n[0][node], begin = n[1][node], dest = n[3][node];
+            const int input = n[4][node], output = n[5][node], owner = n[6][node];
+            const int nominal = n[7][node], ntgt = n[8][node], head_row = n[9][node], target_row = n[10][node];
+            const int action_begin = n[11][node];
+            if (failure_min[lane] != INT32_MAX) continue;
+            const int w = width[output];
+            int bad = 0;
+            for (int p = 0; p < p_train; ++p) {
+                for (int d = 0; d < w; ++d) {
+                    float m0 = 0.0f, m1 = 0.0f;
+                    for (int a = 0; a < ntgt; ++a) {
+                        int e = begin + a;
+                        float c0 = orc_convert(&T, W0, src_type[e], output, lane, src_row[e], p, d);
+                        m0 += c0;
+                        if (!sampled) {
+                            float c1 = orc_convert(&T, W1, src_type[e], output, lane, src_row[e], p, d);
+                            m1 += c1;
+                            if (rb_invalid(c0, c1)) bad = 1;
+                        }
+                        if (!isfinite(c0)) bad = 1;
+                    }
+                    float v0 = m0 / (float)ntgt;
+                    float v1 = sampled ? 0.0f : m1 / (float)ntgt;
+                    if (p == owner && input >= 0) {
+                        float old_v = tab_f(T.tab[5], input)[((int64_t)lane * head_cap[input] + head_row) * w + d];
+                        float sigma = sampled ? v0 : (v0 > 0.0f ? v1 / v0 : 0.0f);
+                        tab_f(T.tab[8], lane * input_count + input)[(int64_t)target_row * w + d] = sigma;
+                        int part = branched ? output : input;
+                        float *adv = tab_f(T.tab[12], lane * action_partitions + part);
+                        float *post = sampled ? NULL : tab_f(T.tab[11], lane * action_partitions + part);
+                        for (int a = 0; a < ntgt; ++a) {
+                            int e = begin + a;
+                            float c0 = ntgt == 1 ? m0 : orc_convert(&T, W0, src_type[e], output, lane, src_row[e], p, d);
+                            float c1 = sampled ? 0.0f
+                                               : (ntgt == 1 ? m1 : orc_convert(&T, W1, src_type[e], output, lane, src_row[e], p, d));
+                            float base = old_v;
+                            if (ntgt > 1) {
+                                float s0 = 0.0f, s1 = 0.0f;
+                                for (int b = 0; b < ntgt; ++b) {
+                                    if (b == a) continue;
+                                    int f = begin + b;
+                                    s0 += orc_convert(&T, W0, src_type[f], output, lane, src_row[f], p, d);
+                                    if (!sampled) s1 += orc_convert(&T, W1, src_type[f], output, lane, src_row[f], p, d);
+                                }
+                                float cont = sampled ? s0 / (float)(ntgt - 1) : (s0 > 0.0f ? s1 / s0 : 0.0f);
+                                base = lambda * cont + (1.0f - lambda) * old_v;
+                            }
+                            float q = sampled ? c0 : (c0 > 0.0f ? c1 / c0 : 0.0f);
+                            int64_t row = (int64_t)action_begin + a;
+                            adv[row * w + d] = q - base;
+                            if (post) post[row * w + d] = c0;
+                            if (!isfinite(q) || !isfinite(base) ||
+                                (!sampled && (c0 < 0.0f || (c0 == 0.0f && fabsf(c1) > 1.0e-7f))))
+                                bad = 1;
+                        }
+                        if (sampled) v0 = lambda * v0 + (1.0f - lambda) * old_v;
+                        else v1 = lambda * v1 + (1.0f - lambda) * v0 * old_v;
+                    }
+                    if (!isfinite(v0) || (!sampled && rb_invalid(v0, v1))) bad = 1;
+                    int64_t wi = ((((int64_t)lane * work_cap[output] + dest) * 2 + arena) * p_train + p) * w + d;
+                    if (W0 && W0[output]) tab_f(W0, output)[wi] = v0;
+                    if (!sampled && W1 && W1[output]) tab_f(W1, output)[wi] = v1;
+                }
+            }
+            if (branched) {
+                float dbar = 0.0f, craw = 0.0f;
+                for (int a = 0; a < ntgt; ++a) {
+                    int e = begin + a;
+                    dbar += orc_scalar(&T, T.tab[4], src_type[e], lane, src_row[e]);
+                    craw += (float)path[e] + multiplier[e] * orc_scalar(&T, T.tab[3], src_type[e], lane, src_row[e]);
+                }
+                dbar /= (float)ntgt;
+                craw /= (float)ntgt;
+                float texec = 0.0f;
+                for (int p = 0; p < p_train; ++p) {
+                    float mean = 0.0f;
+                    for (int a = 0; a < ntgt; ++a) mean += orc_trace(&T, src_type[begin + a], lane, src_row[begin + a], p);
+                    mean /= (float)ntgt;
+                    tab_f(T.tab[2], output)[(((int64_t)lane * work_cap[output] + dest) * 2 + arena) * p_train + p] = mean;
+                    if (ntgt > 1)
+                        for (int a = 0; a < ntgt; ++a) {
+                            float dv = orc_trace(&T, src_type[begin + a], lane, src_row[begin + a], p) - mean;
+                            texec += dv * dv;
+                        }
+                }
+                if (ntgt > 1) texec /= (float)(ntgt - 1);
+                float pdelta = dbar / (float)ntgt, pcost = craw;
+                if (input >= 0) {
+                    int64_t hi = (int64_t)lane * head_cap[input] + head_row;
+                    float old_t = tab_f(T.tab[6], input)[hi], old_c = tab_f(T.tab[7], input)[hi];
+                    float that = ntgt > 1 ? fmaxf(0.0f, texec - dbar) : 0.0f;
+                    float tstar = ntgt > 1 ? that : old_t;
+                    pdelta = (tstar + dbar) / (float)ntgt - tstar / (float)nominal;
+                    pcost = lambda * craw + (1.0f - lambda) * old_c;
+                    tab_f(T.tab[9], lane * input_count + input)[target_row] = that;
+                    tab_f(T.tab[10], lane * input_count + input)[target_row] = craw;
+                }
+                int64_t si = ((int64_t)lane * work_cap[output] + dest) * 2 + arena;
+                if (T.tab[3] && T.tab[3][output]) tab_f(T.tab[3], output)[si] = pcost;
+                if (T.tab[4] && T.tab[4][output]) tab_f(T.tab[4], output)[si] = pdelta;
+                if (!isfinite(texec) || !isfinite(pcost) || !isfinite(pdelta)) bad = 1;
+            }
+            if (bad && node < failure_min[lane]) failure_min[lane] = node;
+        }
+    }
+}
