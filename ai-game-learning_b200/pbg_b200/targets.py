@@ -114,25 +114,42 @@ class LayeredTargets:
         if max_width != max(width) or conversion.numel() != output_count * output_count * max_width:
             raise TargetError("conversion table shape differs from [outputs, outputs, max_width]")
 
-        def table(group) -> Tensor:
-            return torch.tensor([_address(t, device) for t in group], dtype=torch.int64, device=device)
-
-        def ints(values) -> Tensor:
-            return torch.tensor([int(v) for v in values], dtype=torch.int32, device=device)
-
+        # every pointer table and integer table in one host buffer, one copy to the device
         self._arenas = [list(g) for g in (work0, work1, trace, cost, delta, head_v, head_t, head_c, sigma_v,
                                           sigma_t, sigma_c, action_p, action_a)]  # keep the arenas alive
-        self._tables = [table(g) for g in self._arenas]
-        self._ints = [ints(work_cap), ints(head_cap), ints(width),
-                      conversion.to(device=device, dtype=torch.int32).contiguous().flatten()]
+        addresses = [[_address(t, device) for t in g] for g in self._arenas]
+        ints = [[int(v) for v in work_cap], [int(v) for v in head_cap], [int(v) for v in width]]
+        lengths = [len(a) for a in addresses]
+        host = torch.empty(sum(lengths) + (sum(len(i) for i in ints) + 1) // 2, dtype=torch.int64, pin_memory=True)
+        flat = [a for g in addresses for a in g]
+        host[: len(flat)] = torch.tensor(flat, dtype=torch.int64) if flat else host[:0]
+        packed = host[len(flat):].view(torch.int32)
+        cursor = 0
+        int_slices = []
+        for values in ints:
+            packed[cursor: cursor + len(values)] = torch.tensor(values, dtype=torch.int32)
+            int_slices.append((cursor, len(values)))
+            cursor += len(values)
+        self._table_block = host.to(device, non_blocking=True)
+        offset = 0
+        self._tables = []
+        for n in lengths:
+            self._tables.append(self._table_block[offset: offset + n])
+            offset += n
+        int_block = self._table_block[offset:].view(torch.int32)
+        self._ints = [int_block[c: c + n] for c, n in int_slices]
+        self._ints.append(conversion.to(device=device, dtype=torch.int32).contiguous().flatten())
+        self._host_block = host  # pinned source of the asynchronous copy
         self.layer_ptr = layer_ptr.to(device=device, dtype=torch.int32).contiguous()
         self.layers = int(self.layer_ptr.numel()) - 1
         if self.layers < 0:
             raise TargetError("layer_ptr must hold layers + 1 offsets")
         self.nodes = [t.contiguous() for t in nodes]
         self.children = [t.contiguous() for t in children]
-        self.failure_min = torch.full((n_replica,), INT32_MAX, dtype=torch.int32, device=device)
-        self.sync = torch.zeros(2, dtype=torch.int32, device=device)
+        # failure_min [n_replica] then the grid barrier's two words; the kernel sets failure_min itself
+        self._words = torch.zeros(n_replica + 2, dtype=torch.int32, device=device)
+        self.failure_min = self._words[:n_replica]
+        self.sync = self._words[n_replica:]
         self.shape = (int(n_replica), int(input_count), int(output_count), int(action_partition_count),
                       int(p_train), int(max_width))
         self.sampled, self.branched = bool(sampled), bool(branched)
@@ -193,3 +210,93 @@ def layered_target_cuda() -> _Extension:
 
 __all__ = ["BARRIER_TIMEOUT", "INT32_MAX", "LayeredTargets", "TargetError", "conversion_table",
            "layered_target_cuda", "run_layers"]
+
+
+def synthetic_tree_plan(lanes: int, depth: int, branching: int, p_train: int, width: int, *, device,
+                        sampled: bool = False, branched: bool = True, lam: float = 0.5, seed: int = 0):
+    """A seeded full ``branching``-ary forest (one tree of ``depth`` layers per lane) as run_layers arguments.
+
+    One output and one input partition of ``width`` components.  Work rows are
+    double-buffered the way the reference's layer plan lays them out: layer l
+    writes arena (l+1)&1 at rows [0, nodes in the layer), the leaves sit in
+    arena 0 and are overwritten by layer 1.  Owners follow the player clock
+    (layer l is owned by seat l % p_train).  Returns (args, info): ``args`` is
+    the positional argument tuple of ``run_layers`` / ``LayeredTargets`` with
+    device tensors, ``info`` holds counts and the algorithmic bytes of the pass.
+    """
+
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    b, D, P, W, R = int(branching), int(depth), int(p_train), int(width), int(lanes)
+    per_layer = [b ** (D - 1 - layer) for layer in range(D)]
+    nodes_per_lane = sum(per_layer)
+    cap = b ** D
+    cols = {k: [] for k in NODE_COLUMNS}
+    src_row, edges_per_node = [], b
+    sigma_base = np.cumsum([0] + per_layer)  # per lane: nodes of earlier layers
+    layer_ptr = [0]
+    for layer, n in enumerate(per_layer):
+        lane = np.repeat(np.arange(R), n)
+        i = np.tile(np.arange(n), R)
+        count = R * n
+        cols["replica"].append(lane)
+        cols["child_begin"].append(np.zeros(count, np.int64))  # filled below
+        cols["child_count"].append(np.full(count, b))
+        cols["destination_row"].append(i)
+        cols["input_type"].append(np.zeros(count, np.int64))
+        cols["output_type"].append(np.zeros(count, np.int64))
+        cols["owner_slot"].append(np.full(count, layer % P))
+        cols["nominal_degree"].append(np.full(count, b))
+        cols["target_degree"].append(np.full(count, b))
+        rows = sigma_base[layer] + i
+        cols["sigma_head_row"].append(rows)
+        cols["sigma_target_row"].append(rows)
+        cols["action_begin"].append(rows * b)
+        child = (i[:, None] * b + np.arange(b)[None, :]).reshape(-1)
+        # layer 0 reads leaves (arena 0); layer l reads layer l-1's rows in arena l&1
+        arena = 0 if layer == 0 else layer & 1
+        src_row.append(child if arena == 0 else -child - 1)
+        layer_ptr.append(layer_ptr[-1] + count)
+    node_cols = [np.concatenate(cols[k]).astype(np.int32) for k in NODE_COLUMNS]
+    total = int(layer_ptr[-1])
+    node_cols[1] = (np.arange(total, dtype=np.int64) * b).astype(np.int32)
+    edges = total * b
+    children = [np.concatenate(src_row).astype(np.int32), np.zeros(edges, np.int32), np.ones(edges, np.int32),
+                rng.uniform(0.5, 1.0, edges).astype(np.float32)]
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+    mass = rng.uniform(0.05, 1.0, (R, cap, 2, P, W)).astype(np.float32)
+    work0 = [t(mass if not sampled else rng.uniform(-1, 1, mass.shape).astype(np.float32))]
+    work1 = [t(mass * rng.uniform(-1, 1, mass.shape).astype(np.float32))] if not sampled else [
+        torch.empty(0, device=device)]
+    empty = torch.empty(0, device=device)
+    trace = [t(rng.uniform(0, 1, (R, cap, 2, P)).astype(np.float32))] if branched else [empty]
+    cost = [t(rng.uniform(0, 1, (R, cap, 2)).astype(np.float32))] if branched else [empty]
+    delta = [t(rng.uniform(-0.1, 0.1, (R, cap, 2)).astype(np.float32))] if branched else [empty]
+    head_v = [t(rng.uniform(-1, 1, (R, nodes_per_lane, W)).astype(np.float32))]
+    head_t = [t(rng.uniform(0, 1, (R, nodes_per_lane)).astype(np.float32))] if branched else [empty]
+    head_c = [t(rng.uniform(0, 1, (R, nodes_per_lane)).astype(np.float32))] if branched else [empty]
+    sigma_v = list(torch.zeros((R, nodes_per_lane, W), device=device).unbind(0))
+    sigma_t = list(torch.zeros((R, nodes_per_lane), device=device).unbind(0)) if branched else [empty] * R
+    sigma_c = list(torch.zeros((R, nodes_per_lane), device=device).unbind(0)) if branched else [empty] * R
+    action_a = list(torch.zeros((R, nodes_per_lane * b, W), device=device).unbind(0))
+    action_p = list(torch.zeros((R, nodes_per_lane * b, W), device=device).unbind(0)) if not sampled else [empty] * R
+    conversion = torch.arange(W, dtype=torch.int32, device=device)
+    args = (torch.tensor(layer_ptr, dtype=torch.int32), [t(c) for c in node_cols], [t(c) for c in children],
+            work0, work1, trace, cost, delta, head_v, head_t, head_c, sigma_v, sigma_t, sigma_c, action_p, action_a,
+            conversion, [cap], [nodes_per_lane], [W], R, 1, 1, 1, P, W, lam, sampled, branched)
+    # algorithmic bytes per node: node record, edges, children's work (and trace/cost/delta) read once,
+    # the head row, the parent's work row, sigma and per-action targets written once
+    channels = 1 if sampled else 2
+    read = 12 * 4 + b * 16 + b * P * W * channels * 4 + W * 4
+    write = P * W * channels * 4 + W * 4 + b * W * channels * 4
+    if branched:
+        read += b * (P + 2) * 4 + 2 * 4
+        write += (P + 2) * 4 + 2 * 4
+    info = {"lanes": R, "depth": D, "branching": b, "p_train": P, "width": W, "nodes": total, "edges": edges,
+            "bytes_per_node": read + write, "algorithmic_bytes": total * (read + write),
+            "estimator": "sampled" if sampled else "rao_blackwell", "rollout": "branched" if branched else "sequential"}
+    return args, info

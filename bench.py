@@ -308,6 +308,47 @@ def rollout_component(device, hands=65_536, seed=0):
             "gpu_launches": len(counts)}
 
 
+def targets_component(device, lanes=256, depth=8, branching=2, p_train=2, width=8, reps=20):
+    """Layered lambda-return targets over a seeded full binary forest (RB, branched: the widest mode).
+
+    The forest is re-seeded from pristine work arenas before every pass (a device copy outside the
+    timed region); each pass is ONE cooperative launch over all layers, timed with CUDA events.
+    """
+
+    import torch
+    from pbg_b200.targets import INT32_MAX, LayeredTargets, synthetic_tree_plan
+
+    args, info = synthetic_tree_plan(lanes, depth, branching, p_train, width, device=device, seed=5)
+    bound = LayeredTargets(*args)
+    live = [args[3][0], args[4][0], args[5][0], args[6][0], args[7][0]]  # work0, work1, trace, cost, delta
+    pristine = [x.clone() for x in live]
+    stream = torch.cuda.current_stream(device)
+    times = []
+    for rep in range(reps + 3):
+        for dst, src in zip(live, pristine):
+            dst.copy_(src)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        failure = bound.launch()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        if rep >= 3:
+            times.append(a.elapsed_time(b))
+    if not bool((failure == INT32_MAX).all()):
+        raise RuntimeError("layered targets reported a failed lane on the synthetic forest")
+    ms = sorted(times)[len(times) // 2]
+    peak, _ = measured_peak()
+    achieved = info["algorithmic_bytes"] / (ms / 1000.0) / 1e9
+    return {"workload": f"layered targets, {lanes} lanes x full binary tree of depth {depth}, "
+                        f"{info['estimator']} {info['rollout']}, P={p_train}, width {width}",
+            "nodes": info["nodes"], "layers": depth, "us_per_pass": 1000.0 * ms,
+            "nodes_per_s": info["nodes"] / (ms / 1000.0),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "bytes_per_node": info["bytes_per_node"],
+                         "kernel": "layered_targets_kernel"},
+            "gpu_launches": 1}
+
+
 # ----------------------------------------------------------- device arm
 
 
@@ -504,7 +545,8 @@ def main():
         "clocks": clocks.summary(),
     }
     if rank == 0:
-        line["components"] = {"rollout_step": rollout_component(device)}
+        line["components"] = {"rollout_step": rollout_component(device),
+                              "layered_targets": targets_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:

@@ -1,0 +1,88 @@
+"""Compile the reference's own layer operator into oracle/_ref (test infrastructure only).
+
+    python oracle/build_ref.py [--reference <pbg checkout>] [--force]
+
+The reference's queued layered-target operator is one CUDA source file
+(pbg/core/csrc/layered_targets.cu, a torch extension with one entry point,
+``run_layers``).  This recipe compiles that file where it lies in the pbg
+checkout with the reference's own device flags (pbg/core/cuda_layer.py:19-25:
+-O3 --fmad=false) for sm_100a, linking the torch libraries of this
+interpreter, into ``oracle/_ref/ref_layered_targets<EXT_SUFFIX>``.  Nothing is
+copied into this repository.  The GPU tests import the module (when it was
+built) to check the CUDA library against the reference's kernel itself; the
+product never loads it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+import sysconfig
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "_ref")
+MODULE = "ref_layered_targets"
+SOURCE = os.path.join("pbg", "core", "csrc", "layered_targets.cu")
+DEFAULT_REFERENCE = os.environ.get("PBG_REFERENCE", "/root/reference")
+
+
+def target() -> str:
+    return os.path.join(OUT, MODULE + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build(reference: str = DEFAULT_REFERENCE, force: bool = False) -> str | None:
+    """Build the reference operator; None when the pbg checkout is absent."""
+
+    src = os.path.join(reference, SOURCE)
+    if not os.path.exists(src):
+        return None
+    out = target()
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
+        return out
+    import torch
+    from torch.utils import cpp_extension
+
+    os.makedirs(OUT, exist_ok=True)
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    includes = cpp_extension.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"]]
+    libs = cpp_extension.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [os.path.join(cuda, "bin", "nvcc"), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "--fmad=false",
+           "-std=c++17", "-shared", "-Xcompiler", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           f"-DTORCH_EXTENSION_NAME={MODULE}", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           "--expt-relaxed-constexpr", "-o", out, src]
+    for inc in includes:
+        cmd += ["-I", inc]
+    for lib in libs:
+        cmd += ["-L", lib, f"-Xlinker=-rpath,{lib}"]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python", "-lcudart"]
+    subprocess.run(cmd, check=True)
+    return out
+
+
+def load():
+    """Import the built module, or None when it was not built."""
+
+    path = target()
+    if not os.path.exists(path):
+        return None
+    import importlib.util
+
+    import torch  # noqa: F401  (the module links libtorch)
+
+    spec = importlib.util.spec_from_file_location(MODULE, path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args()
+    result = build(a.reference, a.force)
+    print(result if result else f"no pbg checkout at {a.reference}: nothing built")
+    sys.exit(0)

@@ -51,10 +51,10 @@ class PlanRuns:
                                                 self.work_cap, self.head_cap, self.width, **self.kwargs())
         return failure, arenas
 
-    def run_device(self, device, arenas: dict | None = None):
-        import torch
+    def device_args(self, device, arenas: dict | None = None):
+        """Positional arguments of run_layers (both the reference's and pbg_b200's) and the arena tensors."""
 
-        from pbg_b200.targets import run_layers
+        import torch
 
         arenas = self.copy_arenas() if arenas is None else arenas
         n_in, n_out = self.input_count, self.output_count
@@ -75,13 +75,23 @@ class PlanRuns:
             groups[name] = dev(arenas[name], count)
         nodes = [torch.from_numpy(a).to(device) for a in self.nodes]
         children = [torch.from_numpy(a).to(device) for a in self.children]
-        failure = run_layers(torch.from_numpy(self.layer_ptr), nodes, children, groups["work0"], groups["work1"],
-                             groups["trace"], groups["cost"], groups["delta"], groups["head_v"], groups["head_t"],
-                             groups["head_c"], groups["sigma_v"], groups["sigma_t"], groups["sigma_c"],
-                             groups["action_p"], groups["action_a"], torch.from_numpy(self.conversion),
-                             self.work_cap, self.head_cap, self.width, self.n_replica, n_in, n_out,
-                             self.action_partitions, self.p_train, max(self.width), self.lam, self.sampled,
-                             self.branched)
+        args = (torch.from_numpy(self.layer_ptr), nodes, children, groups["work0"], groups["work1"],
+                groups["trace"], groups["cost"], groups["delta"], groups["head_v"], groups["head_t"],
+                groups["head_c"], groups["sigma_v"], groups["sigma_t"], groups["sigma_c"],
+                groups["action_p"], groups["action_a"], torch.from_numpy(self.conversion).flatten().to(device),
+                list(self.work_cap), list(self.head_cap), list(self.width), self.n_replica, n_in, n_out,
+                self.action_partitions, self.p_train, max(self.width), self.lam, self.sampled, self.branched)
+        return args, groups, arenas
+
+    def run_device(self, device, arenas: dict | None = None, runner=None):
+        """Run through ``runner`` (default: pbg_b200.targets.run_layers); returns failure, arenas (numpy)."""
+
+        import torch
+
+        if runner is None:
+            from pbg_b200.targets import run_layers as runner
+        args, groups, arenas = self.device_args(device, arenas)
+        failure = runner(*args)
         torch.cuda.synchronize(device)
         out = {}
         for name, group in groups.items():

@@ -126,3 +126,31 @@ def test_lambda_out_of_range_raises_before_launch():
     forest.lam = 1.5
     with pytest.raises(TargetError):
         forest.run_device(DEV)
+
+
+@pytest.mark.parametrize("sampled,branched", [(False, True), (True, False), (False, False), (True, True)])
+def test_synthetic_tree_plan_matches_oracle(sampled, branched):
+    # the bench workload's generator, at a small size, checked against the restatement
+    from pbg_b200.targets import run_layers, synthetic_tree_plan
+
+    args, info = synthetic_tree_plan(6, 5, 3, 2, 4, device=DEV, sampled=sampled, branched=branched, seed=1)
+    groups = {name: [None if t.numel() == 0 else t.cpu().numpy().copy() for t in group]
+              for name, group in zip(oracle.TARGET_GROUPS, args[3:16])}
+    for name in groups:
+        if all(a is None for a in groups[name]):
+            groups[name] = None
+    ref_failure = oracle.layered_targets(
+        args[0].numpy(), [t.cpu().numpy() for t in args[1]], [t.cpu().numpy() for t in args[2]], groups,
+        args[16].cpu().numpy(), args[17], args[18], args[19], n_replica=args[20], input_count=args[21],
+        output_count=args[22], action_partitions=args[23], p_train=args[24], lam=args[26], sampled=args[27],
+        branched=args[28])
+    failure = run_layers(*args)
+    torch.cuda.synchronize()
+    assert (ref_failure == 2**31 - 1).all()
+    assert np.array_equal(failure.cpu().numpy(), ref_failure)
+    for name, group in zip(oracle.TARGET_GROUPS, args[3:16]):
+        if groups[name] is None:
+            continue
+        for i, (x, t) in enumerate(zip(groups[name], group)):
+            if x is not None:
+                np.testing.assert_array_equal(x, t.cpu().numpy(), err_msg=f"{name}[{i}]")
