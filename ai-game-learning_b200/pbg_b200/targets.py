@@ -9,15 +9,18 @@ INT32_MAX = lane published) out.  The difference is the launch: every layer
 runs inside ONE cooperative kernel with a grid barrier between layers,
 instead of one kernel per layer queued from a host loop.
 
-``LayeredTargets.bind`` builds the device pointer tables once; ``launch``
-then enqueues the single kernel with no allocation or host copy, so a
-caller can replay it (or capture it) per iteration.
+``LayeredTargets`` builds the device pointer tables once; ``launch`` then
+enqueues the single kernel with no allocation or host copy, so a caller can
+replay it per iteration.  ``run_layers`` keeps the last few bindings keyed by
+the arguments' addresses, layer offsets and scalars, so repeated calls over
+persistent arenas (the reference executor's pattern) skip the table upload.
 """
 
 from __future__ import annotations
 
 import ctypes
 import math
+from collections import OrderedDict
 from typing import Sequence
 
 import torch
@@ -162,15 +165,24 @@ class LayeredTargets:
         tb = TargetTables(*[addr(t) for t in self._tables], *[addr(t) for t in self._ints])
         n_replica, input_count, output_count, action_count, p_train, max_width = self.shape
         return (addr(self.layer_ptr), self.layers, nd, ch, tb, n_replica, input_count, output_count, action_count,
-                p_train, max_width, ctypes.c_float(self.lambda_), int(self.sampled), int(self.branched),
-                addr(self.failure_min), addr(self.sync))
+                p_train, max_width, ctypes.c_float(self.lambda_), int(self.sampled), int(self.branched))
 
-    def launch(self, cuda_stream=None) -> Tensor:
-        """Enqueue the single cooperative launch; returns ``failure_min`` (device)."""
+    def launch(self, cuda_stream=None, failure_out: Tensor | None = None) -> Tensor:
+        """Enqueue the single cooperative launch; returns ``failure_min`` (device int32 [n_replica]).
 
+        ``failure_out`` receives the result instead of the binding's own
+        buffer (the kernel initialises it, no clearing needed).  Launches of
+        one binding must be ordered on one stream: they share the grid
+        barrier's words.
+        """
+
+        out = self.failure_min if failure_out is None else failure_out
+        if out.device != self.device or out.dtype != torch.int32 or out.numel() != self.shape[0]:
+            raise TargetError("failure_out must be int32 [n_replica] on the plan's device")
         s = stream(self.device) if cuda_stream is None else ctypes.c_void_p(cuda_stream)
-        call("pbg_layered_targets", *self._args, s)
-        return self.failure_min
+        call("pbg_layered_targets", *self._args, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(self.sync.data_ptr()),
+             s)
+        return out
 
     def reset_barrier(self) -> None:
         """Clear the grid-barrier words after a launch that reported BARRIER_TIMEOUT."""
@@ -187,11 +199,38 @@ def run_layers(layer_ptr_cpu: Tensor, nodes: Sequence[Tensor], children: Sequenc
 
     if layer_ptr_cpu.device.type != "cpu":
         raise TargetError("layer_ptr must be CPU")
-    bound = LayeredTargets(layer_ptr_cpu, nodes, children, work0, work1, trace, cost, delta, head_v, head_t,
-                           head_c, sigma_v, sigma_t, sigma_c, action_p, action_a, conversion, work_cap, head_cap,
-                           width, n_replica, input_count, output_count, action_partition_count, p_train, max_width,
-                           lambda_, sampled, branched)
-    return bound.launch()
+    groups = (work0, work1, trace, cost, delta, head_v, head_t, head_c, sigma_v, sigma_t, sigma_c, action_p, action_a)
+    # a binding depends only on addresses, the layer offsets, the conversion table and the scalars
+    conv_key = (conversion.data_ptr(),) if (conversion.is_cuda and conversion.dtype == torch.int32
+                                             and conversion.is_contiguous()) else tuple(conversion.flatten().tolist())
+    key = (nodes[0].device.index, tuple(layer_ptr_cpu.tolist()), tuple(map(_DATA_PTR, nodes)),
+           tuple(map(_DATA_PTR, children)), tuple(tuple(map(_DATA_PTR, g)) for g in groups), conv_key,
+           tuple(work_cap), tuple(head_cap), tuple(width), n_replica, input_count, output_count,
+           action_partition_count, p_train, max_width, float(lambda_), bool(sampled), bool(branched))
+    bound = _BINDINGS.get(key)
+    if bound is None:
+        bound = LayeredTargets(layer_ptr_cpu, nodes, children, work0, work1, trace, cost, delta, head_v, head_t,
+                               head_c, sigma_v, sigma_t, sigma_c, action_p, action_a, conversion, work_cap, head_cap,
+                               width, n_replica, input_count, output_count, action_partition_count, p_train,
+                               max_width, lambda_, sampled, branched)
+        _BINDINGS[key] = bound
+        while len(_BINDINGS) > _MAX_BINDINGS:
+            _BINDINGS.popitem(last=False)
+    else:
+        _BINDINGS.move_to_end(key)
+    failure = torch.empty(int(n_replica), dtype=torch.int32, device=bound.device)
+    return bound.launch(failure_out=failure)
+
+
+_DATA_PTR = torch.Tensor.data_ptr
+_MAX_BINDINGS = 8
+_BINDINGS: "OrderedDict[tuple, LayeredTargets]" = OrderedDict()
+
+
+def clear_bindings() -> None:
+    """Drop the cached bindings (they keep their arena tensors alive)."""
+
+    _BINDINGS.clear()
 
 
 class _Extension:
@@ -208,8 +247,8 @@ def layered_target_cuda() -> _Extension:
     return _Extension()
 
 
-__all__ = ["BARRIER_TIMEOUT", "INT32_MAX", "LayeredTargets", "TargetError", "conversion_table",
-           "layered_target_cuda", "run_layers"]
+__all__ = ["BARRIER_TIMEOUT", "INT32_MAX", "LayeredTargets", "TargetError", "clear_bindings", "conversion_table",
+           "layered_target_cuda", "run_layers", "synthetic_tree_plan"]
 
 
 def synthetic_tree_plan(lanes: int, depth: int, branching: int, p_train: int, width: int, *, device,

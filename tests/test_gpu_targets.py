@@ -154,3 +154,31 @@ def test_synthetic_tree_plan_matches_oracle(sampled, branched):
         for i, (x, t) in enumerate(zip(groups[name], group)):
             if x is not None:
                 np.testing.assert_array_equal(x, t.cpu().numpy(), err_msg=f"{name}[{i}]")
+
+
+def test_run_layers_rebinds_nothing_and_reads_live_arenas():
+    # repeated calls over the same arenas reuse one binding; the kernel reads the arenas' current contents
+    from pbg_b200 import targets as T
+
+    forest = tf.Forest(23, n_replica=3, sampled=False, branched=True, layers=4)
+    args, groups, arenas = forest.device_args(DEV)
+    T.clear_bindings()
+    first = T.run_layers(*args)
+    assert len(T._BINDINGS) == 1
+    lane, t, row, arena = forest.leaves[0]
+    scale = 2.0
+    groups["work1"][t][lane, row, arena] *= scale
+    second = T.run_layers(*args)
+    torch.cuda.synchronize()
+    assert len(T._BINDINGS) == 1
+    assert first.data_ptr() != second.data_ptr()
+    host = forest.copy_arenas()
+    host["work1"][t][lane, row, arena] *= np.float32(scale)
+    ref_failure, ref = forest.run_oracle(oracle, host)
+    assert np.array_equal(second.cpu().numpy(), ref_failure)
+    for name, group in groups.items():
+        if ref[name] is None:
+            continue
+        for x, y in zip(ref[name], group):
+            if x is not None:
+                np.testing.assert_array_equal(x, y.cpu().numpy(), err_msg=name)
