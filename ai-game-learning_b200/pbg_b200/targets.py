@@ -23,6 +23,7 @@ import math
 from collections import OrderedDict
 from typing import Sequence
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -46,14 +47,6 @@ def _lambda(value: float) -> float:
     if not math.isfinite(result) or not 0.0 <= result <= 1.0:
         raise TargetError("lambda must be finite and lie in [0, 1]")
     return result
-
-
-def _address(t: Tensor | None, device: torch.device) -> int:
-    if t is None or t.numel() == 0:
-        return 0
-    if t.device != device or t.dtype != torch.float32 or not t.is_contiguous():
-        raise TargetError("arena tensors must be contiguous float32 on the plan's device")
-    return t.data_ptr()
 
 
 def conversion_table(widths: Sequence[int], maps: dict[tuple[int, int], Sequence[int]]) -> Tensor:
@@ -117,33 +110,36 @@ class LayeredTargets:
         if max_width != max(width) or conversion.numel() != output_count * output_count * max_width:
             raise TargetError("conversion table shape differs from [outputs, outputs, max_width]")
 
-        # every pointer table and integer table in one host buffer, one copy to the device
+        # every pointer table, the integer tables and the layer offsets in one pinned host buffer, one
+        # copy to the device; like the reference's pointer tables, entries are the tensors' addresses
         self._arenas = [list(g) for g in (work0, work1, trace, cost, delta, head_v, head_t, head_c, sigma_v,
                                           sigma_t, sigma_c, action_p, action_a)]  # keep the arenas alive
-        addresses = [[_address(t, device) for t in g] for g in self._arenas]
-        ints = [[int(v) for v in work_cap], [int(v) for v in head_cap], [int(v) for v in width]]
-        lengths = [len(a) for a in addresses]
-        host = torch.empty(sum(lengths) + (sum(len(i) for i in ints) + 1) // 2, dtype=torch.int64, pin_memory=True)
-        flat = [a for g in addresses for a in g]
-        host[: len(flat)] = torch.tensor(flat, dtype=torch.int64) if flat else host[:0]
-        packed = host[len(flat):].view(torch.int32)
-        cursor = 0
-        int_slices = []
-        for values in ints:
-            packed[cursor: cursor + len(values)] = torch.tensor(values, dtype=torch.int32)
-            int_slices.append((cursor, len(values)))
-            cursor += len(values)
+        for g in self._arenas:
+            if g and (g[0].device != device or g[0].dtype != torch.float32):
+                raise TargetError("arena tensors must be float32 on the plan's device")
+        lengths = [len(g) for g in self._arenas]
+        flat = [p for g in self._arenas for p in map(_DATA_PTR, g)]
+        ints = [int(v) for v in work_cap] + [int(v) for v in head_cap] + [int(v) for v in width]
+        lp = layer_ptr.to(dtype=torch.int32).flatten().tolist() if layer_ptr.device.type == "cpu" else None
+        small = ints + (lp or [])
+        host = torch.empty(len(flat) + (len(small) + 1) // 2, dtype=torch.int64, pin_memory=True)
+        host.numpy()[: len(flat)] = flat
+        host.numpy()[len(flat):].view(np.int32)[: len(small)] = small
         self._table_block = host.to(device, non_blocking=True)
-        offset = 0
-        self._tables = []
+        self._host_block = host  # pinned source of the asynchronous copy
+        self._tables, offset = [], 0
         for n in lengths:
             self._tables.append(self._table_block[offset: offset + n])
             offset += n
         int_block = self._table_block[offset:].view(torch.int32)
-        self._ints = [int_block[c: c + n] for c, n in int_slices]
-        self._ints.append(conversion.to(device=device, dtype=torch.int32).contiguous().flatten())
-        self._host_block = host  # pinned source of the asynchronous copy
-        self.layer_ptr = layer_ptr.to(device=device, dtype=torch.int32).contiguous()
+        n_out, n_in = len(work_cap), len(head_cap)
+        self._ints = [int_block[:n_out], int_block[n_out: n_out + n_in],
+                      int_block[n_out + n_in: 2 * n_out + n_in],
+                      conversion.to(device=device, dtype=torch.int32).contiguous().flatten()]
+        if lp is not None:
+            self.layer_ptr = int_block[len(ints): len(ints) + len(lp)]
+        else:
+            self.layer_ptr = layer_ptr.to(device=device, dtype=torch.int32).contiguous()
         self.layers = int(self.layer_ptr.numel()) - 1
         if self.layers < 0:
             raise TargetError("layer_ptr must hold layers + 1 offsets")

@@ -74,7 +74,7 @@ def _time(fn, reps=20, warmup=3):
 
 @needs_ref
 def test_timing_single_launch_vs_reference_layer_loop():
-    from pbg_b200.targets import LayeredTargets, run_layers
+    from pbg_b200.targets import LayeredTargets, clear_bindings, run_layers
 
     forest = tf.Forest(17, n_replica=64, sampled=False, branched=True, reuse=True, layers=8, width_per_layer=160,
                        extra_edges=False)
@@ -82,10 +82,17 @@ def test_timing_single_launch_vs_reference_layer_loop():
     nodes = int(forest.layer_ptr[-1])
     ref_us, ref_wall = _time(lambda: REF.run_layers(*args))
     ours_us, ours_wall = _time(lambda: run_layers(*args))
+
+    def fresh():
+        clear_bindings()  # a new plan every call: the binding is rebuilt each time
+        run_layers(*args)
+
+    fresh_us, fresh_wall = _time(fresh)
     bound = LayeredTargets(*args)
     bound_us, bound_wall = _time(lambda: bound.launch())
     print(f"\nlayered targets: {nodes} nodes, {forest.layer_ptr.size - 1} layers, 64 lanes, RB branched, P=2")
     print(f"  reference run_layers   : {ref_us:9.1f} us device  {ref_wall:9.1f} us wall")
-    print(f"  pbg_b200 run_layers    : {ours_us:9.1f} us device  {ours_wall:9.1f} us wall")
+    print(f"  pbg_b200 run_layers    : {ours_us:9.1f} us device  {ours_wall:9.1f} us wall  (binding reused)")
+    print(f"  pbg_b200 run_layers    : {fresh_us:9.1f} us device  {fresh_wall:9.1f} us wall  (binding rebuilt)")
     print(f"  pbg_b200 bound launch  : {bound_us:9.1f} us device  {bound_wall:9.1f} us wall")
     assert bound_us < ref_us
