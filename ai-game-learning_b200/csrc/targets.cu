@@ -34,8 +34,11 @@
 // Nodes with more than TGT_MAX_CHILDREN target children read global memory
 // directly.
 // Layers are separated by a bounded grid barrier (the launch is cooperative,
-// so every CTA is resident and the barrier completes); a barrier wait that
-// runs out writes -2 into every lane's failure word and the kernel returns.
+// so every CTA is resident and the barrier completes); there is none before
+// the first layer or after the last.  The failure codes live in a persistent
+// workspace that every call leaves clean; the CTA that finishes last turns
+// them into failure_min.  A barrier wait that runs out makes failure_min -2
+// in every lane.
 #include <climits>
 
 #include "pbg_common.cuh"
@@ -66,9 +69,16 @@ struct TargetArgs {
     int off_part, off_value, off_tail;  // byte offsets inside a warp's staging area
     float lambda;
     bool sampled, branched;
-    int32_t* failure_min;
-    uint32_t* sync;
+    int32_t* failure_min;  // output
+    uint32_t* ws;          // persistent workspace (layout below)
 };
+
+// Workspace words (zero before the first call; every completed call leaves
+// the counters at zero again):  [0] grid-barrier arrivals, [32] barrier
+// generation, [64] CTAs finished, [65] barrier timeout flag, [96 + lane]
+// the lane's failure code (0 = none, else INT_MAX - first failing node, kept
+// with atomicMax so the smallest node wins).
+constexpr int WS_ARRIVE = 0, WS_GEN = 32, WS_DONE = 64, WS_TIMEOUT = 65, WS_FAIL = 96;
 
 __device__ __forceinline__ float* table_ptr(const int64_t* table, int index) {
     return reinterpret_cast<float*>(table[index]);
@@ -135,7 +145,7 @@ __device__ void target_node(const TargetArgs& A, const TargetPart* parts, unsign
     int32_t* epart = reinterpret_cast<int32_t*>(wsm + A.off_part) + gi * TGT_MAX_CHILDREN;
     // wave 2: lane failure word, edges, head rows
     int failed = 0;
-    if (gl == 0) failed = A.failure_min[lane] != INT_MAX;
+    if (gl == 0) failed = __ldcg(reinterpret_cast<const int32_t*>(A.ws + WS_FAIL) + lane) != 0;
     if (staged) {
         for (int a = gl; a < ntgt; a += G) {
             const int src = A.ch.source_type[begin + a];
@@ -304,7 +314,7 @@ __device__ void target_node(const TargetArgs& A, const TargetPart* parts, unsign
             if (!isfinite(trace_exec) || !isfinite(prop_cost) || !isfinite(prop_delta)) bad = true;
         }
     }
-    if (__any_sync(gmask, bad) && gl == 0) atomicMin(A.failure_min + lane, node);
+    if (__any_sync(gmask, bad) && gl == 0) atomicMax(reinterpret_cast<int32_t*>(A.ws + WS_FAIL) + lane, INT_MAX - node);
     __syncwarp(gmask);  // the staging rows are reused by the group's next node
 }
 
@@ -341,11 +351,14 @@ __device__ bool grid_barrier(uint32_t* count, uint32_t* gen, uint32_t& my_gen) {
     return ok != 0;
 }
 
-__global__ void __launch_bounds__(TGT_THREADS, 4) layered_targets_kernel(TargetArgs A) {
+// No barrier before the first layer (the failure codes are clean on entry)
+// and none after the last: the CTA that finishes last publishes failure_min
+// and clears the failure codes for the next call.
+__global__ void __launch_bounds__(TGT_THREADS, 3) layered_targets_kernel(TargetArgs A) {
     extern __shared__ __align__(16) unsigned char tgt_smem_raw[];
     __shared__ TargetPart parts[TGT_MAX_PARTS];
-    uint32_t* count = A.sync;
-    uint32_t* gen = A.sync + 1;
+    uint32_t* count = A.ws + WS_ARRIVE;
+    uint32_t* gen = A.ws + WS_GEN;
     __shared__ uint32_t my_gen_s;
     if (threadIdx.x == 0) my_gen_s = load_acquire_gpu(gen);
     for (int i = threadIdx.x; i < A.output_count; i += blockDim.x) {
@@ -359,13 +372,9 @@ __global__ void __launch_bounds__(TGT_THREADS, 4) layered_targets_kernel(TargetA
         q.width = A.t.width[i];
         parts[i] = q;
     }
-    // the lane failure words start clean; visible to all CTAs after the first barrier
-    if (blockIdx.x == 0)
-        for (int l = threadIdx.x; l < A.n_replica; l += blockDim.x) A.failure_min[l] = INT_MAX;
     __syncthreads();
-    uint32_t my_gen = my_gen_s;
-    if (!grid_barrier(count, gen, my_gen)) goto timeout;
     {
+        uint32_t my_gen = my_gen_s;
         const int G = A.group;
         const int warp_lane = threadIdx.x & 31;
         const int gl = warp_lane & (G - 1);
@@ -379,13 +388,36 @@ __global__ void __launch_bounds__(TGT_THREADS, 4) layered_targets_kernel(TargetA
             const int first = A.layer_ptr[layer], last = A.layer_ptr[layer + 1];
             for (int node = first + group_global; node < last; node += groups_total)
                 target_node(A, parts, wsm, node, (layer + 1) & 1, gl, leader, gmask);
-            if (!grid_barrier(count, gen, my_gen)) goto timeout;
+            if (layer + 1 < A.layers && !grid_barrier(count, gen, my_gen)) {
+                if (threadIdx.x == 0) atomicExch(A.ws + WS_TIMEOUT, 1u);
+                break;
+            }
         }
     }
-    return;
-timeout:
-    if (threadIdx.x == 0)
-        for (int l = 0; l < A.n_replica; ++l) atomicExch(A.failure_min + l, -2);
+    // epilogue: the last CTA to finish publishes the result and clears the codes
+    __shared__ int last_cta;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last_cta = atomicAdd(A.ws + WS_DONE, 1u) == gridDim.x - 1;
+        if (last_cta) __threadfence();
+    }
+    __syncthreads();
+    if (last_cta) {
+        // every other CTA has finished: plain accesses, spread over the CTA
+        const bool timed_out = __ldcg(A.ws + WS_TIMEOUT) != 0u;
+        int32_t* codes = reinterpret_cast<int32_t*>(A.ws + WS_FAIL);
+        for (int l = threadIdx.x; l < A.n_replica; l += blockDim.x) {
+            const int32_t code = __ldcg(codes + l);
+            A.failure_min[l] = timed_out ? -2 : (code ? INT_MAX - code : INT_MAX);
+            codes[l] = 0;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            A.ws[WS_TIMEOUT] = 0u;
+            A.ws[WS_DONE] = 0u;
+        }
+    }
 }
 
 }  // namespace pbg
@@ -395,12 +427,17 @@ using namespace pbg;
 static int align16(int x) { return (x + 15) & ~15; }
 static constexpr int TGT_SMEM_CEILING = 200 * 1024;
 
+extern "C" int64_t pbg_layered_targets_workspace_words(int32_t n_replica) {
+    return n_replica < 0 ? -1 : (int64_t)WS_FAIL + n_replica;
+}
+
 extern "C" int pbg_layered_targets(const int32_t* layer_ptr, int32_t layers, pbg_target_nodes nodes,
                                    pbg_target_children children, pbg_target_tables tables, int32_t n_replica,
                                    int32_t input_count, int32_t output_count, int32_t action_partition_count,
                                    int32_t p_train, int32_t max_width, float lambda, int32_t sampled, int32_t branched,
-                                   int32_t* failure_min, uint32_t* sync, void* stream) {
-    PBG_REQUIRE(layers >= 0 && layer_ptr && failure_min && sync && n_replica >= 1, "layered_targets: bad arguments");
+                                   int32_t* failure_min, uint32_t* workspace, void* stream) {
+    PBG_REQUIRE(layers >= 0 && layer_ptr && failure_min && workspace && n_replica >= 1,
+                "layered_targets: bad arguments");
     PBG_REQUIRE(p_train >= 1 && output_count >= 1 && input_count >= 0 && max_width >= 1,
                 "layered_targets: bad partition counts");
     PBG_REQUIRE(output_count <= TGT_MAX_PARTS, "layered_targets: at most %d output partitions", TGT_MAX_PARTS);
@@ -452,7 +489,7 @@ extern "C" int pbg_layered_targets(const int32_t* layer_ptr, int32_t layers, pbg
     A.action_partitions = action_partition_count; A.p_train = p_train; A.max_width = max_width;
     A.group = group; A.warp_bytes = warp_bytes; A.off_part = off_part; A.off_value = off_value; A.off_tail = off_tail;
     A.lambda = lambda; A.sampled = sampled != 0; A.branched = branched != 0;
-    A.failure_min = failure_min; A.sync = sync;
+    A.failure_min = failure_min; A.ws = workspace;
     void* args[] = {&A};
     return cuda_status(cudaLaunchCooperativeKernel((const void*)layered_targets_kernel, dim3(grid), dim3(TGT_THREADS),
                                                    args, (size_t)smem, as_stream(stream)),

@@ -27,7 +27,7 @@ import numpy as np
 import torch
 from torch import Tensor
 
-from ._native import NativeError, TargetChildren, TargetNodes, TargetTables, call, stream
+from ._native import NativeError, TargetChildren, TargetNodes, TargetTables, call, lib, stream
 
 INT32_MAX = 2**31 - 1
 BARRIER_TIMEOUT = -2  # failure_min value of every lane when a grid barrier wait ran out
@@ -145,10 +145,11 @@ class LayeredTargets:
             raise TargetError("layer_ptr must hold layers + 1 offsets")
         self.nodes = [t.contiguous() for t in nodes]
         self.children = [t.contiguous() for t in children]
-        # failure_min [n_replica] then the grid barrier's two words; the kernel sets failure_min itself
-        self._words = torch.zeros(n_replica + 2, dtype=torch.int32, device=device)
+        # failure_min [n_replica] (written by the kernel), then the persistent workspace (zeroed once)
+        words = int(lib().pbg_layered_targets_workspace_words(int(n_replica)))
+        self._words = torch.zeros(n_replica + words, dtype=torch.int32, device=device)
         self.failure_min = self._words[:n_replica]
-        self.sync = self._words[n_replica:]
+        self.workspace = self._words[n_replica:]
         self.shape = (int(n_replica), int(input_count), int(output_count), int(action_partition_count),
                       int(p_train), int(max_width))
         self.sampled, self.branched = bool(sampled), bool(branched)
@@ -168,22 +169,22 @@ class LayeredTargets:
 
         ``failure_out`` receives the result instead of the binding's own
         buffer (the kernel initialises it, no clearing needed).  Launches of
-        one binding must be ordered on one stream: they share the grid
-        barrier's words.
+        one binding must be ordered on one stream: they share the
+        workspace (grid-barrier words and failure codes).
         """
 
         out = self.failure_min if failure_out is None else failure_out
         if out.device != self.device or out.dtype != torch.int32 or out.numel() != self.shape[0]:
             raise TargetError("failure_out must be int32 [n_replica] on the plan's device")
         s = stream(self.device) if cuda_stream is None else ctypes.c_void_p(cuda_stream)
-        call("pbg_layered_targets", *self._args, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(self.sync.data_ptr()),
-             s)
+        call("pbg_layered_targets", *self._args, ctypes.c_void_p(out.data_ptr()),
+             ctypes.c_void_p(self.workspace.data_ptr()), s)
         return out
 
     def reset_barrier(self) -> None:
-        """Clear the grid-barrier words after a launch that reported BARRIER_TIMEOUT."""
+        """Clear the workspace after a launch that reported BARRIER_TIMEOUT."""
 
-        self.sync.zero_()
+        self.workspace.zero_()
 
 
 def run_layers(layer_ptr_cpu: Tensor, nodes: Sequence[Tensor], children: Sequence[Tensor], work0, work1, trace,

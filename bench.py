@@ -312,7 +312,8 @@ def targets_component(device, lanes=256, depth=8, branching=2, p_train=2, width=
     """Layered lambda-return targets over a seeded full binary forest (RB, branched: the widest mode).
 
     The forest is re-seeded from pristine work arenas before every pass (a device copy outside the
-    timed region); each pass is ONE cooperative launch over all layers, timed with CUDA events.
+    timed region); each pass is ONE cooperative launch over all layers, timed with CUDA events that
+    are queued behind a device-side sleep (so they bracket the kernel, not the host's launch latency).
     """
 
     import torch
@@ -324,9 +325,12 @@ def targets_component(device, lanes=256, depth=8, branching=2, p_train=2, width=
     pristine = [x.clone() for x in live]
     stream = torch.cuda.current_stream(device)
     times = []
+    # every timed launch is queued behind a device-side sleep, so the events bracket the kernel
+    # rather than the host's launch latency
     for rep in range(reps + 3):
         for dst, src in zip(live, pristine):
             dst.copy_(src)
+        torch.cuda._sleep(1_000_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         failure = bound.launch()
@@ -337,11 +341,30 @@ def targets_component(device, lanes=256, depth=8, branching=2, p_train=2, width=
     if not bool((failure == INT32_MAX).all()):
         raise RuntimeError("layered targets reported a failed lane on the synthetic forest")
     ms = sorted(times)[len(times) // 2]
+    # the fixed cost of one inter-layer grid barrier: the same launch over 1 and over 65 empty layers
+    empty = []
+    for layers in (1, 65):
+        plan = list(args)
+        plan[0] = torch.zeros(layers + 1, dtype=torch.int32)
+        hollow = LayeredTargets(*plan)
+        samples = []
+        for rep in range(13):
+            torch.cuda._sleep(1_000_000)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            hollow.launch()
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            if rep >= 3:
+                samples.append(a.elapsed_time(b))
+        empty.append(sorted(samples)[len(samples) // 2])
+    barrier_us = 1000.0 * (empty[1] - empty[0]) / 64
     peak, _ = measured_peak()
     achieved = info["algorithmic_bytes"] / (ms / 1000.0) / 1e9
     return {"workload": f"layered targets, {lanes} lanes x full binary tree of depth {depth}, "
                         f"{info['estimator']} {info['rollout']}, P={p_train}, width {width}",
             "nodes": info["nodes"], "layers": depth, "us_per_pass": 1000.0 * ms,
+            "grid_barrier_us": barrier_us, "empty_launch_us": 1000.0 * empty[0],
             "nodes_per_s": info["nodes"] / (ms / 1000.0),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "bytes_per_node": info["bytes_per_node"],

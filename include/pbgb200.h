@@ -330,18 +330,21 @@ typedef struct {
  * run_layers): lambda-returns, sigma targets and per-action advantages of
  * every topology node, layer by layer, in ONE cooperative launch.
  * layer_ptr [layers+1] (device) bounds each layer's nodes; layer l writes
- * work arena (l+1)&1.  failure_min [n_replica] (device) receives INT_MAX or
- * the first failing node of each lane, or -2 in every lane when a grid
- * barrier wait ran out (bounded wait; the kernel then returns early).
- * sync [2] (device uint32: arrival counter, generation) must hold a zero
- * counter before the call; a completed call leaves it zero again, a timed-out
- * one does not (zero it before the next call).  No reference counterpart for
- * sync: the reference's host loop launches one kernel per layer instead. */
+ * work arena (l+1)&1.  failure_min [n_replica] (device, output) receives
+ * INT_MAX or the first failing node of each lane, or -2 in every lane when a
+ * grid-barrier wait ran out (bounded wait).  At most 16 output partitions.
+ * workspace [pbg_layered_targets_workspace_words(n_replica)] (device
+ * uint32): zero before the first call; each completed call leaves it ready
+ * for the next one, a call that reported -2 does not (zero it again).
+ * Calls sharing a workspace must be ordered on one stream.  The workspace has
+ * no reference counterpart: the reference launches one kernel per layer from
+ * a host loop instead. */
+int64_t pbg_layered_targets_workspace_words(int32_t n_replica);
 int pbg_layered_targets(const int32_t *layer_ptr, int32_t layers, pbg_target_nodes nodes,
                         pbg_target_children children, pbg_target_tables tables, int32_t n_replica,
                         int32_t input_count, int32_t output_count, int32_t action_partition_count,
                         int32_t p_train, int32_t max_width, float lambda, int32_t sampled,
-                        int32_t branched, int32_t *failure_min, uint32_t *sync, void *stream);
+                        int32_t branched, int32_t *failure_min, uint32_t *workspace, void *stream);
 
 /* ---------------------------------------------------------- collective */
 

@@ -110,7 +110,8 @@ def test_bound_relaunch_leaves_barrier_clean():
         failure = bound.launch()
         torch.cuda.synchronize()
         assert (failure.cpu() == 2**31 - 1).all()
-        assert int(bound.sync[0]) == 0
+        ws = bound.workspace.cpu()
+        assert int(ws[0]) == 0 and int(ws[64]) == 0 and int(ws[65]) == 0 and not ws[96:].any()
         for k in counts:
             if ref[k] is None:
                 continue
@@ -182,3 +183,21 @@ def test_run_layers_rebinds_nothing_and_reads_live_arenas():
         for x, y in zip(ref[name], group):
             if x is not None:
                 np.testing.assert_array_equal(x, y.cpu().numpy(), err_msg=name)
+
+
+def test_failure_codes_are_cleared_for_the_next_launch():
+    from pbg_b200.targets import INT32_MAX, LayeredTargets
+
+    forest = tf.Forest(31, n_replica=3, sampled=True, branched=False, layers=3)
+    args, groups, _ = forest.device_args(DEV)
+    bound = LayeredTargets(*args)
+    lane, t, row, arena = forest.leaves[0]
+    good = groups["work0"][t][lane, row, arena].clone()
+    groups["work0"][t][lane, row, arena] = float("nan")
+    first = bound.launch().cpu().clone()
+    assert first[lane] != INT32_MAX and (first[[i for i in range(3) if i != lane]] == INT32_MAX).all()
+    groups["work0"][t][lane, row, arena] = good
+    second = bound.launch().cpu()
+    assert (second == INT32_MAX).all()
+    ws = bound.workspace.cpu()  # counters and failure codes clean; the barrier generation keeps counting
+    assert int(ws[0]) == 0 and int(ws[64]) == 0 and int(ws[65]) == 0 and not ws[96:].any()

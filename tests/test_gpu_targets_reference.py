@@ -59,17 +59,27 @@ def test_forest_matches_reference_kernel(sampled, branched, reuse):
 
 
 def _time(fn, reps=20, warmup=3):
+    """(device us, wall us) per call.  Device: each call queued behind a device-side sleep, so the
+    events bracket the GPU work of the call (its launches, and its host gaps only where the host
+    falls behind the GPU); wall: back-to-back calls, host clock."""
+
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    device = []
+    for _ in range(reps):
+        torch.cuda._sleep(2_000_000)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        stop.record()
+        torch.cuda.synchronize()
+        device.append(start.elapsed_time(stop) * 1e3)
     wall = time.perf_counter()
-    start.record()
     for _ in range(reps):
         fn()
-    stop.record()
     torch.cuda.synchronize()
-    return start.elapsed_time(stop) / reps * 1e3, (time.perf_counter() - wall) / reps * 1e6
+    return sorted(device)[reps // 2], (time.perf_counter() - wall) / reps * 1e6
 
 
 @needs_ref
