@@ -1,0 +1,393 @@
+// Dense bf16 linear layer on the 5th-generation tensor cores:
+//     y[M, N] = act(x[M, K] . w[N, K]^T + bias[N])      (bf16 in/out, fp32 accumulate)
+// the Linear / FFN / attention-projection maps of the poker model
+// (pbg/games/poker/model/primitives.py:35-60 FFN, :97-117 MHA projections,
+// pbg/core/tensor_ops.py Linear: weight [out, in], bias [out]).
+//
+// One persistent CTA per SM walks 128 x BN output tiles (BN <= 256, a
+// divisor of N).  Warp roles:
+//   warp 0  TMA producer: 128x64 x-tiles and BNx64 w-tiles (both K-major,
+//           128-byte swizzle) into a 4-stage shared-memory ring, completion
+//           counted on the stage's "full" mbarrier;
+//   warp 1  owns the tensor memory (2*BN fp32 columns: two accumulators) and
+//           one elected thread issues tcgen05.mma (M=128, N=BN, K=16, both
+//           operands from shared memory) four times per 64-wide k-block, then
+//           tcgen05.commit frees the stage ("empty") and, after the last
+//           k-block, publishes the accumulator ("acc_full");
+//   warps 2-5  epilogue: each thread owns one accumulator row (its warp's
+//           TMEM lane quadrant), loads 32 columns at a time with tcgen05.ld,
+//           adds the bias, applies GELU (erf form, torch's default) and
+//           stores bf16; then releases the accumulator ("acc_empty") so the
+//           next tile's MMAs overlap this epilogue.
+// Every wait is bounded; a wait that runs out records an error code, stops
+// the CTA's loops, waits (bounded) for its own copies and MMAs in flight,
+// frees its tensor memory and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "pbg_common.cuh"
+
+namespace pbg {
+
+constexpr int GM_BM = 128;
+constexpr int GM_BK = 64;  // one 128-byte swizzle row of bf16
+constexpr int GM_STAGES = 4;
+constexpr int GM_THREADS = 192;
+constexpr uint32_t GM_WAIT_TRIES = 1u << 26;
+
+struct GemmArgs {
+    int64_t M;
+    int N, K, BN, tiles_n;
+    int64_t tiles;
+    const float* bias;
+    __nv_bfloat16* y;
+    int act;  // 0 none, 1 gelu
+    uint32_t* error;
+};
+
+__device__ __forceinline__ uint32_t gm_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void gm_mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void gm_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void gm_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool gm_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; also gives up when another role has aborted the CTA.
+__device__ __forceinline__ bool gm_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < GM_WAIT_TRIES; ++i) {
+        if (gm_try_wait(bar, parity)) return true;
+        if ((i & 1023u) == 1023u && *abort_flag) return false;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void gm_tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// K-major operand tile, 128-byte swizzle: rows of 128 B, 8-row (1024 B) atoms.
+__device__ __forceinline__ uint64_t gm_desc(uint32_t smem_addr) {
+    const uint64_t start = (smem_addr >> 4) & 0x3FFFu;
+    const uint64_t lbo = 1;                 // unused by swizzled K-major layouts
+    const uint64_t sbo = 1024 >> 4;         // next 8-row atom
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* sm100 descriptor version */ |
+           (2ull << 61) /* SWIZZLE_128B */;
+}
+
+// kind::f16 instruction descriptor: bf16 x bf16 -> fp32, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t gm_idesc(int bn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void gm_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void gm_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void gm_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void gm_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void gm_tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ float gm_gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    linear_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                          GemmArgs G) {
+    extern __shared__ __align__(16) unsigned char gm_raw[];
+    __shared__ __align__(8) uint64_t full[GM_STAGES], empty[GM_STAGES], acc_full[2], acc_empty[2], done_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ volatile int abort_flag;
+    // 1024-byte aligned ring (the 128-byte swizzle atom)
+    const uint32_t raw = gm_smem(gm_raw);
+    const uint32_t ring = (raw + 1023u) & ~1023u;
+    const uint32_t a_bytes = GM_BM * GM_BK * 2;
+    const uint32_t b_bytes = (uint32_t)G.BN * GM_BK * 2;
+    const uint32_t stage_bytes = a_bytes + b_bytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = G.K / GM_BK;
+    const uint32_t tmem_cols = G.BN * 2 <= 32 ? 32 : (G.BN * 2 <= 64 ? 64 : (G.BN * 2 <= 128 ? 128 : (G.BN * 2 <= 256 ? 256 : 512)));
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < GM_STAGES; ++s) {
+            gm_mbar_init(gm_smem(&full[s]), 1);
+            gm_mbar_init(gm_smem(&empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            gm_mbar_init(gm_smem(&acc_full[b]), 1);
+            gm_mbar_init(gm_smem(&acc_empty[b]), 128);
+        }
+        gm_mbar_init(gm_smem(&done_bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(gm_smem(&tmem_base_s)),
+                     "r"(tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    gm_fence_before();
+    __syncthreads();
+    gm_fence_after();
+    const uint32_t tmem_base = tmem_base_s;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; ok && t < G.tiles; t += gridDim.x) {
+                const int m_blk = (int)(t / G.tiles_n), n_blk = (int)(t % G.tiles_n);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % GM_STAGES;
+                    const uint32_t phase = (it / GM_STAGES) & 1u;
+                    if (!gm_wait(gm_smem(&empty[s]), phase ^ 1u, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = ring + s * stage_bytes;
+                    gm_expect_tx(gm_smem(&full[s]), stage_bytes);
+                    gm_tma_2d(sa, &map_x, kb * GM_BK, m_blk * GM_BM, gm_smem(&full[s]));
+                    gm_tma_2d(sa + a_bytes, &map_w, kb * GM_BK, n_blk * G.BN, gm_smem(&full[s]));
+                }
+            }
+            if (!ok) {
+                atomicCAS(G.error, 0u, 1u);
+                abort_flag = 1;
+            }
+            // every stage's last copy has landed before the CTA can exit
+            const uint32_t issued = it;
+            for (uint32_t k = issued > GM_STAGES ? issued - GM_STAGES : 0; k < issued; ++k) {
+                const uint32_t s = k % GM_STAGES, phase = (k / GM_STAGES) & 1u;
+                for (uint32_t i = 0; i < GM_WAIT_TRIES && !gm_try_wait(gm_smem(&full[s]), phase); ++i) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            const uint32_t idesc = gm_idesc(G.BN);
+            uint32_t it = 0, acc_it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; ok && t < G.tiles; t += gridDim.x, ++acc_it) {
+                const uint32_t b = acc_it & 1u, aphase = (acc_it >> 1) & 1u;
+                if (!gm_wait(gm_smem(&acc_empty[b]), aphase ^ 1u, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                gm_fence_after();
+                const uint32_t d_tmem = tmem_base + b * (uint32_t)G.BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % GM_STAGES;
+                    const uint32_t phase = (it / GM_STAGES) & 1u;
+                    if (!gm_wait(gm_smem(&full[s]), phase, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    gm_fence_after();
+                    const uint32_t sa = ring + s * stage_bytes;
+#pragma unroll
+                    for (int k = 0; k < GM_BK / 16; ++k)
+                        gm_mma(d_tmem, gm_desc(sa + k * 32), gm_desc(sa + a_bytes + k * 32), idesc,
+                               (kb > 0 || k > 0) ? 1u : 0u);
+                    gm_commit(gm_smem(&empty[s]));
+                }
+                if (ok) gm_commit(gm_smem(&acc_full[b]));
+            }
+            if (!ok) {
+                atomicCAS(G.error, 0u, 2u);
+                abort_flag = 1;
+            }
+            // all MMAs this thread issued have completed before the memory is freed
+            gm_commit(gm_smem(&done_bar));
+            for (uint32_t i = 0; i < GM_WAIT_TRIES && !gm_try_wait(gm_smem(&done_bar), 0u); ++i) {
+            }
+        }
+    } else {
+        // ---------------------------------------------------------- epilogue
+        const int quad = warp & 3;  // TMEM lanes this warp may read
+        const int row_in_tile = quad * 32 + lane;
+        uint32_t acc_it = 0;
+        for (int64_t t = blockIdx.x; t < G.tiles; t += gridDim.x, ++acc_it) {
+            const int m_blk = (int)(t / G.tiles_n), n_blk = (int)(t % G.tiles_n);
+            const uint32_t b = acc_it & 1u, aphase = (acc_it >> 1) & 1u;
+            if (!gm_wait(gm_smem(&acc_full[b]), aphase, &abort_flag)) {
+                if (lane == 0) atomicCAS(G.error, 0u, 3u);
+                abort_flag = 1;
+                break;
+            }
+            gm_fence_after();
+            const int64_t row = (int64_t)m_blk * GM_BM + row_in_tile;
+            const int col0 = n_blk * G.BN;
+            for (int c = 0; c < G.BN; c += 32) {
+                float v[32];
+                gm_tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + b * (uint32_t)G.BN + (uint32_t)c, v);
+                if (row < G.M) {
+                    const float* bias = G.bias ? G.bias + col0 + c : nullptr;
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        float x0 = v[j], x1 = v[j + 1];
+                        if (bias) {
+                            x0 += bias[j];
+                            x1 += bias[j + 1];
+                        }
+                        if (G.act == 1) {
+                            x0 = gm_gelu(x0);
+                            x1 = gm_gelu(x1);
+                        }
+                        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+                        packed[j / 2] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(G.y + row * G.N + col0 + c);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+                }
+            }
+            gm_fence_before();
+            gm_arrive(gm_smem(&acc_empty[b]));
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        gm_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 K-major map: rows x K, box box_rows x 64, 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int K, int box_rows) {
+    auto fn = encode_fn();
+    PBG_REQUIRE(fn != nullptr, "linear: cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {(cuuint32_t)GM_BK, (cuuint32_t)box_rows};
+    cuuint32_t elem[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    PBG_REQUIRE(r == CUDA_SUCCESS, "linear: tensor map encoding failed (%d)", (int)r);
+    return 0;
+}
+
+}  // namespace pbg
+
+using namespace pbg;
+
+extern "C" {
+
+int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* w, const float* bias, void* y,
+                    int32_t activation, uint32_t* error, void* stream) {
+    PBG_REQUIRE(M >= 0 && N > 0 && K > 0, "linear: bad shape");
+    PBG_REQUIRE(K % GM_BK == 0, "linear: K must be a multiple of %d", GM_BK);
+    PBG_REQUIRE(N % 16 == 0, "linear: N must be a multiple of 16");
+    PBG_REQUIRE(activation == 0 || activation == 1, "linear: activation must be 0 (none) or 1 (gelu)");
+    PBG_REQUIRE(x && w && y && error, "linear: null pointer");
+    PBG_REQUIRE(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && ((uintptr_t)y % 16) == 0,
+                "linear: x, w and y must be 16-byte aligned");
+    if (M == 0) return 0;
+    // the widest tile (<= 256 columns, a multiple of 32 for the epilogue) that divides N
+    int BN = 0;
+    for (int c = 256; c >= 32; c -= 32)
+        if (N % c == 0) {
+            BN = c;
+            break;
+        }
+    PBG_REQUIRE(BN > 0, "linear: N must be a multiple of 32");
+    CUtensorMap mx, mw;
+    int rc = make_map(&mx, x, M, K, GM_BM);
+    if (rc) return rc;
+    rc = make_map(&mw, w, N, K, BN);
+    if (rc) return rc;
+    GemmArgs G;
+    G.M = M;
+    G.N = N;
+    G.K = K;
+    G.BN = BN;
+    G.tiles_n = N / BN;
+    G.tiles = ((M + GM_BM - 1) / GM_BM) * (int64_t)G.tiles_n;
+    G.bias = bias;
+    G.y = static_cast<__nv_bfloat16*>(y);
+    G.act = activation;
+    G.error = error;
+    const size_t smem = 1024 + (size_t)GM_STAGES * (GM_BM * GM_BK * 2 + (size_t)BN * GM_BK * 2);
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        rc = cuda_status(cudaFuncSetAttribute(linear_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              1024 + GM_STAGES * (GM_BM * GM_BK * 2 + 256 * GM_BK * 2)),
+                         "linear: shared memory size");
+        if (rc) return rc;
+        configured[dev] = 1;
+    }
+    const int64_t grid = G.tiles < sm_count() ? G.tiles : sm_count();
+    linear_tcgen05_kernel<<<(unsigned)grid, GM_THREADS, smem, as_stream(stream)>>>(mx, mw, G);
+    return launch_status("linear_bf16");
+}
+
+}  // extern "C"

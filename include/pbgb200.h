@@ -346,6 +346,18 @@ int pbg_layered_targets(const int32_t *layer_ptr, int32_t layers, pbg_target_nod
                         int32_t p_train, int32_t max_width, float lambda, int32_t sampled,
                         int32_t branched, int32_t *failure_min, uint32_t *workspace, void *stream);
 
+/* ------------------------------------------------------------ model GEMM */
+
+/* pbg/games/poker/model/primitives.py:35-60 (FFN), :97-117 (MHA
+ * projections) and pbg/core/tensor_ops.py Linear: y[M,N] = act(x[M,K] .
+ * w[N,K]^T + bias[N]) with bf16 x, w, y (row-major, 16-byte aligned) and
+ * fp32 bias (may be NULL), fp32 accumulation on the tensor cores (tcgen05,
+ * TMA, tensor memory).  activation: 0 none, 1 GELU (erf form).  K must be a
+ * multiple of 64 and N of 32.  error (device uint32) receives a nonzero code
+ * if a bounded pipeline wait ran out (the output is then incomplete). */
+int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *w, const float *bias, void *y,
+                    int32_t activation, uint32_t *error, void *stream);
+
 /* ---------------------------------------------------------- collective */
 
 /* replica.py:352-362 (all_reduce SUM of the flat fp32 gradient) over NVLink
