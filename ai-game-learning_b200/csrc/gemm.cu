@@ -14,11 +14,14 @@
 //           operands from shared memory) four times per 64-wide k-block, then
 //           tcgen05.commit frees the stage ("empty") and, after the last
 //           k-block, publishes the accumulator ("acc_full");
-//   warps 2-5  epilogue: each thread owns one accumulator row (its warp's
-//           TMEM lane quadrant), loads 32 columns at a time with tcgen05.ld,
-//           adds the bias, applies GELU (erf form, torch's default) and
-//           stores bf16; then releases the accumulator ("acc_empty") so the
-//           next tile's MMAs overlap this epilogue.
+//   warps 2-17 epilogue, four warps per TMEM lane quadrant, each on a quarter
+//           of the tile's columns: a thread owns one accumulator row, loads 32
+//           columns at a time with tcgen05.ld, adds the bias, applies GELU
+//           (erf form, torch's default), packs bf16 into a 64-byte-swizzled
+//           shared-memory block (conflict-free) and one lane TMA-stores the
+//           32x32 block (rows past M are clipped by the tensor map); then the
+//           warp releases the accumulator ("acc_empty") so the next tile's
+//           MMAs overlap this epilogue.
 // Every wait is bounded; a wait that runs out records an error code, stops
 // the CTA's loops, waits (bounded) for its own copies and MMAs in flight,
 // frees its tensor memory and returns.
@@ -35,7 +38,9 @@ namespace pbg {
 constexpr int GM_BM = 128;
 constexpr int GM_BK = 64;  // one 128-byte swizzle row of bf16
 constexpr int GM_STAGES = 4;
-constexpr int GM_THREADS = 192;
+constexpr int GM_EPI_WARPS = 16;  // four per TMEM lane quadrant, each on a quarter of the tile's columns
+constexpr int GM_THREADS = 64 + 32 * GM_EPI_WARPS;
+constexpr int GM_STAGE_OUT = 32 * 64;  // one warp's 32 x 32 bf16 output block (64-byte swizzled rows)
 constexpr uint32_t GM_WAIT_TRIES = 1u << 26;
 
 struct GemmArgs {
@@ -136,11 +141,28 @@ __device__ __forceinline__ void gm_tmem_ld32(uint32_t taddr, float* v) {
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ float gm_gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// erf by the rational approximation of Abramowitz & Stegun, Handbook of
+// Mathematical Functions, formula 7.1.26 (|error| <= 1.5e-7 for all x):
+//   erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),  t = 1 / (1 + p x),  x >= 0,
+// odd in x.  Far below the bf16 rounding of the layer's output; one reciprocal and one exponential
+// on the SFU instead of a branchy library erf.
+__device__ __forceinline__ float gm_erf(float x) {
+    const float ax = fabsf(x);
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
+    float poly = fmaf(1.061405429f, t, -1.453152027f);
+    poly = fmaf(poly, t, 1.421413741f);
+    poly = fmaf(poly, t, -0.284496736f);
+    poly = fmaf(poly, t, 0.254829592f);
+    const float y = fmaf(-poly * t, __expf(-ax * ax), 1.0f);
+    return copysignf(y, x);
+}
+
+// GELU, erf form (torch's default): x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float gm_gelu(float x) { return 0.5f * x * (1.0f + gm_erf(x * 0.70710678118654752f)); }
 
 __global__ void __launch_bounds__(GM_THREADS, 1)
     linear_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                          GemmArgs G) {
+                          const __grid_constant__ CUtensorMap map_y, GemmArgs G) {
     extern __shared__ __align__(16) unsigned char gm_raw[];
     __shared__ __align__(8) uint64_t full[GM_STAGES], empty[GM_STAGES], acc_full[2], acc_empty[2], done_bar;
     __shared__ uint32_t tmem_base_s;
@@ -163,7 +185,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             gm_mbar_init(gm_smem(&acc_full[b]), 1);
-            gm_mbar_init(gm_smem(&acc_empty[b]), 128);
+            gm_mbar_init(gm_smem(&acc_empty[b]), 32 * GM_EPI_WARPS);
         }
         gm_mbar_init(gm_smem(&done_bar), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -253,8 +275,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
     } else {
         // ---------------------------------------------------------- epilogue
+        const int e = warp - 2;
         const int quad = warp & 3;  // TMEM lanes this warp may read
-        const int row_in_tile = quad * 32 + lane;
+        const int part = e >> 2;    // which quarter of the tile's columns
+        const int cols = G.BN / 4;  // a multiple of 32
+        // one 2 KB output block per warp, after the operand ring
+        const uint32_t blk = ring + GM_STAGES * stage_bytes + (uint32_t)e * GM_STAGE_OUT;
         uint32_t acc_it = 0;
         for (int64_t t = blockIdx.x; t < G.tiles; t += gridDim.x, ++acc_it) {
             const int m_blk = (int)(t / G.tiles_n), n_blk = (int)(t % G.tiles_n);
@@ -265,37 +291,54 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 break;
             }
             gm_fence_after();
-            const int64_t row = (int64_t)m_blk * GM_BM + row_in_tile;
-            const int col0 = n_blk * G.BN;
-            for (int c = 0; c < G.BN; c += 32) {
+            const int col_base = n_blk * G.BN + part * cols;
+            for (int c = 0; c < cols; c += 32) {
                 float v[32];
-                gm_tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + b * (uint32_t)G.BN + (uint32_t)c, v);
-                if (row < G.M) {
-                    const float* bias = G.bias ? G.bias + col0 + c : nullptr;
-                    uint32_t packed[16];
+                gm_tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + b * (uint32_t)G.BN + (uint32_t)(part * cols + c),
+                             v);
+                const float* bias = G.bias ? G.bias + col_base + c : nullptr;
+                uint32_t packed[16];
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        float x0 = v[j], x1 = v[j + 1];
-                        if (bias) {
-                            x0 += bias[j];
-                            x1 += bias[j + 1];
-                        }
-                        if (G.act == 1) {
-                            x0 = gm_gelu(x0);
-                            x1 = gm_gelu(x1);
-                        }
-                        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-                        packed[j / 2] = *reinterpret_cast<uint32_t*>(&h);
+                for (int j = 0; j < 32; j += 2) {
+                    float x0 = v[j], x1 = v[j + 1];
+                    if (bias) {
+                        x0 += bias[j];
+                        x1 += bias[j + 1];
                     }
-                    uint4* dst = reinterpret_cast<uint4*>(G.y + row * G.N + col0 + c);
+                    if (G.act == 1) {
+                        x0 = gm_gelu(x0);
+                        x1 = gm_gelu(x1);
+                    }
+                    __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+                    packed[j / 2] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                // the previous TMA store has finished reading the block
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
+                // row `lane`: 64 bytes = four 16-byte chunks, chunk j at position j ^ ((row >> 1) & 3)
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t addr = blk + (uint32_t)lane * 64u + (uint32_t)((q ^ ((lane >> 1) & 3)) * 16);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[4 * q]),
+                                 "r"(packed[4 * q + 1]), "r"(packed[4 * q + 2]), "r"(packed[4 * q + 3])
+                                 : "memory");
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    const int x = col_base + c, y = m_blk * GM_BM + quad * 32;
+                    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                                 ::"l"(reinterpret_cast<uint64_t>(&map_y)), "r"(x), "r"(y), "r"(blk)
+                                 : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
             gm_fence_before();
             gm_arrive(gm_smem(&acc_empty[b]));
         }
+        // the output blocks must be read out before the CTA's shared memory is released
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
     __syncthreads();
     if (warp == 1) {
@@ -319,16 +362,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D bf16 K-major map: rows x K, box box_rows x 64, 128-byte swizzle.
-static int make_map(CUtensorMap* map, const void* base, int64_t rows, int K, int box_rows) {
+// 2-D bf16 row-major map: rows x cols (cols contiguous), box box_rows x box_cols.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int cols, int box_rows, int box_cols,
+                    CUtensorMapSwizzle swizzle) {
     auto fn = encode_fn();
     PBG_REQUIRE(fn != nullptr, "linear: cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    cuuint32_t box[2] = {(cuuint32_t)GM_BK, (cuuint32_t)box_rows};
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t elem[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     PBG_REQUIRE(r == CUDA_SUCCESS, "linear: tensor map encoding failed (%d)", (int)r);
     return 0;
@@ -344,24 +388,26 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* 
                     int32_t activation, uint32_t* error, void* stream) {
     PBG_REQUIRE(M >= 0 && N > 0 && K > 0, "linear: bad shape");
     PBG_REQUIRE(K % GM_BK == 0, "linear: K must be a multiple of %d", GM_BK);
-    PBG_REQUIRE(N % 16 == 0, "linear: N must be a multiple of 16");
+    PBG_REQUIRE(N % 128 == 0, "linear: N must be a multiple of 128");
     PBG_REQUIRE(activation == 0 || activation == 1, "linear: activation must be 0 (none) or 1 (gelu)");
     PBG_REQUIRE(x && w && y && error, "linear: null pointer");
     PBG_REQUIRE(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && ((uintptr_t)y % 16) == 0,
                 "linear: x, w and y must be 16-byte aligned");
     if (M == 0) return 0;
-    // the widest tile (<= 256 columns, a multiple of 32 for the epilogue) that divides N
+    // the widest tile (<= 256 columns, a multiple of 128: four epilogue quarters of 32-column blocks) dividing N
     int BN = 0;
-    for (int c = 256; c >= 32; c -= 32)
+    for (int c = 256; c >= 128; c -= 128)
         if (N % c == 0) {
             BN = c;
             break;
         }
-    PBG_REQUIRE(BN > 0, "linear: N must be a multiple of 32");
-    CUtensorMap mx, mw;
-    int rc = make_map(&mx, x, M, K, GM_BM);
+    PBG_REQUIRE(BN > 0, "linear: N must be a multiple of 128");
+    CUtensorMap mx, mw, my;
+    int rc = make_map(&mx, x, M, K, GM_BM, GM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    rc = make_map(&mw, w, N, K, BN);
+    rc = make_map(&mw, w, N, K, BN, GM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_map(&my, y, M, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
     GemmArgs G;
     G.M = M;
@@ -374,19 +420,21 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* 
     G.y = static_cast<__nv_bfloat16*>(y);
     G.act = activation;
     G.error = error;
-    const size_t smem = 1024 + (size_t)GM_STAGES * (GM_BM * GM_BK * 2 + (size_t)BN * GM_BK * 2);
+    const size_t smem = 1024 + (size_t)GM_STAGES * (GM_BM * GM_BK * 2 + (size_t)BN * GM_BK * 2) +
+                        (size_t)GM_EPI_WARPS * GM_STAGE_OUT;
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
         rc = cuda_status(cudaFuncSetAttribute(linear_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              1024 + GM_STAGES * (GM_BM * GM_BK * 2 + 256 * GM_BK * 2)),
+                                              1024 + GM_STAGES * (GM_BM * GM_BK * 2 + 256 * GM_BK * 2) +
+                                                  GM_EPI_WARPS * GM_STAGE_OUT),
                          "linear: shared memory size");
         if (rc) return rc;
         configured[dev] = 1;
     }
     const int64_t grid = G.tiles < sm_count() ? G.tiles : sm_count();
-    linear_tcgen05_kernel<<<(unsigned)grid, GM_THREADS, smem, as_stream(stream)>>>(mx, mw, G);
+    linear_tcgen05_kernel<<<(unsigned)grid, GM_THREADS, smem, as_stream(stream)>>>(mx, mw, my, G);
     return launch_status("linear_bf16");
 }
 

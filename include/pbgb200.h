@@ -353,7 +353,7 @@ int pbg_layered_targets(const int32_t *layer_ptr, int32_t layers, pbg_target_nod
  * w[N,K]^T + bias[N]) with bf16 x, w, y (row-major, 16-byte aligned) and
  * fp32 bias (may be NULL), fp32 accumulation on the tensor cores (tcgen05,
  * TMA, tensor memory).  activation: 0 none, 1 GELU (erf form).  K must be a
- * multiple of 64 and N of 32.  error (device uint32) receives a nonzero code
+ * multiple of 64 and N of 128.  error (device uint32) receives a nonzero code
  * if a bounded pipeline wait ran out (the output is then incomplete). */
 int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *w, const float *bias, void *y,
                     int32_t activation, uint32_t *error, void *stream);

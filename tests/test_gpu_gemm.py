@@ -22,13 +22,14 @@ def _ref(x, w, b, act):
 
 
 @pytest.mark.parametrize("m,k,n,act,bias", [
-    (128, 64, 64, None, True),
+    (128, 64, 128, None, True),
     (1000, 256, 768, None, True),      # M tail, three 256-wide column tiles
     (777, 256, 1024, "gelu", True),    # FFN w1 shape
     (4096, 1024, 256, None, True),     # FFN w2 shape
-    (300, 128, 96, None, False),       # 96-wide tile, no bias
-    (5000, 512, 160, "gelu", True),    # 160-wide tile
-    (1, 64, 32, "gelu", True),         # one row
+    (300, 128, 384, None, False),      # 128-wide tiles, no bias
+    (5000, 512, 640, "gelu", True),    # 128-wide tiles
+    (1, 64, 128, "gelu", True),        # one row
+    (33, 256, 128, "gelu", True),      # rows past M in the first 32-row block
 ])
 def test_linear_matches_fp32_reference(m, k, n, act, bias):
     from pbg_b200.model import linear, pipeline_error
@@ -67,6 +68,26 @@ def test_linear_rejects_unsupported_shapes():
     x = torch.zeros((8, 100), dtype=torch.bfloat16, device=DEV)
     w = torch.zeros((64, 100), dtype=torch.bfloat16, device=DEV)
     with pytest.raises(NativeError):
-        linear(x, w)
+        linear(x, w)  # K not a multiple of 64
+    with pytest.raises(NativeError):
+        linear(torch.zeros((8, 64), dtype=torch.bfloat16, device=DEV),
+               torch.zeros((192, 64), dtype=torch.bfloat16, device=DEV))  # N not a multiple of 128
     with pytest.raises(NativeError):
         linear(x.float(), w)
+
+
+def test_gelu_epilogue_matches_torch_gelu_to_bf16_rounding():
+    # identity weights: the layer evaluates GELU(x + b) directly; the epilogue's erf
+    # (Abramowitz & Stegun 7.1.26, |error| <= 1.5e-7) may only flip a bf16 rounding
+    from pbg_b200.model import linear
+
+    n = 128
+    x = torch.linspace(-8, 8, 4096 * n, device=DEV).reshape(4096, n).to(torch.bfloat16)
+    w = torch.eye(n, device=DEV, dtype=torch.bfloat16)
+    b = torch.zeros(n, device=DEV)
+    y = linear(x, w, b, "gelu").float()
+    ref = torch.nn.functional.gelu(x.float())
+    ulp = ref.abs().clamp_min(1e-30) * 2.0 ** -8
+    assert bool(((y - ref).abs() <= ulp + 1e-6).all())
+    flips = (y != ref.to(torch.bfloat16).float()).float().mean().item()
+    assert flips < 0.01
