@@ -157,8 +157,29 @@ __device__ __forceinline__ float gm_erf(float x) {
     return copysignf(y, x);
 }
 
-// GELU, erf form (torch's default): x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)).
+// GELU, erf form (torch's default): x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)).  The erf error above
+// is absolute: relative to the output it stays below 1e-4 for x >= -3; further out the output is
+// below 1e-5 in magnitude and the deviation below 1e-6.
 __device__ __forceinline__ float gm_gelu(float x) { return 0.5f * x * (1.0f + gm_erf(x * 0.70710678118654752f)); }
+
+// bias + activation + bf16 packing of one thread's 32 accumulator columns
+template <int ACT>
+__device__ __forceinline__ void gm_convert(const float* v, const float* bias, uint32_t* packed) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        float x0 = v[j], x1 = v[j + 1];
+        if (bias) {
+            x0 += bias[j];
+            x1 += bias[j + 1];
+        }
+        if (ACT == 1) {
+            x0 = gm_gelu(x0);
+            x1 = gm_gelu(x1);
+        }
+        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        packed[j / 2] = *reinterpret_cast<uint32_t*>(&h);
+    }
+}
 
 __global__ void __launch_bounds__(GM_THREADS, 1)
     linear_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
@@ -298,20 +319,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                              v);
                 const float* bias = G.bias ? G.bias + col_base + c : nullptr;
                 uint32_t packed[16];
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    float x0 = v[j], x1 = v[j + 1];
-                    if (bias) {
-                        x0 += bias[j];
-                        x1 += bias[j + 1];
-                    }
-                    if (G.act == 1) {
-                        x0 = gm_gelu(x0);
-                        x1 = gm_gelu(x1);
-                    }
-                    __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-                    packed[j / 2] = *reinterpret_cast<uint32_t*>(&h);
-                }
+                if (G.act == 1) gm_convert<1>(v, bias, packed);
+                else gm_convert<0>(v, bias, packed);
                 // the previous TMA store has finished reading the block
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                 __syncwarp();

@@ -372,6 +372,52 @@ def targets_component(device, lanes=256, depth=8, branching=2, p_train=2, width=
             "gpu_launches": 1}
 
 
+def model_linear_component(device, rows=524_288, reps=10):
+    """The model's dense maps on the tensor cores (pbg_linear_bf16) at d_model 256, hidden 1024:
+    attention in-projection (256 -> 768), FFN w1 with fused GELU (256 -> 1024), FFN w2 (1024 -> 256),
+    over `rows` token rows (about 600 preflop sequences of cfg2's 876 tokens).  Each launch is queued
+    behind a device-side sleep; inputs are larger than L2."""
+
+    import torch
+    from pbg_b200.model import linear, pipeline_error
+
+    _, peak_kind = measured_peak()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops_peak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        tflops_peak = 1590.0
+    g = torch.Generator(device=device).manual_seed(11)
+    out = {}
+    for name, k, n, act in (("w_qkv", 256, 768, None), ("ffn_w1_gelu", 256, 1024, "gelu"),
+                            ("ffn_w2", 1024, 256, None)):
+        x = (torch.randn((rows, k), generator=g, device=device) / 2).to(torch.bfloat16)
+        w = (torch.randn((n, k), generator=g, device=device) / k ** 0.5).to(torch.bfloat16)
+        b = torch.randn((n,), generator=g, device=device) * 0.1
+        y = torch.empty((rows, n), dtype=torch.bfloat16, device=device)
+        times = []
+        for rep in range(reps + 3):
+            torch.cuda._sleep(1_000_000)
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            linear(x, w, b, act, out=y)
+            e.record()
+            torch.cuda.synchronize(device)
+            if rep >= 3:
+                times.append(a.elapsed_time(e))
+        if pipeline_error(device):
+            raise RuntimeError("linear layer pipeline wait ran out")
+        ms = sorted(times)[len(times) // 2]
+        flops = 2.0 * rows * n * k
+        nbytes = 2.0 * (rows * k + n * k + rows * n) + 4.0 * n
+        out[name] = {"m": rows, "k": k, "n": n, "us": 1000.0 * ms, "tflops": flops / ms / 1e9,
+                     "frac_tensor": flops / ms / 1e9 / tflops_peak, "gbs": nbytes / ms / 1e6}
+        del x, w, y
+    return {"workload": f"tcgen05 linear layers over {rows} bf16 token rows (d_model 256, hidden 1024)",
+            "layers": out, "peak_tflops": tflops_peak, "peak_kind": peak_kind, "kernel": "linear_tcgen05_kernel",
+            "gpu_launches": 3}
+
+
 # ----------------------------------------------------------- device arm
 
 
@@ -569,7 +615,8 @@ def main():
     }
     if rank == 0:
         line["components"] = {"rollout_step": rollout_component(device),
-                              "layered_targets": targets_component(device)}
+                              "layered_targets": targets_component(device),
+                              "model_linear": model_linear_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:

@@ -78,7 +78,8 @@ def test_linear_rejects_unsupported_shapes():
 
 def test_gelu_epilogue_matches_torch_gelu_to_bf16_rounding():
     # identity weights: the layer evaluates GELU(x + b) directly; the epilogue's erf
-    # (Abramowitz & Stegun 7.1.26, |error| <= 1.5e-7) may only flip a bf16 rounding
+    # (Abramowitz & Stegun 7.1.26, |error| <= 1.5e-7) stays within one bf16 ulp (plus 1e-6
+    # absolute in the far negative tail, where GELU itself is below 1e-5)
     from pbg_b200.model import linear
 
     n = 128
@@ -89,5 +90,7 @@ def test_gelu_epilogue_matches_torch_gelu_to_bf16_rounding():
     ref = torch.nn.functional.gelu(x.float())
     ulp = ref.abs().clamp_min(1e-30) * 2.0 ** -8
     assert bool(((y - ref).abs() <= ulp + 1e-6).all())
-    flips = (y != ref.to(torch.bfloat16).float()).float().mean().item()
+    # a bf16 rounding may only flip where the erf's absolute error is relatively small
+    body = ref.abs() >= 1e-2
+    flips = (y[body] != ref[body].to(torch.bfloat16).float()).float().mean().item()
     assert flips < 0.01
