@@ -1,0 +1,204 @@
+// Collision-conditioned posterior profiles for branched Rao-Blackwell poker
+// (pbg/games/poker/queued/rb_sampling.py:86-223, sample_children).
+//
+// Two launches:
+//   posterior_cdf_kernel     one warp per (parent, seat): board-conflicting
+//                            private hands weigh 0; the seat's CDF over its
+//                            H hands and its mass, accumulated in double and
+//                            rounded to fp32 per entry (torch's CPU cumsum);
+//                            a warp-wide double scan per 32-hand chunk.
+//   posterior_sample_kernel  one warp per child row, lanes = attempts: each
+//                            lane draws every seat's hand for its attempt
+//                            (POSTERIOR key at draw = attempt, lane = seat;
+//                            target = min(u*mass, nextafter(mass, 0)); the
+//                            first CDF entry strictly above it by an 11-step
+//                            bisection) and tests the seats' cards for a
+//                            collision; a ballot picks the first accepted
+//                            attempt of the round, rounds of 32 run until one
+//                            succeeds or max_attempts is spent.
+// The reference evaluates the whole attempt envelope and takes the first
+// success; stopping at the first successful round gives the same profile,
+// attempt count and exhaustion flag.  A fresh row whose seat has no
+// board-legal mass (the reference's device assert) keeps the inherited
+// profile and sets *status = 1 for the host to raise.
+#include <climits>
+
+#include "pbg_common.cuh"
+
+namespace pbg {
+
+__device__ __forceinline__ double warp_scan_double(double v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    return v;
+}
+
+__global__ void posterior_cdf_kernel(Geo g, int64_t parents, const float* __restrict__ weights,
+                                     const uint8_t* __restrict__ board, float* __restrict__ cdf,
+                                     float* __restrict__ mass) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (warp >= parents * g.P) return;
+    const int64_t b = warp / g.P;
+    int shown[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) shown[k] = board[b * 5 + k];
+    const float* w = weights + warp * g.H;
+    float* c = cdf + warp * g.H;
+    double carry = 0.0;
+    for (int h0 = 0; h0 < g.H; h0 += 32) {
+        const int h = h0 + lane;
+        double v = 0.0;
+        if (h < g.H) {
+            int c0, c1;
+            combo_cards(g.D, g.first, h, c0, c1);
+            bool blocked = false;
+#pragma unroll
+            for (int k = 0; k < 5; ++k) blocked |= shown[k] != 255 && (shown[k] == c0 || shown[k] == c1);
+            v = blocked ? 0.0 : (double)w[h];
+        }
+        v = warp_scan_double(v, lane) + carry;
+        if (h < g.H) c[h] = (float)v;
+        carry = __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) mass[warp] = (float)carry;
+}
+
+__global__ void posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const float* __restrict__ cdf,
+                                        const float* __restrict__ mass, const int32_t* __restrict__ inherited,
+                                        const int64_t* __restrict__ source, const int64_t* __restrict__ ordinal,
+                                        const uint8_t* __restrict__ active, const int64_t* __restrict__ root,
+                                        const int64_t* __restrict__ path, const int64_t* __restrict__ epoch,
+                                        int64_t epoch_scalar, int max_attempts, int32_t* __restrict__ out,
+                                        int32_t* __restrict__ attempt_count, uint8_t* __restrict__ exhausted,
+                                        unsigned long long* __restrict__ min_failing, uint32_t* __restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (r >= rows) return;
+    const int P = g.P, H = g.H;
+    const int64_t src = source[r];
+    const bool fresh = active[r] && ordinal[r] > 0;
+    int32_t result = lane < P ? inherited[src * P + lane] : 0;
+    int count = 0;
+    bool spent = false;
+    if (fresh) {
+        bool legal = true;
+        for (int p = 0; p < P; ++p) legal &= mass[src * P + p] > 0.0f;
+        if (!legal) {
+            if (lane == 0) atomicOr(status, 1u);
+        } else {
+            const int64_t rt = root[r], pt = path[r];
+            const int64_t ep = epoch ? epoch[r] : epoch_scalar;
+            int accepted = -1;
+            int32_t mine[MAXP];
+            for (int base = 0; base < max_attempts && accepted < 0; base += 32) {
+                const int a = base + lane;
+                bool ok = a < max_attempts;
+                int cards[2 * MAXP];
+                for (int p = 0; p < P; ++p) {
+                    const float total = mass[src * P + p];
+                    const float* c = cdf + (src * P + p) * (int64_t)H;
+                    float target = __fmul_rn(key_uniform(rng_key(ns, rt, pt, a, p, ep)), total);
+                    const float cap = __int_as_float(__float_as_int(total) - 1);  // nextafter(total, 0), total > 0
+                    target = cap < target ? cap : target;
+                    int lo = 0, hi = H;
+#pragma unroll
+                    for (int step = 0; step < 11; ++step) {
+                        const int mid = (lo + hi) >> 1;
+                        const int safe = mid < H - 1 ? mid : H - 1;
+                        const bool below = mid < H && c[safe] <= target;
+                        lo = below ? mid + 1 : lo;
+                        hi = below ? hi : mid;
+                    }
+                    mine[p] = lo < H - 1 ? lo : H - 1;
+                    combo_cards(g.D, g.first, mine[p], cards[2 * p], cards[2 * p + 1]);
+                }
+                for (int i = 0; i < 2 * P && ok; ++i)
+                    for (int j = (i | 1) + 1; j < 2 * P; ++j) ok &= cards[i] != cards[j];
+                const unsigned hit = __ballot_sync(0xffffffffu, ok);
+                if (hit) {
+                    const int winner = __ffs(hit) - 1;
+                    accepted = base + winner;
+                    for (int p = 0; p < P; ++p) {
+                        const int32_t v = __shfl_sync(0xffffffffu, mine[p], winner);
+                        if (lane == p) result = v;
+                    }
+                }
+            }
+            if (accepted >= 0) {
+                count = accepted + 1;
+            } else {
+                count = max_attempts;
+                spent = true;
+                if (lane == 0) atomicMin(min_failing, (unsigned long long)(pt ^ INT64_MIN));
+            }
+        }
+    }
+    if (lane < P) out[r * P + lane] = result;
+    if (lane == 0) {
+        attempt_count[r] = count;
+        exhausted[r] = spent ? 1 : 0;
+    }
+}
+
+// min_failing is kept as an order-preserving unsigned image (x ^ sign bit) so
+// an unsigned atomicMin orders signed paths; this pass turns it back.
+__global__ void posterior_finish_kernel(unsigned long long* min_failing) {
+    *min_failing = *min_failing ^ (unsigned long long)INT64_MIN;
+}
+
+__global__ void posterior_init_kernel(unsigned long long* min_failing) {
+    *min_failing = (unsigned long long)INT64_MAX ^ (unsigned long long)INT64_MIN;
+}
+
+}  // namespace pbg
+
+using namespace pbg;
+
+extern "C" {
+
+int64_t pbg_posterior_workspace_floats(pbg_geometry geometry, int64_t parents) {
+    if (check_geometry(geometry) || parents < 0) return -1;
+    const Geo g = derive(geometry);
+    return parents * g.P * (int64_t)(g.H + 1);
+}
+
+int pbg_posterior_sample_children(pbg_geometry geometry, int64_t parents, const float* range_weights,
+                                  const uint8_t* board, const int32_t* inherited, int64_t rows, const int64_t* source,
+                                  const int64_t* ordinal, const uint8_t* active, const int64_t* root,
+                                  const int64_t* path, int64_t seed, int64_t iteration, const int64_t* retry_epoch,
+                                  int64_t retry_epoch_scalar, int32_t max_attempts, float* workspace,
+                                  int32_t* profile, int32_t* attempt_count, uint8_t* exhausted, int64_t* min_failing,
+                                  uint32_t* status, void* stream) {
+    int rc = check_geometry(geometry);
+    if (rc) return rc;
+    const Geo g = derive(geometry);
+    PBG_REQUIRE(parents >= 1 && rows >= 0 && max_attempts >= 1, "posterior: bad sizes");
+    PBG_REQUIRE(g.H <= 2047, "posterior: the 11-step search covers at most 2047 private hands");
+    PBG_REQUIRE(range_weights && board && inherited && workspace && min_failing && status,
+                "posterior: null pointer");
+    PBG_REQUIRE(rows == 0 || (source && ordinal && active && root && path && profile && attempt_count && exhausted),
+                "posterior: null row column");
+    cudaStream_t s = as_stream(stream);
+    float* cdf = workspace;
+    float* mass = workspace + parents * g.P * (int64_t)g.H;
+    unsigned long long* mf = reinterpret_cast<unsigned long long*>(min_failing);
+    posterior_init_kernel<<<1, 1, 0, s>>>(mf);
+    const int64_t cdf_threads = parents * g.P * 32;
+    posterior_cdf_kernel<<<(unsigned)((cdf_threads + 255) / 256), 256, 0, s>>>(g, parents, range_weights, board, cdf,
+                                                                                mass);
+    if (rows > 0) {
+        const uint64_t ns = rng_namespace(seed, iteration, POSTERIOR);
+        const int64_t threads = rows * 32;
+        posterior_sample_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(
+            g, ns, rows, cdf, mass, inherited, source, ordinal, active, root, path, retry_epoch, retry_epoch_scalar,
+            max_attempts, profile, attempt_count, exhausted, mf, status);
+    }
+    posterior_finish_kernel<<<1, 1, 0, s>>>(mf);
+    return launch_status("posterior_sample_children");
+}
+
+}  // extern "C"

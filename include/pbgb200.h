@@ -293,6 +293,30 @@ int pbg_adam_step(int64_t n, float *master, float *grad, float *first, float *se
                   const float *controls, int64_t *step, int32_t decoupled, double *partials,
                   double *report, void *stream);
 
+/* ------------------------------------------- collision-conditioned sampler */
+
+/* Workspace (device floats) for pbg_posterior_sample_children: the parents'
+ * per-seat CDFs and masses, parents * players * (private_hands + 1). */
+int64_t pbg_posterior_workspace_floats(pbg_geometry geometry, int64_t parents);
+
+/* pbg/games/poker/queued/rb_sampling.py:86-223 (CollisionConditionedProfile
+ * Sampler.sample_children): one generating profile per child row.
+ * range_weights f32 [parents, P, H], board u8 [parents, 5], inherited i32
+ * [parents, P]; per row: source, ordinal, root, path (int64), active (u8);
+ * retry_epoch int64 [rows] or NULL (then retry_epoch_scalar).  Outputs:
+ * profile i32 [rows, P], attempt_count i32 [rows], exhausted u8 [rows],
+ * min_failing int64 [1] (smallest path of an exhausted row, INT64_MAX if
+ * none).  *status (device, caller-zeroed) becomes 1 when a fresh row's seat
+ * has no board-legal mass (the reference's device assert; here the row keeps
+ * its inherited profile and the host raises). */
+int pbg_posterior_sample_children(pbg_geometry geometry, int64_t parents, const float *range_weights,
+                                  const uint8_t *board, const int32_t *inherited, int64_t rows,
+                                  const int64_t *source, const int64_t *ordinal, const uint8_t *active,
+                                  const int64_t *root, const int64_t *path, int64_t seed, int64_t iteration,
+                                  const int64_t *retry_epoch, int64_t retry_epoch_scalar, int32_t max_attempts,
+                                  float *workspace, int32_t *profile, int32_t *attempt_count, uint8_t *exhausted,
+                                  int64_t *min_failing, uint32_t *status, void *stream);
+
 /* ------------------------------------------------------- layered targets */
 
 /* Device tables of per-partition arena pointers (int64 device addresses, 0 =

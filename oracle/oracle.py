@@ -102,6 +102,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_policy_probabilities": (None, [_I64, _I32, _I32, _I64, _P, _P, _P, _P, _P, _P, _P]),
         "orc_ppo_categorical": (None, [_I64, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
         "orc_adam": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P]),
+        "orc_posterior_sample": (None, [Geom, _I64, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32,
+                                        _P, _P, _P, _P, _P]),
         "orc_layered_targets": (None, [_P, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32,
                                        _I32, _I32, _I32, ctypes.c_float, _I32, _I32, _P]),
     }
@@ -631,3 +633,29 @@ def layered_targets(layer_ptr, nodes, children, arenas: dict, conversion, work_c
                               input_count, output_count, action_partitions, p_train, int(max(width)),
                               float(lam), int(sampled), int(branched), _ptr(failure))
     return failure
+
+
+def posterior_sample(geometry_tuple, weights, board, inherited, source, ordinal, active, root, path, seed,
+                     iteration, epoch, max_attempts):
+    """rb_sampling.py:86-223 on host arrays.  Returns (profile [G,P] int32, attempt_count [G] int32,
+    exhausted [G] bool, minimum failing path, per-row margin [G])."""
+
+    players, stack, ranks = geometry_tuple
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    B = w.shape[0]
+    G = len(source)
+    bd = np.ascontiguousarray(board, dtype=np.uint8)
+    inh = np.ascontiguousarray(inherited, dtype=np.int32)
+    cols = [np.ascontiguousarray(x, dtype=np.int64) for x in (source, ordinal, root, path)]
+    act = np.ascontiguousarray(active, dtype=np.uint8)
+    ep = np.ascontiguousarray(np.broadcast_to(np.asarray(epoch, dtype=np.int64), (G,)))
+    out = np.zeros((G, int(players)), dtype=np.int32)
+    count = np.zeros(G, dtype=np.int32)
+    exh = np.zeros(G, dtype=np.uint8)
+    worst = np.zeros(1, dtype=np.int64)
+    margin = np.zeros(G, dtype=np.float64)
+    lib().orc_posterior_sample(Geom(int(players), float(stack), int(ranks)), B, _ptr(w), _ptr(bd), _ptr(inh), G,
+                               _ptr(cols[0]), _ptr(cols[1]), _ptr(act), _ptr(cols[2]), _ptr(cols[3]), int(seed),
+                               int(iteration), _ptr(ep), int(max_attempts), _ptr(out), _ptr(count), _ptr(exh),
+                               _ptr(worst), _ptr(margin))
+    return out, count, exh.astype(bool), int(worst[0]), margin

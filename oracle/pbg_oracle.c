@@ -1098,3 +1098,115 @@ void orc_layered_targets(const int32_t *layer_ptr, int32_t layers, const int32_t
         }
     }
 }
+
+/* --------------------------------------------- collision-conditioned sampler */
+
+/*
+ * pbg/games/poker/queued/rb_sampling.py:86-223
+ * (CollisionConditionedProfileSampler.sample_children).  Per parent and seat:
+ * board-conflicting private hands get weight 0; the seat's mass and CDF are
+ * prefix sums accumulated in double and rounded to fp32 per entry (torch's
+ * CPU cumsum).  Per fresh child row (active and ordinal > 0): for attempts
+ * a = 0..max_attempts-1, every seat draws a POSTERIOR key at (root, path,
+ * draw a, lane seat, retry epoch), target = min(u*mass, nextafter(mass, 0)),
+ * and takes the first CDF entry strictly above the target (an 11-step fixed
+ * bisection, rb_sampling.py:31-55); the first attempt whose seats' hands
+ * share no card wins.  Other rows, and rows whose attempts all collide, keep
+ * the parent's inherited profile.  `margin` (optional, per row) receives the
+ * smallest distance from a target to a bounding CDF edge over the attempts
+ * up to the accepted one, divided by the seat mass: where it is tiny another
+ * summation order may pick a neighbouring hand.
+ */
+void orc_posterior_sample(orc_geom g, int64_t B, const float *weights, const uint8_t *board,
+                          const int32_t *inherited, int64_t G, const int64_t *source, const int64_t *ordinal,
+                          const uint8_t *active, const int64_t *root, const int64_t *path, int64_t seed,
+                          int64_t iteration, const int64_t *epoch, int32_t max_attempts, int32_t *out,
+                          int32_t *attempt_count, uint8_t *exhausted, int64_t *min_failing, double *margin) {
+    const int P = g.players, D = 4 * g.rank_count, first = 52 - D, H = D * (D - 1) / 2;
+    int *c0 = (int *)malloc(sizeof(int) * H), *c1 = (int *)malloc(sizeof(int) * H);
+    for (int i = 0, id = 0; i < D; ++i)
+        for (int j = i + 1; j < D; ++j, ++id) {
+            c0[id] = i + first;
+            c1[id] = j + first;
+        }
+    float *cdf = (float *)malloc(sizeof(float) * (size_t)B * P * H);
+    float *mass = (float *)malloc(sizeof(float) * (size_t)B * P);
+    for (int64_t b = 0; b < B; ++b) {
+        for (int p = 0; p < P; ++p) {
+            double run = 0.0;
+            const float *w = weights + ((size_t)b * P + p) * H;
+            float *c = cdf + ((size_t)b * P + p) * H;
+            for (int h = 0; h < H; ++h) {
+                int blocked = 0;
+                for (int k = 0; k < 5; ++k) {
+                    int card = board[b * 5 + k];
+                    if (card != 255 && (card == c0[h] || card == c1[h])) blocked = 1;
+                }
+                run += blocked ? 0.0 : (double)w[h];
+                c[h] = (float)run;
+            }
+            mass[(size_t)b * P + p] = (float)run;
+        }
+    }
+    uint64_t ns = rng_namespace(seed, iteration, 3 /* POSTERIOR */);
+    int64_t worst = INT64_MAX;
+    int32_t *sel = (int32_t *)malloc(sizeof(int32_t) * P);
+    for (int64_t r = 0; r < G; ++r) {
+        const int64_t src = source[r];
+        const int fresh = active[r] && ordinal[r] > 0;
+        double row_margin = 1.0;
+        attempt_count[r] = 0;
+        exhausted[r] = 0;
+        for (int p = 0; p < P; ++p) out[r * P + p] = inherited[src * P + p];
+        if (fresh) {
+            int accepted = -1;
+            for (int a = 0; a < max_attempts && accepted < 0; ++a) {
+                for (int p = 0; p < P; ++p) {
+                    const float total = mass[(size_t)src * P + p];
+                    const float *c = cdf + ((size_t)src * P + p) * H;
+                    float target = uniform_of(rng_key(ns, root[r], path[r], a, p, epoch[r])) * total;
+                    const float cap = nextafterf(total, 0.0f);
+                    if (cap < target) target = cap;
+                    int lo = 0, hi = H;
+                    for (int step = 0; step < 11; ++step) {
+                        int mid = (lo + hi) >> 1;
+                        int safe = mid < H - 1 ? mid : H - 1;
+                        int below = mid < H && c[safe] <= target;
+                        if (below) lo = mid + 1;
+                        else hi = mid;
+                    }
+                    sel[p] = lo < H - 1 ? lo : H - 1;
+                    if (margin && total > 0.0f) {
+                        double up = (double)c[sel[p]] - target;
+                        double down = sel[p] > 0 ? (double)target - c[sel[p] - 1] : (double)target;
+                        double m = (up < down ? up : down) / total;
+                        if (m < 0) m = -m;
+                        if (m < row_margin) row_margin = m;
+                    }
+                }
+                int clash = 0;
+                for (int p = 0; p < P && !clash; ++p)
+                    for (int q = p + 1; q < P && !clash; ++q)
+                        if (c0[sel[p]] == c0[sel[q]] || c0[sel[p]] == c1[sel[q]] || c1[sel[p]] == c0[sel[q]] ||
+                            c1[sel[p]] == c1[sel[q]])
+                            clash = 1;
+                if (!clash) accepted = a;
+            }
+            if (accepted >= 0) {
+                for (int p = 0; p < P; ++p) out[r * P + p] = sel[p];
+                attempt_count[r] = accepted + 1;
+            } else {
+                exhausted[r] = 1;
+                attempt_count[r] = max_attempts;
+                if (path[r] < worst) worst = path[r];
+            }
+        }
+        if (margin) margin[r] = row_margin;
+    }
+    *min_failing = worst;
+    free(sel);
+    free(mass);
+    free(cdf);
+    free(c0);
+    free(c1);
+}

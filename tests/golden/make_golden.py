@@ -14,7 +14,9 @@ shims before calling them:
 * ``PokerLegality.__post_init__`` keeps the legality checks without the
   device test (policy.py:34-52);
 * ``PokerStateMachine.initial_roots`` is re-compiled from the reference's own
-  source with only its device-type guard removed (hooks.py:369-371).
+  source with only its device-type guard removed (hooks.py:369-371);
+* ``CollisionConditionedProfileSampler.sample_children`` likewise
+  (rb_sampling.py:107-108).
 
 Everything else runs unmodified.  The fixtures are small ``.npz`` files that
 the ``-m "not gpu"`` tests use to pin the oracle and the ``-m gpu`` tests use
@@ -72,6 +74,16 @@ def _install_shims():
     namespace: dict = {}
     exec(compile(source, hooks.__file__, "exec"), hooks.__dict__, namespace)
     hooks.PokerStateMachine.initial_roots = namespace["initial_roots"]
+
+    from pbg.games.poker.queued import rb_sampling
+
+    source = textwrap.dedent(inspect.getsource(rb_sampling.CollisionConditionedProfileSampler.sample_children))
+    guard = 'if device.type != "cuda":'
+    assert guard in source, "reference sample_children changed shape"
+    source = source.replace(guard, "if False:")
+    namespace = {}
+    exec(compile(source, rb_sampling.__file__, "exec"), rb_sampling.__dict__, namespace)
+    rb_sampling.CollisionConditionedProfileSampler.sample_children = namespace["sample_children"]
 
 
 STATE_FIELDS = ("board_cards", "combo_ids", "button", "street", "to_act", "stacks", "committed",
@@ -440,27 +452,103 @@ def gen_model_input(out, poker):
         out[f"{tag}_post_full"] = _np(machine.direct_model_input(post, state, torch.from_numpy(reach), history))
 
 
+def gen_posterior(out):
+    """rb_sampling.py:86-223: collision-conditioned posterior profiles on seeded parents."""
+
+    import torch
+    from pbg.games.poker.queued.hooks import NLHEGeometry, PAD_CARD
+    from pbg.games.poker.queued.rb_sampling import CollisionConditionedProfileSampler
+
+    cases = [((2, 8.0, 4), 256, "int"), ((3, 8.0, 4), 256, "tensor"), ((6, 100.0, 13), 256, "int"),
+             ((4, 20.5, 9), 256, "tensor"), ((4, 8.0, 4), 3, "int"), ((3, 8.0, 4), 1, "tensor")]
+    for ci, ((players, stack, ranks), attempts, epoch_kind) in enumerate(cases):
+        g = torch.Generator().manual_seed(1000 + ci)
+        geometry = NLHEGeometry(players, stack, ranks)
+        hands, deck, first = geometry.private_hands, geometry.deck_cards, geometry.first_card
+        parents, edges = 12, 48
+        weights = torch.rand((parents, players, hands), generator=g)
+        weights[torch.rand(weights.shape, generator=g) < 0.3] = 0.0
+        if attempts <= 3:  # concentrate mass on a few combos so collisions (and exhaustion) happen
+            keep = torch.rand(weights.shape, generator=g) < (6.0 / hands)
+            weights = torch.where(keep, weights + 0.1, torch.zeros_like(weights))
+            weights[..., 0] += 1.0
+        board = torch.full((parents, 5), PAD_CARD, dtype=torch.uint8)
+        for b in range(parents):
+            shown = [0, 3, 4, 5][b % 4]
+            cards = torch.randperm(deck, generator=g)[:shown] + first
+            board[b, :shown] = cards.to(torch.uint8)
+        # every seat of every parent keeps some board-legal mass (the reference asserts it)
+        # every seat of every parent keeps some board-legal mass (the reference asserts it)
+        pairs = torch.tensor([(i + first, j + first) for i in range(deck) for j in range(i + 1, deck)])
+        for b in range(parents):
+            shown = board[b][board[b] != PAD_CARD].long()
+            legal = ~((pairs[:, :, None] == shown[None, None, :]).any(-1).any(-1))
+            for p in range(players):
+                if float((weights[b, p] * legal).sum()) == 0.0:
+                    pick = torch.nonzero(legal).flatten()
+                    weights[b, p, pick[int(torch.randint(0, pick.numel(), (1,), generator=g))]] = 0.5
+        inherited = torch.randint(0, hands, (parents, players), generator=g, dtype=torch.int32)
+        source = torch.randint(0, parents, (edges,), generator=g, dtype=torch.int64)
+        ordinal = torch.randint(0, 4, (edges,), generator=g, dtype=torch.int64)
+        active = torch.rand((edges,), generator=g) < 0.85
+        root = torch.randint(0, 2**62, (edges,), generator=g, dtype=torch.int64)
+        path = torch.randint(-2**62, 2**62, (edges,), generator=g, dtype=torch.int64)
+        # an epoch tensor must broadcast against the [edge, attempt, seat] address grid
+        epoch = 3 if epoch_kind == "int" else torch.randint(0, 5, (edges, 1, 1), generator=g, dtype=torch.int64)
+        sampler = CollisionConditionedProfileSampler(geometry, max_attempts=attempts)
+        seed, iteration = 77 + ci, 5 + ci
+        result = sampler.sample_children(range_weights=weights, board_cards=board, inherited_profile=inherited,
+                                         source=source, ordinal=ordinal, active=active, root=root, path=path,
+                                         seed=seed, iteration=iteration, retry_epoch=epoch)
+        obs = sampler.last_observation
+        pre = f"c{ci}_"
+        out[pre + "geometry"] = np.array([players, stack, ranks], dtype=np.float64)
+        out[pre + "max_attempts"] = np.array(attempts)
+        out[pre + "seed_iteration"] = np.array([seed, iteration], dtype=np.int64)
+        for name, value in (("weights", weights), ("board", board), ("inherited", inherited), ("source", source),
+                            ("ordinal", ordinal), ("active", active), ("root", root), ("path", path)):
+            out[pre + name] = _np(value)
+        out[pre + "epoch"] = (_np(epoch).reshape(edges).astype(np.int64) if torch.is_tensor(epoch)
+                              else np.full((edges,), epoch, dtype=np.int64))
+        out[pre + "result"] = _np(result)
+        out[pre + "attempt_count"] = _np(obs.attempt_count)
+        out[pre + "exhausted"] = _np(obs.exhausted)
+        out[pre + "minimum_failing"] = np.array(int(obs.minimum_failing_address))
+    out["cases"] = np.array(len(cases))
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="root of a pbg checkout")
     parser.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    parser.add_argument("--only", default=None, help="comma-separated fixture names to (re)generate")
     args = parser.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     sys.path.insert(0, os.path.join(os.path.abspath(args.reference), "tests"))
     import torch
     torch.manual_seed(0)
     _install_shims()
-    rng_out, poker_out, policy_out, loss_out, adam_out, ka_out = {}, {}, {}, {}, {}, {}
-    gen_rng(rng_out)
-    gen_poker(poker_out)
-    gen_known_answers(ka_out)
-    gen_policy(policy_out, poker_out)
-    gen_loss(loss_out)
-    gen_adam(adam_out)
-    mi_out = {}
-    gen_model_input(mi_out, poker_out)
-    for name, data in (("rng", rng_out), ("poker", poker_out), ("known_answers", ka_out),
-                       ("policy", policy_out), ("loss", loss_out), ("adam", adam_out), ("model_input", mi_out)):
+    only = set(args.only.split(",")) if args.only else None
+    if only == {"posterior"}:
+        post_out = {}
+        gen_posterior(post_out)
+        outputs = (("posterior", post_out),)
+    else:
+        rng_out, poker_out, policy_out, loss_out, adam_out, ka_out = {}, {}, {}, {}, {}, {}
+        gen_rng(rng_out)
+        gen_poker(poker_out)
+        gen_known_answers(ka_out)
+        gen_policy(policy_out, poker_out)
+        gen_loss(loss_out)
+        gen_adam(adam_out)
+        mi_out, post_out = {}, {}
+        gen_model_input(mi_out, poker_out)
+        gen_posterior(post_out)
+        outputs = (("rng", rng_out), ("poker", poker_out), ("known_answers", ka_out), ("policy", policy_out),
+                   ("loss", loss_out), ("adam", adam_out), ("model_input", mi_out), ("posterior", post_out))
+        if only is not None:
+            outputs = tuple(item for item in outputs if item[0] in only)
+    for name, data in outputs:
         np.savez_compressed(os.path.join(args.out, f"{name}.npz"), **data)
         print(name, len(data), os.path.getsize(os.path.join(args.out, f"{name}.npz")))
 
