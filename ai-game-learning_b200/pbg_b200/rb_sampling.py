@@ -74,7 +74,7 @@ class CollisionConditionedProfileSampler:
                 raise PosteriorSamplingError("retry_epoch must be a scalar or hold one value per child row")
         else:
             epoch_scalar = int(retry_epoch)
-        g = self.geometry.c()
+        g = self.geometry.c
         work = torch.empty(int(lib().pbg_posterior_workspace_floats(g, parents)), dtype=torch.float32, device=device)
         profile = torch.empty((edges, players), dtype=torch.int32, device=device)
         count = torch.empty(edges, dtype=torch.int32, device=device)
