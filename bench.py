@@ -418,6 +418,56 @@ def model_linear_component(device, rows=524_288, reps=10):
             "gpu_launches": 3}
 
 
+def posterior_component(device, parents=4096, rows=16384, reps=10):
+    """Collision-conditioned posterior profiles (rb_sampling.py): 6-max R13 (1326 private hands), `parents`
+    parent rows of [6, 1326] fp32 range weights (board-conflicting hands masked; flop/turn/river boards),
+    `rows` fresh child rows, up to 256 attempts each.  One call = the CDF pass + the sampling pass, each
+    call queued behind a device-side sleep."""
+
+    import numpy as np
+    import torch
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.rb_sampling import CollisionConditionedProfileSampler
+
+    geo = NLHEGeometry(6, 100.0, 13)
+    g = torch.Generator(device=device).manual_seed(21)
+    w = torch.rand((parents, 6, geo.private_hands), generator=g, device=device)
+    board = torch.full((parents, 5), 255, dtype=torch.uint8, device=device)
+    rng = np.random.default_rng(21)
+    cards = np.stack([rng.permutation(52)[:5] for _ in range(parents)])
+    shown = np.array([3, 4, 5])[np.arange(parents) % 3]
+    host = np.where(np.arange(5)[None, :] < shown[:, None], cards, 255).astype(np.uint8)
+    board.copy_(torch.from_numpy(host))
+    inherited = torch.randint(0, geo.private_hands, (parents, 6), generator=g, device=device, dtype=torch.int32)
+    source = torch.randint(0, parents, (rows,), generator=g, device=device)
+    ordinal = torch.ones(rows, dtype=torch.int64, device=device)
+    active = torch.ones(rows, dtype=torch.bool, device=device)
+    root = torch.randint(0, 2**62, (rows,), generator=g, device=device)
+    path = torch.randint(0, 2**62, (rows,), generator=g, device=device)
+    sampler = CollisionConditionedProfileSampler(geo)
+    times = []
+    for rep in range(reps + 3):
+        torch.cuda._sleep(1_000_000)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        sampler.sample_children(range_weights=w, board_cards=board, inherited_profile=inherited, source=source,
+                                ordinal=ordinal, active=active, root=root, path=path, seed=1, iteration=rep,
+                                retry_epoch=0)
+        e.record()
+        torch.cuda.synchronize(device)
+        if rep >= 3:
+            times.append(a.elapsed_time(e))
+    ms = sorted(times)[len(times) // 2]
+    counts = sampler.last_observation.attempt_count.float()
+    peak, _ = measured_peak()
+    cdf_bytes = parents * 6 * geo.private_hands * 8  # weights read + CDF written, fp32
+    return {"workload": f"collision-conditioned posterior, 6-max R13, {parents} parents x 6 x 1326, {rows} child rows",
+            "us_per_call": 1000.0 * ms, "rows_per_s": rows / (ms / 1000.0),
+            "mean_attempts": float(counts.mean()), "exhausted": int(sampler.last_observation.exhausted.sum()),
+            "cdf_pass_bytes": cdf_bytes, "cdf_pass_gbs_upper": cdf_bytes / (ms / 1000.0) / 1e9, "peak_gbs": peak,
+            "kernels": ["posterior_cdf_kernel", "posterior_sample_kernel"], "gpu_launches": 4}
+
+
 # ----------------------------------------------------------- device arm
 
 
@@ -616,7 +666,8 @@ def main():
     if rank == 0:
         line["components"] = {"rollout_step": rollout_component(device),
                               "layered_targets": targets_component(device),
-                              "model_linear": model_linear_component(device)}
+                              "model_linear": model_linear_component(device),
+                              "posterior_sampler": posterior_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:
