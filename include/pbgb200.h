@@ -317,6 +317,27 @@ int pbg_posterior_sample_children(pbg_geometry geometry, int64_t parents, const 
                                   float *workspace, int32_t *profile, int32_t *attempt_count, uint8_t *exhausted,
                                   int64_t *min_failing, uint32_t *status, void *stream);
 
+/* ------------------------------------------------ branched learner sampling */
+
+/* Workspace bytes (device, 16-byte aligned) for pbg_alias_table over n weights. */
+int64_t pbg_alias_workspace_bytes(int64_t n);
+
+/* pbg/core/csrc/alias_table.cu:11-44 (Walker alias table, Vose's two-stack
+ * construction in float64; learner.py:1519-1543 builds scaled = n * softmax
+ * of the log weights): probability f64 [n] and alias i32 [n]; scaled f64 [n]
+ * is consumed as the reference consumes it.  Identical table to the
+ * reference's single-thread kernel; replaces its small/large stacks with
+ * `workspace`. */
+int pbg_alias_table(int64_t n, double *scaled, double *probability, int32_t *alias, void *workspace, void *stream);
+
+/* pbg/core/csrc/branching_metadata.cu:9-31 (decision_log_mass):
+ * log_mass f32 [n] with log_mass[v] = log_mass[parent[v]] -
+ * logf(degree[parent[v]]) (roots 0), parents at smaller indices.  *failure
+ * (caller-zeroed) receives 1 (parent >= node) or 2 (parent degree <= 0) of
+ * the first failing node in index order.  workspace: 8 device bytes. */
+int pbg_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *degree, float *log_mass,
+                          int32_t *failure, void *workspace, void *stream);
+
 /* ------------------------------------------------------- layered targets */
 
 /* Device tables of per-partition arena pointers (int64 device addresses, 0 =

@@ -1,13 +1,15 @@
-"""Compile the reference's own layer operator into oracle/_ref (test infrastructure only).
+"""Compile the reference's own native operators into oracle/_ref (test infrastructure only).
 
     python oracle/build_ref.py [--reference <pbg checkout>] [--force]
 
-The reference's queued layered-target operator is one CUDA source file
-(pbg/core/csrc/layered_targets.cu, a torch extension with one entry point,
-``run_layers``).  This recipe compiles that file where it lies in the pbg
-checkout with the reference's own device flags (pbg/core/cuda_layer.py:19-25:
--O3 --fmad=false) for sm_100a, linking the torch libraries of this
-interpreter, into ``oracle/_ref/ref_layered_targets<EXT_SUFFIX>``.  Nothing is
+The reference's native operators are single CUDA source files, each a torch
+extension with one entry point: pbg/core/csrc/layered_targets.cu
+(``run_layers``), alias_table.cu (``build_alias_table``) and
+branching_metadata.cu (``decision_log_mass``).  This recipe compiles each file
+where it lies in the pbg checkout with the reference's own device flags
+(pbg/core/cuda_layer.py:19-25, cuda_alias.py, cuda_branching.py: -O3
+--fmad=false) for sm_100a, linking the torch libraries of this interpreter,
+into ``oracle/_ref/<module><EXT_SUFFIX>``.  Nothing is
 copied into this repository.  The GPU tests import the module (when it was
 built) to check the CUDA library against the reference's kernel itself; the
 product never loads it.
@@ -23,24 +25,40 @@ import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
+MODULES = {
+    "ref_layered_targets": os.path.join("pbg", "core", "csrc", "layered_targets.cu"),
+    "ref_alias_table": os.path.join("pbg", "core", "csrc", "alias_table.cu"),
+    "ref_branching_metadata": os.path.join("pbg", "core", "csrc", "branching_metadata.cu"),
+}
 MODULE = "ref_layered_targets"
-SOURCE = os.path.join("pbg", "core", "csrc", "layered_targets.cu")
 DEFAULT_REFERENCE = os.environ.get("PBG_REFERENCE", "/root/reference")
 
 
-def target() -> str:
-    return os.path.join(OUT, MODULE + sysconfig.get_config_var("EXT_SUFFIX"))
+def target(module: str = MODULE) -> str:
+    return os.path.join(OUT, module + sysconfig.get_config_var("EXT_SUFFIX"))
 
 
 def build(reference: str = DEFAULT_REFERENCE, force: bool = False) -> str | None:
-    """Build the reference operator; None when the pbg checkout is absent."""
+    """Build every reference operator (in parallel); None when the pbg checkout is absent."""
 
-    src = os.path.join(reference, SOURCE)
-    if not os.path.exists(src):
+    if not os.path.exists(os.path.join(reference, MODULES[MODULE])):
         return None
-    out = target()
+    jobs = []
+    for module in MODULES:
+        cmd = _command(reference, module, force)
+        if cmd is not None:
+            jobs.append(subprocess.Popen(cmd))
+    for job in jobs:
+        if job.wait() != 0:
+            raise RuntimeError("building a reference operator failed")
+    return target()
+
+
+def _command(reference: str, module: str, force: bool) -> list[str] | None:
+    src = os.path.join(reference, MODULES[module])
+    out = target(module)
     if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
-        return out
+        return None
     import torch
     from torch.utils import cpp_extension
 
@@ -51,28 +69,27 @@ def build(reference: str = DEFAULT_REFERENCE, force: bool = False) -> str | None
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     cmd = [os.path.join(cuda, "bin", "nvcc"), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "--fmad=false",
            "-std=c++17", "-shared", "-Xcompiler", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
-           f"-DTORCH_EXTENSION_NAME={MODULE}", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           f"-DTORCH_EXTENSION_NAME={module}", "-DTORCH_API_INCLUDE_EXTENSION_H",
            "--expt-relaxed-constexpr", "-o", out, src]
     for inc in includes:
         cmd += ["-I", inc]
     for lib in libs:
         cmd += ["-L", lib, f"-Xlinker=-rpath,{lib}"]
     cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python", "-lcudart"]
-    subprocess.run(cmd, check=True)
-    return out
+    return cmd
 
 
-def load():
-    """Import the built module, or None when it was not built."""
+def load(module: str = MODULE):
+    """Import a built module, or None when it was not built."""
 
-    path = target()
+    path = target(module)
     if not os.path.exists(path):
         return None
     import importlib.util
 
     import torch  # noqa: F401  (the module links libtorch)
 
-    spec = importlib.util.spec_from_file_location(MODULE, path)
+    spec = importlib.util.spec_from_file_location(module, path)
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     return module

@@ -104,6 +104,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_adam": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P]),
         "orc_posterior_sample": (None, [Geom, _I64, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32,
                                         _P, _P, _P, _P, _P]),
+        "orc_alias_table": (None, [_I64, _P, _P, _P]),
+        "orc_decision_log_mass": (_I32, [_I64, _P, _P, _P]),
         "orc_layered_targets": (None, [_P, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32,
                                        _I32, _I32, _I32, ctypes.c_float, _I32, _I32, _P]),
     }
@@ -659,3 +661,24 @@ def posterior_sample(geometry_tuple, weights, board, inherited, source, ordinal,
                                int(iteration), _ptr(ep), int(max_attempts), _ptr(out), _ptr(count), _ptr(exh),
                                _ptr(worst), _ptr(margin))
     return out, count, exh.astype(bool), int(worst[0]), margin
+
+
+def alias_table(scaled):
+    """alias_table.cu:11-44 on a float64 vector (not modified); returns (probability, alias, final scaled)."""
+
+    work = np.array(scaled, dtype=np.float64, copy=True)
+    n = work.size
+    prob = np.empty(n, np.float64)
+    alias = np.empty(n, np.int32)
+    lib().orc_alias_table(n, _ptr(work), _ptr(prob), _ptr(alias))
+    return prob, alias, work
+
+
+def decision_log_mass(parent, degree):
+    """branching_metadata.cu:9-31; returns (log_mass f32 [n] (NaN after a failure), failure code)."""
+
+    p = np.ascontiguousarray(parent, dtype=np.int32)
+    d = np.ascontiguousarray(degree, dtype=np.int32)
+    out = np.full(p.size, np.nan, np.float32)
+    code = lib().orc_decision_log_mass(p.size, _ptr(p), _ptr(d), _ptr(out))
+    return out, int(code)

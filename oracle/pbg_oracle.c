@@ -1210,3 +1210,45 @@ void orc_posterior_sample(orc_geom g, int64_t B, const float *weights, const uin
     free(c0);
     free(c1);
 }
+
+/* ------------------------------------------------ branched learner sampling */
+
+/* pbg/core/csrc/alias_table.cu:11-44: Vose's two-stack Walker construction
+ * over scaled weights (float64), in the reference's push/pop order. */
+void orc_alias_table(int64_t n, double *scaled, double *probability, int32_t *alias) {
+    int64_t *small = (int64_t *)malloc(sizeof(int64_t) * n), *large = (int64_t *)malloc(sizeof(int64_t) * n);
+    int64_t ns = 0, nl = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        probability[i] = 1.0;
+        alias[i] = (int32_t)i;
+        if (scaled[i] < 1.0) small[ns++] = i;
+        else large[nl++] = i;
+    }
+    while (ns != 0 && nl != 0) {
+        int64_t low = small[--ns], high = large[--nl];
+        double p = scaled[low];
+        probability[low] = p;
+        alias[low] = (int32_t)high;
+        scaled[high] -= 1.0 - p;
+        if (scaled[high] < 1.0) small[ns++] = high;
+        else large[nl++] = high;
+    }
+    free(small);
+    free(large);
+}
+
+/* pbg/core/csrc/branching_metadata.cu:9-31: decision log mass in node order;
+ * returns the failure code (0, 1 or 2) of the first failing node. */
+int32_t orc_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *degree, float *log_mass) {
+    for (int64_t v = 0; v < n; ++v) {
+        int32_t a = parent[v];
+        if (a >= v) return 1;
+        if (a < 0) {
+            log_mass[v] = 0.0f;
+            continue;
+        }
+        if (degree[a] <= 0) return 2;
+        log_mass[v] = log_mass[a] - logf((float)degree[a]);
+    }
+    return 0;
+}
