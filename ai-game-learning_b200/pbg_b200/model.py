@@ -1,5 +1,9 @@
 """Dense layers of the poker policy/value model on the tensor cores.
 
+``attention`` is the reach-biased self-attention core of the model's MHA
+(pbg/games/poker/model/primitives.py:63-283) on the tensor cores; ``MHA``
+composes it with the two projections.
+
 ``linear`` is the affine map of pbg/core/tensor_ops.py ``Linear`` (weight
 ``[out, in]``, bias ``[out]``) as used by the model's FFN
 (pbg/games/poker/model/primitives.py:35-60: ``w2(gelu(w1(x)))``) and by the
@@ -82,4 +86,54 @@ class FFN:
         return self.w2(self.w1(x, "gelu"))
 
 
-__all__ = ["FFN", "Linear", "linear", "pipeline_error"]
+def attention(qkv: Tensor, heads: int, q_scale: Tensor, key_bias: Tensor | None = None,
+              key_mask: Tensor | None = None) -> Tensor:
+    """Self-attention core of primitives.py MHA for heads of width 32 (pbg_attention_bf16).
+
+    ``qkv`` bf16 ``[B, L, 3 * heads * 32]`` (the fused in-projection's output),
+    ``q_scale`` fp32 ``[heads]`` = 1 / (temperature * sqrt(32)), ``key_bias``
+    fp32 ``[B, L]``, ``key_mask`` bool ``[B, L]``.  Returns merged heads, bf16
+    ``[B, L, heads * 32]``.
+    """
+
+    if qkv.dtype != torch.bfloat16 or qkv.ndim != 3 or qkv.shape[2] != 3 * heads * 32:
+        raise NativeError("attention takes bf16 qkv [B, L, 3 * heads * 32]")
+    batch, length, _ = qkv.shape
+    qkv = qkv.contiguous()
+    if key_bias is not None and (key_bias.dtype != torch.float32 or key_bias.shape != (batch, length)):
+        raise NativeError("key_bias must be float32 [B, L]")
+    if key_mask is not None and (key_mask.dtype != torch.bool or key_mask.shape != (batch, length)):
+        raise NativeError("key_mask must be bool [B, L]")
+    scale = q_scale.to(device=qkv.device, dtype=torch.float32).contiguous()
+    if scale.shape != (heads,):
+        raise NativeError("q_scale must hold one value per head")
+    out = torch.empty((batch, length, heads * 32), dtype=torch.bfloat16, device=qkv.device)
+    mask = None if key_mask is None else key_mask.contiguous().view(torch.uint8)
+    call("pbg_attention_bf16", batch, length, heads, ptr(qkv), ptr(None if key_bias is None else key_bias.contiguous()),
+         ptr(mask), ptr(scale), ptr(out), ptr(_error_word(qkv.device)), stream(qkv.device))
+    return out
+
+
+class MHA:
+    """primitives.py:63-283 MHA (self-attention) with the reference's parameters.
+
+    ``w_qkv`` / ``w_o`` are Linear maps (weight ``[3d, d]`` / ``[d, d]``),
+    ``theta`` ``[heads]`` gives the learned temperature softplus(theta) + 0.5.
+    """
+
+    def __init__(self, w_qkv: Linear, w_o: Linear, theta: Tensor, heads: int) -> None:
+        d = w_o.weight.shape[0]
+        if d != heads * 32 or w_qkv.weight.shape != (3 * d, d):
+            raise NativeError("MHA: this build's attention core takes heads of width 32")
+        self.w_qkv, self.w_o, self.heads = w_qkv, w_o, heads
+        temperature = torch.nn.functional.softplus(theta.float()) + 0.5
+        self.q_scale = (1.0 / (temperature * 32 ** 0.5)).contiguous()
+
+    def forward_biased(self, x: Tensor, key_bias: Tensor | None, key_mask: Tensor | None) -> Tensor:
+        merged = attention(self.w_qkv(x), self.heads, self.q_scale.to(x.device), key_bias, key_mask)
+        return self.w_o(merged)
+
+    __call__ = forward_biased
+
+
+__all__ = ["FFN", "Linear", "MHA", "attention", "linear", "pipeline_error"]

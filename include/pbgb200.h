@@ -403,6 +403,18 @@ int pbg_layered_targets(const int32_t *layer_ptr, int32_t layers, pbg_target_nod
 int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *w, const float *bias, void *y,
                     int32_t activation, uint32_t *error, void *stream);
 
+/* pbg/games/poker/model/primitives.py:63-283 (MHA, self-attention, heads of
+ * width 32): out[b, q, h] = softmax_k((q_h / temperature_h) . k_h / sqrt(32)
+ * + key_bias[b, k], keys with key_mask 0 excluded) . v_h.  qkv bf16
+ * [batch, len, 3 * heads * 32] (the fused in-projection: q | k | v, heads
+ * contiguous inside each), key_bias f32 [batch, len] or NULL, key_mask u8
+ * [batch, len] or NULL (all present), q_scale f32 [heads] = 1 /
+ * (temperature_h * sqrt(32)), out bf16 [batch, len, heads * 32] (merged
+ * heads).  Rows whose keys are all masked give 0.  error (device) as for
+ * pbg_linear_bf16. */
+int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, const void *qkv, const float *key_bias,
+                       const uint8_t *key_mask, const float *q_scale, void *out, uint32_t *error, void *stream);
+
 /* ---------------------------------------------------------- collective */
 
 /* replica.py:352-362 (all_reduce SUM of the flat fp32 gradient) over NVLink
