@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(AttnArgs A) {
     extern __shared__ __align__(16) unsigned char at_raw[];
     __shared__ __align__(8) uint64_t bar_s, bar_pv, bar_done;
     __shared__ uint32_t tmem_s;
+    __shared__ float kterm[AT_BLOCK];  // per key of the block: base-2 bias, or -inf when absent
     const uint32_t base = (at_smem(at_raw) + 1023u) & ~1023u;
     unsigned char* sm = at_raw + (base - at_smem(at_raw));
     const int r = threadIdx.x, warp = r >> 5;
@@ -177,6 +178,10 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(AttnArgs A) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sm + AT_K + sw128(r, j)) = kc[j];
         {
+            const bool present = key < A.len && (!A.key_mask || A.key_mask[row0 + key]);
+            kterm[r] = present ? (A.key_bias ? A.key_bias[row0 + key] * 1.4426950408889634f : 0.0f) : -INFINITY;
+        }
+        {
             // V^T: element (d, key) in column block key / 64, byte (key % 64) * 2 of row d
             const int blk = r >> 6, col = r & 63;
             const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(vc);
@@ -204,25 +209,18 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(AttnArgs A) {
             break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // 3. online softmax over this block's keys (base 2)
-        const float* bias = A.key_bias ? A.key_bias + row0 + kb * AT_BLOCK : nullptr;
-        const uint8_t* mask = A.key_mask ? A.key_mask + row0 + kb * AT_BLOCK : nullptr;
-        const int valid = A.len - kb * AT_BLOCK;
+        // 3. online softmax over this block's keys (base 2); absent keys carry -inf
         float bmax = -INFINITY;
         for (int c = 0; c < AT_BLOCK; c += 32) {
             float s[32];
             at_ld32(lane_base + (uint32_t)c, s);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int k = c + j;
-                const bool present = k < valid && (!mask || mask[k]);
-                const float bk = present && bias ? bias[k] * 1.4426950408889634f : 0.0f;
-                const float x = present ? fmaf(s[j], scale2, bk) : -INFINITY;
-                bmax = fmaxf(bmax, x);
-            }
+            for (int j = 0; j < 32; ++j) bmax = fmaxf(bmax, fmaf(s[j], scale2, kterm[c + j]));
         }
         const float m_new = fmaxf(m, bmax);
-        const float corr = m_new == -INFINITY ? 1.0f : exp2f(m - m_new);
+        const bool any = m_new != -INFINITY;  // some key so far is present
+        const float corr = any ? exp2f(m - m_new) : 1.0f;
+        const float shift = any ? m_new : 0.0f;
         float sum = 0.0f;
         for (int c = 0; c < AT_BLOCK; c += 32) {
             float s[32];
@@ -230,17 +228,10 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(AttnArgs A) {
             uint32_t packed[16];
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-                float p2[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int k = c + j + u;
-                    const bool present = k < valid && (!mask || mask[k]);
-                    const float bk = present && bias ? bias[k] * 1.4426950408889634f : 0.0f;
-                    const float x = fmaf(s[j + u], scale2, bk);
-                    p2[u] = present && m_new != -INFINITY ? exp2f(x - m_new) : 0.0f;
-                    sum += p2[u];
-                }
-                __nv_bfloat162 hv = __floats2bfloat162_rn(p2[0], p2[1]);
+                const float p0 = exp2f(fmaf(s[j], scale2, kterm[c + j]) - shift);
+                const float p1 = exp2f(fmaf(s[j + 1], scale2, kterm[c + j + 1]) - shift);
+                sum += p0 + p1;
+                __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
                 packed[j / 2] = *reinterpret_cast<uint32_t*>(&hv);
             }
             // row r of P: keys c..c+31 are chunks c/8 .. c/8+3 of column block c / 64
