@@ -418,6 +418,42 @@ def model_linear_component(device, rows=524_288, reps=10):
             "gpu_launches": 3}
 
 
+def model_attention_component(device, batch=600, length=876, heads=8, reps=10):
+    """The model's reach-biased self-attention core (pbg_attention_bf16) at cfg2's preflop sequence
+    length: `batch` sequences x `length` tokens x `heads` heads of width 32, fp32 key bias and key mask.
+    Each launch queued behind a device-side sleep."""
+
+    import math
+
+    import torch
+    from pbg_b200.model import attention, pipeline_error
+
+    g = torch.Generator(device=device).manual_seed(13)
+    qkv = torch.randn((batch, length, 3 * heads * 32), generator=g, device=device).to(torch.bfloat16)
+    bias = torch.randn((batch, length), generator=g, device=device)
+    mask = torch.rand((batch, length), generator=g, device=device) > 0.1
+    q_scale = torch.full((heads,), 1.0 / math.sqrt(32), device=device)
+    times = []
+    for rep in range(reps + 3):
+        torch.cuda._sleep(1_000_000)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        attention(qkv, heads, q_scale, bias, mask)
+        e.record()
+        torch.cuda.synchronize(device)
+        if rep >= 3:
+            times.append(a.elapsed_time(e))
+    if pipeline_error(device):
+        raise RuntimeError("attention pipeline wait ran out")
+    ms = sorted(times)[len(times) // 2]
+    flops = 4.0 * batch * heads * length * length * 32
+    exps = float(batch * heads * length * length)
+    return {"workload": f"reach-biased attention core, {batch} sequences x {length} tokens x {heads} heads (width 32)",
+            "us": 1000.0 * ms, "tflops": flops / ms / 1e9, "exp_per_s": exps / (ms / 1000.0),
+            "bound": "SFU/latency (softmax); the tensor pipe does 2 MMAs of 128x128x32 and 8 of 128x32x16 per key block",
+            "kernel": "attention_kernel", "gpu_launches": 1}
+
+
 def posterior_component(device, parents=4096, rows=16384, reps=10):
     """Collision-conditioned posterior profiles (rb_sampling.py): 6-max R13 (1326 private hands), `parents`
     parent rows of [6, 1326] fp32 range weights (board-conflicting hands masked; flop/turn/river boards),
@@ -667,6 +703,7 @@ def main():
         line["components"] = {"rollout_step": rollout_component(device),
                               "layered_targets": targets_component(device),
                               "model_linear": model_linear_component(device),
+                              "model_attention": model_attention_component(device),
                               "posterior_sampler": posterior_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
