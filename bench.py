@@ -700,11 +700,13 @@ def main():
         "clocks": clocks.summary(),
     }
     if rank == 0:
-        line["components"] = {"rollout_step": rollout_component(device),
-                              "layered_targets": targets_component(device),
-                              "model_linear": model_linear_component(device),
-                              "model_attention": model_attention_component(device),
-                              "posterior_sampler": posterior_component(device)}
+        line["components"] = {}
+        if world == 1:  # single-GPU kernels of the path, measured once, outside the scaling runs
+            line["components"] = {"rollout_step": rollout_component(device),
+                                  "layered_targets": targets_component(device),
+                                  "model_linear": model_linear_component(device),
+                                  "model_attention": model_attention_component(device),
+                                  "posterior_sampler": posterior_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:
