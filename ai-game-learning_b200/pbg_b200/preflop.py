@@ -1,0 +1,364 @@
+"""The preflop class-row policy/value network on this build's kernels.
+
+``PreflopModel.forward`` computes pbg/games/poker/model/preflop.py:472-693
+(``PreflopEncoder.forward``) with the shared trunk and readout of
+pbg/games/poker/model/shared.py, from the reference's own parameters (a
+dict keyed by the two modules' ``state_dict`` names).  Every dense map of the
+trunk and readout runs on ``pbg_linear_bf16`` (tcgen05, bf16 operands, fp32
+accumulation; K zero-padded to 64 and N to 128 once at bind time), every
+LayerNorm on ``pbg_layernorm``, every attention on ``pbg_attention_bf16``.
+FamilyFFN's common and static maps become one GEMM over the concatenated
+inputs with GELU in its epilogue.  The residual stream stays fp32; the
+token assembly (embeddings, the 1- and 6-wide affine maps of the scalars),
+the incidence mass reductions (fp32 batched GEMMs, as the reference keeps
+them) and the small elementwise steps are torch operations on the device.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+from torch.nn import functional as F
+
+from ._native import NativeError, call, ptr, stream
+from .model import attention, linear
+
+
+@dataclass(frozen=True)
+class PreflopConfig:
+    """The fields of pbg PokerModelConfig (preflop.py:31-54) the forward uses."""
+
+    d_model: int = 256
+    n_heads: int = 8
+    layers: int = 6
+    m_raise: int = 4
+    k_act: int = 7
+    s_min: float = 0.02
+    max_players: int = 9
+    class_embedding_dim: int = 32
+    ffn_hidden: int | None = None
+    max_history_tokens: int = 256
+    folder_beta_rank: int = 16
+    folder_line_dim: int = 8
+    eps: float = 1e-8
+
+    @property
+    def hidden(self) -> int:
+        return self.ffn_hidden or 4 * self.d_model
+
+
+def class_geometry(rank_count: int):
+    """pbg/games/poker/cards.py DeckGeometry for the preflop network: combo cards, class of each combo,
+    class sizes, the orbit-averaged card incidence [classes, cards] and the overlap scalars (preflop.py:234-253)."""
+
+    deck = 4 * rank_count
+    first = 52 - deck
+    combos = [(i, j) for i in range(deck) for j in range(i + 1, deck)]
+
+    def klass(a, b):
+        ra, rb = (a + first) // 4 - (13 - rank_count), (b + first) // 4 - (13 - rank_count)
+        high, low = max(ra, rb), min(ra, rb)
+        hp, lp = rank_count - 1 - high, rank_count - 1 - low
+        suited_or_pair = ra == rb or (a + first) % 4 == (b + first) % 4
+        return hp * rank_count + lp if suited_or_pair else lp * rank_count + hp
+
+    classes = rank_count * rank_count
+    of_combo = torch.tensor([klass(a, b) for a, b in combos], dtype=torch.long)
+    sizes = torch.bincount(of_combo, minlength=classes).to(torch.float32)
+    orbit = torch.zeros((classes, deck), dtype=torch.float32)
+    cards = torch.tensor(combos, dtype=torch.long)
+    orbit.index_put_((of_combo[:, None].expand(-1, 2).reshape(-1), cards.reshape(-1)),
+                     torch.ones(cards.numel(), dtype=torch.float32), accumulate=True)
+    orbit = orbit / sizes[:, None]
+    overlap = orbit @ orbit.T
+    within = overlap.diagonal()
+    cross = (overlap.sum(1) - within) / (classes - 1)
+    return sizes, orbit, torch.stack((within, cross), dim=1)
+
+
+class _Map:
+    """A Linear bound for pbg_linear_bf16: bf16 weight padded to K % 64 == 0 and N % 128 == 0."""
+
+    def __init__(self, weight: Tensor, bias: Tensor | None, device) -> None:
+        n, k = weight.shape
+        self.n, self.k = n, k
+        self.kp, self.np_ = -(-k // 64) * 64, -(-n // 128) * 128
+        w = torch.zeros((self.np_, self.kp), dtype=torch.bfloat16, device=device)
+        w[:n, :k] = weight.to(device=device, dtype=torch.bfloat16)
+        self.weight = w
+        self.bias = None
+        if bias is not None:
+            b = torch.zeros(self.np_, dtype=torch.float32, device=device)
+            b[:n] = bias.to(device=device, dtype=torch.float32)
+            self.bias = b
+
+    def __call__(self, x: Tensor, activation: str | None = None) -> Tensor:
+        lead = x.shape[:-1]
+        rows = x.reshape(-1, x.shape[-1])
+        if self.kp != self.k:
+            rows = F.pad(rows, (0, self.kp - self.k))
+        y = linear(rows.to(torch.bfloat16).contiguous(), self.weight, self.bias, activation)
+        if self.np_ != self.n:
+            y = y[:, : self.n]
+        return y.reshape(*lead, self.n)
+
+
+def _cat_maps(first: Tensor, second: Tensor) -> Tensor:
+    return torch.cat((first, second), dim=1)
+
+
+class PreflopModel:
+    """Binds the reference's shared and encoder parameters (name -> tensor) to this build's kernels."""
+
+    def __init__(self, cfg: PreflopConfig, rank_count: int, params: dict[str, Tensor], device) -> None:
+        if cfg.d_model != cfg.n_heads * 32:
+            raise NativeError("this build's attention core takes heads of width 32")
+        self.cfg, self.device = cfg, torch.device(device)
+        self.rank_count = rank_count
+        self.n_cards = 4 * rank_count
+        self.n_classes = rank_count * rank_count
+        sizes, orbit, overlap = class_geometry(rank_count)
+        self.class_sizes = sizes.to(self.device)
+        self.class_card_geometry = orbit.to(self.device)
+        self.class_overlap_scalars = overlap.to(self.device)
+        p = {k: v.to(self.device, torch.float32) for k, v in params.items()}
+        self.p = p
+        lin = lambda name, bias=True: _Map(p[name + ".weight"], p.get(name + ".bias") if bias else None, self.device)  # noqa: E731
+        self.class_row_affine = lin("class_row_affine")
+        self.layers = []
+        for i in range(cfg.layers):
+            inc = f"incidence_residuals.{i}"
+            ffn = f"layer_ffns.{i}"
+            mha = f"attentions.{i}"
+            theta = p[f"{mha}.theta"]
+            temperature = F.softplus(theta) + 0.5
+            self.layers.append({
+                "ln": (p[f"layer_norms.{i}.weight"], p[f"layer_norms.{i}.bias"]),
+                "inc_ln": (p[f"{inc}.norm.weight"], p[f"{inc}.norm.bias"]),
+                "source": lin(f"{inc}.source", False),
+                "query": lin(f"{inc}.query"),
+                "identical": lin(f"{inc}.identical", False),
+                "own": lin(f"{inc}.own", False),
+                "inc_out": lin(f"{inc}.output"),
+                "w_qkv": lin(f"{mha}.w_qkv"),
+                "w_o": lin(f"{mha}.w_o"),
+                "q_scale": (1.0 / (temperature * math.sqrt(32))).contiguous(),
+                # FamilyFFN (shared.py:19-33): common(x) + static[pre](s) as one map over [x, s]
+                "ffn_in": _Map(_cat_maps(p[f"{ffn}.common.weight"], p[f"{ffn}.static.pre.weight"]),
+                               p[f"{ffn}.common.bias"], self.device),
+                "ffn_out": lin(f"{ffn}.output"),
+            })
+        self.final_ln = (p["final_norm.weight"], p["final_norm.bias"])
+
+        def ffn(name):
+            return (lin(name + ".w1"), lin(name + ".w2"), p[name + ".w1.weight"], p[name + ".w1.bias"])
+
+        self.actor_seat_features = ffn("actor_seat_features")
+        self.seat_features = ffn("seat_features")
+        self.global_features = ffn("global_features")
+        self.type_features = ffn("type_features")
+        self.raise_features = ffn("raise_features")
+        self.value_features = ffn("value_head.features")
+        self.type_head = lin("type_head.affine")
+        self.mixture_affine = lin("raise_head.mixture_affine")
+        self.allin_affine = lin("raise_head.allin_affine")
+        self.value_affine = lin("value_head.affine")
+        self._factored: dict = {}
+
+    # ------------------------------------------------------------ kernels
+    def _ln(self, x: Tensor, gain_bias) -> Tensor:
+        d = x.shape[-1]
+        rows = x.reshape(-1, d).contiguous()
+        out = torch.empty(rows.shape, dtype=torch.bfloat16, device=x.device)
+        call("pbg_layernorm", rows.shape[0], d, ptr(rows), int(rows.dtype == torch.bfloat16), ptr(gain_bias[0]),
+             ptr(gain_bias[1]), 1e-5, ptr(out), 1, stream(x.device))
+        return out.reshape(x.shape)
+
+    def _ffn(self, maps, x: Tensor) -> Tensor:
+        return maps[1](maps[0](x, "gelu"))
+
+    def _ffn_factored(self, maps, rows: Tensor, context: Tensor) -> Tensor:
+        """primitives.py:62-71 forward_factored: the context projected once per decision."""
+
+        split = rows.shape[-1]
+        key = (id(maps), split)
+        if key not in self._factored:
+            w1, b1 = maps[2], maps[3]
+            self._factored[key] = (_Map(w1[:, :split], b1, self.device), _Map(w1[:, split:], None, self.device))
+        row_map, ctx_map = self._factored[key]
+        hidden = row_map(rows).float() + ctx_map(context).float()[:, None, :]
+        return maps[1](F.gelu(hidden))
+
+    # ------------------------------------------------------------ forward
+    def _public_tokens(self, pub, seat_mask: Tensor, relative_seats: Tensor):
+        """preflop.py:373-470."""
+
+        p = self.p
+        batch, players = seat_mask.shape
+        dev = self.device
+        groups = [pub["pot"][:, None], pub["stacks"], pub["committed"], pub["street"].float()[:, None],
+                  pub["legality_summary"].float(), pub["n_ticks"].float()[:, None],
+                  pub["raise_grid_bounds"].float()]
+        kinds = [(1, 0), (players, 1), (players, 2), (1, 3), (pub["legality_summary"].shape[1], 4), (1, 5), (2, 6)]
+        if pub.get("committed_street") is not None:
+            groups.append(pub["committed_street"].float())
+            kinds.append((players, 7))
+        exact = [pub[k].float()[:, None] for k in ("call_amount", "current_bet", "min_raise_to", "max_raise_to",
+                                                  "last_full_raise") if pub.get(k) is not None]
+        if exact:
+            groups.append(torch.cat(exact, 1))
+            kinds.append((len(exact), 8))
+        if pub.get("legal_action_mask") is not None:
+            groups.append(pub["legal_action_mask"].float())
+            kinds.append((pub["legal_action_mask"].shape[1], 9))
+        if pub.get("raise_ticks") is not None:
+            groups.append(pub["raise_ticks"].float())
+            kinds.append((pub["raise_ticks"].shape[1], 10))
+        scalars = torch.cat(groups, 1)
+        type_ids = torch.cat([torch.full((n,), k, dtype=torch.long, device=dev) for n, k in kinds])
+        w = p["public_scalar_affine.weight"][:, 0]
+        token = scalars[..., None] * w + p["public_scalar_affine.bias"] + p["public_type_embedding.weight"][type_ids]
+        seat_pos = p["seat_embedding.weight"][relative_seats]
+        rest = scalars.shape[1] - 1 - 2 * players
+        zeros = lambda n: torch.zeros((batch, n, self.cfg.d_model), device=dev)  # noqa: E731
+        token = token + torch.cat((zeros(1), seat_pos, seat_pos, zeros(rest)), 1)
+        valid = torch.cat((torch.ones((batch, 1), dtype=torch.bool, device=dev), seat_mask, seat_mask,
+                           torch.ones((batch, rest), dtype=torch.bool, device=dev)), 1)
+        h = pub.get("history")
+        if h is not None and h["mask"].shape[1]:
+            numeric = torch.stack([h[k].float() for k in ("amount", "pot_before", "call_amount", "current_bet",
+                                                          "min_raise_to", "max_raise_to")], -1)
+            ht = numeric @ p["history_numeric_affine.weight"].T + p["history_numeric_affine.bias"]
+            ht = ht + p["history_action_embedding.weight"][h["action"].clamp(0, 3).long()]
+            ht = ht + p["history_street_embedding.weight"][h["street"].clamp(0, 3).long()]
+            ht = ht + p["history_position_embedding.weight"][torch.arange(h["mask"].shape[1], device=dev)][None]
+            actor = h["actor"].clamp(0, players - 1).long()
+            ht = ht + p["seat_embedding.weight"][relative_seats.gather(1, actor)] * (h["actor"] >= 0)[..., None]
+            token = torch.cat((token, ht), 1)
+            valid = torch.cat((valid, h["mask"].bool()), 1)
+        mean = (token * valid[..., None]).sum(1) / valid.sum(1, keepdim=True)
+        state = p["state_token"] + mean
+        return (torch.cat((token, state[:, None]), 1),
+                torch.cat((valid, torch.ones((batch, 1), dtype=torch.bool, device=dev)), 1))
+
+    def _incidence(self, layer, rows: Tensor, mass: Tensor, incidence: Tensor, identical_scale: Tensor):
+        """incidence.py:30-84 (IncidenceResidual.forward)."""
+
+        normalized = self._ln(rows, layer["inc_ln"])
+        source = layer["source"](normalized).float() * mass.float()[..., None]
+        card_acc = torch.einsum("brc,bprd->bpcd", incidence, source)
+        card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc)
+        same = source * identical_scale[:, None, :, None]
+        other_equal = same.sum(1, keepdim=True) - same
+        other_card = card_overlap.sum(1, keepdim=True) - card_overlap - 2.0 * other_equal
+        own_card = card_overlap - 2.0 * same
+        inner = (layer["query"](normalized).float() + other_card + layer["identical"](other_equal).float()
+                 + layer["own"](own_card).float())
+        residual = layer["inc_out"](F.gelu(inner))
+        return residual, other_card, other_equal, own_card
+
+    def forward(self, pub: dict, class_ranges: Tensor, class_mask: Tensor | None = None,
+                actor_seat: Tensor | None = None):
+        """preflop.py:472-693 -> (raw policy fields, value [B, K])."""
+
+        cfg, p, dev = self.cfg, self.p, self.device
+        d, K = cfg.d_model, self.n_classes
+        ranges = class_ranges.to(dev, torch.float32)
+        batch, players = ranges.shape[:2]
+        actor = (pub["to_act"] if actor_seat is None else actor_seat).long()
+        seat_mask = pub.get("seat_mask")
+        seat_mask = torch.ones((batch, players), dtype=torch.bool, device=dev) if seat_mask is None else seat_mask.bool()
+        cmask = torch.ones_like(ranges, dtype=torch.bool) if class_mask is None else class_mask.bool()
+        cmask = cmask & seat_mask[:, :, None]
+        status = pub.get("status")
+        status = torch.zeros((batch, players), dtype=torch.long, device=dev) if status is None else status.long()
+        seat_ids = torch.arange(players, device=dev)[None].expand(batch, -1)
+        button = pub.get("button")
+        relative = torch.remainder(seat_ids - button[:, None].long(), players) if button is not None else seat_ids
+        class_ids = torch.arange(K, device=dev)
+        class_emb = p["class_embedding.weight"][class_ids][None].expand(batch, -1, -1)
+        expanded_emb = class_emb[:, None].expand(-1, players, -1, -1)
+        size_feature = (self.class_sizes / 12.0)[None, None].expand(batch, players, -1)
+        geometry = torch.cat((self.class_card_geometry, self.class_overlap_scalars), -1)
+        expanded_geometry = geometry[None, None].expand(batch, players, -1, -1)
+        log_range = torch.log(ranges.clamp_min(cfg.eps))
+        row_feature = torch.cat((ranges[..., None], log_range[..., None], size_feature[..., None], expanded_emb,
+                                 expanded_geometry, torch.ones_like(ranges)[..., None]), -1)
+        row = self.class_row_affine(row_feature).float()
+        row = row + p["seat_embedding.weight"][relative][:, :, None]
+        row = row + p["status_embedding.weight"][status][:, :, None]
+        actor_flag = (torch.arange(players, device=dev)[None] == actor[:, None]).long()
+        row = row + p["actor_embedding.weight"][actor_flag][:, :, None]
+        row_flat = row.reshape(batch, players * K, d)
+        public_token, public_mask = self._public_tokens(pub, seat_mask, relative)
+        actor_relative = relative.gather(1, actor[:, None]).squeeze(1)
+        anchors = p["anchor_tokens"][None] + p["anchor_seat_embedding.weight"][actor_relative][:, None]
+        x = torch.cat((row_flat, public_token, anchors), 1)
+        length = x.shape[1]
+        key_mask = torch.cat((cmask.reshape(batch, players * K), public_mask,
+                              torch.ones((batch, cfg.k_act), dtype=torch.bool, device=dev)), 1)
+        masked_range = ranges * cmask.float()
+        normalized = masked_range / masked_range.sum(-1, keepdim=True).clamp_min(cfg.eps)
+        key_bias = torch.cat((torch.log(normalized.clamp_min(cfg.eps)).reshape(batch, players * K),
+                              torch.zeros((batch, length - players * K), device=dev)), 1).contiguous()
+        side_class = torch.cat((expanded_emb, ranges[..., None], log_range[..., None], expanded_geometry), -1)
+        incidence = self.class_card_geometry[None].expand(batch, -1, -1)
+        identical_scale = (1.0 / self.class_sizes)[None].expand(batch, -1)
+
+        def pad_rows(value: Tensor) -> Tensor:
+            rows = value.reshape(batch, players * K, -1)
+            return F.pad(rows, (0, 0, 0, length - rows.shape[1]))
+
+        for layer in self.layers:
+            row_state = x[:, : players * K].reshape(batch, players, K, d)
+            j, oc, oe, _ = self._incidence(layer, row_state, normalized, incidence, identical_scale)
+            nx = self._ln(x, layer["ln"])
+            qkv = layer["w_qkv"](nx)
+            attended = attention(qkv.contiguous(), cfg.n_heads, layer["q_scale"], key_bias, key_mask)
+            x_hat = x + layer["w_o"](attended).float()
+            dynamic = torch.cat((j.float(), oc * oc, oc * oe), -1)
+            common = torch.cat((self._ln(x_hat, layer["ln"]).float(), pad_rows(dynamic)), -1)
+            hidden = layer["ffn_in"](torch.cat((common, pad_rows(side_class)), -1), "gelu")
+            x = x_hat + layer["ffn_out"](hidden).float()
+
+        final = self._ln(x, self.final_ln).float()
+        final_rows = final[:, : players * K].reshape(batch, players, K, d)
+        final_public = final[:, players * K: -cfg.k_act]
+        final_anchors = final[:, -cfg.k_act:]
+        public_valid = public_mask.float()
+        public_mean = (final_public * public_valid[..., None]).sum(1) / public_valid.sum(1, keepdim=True)
+        actor_anchor = torch.cat((final_anchors[:, 0], final_anchors[:, 1], final_anchors[:, 2],
+                                  final_anchors[:, 3:].mean(1)), -1)
+        actor_summary = self._ffn(self.actor_seat_features, actor_anchor).float()
+        mass = masked_range.sum(-1)
+        pooled = (final_rows * masked_range[..., None]).sum(2) / mass[..., None].clamp_min(cfg.eps)
+        seat_meta = torch.stack((mass, status.float() / 2.0, relative.float() / max(cfg.max_players - 1, 1)), -1)
+        seat_summary = self._ffn(self.seat_features, torch.cat((pooled, seat_meta), -1)).float()
+        selector = torch.arange(players, device=dev)[None] == actor[:, None]
+        seat_summary = torch.where(selector[..., None], actor_summary[:, None], seat_summary)
+        seat_summary = seat_summary.masked_fill(~seat_mask[..., None], 0.0)
+        ordered = torch.zeros_like(seat_summary).scatter(1, relative[..., None].expand(-1, -1, d), seat_summary)
+        padded = torch.cat((ordered, torch.zeros((batch, cfg.max_players - players, d), device=dev)), 1)
+        global_feature = self._ffn(self.global_features,
+                                   torch.cat((public_mean, actor_summary, padded.reshape(batch, -1)), -1)).float()
+        actor_rows = final_rows[torch.arange(batch, device=dev), actor]
+        # shared.py:74-92 readout
+        rows = torch.cat((actor_rows, class_emb), -1)
+        context = torch.cat((final_anchors.flatten(1), global_feature), -1)
+        z_type = self._ffn_factored(self.type_features, rows, context).float()
+        z_raise = self._ffn_factored(self.raise_features, rows, context).float()
+        raw = self.mixture_affine(z_raise).float()
+        m = cfg.m_raise
+        omega = torch.softmax(raw[..., :m], -1)
+        mu = torch.sigmoid(raw[..., m:2 * m])
+        s = F.softplus(raw[..., 2 * m:]) + cfg.s_min
+        iota = torch.sigmoid(self.allin_affine(z_type).float()).squeeze(-1)
+        value_features = self._ffn_factored(self.value_features, rows, context)
+        value = self.value_affine(value_features).float().squeeze(-1)
+        return {"type_logits": self.type_head(z_type).float(), "omega": omega, "mu": mu, "s": s, "iota": iota}, value
+
+
+__all__ = ["PreflopConfig", "PreflopModel", "class_geometry"]

@@ -415,6 +415,13 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *
 int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, const void *qkv, const float *key_bias,
                        const uint8_t *key_mask, const float *q_scale, void *out, uint32_t *error, void *stream);
 
+/* pbg/core/tensor_ops.py:70-81 (LayerNorm over the last dimension, d <= 1024):
+ * y = (x - mean) / sqrt(var + eps) * gain + bias, fp32 statistics; x and y
+ * are bf16 when x_bf16 / y_bf16 is nonzero, else fp32; gain and bias may be
+ * NULL. */
+int pbg_layernorm(int64_t rows, int32_t d, const void *x, int32_t x_bf16, const float *gain, const float *bias,
+                  float eps, void *y, int32_t y_bf16, void *stream);
+
 /* ---------------------------------------------------------- collective */
 
 /* replica.py:352-362 (all_reduce SUM of the flat fp32 gradient) over NVLink

@@ -517,6 +517,111 @@ def gen_posterior(out):
     out["cases"] = np.array(len(cases))
 
 
+def gen_preflop_model(out):
+    """preflop.py:472-693 (PreflopEncoder.forward) with shared.py's trunk and readout, fp32 on CPU.
+
+    The reference's accelerator guards (tensor_ops._accelerator, MHA.forward's device check) are
+    lifted for this run only; weights come from tests/golden/model_params.py by name.
+    """
+
+    import inspect
+    import textwrap
+
+    import torch
+    from pbg.core import tensor_ops
+    from pbg.games.poker.cards import DeckGeometry
+    from pbg.games.poker.model import primitives
+    from pbg.games.poker.model.preflop import (PackedPublicHistory, PokerModelConfig, PokerPublicBatch,
+                                               PreflopEncoder, PreflopMasks)
+    from pbg.games.poker.model.shared import SharedPokerParameters
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    import model_params
+
+    tensor_ops._accelerator = lambda value: None
+    source = textwrap.dedent(inspect.getsource(primitives.MHA.forward))
+    guard = 'if q.device.type not in ("cuda", "mps"):'
+    assert guard in source, "reference MHA.forward changed shape"
+    namespace: dict = {}
+    exec(compile(source.replace(guard, "if False:"), primitives.__file__, "exec"), primitives.__dict__, namespace)
+    primitives.MHA.forward = namespace["forward"]
+
+    cfg = PokerModelConfig(**model_params.CONFIG)
+    geometry = DeckGeometry(model_params.RANKS)
+    shared = SharedPokerParameters(cfg, geometry.n_cards)
+    encoder = PreflopEncoder(cfg, geometry)
+    with torch.no_grad():
+        for module in (shared, encoder):
+            for name, param in module.named_parameters():
+                param.copy_(torch.from_numpy(model_params.parameter(name, tuple(param.shape))))
+    g = torch.Generator().manual_seed(2024)
+    batch, players, tokens = 3, 2, 8
+    k = geometry.n_classes
+    history = PackedPublicHistory(
+        actor=torch.randint(-1, players, (batch, tokens), generator=g),
+        street=torch.randint(0, 4, (batch, tokens), generator=g),
+        action=torch.randint(0, 4, (batch, tokens), generator=g),
+        amount=torch.rand((batch, tokens), generator=g) * 4,
+        pot_before=torch.rand((batch, tokens), generator=g) * 6,
+        call_amount=torch.rand((batch, tokens), generator=g),
+        current_bet=torch.rand((batch, tokens), generator=g) * 2,
+        min_raise_to=torch.rand((batch, tokens), generator=g) * 2,
+        max_raise_to=torch.rand((batch, tokens), generator=g) * 8,
+        mask=torch.rand((batch, tokens), generator=g) < 0.7,
+    )
+    history.mask[:, 0] = True
+    pub = PokerPublicBatch(
+        street=torch.zeros(batch, dtype=torch.long),
+        board=torch.full((batch, 5), 255, dtype=torch.long),
+        pot=torch.rand(batch, generator=g) * 3 + 1.5,
+        stacks=torch.rand((batch, players), generator=g) * 8,
+        committed=torch.rand((batch, players), generator=g),
+        to_act=torch.randint(0, players, (batch,), generator=g),
+        legality_summary=torch.rand((batch, 4), generator=g),
+        n_ticks=torch.full((batch,), 16.0),
+        raise_grid_bounds=torch.rand((batch, 2), generator=g),
+        status=torch.randint(0, 3, (batch, players), generator=g),
+        seat_mask=torch.ones((batch, players), dtype=torch.bool),
+        button=torch.randint(0, players, (batch,), generator=g),
+        committed_street=torch.rand((batch, players), generator=g),
+        call_amount=torch.rand(batch, generator=g),
+        current_bet=torch.rand(batch, generator=g) * 2,
+        min_raise_to=torch.rand(batch, generator=g) * 2,
+        max_raise_to=torch.rand(batch, generator=g) * 8,
+        last_full_raise=torch.ones(batch),
+        legal_action_mask=torch.rand((batch, 6), generator=g) < 0.8,
+        raise_ticks=torch.rand((batch, 5), generator=g),
+        history=history,
+    )
+    ranges = torch.rand((batch, players, k), generator=g)
+    ranges[torch.rand(ranges.shape, generator=g) < 0.25] = 0.0
+    class_mask = torch.rand((batch, players, k), generator=g) < 0.9
+    masks = PreflopMasks(class_mask=class_mask)
+    with torch.no_grad():
+        result = encoder(shared, pub, ranges, None, masks)
+    for name in ("street", "board", "pot", "stacks", "committed", "to_act", "legality_summary", "n_ticks",
+                 "raise_grid_bounds", "status", "seat_mask", "button", "committed_street", "call_amount",
+                 "current_bet", "min_raise_to", "max_raise_to", "last_full_raise", "legal_action_mask",
+                 "raise_ticks"):
+        out["pub_" + name] = _np(getattr(pub, name))
+    for name in ("actor", "street", "action", "amount", "pot_before", "call_amount", "current_bet",
+                 "min_raise_to", "max_raise_to", "mask"):
+        out["hist_" + name] = _np(getattr(history, name))
+    out["class_ranges"] = _np(ranges)
+    out["class_mask"] = _np(class_mask)
+    for name, value in result.raw.items():
+        out["raw_" + name] = _np(value)
+    out["value"] = _np(result.v)
+    spec = []
+    for module in (shared, encoder):
+        for name, param in module.named_parameters():
+            spec.append(name + ":" + ",".join(str(n) for n in param.shape))
+    out["param_spec"] = np.array(spec)
+    out["class_sizes"] = _np(encoder.class_sizes)
+    out["class_card_geometry"] = _np(encoder.class_card_geometry)
+    out["class_overlap_scalars"] = _np(encoder.class_overlap_scalars)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="root of a pbg checkout")
@@ -533,6 +638,10 @@ def main() -> None:
         post_out = {}
         gen_posterior(post_out)
         outputs = (("posterior", post_out),)
+    elif only == {"preflop_model"}:
+        model_out = {}
+        gen_preflop_model(model_out)
+        outputs = (("preflop_model", model_out),)
     else:
         rng_out, poker_out, policy_out, loss_out, adam_out, ka_out = {}, {}, {}, {}, {}, {}
         gen_rng(rng_out)
