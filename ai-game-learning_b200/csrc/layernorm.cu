@@ -1,7 +1,8 @@
 // Row LayerNorm with learned gain and bias (pbg/core/tensor_ops.py LayerNorm,
 // F.layer_norm over the last dimension, eps as given): one warp per row, fp32
 // statistics (mean, then the centred second moment), input fp32 or bf16,
-// output bf16 (the next tensor-core map's operand) or fp32.
+// output bf16 (the next tensor-core map's operand) or fp32, written with its
+// own row stride (so it can fill a slice of a wider operand buffer).
 #include <cuda_bf16.h>
 
 #include "pbg_common.cuh"
@@ -10,7 +11,7 @@ namespace pbg {
 
 template <typename In, typename Out>
 __global__ void layernorm_kernel(int64_t rows, int d, const In* __restrict__ x, const float* __restrict__ gain,
-                                 const float* __restrict__ bias, float eps, Out* __restrict__ y) {
+                                 const float* __restrict__ bias, float eps, Out* __restrict__ y, int64_t ldy) {
     const int lane = threadIdx.x & 31;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= rows) return;
@@ -29,7 +30,7 @@ __global__ void layernorm_kernel(int64_t rows, int d, const In* __restrict__ x, 
     for (int i = 0; i < count; ++i) sq += (v[i] - mean) * (v[i] - mean);
     sq = warp_sum(sq);
     const float inv = rsqrtf(sq / (float)d + eps);
-    Out* yr = y + row * d;
+    Out* yr = y + row * ldy;
     count = 0;
     for (int c = lane; c < d; c += 32) {
         float t = (v[count++] - mean) * inv;
@@ -44,22 +45,24 @@ __global__ void layernorm_kernel(int64_t rows, int d, const In* __restrict__ x, 
 using namespace pbg;
 
 extern "C" int pbg_layernorm(int64_t rows, int32_t d, const void* x, int32_t x_bf16, const float* gain,
-                             const float* bias, float eps, void* y, int32_t y_bf16, void* stream) {
+                             const float* bias, float eps, void* y, int32_t y_bf16, int64_t ldy, void* stream) {
     PBG_REQUIRE(rows >= 0 && d >= 1 && d <= 1024, "layernorm: width must be in [1, 1024]");
+    PBG_REQUIRE(ldy >= d, "layernorm: output row stride must be at least the width");
     PBG_REQUIRE(rows == 0 || (x && y), "layernorm: null pointer");
     if (rows == 0) return 0;
     const unsigned blocks = (unsigned)((rows * 32 + 255) / 256);
     cudaStream_t s = as_stream(stream);
     if (x_bf16 && y_bf16)
         layernorm_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, 256, 0, s>>>(
-            rows, d, (const __nv_bfloat16*)x, gain, bias, eps, (__nv_bfloat16*)y);
+            rows, d, (const __nv_bfloat16*)x, gain, bias, eps, (__nv_bfloat16*)y, ldy);
     else if (x_bf16)
         layernorm_kernel<__nv_bfloat16, float><<<blocks, 256, 0, s>>>(rows, d, (const __nv_bfloat16*)x, gain, bias,
-                                                                      eps, (float*)y);
+                                                                      eps, (float*)y, ldy);
     else if (y_bf16)
         layernorm_kernel<float, __nv_bfloat16><<<blocks, 256, 0, s>>>(rows, d, (const float*)x, gain, bias, eps,
-                                                                      (__nv_bfloat16*)y);
+                                                                      (__nv_bfloat16*)y, ldy);
     else
-        layernorm_kernel<float, float><<<blocks, 256, 0, s>>>(rows, d, (const float*)x, gain, bias, eps, (float*)y);
+        layernorm_kernel<float, float><<<blocks, 256, 0, s>>>(rows, d, (const float*)x, gain, bias, eps, (float*)y,
+                                                              ldy);
     return launch_status("layernorm");
 }

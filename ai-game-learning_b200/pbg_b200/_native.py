@@ -110,7 +110,7 @@ SIGNATURES: dict[str, tuple] = {
                                    _I32, _I32, ctypes.c_float, _I32, _I32, _P, _P, _P]),
     "pbg_linear_bf16": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
     "pbg_attention_bf16": (_I32, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
-    "pbg_layernorm": (_I32, [_I64, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _I32, _P]),
+    "pbg_layernorm": (_I32, [_I64, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _I32, _I64, _P]),
     "pbg_nvls_signal_bytes": (_I64, []),
     "pbg_nvls_allreduce_sum_f32": (_I32, [_I64, _P, _P, _I64, _I32, _I32, _P, _P]),
     "pbg_adam_partials_size": (_I64, [_I64]),

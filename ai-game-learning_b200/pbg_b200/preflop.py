@@ -16,6 +16,7 @@ them) and the small elementwise steps are torch operations on the device.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -98,9 +99,11 @@ class _Map:
     def __call__(self, x: Tensor, activation: str | None = None) -> Tensor:
         lead = x.shape[:-1]
         rows = x.reshape(-1, x.shape[-1])
-        if self.kp != self.k:
+        if rows.dtype != torch.bfloat16:
+            rows = rows.to(torch.bfloat16)
+        if rows.shape[1] != self.kp:  # already padded operands (width kp) pass straight through
             rows = F.pad(rows, (0, self.kp - self.k))
-        y = linear(rows.to(torch.bfloat16).contiguous(), self.weight, self.bias, activation)
+        y = linear(rows if rows.is_contiguous() else rows.contiguous(), self.weight, self.bias, activation)
         if self.np_ != self.n:
             y = y[:, : self.n]
         return y.reshape(*lead, self.n)
@@ -169,13 +172,19 @@ class PreflopModel:
         self._factored: dict = {}
 
     # ------------------------------------------------------------ kernels
-    def _ln(self, x: Tensor, gain_bias) -> Tensor:
+    def _ln(self, x: Tensor, gain_bias, out: Tensor | None = None) -> Tensor:
+        """LayerNorm -> bf16, into `out` (rows of any stride, e.g. a slice of a wider operand) if given."""
+
         d = x.shape[-1]
         rows = x.reshape(-1, d).contiguous()
-        out = torch.empty(rows.shape, dtype=torch.bfloat16, device=x.device)
+        if out is None:
+            out = torch.empty(rows.shape, dtype=torch.bfloat16, device=x.device)
+            target, ldy = out, d
+        else:
+            target, ldy = out, out.stride(-2)
         call("pbg_layernorm", rows.shape[0], d, ptr(rows), int(rows.dtype == torch.bfloat16), ptr(gain_bias[0]),
-             ptr(gain_bias[1]), 1e-5, ptr(out), 1, stream(x.device))
-        return out.reshape(x.shape)
+             ptr(gain_bias[1]), 1e-5, ctypes.c_void_p(target.data_ptr()), 1, ldy, stream(x.device))
+        return out.reshape(x.shape) if out.is_contiguous() else out
 
     def _ffn(self, maps, x: Tensor) -> Tensor:
         return maps[1](maps[0](x, "gelu"))
@@ -308,20 +317,27 @@ class PreflopModel:
         incidence = self.class_card_geometry[None].expand(batch, -1, -1)
         identical_scale = (1.0 / self.class_sizes)[None].expand(batch, -1)
 
-        def pad_rows(value: Tensor) -> Tensor:
-            rows = value.reshape(batch, players * K, -1)
-            return F.pad(rows, (0, 0, 0, length - rows.shape[1]))
+        # FamilyFFN operand [LN(x_hat) | j, oc^2, oc*oe | side] in one bf16 buffer, padded to the map's K;
+        # the side features (fixed across layers) and the zero rows of non-class tokens are written once
+        rows_k = players * K
+        width = self.layers[0]["ffn_in"].kp if self.layers else 0
+        operand = torch.zeros((batch, length, width), dtype=torch.bfloat16, device=dev)
+        side_width = side_class.shape[-1]
+        operand[:, :rows_k, 4 * d: 4 * d + side_width] = side_class.reshape(batch, rows_k, side_width)
 
         for layer in self.layers:
-            row_state = x[:, : players * K].reshape(batch, players, K, d)
+            row_state = x[:, :rows_k].reshape(batch, players, K, d)
             j, oc, oe, _ = self._incidence(layer, row_state, normalized, incidence, identical_scale)
             nx = self._ln(x, layer["ln"])
             qkv = layer["w_qkv"](nx)
             attended = attention(qkv.contiguous(), cfg.n_heads, layer["q_scale"], key_bias, key_mask)
             x_hat = x + layer["w_o"](attended).float()
-            dynamic = torch.cat((j.float(), oc * oc, oc * oe), -1)
-            common = torch.cat((self._ln(x_hat, layer["ln"]).float(), pad_rows(dynamic)), -1)
-            hidden = layer["ffn_in"](torch.cat((common, pad_rows(side_class)), -1), "gelu")
+            self._ln(x_hat, layer["ln"], operand.view(batch * length, width)[:, :d])
+            dyn = operand[:, :rows_k, d: 4 * d].view(batch, players, K, 3, d)
+            dyn[..., 0, :] = j
+            dyn[..., 1, :] = oc * oc
+            dyn[..., 2, :] = oc * oe
+            hidden = layer["ffn_in"](operand, "gelu")
             x = x_hat + layer["ffn_out"](hidden).float()
 
         final = self._ln(x, self.final_ln).float()
@@ -361,4 +377,52 @@ class PreflopModel:
         return {"type_logits": self.type_head(z_type).float(), "omega": omega, "mu": mu, "s": s, "iota": iota}, value
 
 
-__all__ = ["PreflopConfig", "PreflopModel", "class_geometry"]
+def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int, ...]]:
+    """Names and shapes of the parameters PreflopModel binds (SharedPokerParameters, shared.py:36-72,
+    and PreflopEncoder, preflop.py:206-233), the state_dict names of the reference modules."""
+
+    d, dc, h = cfg.d_model, cfg.class_embedding_dim, cfg.hidden
+    n_cards = 4 * rank_count
+    pre = dc + 4 + n_cards
+    post = dc + 3 + n_cards + 4 * cfg.folder_beta_rank + 2 * d
+    readout = (2 + cfg.k_act) * d + dc
+    shapes: dict[str, tuple[int, ...]] = {
+        "state_token": (d,), "anchor_tokens": (cfg.k_act, d), "seat_embedding.weight": (cfg.max_players, d),
+        "status_embedding.weight": (3, d), "actor_embedding.weight": (2, d),
+        "public_scalar_affine.weight": (d, 1), "public_scalar_affine.bias": (d,),
+        "public_type_embedding.weight": (13, d), "history_numeric_affine.weight": (d, 6),
+        "history_numeric_affine.bias": (d,), "history_action_embedding.weight": (4, d),
+        "history_street_embedding.weight": (4, d), "history_position_embedding.weight": (cfg.max_history_tokens, d),
+        "anchor_seat_embedding.weight": (cfg.max_players, d),
+        "final_norm.weight": (d,), "final_norm.bias": (d,),
+        "class_embedding.weight": (rank_count * rank_count, dc),
+        "class_row_affine.weight": (d, dc + 4 + n_cards + 2), "class_row_affine.bias": (d,),
+        "type_head.affine.weight": (3, d), "type_head.affine.bias": (3,),
+        "raise_head.mixture_affine.weight": (3 * cfg.m_raise, d), "raise_head.mixture_affine.bias": (3 * cfg.m_raise,),
+        "raise_head.allin_affine.weight": (1, d), "raise_head.allin_affine.bias": (1,),
+        "value_head.affine.weight": (1, d), "value_head.affine.bias": (1,),
+    }
+    for i in range(cfg.layers):
+        shapes.update({
+            f"layer_norms.{i}.weight": (d,), f"layer_norms.{i}.bias": (d,),
+            f"attentions.{i}.theta": (cfg.n_heads,), f"attentions.{i}.w_qkv.weight": (3 * d, d),
+            f"attentions.{i}.w_qkv.bias": (3 * d,), f"attentions.{i}.w_o.weight": (d, d),
+            f"attentions.{i}.w_o.bias": (d,),
+            f"incidence_residuals.{i}.norm.weight": (d,), f"incidence_residuals.{i}.norm.bias": (d,),
+            f"incidence_residuals.{i}.source.weight": (d, d), f"incidence_residuals.{i}.query.weight": (d, d),
+            f"incidence_residuals.{i}.query.bias": (d,), f"incidence_residuals.{i}.identical.weight": (d, d),
+            f"incidence_residuals.{i}.own.weight": (d, d), f"incidence_residuals.{i}.output.weight": (d, d),
+            f"incidence_residuals.{i}.output.bias": (d,),
+            f"layer_ffns.{i}.common.weight": (h, 4 * d), f"layer_ffns.{i}.common.bias": (h,),
+            f"layer_ffns.{i}.static.pre.weight": (h, pre), f"layer_ffns.{i}.static.post.weight": (h, post),
+            f"layer_ffns.{i}.output.weight": (d, h), f"layer_ffns.{i}.output.bias": (d,),
+        })
+    for name, (fan_in, out) in {"actor_seat_features": (4 * d, d), "seat_features": (d + 3, d),
+                                "global_features": ((2 + cfg.max_players) * d, d), "type_features": (readout, d),
+                                "raise_features": (readout, d), "value_head.features": (readout, d)}.items():
+        shapes.update({f"{name}.w1.weight": (h, fan_in), f"{name}.w1.bias": (h,),
+                       f"{name}.w2.weight": (out, h), f"{name}.w2.bias": (out,)})
+    return shapes
+
+
+__all__ = ["PreflopConfig", "PreflopModel", "class_geometry", "parameter_shapes"]

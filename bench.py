@@ -454,6 +454,79 @@ def model_attention_component(device, batch=600, length=876, heads=8, reps=10):
             "kernel": "attention_kernel", "gpu_launches": 1}
 
 
+def preflop_forward_component(device, batch=256, players=2, history=16, reps=5):
+    """The preflop policy/value network forward (pbg_b200.preflop, the reference's default
+    PokerModelConfig: d_model 256, 8 heads, 6 layers, hidden 1024, R13 -> 169 class rows per seat)
+    for `batch` heads-up decisions with `history` public-history tokens; random weights of that
+    architecture, synthetic public batch.  Timed with CUDA events (host orchestration included)."""
+
+    import torch
+    from pbg_b200.preflop import PreflopConfig, PreflopModel, parameter_shapes
+
+    cfg = PreflopConfig()
+    g = torch.Generator().manual_seed(17)
+    params = {}
+    for name, shape in parameter_shapes(cfg, 13).items():
+        scale = (1.0 / shape[1] ** 0.5) if len(shape) == 2 and "embedding" not in name else 0.05
+        params[name] = torch.randn(shape, generator=g) * scale
+        if name.endswith("theta"):
+            params[name] = torch.full(shape, -0.4328)
+        if (name.startswith("layer_norms") or "norm.weight" in name) and name.endswith("weight"):
+            params[name] = torch.ones(shape)
+    model = PreflopModel(cfg, 13, params, device)
+    d = torch.Generator(device=device).manual_seed(18)
+    r = lambda *shape: torch.rand(shape, generator=d, device=device)  # noqa: E731
+    pub = {"street": torch.zeros(batch, dtype=torch.long, device=device),
+           "pot": r(batch) * 3, "stacks": r(batch, players) * 100, "committed": r(batch, players),
+           "to_act": torch.randint(0, players, (batch,), generator=d, device=device),
+           "legality_summary": r(batch, 4), "n_ticks": torch.full((batch,), 200.0, device=device),
+           "raise_grid_bounds": r(batch, 2), "status": torch.zeros((batch, players), dtype=torch.long, device=device),
+           "seat_mask": torch.ones((batch, players), dtype=torch.bool, device=device),
+           "button": torch.randint(0, players, (batch,), generator=d, device=device),
+           "committed_street": r(batch, players), "call_amount": r(batch), "current_bet": r(batch),
+           "min_raise_to": r(batch), "max_raise_to": r(batch) * 100, "last_full_raise": torch.ones(batch, device=device),
+           "history": {"actor": torch.randint(-1, players, (batch, history), generator=d, device=device),
+                       "street": torch.zeros((batch, history), dtype=torch.long, device=device),
+                       "action": torch.randint(0, 3, (batch, history), generator=d, device=device),
+                       "amount": r(batch, history), "pot_before": r(batch, history), "call_amount": r(batch, history),
+                       "current_bet": r(batch, history), "min_raise_to": r(batch, history),
+                       "max_raise_to": r(batch, history), "mask": r(batch, history) < 0.8}}
+    ranges = r(batch, players, 169)
+
+    def timed(fn):
+        times = []
+        for rep in range(reps + 2):
+            torch.cuda.synchronize(device)
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(device)
+            if rep >= 2:
+                times.append(a.elapsed_time(e))
+        return sorted(times)[len(times) // 2]
+
+    eager_ms = timed(lambda: model.forward(pub, ranges))
+    # the same forward captured once in a CUDA graph (every launch is on the current stream and
+    # nothing reads the device from the host), replayed without Python in between
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        model.forward(pub, ranges)
+    torch.cuda.current_stream(device).wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        model.forward(pub, ranges)
+    ms = timed(graph.replay)
+    del graph
+    tokens = players * 169 + 1 + 4 * players + 1 + 4 + 1 + 2 + 5 + history + 1 + cfg.k_act
+    return {"workload": f"preflop policy/value forward, default PokerModelConfig, R13 heads-up, {batch} decisions, "
+                        f"{tokens} tokens each", "ms": ms, "eager_ms": eager_ms, "launch": "CUDA graph replay",
+            "decisions_per_s": batch / (ms / 1000.0),
+            "class_rows_per_s": batch * 169 / (ms / 1000.0), "token_rows_per_s": batch * tokens / (ms / 1000.0),
+            "kernels": ["linear_tcgen05_kernel", "attention_kernel", "layernorm_kernel"]}
+
+
 def posterior_component(device, parents=4096, rows=16384, reps=10):
     """Collision-conditioned posterior profiles (rb_sampling.py): 6-max R13 (1326 private hands), `parents`
     parent rows of [6, 1326] fp32 range weights (board-conflicting hands masked; flop/turn/river boards),
@@ -706,6 +779,7 @@ def main():
                                   "layered_targets": targets_component(device),
                                   "model_linear": model_linear_component(device),
                                   "model_attention": model_attention_component(device),
+                                  "preflop_forward": preflop_forward_component(device),
                                   "posterior_sampler": posterior_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce

@@ -418,9 +418,9 @@ int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, const void *qk
 /* pbg/core/tensor_ops.py:70-81 (LayerNorm over the last dimension, d <= 1024):
  * y = (x - mean) / sqrt(var + eps) * gain + bias, fp32 statistics; x and y
  * are bf16 when x_bf16 / y_bf16 is nonzero, else fp32; gain and bias may be
- * NULL. */
+ * NULL; row i of y starts at y + i * ldy elements (ldy >= d). */
 int pbg_layernorm(int64_t rows, int32_t d, const void *x, int32_t x_bf16, const float *gain, const float *bias,
-                  float eps, void *y, int32_t y_bf16, void *stream);
+                  float eps, void *y, int32_t y_bf16, int64_t ldy, void *stream);
 
 /* ---------------------------------------------------------- collective */
 
