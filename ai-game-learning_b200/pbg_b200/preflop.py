@@ -142,9 +142,9 @@ class PreflopModel:
                 "ln": (p[f"layer_norms.{i}.weight"], p[f"layer_norms.{i}.bias"]),
                 "inc_ln": (p[f"{inc}.norm.weight"], p[f"{inc}.norm.bias"]),
                 "source": lin(f"{inc}.source", False),
-                "query": lin(f"{inc}.query"),
-                "identical": lin(f"{inc}.identical", False),
-                "own": lin(f"{inc}.own", False),
+                # query(n) + identical(other_equal) + own(own_card) as one map over [n | other_equal | own_card]
+                "inc_in": _Map(torch.cat((p[f"{inc}.query.weight"], p[f"{inc}.identical.weight"],
+                                          p[f"{inc}.own.weight"]), dim=1), p[f"{inc}.query.bias"], self.device),
                 "inc_out": lin(f"{inc}.output"),
                 "w_qkv": lin(f"{mha}.w_qkv"),
                 "w_o": lin(f"{mha}.w_o"),
@@ -184,7 +184,7 @@ class PreflopModel:
             target, ldy = out, out.stride(-2)
         call("pbg_layernorm", rows.shape[0], d, ptr(rows), int(rows.dtype == torch.bfloat16), ptr(gain_bias[0]),
              ptr(gain_bias[1]), 1e-5, ctypes.c_void_p(target.data_ptr()), 1, ldy, stream(x.device))
-        return out.reshape(x.shape) if out.is_contiguous() else out
+        return out.reshape(x.shape)  # a view also for a strided slice (only leading dimensions split)
 
     def _ffn(self, maps, x: Tensor) -> Tensor:
         return maps[1](maps[0](x, "gelu"))
@@ -256,7 +256,9 @@ class PreflopModel:
     def _incidence(self, layer, rows: Tensor, mass: Tensor, incidence: Tensor, identical_scale: Tensor):
         """incidence.py:30-84 (IncidenceResidual.forward)."""
 
-        normalized = self._ln(rows, layer["inc_ln"])
+        batch, players, k, d = rows.shape
+        operand = torch.empty((batch, players, k, 3 * d), dtype=torch.bfloat16, device=rows.device)
+        normalized = self._ln(rows, layer["inc_ln"], operand.view(-1, 3 * d)[:, :d])
         source = layer["source"](normalized).float() * mass.float()[..., None]
         card_acc = torch.einsum("brc,bprd->bpcd", incidence, source)
         card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc)
@@ -264,8 +266,9 @@ class PreflopModel:
         other_equal = same.sum(1, keepdim=True) - same
         other_card = card_overlap.sum(1, keepdim=True) - card_overlap - 2.0 * other_equal
         own_card = card_overlap - 2.0 * same
-        inner = (layer["query"](normalized).float() + other_card + layer["identical"](other_equal).float()
-                 + layer["own"](own_card).float())
+        operand[..., d: 2 * d] = other_equal
+        operand[..., 2 * d:] = own_card
+        inner = layer["inc_in"](operand).float() + other_card
         residual = layer["inc_out"](F.gelu(inner))
         return residual, other_card, other_equal, own_card
 
