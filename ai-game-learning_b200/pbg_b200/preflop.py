@@ -113,8 +113,13 @@ def _cat_maps(first: Tensor, second: Tensor) -> Tensor:
     return torch.cat((first, second), dim=1)
 
 
-class PreflopModel:
-    """Binds the reference's shared and encoder parameters (name -> tensor) to this build's kernels."""
+class FamilyModel:
+    """The shared trunk and readout (shared.py) bound to this build's kernels; a family adds its tokens.
+
+    ``family`` selects FamilyFFN's static adapter ("pre" or "post", shared.py:19-33).
+    """
+
+    family = "pre"
 
     def __init__(self, cfg: PreflopConfig, rank_count: int, params: dict[str, Tensor], device) -> None:
         if cfg.d_model != cfg.n_heads * 32:
@@ -122,15 +127,10 @@ class PreflopModel:
         self.cfg, self.device = cfg, torch.device(device)
         self.rank_count = rank_count
         self.n_cards = 4 * rank_count
-        self.n_classes = rank_count * rank_count
-        sizes, orbit, overlap = class_geometry(rank_count)
-        self.class_sizes = sizes.to(self.device)
-        self.class_card_geometry = orbit.to(self.device)
-        self.class_overlap_scalars = overlap.to(self.device)
         p = {k: v.to(self.device, torch.float32) for k, v in params.items()}
         self.p = p
         lin = lambda name, bias=True: _Map(p[name + ".weight"], p.get(name + ".bias") if bias else None, self.device)  # noqa: E731
-        self.class_row_affine = lin("class_row_affine")
+        self._lin = lin
         self.layers = []
         for i in range(cfg.layers):
             inc = f"incidence_residuals.{i}"
@@ -149,8 +149,8 @@ class PreflopModel:
                 "w_qkv": lin(f"{mha}.w_qkv"),
                 "w_o": lin(f"{mha}.w_o"),
                 "q_scale": (1.0 / (temperature * math.sqrt(32))).contiguous(),
-                # FamilyFFN (shared.py:19-33): common(x) + static[pre](s) as one map over [x, s]
-                "ffn_in": _Map(_cat_maps(p[f"{ffn}.common.weight"], p[f"{ffn}.static.pre.weight"]),
+                # FamilyFFN (shared.py:19-33): common(x) + static[family](s) as one map over [x, s]
+                "ffn_in": _Map(_cat_maps(p[f"{ffn}.common.weight"], p[f"{ffn}.static.{self.family}.weight"]),
                                p[f"{ffn}.common.bias"], self.device),
                 "ffn_out": lin(f"{ffn}.output"),
             })
@@ -200,6 +200,89 @@ class PreflopModel:
         row_map, ctx_map = self._factored[key]
         hidden = row_map(rows).float() + ctx_map(context).float()[:, None, :]
         return maps[1](F.gelu(hidden))
+
+    def _incidence(self, layer, rows: Tensor, mass: Tensor, incidence: Tensor, identical_scale: Tensor):
+        """incidence.py:30-84 (IncidenceResidual.forward)."""
+
+        batch, players, k, d = rows.shape
+        operand = torch.empty((batch, players, k, 3 * d), dtype=torch.bfloat16, device=rows.device)
+        normalized = self._ln(rows, layer["inc_ln"], operand.view(-1, 3 * d)[:, :d])
+        source = layer["source"](normalized).float() * mass.float()[..., None]
+        card_acc = torch.einsum("brc,bprd->bpcd", incidence, source)
+        card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc)
+        same = source * identical_scale[:, None, :, None]
+        other_equal = same.sum(1, keepdim=True) - same
+        other_card = card_overlap.sum(1, keepdim=True) - card_overlap - 2.0 * other_equal
+        own_card = card_overlap - 2.0 * same
+        operand[..., d: 2 * d] = other_equal
+        operand[..., 2 * d:] = own_card
+        inner = layer["inc_in"](operand).float() + other_card
+        residual = layer["inc_out"](F.gelu(inner))
+        return residual, other_card, other_equal, own_card
+
+    def _trunk(self, x: Tensor, players: int, rows_per_seat: int, mass: Tensor, incidence: Tensor,
+               identical_scale: Tensor, side: Tensor, key_bias: Tensor, key_mask: Tensor) -> Tensor:
+        """The shared layers (preflop.py:614-641 / postflop.py:658-685): incidence residual, LayerNorm,
+        biased attention, FamilyFFN over [LN(x_hat) | j, oc^2, oc*oe] and the family's side rows."""
+
+        cfg = self.cfg
+        d = cfg.d_model
+        batch, length, _ = x.shape
+        rows_k = players * rows_per_seat
+        # FamilyFFN operand [LN(x_hat) | j, oc^2, oc*oe | side] in one bf16 buffer, padded to the map's K;
+        # the side features (fixed across layers) and the zero rows of non-row tokens are written once
+        width = self.layers[0]["ffn_in"].kp if self.layers else 0
+        operand = torch.zeros((batch, length, width), dtype=torch.bfloat16, device=x.device)
+        side_width = side.shape[-1]
+        operand[:, :rows_k, 4 * d: 4 * d + side_width] = side.reshape(batch, rows_k, side_width)
+        for layer in self.layers:
+            row_state = x[:, :rows_k].reshape(batch, players, rows_per_seat, d)
+            j, oc, oe, _ = self._incidence(layer, row_state, mass, incidence, identical_scale)
+            nx = self._ln(x, layer["ln"])
+            qkv = layer["w_qkv"](nx)
+            attended = attention(qkv.contiguous(), cfg.n_heads, layer["q_scale"], key_bias, key_mask)
+            x_hat = x + layer["w_o"](attended).float()
+            self._ln(x_hat, layer["ln"], operand.view(batch * length, width)[:, :d])
+            dyn = operand[:, :rows_k, d: 4 * d].view(batch, players, rows_per_seat, 3, d)
+            dyn[..., 0, :] = j
+            dyn[..., 1, :] = oc * oc
+            dyn[..., 2, :] = oc * oe
+            hidden = layer["ffn_in"](operand, "gelu")
+            x = x_hat + layer["ffn_out"](hidden).float()
+        return x
+
+    def _readout(self, actor_rows: Tensor, private_embedding: Tensor, anchors: Tensor, global_feature: Tensor):
+        """shared.py:74-92 readout -> (raw policy fields, value)."""
+
+        cfg = self.cfg
+        rows = torch.cat((actor_rows, private_embedding), -1)
+        context = torch.cat((anchors.flatten(1), global_feature), -1)
+        z_type = self._ffn_factored(self.type_features, rows, context).float()
+        z_raise = self._ffn_factored(self.raise_features, rows, context).float()
+        raw = self.mixture_affine(z_raise).float()
+        m = cfg.m_raise
+        omega = torch.softmax(raw[..., :m], -1)
+        mu = torch.sigmoid(raw[..., m:2 * m])
+        s = F.softplus(raw[..., 2 * m:]) + cfg.s_min
+        iota = torch.sigmoid(self.allin_affine(z_type).float()).squeeze(-1)
+        value_features = self._ffn_factored(self.value_features, rows, context)
+        value = self.value_affine(value_features).float().squeeze(-1)
+        return {"type_logits": self.type_head(z_type).float(), "omega": omega, "mu": mu, "s": s, "iota": iota}, value
+
+
+class PreflopModel(FamilyModel):
+    """The preflop family (preflop.py): 169 class rows per seat, class geometry, class-row affine."""
+
+    family = "pre"
+
+    def __init__(self, cfg: PreflopConfig, rank_count: int, params: dict[str, Tensor], device) -> None:
+        super().__init__(cfg, rank_count, params, device)
+        self.class_row_affine = self._lin("class_row_affine")
+        self.n_classes = rank_count * rank_count
+        sizes, orbit, overlap = class_geometry(rank_count)
+        self.class_sizes = sizes.to(self.device)
+        self.class_card_geometry = orbit.to(self.device)
+        self.class_overlap_scalars = overlap.to(self.device)
 
     # ------------------------------------------------------------ forward
     def _public_tokens(self, pub, seat_mask: Tensor, relative_seats: Tensor):
@@ -253,25 +336,6 @@ class PreflopModel:
         return (torch.cat((token, state[:, None]), 1),
                 torch.cat((valid, torch.ones((batch, 1), dtype=torch.bool, device=dev)), 1))
 
-    def _incidence(self, layer, rows: Tensor, mass: Tensor, incidence: Tensor, identical_scale: Tensor):
-        """incidence.py:30-84 (IncidenceResidual.forward)."""
-
-        batch, players, k, d = rows.shape
-        operand = torch.empty((batch, players, k, 3 * d), dtype=torch.bfloat16, device=rows.device)
-        normalized = self._ln(rows, layer["inc_ln"], operand.view(-1, 3 * d)[:, :d])
-        source = layer["source"](normalized).float() * mass.float()[..., None]
-        card_acc = torch.einsum("brc,bprd->bpcd", incidence, source)
-        card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc)
-        same = source * identical_scale[:, None, :, None]
-        other_equal = same.sum(1, keepdim=True) - same
-        other_card = card_overlap.sum(1, keepdim=True) - card_overlap - 2.0 * other_equal
-        own_card = card_overlap - 2.0 * same
-        operand[..., d: 2 * d] = other_equal
-        operand[..., 2 * d:] = own_card
-        inner = layer["inc_in"](operand).float() + other_card
-        residual = layer["inc_out"](F.gelu(inner))
-        return residual, other_card, other_equal, own_card
-
     def forward(self, pub: dict, class_ranges: Tensor, class_mask: Tensor | None = None,
                 actor_seat: Tensor | None = None):
         """preflop.py:472-693 -> (raw policy fields, value [B, K])."""
@@ -320,29 +384,7 @@ class PreflopModel:
         incidence = self.class_card_geometry[None].expand(batch, -1, -1)
         identical_scale = (1.0 / self.class_sizes)[None].expand(batch, -1)
 
-        # FamilyFFN operand [LN(x_hat) | j, oc^2, oc*oe | side] in one bf16 buffer, padded to the map's K;
-        # the side features (fixed across layers) and the zero rows of non-class tokens are written once
-        rows_k = players * K
-        width = self.layers[0]["ffn_in"].kp if self.layers else 0
-        operand = torch.zeros((batch, length, width), dtype=torch.bfloat16, device=dev)
-        side_width = side_class.shape[-1]
-        operand[:, :rows_k, 4 * d: 4 * d + side_width] = side_class.reshape(batch, rows_k, side_width)
-
-        for layer in self.layers:
-            row_state = x[:, :rows_k].reshape(batch, players, K, d)
-            j, oc, oe, _ = self._incidence(layer, row_state, normalized, incidence, identical_scale)
-            nx = self._ln(x, layer["ln"])
-            qkv = layer["w_qkv"](nx)
-            attended = attention(qkv.contiguous(), cfg.n_heads, layer["q_scale"], key_bias, key_mask)
-            x_hat = x + layer["w_o"](attended).float()
-            self._ln(x_hat, layer["ln"], operand.view(batch * length, width)[:, :d])
-            dyn = operand[:, :rows_k, d: 4 * d].view(batch, players, K, 3, d)
-            dyn[..., 0, :] = j
-            dyn[..., 1, :] = oc * oc
-            dyn[..., 2, :] = oc * oe
-            hidden = layer["ffn_in"](operand, "gelu")
-            x = x_hat + layer["ffn_out"](hidden).float()
-
+        x = self._trunk(x, players, K, normalized, incidence, identical_scale, side_class, key_bias, key_mask)
         final = self._ln(x, self.final_ln).float()
         final_rows = final[:, : players * K].reshape(batch, players, K, d)
         final_public = final[:, players * K: -cfg.k_act]
@@ -364,20 +406,8 @@ class PreflopModel:
         global_feature = self._ffn(self.global_features,
                                    torch.cat((public_mean, actor_summary, padded.reshape(batch, -1)), -1)).float()
         actor_rows = final_rows[torch.arange(batch, device=dev), actor]
-        # shared.py:74-92 readout
-        rows = torch.cat((actor_rows, class_emb), -1)
-        context = torch.cat((final_anchors.flatten(1), global_feature), -1)
-        z_type = self._ffn_factored(self.type_features, rows, context).float()
-        z_raise = self._ffn_factored(self.raise_features, rows, context).float()
-        raw = self.mixture_affine(z_raise).float()
-        m = cfg.m_raise
-        omega = torch.softmax(raw[..., :m], -1)
-        mu = torch.sigmoid(raw[..., m:2 * m])
-        s = F.softplus(raw[..., 2 * m:]) + cfg.s_min
-        iota = torch.sigmoid(self.allin_affine(z_type).float()).squeeze(-1)
-        value_features = self._ffn_factored(self.value_features, rows, context)
-        value = self.value_affine(value_features).float().squeeze(-1)
-        return {"type_logits": self.type_head(z_type).float(), "omega": omega, "mu": mu, "s": s, "iota": iota}, value
+        return self._readout(actor_rows, class_emb, final_anchors, global_feature)
+
 
 
 def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int, ...]]:
@@ -428,4 +458,4 @@ def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int
     return shapes
 
 
-__all__ = ["PreflopConfig", "PreflopModel", "class_geometry", "parameter_shapes"]
+__all__ = ["FamilyModel", "PreflopConfig", "PreflopModel", "class_geometry", "parameter_shapes"]

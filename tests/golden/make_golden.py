@@ -622,6 +622,128 @@ def gen_preflop_model(out):
     out["class_overlap_scalars"] = _np(encoder.class_overlap_scalars)
 
 
+def gen_postflop_model(out):
+    """postflop.py:538-784 (PostflopEncoder.forward) with shared.py's trunk and readout, fp32 on CPU.
+
+    Three seats (one folded, so the folder context is live), a flop or turn board, the compact
+    board-compatible combo rows, and evaluator-summary fields of the shapes the encoder reads
+    (hand log ratios, beta eigenpairs, folder masses / single-card ratios / line metadata / seats,
+    tight-cluster scalar) drawn at random; accelerator guards lifted as for the preflop run.
+    """
+
+    import inspect
+    import textwrap
+
+    import torch
+    from pbg.core import tensor_ops
+    from pbg.games.poker.cards import DeckGeometry
+    from pbg.games.poker.model import primitives
+    from pbg.games.poker.model.postflop import PostflopEncoder, PostflopMasks
+    from pbg.games.poker.model.preflop import PackedPublicHistory, PokerModelConfig, PokerPublicBatch
+    from pbg.games.poker.model.shared import SharedPokerParameters
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    import model_params
+
+    tensor_ops._accelerator = lambda value: None
+    source = textwrap.dedent(inspect.getsource(primitives.MHA.forward))
+    guard = 'if q.device.type not in ("cuda", "mps"):'
+    if guard in source:
+        namespace: dict = {}
+        exec(compile(source.replace(guard, "if False:"), primitives.__file__, "exec"), primitives.__dict__, namespace)
+        primitives.MHA.forward = namespace["forward"]
+
+    cfg = PokerModelConfig(**model_params.POSTFLOP_CONFIG)
+    geometry = DeckGeometry(model_params.RANKS)
+    shared = SharedPokerParameters(cfg, geometry.n_cards)
+    encoder = PostflopEncoder(cfg, geometry)
+    with torch.no_grad():
+        for module in (shared, encoder):
+            for name, param in module.named_parameters():
+                param.copy_(torch.from_numpy(model_params.parameter(name, tuple(param.shape))))
+    g = torch.Generator().manual_seed(4048)
+    batch, players, tokens, folders = 3, 3, 6, 2
+    deck, first, hands = geometry.n_cards, geometry.first_card, geometry.n_hands
+    combos = torch.tensor(geometry.combo_cards, dtype=torch.long)
+    board = torch.full((batch, 5), -1, dtype=torch.long)
+    compat = torch.ones((batch, hands), dtype=torch.bool)
+    for b in range(batch):
+        shown = [3, 4, 3][b]
+        cards = torch.randperm(deck, generator=g)[:shown] + first
+        board[b, :shown] = cards
+        compat[b] = ~(combos[:, :, None] == cards[None, None, :]).any(-1).any(-1)
+    compact_size = int(compat.sum(1).max())
+    status = torch.zeros((batch, players), dtype=torch.long)
+    status[:, 2] = 1  # seat 2 folded
+    to_act = torch.tensor([0, 1, 0])
+    history = PackedPublicHistory(
+        actor=torch.randint(-1, players, (batch, tokens), generator=g),
+        street=torch.randint(0, 4, (batch, tokens), generator=g),
+        action=torch.randint(0, 4, (batch, tokens), generator=g),
+        amount=torch.rand((batch, tokens), generator=g) * 4,
+        pot_before=torch.rand((batch, tokens), generator=g) * 6,
+        call_amount=torch.rand((batch, tokens), generator=g),
+        current_bet=torch.rand((batch, tokens), generator=g) * 2,
+        min_raise_to=torch.rand((batch, tokens), generator=g) * 2,
+        max_raise_to=torch.rand((batch, tokens), generator=g) * 8,
+        mask=torch.rand((batch, tokens), generator=g) < 0.7,
+    )
+    history.mask[:, 0] = True
+    pub = PokerPublicBatch(
+        street=torch.ones(batch, dtype=torch.long), board=board, pot=torch.rand(batch, generator=g) * 3 + 1.5,
+        stacks=torch.rand((batch, players), generator=g) * 8, committed=torch.rand((batch, players), generator=g),
+        to_act=to_act, legality_summary=torch.rand((batch, 4), generator=g), n_ticks=torch.full((batch,), 16.0),
+        raise_grid_bounds=torch.rand((batch, 2), generator=g), status=status,
+        seat_mask=torch.ones((batch, players), dtype=torch.bool), button=torch.randint(0, players, (batch,), generator=g),
+        committed_street=torch.rand((batch, players), generator=g), call_amount=torch.rand(batch, generator=g),
+        current_bet=torch.rand(batch, generator=g), min_raise_to=torch.rand(batch, generator=g),
+        max_raise_to=torch.rand(batch, generator=g) * 8, last_full_raise=torch.ones(batch),
+        legal_action_mask=torch.rand((batch, 6), generator=g) < 0.8, raise_ticks=torch.rand((batch, 5), generator=g),
+        history=history,
+    )
+    ranges = torch.rand((batch, players, hands), generator=g)
+    rank = 3
+    eigvec = torch.randn((batch, deck, rank), generator=g)
+    summary = {
+        "hand_log_ratio": torch.randn((batch, hands), generator=g) * 0.3,
+        "beta_eigenvalue": torch.randn((batch, rank), generator=g),
+        "beta_eigenvector": eigvec / eigvec.norm(dim=1, keepdim=True),
+        "folder_log_mass": -torch.rand((batch, folders), generator=g),
+        "folder_single_card_log_ratio": -torch.rand((batch, folders, deck), generator=g) * 0.5,
+        "folder_line_meta": torch.rand((batch, folders, cfg.folder_line_dim), generator=g),
+        "folder_mask": torch.tensor([[True, False], [True, True], [True, False]]),
+        "folder_seat": torch.full((batch, folders), 2, dtype=torch.long),
+        "tight_cluster_scalar": torch.rand(batch, generator=g),
+    }
+    fold_lines = torch.rand((batch, folders, cfg.folder_line_dim), generator=g)
+    masks = PostflopMasks(compatibility=compat, evaluator_summary=summary, fold_line_features=fold_lines,
+                          compact_size=compact_size)
+    with torch.no_grad():
+        result = encoder(shared, pub, ranges, None, masks)
+    for name in ("street", "board", "pot", "stacks", "committed", "to_act", "legality_summary", "n_ticks",
+                 "raise_grid_bounds", "status", "seat_mask", "button", "committed_street", "call_amount",
+                 "current_bet", "min_raise_to", "max_raise_to", "last_full_raise", "legal_action_mask",
+                 "raise_ticks"):
+        out["pub_" + name] = _np(getattr(pub, name))
+    for name in ("actor", "street", "action", "amount", "pot_before", "call_amount", "current_bet",
+                 "min_raise_to", "max_raise_to", "mask"):
+        out["hist_" + name] = _np(getattr(history, name))
+    for name, value in summary.items():
+        out["summary_" + name] = _np(value)
+    out["combo_ranges"] = _np(ranges)
+    out["compatibility"] = _np(compat)
+    out["fold_line_features"] = _np(fold_lines)
+    out["compact_size"] = np.array(compact_size)
+    for name, value in result.raw.items():
+        out["raw_" + name] = _np(value)
+    out["value"] = _np(result.v)
+    spec = []
+    for module in (shared, encoder):
+        for name, param in module.named_parameters():
+            spec.append(name + ":" + ",".join(str(n) for n in param.shape))
+    out["param_spec"] = np.array(spec)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="root of a pbg checkout")
@@ -642,6 +764,10 @@ def main() -> None:
         model_out = {}
         gen_preflop_model(model_out)
         outputs = (("preflop_model", model_out),)
+    elif only == {"postflop_model"}:
+        model_out = {}
+        gen_postflop_model(model_out)
+        outputs = (("postflop_model", model_out),)
     else:
         rng_out, poker_out, policy_out, loss_out, adam_out, ka_out = {}, {}, {}, {}, {}, {}
         gen_rng(rng_out)

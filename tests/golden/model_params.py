@@ -37,3 +37,6 @@ def parameter(name: str, shape: tuple[int, ...]) -> np.ndarray:
     else:
         value = rng.normal(0.0, 0.05, shape)
     return _bf16_round(np.asarray(value, dtype=np.float32))
+
+# the postflop run has three seats (one folded), so the table holds up to three players
+POSTFLOP_CONFIG = dict(CONFIG, max_players=3)
