@@ -89,6 +89,45 @@ class NLHEGeometry:
     def c(self) -> N.Geometry:
         return N.Geometry(self.players, self.stack_ticks, self.rank_count)
 
+    @property
+    def public_model_input_width(self) -> int:
+        return 8 + 10 * self.players
+
+    @property
+    def history_model_input_width(self) -> int:
+        return 10 * self.history_tokens
+
+    @property
+    def preflop_model_input_width(self) -> int:
+        return self.public_model_input_width + self.players * self.private_classes + self.history_model_input_width
+
+    @property
+    def postflop_base_model_input_width(self) -> int:
+        return self.public_model_input_width + self.players * self.private_hands + self.history_model_input_width
+
+    @property
+    def folded_summary_width(self) -> int:
+        """hooks.py:171-185: Lambda_B [H], full-rank beta eigenpairs [C + C*C], folder log masses [P],
+        card masses [P*C], tight scalar and validity flag; none heads-up (a fold is terminal)."""
+
+        if self.players == 2:
+            return 0
+        cards = self.deck_cards
+        return self.private_hands + cards + cards * cards + self.players + self.players * cards + 2
+
+    @property
+    def postflop_model_input_width(self) -> int:
+        return self.postflop_base_model_input_width + self.folded_summary_width
+
+    def model_input_width(self, input_type: str) -> int:
+        """hooks.py:157-162."""
+
+        if input_type == "pre":
+            return self.preflop_model_input_width
+        if input_type.startswith("post_") and input_type[5:].isdigit():
+            return self.postflop_model_input_width
+        raise ValueError(f"unknown poker input partition {input_type!r}")
+
     def combo_id(self, first: Tensor, second: Tensor) -> Tensor:
         low = torch.minimum(first, second).to(torch.int64) - self.first_card
         high = torch.maximum(first, second).to(torch.int64) - self.first_card
@@ -307,15 +346,7 @@ class PokerStateMachine:
     def model_input_width(self, input_type: str) -> int:
         """hooks.py:138-169: retained row width of a partition."""
 
-        g = self.geometry
-        P, D, H, K = g.players, g.deck_cards, g.private_hands, g.private_classes
-        base = 8 + 10 * P + 10 * g.history_tokens
-        if input_type == "pre":
-            return base + P * K
-        if input_type.startswith("post_") and input_type[5:].isdigit():
-            folded = 0 if P == 2 else H + D + D * D + P + P * D + 2
-            return base + P * H + folded
-        raise ValueError(f"unknown poker input partition {input_type!r}")
+        return self.geometry.model_input_width(input_type)
 
     def direct_model_input(self, input_type: str, state: PokerState, log_reach: Tensor | None = None,
                            history: PokerHistory | None = None) -> Tensor:

@@ -25,6 +25,7 @@ import torch
 from torch import Tensor
 from torch.nn import functional as F
 
+from .checks import _assert, input_errors, raise_input_errors
 from .preflop import FamilyModel, PreflopConfig
 
 
@@ -62,15 +63,6 @@ class CompactMap:
     @property
     def full_size(self) -> int:
         return self.full_to_compact.shape[1]
-
-
-def _assert(condition: Tensor, message: str) -> None:
-    """primitives.py:15-21: an asynchronous device check on CUDA, a ValueError elsewhere."""
-
-    if condition.device.type == "cuda":
-        torch._assert_async(condition, message)
-    elif not bool(condition):
-        raise ValueError(message)
 
 
 def build_compact_map(compatibility: Tensor, compact_size: int | None = None) -> CompactMap:
@@ -293,7 +285,7 @@ class PostflopModel(FamilyModel):
             safe_seat = seat.to(device=dev, dtype=torch.long).clamp(0, players - 1)
             seat_context = seat_context.scatter_add(1, safe_seat[..., None].expand(-1, -1, d), context + folder_pool)
         board_ordinal = (board - self.first_card).clamp(0, self.n_cards - 1).long()
-        on_board = F.one_hot(board_ordinal, self.n_cards).bool() & (board >= 0)[..., None]
+        on_board = (board_ordinal[..., None] == torch.arange(self.n_cards, device=dev)) & (board >= 0)[..., None]
         available = ~on_board.any(1)
         real = (board >= 0).sum(1)
         uniform = available.float() * (2.0 / (self.n_cards - real).float())[:, None]
@@ -568,4 +560,4 @@ def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int
 
 
 __all__ = ["CompactMap", "PostflopMasks", "PostflopModel", "build_compact_map", "compact_gather",
-           "compact_scatter", "parameter_shapes"]
+           "compact_scatter", "input_errors", "parameter_shapes", "raise_input_errors"]

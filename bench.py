@@ -45,6 +45,9 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--profile-forward", choices=("preflop", "postflop"), default=None,
+                   help="run one eager forward of that component between cudaProfilerStart/Stop (for ncu "
+                        "--profile-from-start off) after two warm-up forwards, print nothing else, exit")
     return p.parse_args()
 
 
@@ -464,19 +467,83 @@ def preflop_forward_component(device, batch=256, players=2, history=16, reps=5):
     from pbg_b200.preflop import PreflopConfig, PreflopModel, parameter_shapes
 
     cfg = PreflopConfig()
-    g = torch.Generator().manual_seed(17)
+    model = PreflopModel(cfg, 13, _random_params(parameter_shapes(cfg, 13)), device)
+    pub = _synthetic_pub(device, batch, players, history, street=0)
+    d = torch.Generator(device=device).manual_seed(19)
+    ranges = torch.rand((batch, players, 169), generator=d, device=device)
+    ms, eager_ms = _time_forward(device, lambda: model.forward(pub, ranges), reps)
+    tokens = players * 169 + 1 + 4 * players + 1 + 4 + 1 + 2 + 5 + history + 1 + cfg.k_act
+    return {"workload": f"preflop policy/value forward, default PokerModelConfig, R13 heads-up, {batch} decisions, "
+                        f"{tokens} tokens each", "ms": ms, "eager_ms": eager_ms, "launch": "CUDA graph replay",
+            "decisions_per_s": batch / (ms / 1000.0),
+            "class_rows_per_s": batch * 169 / (ms / 1000.0), "token_rows_per_s": batch * tokens / (ms / 1000.0),
+            "kernels": ["linear_tcgen05_kernel", "attention_kernel", "layernorm_kernel"]}
+
+
+def postflop_forward_component(device, batch=24, players=2, history=16, reps=5):
+    """The compact postflop policy/value network forward (pbg_b200.postflop, default PokerModelConfig,
+    R13) for `batch` heads-up flop decisions: 1,176 board-compatible combo rows per live seat, evaluator
+    summary with hand log ratios and rank-16 beta eigenpairs; random weights of that architecture,
+    synthetic public batch.  Timed with CUDA events over CUDA-graph replay (and eagerly)."""
+
+    import torch
+    from pbg_b200.postflop import PostflopMasks, PostflopModel, input_errors, parameter_shapes
+    from pbg_b200.preflop import PreflopConfig
+
+    cfg = PreflopConfig()
+    model = PostflopModel(cfg, 13, _random_params(parameter_shapes(cfg, 13)), device)
+    pub = _synthetic_pub(device, batch, players, history, street=1)
+    g = torch.Generator().manual_seed(20)
+    hands = 1326
+    combos = torch.combinations(torch.arange(52), 2)
+    board = torch.stack([torch.randperm(52, generator=g)[:3] for _ in range(batch)])
+    pub["board"] = torch.cat((board, torch.full((batch, 2), -1, dtype=torch.long)), 1).to(device)
+    compat = ~(combos[None, :, :, None] == board[:, None, None, :]).any(-1).any(-1)
+    compact = 1176
+    vector = torch.randn((batch, 52, 16), generator=g)
+    summary = {"hand_log_ratio": torch.randn((batch, hands), generator=g).to(device) * 0.3,
+               "beta_eigenvalue": torch.randn((batch, 16), generator=g).to(device),
+               "beta_eigenvector": (vector / vector.norm(dim=1, keepdim=True)).to(device)}
+    masks = PostflopMasks(compatibility=compat.to(device), evaluator_summary=summary, compact_size=compact)
+    ranges = torch.rand((batch, players, hands), generator=g).to(device)
+    ms, eager_ms = _time_forward(device, lambda: model.forward(pub, ranges, None, masks), reps)
+    if input_errors(device):
+        raise RuntimeError("postflop bench inputs failed the encoder's checks")
+    tokens = players * compact + 1 + 1 + 4 * players + 1 + 4 + 1 + 2 + 5 + 3 + 5 + history + cfg.k_act
+    return {"workload": f"postflop policy/value forward, default PokerModelConfig, R13 heads-up flop, {batch} "
+                        f"decisions, {players} x {compact} compact combo rows, {tokens} tokens each", "ms": ms,
+            "eager_ms": eager_ms, "launch": "CUDA graph replay", "decisions_per_s": batch / (ms / 1000.0),
+            "combo_rows_per_s": batch * players * compact / (ms / 1000.0),
+            "token_rows_per_s": batch * tokens / (ms / 1000.0),
+            "kernels": ["linear_tcgen05_kernel", "attention_kernel", "layernorm_kernel"]}
+
+
+def _random_params(shapes: dict, seed: int = 17) -> dict:
+    """Random weights of the given architecture: N(0, 1/fan_in) maps, N(0, 0.05) vectors, unit LayerNorm
+    gains, temperatures 1 (theta = log(expm1(0.5)))."""
+
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
     params = {}
-    for name, shape in parameter_shapes(cfg, 13).items():
+    for name, shape in shapes.items():
         scale = (1.0 / shape[1] ** 0.5) if len(shape) == 2 and "embedding" not in name else 0.05
         params[name] = torch.randn(shape, generator=g) * scale
         if name.endswith("theta"):
             params[name] = torch.full(shape, -0.4328)
         if (name.startswith("layer_norms") or "norm.weight" in name) and name.endswith("weight"):
             params[name] = torch.ones(shape)
-    model = PreflopModel(cfg, 13, params, device)
+    return params
+
+
+def _synthetic_pub(device, batch: int, players: int, history: int, street: int) -> dict:
+    """A seeded public batch (PokerPublicBatch fields, preflop.py:104-170) of the given shape."""
+
+    import torch
+
     d = torch.Generator(device=device).manual_seed(18)
     r = lambda *shape: torch.rand(shape, generator=d, device=device)  # noqa: E731
-    pub = {"street": torch.zeros(batch, dtype=torch.long, device=device),
+    return {"street": torch.full((batch,), street, dtype=torch.long, device=device),
            "pot": r(batch) * 3, "stacks": r(batch, players) * 100, "committed": r(batch, players),
            "to_act": torch.randint(0, players, (batch,), generator=d, device=device),
            "legality_summary": r(batch, 4), "n_ticks": torch.full((batch,), 200.0, device=device),
@@ -491,7 +558,26 @@ def preflop_forward_component(device, batch=256, players=2, history=16, reps=5):
                        "amount": r(batch, history), "pot_before": r(batch, history), "call_amount": r(batch, history),
                        "current_bet": r(batch, history), "min_raise_to": r(batch, history),
                        "max_raise_to": r(batch, history), "mask": r(batch, history) < 0.8}}
-    ranges = r(batch, players, 169)
+
+
+PROFILE_ONE_FORWARD = False
+
+
+def _time_forward(device, forward, reps: int):
+    """Median CUDA-event time (ms) of a forward replayed from a CUDA graph, and of the eager forward.
+    With PROFILE_ONE_FORWARD: two warm-up forwards, then one between cudaProfilerStart/Stop (no timing)."""
+
+    import torch
+
+    if PROFILE_ONE_FORWARD:
+        forward()
+        forward()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.start()
+        forward()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.stop()
+        return float("nan"), float("nan")
 
     def timed(fn):
         times = []
@@ -506,25 +592,20 @@ def preflop_forward_component(device, batch=256, players=2, history=16, reps=5):
                 times.append(a.elapsed_time(e))
         return sorted(times)[len(times) // 2]
 
-    eager_ms = timed(lambda: model.forward(pub, ranges))
+    eager_ms = timed(forward)
     # the same forward captured once in a CUDA graph (every launch is on the current stream and
     # nothing reads the device from the host), replayed without Python in between
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(stream):
-        model.forward(pub, ranges)
+        forward()
     torch.cuda.current_stream(device).wait_stream(stream)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        model.forward(pub, ranges)
+        forward()
     ms = timed(graph.replay)
     del graph
-    tokens = players * 169 + 1 + 4 * players + 1 + 4 + 1 + 2 + 5 + history + 1 + cfg.k_act
-    return {"workload": f"preflop policy/value forward, default PokerModelConfig, R13 heads-up, {batch} decisions, "
-                        f"{tokens} tokens each", "ms": ms, "eager_ms": eager_ms, "launch": "CUDA graph replay",
-            "decisions_per_s": batch / (ms / 1000.0),
-            "class_rows_per_s": batch * 169 / (ms / 1000.0), "token_rows_per_s": batch * tokens / (ms / 1000.0),
-            "kernels": ["linear_tcgen05_kernel", "attention_kernel", "layernorm_kernel"]}
+    return ms, eager_ms
 
 
 def posterior_component(device, parents=4096, rows=16384, reps=10):
@@ -592,6 +673,11 @@ def main():
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.profile_forward:
+        global PROFILE_ONE_FORWARD
+        PROFILE_ONE_FORWARD = True
+        globals()[f"{args.profile_forward}_forward_component"](device)
+        return
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
@@ -780,6 +866,7 @@ def main():
                                   "model_linear": model_linear_component(device),
                                   "model_attention": model_attention_component(device),
                                   "preflop_forward": preflop_forward_component(device),
+                                  "postflop_forward": postflop_forward_component(device),
                                   "posterior_sampler": posterior_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce

@@ -338,6 +338,23 @@ int pbg_alias_table(int64_t n, double *scaled, double *probability, int32_t *ali
 int pbg_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *degree, float *log_mass,
                           int32_t *failure, void *workspace, void *stream);
 
+/* ------------------------------------------- multiway folded statistics */
+
+/* Removal queries of one decision row for a deck of `cards` cards: 1 + C + C(C-1)/2
+ * (pbg/games/poker/queued/folded.py:81-92), or -1 outside [2, 52]. */
+int64_t pbg_folded_query_count(int32_t cards);
+
+/* pbg/games/poker/queued/folded.py:111-232 (_phi_queries over every removal
+ * query, called in chunks at folded.py:313-327): probability f32 [B,P,H]
+ * (each folded seat's normalised, board-masked range; zero for other seats),
+ * folder_mask / tight_mask u8 [B,P], base_cards f32 [B] (deck cards minus
+ * board cards) -> phi f32 [B,Q] (phi + triple, as _phi_queries returns it)
+ * and triple f32 [B,Q].  P <= 6, cards = 4R <= 52, H = C(C-1)/2; fp32 within
+ * rounding of the reference's own fp32 evaluation. */
+int pbg_folded_phi_queries(int64_t batch, int32_t players, int32_t cards, const float *probability,
+                           const uint8_t *folder_mask, const uint8_t *tight_mask, const float *base_cards,
+                           float *phi, float *triple, void *stream);
+
 /* ------------------------------------------------------- layered targets */
 
 /* Device tables of per-partition arena pointers (int64 device addresses, 0 =

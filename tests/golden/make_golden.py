@@ -744,6 +744,93 @@ def gen_postflop_model(out):
     out["param_spec"] = np.array(spec)
 
 
+FOLDED_CASES = (
+    # (players, stack, ranks, batch, folded seats per row, tight seats per row, board cards per row, line_dim, beta_rank)
+    (3, 8.0, 4, 3, ((2,), (1,), (0, 2)), ((2,), (), (0, 2)), (3, 4, 5), 3, 4),
+    (4, 8.0, 4, 2, ((1, 2, 3), (0, 2, 3)), ((1, 2, 3), (0, 3)), (3, 5), 0, 16),
+    (6, 8.0, 5, 2, ((1, 2, 4, 5), (0, 1, 3)), ((1, 2, 4, 5), (0, 1, 3)), (4, 3), 0, 20),
+    (6, 100.0, 13, 1, ((0, 2, 3, 5),), ((0, 2, 3, 5),), (3,), 0, 52),
+)
+
+
+def gen_folded(out):
+    """folded.py:235-460 (_folded_statistics_fp32 and its _phi_queries finite-difference queries) on CPU.
+
+    Four geometries (3-, 4- and 6-handed, R4 / R5 / R13) with one to four folded seats, tight-folder
+    subsets, flop / turn / river boards, random ranges with zeros, a negative and a non-finite entry;
+    the per-query phi and triple terms are recorded from inside the reference call.  The reference's
+    one device-type test (folded.py:251) is lifted for this run.
+    """
+
+    import torch
+    from pbg.games.poker.queued import folded
+    from pbg.games.poker.queued.hooks import FOLDED, PAD_CARD, NLHEGeometry, PokerStateMachine
+
+    source = textwrap.dedent(inspect.getsource(folded._folded_statistics_fp32))
+    guard = 'board_cards.device.type != "cuda"'
+    assert guard in source, "reference folded statistics changed shape"
+    namespace: dict = {}
+    exec(compile(source.replace(guard, "False"), folded.__file__, "exec"), folded.__dict__, namespace)
+    folded._folded_statistics_fp32 = namespace["_folded_statistics_fp32"]
+    recorded = []
+    original = folded._phi_queries
+
+    def recording(*args, **kwargs):
+        result = original(*args, **kwargs)
+        recorded.append(result)
+        return result
+
+    folded._phi_queries = recording
+    g = torch.Generator().manual_seed(5150)
+    for index, (players, stack, ranks, batch, folds, tights, shown, line_dim, beta_rank) in enumerate(FOLDED_CASES):
+        geometry = NLHEGeometry(players, stack, ranks)
+        machine = PokerStateMachine(geometry)
+        hands, cards = geometry.private_hands, geometry.deck_cards
+        combo = machine.combo_cards(torch.arange(hands, dtype=torch.int32))
+        board = torch.full((batch, 5), PAD_CARD, dtype=torch.uint8)
+        status = torch.zeros((batch, players), dtype=torch.int8)
+        tight = torch.zeros((batch, players), dtype=torch.bool)
+        for b in range(batch):
+            board[b, : shown[b]] = (torch.randperm(cards, generator=g)[: shown[b]] + geometry.first_card).to(torch.uint8)
+            status[b, list(folds[b])] = FOLDED
+            tight[b, list(tights[b])] = True
+        weights = torch.rand((batch, players, hands), generator=g)
+        weights = weights * (torch.rand((batch, players, hands), generator=g) > 0.2)
+        weights[0, 0, 3] = -0.5
+        weights[0, -1, 5] = float("inf")
+        weights[-1, 1, 7] = float("nan")
+        line = torch.rand((batch, players, line_dim), generator=g) if line_dim else None
+        recorded.clear()
+        result = folded.folded_statistics(geometry, board_cards=board, range_weights=weights, status=status,
+                                          combo_cards=combo, beta_rank=beta_rank, line_dim=line_dim,
+                                          line_metadata=line, tight_mask=tight)
+        prefix = f"c{index}_"
+        out[prefix + "geometry"] = np.array([players, stack, ranks, beta_rank, line_dim], dtype=np.float64)
+        out[prefix + "board_cards"] = _np(board)
+        out[prefix + "range_weights"] = _np(weights)
+        out[prefix + "status"] = _np(status)
+        out[prefix + "tight_mask"] = _np(tight)
+        if line is not None:
+            out[prefix + "line_metadata"] = _np(line)
+        out[prefix + "phi"] = _np(torch.cat([r[0] for r in recorded], 1))
+        out[prefix + "triple"] = _np(torch.cat([r[1] for r in recorded], 1))
+        for name, value in result.items():
+            out[prefix + name] = _np(value)
+        if beta_rank == cards:  # the retained-row layout holds the full-rank eigenpairs (hooks.py:1983-1997)
+            out[prefix + "packed"] = _np(folded.pack_folded_statistics(geometry, result))
+    out["workspace_row_bytes"] = np.array([folded.folded_statistics_workspace_row_bytes(NLHEGeometry(*c[:3]))
+                                           for c in FOLDED_CASES] +
+                                          [folded.folded_statistics_workspace_row_bytes(NLHEGeometry(6, 128.0, 13))])
+    out["family_workspace_row_bytes"] = np.array([folded.sequential_family_workspace_row_bytes(NLHEGeometry(*c[:3]), 4)
+                                                  for c in FOLDED_CASES] +
+                                                 [folded.sequential_family_workspace_row_bytes(NLHEGeometry(6, 128.0, 13), 4)])
+    folded._phi_queries = original
+
+
+GENERATORS = {"posterior": gen_posterior, "preflop_model": gen_preflop_model, "postflop_model": gen_postflop_model,
+              "folded": gen_folded}
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="root of a pbg checkout")
@@ -756,18 +843,12 @@ def main() -> None:
     torch.manual_seed(0)
     _install_shims()
     only = set(args.only.split(",")) if args.only else None
-    if only == {"posterior"}:
-        post_out = {}
-        gen_posterior(post_out)
-        outputs = (("posterior", post_out),)
-    elif only == {"preflop_model"}:
-        model_out = {}
-        gen_preflop_model(model_out)
-        outputs = (("preflop_model", model_out),)
-    elif only == {"postflop_model"}:
-        model_out = {}
-        gen_postflop_model(model_out)
-        outputs = (("postflop_model", model_out),)
+    if only is not None and only <= set(GENERATORS):
+        outputs = []
+        for name in sorted(only):
+            data: dict = {}
+            GENERATORS[name](data)
+            outputs.append((name, data))
     else:
         rng_out, poker_out, policy_out, loss_out, adam_out, ka_out = {}, {}, {}, {}, {}, {}
         gen_rng(rng_out)

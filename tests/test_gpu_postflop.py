@@ -63,6 +63,9 @@ def test_postflop_forward_matches_reference_module(gold):
     pub, ranges, masks = _inputs(d)
     raw, value = model.forward(pub, ranges, None, masks)
     torch.cuda.synchronize()
+    from pbg_b200.postflop import input_errors
+
+    assert input_errors(DEV) == []
     print("\nmax |b200 - reference|:", _worst(raw, value, d))
     assert set(raw) == {k[4:] for k in d if k.startswith("raw_")}
     for k in raw:
@@ -94,3 +97,18 @@ def test_postflop_forward_detects_a_changed_weight(gold):
     pub, ranges, masks = _inputs(d)
     raw, value = _model(params).forward(pub, ranges, None, masks)
     assert max(_worst(raw, value, d).values()) > 0.05
+
+
+def test_postflop_input_check_records_a_folded_actor(gold):
+    # postflop.py:409-412: the actor seat must be present; seat 2 is folded in every decision of the
+    # fixture.  The check is recorded on the device (every index stays in range) and raised on the host.
+    from pbg_b200.postflop import input_errors, raise_input_errors
+
+    d = gold("postflop_model")
+    model = _model(_params(d))
+    pub, ranges, masks = _inputs(d)
+    input_errors(DEV)
+    model.forward(pub, ranges, torch.full((ranges.shape[0],), 2, dtype=torch.long, device=DEV), masks)
+    with pytest.raises(ValueError, match="the actor seat must be present"):
+        raise_input_errors(DEV)
+    assert input_errors(DEV) == []
