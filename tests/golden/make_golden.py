@@ -16,7 +16,10 @@ shims before calling them:
 * ``PokerStateMachine.initial_roots`` is re-compiled from the reference's own
   source with only its device-type guard removed (hooks.py:369-371);
 * ``CollisionConditionedProfileSampler.sample_children`` likewise
-  (rb_sampling.py:107-108).
+  (rb_sampling.py:107-108);
+* ``folded._folded_statistics_fp32`` likewise (its board device-type test,
+  folded.py:251), and the model runs lift ``tensor_ops._accelerator`` and the
+  device test of ``MHA.forward``.
 
 Everything else runs unmodified.  The fixtures are small ``.npz`` files that
 the ``-m "not gpu"`` tests use to pin the oracle and the ``-m gpu`` tests use
