@@ -1,8 +1,14 @@
 // Dense bf16 linear layer on the 5th-generation tensor cores:
-//     y[M, N] = act(x[M, K] . w[N, K]^T + bias[N])      (bf16 in/out, fp32 accumulate)
-// the Linear / FFN / attention-projection maps of the poker model
-// (pbg/games/poker/model/primitives.py:35-60 FFN, :97-117 MHA projections,
-// pbg/core/tensor_ops.py Linear: weight [out, in], bias [out]).
+//     y[M, N] = act(x[M, K] . w[N, K]^T * row_scale[M] + bias[N] + residual[M, N])
+// bf16 operands, fp32 accumulate, bf16 or fp32 output; the Linear / FFN /
+// attention-projection maps of the poker model (pbg/games/poker/model/
+// primitives.py:35-60 FFN, :97-117 MHA projections, pbg/core/tensor_ops.py
+// Linear: weight [out, in], bias [out]) with the elementwise steps that follow
+// them in the model fused into the epilogue: the per-row mass scale of the
+// incidence source map, the fp32 residual add of the attention output and FFN
+// maps, and the pre-activation residual of the incidence query map
+// (pbg/games/poker/model/incidence.py:57-84).  x, residual and y take their own
+// row strides, so a map can read or fill a column slice of a wider buffer.
 //
 // One persistent CTA per SM walks 128 x BN output tiles (BN <= 256, a
 // divisor of N).  Warp roles:
@@ -16,12 +22,13 @@
 //           k-block, publishes the accumulator ("acc_full");
 //   warps 2-17 epilogue, four warps per TMEM lane quadrant, each on a quarter
 //           of the tile's columns: a thread owns one accumulator row, loads 32
-//           columns at a time with tcgen05.ld, adds the bias, applies GELU
-//           (erf form, torch's default), packs bf16 into a 64-byte-swizzled
+//           columns at a time with tcgen05.ld, applies the row scale, bias,
+//           residual (128 contiguous bytes of its row) and GELU (erf form,
+//           torch's default), packs bf16 (or keeps fp32) into a 64-byte-swizzled
 //           shared-memory block (conflict-free) and one lane TMA-stores the
-//           32x32 block (rows past M are clipped by the tensor map); then the
-//           warp releases the accumulator ("acc_empty") so the next tile's
-//           MMAs overlap this epilogue.
+//           32x32 bf16 block (two 32x16 fp32 blocks; rows past M are clipped by
+//           the tensor map); then the warp releases the accumulator
+//           ("acc_empty") so the next tile's MMAs overlap this epilogue.
 // Every wait is bounded; a wait that runs out records an error code, stops
 // the CTA's loops, waits (bounded) for its own copies and MMAs in flight,
 // frees its tensor memory and returns.
@@ -48,8 +55,11 @@ struct GemmArgs {
     int N, K, BN, tiles_n;
     int64_t tiles;
     const float* bias;
-    __nv_bfloat16* y;
-    int act;  // 0 none, 1 gelu
+    const float* row_scale;  // [M] or null
+    const float* residual;   // [M, ldr] fp32 or null
+    int64_t ldr;
+    int act;                 // 0 none, 1 gelu
+    int out_f32;             // 0 bf16, 1 fp32
     uint32_t* error;
 };
 
@@ -162,23 +172,34 @@ __device__ __forceinline__ float gm_erf(float x) {
 // below 1e-5 in magnitude and the deviation below 1e-6.
 __device__ __forceinline__ float gm_gelu(float x) { return 0.5f * x * (1.0f + gm_erf(x * 0.70710678118654752f)); }
 
-// bias + activation + bf16 packing of one thread's 32 accumulator columns
+// activation and bf16 packing of one thread's 32 finished columns (two at a time: few live registers)
 template <int ACT>
-__device__ __forceinline__ void gm_convert(const float* v, const float* bias, uint32_t* packed) {
+__device__ __forceinline__ void gm_pack_bf16(const float* v, uint32_t* packed) {
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-        float x0 = v[j], x1 = v[j + 1];
-        if (bias) {
-            x0 += bias[j];
-            x1 += bias[j + 1];
-        }
-        if (ACT == 1) {
-            x0 = gm_gelu(x0);
-            x1 = gm_gelu(x1);
-        }
+        const float x0 = ACT == 1 ? gm_gelu(v[j]) : v[j];
+        const float x1 = ACT == 1 ? gm_gelu(v[j + 1]) : v[j + 1];
         __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
         packed[j / 2] = *reinterpret_cast<uint32_t*>(&h);
     }
+}
+
+// one 32 x 64-byte block row (`lane`) of the swizzled staging block: chunk q at position q ^ ((row >> 1) & 3)
+__device__ __forceinline__ void gm_stage_row(uint32_t blk, int lane, const uint32_t* words) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t addr = blk + (uint32_t)lane * 64u + (uint32_t)((q ^ ((lane >> 1) & 3)) * 16);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(words[4 * q]), "r"(words[4 * q + 1]),
+                     "r"(words[4 * q + 2]), "r"(words[4 * q + 3])
+                     : "memory");
+    }
+}
+
+__device__ __forceinline__ void gm_store_block(const CUtensorMap* map, uint32_t blk, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(blk)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(GM_THREADS, 1)
@@ -317,29 +338,61 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 float v[32];
                 gm_tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + b * (uint32_t)G.BN + (uint32_t)(part * cols + c),
                              v);
-                const float* bias = G.bias ? G.bias + col_base + c : nullptr;
-                uint32_t packed[16];
-                if (G.act == 1) gm_convert<1>(v, bias, packed);
-                else gm_convert<0>(v, bias, packed);
-                // the previous TMA store has finished reading the block
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-                __syncwarp();
-                // row `lane`: 64 bytes = four 16-byte chunks, chunk j at position j ^ ((row >> 1) & 3)
+                const int64_t row = (int64_t)m_blk * GM_BM + quad * 32 + lane;
+                const bool live = row < G.M;
+                if (G.row_scale) {
+                    const float scale = live ? G.row_scale[row] : 0.0f;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t addr = blk + (uint32_t)lane * 64u + (uint32_t)((q ^ ((lane >> 1) & 3)) * 16);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[4 * q]),
-                                 "r"(packed[4 * q + 1]), "r"(packed[4 * q + 2]), "r"(packed[4 * q + 3])
-                                 : "memory");
+                    for (int j = 0; j < 32; ++j) v[j] *= scale;
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-                    const int x = col_base + c, y = m_blk * GM_BM + quad * 32;
-                    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
-                                 ::"l"(reinterpret_cast<uint64_t>(&map_y)), "r"(x), "r"(y), "r"(blk)
-                                 : "memory");
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                if (G.bias) {
+                    const float* bias = G.bias + col_base + c;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += bias[j];
+                }
+                if (G.residual && live) {
+                    const float4* r4 = reinterpret_cast<const float4*>(G.residual + row * G.ldr + col_base + c);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        float4 r[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) r[q] = __ldg(r4 + 4 * half + q);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            v[16 * half + 4 * q] += r[q].x;
+                            v[16 * half + 4 * q + 1] += r[q].y;
+                            v[16 * half + 4 * q + 2] += r[q].z;
+                            v[16 * half + 4 * q + 3] += r[q].w;
+                        }
+                    }
+                }
+                const int y0 = m_blk * GM_BM + quad * 32;
+                const bool gelu = G.act == 1;
+                if (!G.out_f32) {
+                    uint32_t packed[16];
+                    if (gelu) gm_pack_bf16<1>(v, packed);
+                    else gm_pack_bf16<0>(v, packed);
+                    // the previous TMA store has finished reading the block
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    __syncwarp();
+                    gm_stage_row(blk, lane, packed);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) gm_store_block(&map_y, blk, col_base + c, y0);
+                } else {
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        if (gelu) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) v[16 * half + j] = gm_gelu(v[16 * half + j]);
+                        }
+                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                        __syncwarp();
+                        gm_stage_row(blk, lane, reinterpret_cast<const uint32_t*>(v + 16 * half));
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) gm_store_block(&map_y, blk, col_base + c + 16 * half, y0);
+                    }
                 }
             }
             gm_fence_before();
@@ -371,18 +424,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D bf16 row-major map: rows x cols (cols contiguous), box box_rows x box_cols.
-static int make_map(CUtensorMap* map, const void* base, int64_t rows, int cols, int box_rows, int box_cols,
-                    CUtensorMapSwizzle swizzle) {
+// 2-D row-major map (bf16 or fp32): rows x cols (cols contiguous, `ld` elements between rows), box
+// box_rows x box_cols.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int cols, int64_t ld, int box_rows,
+                    int box_cols, CUtensorMapSwizzle swizzle, bool f32 = false) {
     auto fn = encode_fn();
     PBG_REQUIRE(fn != nullptr, "linear: cuTensorMapEncodeTiled is unavailable");
+    const int esize = f32 ? 4 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * esize};
     cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t elem[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     PBG_REQUIRE(r == CUDA_SUCCESS, "linear: tensor map encoding failed (%d)", (int)r);
     return 0;
 }
@@ -393,13 +448,19 @@ using namespace pbg;
 
 extern "C" {
 
-int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* w, const float* bias, void* y,
-                    int32_t activation, uint32_t* error, void* stream) {
+int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, const void* w, const float* bias,
+                  const float* row_scale, const float* residual, int64_t ldr, void* y, int64_t ldy, int32_t y_f32,
+                  int32_t activation, uint32_t* error, void* stream) {
     PBG_REQUIRE(M >= 0 && N > 0 && K > 0, "linear: bad shape");
     PBG_REQUIRE(K % GM_BK == 0, "linear: K must be a multiple of %d", GM_BK);
     PBG_REQUIRE(N % 128 == 0, "linear: N must be a multiple of 128");
     PBG_REQUIRE(activation == 0 || activation == 1, "linear: activation must be 0 (none) or 1 (gelu)");
+    PBG_REQUIRE(y_f32 == 0 || y_f32 == 1, "linear: y_f32 must be 0 (bf16) or 1 (fp32)");
     PBG_REQUIRE(x && w && y && error, "linear: null pointer");
+    PBG_REQUIRE(ldx >= K && (ldx * 2) % 16 == 0, "linear: x row stride must be >= K and a multiple of 8");
+    PBG_REQUIRE(ldy >= N && (ldy * (y_f32 ? 4 : 2)) % 16 == 0, "linear: y row stride must be >= N, 16-byte rows");
+    PBG_REQUIRE(!residual || (ldr >= N && ldr % 4 == 0 && ((uintptr_t)residual % 16) == 0),
+                "linear: residual must be 16-byte aligned with a row stride >= N and a multiple of 4");
     PBG_REQUIRE(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && ((uintptr_t)y % 16) == 0,
                 "linear: x, w and y must be 16-byte aligned");
     if (M == 0) return 0;
@@ -412,11 +473,12 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* 
         }
     PBG_REQUIRE(BN > 0, "linear: N must be a multiple of 128");
     CUtensorMap mx, mw, my;
-    int rc = make_map(&mx, x, M, K, GM_BM, GM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    int rc = make_map(&mx, x, M, K, ldx, GM_BM, GM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    rc = make_map(&mw, w, N, K, BN, GM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = make_map(&mw, w, N, K, K, BN, GM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    rc = make_map(&my, y, M, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    // output blocks of 32 rows x 64 bytes: 32 bf16 or 16 fp32 columns
+    rc = make_map(&my, y, M, N, ldy, 32, y_f32 ? 16 : 32, CU_TENSOR_MAP_SWIZZLE_64B, y_f32 != 0);
     if (rc) return rc;
     GemmArgs G;
     G.M = M;
@@ -426,8 +488,11 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* 
     G.tiles_n = N / BN;
     G.tiles = ((M + GM_BM - 1) / GM_BM) * (int64_t)G.tiles_n;
     G.bias = bias;
-    G.y = static_cast<__nv_bfloat16*>(y);
+    G.row_scale = row_scale;
+    G.residual = residual;
+    G.ldr = ldr;
     G.act = activation;
+    G.out_f32 = y_f32;
     G.error = error;
     const size_t smem = 1024 + (size_t)GM_STAGES * (GM_BM * GM_BK * 2 + (size_t)BN * GM_BK * 2) +
                         (size_t)GM_EPI_WARPS * GM_STAGE_OUT;
@@ -445,6 +510,11 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* 
     const int64_t grid = G.tiles < sm_count() ? G.tiles : sm_count();
     linear_tcgen05_kernel<<<(unsigned)grid, GM_THREADS, smem, as_stream(stream)>>>(mx, mw, my, G);
     return launch_status("linear_bf16");
+}
+
+int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* w, const float* bias, void* y,
+                    int32_t activation, uint32_t* error, void* stream) {
+    return pbg_linear_ex(M, N, K, x, K, w, bias, nullptr, nullptr, 0, y, N, 0, activation, error, stream);
 }
 
 }  // extern "C"

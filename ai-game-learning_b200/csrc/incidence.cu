@@ -1,0 +1,106 @@
+// The elementwise part of the incidence residual
+// (pbg/games/poker/model/incidence.py:57-84) after its two fp32 card
+// contractions: for every decision b, private row r and feature c, over the
+// P seats p
+//     same_p  = source_p * identical_scale[b, r]
+//     oe_p    = sum_q same_q - same_p                        (other_equal)
+//     oc_p    = (sum_q overlap_q - overlap_p) - 2 oe_p       (other_card)
+//     own_p   = overlap_p - 2 same_p                         (own_card)
+// with the seat sums in seat order, as the reference's .sum(1) adds them.
+// One pass writes every consumer's copy: oe and own as bf16 into the
+// identical / own columns of the incidence map's staged operand, oc as fp32
+// (the pre-activation residual of that map's epilogue), and oc^2, oc * oe as
+// bf16 into the FamilyFFN operand rows of the token sequence.  A thread owns
+// four consecutive features of one (b, r) for all seats (float4 loads).
+#include <cuda_bf16.h>
+
+#include "pbg_common.cuh"
+
+namespace pbg {
+
+constexpr int IC_MAXP = 9;  // PokerModelConfig.max_players (preflop.py:80)
+
+__device__ __forceinline__ void ic_store4(__nv_bfloat16* p, float a, float b, float c, float d) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&lo);
+    w.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = w;
+}
+
+__global__ void incidence_combine_kernel(int64_t batch, int players, int64_t rows, int d,
+                                         const float* __restrict__ source, const float* __restrict__ overlap,
+                                         const float* __restrict__ identical_scale, __nv_bfloat16* __restrict__ inc,
+                                         int64_t ld_inc, int col_equal, int col_own, float* __restrict__ other_card,
+                                         __nv_bfloat16* __restrict__ ffn, int64_t ffn_batch_stride, int64_t ld_ffn,
+                                         int col_square, int col_product) {
+    const int quads = d >> 2;
+    const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (item >= batch * rows * quads) return;
+    const int q = (int)(item % quads);
+    const int64_t br = item / quads;
+    const int64_t b = br / rows, r = br - b * rows;
+    const float scale = identical_scale[b * rows + r];
+    // pass 1: the seat sums (seat order); pass 2 re-reads each seat's four features (L1-resident) and
+    // writes every output, so the thread holds no per-seat arrays
+    float4 total_same = make_float4(0.f, 0.f, 0.f, 0.f), total_card = total_same;
+    for (int p = 0; p < players; ++p) {
+        const int64_t at = ((b * players + p) * rows + r) * d + 4 * q;
+        const float4 s = __ldg(reinterpret_cast<const float4*>(source + at));
+        const float4 o = __ldg(reinterpret_cast<const float4*>(overlap + at));
+        total_same.x += s.x * scale;
+        total_same.y += s.y * scale;
+        total_same.z += s.z * scale;
+        total_same.w += s.w * scale;
+        total_card.x += o.x;
+        total_card.y += o.y;
+        total_card.z += o.z;
+        total_card.w += o.w;
+    }
+    for (int p = 0; p < players; ++p) {
+        const int64_t row = (b * players + p) * rows + r;
+        const float4 s = __ldg(reinterpret_cast<const float4*>(source + row * d + 4 * q));
+        const float4 o = __ldg(reinterpret_cast<const float4*>(overlap + row * d + 4 * q));
+        const float4 sm = make_float4(s.x * scale, s.y * scale, s.z * scale, s.w * scale);
+        const float4 oe = make_float4(total_same.x - sm.x, total_same.y - sm.y, total_same.z - sm.z,
+                                      total_same.w - sm.w);
+        const float4 oc = make_float4((total_card.x - o.x) - 2.0f * oe.x, (total_card.y - o.y) - 2.0f * oe.y,
+                                      (total_card.z - o.z) - 2.0f * oe.z, (total_card.w - o.w) - 2.0f * oe.w);
+        *reinterpret_cast<float4*>(other_card + row * d + 4 * q) = oc;
+        __nv_bfloat16* ir = inc + row * ld_inc + 4 * q;
+        ic_store4(ir + col_equal, oe.x, oe.y, oe.z, oe.w);
+        ic_store4(ir + col_own, o.x - 2.0f * sm.x, o.y - 2.0f * sm.y, o.z - 2.0f * sm.z, o.w - 2.0f * sm.w);
+        if (ffn) {
+            __nv_bfloat16* fr = ffn + b * ffn_batch_stride + ((int64_t)p * rows + r) * ld_ffn + 4 * q;
+            ic_store4(fr + col_square, oc.x * oc.x, oc.y * oc.y, oc.z * oc.z, oc.w * oc.w);
+            ic_store4(fr + col_product, oc.x * oe.x, oc.y * oe.y, oc.z * oe.z, oc.w * oe.w);
+        }
+    }
+}
+
+}  // namespace pbg
+
+using namespace pbg;
+
+extern "C" int pbg_incidence_combine(int64_t batch, int32_t players, int64_t rows, int32_t d, const float* source,
+                                     const float* overlap, const float* identical_scale, void* inc, int64_t ld_inc,
+                                     int32_t col_equal, int32_t col_own, float* other_card, void* ffn,
+                                     int64_t ffn_batch_stride, int64_t ld_ffn, int32_t col_square,
+                                     int32_t col_product, void* stream) {
+    PBG_REQUIRE(batch >= 0 && rows >= 0 && players >= 1 && players <= IC_MAXP, "incidence_combine: bad shape");
+    PBG_REQUIRE(d >= 4 && d % 4 == 0, "incidence_combine: width must be a multiple of 4");
+    PBG_REQUIRE(ld_inc % 4 == 0 && col_equal % 4 == 0 && col_own % 4 == 0 && ld_ffn % 4 == 0 &&
+                    col_square % 4 == 0 && col_product % 4 == 0 && ffn_batch_stride % 4 == 0,
+                "incidence_combine: strides and column offsets must be multiples of 4 elements");
+    const int64_t items = batch * rows * (d / 4);
+    if (items == 0) return 0;
+    PBG_REQUIRE(source && overlap && identical_scale && inc && other_card, "incidence_combine: null pointer");
+    PBG_REQUIRE(((uintptr_t)source % 16) == 0 && ((uintptr_t)overlap % 16) == 0 && ((uintptr_t)other_card % 16) == 0 &&
+                    ((uintptr_t)inc % 8) == 0 && ((uintptr_t)ffn % 8) == 0,
+                "incidence_combine: misaligned buffer");
+    incidence_combine_kernel<<<(unsigned)((items + 255) / 256), 256, 0, as_stream(stream)>>>(
+        batch, players, rows, d, source, overlap, identical_scale, static_cast<__nv_bfloat16*>(inc), ld_inc,
+        col_equal, col_own, other_card, static_cast<__nv_bfloat16*>(ffn), ffn_batch_stride, ld_ffn, col_square,
+        col_product);
+    return launch_status("incidence_combine");
+}

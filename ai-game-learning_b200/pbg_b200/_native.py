@@ -111,6 +111,11 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_layered_targets": (_I32, [_P, _I32, TargetNodes, TargetChildren, TargetTables, _I32, _I32, _I32, _I32,
                                    _I32, _I32, ctypes.c_float, _I32, _I32, _P, _P, _P]),
     "pbg_linear_bf16": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
+    "pbg_linear_ex": (_I32, [_I64, _I32, _I32, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _P, _P]),
+    "pbg_layernorm_rows": (_I32, [_I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P, ctypes.c_float, _P, _I32, _I64,
+                                  _I64, _P]),
+    "pbg_incidence_combine": (_I32, [_I64, _I32, _I64, _I32, _P, _P, _P, _P, _I64, _I32, _I32, _P, _P, _I64, _I64,
+                                     _I32, _I32, _P]),
     "pbg_attention_bf16": (_I32, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_layernorm": (_I32, [_I64, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _I32, _I64, _P]),
     "pbg_nvls_signal_bytes": (_I64, []),
@@ -174,6 +179,22 @@ def ptr(t: torch.Tensor | None):
         raise NativeError("libpbgb200 operates on CUDA tensors only")
     if not t.is_contiguous():
         raise NativeError("libpbgb200 requires contiguous tensors")
+    items = getattr(_keep, "items", None)
+    if items is None:
+        items = _keep.items = []
+    items.append(t)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def rows_ptr(t: torch.Tensor | None):
+    """Device pointer of a CUDA matrix whose rows are contiguous (any row stride), kept alive for call()."""
+
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise NativeError("libpbgb200 operates on CUDA tensors only")
+    if t.ndim != 2 or t.stride(1) != 1:
+        raise NativeError("libpbgb200 requires a matrix with contiguous rows")
     items = getattr(_keep, "items", None)
     if items is None:
         items = _keep.items = []

@@ -24,8 +24,8 @@ import torch
 from torch import Tensor
 from torch.nn import functional as F
 
-from ._native import NativeError, call, ptr, stream
-from .model import attention, linear
+from ._native import NativeError, call, ptr, rows_ptr, stream
+from .model import attention, linear, linear_ex
 
 
 @dataclass(frozen=True)
@@ -107,6 +107,20 @@ class _Map:
         if self.np_ != self.n:
             y = y[:, : self.n]
         return y.reshape(*lead, self.n)
+
+    def apply(self, rows: Tensor, activation: str | None = None, *, row_scale: Tensor | None = None,
+              residual: Tensor | None = None, out: Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """The map over a bf16 matrix of width kp (rows contiguous, any row stride) with the fused
+        epilogue of ``linear_ex``: per-row scale, fp32 residual, fp32 or bf16 output."""
+
+        if rows.ndim != 2 or rows.shape[1] != self.kp:
+            raise NativeError("map operand must be a [rows, padded in] matrix")
+        if self.np_ != self.n and (residual is not None or out is not None):
+            raise NativeError("a fused residual or output buffer needs an unpadded output width")
+        y = linear_ex(rows, self.weight, self.bias, activation, row_scale=row_scale, residual=residual, out=out,
+                      out_dtype=out_dtype)
+        return y if self.np_ == self.n else y[:, : self.n]
 
 
 def _cat_maps(first: Tensor, second: Tensor) -> Tensor:
@@ -201,54 +215,69 @@ class FamilyModel:
         hidden = row_map(rows).float() + ctx_map(context).float()[:, None, :]
         return maps[1](F.gelu(hidden))
 
-    def _incidence(self, layer, rows: Tensor, mass: Tensor, incidence: Tensor, identical_scale: Tensor):
-        """incidence.py:30-84 (IncidenceResidual.forward)."""
+    def _ln_rows(self, x: Tensor, gain_bias, group_rows: int, out: Tensor) -> Tensor:
+        """LayerNorm of the first ``group_rows`` tokens of every sequence of ``x`` [B, L, d] (fp32,
+        contiguous) into ``out`` [B * group_rows, d] (bf16, rows contiguous, any row stride)."""
 
-        batch, players, k, d = rows.shape
-        operand = torch.empty((batch, players, k, 3 * d), dtype=torch.bfloat16, device=rows.device)
-        normalized = self._ln(rows, layer["inc_ln"], operand.view(-1, 3 * d)[:, :d])
-        source = layer["source"](normalized).float() * mass.float()[..., None]
-        card_acc = torch.einsum("brc,bprd->bpcd", incidence, source)
-        card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc)
-        same = source * identical_scale[:, None, :, None]
-        other_equal = same.sum(1, keepdim=True) - same
-        other_card = card_overlap.sum(1, keepdim=True) - card_overlap - 2.0 * other_equal
-        own_card = card_overlap - 2.0 * same
-        operand[..., d: 2 * d] = other_equal
-        operand[..., 2 * d:] = own_card
-        inner = layer["inc_in"](operand).float() + other_card
-        residual = layer["inc_out"](F.gelu(inner))
-        return residual, other_card, other_equal, own_card
+        batch, length, d = x.shape
+        call("pbg_layernorm_rows", batch * group_rows, d, group_rows, ptr(x), 0, length * d, d, ptr(gain_bias[0]),
+             ptr(gain_bias[1]), 1e-5, rows_ptr(out), 1, group_rows * out.stride(0), out.stride(0), stream(x.device))
+        return out
+
+    def _incidence(self, layer, x: Tensor, players: int, rows: int, mass: Tensor, incidence: Tensor,
+                   identical_scale: Tensor, ffn_operand: Tensor) -> Tensor:
+        """incidence.py:30-84 (IncidenceResidual.forward) on the private rows of the residual stream
+        ``x`` [B, L, d]: LayerNorm into the staged operand [n | oe | own], the source map with the row
+        mass fused as a row scale (fp32 out), the two fp32 card contractions, one combine pass (oe and
+        own into the operand, oc as the query map's pre-GELU residual, oc^2 and oc*oe into the
+        FamilyFFN operand ``ffn_operand`` [B, L, W]), the query/identical/own map with residual and
+        GELU fused, and the output map.  Returns j, bf16 [B * players * rows, d]."""
+
+        batch, length, d = x.shape
+        count = batch * players * rows
+        operand = torch.empty((count, 3 * d), dtype=torch.bfloat16, device=x.device)
+        self._ln_rows(x, layer["inc_ln"], players * rows, operand[:, :d])
+        source = layer["source"].apply(operand[:, :d], row_scale=mass, out_dtype=torch.float32)
+        card_acc = torch.einsum("brc,bprd->bpcd", incidence, source.view(batch, players, rows, d))
+        card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc).contiguous()
+        other_card = torch.empty_like(source)
+        width = ffn_operand.shape[-1]
+        call("pbg_incidence_combine", batch, players, rows, d, ptr(source), ptr(card_overlap), ptr(identical_scale),
+             ptr(operand), 3 * d, d, 2 * d, ptr(other_card), ptr(ffn_operand), length * width, width, 2 * d, 3 * d,
+             stream(x.device))
+        hidden = layer["inc_in"].apply(operand, "gelu", residual=other_card)
+        return layer["inc_out"].apply(hidden)
 
     def _trunk(self, x: Tensor, players: int, rows_per_seat: int, mass: Tensor, incidence: Tensor,
                identical_scale: Tensor, side: Tensor, key_bias: Tensor, key_mask: Tensor) -> Tensor:
         """The shared layers (preflop.py:614-641 / postflop.py:658-685): incidence residual, LayerNorm,
-        biased attention, FamilyFFN over [LN(x_hat) | j, oc^2, oc*oe] and the family's side rows."""
+        biased attention with the residual add fused into the output map, FamilyFFN over
+        [LN(x_hat) | j, oc^2, oc*oe | side] with the residual add fused into its output map."""
 
         cfg = self.cfg
         d = cfg.d_model
         batch, length, _ = x.shape
         rows_k = players * rows_per_seat
-        # FamilyFFN operand [LN(x_hat) | j, oc^2, oc*oe | side] in one bf16 buffer, padded to the map's K;
+        # FamilyFFN operand [LN(x_hat) | j | oc^2 | oc*oe | side] in one bf16 buffer, padded to the map's K;
         # the side features (fixed across layers) and the zero rows of non-row tokens are written once
         width = self.layers[0]["ffn_in"].kp if self.layers else 0
         operand = torch.zeros((batch, length, width), dtype=torch.bfloat16, device=x.device)
         side_width = side.shape[-1]
         operand[:, :rows_k, 4 * d: 4 * d + side_width] = side.reshape(batch, rows_k, side_width)
+        mass_rows = mass.reshape(-1).to(torch.float32).contiguous()
+        scale_rows = identical_scale.to(torch.float32).contiguous()
+        x = x.contiguous()
+        flat = operand.view(batch * length, width)
         for layer in self.layers:
-            row_state = x[:, :rows_k].reshape(batch, players, rows_per_seat, d)
-            j, oc, oe, _ = self._incidence(layer, row_state, mass, incidence, identical_scale)
+            j = self._incidence(layer, x, players, rows_per_seat, mass_rows, incidence, scale_rows, operand)
+            operand[:, :rows_k, d: 2 * d] = j.view(batch, rows_k, d)
             nx = self._ln(x, layer["ln"])
             qkv = layer["w_qkv"](nx)
             attended = attention(qkv.contiguous(), cfg.n_heads, layer["q_scale"], key_bias, key_mask)
-            x_hat = x + layer["w_o"](attended).float()
-            self._ln(x_hat, layer["ln"], operand.view(batch * length, width)[:, :d])
-            dyn = operand[:, :rows_k, d: 4 * d].view(batch, players, rows_per_seat, 3, d)
-            dyn[..., 0, :] = j
-            dyn[..., 1, :] = oc * oc
-            dyn[..., 2, :] = oc * oe
-            hidden = layer["ffn_in"](operand, "gelu")
-            x = x_hat + layer["ffn_out"](hidden).float()
+            x_hat = layer["w_o"].apply(attended.view(-1, d), residual=x.view(-1, d), out_dtype=torch.float32)
+            self._ln(x_hat, layer["ln"], flat[:, :d])
+            hidden = layer["ffn_in"].apply(flat, "gelu")
+            x = layer["ffn_out"].apply(hidden, residual=x_hat, out_dtype=torch.float32).view(batch, length, d)
         return x
 
     def _readout(self, actor_rows: Tensor, private_embedding: Tensor, anchors: Tensor, global_feature: Tensor):

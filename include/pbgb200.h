@@ -420,6 +420,20 @@ int pbg_layered_targets(const int32_t *layer_ptr, int32_t layers, pbg_target_nod
 int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *w, const float *bias, void *y,
                     int32_t activation, uint32_t *error, void *stream);
 
+/* The same map with the model's following elementwise steps fused into the
+ * epilogue: y = act(acc * row_scale[m] + bias[n] + residual[m, n]), where acc
+ * = x . w^T in fp32 and each term may be absent (NULL): the per-row mass scale
+ * of the incidence source map (pbg/games/poker/model/incidence.py:57-58), the
+ * fp32 residual adds after the attention output and FFN maps (preflop.py:
+ * 634-641, postflop.py:678-685), and the pre-GELU residual of the incidence
+ * query map (incidence.py:77-84).  x rows are ldx elements apart (ldx >= K,
+ * a multiple of 8), residual rows ldr floats apart (>= N, a multiple of 4,
+ * 16-byte aligned), y rows ldy elements apart; y is fp32 when y_f32 is 1,
+ * else bf16 (rows 16-byte aligned).  Other rules as for pbg_linear_bf16. */
+int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void *x, int64_t ldx, const void *w, const float *bias,
+                  const float *row_scale, const float *residual, int64_t ldr, void *y, int64_t ldy, int32_t y_f32,
+                  int32_t activation, uint32_t *error, void *stream);
+
 /* pbg/games/poker/model/primitives.py:63-283 (MHA, self-attention, heads of
  * width 32): out[b, q, h] = softmax_k((q_h / temperature_h) . k_h / sqrt(32)
  * + key_bias[b, k], keys with key_mask 0 excluded) . v_h.  qkv bf16
@@ -438,6 +452,29 @@ int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, const void *qk
  * NULL; row i of y starts at y + i * ldy elements (ldy >= d). */
 int pbg_layernorm(int64_t rows, int32_t d, const void *x, int32_t x_bf16, const float *gain, const float *bias,
                   float eps, void *y, int32_t y_bf16, int64_t ldy, void *stream);
+
+/* The same over a row block of every sequence of a batch: launch row i is
+ * row r = i % group_rows of group g = i / group_rows, read at x + g *
+ * x_group_stride + r * ldx and written at y + g * y_group_stride + r * ldy
+ * (elements). */
+int pbg_layernorm_rows(int64_t rows, int32_t d, int64_t group_rows, const void *x, int32_t x_bf16,
+                       int64_t x_group_stride, int64_t ldx, const float *gain, const float *bias, float eps, void *y,
+                       int32_t y_bf16, int64_t y_group_stride, int64_t ldy, void *stream);
+
+/* pbg/games/poker/model/incidence.py:57-70 after the two card contractions:
+ * source and overlap f32 [B, P, R, d] (contiguous), identical_scale f32
+ * [B, R]; per (b, r, feature) over the seats p (sums in seat order):
+ * same = source * scale, oe = sum(same) - same, oc = (sum(overlap) - overlap)
+ * - 2 oe, own = overlap - 2 same.  Writes oe and own as bf16 into columns
+ * col_equal / col_own of `inc` (row (b*P + p)*R + r, ld_inc elements apart),
+ * oc as f32 into other_card [B, P, R, d], and, when ffn is not NULL, oc*oc and
+ * oc*oe as bf16 into columns col_square / col_product of the FamilyFFN
+ * operand row p*R + r of sequence b (ffn + b * ffn_batch_stride + row *
+ * ld_ffn).  d, strides and column offsets are multiples of 4; P <= 9. */
+int pbg_incidence_combine(int64_t batch, int32_t players, int64_t rows, int32_t d, const float *source,
+                          const float *overlap, const float *identical_scale, void *inc, int64_t ld_inc,
+                          int32_t col_equal, int32_t col_own, float *other_card, void *ffn, int64_t ffn_batch_stride,
+                          int64_t ld_ffn, int32_t col_square, int32_t col_product, void *stream);
 
 /* ---------------------------------------------------------- collective */
 
