@@ -45,9 +45,10 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
-    p.add_argument("--profile-forward", choices=("preflop", "postflop"), default=None,
-                   help="run one eager forward of that component between cudaProfilerStart/Stop (for ncu "
-                        "--profile-from-start off) after two warm-up forwards, print nothing else, exit")
+    p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention"), default=None,
+                   help="run one eager forward of that component (attention: one attention-core launch at the "
+                        "postflop sequence length, 48 x 2,406 tokens x 8 heads) between cudaProfilerStart/Stop "
+                        "(for ncu --profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
 
 
@@ -457,6 +458,29 @@ def model_attention_component(device, batch=600, length=876, heads=8, reps=10):
             "kernel": "attention_kernel", "gpu_launches": 1}
 
 
+def profile_attention(device, batch=48, length=2406, heads=8):
+    """Two warm-up launches of the attention core at the postflop sequence length, then one between
+    cudaProfilerStart/Stop (qkv 177 MB: larger than L2)."""
+
+    import math
+
+    import torch
+    from pbg_b200.model import attention
+
+    g = torch.Generator(device=device).manual_seed(14)
+    qkv = torch.randn((batch, length, 3 * heads * 32), generator=g, device=device).to(torch.bfloat16)
+    bias = torch.randn((batch, length), generator=g, device=device)
+    mask = torch.rand((batch, length), generator=g, device=device) > 0.1
+    q_scale = torch.full((heads,), 1.0 / math.sqrt(32), device=device)
+    for _ in range(2):
+        attention(qkv, heads, q_scale, bias, mask)
+    torch.cuda.synchronize(device)
+    torch.cuda.profiler.start()
+    attention(qkv, heads, q_scale, bias, mask)
+    torch.cuda.synchronize(device)
+    torch.cuda.profiler.stop()
+
+
 def preflop_forward_component(device, batch=256, players=2, history=16, reps=5):
     """The preflop policy/value network forward (pbg_b200.preflop, the reference's default
     PokerModelConfig: d_model 256, 8 heads, 6 layers, hidden 1024, R13 -> 169 class rows per seat)
@@ -673,6 +697,9 @@ def main():
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.profile_forward == "attention":
+        profile_attention(device)
+        return
     if args.profile_forward:
         global PROFILE_ONE_FORWARD
         PROFILE_ONE_FORWARD = True

@@ -51,6 +51,26 @@ def test_attention_matches_fp32_reference(batch, length, heads, biased, masked):
     torch.testing.assert_close(out.float(), _reference(qkv, heads, q_scale, bias, mask), rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("length,heads", [(2406, 8), (384, 8), (640, 2)])
+def test_attention_rising_bias_moves_the_shift(length, heads):
+    # a key bias rising along the sequence makes the running maximum grow block after block (the
+    # shift of the accumulated output moves whenever it grows by more than 2^8); leading keys absent
+    from pbg_b200.model import attention, pipeline_error
+
+    batch = 2
+    g = torch.Generator(device=DEV).manual_seed(length)
+    qkv = torch.randn((batch, length, 3 * heads * 32), generator=g, device=DEV).to(torch.bfloat16)
+    q_scale = torch.full((heads,), 1.0 / math.sqrt(32), device=DEV)
+    bias = torch.linspace(-60.0, 20.0, length, device=DEV)[None].expand(batch, -1).contiguous()
+    bias = bias + torch.randn((batch, length), generator=g, device=DEV)
+    mask = torch.rand((batch, length), generator=g, device=DEV) > 0.2
+    mask[0, :100] = False
+    out = attention(qkv, heads, q_scale, bias, mask)
+    torch.cuda.synchronize()
+    assert pipeline_error(DEV) == 0
+    torch.testing.assert_close(out.float(), _reference(qkv, heads, q_scale, bias, mask), rtol=2e-2, atol=2e-2)
+
+
 def test_attention_all_keys_masked_gives_zero():
     from pbg_b200.model import attention
 
