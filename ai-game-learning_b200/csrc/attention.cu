@@ -52,6 +52,13 @@ __device__ __forceinline__ bool at_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// max(a, b, c) in one instruction
+__device__ __forceinline__ float at_max3(float a, float b, float c) {
+    float m;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+    return m;
+}
+
 // 2^x on the special-function unit (ex2.approx: relative error about 2^-22; 0 for -inf)
 __device__ __forceinline__ float at_exp2(float x) {
     float y;
@@ -273,14 +280,11 @@ __global__ void __launch_bounds__(AttnPlan<T>::threads, 1) attention_kernel(Attn
                 sv[j + 1] = t0.y;
                 sv[j + 2] = t1.x;
                 sv[j + 3] = t1.y;
-                const int a = (j >> 2) & 1;
-                mx[4 * a] = fmaxf(mx[4 * a], t0.x);
-                mx[4 * a + 1] = fmaxf(mx[4 * a + 1], t0.y);
-                mx[4 * a + 2] = fmaxf(mx[4 * a + 2], t1.x);
-                mx[4 * a + 3] = fmaxf(mx[4 * a + 3], t1.y);
+                const int a = (j >> 2) & 3;
+                mx[2 * a] = at_max3(mx[2 * a], t0.x, t0.y);
+                mx[2 * a + 1] = at_max3(mx[2 * a + 1], t1.x, t1.y);
             }
-            const float bmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            const float bmax = at_max3(at_max3(mx[0], mx[1], mx[2]), at_max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
             // move the shift to the new maximum when it grows past the threshold: earlier P values
             // (in the output and the sum) are rescaled by 2^(shift - new shift); the first present key
             // always sets it (the output is still empty then: the first product overwrites it)
