@@ -104,3 +104,33 @@ extern "C" int pbg_incidence_combine(int64_t batch, int32_t players, int64_t row
         col_product);
     return launch_status("incidence_combine");
 }
+
+namespace pbg {
+
+// rows of a contiguous bf16 matrix [rows, d] copied into the row block of every sequence of a wider
+// buffer: row i -> dst + (i / group_rows) * group_stride + (i % group_rows) * ld (16-byte vectors)
+__global__ void scatter_rows_kernel(int64_t rows, int d, int64_t group_rows, const uint4* __restrict__ src,
+                                    __nv_bfloat16* __restrict__ dst, int64_t group_stride, int64_t ld) {
+    const int vecs = d >> 3;
+    const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (item >= rows * vecs) return;
+    const int64_t row = item / vecs;
+    const int v = (int)(item - row * vecs);
+    const int64_t g = row / group_rows, r = row - g * group_rows;
+    *reinterpret_cast<uint4*>(dst + g * group_stride + r * ld + 8 * v) = __ldg(src + item);
+}
+
+}  // namespace pbg
+
+extern "C" int pbg_scatter_rows_bf16(int64_t rows, int32_t d, int64_t group_rows, const void* src, void* dst,
+                                     int64_t group_stride, int64_t ld, void* stream) {
+    PBG_REQUIRE(rows >= 0 && d >= 8 && d % 8 == 0 && group_rows >= 1, "scatter_rows: bad shape");
+    PBG_REQUIRE(ld % 8 == 0 && group_stride % 8 == 0 && ld >= d, "scatter_rows: strides must be multiples of 8");
+    if (rows == 0) return 0;
+    PBG_REQUIRE(src && dst && ((uintptr_t)src % 16) == 0 && ((uintptr_t)dst % 16) == 0,
+                "scatter_rows: buffers must be 16-byte aligned");
+    const int64_t items = rows * (d / 8);
+    scatter_rows_kernel<<<(unsigned)((items + 255) / 256), 256, 0, as_stream(stream)>>>(
+        rows, d, group_rows, static_cast<const uint4*>(src), static_cast<__nv_bfloat16*>(dst), group_stride, ld);
+    return launch_status("scatter_rows_bf16");
+}

@@ -479,8 +479,8 @@ class PostflopModel(FamilyModel):
         incidence_mass = corrected.exp() * compact_mask
         identical_scale = torch.ones((batch, q), device=dev)
 
-        x = self._trunk(x, live, q, incidence_mass, geometry[..., : self.n_cards], identical_scale, side,
-                        key_bias, key_mask)
+        x = self._trunk(x, live, q, incidence_mass, geometry[..., : self.n_cards].contiguous(), identical_scale,
+                        side, key_bias, key_mask)
         final = self._ln(x, self.final_ln).float()
         final_rows = final[:, :rows_k].reshape(batch, live, q, d)
         final_public = final[:, rows_k: -cfg.k_act]

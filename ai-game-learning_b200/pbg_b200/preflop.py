@@ -238,8 +238,17 @@ class FamilyModel:
         operand = torch.empty((count, 3 * d), dtype=torch.bfloat16, device=x.device)
         self._ln_rows(x, layer["inc_ln"], players * rows, operand[:, :d])
         source = layer["source"].apply(operand[:, :d], row_scale=mass, out_dtype=torch.float32)
-        card_acc = torch.einsum("brc,bprd->bpcd", incidence, source.view(batch, players, rows, d))
-        card_overlap = torch.einsum("brc,bpcd->bprd", incidence, card_acc).contiguous()
+        # the two fp32 card contractions as batched GEMMs over the [R, d] blocks of every (decision, seat),
+        # with no permuted copies: a shared incidence [R, C] (class rows) or one per decision [B, R, C]
+        if incidence.dim() == 2:
+            blocks = source.view(batch * players, rows, d)
+            card_acc = torch.matmul(incidence.t(), blocks)
+            card_overlap = torch.matmul(incidence, card_acc)
+        else:
+            blocks = source.view(batch, players, rows, d)
+            card_acc = torch.matmul(incidence.transpose(1, 2)[:, None], blocks)
+            card_overlap = torch.matmul(incidence[:, None], card_acc)
+        card_overlap = card_overlap.contiguous()
         other_card = torch.empty_like(source)
         width = ffn_operand.shape[-1]
         call("pbg_incidence_combine", batch, players, rows, d, ptr(source), ptr(card_overlap), ptr(identical_scale),
@@ -270,7 +279,8 @@ class FamilyModel:
         flat = operand.view(batch * length, width)
         for layer in self.layers:
             j = self._incidence(layer, x, players, rows_per_seat, mass_rows, incidence, scale_rows, operand)
-            operand[:, :rows_k, d: 2 * d] = j.view(batch, rows_k, d)
+            call("pbg_scatter_rows_bf16", batch * rows_k, d, rows_k, ptr(j), rows_ptr(flat[:, d: 2 * d]),
+                 length * width, width, stream(x.device))
             nx = self._ln(x, layer["ln"])
             qkv = layer["w_qkv"](nx)
             attended = attention(qkv.contiguous(), cfg.n_heads, layer["q_scale"], key_bias, key_mask)
@@ -410,7 +420,7 @@ class PreflopModel(FamilyModel):
         key_bias = torch.cat((torch.log(normalized.clamp_min(cfg.eps)).reshape(batch, players * K),
                               torch.zeros((batch, length - players * K), device=dev)), 1).contiguous()
         side_class = torch.cat((expanded_emb, ranges[..., None], log_range[..., None], expanded_geometry), -1)
-        incidence = self.class_card_geometry[None].expand(batch, -1, -1)
+        incidence = self.class_card_geometry
         identical_scale = (1.0 / self.class_sizes)[None].expand(batch, -1)
 
         x = self._trunk(x, players, K, normalized, incidence, identical_scale, side_class, key_bias, key_mask)

@@ -471,6 +471,14 @@ int pbg_layernorm_rows(int64_t rows, int32_t d, int64_t group_rows, const void *
  * oc*oe as bf16 into columns col_square / col_product of the FamilyFFN
  * operand row p*R + r of sequence b (ffn + b * ffn_batch_stride + row *
  * ld_ffn).  d, strides and column offsets are multiples of 4; P <= 9. */
+/* Copy of a contiguous bf16 matrix [rows, d] into the row block of every
+ * sequence of a wider buffer: row i goes to dst + (i / group_rows) *
+ * group_stride + (i % group_rows) * ld (elements; d, ld, group_stride
+ * multiples of 8, 16-byte aligned buffers).  Places the incidence residual j
+ * into the FamilyFFN operand rows of the private tokens. */
+int pbg_scatter_rows_bf16(int64_t rows, int32_t d, int64_t group_rows, const void *src, void *dst,
+                          int64_t group_stride, int64_t ld, void *stream);
+
 int pbg_incidence_combine(int64_t batch, int32_t players, int64_t rows, int32_t d, const float *source,
                           const float *overlap, const float *identical_scale, void *inc, int64_t ld_inc,
                           int32_t col_equal, int32_t col_own, float *other_card, void *ffn, int64_t ffn_batch_stride,

@@ -100,3 +100,18 @@ def test_incidence_combine_matches_reference_terms(players):
     torch.testing.assert_close(f[..., 3 * d: 4 * d].float(), _bf(oc * oe).float(), **ulp)
     assert torch.count_nonzero(ffn[:, players * rows:]) == 0
     assert torch.count_nonzero(f[..., : 2 * d]) == 0 and torch.count_nonzero(f[..., 4 * d:]) == 0
+
+
+def test_scatter_rows_places_each_block():
+    from pbg_b200._native import call, ptr, rows_ptr, stream
+
+    g = torch.Generator(device=DEV).manual_seed(9)
+    batch, group, length, d, width = 5, 37, 50, 256, 1024
+    src = torch.randn((batch * group, d), generator=g, device=DEV).to(torch.bfloat16)
+    dst = torch.zeros((batch * length, width), dtype=torch.bfloat16, device=DEV)
+    call("pbg_scatter_rows_bf16", batch * group, d, group, ptr(src), rows_ptr(dst[:, 256: 256 + d]), length * width,
+         width, stream(DEV))
+    view = dst.view(batch, length, width)
+    assert torch.equal(view[:, :group, 256: 256 + d], src.view(batch, group, d))
+    assert torch.count_nonzero(view[:, group:]) == 0
+    assert torch.count_nonzero(view[:, :, :256]) == 0 and torch.count_nonzero(view[:, :, 256 + d:]) == 0
