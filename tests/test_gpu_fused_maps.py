@@ -115,3 +115,25 @@ def test_scatter_rows_places_each_block():
     assert torch.equal(view[:, :group, 256: 256 + d], src.view(batch, group, d))
     assert torch.count_nonzero(view[:, group:]) == 0
     assert torch.count_nonzero(view[:, :, :256]) == 0 and torch.count_nonzero(view[:, :, 256 + d:]) == 0
+
+
+@pytest.mark.parametrize("d,x_bf16,y_bf16", [(256, False, True), (128, False, True), (512, False, True),
+                                             (200, False, True), (256, True, True), (256, False, False),
+                                             (96, True, False)])
+def test_layernorm_paths_match_torch(d, x_bf16, y_bf16):
+    # the vectorised path (fp32 in, bf16 out, width a multiple of 128) and the general one
+    from pbg_b200._native import call, ptr, stream
+
+    g = torch.Generator(device=DEV).manual_seed(d)
+    rows = 1000
+    x = torch.randn((rows, d), generator=g, device=DEV) * 2 + 0.5
+    if x_bf16:
+        x = x.to(torch.bfloat16)
+    gain = torch.rand(d, generator=g, device=DEV) + 0.5
+    bias = torch.randn(d, generator=g, device=DEV)
+    y = torch.empty((rows, d), dtype=torch.bfloat16 if y_bf16 else torch.float32, device=DEV)
+    call("pbg_layernorm", rows, d, ptr(x), int(x_bf16), ptr(gain), ptr(bias), 1e-5, ptr(y), int(y_bf16), d,
+         stream(DEV))
+    want = F.layer_norm(x.float(), (d,), gain, bias, 1e-5)
+    tol = 2e-2 if y_bf16 else 1e-5
+    torch.testing.assert_close(y.float(), want, rtol=tol, atol=tol)
