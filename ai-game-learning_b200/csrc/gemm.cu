@@ -6,8 +6,10 @@
 // Linear: weight [out, in], bias [out]) with the elementwise steps that follow
 // them in the model fused into the epilogue: the per-row mass scale of the
 // incidence source map, the fp32 residual add of the attention output and FFN
-// maps, and the pre-activation residual of the incidence query map
-// (pbg/games/poker/model/incidence.py:57-84).  x, residual and y take their own
+// maps, the pre-activation residual of the incidence query map
+// (pbg/games/poker/model/incidence.py:57-84), and the per-decision context
+// projection that a factored FFN adds to every row of its decision
+// (pbg/games/poker/model/primitives.py:62-71, a residual row per group of rows).  x, residual and y take their own
 // row strides, so a map can read or fill a column slice of a wider buffer.
 //
 // One persistent CTA per SM walks 128 x BN output tiles (BN <= 256, a
@@ -56,8 +58,8 @@ struct GemmArgs {
     int64_t tiles;
     const float* bias;
     const float* row_scale;  // [M] or null
-    const float* residual;   // [M, ldr] fp32 or null
-    int64_t ldr;
+    const float* residual;   // fp32, row m at residual + (m / res_div) * ldr, or null
+    int64_t ldr, res_div;
     int act;                 // 0 none, 1 gelu
     int out_f32;             // 0 bf16, 1 fp32
     uint32_t* error;
@@ -351,7 +353,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     for (int j = 0; j < 32; ++j) v[j] += bias[j];
                 }
                 if (G.residual && live) {
-                    const float4* r4 = reinterpret_cast<const float4*>(G.residual + row * G.ldr + col_base + c);
+                    const float4* r4 =
+                        reinterpret_cast<const float4*>(G.residual + (row / G.res_div) * G.ldr + col_base + c);
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {
                         float4 r[4];
@@ -449,8 +452,8 @@ using namespace pbg;
 extern "C" {
 
 int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, const void* w, const float* bias,
-                  const float* row_scale, const float* residual, int64_t ldr, void* y, int64_t ldy, int32_t y_f32,
-                  int32_t activation, uint32_t* error, void* stream) {
+                  const float* row_scale, const float* residual, int64_t ldr, int64_t residual_row_div, void* y,
+                  int64_t ldy, int32_t y_f32, int32_t activation, uint32_t* error, void* stream) {
     PBG_REQUIRE(M >= 0 && N > 0 && K > 0, "linear: bad shape");
     PBG_REQUIRE(K % GM_BK == 0, "linear: K must be a multiple of %d", GM_BK);
     PBG_REQUIRE(N % 128 == 0, "linear: N must be a multiple of 128");
@@ -459,7 +462,7 @@ int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, c
     PBG_REQUIRE(x && w && y && error, "linear: null pointer");
     PBG_REQUIRE(ldx >= K && (ldx * 2) % 16 == 0, "linear: x row stride must be >= K and a multiple of 8");
     PBG_REQUIRE(ldy >= N && (ldy * (y_f32 ? 4 : 2)) % 16 == 0, "linear: y row stride must be >= N, 16-byte rows");
-    PBG_REQUIRE(!residual || (ldr >= N && ldr % 4 == 0 && ((uintptr_t)residual % 16) == 0),
+    PBG_REQUIRE(!residual || (ldr >= N && ldr % 4 == 0 && ((uintptr_t)residual % 16) == 0 && residual_row_div >= 1),
                 "linear: residual must be 16-byte aligned with a row stride >= N and a multiple of 4");
     PBG_REQUIRE(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && ((uintptr_t)y % 16) == 0,
                 "linear: x, w and y must be 16-byte aligned");
@@ -491,6 +494,7 @@ int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, c
     G.row_scale = row_scale;
     G.residual = residual;
     G.ldr = ldr;
+    G.res_div = residual_row_div >= 1 ? residual_row_div : 1;
     G.act = activation;
     G.out_f32 = y_f32;
     G.error = error;
@@ -514,7 +518,7 @@ int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, c
 
 int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void* x, const void* w, const float* bias, void* y,
                     int32_t activation, uint32_t* error, void* stream) {
-    return pbg_linear_ex(M, N, K, x, K, w, bias, nullptr, nullptr, 0, y, N, 0, activation, error, stream);
+    return pbg_linear_ex(M, N, K, x, K, w, bias, nullptr, nullptr, 0, 1, y, N, 0, activation, error, stream);
 }
 
 }  // extern "C"

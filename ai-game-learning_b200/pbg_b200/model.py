@@ -64,13 +64,14 @@ def linear(x: Tensor, weight: Tensor, bias: Tensor | None = None, activation: st
 
 
 def linear_ex(x: Tensor, weight: Tensor, bias: Tensor | None = None, activation: str | None = None, *,
-              row_scale: Tensor | None = None, residual: Tensor | None = None, out: Tensor | None = None,
-              out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+              row_scale: Tensor | None = None, residual: Tensor | None = None, residual_group: int = 1,
+              out: Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
     """``act(x @ weight.T * row_scale[:, None] + bias + residual)`` on ``pbg_linear_ex``.
 
     ``x`` bf16 ``[M, K]`` and ``out`` ``[M, N]`` may be column slices of wider buffers (rows
-    contiguous, any row stride); ``residual`` fp32 ``[M, N]`` likewise; ``row_scale`` fp32 ``[M]``.
-    The output is bf16 or fp32 (``out_dtype``, or ``out``'s dtype).
+    contiguous, any row stride); ``residual`` fp32 ``[M / residual_group, N]`` likewise, row m of
+    the output adding residual row ``m // residual_group``; ``row_scale`` fp32 ``[M]``.  The output
+    is bf16 or fp32 (``out_dtype``, or ``out``'s dtype).
     """
 
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or x.ndim != 2:
@@ -83,14 +84,15 @@ def linear_ex(x: Tensor, weight: Tensor, bias: Tensor | None = None, activation:
         raise NativeError("linear_ex: bias must be float32 [out]")
     if row_scale is not None and (row_scale.dtype != torch.float32 or row_scale.shape != (m,)):
         raise NativeError("linear_ex: row_scale must be float32 [M]")
-    if residual is not None and (residual.dtype != torch.float32 or residual.shape != (m, n)):
-        raise NativeError("linear_ex: residual must be float32 [M, out]")
+    if residual is not None and (residual.dtype != torch.float32 or residual_group < 1 or m % residual_group
+                                 or residual.shape != (m // residual_group, n)):
+        raise NativeError("linear_ex: residual must be float32 [M / residual_group, out]")
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype, device=x.device)
     if out.shape != (m, n) or out.dtype not in (torch.bfloat16, torch.float32):
         raise NativeError("linear_ex: out must be [M, out] bf16 or fp32")
     call("pbg_linear_ex", m, n, k, rows_ptr(x), x.stride(0), ptr(weight.contiguous()), ptr(bias), ptr(row_scale),
-         rows_ptr(residual), 0 if residual is None else residual.stride(0), rows_ptr(out), out.stride(0),
+         rows_ptr(residual), 0 if residual is None else residual.stride(0), residual_group, rows_ptr(out), out.stride(0),
          int(out.dtype == torch.float32), ACTIVATIONS[activation], ptr(_error_word(x.device)), stream(x.device))
     return out
 

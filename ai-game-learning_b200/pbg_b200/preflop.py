@@ -109,7 +109,7 @@ class _Map:
         return y.reshape(*lead, self.n)
 
     def apply(self, rows: Tensor, activation: str | None = None, *, row_scale: Tensor | None = None,
-              residual: Tensor | None = None, out: Tensor | None = None,
+              residual: Tensor | None = None, residual_group: int = 1, out: Tensor | None = None,
               out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
         """The map over a bf16 matrix of width kp (rows contiguous, any row stride) with the fused
         epilogue of ``linear_ex``: per-row scale, fp32 residual, fp32 or bf16 output."""
@@ -118,9 +118,18 @@ class _Map:
             raise NativeError("map operand must be a [rows, padded in] matrix")
         if self.np_ != self.n and (residual is not None or out is not None):
             raise NativeError("a fused residual or output buffer needs an unpadded output width")
-        y = linear_ex(rows, self.weight, self.bias, activation, row_scale=row_scale, residual=residual, out=out,
-                      out_dtype=out_dtype)
+        y = linear_ex(rows, self.weight, self.bias, activation, row_scale=row_scale, residual=residual,
+                      residual_group=residual_group, out=out, out_dtype=out_dtype)
         return y if self.np_ == self.n else y[:, : self.n]
+
+
+def _padded(x: Tensor, width: int) -> Tensor:
+    """x as a contiguous bf16 matrix zero-padded to ``width`` columns (the map's padded K)."""
+
+    x = x.reshape(-1, x.shape[-1]).to(torch.bfloat16)
+    if x.shape[1] != width:
+        x = F.pad(x, (0, width - x.shape[1]))
+    return x.contiguous()
 
 
 def _cat_maps(first: Tensor, second: Tensor) -> Tensor:
@@ -212,8 +221,13 @@ class FamilyModel:
             w1, b1 = maps[2], maps[3]
             self._factored[key] = (_Map(w1[:, :split], b1, self.device), _Map(w1[:, split:], None, self.device))
         row_map, ctx_map = self._factored[key]
-        hidden = row_map(rows).float() + ctx_map(context).float()[:, None, :]
-        return maps[1](F.gelu(hidden))
+        # the context projection is computed once per decision (fp32) and added to each of its rows in the
+        # row map's epilogue, GELU fused there too
+        batch, count, _ = rows.shape
+        ctx = ctx_map.apply(_padded(context, ctx_map.kp), out_dtype=torch.float32)
+        hidden = row_map.apply(_padded(rows.reshape(batch * count, -1), row_map.kp), "gelu", residual=ctx,
+                               residual_group=count)
+        return maps[1](hidden.view(batch, count, -1))
 
     def _ln_rows(self, x: Tensor, gain_bias, group_rows: int, out: Tensor) -> Tensor:
         """LayerNorm of the first ``group_rows`` tokens of every sequence of ``x`` [B, L, d] (fp32,

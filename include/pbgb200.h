@@ -426,13 +426,16 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *
  * of the incidence source map (pbg/games/poker/model/incidence.py:57-58), the
  * fp32 residual adds after the attention output and FFN maps (preflop.py:
  * 634-641, postflop.py:678-685), and the pre-GELU residual of the incidence
- * query map (incidence.py:77-84).  x rows are ldx elements apart (ldx >= K,
- * a multiple of 8), residual rows ldr floats apart (>= N, a multiple of 4,
- * 16-byte aligned), y rows ldy elements apart; y is fp32 when y_f32 is 1,
- * else bf16 (rows 16-byte aligned).  Other rules as for pbg_linear_bf16. */
+ * query map (incidence.py:77-84), and the context projection of a factored
+ * FFN (primitives.py:62-71), one residual row shared by residual_row_div
+ * consecutive rows (row m reads residual row m / residual_row_div).  x rows
+ * are ldx elements apart (ldx >= K, a multiple of 8), residual rows ldr
+ * floats apart (>= N, a multiple of 4, 16-byte aligned), y rows ldy elements
+ * apart; y is fp32 when y_f32 is 1, else bf16 (rows 16-byte aligned).  Other
+ * rules as for pbg_linear_bf16. */
 int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void *x, int64_t ldx, const void *w, const float *bias,
-                  const float *row_scale, const float *residual, int64_t ldr, void *y, int64_t ldy, int32_t y_f32,
-                  int32_t activation, uint32_t *error, void *stream);
+                  const float *row_scale, const float *residual, int64_t ldr, int64_t residual_row_div, void *y,
+                  int64_t ldy, int32_t y_f32, int32_t activation, uint32_t *error, void *stream);
 
 /* pbg/games/poker/model/primitives.py:63-283 (MHA, self-attention, heads of
  * width 32): out[b, q, h] = softmax_k((q_h / temperature_h) . k_h / sqrt(32)

@@ -20,7 +20,7 @@ def _bf(x):
 
 
 @pytest.mark.parametrize("m,n,k", [(300, 256, 256), (1000, 128, 384), (77, 256, 768)])
-@pytest.mark.parametrize("mode", ["scale_f32", "residual_f32", "residual_gelu_bf16", "strided"])
+@pytest.mark.parametrize("mode", ["scale_f32", "residual_f32", "residual_gelu_bf16", "strided", "grouped_residual"])
 def test_linear_ex_matches_torch(m, n, k, mode):
     from pbg_b200.model import linear_ex, pipeline_error
 
@@ -41,6 +41,11 @@ def test_linear_ex_matches_torch(m, n, k, mode):
     elif mode == "residual_gelu_bf16":
         y = linear_ex(x, w, bias, "gelu", residual=residual)
         want = F.gelu(acc + bias + residual)
+    elif mode == "grouped_residual":  # one residual row per group of rows (a factored FFN's context)
+        group = {300: 5, 1000: 8, 77: 7}[m]
+        ctx = torch.randn((m // group, n), generator=g, device=DEV)
+        y = linear_ex(x, w, bias, "gelu", residual=ctx, residual_group=group)
+        want = F.gelu(acc + bias + ctx.repeat_interleave(group, 0))
     else:  # strided operand, fp32 residual slice, output into a column slice of a wider bf16 buffer
         out_wide = torch.zeros((m, n + 128), dtype=torch.bfloat16, device=DEV)
         res_wide = torch.randn((m, n + 64), generator=g, device=DEV)
