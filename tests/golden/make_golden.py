@@ -830,8 +830,150 @@ def gen_folded(out):
     folded._phi_queries = original
 
 
+def gen_queued_model(out):
+    """queued/model.py:147-452 (QueuedPokerModel: retained model-input rows -> encoders -> outputs) on CPU.
+
+    A 3-handed R4 geometry: player-node states from seeded random-play trajectories, each encoded by
+    the reference's own direct_model_input with random log reach and the public history; postflop
+    rows with a folded seat carry the reference's packed folded statistics (as hooks.py:1968-2006
+    seals them).  The model is the reference QueuedPokerModel with branching heads, weights drawn by
+    model_params.parameter from the state_dict names.  Recorded: forward_partition for every
+    partition present, and learner_operation on a sampled private state.  Device guards lifted as in
+    the encoder runs (state_from_model_input, forward_partition and the folded-statistics board test).
+    """
+
+    import inspect
+    import textwrap
+
+    import torch
+    from pbg.core import tensor_ops
+    from pbg.core.rollout import child_path_keys
+    from pbg.games.poker.model import primitives
+    from pbg.games.poker.model.preflop import PokerModelConfig
+    from pbg.games.poker.queued import folded, hooks
+    from pbg.games.poker.queued import model as qmodel
+    from pbg.games.poker.queued.hooks import FOLDED, NLHEGeometry, PokerHistory, PokerStateMachine
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    import model_params
+
+    def lift(owner, name, guard, replacement="False", module=None):
+        source = textwrap.dedent(inspect.getsource(getattr(owner, name)))
+        assert guard in source, f"reference {name} changed shape"
+        namespace: dict = {}
+        mod = module or inspect.getmodule(owner)
+        exec(compile(source.replace(guard, replacement), mod.__file__, "exec"), mod.__dict__, namespace)
+        setattr(owner, name, namespace[name])
+
+    tensor_ops._accelerator = lambda value: None
+    lift(primitives.MHA, "forward", 'if q.device.type not in ("cuda", "mps"):', "if False:", primitives)
+    lift(hooks.PokerStateMachine, "state_from_model_input", 'model_input.device.type not in ("cuda", "mps")', "False",
+         hooks)
+    lift(qmodel.QueuedPokerModel, "forward_partition", 'model_input.device.type not in ("cuda", "mps")', "False",
+         qmodel)
+    lift(folded, "_folded_statistics_fp32", 'board_cards.device.type != "cuda"', "False", folded)
+
+    geometry = NLHEGeometry(3, 8.0, 4)
+    machine = PokerStateMachine(geometry)
+    cfg = PokerModelConfig(**dict(model_params.CONFIG, max_players=3, use_branching_heads=True,
+                                  max_history_tokens=geometry.player_node_bound + 3))
+    model = qmodel.QueuedPokerModel(geometry, cfg)
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            param.copy_(torch.from_numpy(model_params.parameter(name, tuple(param.shape))))
+    rng = np.random.default_rng(31)
+    B, seed, iteration = 48, 77, 5
+    state = machine.initial_roots(B, seed=seed, iteration=iteration, retry_epoch=0, device="cpu")
+    history = machine.empty_history(B, torch.device("cpu"))
+    path = torch.zeros(B, dtype=torch.int64)
+    root = torch.arange(B, dtype=torch.int64)
+    snaps = []
+    for step in range(40):
+        active = ~state.terminal
+        if not bool(active.any()):
+            break
+        rows = torch.nonzero(active).flatten()
+        sub = hooks.PokerState(*(getattr(state, n)[rows] for n in STATE_FIELDS))
+        sub_hist = PokerHistory(*(getattr(history, n)[rows] for n in HISTORY_FIELDS))
+        snaps.append((sub, sub_hist))
+        mask = machine.legality(sub).mask
+        chosen = []
+        for i in range(rows.numel()):
+            legal = torch.nonzero(mask[i]).flatten().numpy()
+            u = rng.random()
+            if u < 0.2 and mask[i, 0]:
+                chosen.append(0)
+            elif u < 0.6:
+                chosen.append(1)
+            else:
+                raises = legal[legal >= 2]
+                chosen.append(int(rng.choice(raises)) if raises.size else 1)
+        action = torch.tensor(chosen, dtype=torch.int32)
+        sub_hist = machine.append_player_history(sub, action, sub_hist)
+        nxt = machine.step_player(sub, action)
+        for generation in range(3):
+            chance = machine.needs_chance(nxt)
+            sub_hist = machine.append_chance_history(nxt, chance, sub_hist)
+            nxt = machine.deal_next_street_keyed(nxt, seed=seed, iteration=iteration, root=root[rows],
+                                                 path=path[rows], draw=generation, retry_epoch=0, lane=0)
+        for n in STATE_FIELDS:
+            getattr(state, n)[rows] = getattr(nxt, n)
+        for n in HISTORY_FIELDS:
+            getattr(history, n)[rows] = getattr(sub_hist, n)
+        path[rows] = child_path_keys(path[rows], 1)
+    groups: dict = {}
+    for sub, sub_hist in snaps:
+        for i in range(sub.rows):
+            if bool(sub.terminal[i]):
+                continue
+            street = int(sub.street[i])
+            live = int((sub.status[i] != FOLDED).sum())
+            kind = "pre" if street == 0 else f"post_{live}"
+            groups.setdefault(kind, []).append((sub, sub_hist, i))
+    out["partitions"] = np.array(sorted(groups))
+    for kind, items in sorted(groups.items()):
+        items = items[:: max(1, len(items) // 12)][:12]
+        st = hooks.PokerState(*(torch.stack([getattr(s, n)[i] for s, _, i in items]) for n in STATE_FIELDS))
+        hi = PokerHistory(*(torch.stack([getattr(h, n)[i] for _, h, i in items]) for n in HISTORY_FIELDS))
+        n, P, H = st.rows, geometry.players, geometry.private_hands
+        reach = torch.from_numpy(rng.standard_normal((n, P, H)).astype(np.float32) * 2.0)
+        reach[torch.from_numpy(rng.random((n, P, H)) < 0.15)] = -torch.inf
+        rows_in = machine.direct_model_input(kind, st, reach, hi)
+        if kind != "pre" and bool((st.status == FOLDED).any()):
+            summary = folded.folded_statistics(
+                geometry, board_cards=st.board_cards,
+                range_weights=torch.exp(reach).masked_fill(~torch.isfinite(reach), 0.0), status=st.status,
+                combo_cards=machine.combo_cards(torch.arange(H, dtype=torch.int32)), beta_rank=geometry.deck_cards,
+                line_dim=0, tight_mask=hooks.SequentialPokerHooks._tight_folder_mask(
+                    type("G", (), {"geometry": geometry})(), hi, st.status))
+            rows_in[:, geometry.postflop_base_model_input_width:] = folded.pack_folded_statistics(geometry, summary)
+        combos = machine.combo_cards(torch.arange(H, dtype=torch.int32)).to(torch.int64)
+        board = st.board_cards.to(torch.int64)
+        clash = ((combos[None, :, :, None] == board[:, None, None, :]) & (board != 255)[:, None, None, :]).any(-1).any(-1)
+        private = torch.stack([torch.from_numpy(rng.choice(np.nonzero(~clash[r].numpy())[0], P, replace=False))
+                               for r in range(n)]).to(torch.int32)
+        owner = st.to_act.to(torch.int64)
+        with torch.no_grad():
+            full = model.forward_partition(kind, rows_in)
+            learner = model.learner_operation(kind, rows_in, private, owner)
+        tag = "q_" + kind
+        out[tag + "_model_input"] = _np(rows_in)
+        out[tag + "_private"] = _np(private)
+        for name, value in full.policy_raw.items():
+            out[tag + "_raw_" + name] = _np(value)
+        out[tag + "_value"] = _np(full.value)
+        for name, value in full.public_heads.items():
+            out[tag + "_head_" + name] = _np(value)
+        for name, value in learner.policy_raw.items():
+            out[tag + "_lraw_" + name] = _np(value)
+        out[tag + "_lvalue"] = _np(learner.value)
+    spec = [name + ":" + ",".join(str(x) for x in param.shape) for name, param in model.named_parameters()]
+    out["param_spec"] = np.array(spec)
+    out["config"] = np.array([cfg.max_history_tokens, cfg.max_players])
+
+
 GENERATORS = {"posterior": gen_posterior, "preflop_model": gen_preflop_model, "postflop_model": gen_postflop_model,
-              "folded": gen_folded}
+              "folded": gen_folded, "queued_model": gen_queued_model}
 
 
 def main() -> None:
