@@ -90,6 +90,19 @@ class NLHEGeometry:
         return N.Geometry(self.players, self.stack_ticks, self.rank_count)
 
     @property
+    def player_node_bound(self) -> int:
+        return math.ceil(self.stack_bb * self.players + 3 * self.players - self.stack_bb + 1)
+
+    def model_private_width(self, input_type: str) -> int:
+        """hooks.py:164-169."""
+
+        if input_type == "pre":
+            return self.private_classes
+        if input_type.startswith("post_") and input_type[5:].isdigit():
+            return self.private_hands
+        raise ValueError(f"unknown poker input partition {input_type!r}")
+
+    @property
     def public_model_input_width(self) -> int:
         return 8 + 10 * self.players
 
@@ -363,6 +376,65 @@ class PokerStateMachine:
              ptr(None if log_reach is None else log_reach.float().contiguous()), hist, ptr(out), width,
              stream(state.device))
         return out
+
+    def state_from_model_input(self, input_type: str, model_input: Tensor, combo_ids: Tensor) -> PokerState:
+        """hooks.py:812-881: the public transition state recovered from a retained model-input row
+        (the layout direct_model_input writes), with the given private combos."""
+
+        g = self.geometry
+        players = g.players
+        if (not model_input.is_cuda or model_input.dtype not in (torch.float32, torch.float16, torch.bfloat16)
+                or model_input.ndim != 2 or model_input.shape[1] != g.model_input_width(input_type)
+                or combo_ids.shape != (model_input.shape[0], players) or combo_ids.dtype != torch.int32
+                or combo_ids.device != model_input.device):
+            raise QueuedPokerError("retained model input cannot reconstruct poker state")
+        value = model_input.float()
+        widths = (1, 5, players, players, players, players, players, 3 * players, players, 1, 1, players)
+        parts = torch.split(value[:, : sum(widths)], widths, dim=1)
+        scale = float(g.stack_bb)
+        board = torch.where(parts[1] < 0, torch.full_like(parts[1], PAD_CARD),
+                            torch.round(parts[1] * max(1, g.deck_cards - 1) + g.first_card)).to(torch.uint8)
+        state = PokerState(
+            board.contiguous(), combo_ids.contiguous(), parts[3].argmax(-1).to(torch.int32),
+            torch.round(parts[0][:, 0] * 3).to(torch.int32), parts[2].argmax(-1).to(torch.int32),
+            (parts[4] * scale).contiguous(), (parts[5] * scale).contiguous(), (parts[6] * scale).contiguous(),
+            parts[7].reshape(-1, players, 3).argmax(-1).to(torch.int8), (parts[9][:, 0] * scale).contiguous(),
+            (parts[10][:, 0] * scale).contiguous(), parts[8].gt(0.5).contiguous(), parts[11].gt(0.5).contiguous(),
+            torch.zeros(model_input.shape[0], dtype=torch.bool, device=model_input.device))
+        state.validate(g)
+        return state
+
+    def model_context(self, input_type: str, model_input: Tensor) -> tuple[Tensor, PokerHistory]:
+        """hooks.py:665-699: the retained log reach [B, P, K or H] and public history of a row."""
+
+        g = self.geometry
+        players, width, tokens = g.players, g.model_private_width(input_type), g.history_tokens
+        offset = 8 + 10 * players
+        reach = model_input[:, offset: offset + players * width].float()
+        offset += players * width
+        columns = [model_input[:, offset + i * tokens: offset + (i + 1) * tokens] for i in range(10)]
+        offset += 10 * tokens
+        base = g.preflop_model_input_width if input_type == "pre" else g.postflop_base_model_input_width
+        if offset != base or model_input.shape[1] != g.model_input_width(input_type):
+            raise QueuedPokerError("retained model context layout is not exact")
+        history = PokerHistory(*(columns[i].round().to(torch.int64) for i in range(3)),
+                               *(columns[i].float() for i in range(3, 9)), columns[9].gt(0.5))
+        return reach.reshape(-1, players, width), history
+
+    def expand_preflop_reach(self, compact: Tensor) -> Tensor:
+        """hooks.py:650-655: class-wide log reach spread to every combo of its class."""
+
+        if compact.shape[-1] != self.geometry.private_classes:
+            raise QueuedPokerError("preflop reach is not class-wide")
+        classes = self._combo_class(compact.device)
+        counts = torch.bincount(classes, minlength=self.geometry.private_classes).to(torch.float32)
+        return compact.index_select(-1, classes) - counts.log().index_select(0, classes)
+
+    def exact_model_context(self, input_type: str, model_input: Tensor) -> tuple[Tensor, PokerHistory]:
+        """hooks.py:701-706."""
+
+        reach, history = self.model_context(input_type, model_input)
+        return (self.expand_preflop_reach(reach) if input_type == "pre" else reach), history
 
     def combo_cards(self, combo_ids: Tensor) -> Tensor:
         ids = combo_ids.to(torch.int32).contiguous()

@@ -26,7 +26,7 @@ from torch import Tensor
 from torch.nn import functional as F
 
 from .checks import _assert, input_errors, raise_input_errors
-from .preflop import FamilyModel, PreflopConfig
+from .preflop import FamilyModel, PolicyOutput, PreflopConfig
 
 
 @dataclass
@@ -429,6 +429,13 @@ class PostflopModel(FamilyModel):
         """postflop.py:538-784 -> (raw policy fields over the full hand width [B,H,...], value [B,H]);
         with ``selected_private`` [B] the one selected row per decision ([B,1,...])."""
 
+        out = self.forward_output(pub, combo_ranges, actor_seat, masks, selected_private=selected_private)
+        return out.raw, out.v
+
+    def forward_output(self, pub: dict, combo_ranges: Tensor, actor_seat: Tensor | None = None,
+                       masks: PostflopMasks | None = None, *, selected_private: Tensor | None = None) -> PolicyOutput:
+        """postflop.py:538-784 -> PolicyOutput(raw, v, t, c)."""
+
         if masks is None:
             raise ValueError("postflop forward requires supplied compatibility")
         cfg, p, d, eps = self.cfg, self.p, self.cfg.d_model, self.cfg.eps
@@ -534,7 +541,8 @@ class PostflopModel(FamilyModel):
         raw["mu"] = raw["mu"].masked_fill(invalid[..., None], 0.5)
         raw["s"] = raw["s"].masked_fill(invalid[..., None], 1.0)
         raw["iota"] = raw["iota"].masked_fill(invalid, 0.5)
-        return raw, value
+        t, cost = self._branching(global_feature, public_mean, padded)
+        return PolicyOutput(raw, value, t, cost)
 
 
 def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int, ...]]:

@@ -80,6 +80,16 @@ def class_geometry(rank_count: int):
     return sizes, orbit, torch.stack((within, cross), dim=1)
 
 
+@dataclass
+class PolicyOutput:
+    """preflop.py PolicyOutput: raw policy fields, values, and the optional public branching heads."""
+
+    raw: dict
+    v: Tensor
+    t: Tensor | None = None
+    c: Tensor | None = None
+
+
 class _Map:
     """A Linear bound for pbg_linear_bf16: bf16 weight padded to K % 64 == 0 and N % 128 == 0."""
 
@@ -192,6 +202,12 @@ class FamilyModel:
         self.mixture_affine = lin("raise_head.mixture_affine")
         self.allin_affine = lin("raise_head.allin_affine")
         self.value_affine = lin("value_head.affine")
+        # PublicBranchingHeads (heads.py:83-104), present when the configuration enables them
+        self.branching = None
+        if "branching_heads.public_features.w1.weight" in p:
+            self.branching = (ffn("branching_heads.public_features"), ffn("branching_heads.t_features"),
+                              ffn("branching_heads.c_features"), lin("branching_heads.t_affine"),
+                              lin("branching_heads.c_affine"))
         self._factored: dict = {}
 
     # ------------------------------------------------------------ kernels
@@ -304,23 +320,43 @@ class FamilyModel:
             x = layer["ffn_out"].apply(hidden, residual=x_hat, out_dtype=torch.float32).view(batch, length, d)
         return x
 
+    def _head(self, head: "_Map", x: Tensor) -> Tensor:
+        """A final affine head with fp32 output (the fields leave the network in fp32)."""
+
+        lead = x.shape[:-1]
+        return head.apply(_padded(x, head.kp), out_dtype=torch.float32).reshape(*lead, head.n)
+
     def _readout(self, actor_rows: Tensor, private_embedding: Tensor, anchors: Tensor, global_feature: Tensor):
         """shared.py:74-92 readout -> (raw policy fields, value)."""
 
         cfg = self.cfg
         rows = torch.cat((actor_rows, private_embedding), -1)
         context = torch.cat((anchors.flatten(1), global_feature), -1)
-        z_type = self._ffn_factored(self.type_features, rows, context).float()
-        z_raise = self._ffn_factored(self.raise_features, rows, context).float()
-        raw = self.mixture_affine(z_raise).float()
+        z_type = self._ffn_factored(self.type_features, rows, context)
+        z_raise = self._ffn_factored(self.raise_features, rows, context)
+        raw = self._head(self.mixture_affine, z_raise)
         m = cfg.m_raise
         omega = torch.softmax(raw[..., :m], -1)
         mu = torch.sigmoid(raw[..., m:2 * m])
         s = F.softplus(raw[..., 2 * m:]) + cfg.s_min
-        iota = torch.sigmoid(self.allin_affine(z_type).float()).squeeze(-1)
+        iota = torch.sigmoid(self._head(self.allin_affine, z_type)).squeeze(-1)
         value_features = self._ffn_factored(self.value_features, rows, context)
-        value = self.value_affine(value_features).float().squeeze(-1)
-        return {"type_logits": self.type_head(z_type).float(), "omega": omega, "mu": mu, "s": s, "iota": iota}, value
+        value = self._head(self.value_affine, value_features).squeeze(-1)
+        return {"type_logits": self._head(self.type_head, z_type), "omega": omega, "mu": mu, "s": s,
+                "iota": iota}, value
+
+    def _branching(self, global_feature: Tensor, public_mean: Tensor, padded_seats: Tensor):
+        """heads.py:83-104 (PublicBranchingHeads) on [global feature, public mean, seat summaries]:
+        (trace variance T, subtree cost C), fp32 [B]; (None, None) when the heads are absent."""
+
+        if self.branching is None:
+            return None, None
+        public_features, t_features, c_features, t_affine, c_affine = self.branching
+        public = torch.cat((global_feature, public_mean, padded_seats.flatten(1)), -1)
+        features = self._ffn(public_features, public)
+        t_logit = self._head(t_affine, self._ffn(t_features, features)).squeeze(-1)
+        c_logit = self._head(c_affine, self._ffn(c_features, features)).squeeze(-1)
+        return torch.sigmoid(t_logit), torch.exp(c_logit.clamp(min=-30.0, max=30.0))
 
 
 class PreflopModel(FamilyModel):
@@ -390,8 +426,16 @@ class PreflopModel(FamilyModel):
                 torch.cat((valid, torch.ones((batch, 1), dtype=torch.bool, device=dev)), 1))
 
     def forward(self, pub: dict, class_ranges: Tensor, class_mask: Tensor | None = None,
-                actor_seat: Tensor | None = None):
-        """preflop.py:472-693 -> (raw policy fields, value [B, K])."""
+                actor_seat: Tensor | None = None, *, selected_private: Tensor | None = None):
+        """preflop.py:472-693 -> (raw policy fields, value [B, K]) ([B, 1] with ``selected_private``)."""
+
+        out = self.forward_output(pub, class_ranges, class_mask, actor_seat, selected_private=selected_private)
+        return out.raw, out.v
+
+    def forward_output(self, pub: dict, class_ranges: Tensor, class_mask: Tensor | None = None,
+                       actor_seat: Tensor | None = None, *, selected_private: Tensor | None = None) -> PolicyOutput:
+        """preflop.py:472-693 -> PolicyOutput(raw, v, t, c): every actor class row, or the one class
+        ``selected_private`` [B] names (the learner row), and the public branching heads."""
 
         cfg, p, dev = self.cfg, self.p, self.device
         d, K = cfg.d_model, self.n_classes
@@ -459,7 +503,13 @@ class PreflopModel(FamilyModel):
         global_feature = self._ffn(self.global_features,
                                    torch.cat((public_mean, actor_summary, padded.reshape(batch, -1)), -1)).float()
         actor_rows = final_rows[torch.arange(batch, device=dev), actor]
-        return self._readout(actor_rows, class_emb, final_anchors, global_feature)
+        if selected_private is not None:
+            selected = selected_private.to(dev).long()[:, None, None]
+            actor_rows = actor_rows.gather(1, selected.expand(-1, 1, d))
+            class_emb = class_emb.gather(1, selected.expand(-1, 1, cfg.class_embedding_dim))
+        raw, value = self._readout(actor_rows, class_emb, final_anchors, global_feature)
+        t, cost = self._branching(global_feature, public_mean, padded)
+        return PolicyOutput(raw, value, t, cost)
 
 
 
@@ -511,4 +561,4 @@ def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int
     return shapes
 
 
-__all__ = ["FamilyModel", "PreflopConfig", "PreflopModel", "class_geometry", "parameter_shapes"]
+__all__ = ["FamilyModel", "PolicyOutput", "PreflopConfig", "PreflopModel", "class_geometry", "parameter_shapes"]

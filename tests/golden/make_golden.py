@@ -834,7 +834,8 @@ def gen_queued_model(out):
     """queued/model.py:147-452 (QueuedPokerModel: retained model-input rows -> encoders -> outputs) on CPU.
 
     A 3-handed R4 geometry: player-node states from seeded random-play trajectories, each encoded by
-    the reference's own direct_model_input with random log reach and the public history; postflop
+    the reference's own direct_model_input with random log reach (log path probabilities, at most 0)
+    and the public history; postflop
     rows with a folded seat carry the reference's packed folded statistics (as hooks.py:1968-2006
     seals them).  The model is the reference QueuedPokerModel with branching heads, weights drawn by
     model_params.parameter from the state_dict names.  Recorded: forward_partition for every
@@ -936,7 +937,8 @@ def gen_queued_model(out):
         st = hooks.PokerState(*(torch.stack([getattr(s, n)[i] for s, _, i in items]) for n in STATE_FIELDS))
         hi = PokerHistory(*(torch.stack([getattr(h, n)[i] for _, h, i in items]) for n in HISTORY_FIELDS))
         n, P, H = st.rows, geometry.players, geometry.private_hands
-        reach = torch.from_numpy(rng.standard_normal((n, P, H)).astype(np.float32) * 2.0)
+        # log reach as the rollout carries it: log of path probabilities (at most 0), some rows unreachable
+        reach = torch.from_numpy(np.log(rng.random((n, P, H)).astype(np.float32) ** 2))
         reach[torch.from_numpy(rng.random((n, P, H)) < 0.15)] = -torch.inf
         rows_in = machine.direct_model_input(kind, st, reach, hi)
         if kind != "pre" and bool((st.status == FOLDED).any()):
