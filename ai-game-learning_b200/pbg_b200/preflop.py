@@ -202,12 +202,9 @@ class FamilyModel:
         self.mixture_affine = lin("raise_head.mixture_affine")
         self.allin_affine = lin("raise_head.allin_affine")
         self.value_affine = lin("value_head.affine")
-        # PublicBranchingHeads (heads.py:83-104), present when the configuration enables them
-        self.branching = None
-        if "branching_heads.public_features.w1.weight" in p:
-            self.branching = (ffn("branching_heads.public_features"), ffn("branching_heads.t_features"),
-                              ffn("branching_heads.c_features"), lin("branching_heads.t_affine"),
-                              lin("branching_heads.c_affine"))
+        # PublicBranchingHeads (heads.py:83-104), present when the configuration enables them: one
+        # public row per decision, evaluated in fp32 (the cost head is an exponential of its logit)
+        self.branching = "branching_heads.public_features.w1.weight" in p
         self._factored: dict = {}
 
     # ------------------------------------------------------------ kernels
@@ -349,13 +346,20 @@ class FamilyModel:
         """heads.py:83-104 (PublicBranchingHeads) on [global feature, public mean, seat summaries]:
         (trace variance T, subtree cost C), fp32 [B]; (None, None) when the heads are absent."""
 
-        if self.branching is None:
+        if not self.branching:
             return None, None
-        public_features, t_features, c_features, t_affine, c_affine = self.branching
-        public = torch.cat((global_feature, public_mean, padded_seats.flatten(1)), -1)
-        features = self._ffn(public_features, public)
-        t_logit = self._head(t_affine, self._ffn(t_features, features)).squeeze(-1)
-        c_logit = self._head(c_affine, self._ffn(c_features, features)).squeeze(-1)
+        p = self.p
+
+        def ffn(name: str, x: Tensor) -> Tensor:
+            hidden = F.gelu(F.linear(x, p[name + ".w1.weight"], p[name + ".w1.bias"]))
+            return F.linear(hidden, p[name + ".w2.weight"], p[name + ".w2.bias"])
+
+        public = torch.cat((global_feature, public_mean, padded_seats.flatten(1)), -1).float()
+        features = ffn("branching_heads.public_features", public)
+        t_logit = F.linear(ffn("branching_heads.t_features", features), p["branching_heads.t_affine.weight"],
+                           p["branching_heads.t_affine.bias"]).squeeze(-1)
+        c_logit = F.linear(ffn("branching_heads.c_features", features), p["branching_heads.c_affine.weight"],
+                           p["branching_heads.c_affine.bias"]).squeeze(-1)
         return torch.sigmoid(t_logit), torch.exp(c_logit.clamp(min=-30.0, max=30.0))
 
 
