@@ -632,6 +632,92 @@ def _time_forward(device, forward, reps: int):
     return ms, eager_ms
 
 
+def _device_ms(device, fn, reps: int = 10) -> float:
+    """Median CUDA-event time (ms) of fn, each call queued behind a device-side sleep."""
+
+    import torch
+
+    times = []
+    for rep in range(reps + 2):
+        torch.cuda._sleep(1_000_000)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize(device)
+        if rep >= 2:
+            times.append(a.elapsed_time(e))
+    return sorted(times)[len(times) // 2]
+
+
+def folded_component(device, rows=64):
+    """Multiway folded statistics (queued/folded.py): 6-max R13, four folded seats (all tight), flop
+    boards, `rows` decisions; the finite-difference removal queries (1 + 52 + 1326 per decision) in
+    one launch of pbg_folded_phi_queries, and the whole folded_statistics call (normalisation, queries,
+    assembly, torch.linalg.eigh of the 52 x 52 beta matrices, card masses)."""
+
+    import torch
+    from pbg_b200.folded import folded_statistics, phi_queries
+    from pbg_b200.poker import NLHEGeometry, PokerStateMachine
+
+    geo = NLHEGeometry(6, 100.0, 13)
+    combo = PokerStateMachine(geo).combo_cards(torch.arange(geo.private_hands, dtype=torch.int32, device=device))
+    g = torch.Generator(device=device).manual_seed(23)
+    status = torch.zeros((rows, 6), dtype=torch.int8, device=device)
+    status[:, 2:] = 1
+    board = torch.full((rows, 5), 255, dtype=torch.uint8, device=device)
+    board[:, :3] = torch.tensor([3, 17, 40], dtype=torch.uint8, device=device)
+    weights = torch.rand((rows, 6, geo.private_hands), generator=g, device=device)
+    folder = status.eq(1)
+    raw = weights * folder[..., None]
+    clash = ((combo.long()[None, :, :, None] == board.long()[:, None, None, :]) & (board != 255)[:, None, None, :]).any(-1).any(-1)
+    raw = raw.masked_fill(clash[:, None], 0.0)
+    prob = raw / raw.sum(-1, keepdim=True).clamp_min(1e-38)
+    base = torch.full((rows,), 49.0, device=device)
+    queries_ms = _device_ms(device, lambda: phi_queries(prob, folder, folder, base, 52))
+    whole_ms = _device_ms(device, lambda: folded_statistics(geo, board_cards=board, range_weights=weights, status=status,
+                                                            combo_cards=combo, beta_rank=52, line_dim=0), reps=5)
+    queries = 1 + 52 + 1326
+    return {"workload": f"folded statistics, 6-max R13, 4 tight folders, flop, {rows} decisions x {queries} removal "
+                        "queries", "phi_queries_ms": queries_ms, "folded_statistics_ms": whole_ms,
+            "queries_per_s": rows * queries / (queries_ms / 1000.0), "decisions_per_s": rows / (whole_ms / 1000.0),
+            "bound": "FP32 issue (per-query hand sums over shared memory)", "kernel": "folded_phi_kernel",
+            "gpu_launches": 1}
+
+
+def branching_component(device, n_alias=65536, n_nodes=200000):
+    """Branched learner sampling metadata: the Walker alias table over `n_alias` weights
+    (alias_table.cu) and the decision log mass of an `n_nodes`-node forest (branching_metadata.cu),
+    each launch sequence queued behind a device-side sleep."""
+
+    import numpy as np
+    import torch
+    from pbg_b200.branching import build_alias_table, decision_log_mass
+
+    logw = torch.linspace(-40.0, 0.0, n_alias, dtype=torch.float64, device=device)
+    w = torch.softmax(logw, 0) * n_alias
+    prob, alias = torch.empty_like(w), torch.empty(n_alias, dtype=torch.int32, device=device)
+    alias_ms = _device_ms(device, lambda: build_alias_table(w.clone(), prob, alias))
+    rng = np.random.default_rng(5)
+    parent = np.full(n_nodes, -1, dtype=np.int32)
+    degree = np.zeros(n_nodes, dtype=np.int32)
+    nxt = 1
+    for node in range(n_nodes):
+        kids = min(int(rng.integers(1, 6)), n_nodes - nxt)
+        parent[nxt: nxt + kids] = node
+        degree[node] = kids
+        nxt += kids
+        if nxt >= n_nodes:
+            break
+    pp, dd = torch.from_numpy(parent).to(device), torch.from_numpy(degree).to(device)
+    fail = torch.zeros(1, dtype=torch.int32, device=device)
+    mass_ms = _device_ms(device, lambda: decision_log_mass(pp, dd, fail))
+    return {"workload": f"alias table over {n_alias} weights; decision log mass of a {n_nodes}-node forest",
+            "alias_table_ms": alias_ms, "decision_log_mass_ms": mass_ms,
+            "kernels": ["alias_classify_kernel", "alias_block_scan_kernel", "alias_scatter_kernel", "alias_pair_kernel",
+                        "decision_log_mass_kernel"], "gpu_launches": 6}
+
+
 def posterior_component(device, parents=4096, rows=16384, reps=10):
     """Collision-conditioned posterior profiles (rb_sampling.py): 6-max R13 (1326 private hands), `parents`
     parent rows of [6, 1326] fp32 range weights (board-conflicting hands masked; flop/turn/river boards),
@@ -894,7 +980,9 @@ def main():
                                   "model_attention": model_attention_component(device),
                                   "preflop_forward": preflop_forward_component(device),
                                   "postflop_forward": postflop_forward_component(device),
-                                  "posterior_sampler": posterior_component(device)}
+                                  "posterior_sampler": posterior_component(device),
+                                  "folded_statistics": folded_component(device),
+                                  "branched_sampling": branching_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:
