@@ -259,4 +259,29 @@ class QueuedPokerModel:
     __call__ = forward
 
 
-__all__ = ["ModelEvaluation", "PokerModelError", "QueuedPokerModel", "fold_line_metadata"]
+def parameter_shapes(cfg: PreflopConfig, rank_count: int, branching_heads: bool = False) -> dict[str, tuple[int, ...]]:
+    """The reference QueuedPokerModel's parameter names and shapes (``shared.*``, ``pre_encoder.*``,
+    ``post_encoder.*``; model.py:150-164), with the public branching heads when the mode is branched."""
+
+    from .postflop import parameter_shapes as post_shapes
+    from .preflop import parameter_shapes as pre_shapes
+
+    pre = pre_shapes(cfg, rank_count)
+    shared = {k: v for k, v in pre.items() if not k.startswith(("class_embedding", "class_row_affine"))}
+    shapes = {f"shared.{k}": v for k, v in shared.items()}
+    heads = {}
+    if branching_heads:
+        d, h = cfg.d_model, cfg.hidden
+        public = (2 + cfg.max_players) * d
+        for name, fan_in in (("public_features", public), ("t_features", d), ("c_features", d)):
+            heads.update({f"branching_heads.{name}.w1.weight": (h, fan_in), f"branching_heads.{name}.w1.bias": (h,),
+                          f"branching_heads.{name}.w2.weight": (d, h), f"branching_heads.{name}.w2.bias": (d,)})
+        for name in ("t_affine", "c_affine"):
+            heads.update({f"branching_heads.{name}.weight": (1, d), f"branching_heads.{name}.bias": (1,)})
+    for family, table in (("pre_encoder", pre), ("post_encoder", post_shapes(cfg, rank_count))):
+        shapes.update({f"{family}.{k}": v for k, v in table.items() if k not in shared})
+        shapes.update({f"{family}.{k}": v for k, v in heads.items()})
+    return shapes
+
+
+__all__ = ["ModelEvaluation", "PokerModelError", "QueuedPokerModel", "fold_line_metadata", "parameter_shapes"]

@@ -632,6 +632,52 @@ def _time_forward(device, forward, reps: int):
     return ms, eager_ms
 
 
+def rollout_with_model_component(device, hands=1024):
+    """Family-scheduled rollout with the policy network in the loop (pbg_b200.family_rollout): HU 100bb
+    R13 (cfg2), `hands` roots played to the end; every step groups the live hands by partition (preflop
+    classes / postflop combos), encodes their retained rows, evaluates QueuedPokerModel with cfg2's
+    architecture (d_model 128, 2 layers, 4 heads, class embedding 32, hidden 512, M = 2; random weights)
+    and runs the fused rollout step and reach update.  Player decisions per second of the whole loop
+    (host grouping included), the metric of pbg.benchmark's player_nodes_per_second."""
+
+    import time
+
+    import torch
+    from pbg_b200.family_rollout import FamilyRollout
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.preflop import PreflopConfig
+    from pbg_b200.queued_model import QueuedPokerModel, parameter_shapes
+
+    geo = NLHEGeometry(2, 100.0, 13)
+    cfg = PreflopConfig(d_model=128, n_heads=4, layers=2, m_raise=2, k_act=5, max_players=2,
+                        class_embedding_dim=32, ffn_hidden=512, max_history_tokens=geo.history_tokens)
+    model = QueuedPokerModel(geo, cfg, _random_params(parameter_shapes(cfg, 13), seed=29), device)
+
+    def play():
+        roll = FamilyRollout(model, seed=41, iteration=3)
+        arena, log_reach = roll.roots(hands, device=device)
+        total, steps = 0, 0
+        while True:
+            n = roll.step(arena, log_reach)
+            if n == 0:
+                break
+            total, steps = total + n, steps + 1
+        return total, steps, roll.families
+
+    play()  # warm-up (bindings, first launches)
+    torch.cuda.synchronize(device)
+    t = time.perf_counter()
+    decisions, steps, families = play()
+    torch.cuda.synchronize(device)
+    seconds = time.perf_counter() - t
+    return {"workload": f"family-scheduled rollout with the model in the loop, HU 100bb R13, {hands} hands to the "
+                        "end, cfg2 architecture (d_model 128, 2 layers, 4 heads), random weights",
+            "decisions": decisions, "steps": steps, "families": families, "seconds": seconds,
+            "decisions_per_s": decisions / seconds,
+            "kernels": ["direct_model_input_kernel", "linear_tcgen05_kernel", "attention_kernel", "rollout_step_kernel",
+                        "reach_kernel"]}
+
+
 def _device_ms(device, fn, reps: int = 10) -> float:
     """Median CUDA-event time (ms) of fn, each call queued behind a device-side sleep."""
 
@@ -982,7 +1028,8 @@ def main():
                                   "postflop_forward": postflop_forward_component(device),
                                   "posterior_sampler": posterior_component(device),
                                   "folded_statistics": folded_component(device),
-                                  "branched_sampling": branching_component(device)}
+                                  "branched_sampling": branching_component(device),
+                                  "rollout_with_model": rollout_with_model_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1:

@@ -76,3 +76,18 @@ def test_compact_map_rejects_bad_inputs():
         build_compact_map(torch.ones((2, 4), dtype=torch.bool), 5)
     with pytest.raises(ValueError, match="omits compatible rows"):
         build_compact_map(torch.ones((2, 4), dtype=torch.bool), 3)
+
+
+def test_queued_parameter_shapes_match_reference_module(gold):
+    import model_params
+    from pbg_b200.preflop import PreflopConfig
+    from pbg_b200.queued_model import parameter_shapes
+
+    d = gold("queued_model")
+    spec = {}
+    for item in d["param_spec"]:
+        name, dims = str(item).split(":")
+        spec[name] = tuple(int(x) for x in dims.split(","))
+    history, players = (int(x) for x in d["config"])
+    cfg = PreflopConfig(**dict(model_params.CONFIG, max_players=players, max_history_tokens=history))
+    assert parameter_shapes(cfg, model_params.RANKS, branching_heads=True) == spec
