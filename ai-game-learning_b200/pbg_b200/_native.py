@@ -107,6 +107,7 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_decision_log_mass": (_I32, [_I64, _P, _P, _P, _P, _P, _P]),
     "pbg_folded_query_count": (_I64, [_I32]),
     "pbg_folded_phi_queries": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_symmetric_eigh": (_I32, [_I64, _I32, _P, _P, _P, _I32, _P]),
     "pbg_layered_targets_workspace_words": (_I64, [_I32]),
     "pbg_layered_targets": (_I32, [_P, _I32, TargetNodes, TargetChildren, TargetTables, _I32, _I32, _I32, _I32,
                                    _I32, _I32, ctypes.c_float, _I32, _I32, _P, _P, _P]),

@@ -5,9 +5,11 @@ private hand, the signed beta eigenpairs, folder log masses, card masses, line
 metadata, masks, seats and the tight-cluster scalar) for the postflop model
 input.  The finite-difference estimator over every zero-, one- and two-card
 removal query (folded.py:111-232, the reference's dense chunked einsums) runs in
-one launch of ``pbg_folded_phi_queries``; the range normalisation before it and
-the alpha / beta assembly, ``torch.linalg.eigh`` and the card masses after it
-are torch operations on the device, as in the reference.
+one launch of ``pbg_folded_phi_queries``; the eigendecomposition of the beta
+matrices (the reference's ``torch.linalg.eigh``) runs in one launch of
+``pbg_symmetric_eigh``; the range normalisation and the alpha / beta assembly
+and card masses around them are torch operations on the device, as in the
+reference.
 """
 
 from __future__ import annotations
@@ -73,6 +75,22 @@ def phi_queries(probability: Tensor, folder_mask: Tensor, tight_mask: Tensor, ba
     return phi, triple
 
 
+def symmetric_eigh(matrices: Tensor, max_sweeps: int = 20) -> tuple[Tensor, Tensor]:
+    """torch.linalg.eigh's contract for a batch of small symmetric fp32 matrices [B, n, n] (n <= 64):
+    eigenvalues ascending [B, n] and eigenvectors as columns [B, n, n], on pbg_symmetric_eigh (Jacobi,
+    one CTA per matrix) instead of a library solver that takes the batch one matrix at a time."""
+
+    if matrices.ndim != 3 or matrices.shape[1] != matrices.shape[2] or not matrices.is_cuda:
+        raise NativeError("symmetric_eigh takes CUDA matrices [B, n, n]")
+    batch, n, _ = matrices.shape
+    source = matrices.to(torch.float32).contiguous()
+    values = torch.empty((batch, n), dtype=torch.float32, device=source.device)
+    vectors = torch.empty((batch, n, n), dtype=torch.float32, device=source.device)
+    call("pbg_symmetric_eigh", batch, n, ptr(source), ptr(values), ptr(vectors), max_sweeps, stream(source.device))
+    order = values.argsort(-1)
+    return values.gather(1, order), vectors.gather(2, order[:, None].expand(-1, n, -1))
+
+
 def _board_card_mask(board_cards: Tensor, board_valid: Tensor, first_card: int, cards: int) -> Tensor:
     """folded.py:330-336: each board slot's validity written at its clamped deck-local index in slot
     order (an empty slot, clamped to the last card, written after that card clears its mark)."""
@@ -133,7 +151,7 @@ def _folded_statistics_fp32(geometry: NLHEGeometry, *, board_cards: Tensor, rang
     hand_log_ratio = (alpha[:, combo_local[:, 0]] + alpha[:, combo_local[:, 1]]
                       + beta[:, combo_local[:, 0], combo_local[:, 1]])
     if beta_rank:
-        eigenvalue, eigenvector = torch.linalg.eigh(beta)
+        eigenvalue, eigenvector = symmetric_eigh(beta)
         order = torch.argsort(eigenvalue.abs(), dim=-1, descending=True, stable=True)[:, :beta_rank]
         eigenvalue = eigenvalue.gather(1, order)
         eigenvector = eigenvector.gather(2, order[:, None].expand(-1, cards, -1))
@@ -224,5 +242,5 @@ def unpack_folded_statistics(geometry: NLHEGeometry, packed: Tensor, *, beta_ran
 
 
 __all__ = ["FoldedStatisticsError", "folded_statistics", "folded_statistics_workspace_row_bytes",
-           "pack_folded_statistics", "phi_queries", "sequential_family_workspace_row_bytes",
+           "pack_folded_statistics", "phi_queries", "sequential_family_workspace_row_bytes", "symmetric_eigh",
            "unpack_folded_statistics"]

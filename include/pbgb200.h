@@ -355,6 +355,15 @@ int pbg_folded_phi_queries(int64_t batch, int32_t players, int32_t cards, const 
                            const uint8_t *folder_mask, const uint8_t *tight_mask, const float *base_cards,
                            float *phi, float *triple, void *stream);
 
+/* Batched symmetric eigendecomposition, n <= 64 (the beta matrices of the
+ * folded statistics, pbg/games/poker/queued/folded.py:352, there
+ * torch.linalg.eigh): cyclic Jacobi with round-robin parallel ordering, one CTA
+ * per matrix, fp32.  matrices f32 [batch, n, n] (the symmetric part is used),
+ * values f32 [batch, n] and vectors f32 [batch, n, n] (eigenvector j in column
+ * j), unsorted; at most max_sweeps sweeps. */
+int pbg_symmetric_eigh(int64_t batch, int32_t n, const float *matrices, float *values, float *vectors,
+                       int32_t max_sweeps, void *stream);
+
 /* ------------------------------------------------------- layered targets */
 
 /* Device tables of per-partition arena pointers (int64 device addresses, 0 =

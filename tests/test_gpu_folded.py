@@ -244,3 +244,25 @@ def test_timing_six_handed_full_deck():
     torch.cuda.synchronize()
     print(f"\nfolded phi queries, 6-handed R13, 4 folders (all tight), {batch} rows x 1379 queries: "
           f"{a.elapsed_time(b):.3f} ms; whole folded_statistics {1e3 * (time.perf_counter() - t):.1f} ms")
+
+
+@pytest.mark.parametrize("n,batch", [(52, 40), (16, 7), (20, 3), (33, 5)])
+def test_symmetric_eigh_matches_torch(n, batch):
+    from pbg_b200.folded import symmetric_eigh
+
+    g = torch.Generator(device=DEV).manual_seed(n)
+    a = torch.randn((batch, n, n), generator=g, device=DEV) * 0.1
+    a = a + a.transpose(1, 2)
+    a[0, :5] = 0.0          # zero rows and columns (board cards): a degenerate zero eigenvalue
+    a[0, :, :5] = 0.0
+    if batch > 1:
+        a[1] = torch.diag(torch.tensor([1.0, 1.0, -2.0] + [0.5] * (n - 3), device=DEV))  # repeated eigenvalues
+    values, vectors = symmetric_eigh(a)
+    want = torch.linalg.eigh(a.double()).eigenvalues.float()
+    scale = float(want.abs().max())
+    torch.testing.assert_close(values, want, rtol=0, atol=2e-6 * scale * n)
+    eye = torch.eye(n, device=DEV).expand(batch, -1, -1)
+    # fp32 rotations accumulate about one rounding per sweep and index into V: orthogonal to 5e-5 at n = 52
+    torch.testing.assert_close(vectors.transpose(1, 2) @ vectors, eye, rtol=0, atol=5e-5)
+    torch.testing.assert_close(vectors @ torch.diag_embed(values) @ vectors.transpose(1, 2), a, rtol=0,
+                               atol=2e-6 * scale * n)
