@@ -34,6 +34,17 @@ constexpr int FD_MAXC = 52;
 constexpr int FD_CPAD = 64;
 constexpr int FD_WARPS = 8;
 constexpr int FD_THREADS = 32 * FD_WARPS;
+constexpr int FD_DENSE = 4;  // folders handled by the one-pass path
+// pair s of four dense folder slots, (i < j) in lexicographic order, and the other two slots of the
+// pair (its hubs, increasing): the seat order the reference accumulates pairs and hubs in.  Unrolled
+// loops over s make these compile-time constants (register arrays stay in registers).
+__device__ __forceinline__ constexpr int fd_pair_i(int s) { return s < 3 ? 0 : (s < 5 ? 1 : 2); }
+__device__ __forceinline__ constexpr int fd_pair_j(int s) { return s < 3 ? s + 1 : (s < 5 ? s - 1 : 3); }
+__device__ __forceinline__ constexpr int fd_hub(int s, int u) {
+    // the u-th slot of {0, 1, 2, 3} outside {i, j}
+    return u == 0 ? (fd_pair_i(s) == 0 ? (fd_pair_j(s) == 1 ? 2 : 1) : 0)
+                  : (fd_pair_j(s) == 3 ? (fd_pair_i(s) == 2 ? 1 : 2) : 3);
+}
 
 __device__ __forceinline__ float fd_clamp_tiny(float x) {
     // torch's clamp_min: NaN passes through
@@ -56,7 +67,7 @@ __device__ __forceinline__ float fd_warp_sum(float v) {
     return v;
 }
 
-__global__ void __launch_bounds__(FD_THREADS)
+__global__ void __launch_bounds__(FD_THREADS, 3)
 folded_phi_kernel(int players, int cards, int hands, int queries, int queries_per_warp,
                   const float* __restrict__ probability, const uint8_t* __restrict__ folder_mask,
                   const uint8_t* __restrict__ tight_mask, const float* __restrict__ base_cards,
@@ -77,6 +88,18 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
         tmask |= (tight_mask[row * players + f] ? 1u : 0u) << f;
     }
     const int folders = __popc(fmask);
+    // the folders in seat order as dense slots, and which slots are tight
+    int fseat[FD_DENSE] = {0, 0, 0, 0};
+    unsigned dtight = 0;
+    {
+        int k = 0;
+        for (int f = 0; f < players && k < FD_DENSE; ++f)
+            if (fmask >> f & 1u) {
+                fseat[k] = f;
+                dtight |= (tmask >> f & 1u) << k;
+                ++k;
+            }
+    }
     const float* src = probability + row * (int64_t)players * hands;
     for (int i = threadIdx.x; i < players * hands; i += FD_THREADS) prob[i] = src[i];
     for (int h = threadIdx.x; h < hands; h += FD_THREADS) {
@@ -159,6 +182,82 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
             if (folders > packed) phi = phi + logf(fd_clamp_tiny(numerator / denominator));
         }
 
+        float triple = 0.0f;
+        if (folders <= FD_DENSE) {
+            // the dense slots' surviving masses (selected with compile-time indices)
+            float sd[FD_DENSE];
+#pragma unroll
+            for (int k = 0; k < FD_DENSE; ++k) {
+                sd[k] = 1.0f;
+#pragma unroll
+                for (int f = 0; f < FD_MAXP; ++f) sd[k] = fseat[k] == f ? surviving[f] : sd[k];
+            }
+            // at most four folders (every decision with two live seats or more at six seats): one pass
+            // over the surviving hands accumulates every folder pair's identical-hand sum and every tight
+            // pair's edge sum against each of its (at most two) hubs
+            float ident[6], tri[6][2];
+#pragma unroll
+            for (int i = 0; i < 6; ++i) ident[i] = tri[i][0] = tri[i][1] = 0.0f;
+            for (int h = lane; h < hands; h += 32) {
+                const uint16_t pr = comb[h];
+                const int c1 = pr & 0xff, c2 = pr >> 8;
+                if (c1 == ra || c1 == rb || c2 == ra || c2 == rb) continue;
+                float ph[FD_DENSE], d1[FD_DENSE], d2[FD_DENSE];
+#pragma unroll
+                for (int i = 0; i < FD_DENSE; ++i) {
+                    ph[i] = i < folders ? prob[fseat[i] * hands + h] : 0.0f;
+                    d1[i] = (dtight >> i & 1u) ? delta[fseat[i] * FD_CPAD + c1] : 0.0f;
+                    d2[i] = (dtight >> i & 1u) ? delta[fseat[i] * FD_CPAD + c2] : 0.0f;
+                }
+#pragma unroll
+                for (int s = 0; s < 6; ++s) {
+                    const int i = fd_pair_i(s), j = fd_pair_j(s);
+                    ident[s] += ph[i] * ph[j];
+                    const float edge = d1[i] * d2[j] + d2[i] * d1[j];
+                    tri[s][0] += edge * ph[fd_hub(s, 0)];
+                    tri[s][1] += edge * ph[fd_hub(s, 1)];
+                }
+            }
+            if (folders >= 2) {
+                const float uniform_pair = fd_clamp_tiny((1.0f - 4.0f / available) + 1.0f / denominator);
+#pragma unroll
+                for (int s = 0; s < 6; ++s) {
+                    const int i = fd_pair_i(s), j = fd_pair_j(s);
+                    if (j >= folders) continue;
+                    const int f = fseat[i], g = fseat[j];
+                    float dot = 0.0f;
+                    for (int c = lane; c < cards; c += 32) dot += cond[f * FD_CPAD + c] * cond[g * FD_CPAD + c];
+                    dot = fd_warp_sum(dot);
+                    const float same = 2.0f * fd_warp_sum(ident[s]) / (sd[i] * sd[j]);
+                    const float disjoint = fd_clamp_tiny((1.0f - dot) + 0.5f * same);
+                    phi = phi + logf(disjoint / uniform_pair);
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < 6; ++s) {
+                const int i = fd_pair_i(s), j = fd_pair_j(s);
+                if (!((dtight >> i & 1u) && (dtight >> j & 1u))) continue;
+                const float* left = delta + fseat[i] * FD_CPAD;
+                const float* right = delta + fseat[j] * FD_CPAD;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int k = fd_hub(s, u);
+                    if (k >= folders) continue;
+                    const int hub = fseat[k];
+                    const float matrix_term = fd_warp_sum(tri[s][u]) / sd[k];
+                    const float* hm = cond + hub * FD_CPAD;
+                    float diagonal = 0.0f, hl = 0.0f, hr = 0.0f;
+                    for (int c = lane; c < cards; c += 32) {
+                        diagonal += hm[c] * left[c] * right[c];
+                        hl += hm[c] * left[c];
+                        hr += hm[c] * right[c];
+                    }
+                    diagonal = fd_warp_sum(diagonal);
+                    const float outer = fd_warp_sum(hl) * fd_warp_sum(hr);
+                    triple = triple + ((matrix_term + diagonal) - outer);
+                }
+            }
+        } else {
         // pairwise disjointness: H-wide sums of p_f p_g over surviving hands for every folder pair
         if (folders >= 2) {
             float ident[FD_MAXP * (FD_MAXP - 1) / 2];
@@ -195,7 +294,6 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
         }
 
         // triple clusters: for each tight pair, the edge sum over surviving hands weighted by every hub
-        float triple = 0.0f;
         for (int f = 0; f < players; ++f) {
             for (int g = f + 1; g < players; ++g) {
                 if (!((tmask >> f & 1u) && (tmask >> g & 1u))) continue;
@@ -231,6 +329,7 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
                     triple = triple + ((matrix_term + diagonal) - outer);
                 }
             }
+        }
         }
         if (lane == 0) {
             phi_out[row * queries + q] = phi + triple;

@@ -45,10 +45,13 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
-    p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention"), default=None,
+    p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior"),
+                   default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
-                        "postflop sequence length, 48 x 2,406 tokens x 8 heads) between cudaProfilerStart/Stop "
-                        "(for ncu --profile-from-start off) after two warm-up runs, print nothing else, exit")
+                        "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
+                        "the beta eigendecomposition of components.folded_statistics; posterior: one call of "
+                        "components.posterior_sampler) between cudaProfilerStart/Stop (for ncu "
+                        "--profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
 
 
@@ -683,6 +686,15 @@ def _device_ms(device, fn, reps: int = 10) -> float:
 
     import torch
 
+    if PROFILE_ONE_FORWARD:
+        fn()
+        fn()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.start()
+        fn()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.stop()
+        return float("nan")
     times = []
     for rep in range(reps + 2):
         torch.cuda._sleep(1_000_000)
@@ -720,6 +732,12 @@ def folded_component(device, rows=64):
     raw = raw.masked_fill(clash[:, None], 0.0)
     prob = raw / raw.sum(-1, keepdim=True).clamp_min(1e-38)
     base = torch.full((rows,), 49.0, device=device)
+    if PROFILE_ONE_FORWARD:
+        from pbg_b200.folded import symmetric_eigh
+
+        beta = torch.randn((rows, 52, 52), generator=g, device=device)
+        _device_ms(device, lambda: (phi_queries(prob, folder, folder, base, 52), symmetric_eigh(beta + beta.mT)))
+        return {}
     queries_ms = _device_ms(device, lambda: phi_queries(prob, folder, folder, base, 52))
     whole_ms = _device_ms(device, lambda: folded_statistics(geo, board_cards=board, range_weights=weights, status=status,
                                                             combo_cards=combo, beta_rank=52, line_dim=0), reps=5)
@@ -791,6 +809,11 @@ def posterior_component(device, parents=4096, rows=16384, reps=10):
     root = torch.randint(0, 2**62, (rows,), generator=g, device=device)
     path = torch.randint(0, 2**62, (rows,), generator=g, device=device)
     sampler = CollisionConditionedProfileSampler(geo)
+    if PROFILE_ONE_FORWARD:
+        _device_ms(device, lambda: sampler.sample_children(
+            range_weights=w, board_cards=board, inherited_profile=inherited, source=source, ordinal=ordinal,
+            active=active, root=root, path=path, seed=1, iteration=0, retry_epoch=0))
+        return {}
     times = []
     for rep in range(reps + 3):
         torch.cuda._sleep(1_000_000)
@@ -835,7 +858,9 @@ def main():
     if args.profile_forward:
         global PROFILE_ONE_FORWARD
         PROFILE_ONE_FORWARD = True
-        globals()[f"{args.profile_forward}_forward_component"](device)
+        name = {"folded": "folded_component", "posterior": "posterior_component"}.get(
+            args.profile_forward, f"{args.profile_forward}_forward_component")
+        globals()[name](device)
         return
     if world > 1:
         import datetime
