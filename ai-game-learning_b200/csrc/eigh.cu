@@ -11,9 +11,10 @@
 // round are disjoint, so their rotations are computed together (one thread per
 // pair: t = sign(tau) / (|tau| + sqrt(1 + tau^2)), tau = (a_qq - a_pp) / 2 a_pq,
 // c = 1 / sqrt(1 + t^2), s = t c, the rotation that zeroes a_pq) and applied
-// together: A <- J^T A (rows p, q), then A <- A J and V <- V J (columns p, q).
-// Sweeps stop when the off-diagonal mass is below eps^2 of the total (or after
-// the given number of sweeps).  Eigenvalues are the diagonal, eigenvectors the
+// together: A <- J^T A (rows p, q), then A <- A J and V <- V J (columns p, q);
+// the pairs of a round follow the circle method in closed form.  Sweeps stop
+// when the off-diagonal mass reaches the fp32 floor, or stops falling once it
+// is near that floor (or after the given number of sweeps).  Eigenvalues are the diagonal, eigenvectors the
 // columns of V, unsorted.
 #include "pbg_common.cuh"
 
@@ -23,14 +24,29 @@ constexpr int EJ_MAXN = 64;
 constexpr int EJ_LD = EJ_MAXN + 1;  // padded row stride (bank spread)
 constexpr int EJ_THREADS = 256;
 
+// pair k of round r of the circle method over `even` indices (p < q)
+__device__ __forceinline__ void ej_pair(int even, int r, int k, int& p, int& q) {
+    const int m = even - 1;
+    if (k == 0) {
+        p = r;
+        q = m;
+    } else {
+        p = (r + k) % m;
+        q = (r - k + m) % m;
+    }
+    if (p > q) {
+        const int t = p;
+        p = q;
+        q = t;
+    }
+}
+
 __global__ void __launch_bounds__(EJ_THREADS)
 jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict__ values, float* __restrict__ vectors,
                    int max_sweeps) {
     __shared__ float A[EJ_MAXN * EJ_LD];
     __shared__ float V[EJ_MAXN * EJ_LD];
     __shared__ float cs[EJ_MAXN / 2][2];
-    __shared__ int pairs[EJ_MAXN / 2][2];
-    __shared__ int order[EJ_MAXN];
     __shared__ float norms[2];
     const int64_t m = blockIdx.x;
     const float* src = matrices + m * (int64_t)n * n;
@@ -41,8 +57,8 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
         A[r * EJ_LD + c] = 0.5f * (src[r * n + c] + src[c * n + r]);  // symmetric part, as eigh reads one triangle
         V[r * EJ_LD + c] = r == c ? 1.0f : 0.0f;
     }
-    for (int i = threadIdx.x; i < even; i += EJ_THREADS) order[i] = i;
     __syncthreads();
+    float previous_off = INFINITY;
     for (int sweep = 0; sweep < max_sweeps; ++sweep) {
         // convergence: off-diagonal against total squared mass
         if (threadIdx.x < 32) {
@@ -61,19 +77,19 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
             }
         }
         __syncthreads();
-        if (!(norms[0] > 1e-14f * norms[1])) break;
+        // converged: the off-diagonal mass is at the fp32 floor (1e-12 of the total), or it is small
+        // (1e-9 of the total, where convergence is quadratic) and the last sweep removed less than three
+        // quarters of it (rounding floor reached).  Early sweeps converge only linearly, by 3-5x each.
+        const float off = norms[0];
+        if (!(off > 1e-12f * norms[1]) || (off <= 1e-9f * norms[1] && off > 0.25f * previous_off)) break;
+        previous_off = off;
         for (int round = 0; round < even - 1; ++round) {
-            // round-robin pairing: order[0] fixed, the rest rotate one place per round
+            // round-robin (circle) pairing: index even-1 fixed, pair k of round r joins
+            // (r + k) mod (even-1) and (r - k) mod (even-1), pair 0 joins r with the fixed index
             if (threadIdx.x < half) {
                 const int k = threadIdx.x;
-                int p = order[k], q = order[even - 1 - k];
-                if (p > q) {
-                    const int t = p;
-                    p = q;
-                    q = t;
-                }
-                pairs[k][0] = p;
-                pairs[k][1] = q;
+                int p, q;
+                ej_pair(even, round, k, p, q);
                 float c = 1.0f, s = 0.0f;
                 if (q < n) {
                     const float apq = A[p * EJ_LD + q];
@@ -91,7 +107,8 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
             // rows p, q of A: A <- J^T A
             for (int i = threadIdx.x; i < half * n; i += EJ_THREADS) {
                 const int k = i / n, col = i - k * n;
-                const int p = pairs[k][0], q = pairs[k][1];
+                int p, q;
+                ej_pair(even, round, k, p, q);
                 if (q >= n) continue;
                 const float c = cs[k][0], s = cs[k][1];
                 const float ap = A[p * EJ_LD + col], aq = A[q * EJ_LD + col];
@@ -102,7 +119,8 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
             // columns p, q of A and V: A <- A J, V <- V J
             for (int i = threadIdx.x; i < half * n; i += EJ_THREADS) {
                 const int k = i / n, row = i - k * n;
-                const int p = pairs[k][0], q = pairs[k][1];
+                int p, q;
+                ej_pair(even, round, k, p, q);
                 if (q >= n) continue;
                 const float c = cs[k][0], s = cs[k][1];
                 const float ap = A[row * EJ_LD + p], aq = A[row * EJ_LD + q];
@@ -111,12 +129,6 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
                 const float vp = V[row * EJ_LD + p], vq = V[row * EJ_LD + q];
                 V[row * EJ_LD + p] = c * vp - s * vq;
                 V[row * EJ_LD + q] = s * vp + c * vq;
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                const int last = order[even - 1];
-                for (int i = even - 1; i > 1; --i) order[i] = order[i - 1];
-                order[1] = last;
             }
             __syncthreads();
         }

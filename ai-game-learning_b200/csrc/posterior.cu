@@ -49,20 +49,32 @@ __global__ void posterior_cdf_kernel(Geo g, int64_t parents, const float* __rest
     const float* w = weights + warp * g.H;
     float* c = cdf + warp * g.H;
     double carry = 0.0;
-    for (int h0 = 0; h0 < g.H; h0 += 32) {
-        const int h = h0 + lane;
-        double v = 0.0;
-        if (h < g.H) {
-            int c0, c1;
-            combo_cards(g.D, g.first, h, c0, c1);
-            bool blocked = false;
+    // eight 32-hand chunks per group: the group's loads are issued together, so their latency overlaps
+    constexpr int GROUP = 8;
+    for (int g0 = 0; g0 < g.H; g0 += 32 * GROUP) {
+        float loaded[GROUP];
 #pragma unroll
-            for (int k = 0; k < 5; ++k) blocked |= shown[k] != 255 && (shown[k] == c0 || shown[k] == c1);
-            v = blocked ? 0.0 : (double)w[h];
+        for (int i = 0; i < GROUP; ++i) {
+            const int h = g0 + 32 * i + lane;
+            loaded[i] = h < g.H ? __ldg(w + h) : 0.0f;
         }
-        v = warp_scan_double(v, lane) + carry;
-        if (h < g.H) c[h] = (float)v;
-        carry = __shfl_sync(0xffffffffu, v, 31);
+#pragma unroll
+        for (int i = 0; i < GROUP; ++i) {
+            const int h = g0 + 32 * i + lane;
+            if (g0 + 32 * i >= g.H) break;
+            double v = 0.0;
+            if (h < g.H) {
+                int c0, c1;
+                combo_cards(g.D, g.first, h, c0, c1);
+                bool blocked = false;
+#pragma unroll
+                for (int k = 0; k < 5; ++k) blocked |= shown[k] != 255 && (shown[k] == c0 || shown[k] == c1);
+                v = blocked ? 0.0 : (double)loaded[i];
+            }
+            v = warp_scan_double(v, lane) + carry;
+            if (h < g.H) c[h] = (float)v;
+            carry = __shfl_sync(0xffffffffu, v, 31);
+        }
     }
     if (lane == 0) mass[warp] = (float)carry;
 }
