@@ -2,7 +2,9 @@
 // (pbg/games/poker/queued/rb_sampling.py:86-223, sample_children).
 //
 // Two launches:
-//   posterior_cdf_kernel     one warp per (parent, seat): board-conflicting
+//   posterior_cdf_kernel     one warp per (parent, seat), grid-stride; the
+//                            hand -> card pair table decoded once per CTA
+//                            into shared memory; board-conflicting
 //                            private hands weigh 0; the seat's CDF over its
 //                            H hands and its mass, accumulated in double and
 //                            rounded to fp32 per entry (torch's CPU cumsum);
@@ -36,47 +38,61 @@ __device__ __forceinline__ double warp_scan_double(double v, int lane) {
     return v;
 }
 
-__global__ void posterior_cdf_kernel(Geo g, int64_t parents, const float* __restrict__ weights,
-                                     const uint8_t* __restrict__ board, float* __restrict__ cdf,
-                                     float* __restrict__ mass) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (warp >= parents * g.P) return;
-    const int64_t b = warp / g.P;
-    int shown[5];
-#pragma unroll
-    for (int k = 0; k < 5; ++k) shown[k] = board[b * 5 + k];
-    const float* w = weights + warp * g.H;
-    float* c = cdf + warp * g.H;
-    double carry = 0.0;
-    // eight 32-hand chunks per group: the group's loads are issued together, so their latency overlaps
-    constexpr int GROUP = 8;
-    for (int g0 = 0; g0 < g.H; g0 += 32 * GROUP) {
-        float loaded[GROUP];
-#pragma unroll
-        for (int i = 0; i < GROUP; ++i) {
-            const int h = g0 + 32 * i + lane;
-            loaded[i] = h < g.H ? __ldg(w + h) : 0.0f;
-        }
-#pragma unroll
-        for (int i = 0; i < GROUP; ++i) {
-            const int h = g0 + 32 * i + lane;
-            if (g0 + 32 * i >= g.H) break;
-            double v = 0.0;
-            if (h < g.H) {
-                int c0, c1;
-                combo_cards(g.D, g.first, h, c0, c1);
-                bool blocked = false;
-#pragma unroll
-                for (int k = 0; k < 5; ++k) blocked |= shown[k] != 255 && (shown[k] == c0 || shown[k] == c1);
-                v = blocked ? 0.0 : (double)loaded[i];
-            }
-            v = warp_scan_double(v, lane) + carry;
-            if (h < g.H) c[h] = (float)v;
-            carry = __shfl_sync(0xffffffffu, v, 31);
-        }
+constexpr int PC_THREADS = 256;
+constexpr int PC_MAX_HANDS = 1326;  // 52 cards
+
+// persistent: each CTA decodes the hand -> card pair table into shared memory once, then its warps take
+// (parent, seat) rows in a grid stride
+__global__ void __launch_bounds__(PC_THREADS)
+posterior_cdf_kernel(Geo g, int64_t parents, const float* __restrict__ weights,
+                     const uint8_t* __restrict__ board, float* __restrict__ cdf, float* __restrict__ mass) {
+    __shared__ uint16_t pair_cards[PC_MAX_HANDS];  // c0 | c1 << 8, absolute card indices
+    for (int h = threadIdx.x; h < g.H; h += PC_THREADS) {
+        int c0, c1;
+        combo_cards(g.D, g.first, h, c0, c1);
+        pair_cards[h] = (uint16_t)(c0 | (c1 << 8));
     }
-    if (lane == 0) mass[warp] = (float)carry;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = parents * g.P;
+    const int64_t warps = (int64_t)gridDim.x * (PC_THREADS / 32);
+    for (int64_t warp = ((int64_t)blockIdx.x * PC_THREADS + threadIdx.x) >> 5; warp < rows; warp += warps) {
+        const int64_t b = warp / g.P;
+        uint64_t shown = 0;  // board cards as a 64-bit set (255 = not dealt)
+#pragma unroll
+        for (int k = 0; k < 5; ++k) {
+            const int card = board[b * 5 + k];
+            if (card < 64) shown |= 1ull << card;
+        }
+        const float* w = weights + warp * g.H;
+        float* c = cdf + warp * g.H;
+        double carry = 0.0;
+        // eight 32-hand chunks per group: the group's loads are issued together, so their latency overlaps
+        constexpr int GROUP = 8;
+        for (int g0 = 0; g0 < g.H; g0 += 32 * GROUP) {
+            float loaded[GROUP];
+#pragma unroll
+            for (int i = 0; i < GROUP; ++i) {
+                const int h = g0 + 32 * i + lane;
+                loaded[i] = h < g.H ? __ldg(w + h) : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < GROUP; ++i) {
+                const int h = g0 + 32 * i + lane;
+                if (g0 + 32 * i >= g.H) break;
+                double v = 0.0;
+                if (h < g.H) {
+                    const unsigned pc = pair_cards[h];
+                    const bool blocked = ((shown >> (pc & 0xffu)) | (shown >> (pc >> 8))) & 1ull;
+                    v = blocked ? 0.0 : (double)loaded[i];
+                }
+                v = warp_scan_double(v, lane) + carry;
+                if (h < g.H) c[h] = (float)v;
+                carry = __shfl_sync(0xffffffffu, v, 31);
+            }
+        }
+        if (lane == 0) mass[warp] = (float)carry;
+    }
 }
 
 __global__ void posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const float* __restrict__ cdf,
@@ -199,9 +215,8 @@ int pbg_posterior_sample_children(pbg_geometry geometry, int64_t parents, const 
     float* mass = workspace + parents * g.P * (int64_t)g.H;
     unsigned long long* mf = reinterpret_cast<unsigned long long*>(min_failing);
     posterior_init_kernel<<<1, 1, 0, s>>>(mf);
-    const int64_t cdf_threads = parents * g.P * 32;
-    posterior_cdf_kernel<<<(unsigned)((cdf_threads + 255) / 256), 256, 0, s>>>(g, parents, range_weights, board, cdf,
-                                                                                mass);
+    posterior_cdf_kernel<<<stride_grid(parents * g.P * 32, PC_THREADS), PC_THREADS, 0, s>>>(g, parents, range_weights,
+                                                                                           board, cdf, mass);
     if (rows > 0) {
         const uint64_t ns = rng_namespace(seed, iteration, POSTERIOR);
         const int64_t threads = rows * 32;
