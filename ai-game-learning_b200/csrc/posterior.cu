@@ -14,7 +14,8 @@
 //                            (POSTERIOR key at draw = attempt, lane = seat;
 //                            target = min(u*mass, nextafter(mass, 0)); the
 //                            first CDF entry strictly above it by an 11-step
-//                            bisection) and tests the seats' cards for a
+//                            bisection, the seats' bisections interleaved so
+//                            their loads overlap) and tests the seats' cards for a
 //                            collision; a ballot picks the first accepted
 //                            attempt of the round, rounds of 32 run until one
 //                            succeeds or max_attempts is spent.
@@ -95,7 +96,7 @@ posterior_cdf_kernel(Geo g, int64_t parents, const float* __restrict__ weights,
     }
 }
 
-__global__ void posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const float* __restrict__ cdf,
+__global__ void __launch_bounds__(128, 8) posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const float* __restrict__ cdf,
                                         const float* __restrict__ mass, const int32_t* __restrict__ inherited,
                                         const int64_t* __restrict__ source, const int64_t* __restrict__ ordinal,
                                         const uint8_t* __restrict__ active, const int64_t* __restrict__ root,
@@ -125,32 +126,50 @@ __global__ void posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const 
             for (int base = 0; base < max_attempts && accepted < 0; base += 32) {
                 const int a = base + lane;
                 bool ok = a < max_attempts;
-                int cards[2 * MAXP];
-                for (int p = 0; p < P; ++p) {
-                    const float total = mass[src * P + p];
-                    const float* c = cdf + (src * P + p) * (int64_t)H;
-                    float target = __fmul_rn(key_uniform(rng_key(ns, rt, pt, a, p, ep)), total);
-                    const float cap = __int_as_float(__float_as_int(total) - 1);  // nextafter(total, 0), total > 0
-                    target = cap < target ? cap : target;
-                    int lo = 0, hi = H;
+                // the seats' bisections advance together, so their dependent CDF loads overlap
+                float target[MAXP];
+                int lo[MAXP], hi[MAXP];
 #pragma unroll
-                    for (int step = 0; step < 11; ++step) {
-                        const int mid = (lo + hi) >> 1;
-                        const int safe = mid < H - 1 ? mid : H - 1;
-                        const bool below = mid < H && c[safe] <= target;
-                        lo = below ? mid + 1 : lo;
-                        hi = below ? hi : mid;
-                    }
-                    mine[p] = lo < H - 1 ? lo : H - 1;
-                    combo_cards(g.D, g.first, mine[p], cards[2 * p], cards[2 * p + 1]);
+                for (int p = 0; p < MAXP; ++p) {
+                    if (p >= P) break;
+                    const float total = mass[src * P + p];
+                    const float t = __fmul_rn(key_uniform(rng_key(ns, rt, pt, a, p, ep)), total);
+                    const float cap = __int_as_float(__float_as_int(total) - 1);  // nextafter(total, 0), total > 0
+                    target[p] = cap < t ? cap : t;
+                    lo[p] = 0;
+                    hi[p] = H;
                 }
-                for (int i = 0; i < 2 * P && ok; ++i)
-                    for (int j = (i | 1) + 1; j < 2 * P; ++j) ok &= cards[i] != cards[j];
+#pragma unroll
+                for (int step = 0; step < 11; ++step) {
+#pragma unroll
+                    for (int p = 0; p < MAXP; ++p) {
+                        if (p >= P) break;
+                        const float* c = cdf + (src * P + p) * (int64_t)H;
+                        const int mid = (lo[p] + hi[p]) >> 1;
+                        const int safe = mid < H - 1 ? mid : H - 1;
+                        const bool below = mid < H && c[safe] <= target[p];
+                        lo[p] = below ? mid + 1 : lo[p];
+                        hi[p] = below ? hi[p] : mid;
+                    }
+                }
+                uint64_t held = 0;  // cards of the seats drawn so far; a repeat is a collision
+#pragma unroll
+                for (int p = 0; p < MAXP; ++p) {
+                    if (p >= P) break;
+                    mine[p] = lo[p] < H - 1 ? lo[p] : H - 1;
+                    int c0, c1;
+                    combo_cards(g.D, g.first, mine[p], c0, c1);
+                    const uint64_t pair = (1ull << c0) | (1ull << c1);
+                    ok &= (held & pair) == 0;
+                    held |= pair;
+                }
                 const unsigned hit = __ballot_sync(0xffffffffu, ok);
                 if (hit) {
                     const int winner = __ffs(hit) - 1;
                     accepted = base + winner;
-                    for (int p = 0; p < P; ++p) {
+#pragma unroll
+                    for (int p = 0; p < MAXP; ++p) {
+                        if (p >= P) break;
                         const int32_t v = __shfl_sync(0xffffffffu, mine[p], winner);
                         if (lane == p) result = v;
                     }
