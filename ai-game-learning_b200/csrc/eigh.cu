@@ -47,6 +47,7 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
     __shared__ float A[EJ_MAXN * EJ_LD];
     __shared__ float V[EJ_MAXN * EJ_LD];
     __shared__ float cs[EJ_MAXN / 2][2];
+    __shared__ int pairs[EJ_MAXN / 2][2];
     __shared__ float norms[2];
     const int64_t m = blockIdx.x;
     const float* src = matrices + m * (int64_t)n * n;
@@ -102,25 +103,29 @@ jacobi_eigh_kernel(int n, const float* __restrict__ matrices, float* __restrict_
                 }
                 cs[k][0] = c;
                 cs[k][1] = s;
+                pairs[k][0] = p;
+                pairs[k][1] = q;
             }
             __syncthreads();
-            // rows p, q of A: A <- J^T A
-            for (int i = threadIdx.x; i < half * n; i += EJ_THREADS) {
-                const int k = i / n, col = i - k * n;
-                int p, q;
-                ej_pair(even, round, k, p, q);
-                if (q >= n) continue;
-                const float c = cs[k][0], s = cs[k][1];
-                const float ap = A[p * EJ_LD + col], aq = A[q * EJ_LD + col];
-                A[p * EJ_LD + col] = c * ap - s * aq;
-                A[q * EJ_LD + col] = s * ap + c * aq;
+            // rows p, q of A: A <- J^T A.  Thread t owns column t mod 64 for the pairs k = t / 64 (mod 4).
+            const int lane64 = threadIdx.x & (EJ_MAXN - 1), group = threadIdx.x / EJ_MAXN;
+            constexpr int GROUPS = EJ_THREADS / EJ_MAXN;
+            if (lane64 < n) {
+                const int col = lane64;
+                for (int k = group; k < half; k += GROUPS) {
+                    const int p = pairs[k][0], q = pairs[k][1];
+                    if (q >= n) continue;
+                    const float c = cs[k][0], s = cs[k][1];
+                    const float ap = A[p * EJ_LD + col], aq = A[q * EJ_LD + col];
+                    A[p * EJ_LD + col] = c * ap - s * aq;
+                    A[q * EJ_LD + col] = s * ap + c * aq;
+                }
             }
             __syncthreads();
-            // columns p, q of A and V: A <- A J, V <- V J
-            for (int i = threadIdx.x; i < half * n; i += EJ_THREADS) {
-                const int k = i / n, row = i - k * n;
-                int p, q;
-                ej_pair(even, round, k, p, q);
+            // columns p, q of A and V: A <- A J, V <- V J (thread t owns row t mod 64)
+            for (int k = group; k < half && lane64 < n; k += GROUPS) {
+                const int row = lane64;
+                const int p = pairs[k][0], q = pairs[k][1];
                 if (q >= n) continue;
                 const float c = cs[k][0], s = cs[k][1];
                 const float ap = A[row * EJ_LD + p], aq = A[row * EJ_LD + q];
