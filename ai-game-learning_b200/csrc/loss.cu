@@ -146,8 +146,10 @@ struct LegalBits {
 // fixed counter slot lets launches with different grids share one buffer.
 // The last block to arrive sums all blocks in block order (deterministic),
 // publishes stats (rows = -1 if any block reported an error) and clears slot 0.
+// Returns true in the last block (every block's earlier global writes are then
+// visible to it).
 template <int BLOCK>
-__device__ __forceinline__ void block_stats(RowStats& s, double* partials, double* stats, bool failed = false) {
+__device__ __forceinline__ bool block_stats(RowStats& s, double* partials, double* stats, bool failed = false) {
     __shared__ float red[BLOCK / 32][LOSS_STATS];
     __shared__ bool last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -168,7 +170,7 @@ __device__ __forceinline__ void block_stats(RowStats& s, double* partials, doubl
     __syncthreads();
     if (threadIdx.x == 0) last = atomicAdd(word, 1u) == gridDim.x - 1;
     __syncthreads();
-    if (!last) return;
+    if (!last) return false;
     __threadfence();
     if (threadIdx.x < LOSS_STATS) {
         double acc = 0.0;
@@ -178,6 +180,7 @@ __device__ __forceinline__ void block_stats(RowStats& s, double* partials, doubl
     }
     __syncthreads();
     if (threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(partials) = 0ull;  // ready for the next launch
+    return true;
 }
 
 // Rows a grid-stride loop starting at r0 with step `stride` visits below N.
@@ -515,6 +518,184 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
     block_stats<LOSS_BLOCK>(s, partials, stats);
 }
 
+// Loss backward fused with the readout's weight gradient ------------------
+//
+// The learner's readout maps a hidden row h_r (bf16, width d) to the A = 8
+// logits, x_r = W h_r + b.  Its gradients are rank-8 sums over the decisions,
+// dW[a][k] = sum_r dx_r[a] h_r[k] and db[a] = sum_r dx_r[a], taken of the bf16
+// dlogits this pass writes (the operand a separate weight-gradient GEMM would
+// read back).  With 8 outputs that is 16 FLOPs per hidden element, about 8
+// FLOP/B: below the FP32 ridge, so the sum runs on the FMA pipe inside the
+// loss pass and the pass stays HBM bound at 56 + 2d bytes per row, with no
+// second launch re-reading dlogits.
+//
+// Warps take 32-row chunks: lane l computes row l's dlogits (row8_backward),
+// then the warp walks the chunk's 32 hidden rows in groups of 4 or 8: lane l
+// holds columns [l*DC, l*DC + DC) of each row (one coalesced 2d-byte row per
+// warp load) and adds the row's dlogits, broadcast by shuffles, times its
+// columns into packed fp32 accumulators.  A CTA's warps add their partial sums
+// in warp order in shared memory; CTA partials go to caller scratch after the
+// loss statistics, and the last CTA adds them in CTA order (in double), so
+// the result does not depend on scheduling.
+constexpr int RO_WARPS = 8;
+constexpr int RO_THREADS = 32 * RO_WARPS;
+
+// hidden rows loaded per batch, and the occupancy the register budget is set for
+template <int DC>
+__host__ __device__ constexpr int ro_group() {
+    return DC == 8 ? 4 : 8;
+}
+
+template <int DC>
+struct HiddenVec;
+template <>
+struct HiddenVec<2> {
+    using T = uint32_t;
+};
+template <>
+struct HiddenVec<4> {
+    using T = uint2;
+};
+template <>
+struct HiddenVec<8> {
+    using T = uint4;
+};
+
+template <int DC>
+__host__ __device__ constexpr int ro_min_blocks() {
+    return DC <= 2 ? 3 : 2;
+}
+
+template <int DC>
+constexpr size_t ro_smem() {
+    return (size_t)RO_WARPS * (8 * 32 * DC + 8) * sizeof(float);
+}
+
+template <int DC>
+__global__ void __launch_bounds__(RO_THREADS, ro_min_blocks<DC>())
+ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __restrict__ mask,
+                   const int32_t* __restrict__ action, const float* __restrict__ old_logp,
+                   const float* __restrict__ adv, const float* __restrict__ weight,
+                   const float* __restrict__ controls, const typename HiddenVec<DC>::T* __restrict__ hidden,
+                   uint4* __restrict__ dlogits, float* __restrict__ dweight, float* __restrict__ dbias,
+                   double* partials, double* stats) {
+    using HV = typename HiddenVec<DC>::T;
+    constexpr int D = 32 * DC;
+    constexpr int OUT = 8 * D + 8;  // dW [8][D], then db [8]
+    extern __shared__ float ro_red[];  // [RO_WARPS][OUT]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    LossControls k = load_controls(controls);
+    RowStats s;
+    s.zero();
+    float2 acc[8][DC / 2];
+    float db[8];
+    #pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        db[a] = 0.0f;
+        #pragma unroll
+        for (int j = 0; j < DC / 2; ++j) acc[a][j] = make_float2(0.0f, 0.0f);
+    }
+    float rows_done = 0.0f;
+    const int64_t chunks = (N + 31) / 32;
+    const int64_t wstride = (int64_t)gridDim.x * RO_WARPS;
+    for (int64_t c = (int64_t)blockIdx.x * RO_WARPS + warp; c < chunks; c += wstride) {
+        const int64_t r = c * 32 + lane;
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (r < N) {
+            Row8 row = load_row8(r, logits, mask, action, old_logp, adv, weight);
+            row8_backward(row, k, s, out);
+            __stcs(dlogits + r, out);
+            rows_done += 1.0f;
+        }
+        {
+            const float2 d01 = bf2_to_f2(out.x), d23 = bf2_to_f2(out.y), d45 = bf2_to_f2(out.z),
+                         d67 = bf2_to_f2(out.w);
+            db[0] += d01.x; db[1] += d01.y; db[2] += d23.x; db[3] += d23.y;
+            db[4] += d45.x; db[5] += d45.y; db[6] += d67.x; db[7] += d67.y;
+        }
+        constexpr int G = ro_group<DC>();
+        #pragma unroll 1
+        for (int g = 0; g < 32; g += G) {
+            HV hv[G];
+            #pragma unroll
+            for (int i = 0; i < G; ++i) {
+                const int64_t rr = c * 32 + g + i;
+                hv[i] = rr < N ? __ldcs(hidden + rr * 32 + lane) : HV{};
+            }
+            #pragma unroll
+            for (int i = 0; i < G; ++i) {
+                const int src = g + i;
+                const float2 d01 = bf2_to_f2(__shfl_sync(0xffffffffu, out.x, src));
+                const float2 d23 = bf2_to_f2(__shfl_sync(0xffffffffu, out.y, src));
+                const float2 d45 = bf2_to_f2(__shfl_sync(0xffffffffu, out.z, src));
+                const float2 d67 = bf2_to_f2(__shfl_sync(0xffffffffu, out.w, src));
+                const float dl[8] = {d01.x, d01.y, d23.x, d23.y, d45.x, d45.y, d67.x, d67.y};
+                const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv[i]);
+                float2 h[DC / 2];
+                #pragma unroll
+                for (int j = 0; j < DC / 2; ++j) h[j] = bf2_to_f2(hw[j]);
+                #pragma unroll
+                for (int a = 0; a < 8; ++a) {
+                    const float2 da = make_float2(dl[a], dl[a]);
+                    #pragma unroll
+                    for (int j = 0; j < DC / 2; ++j) acc[a][j] = __ffma2_rn(h[j], da, acc[a][j]);
+                }
+            }
+        }
+    }
+    // this warp's partial sums, then the CTA's in warp order
+    float* mine = ro_red + warp * OUT;
+    #pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        #pragma unroll
+        for (int j = 0; j < DC / 2; ++j)
+            *reinterpret_cast<float2*>(mine + a * D + lane * DC + 2 * j) = acc[a][j];
+        const float t = warp_sum(db[a]);
+        if (lane == 0) mine[8 * D + a] = t;
+    }
+    __syncthreads();
+    float* cta = reinterpret_cast<float*>(partials + 1 + (int64_t)gridDim.x * LOSS_STATS) + (int64_t)blockIdx.x * OUT;
+    for (int o = threadIdx.x; o < OUT; o += RO_THREADS) {
+        float v = 0.0f;
+        #pragma unroll
+        for (int w = 0; w < RO_WARPS; ++w) v += ro_red[w * OUT + o];
+        cta[o] = v;
+    }
+    s.v[7] = rows_done;
+    if (block_stats<RO_THREADS>(s, partials, stats)) {
+        const float* all = reinterpret_cast<const float*>(partials + 1 + (int64_t)gridDim.x * LOSS_STATS);
+        for (int o = threadIdx.x; o < OUT; o += RO_THREADS) {
+            double v = 0.0;
+            for (unsigned b = 0; b < gridDim.x; ++b) v += (double)__ldcg(all + (int64_t)b * OUT + o);
+            if (o < 8 * D) dweight[o] = (float)v;
+            else dbias[o - 8 * D] = (float)v;
+        }
+    }
+}
+
+template <int DC>
+int readout_grid_dc(int64_t N) {
+    static int per_sm[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int slot = dev >= 0 && dev < 64 ? dev : 0;
+    if (per_sm[slot] == 0) {
+        int n = 0;
+        if (cudaFuncSetAttribute(ppo_readout_kernel<DC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)ro_smem<DC>()) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, ppo_readout_kernel<DC>, RO_THREADS, ro_smem<DC>()) !=
+                cudaSuccess ||
+            n <= 0)
+            n = 1;
+        per_sm[slot] = n;
+    }
+    return stride_grid((N + 31) / 32, RO_WARPS, per_sm[slot]);
+}
+
+int readout_grid(int64_t N, int d) {
+    return d == 64 ? readout_grid_dc<2>(N) : d == 128 ? readout_grid_dc<4>(N) : readout_grid_dc<8>(N);
+}
+
 // One wave of resident blocks (occupancy of the vector kernel), grid-stride beyond.
 int ppo_grid(int64_t N) {
     static int per_sm[64] = {0};
@@ -585,6 +766,44 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
                                                               weight, controls, (float*)dlogits, partials, stats);
     }
     return launch_status("ppo_categorical_backward");
+}
+
+int64_t pbg_ppo_readout_partials_size(int64_t N, int32_t A, int32_t d) {
+    if (A != 8 || !(d == 64 || d == 128 || d == 256)) return -1;
+    const int64_t grid = readout_grid(N > 0 ? N : 1, d);
+    const int64_t floats = grid * (8LL * d + 8);
+    // counter/error slot, per-block statistics, then per-block dW/db partials (two floats per slot)
+    return 1 + grid * LOSS_STATS + (floats + 1) / 2;
+}
+
+int pbg_ppo_readout_backward(int64_t N, int32_t A, const void* logits, const uint8_t* mask, const int32_t* action,
+                             const float* old_logp, const float* adv, const float* weight, const float* controls,
+                             const void* hidden, int32_t d, void* dlogits, float* dweight, float* dbias,
+                             double* partials, double* stats, void* stream) {
+    PBG_REQUIRE(N >= 0 && A == 8, "ppo_readout: need N >= 0 and A == 8");
+    PBG_REQUIRE(d == 64 || d == 128 || d == 256, "ppo_readout: hidden width must be 64, 128 or 256");
+    PBG_REQUIRE(controls && partials && stats && dweight && dbias, "ppo_readout: null controls, scratch or output");
+    PBG_REQUIRE(N == 0 || (logits && mask && action && old_logp && adv && weight && hidden && dlogits),
+                "ppo_readout: null argument");
+    PBG_REQUIRE(N == 0 || ((uintptr_t)logits % 16 == 0 && (uintptr_t)dlogits % 16 == 0 && (uintptr_t)mask % 8 == 0 &&
+                           (uintptr_t)hidden % 16 == 0),
+                "ppo_readout: logits, dlogits and hidden must be 16-byte aligned, mask 8-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    const int grid = readout_grid(N > 0 ? N : 1, d);
+    if (d == 64) {
+        ppo_readout_kernel<2><<<grid, RO_THREADS, ro_smem<2>(), s>>>(
+            N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
+            (const uint32_t*)hidden, (uint4*)dlogits, dweight, dbias, partials, stats);
+    } else if (d == 128) {
+        ppo_readout_kernel<4><<<grid, RO_THREADS, ro_smem<4>(), s>>>(
+            N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
+            (const uint2*)hidden, (uint4*)dlogits, dweight, dbias, partials, stats);
+    } else {
+        ppo_readout_kernel<8><<<grid, RO_THREADS, ro_smem<8>(), s>>>(
+            N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
+            (const uint4*)hidden, (uint4*)dlogits, dweight, dbias, partials, stats);
+    }
+    return launch_status("ppo_readout_backward");
 }
 
 }  // extern "C"

@@ -99,6 +99,8 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_ppo_partials_size": (_I64, [_I64, _I32]),
     "pbg_ppo_categorical_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_ppo_categorical_backward_noalloc": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_ppo_readout_partials_size": (_I64, [_I64, _I32, _I32]),
+    "pbg_ppo_readout_backward": (_I32, [_I64, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P]),
     "pbg_posterior_workspace_floats": (_I64, [G, _I64]),
     "pbg_posterior_sample_children": (_I32, [G, _I64, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _I64,
                                              _I32, _P, _P, _P, _P, _P, _P, _P]),

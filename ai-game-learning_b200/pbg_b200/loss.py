@@ -107,6 +107,47 @@ class BoundPPOBackward:
             check(rc, "pbg_ppo_categorical_backward")
 
 
+class FusedPPOReadoutBackward:
+    """The loss backward fused with the readout's weight gradient.
+
+    The logits come from a readout ``x = h W^T + b`` (pbg/core/tensor_ops.py:25-38) over hidden rows
+    ``h`` [N, d] (bf16, d = 64, 128 or 256) with A = 8 outputs.  One pass writes the bf16 dlogits
+    (the values ``FusedPPOBackward`` writes) and the readout's ``dweight`` [8, d] and ``dbias`` [8]
+    (fp32 sums of the bf16 dlogits against the hidden rows): the gradients autograd would form next
+    with a separate weight-gradient GEMM that re-reads dlogits.
+    """
+
+    def __init__(self, rows: int, hidden: int, device, config: LossConfig = LossConfig()) -> None:
+        self.rows, self.hidden = int(rows), int(hidden)
+        self.device = torch.device(device)
+        n = int(lib().pbg_ppo_readout_partials_size(self.rows, 8, self.hidden))
+        if n < 0:
+            raise ValueError("readout width must be 64, 128 or 256")
+        self.loss = FusedPPOBackward(rows, 8, device, config)
+        self.partials = torch.zeros(n, dtype=torch.float64, device=self.device)
+        self.dweight = torch.zeros((8, self.hidden), dtype=torch.float32, device=self.device)
+        self.dbias = torch.zeros(8, dtype=torch.float32, device=self.device)
+
+    def set_controls(self, *, scale: float = 1.0, inv_count: float | None = None) -> None:
+        self.loss.set_controls(scale=scale, inv_count=inv_count)
+
+    def __call__(self, logits: Tensor, mask: Tensor, action: Tensor, old_logp: Tensor, advantage: Tensor,
+                 weight: Tensor, hidden: Tensor, dlogits: Tensor | None = None):
+        """Returns (dlogits, dweight, dbias, stats); the last three are this object's buffers."""
+
+        if tuple(logits.shape) != (self.rows, 8) or logits.dtype != torch.bfloat16:
+            raise ValueError("readout loss needs bf16 logits of the admitted [rows, 8] shape")
+        if tuple(hidden.shape) != (self.rows, self.hidden) or hidden.dtype != torch.bfloat16:
+            raise ValueError("hidden rows must be bf16 [rows, hidden]")
+        if dlogits is None:
+            dlogits = torch.empty_like(logits)
+        call("pbg_ppo_readout_backward", self.rows, 8, ptr(logits),
+             ptr(mask.view(torch.uint8) if mask.dtype == torch.bool else mask), ptr(action), ptr(old_logp),
+             ptr(advantage), ptr(weight), ptr(self.loss.controls), ptr(hidden), self.hidden, ptr(dlogits),
+             ptr(self.dweight), ptr(self.dbias), ptr(self.partials), ptr(self.loss.stats), stream(logits.device))
+        return dlogits, self.dweight, self.dbias, self.loss.stats
+
+
 def fused_ppo_backward(logits, mask, action, old_logp, advantage, weight, config: LossConfig = LossConfig(), *,
                        scale: float = 1.0, inv_count: float | None = None):
     op = FusedPPOBackward(logits.shape[0], logits.shape[1], logits.device, config)

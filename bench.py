@@ -45,12 +45,14 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
-    p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior"),
+    p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
+                                                 "readout"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
                         "the beta eigendecomposition of components.folded_statistics; posterior: one call of "
-                        "components.posterior_sampler) between cudaProfilerStart/Stop (for ncu "
+                        "components.posterior_sampler; readout: one launch of components.loss_readout) "
+                        "between cudaProfilerStart/Stop (for ncu "
                         "--profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
 
@@ -708,6 +710,33 @@ def _device_ms(device, fn, reps: int = 10) -> float:
     return sorted(times)[len(times) // 2]
 
 
+def readout_component(device, rows=4_194_304, hidden=128, reps=10):
+    """The loss backward fused with the readout's weight gradient (pbg_ppo_readout_backward) on the cfg5
+    rows (4,194,304 x 8, bf16 logits) with bf16 hidden rows of width `hidden`: one launch writes dlogits,
+    dweight [8, hidden] and dbias.  Algorithmic bytes per row: 56 (the loss) + 2 * hidden (the hidden row),
+    against the measured HBM copy bandwidth; each launch is queued behind a device-side sleep."""
+
+    import torch
+    from pbg_b200.loss import FusedPPOReadoutBackward, LossConfig
+
+    logits, mask, action, old, adv, weight = make_inputs(rows, 8, 0, device)
+    g = torch.Generator(device=device).manual_seed(5)
+    h = torch.randn((rows, hidden), generator=g, device=device).to(torch.bfloat16)
+    op = FusedPPOReadoutBackward(rows, hidden, device, LossConfig())
+    dl = torch.empty_like(logits)
+    ms = _device_ms(device, lambda: op(logits, mask, action, old, adv, weight, h, dl), reps)
+    if PROFILE_ONE_FORWARD:
+        return {}
+    peak, kind = measured_peak()
+    per_row = 56 + 2 * hidden
+    gbs = per_row * rows / (ms / 1000.0) / 1e9
+    return {"workload": f"cfg5 rows ({rows} x 8, bf16) with the readout's weight gradient, hidden width {hidden}",
+            "us": 1000.0 * ms, "decisions_per_s": rows / (ms / 1000.0),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "bytes_per_row": per_row, "peak_kind": kind},
+            "kernel": "ppo_readout_kernel", "gpu_launches": 1}
+
+
 def folded_component(device, rows=64):
     """Multiway folded statistics (queued/folded.py): 6-max R13, four folded seats (all tight), flop
     boards, `rows` decisions; the finite-difference removal queries (1 + 52 + 1326 per decision) in
@@ -858,7 +887,8 @@ def main():
     if args.profile_forward:
         global PROFILE_ONE_FORWARD
         PROFILE_ONE_FORWARD = True
-        name = {"folded": "folded_component", "posterior": "posterior_component"}.get(
+        name = {"folded": "folded_component", "posterior": "posterior_component",
+                "readout": "readout_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         globals()[name](device)
         return
@@ -1052,6 +1082,7 @@ def main():
                                   "preflop_forward": preflop_forward_component(device),
                                   "postflop_forward": postflop_forward_component(device),
                                   "posterior_sampler": posterior_component(device),
+                                  "loss_readout": readout_component(device),
                                   "folded_statistics": folded_component(device),
                                   "branched_sampling": branching_component(device),
                                   "rollout_with_model": rollout_with_model_component(device)}

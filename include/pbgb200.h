@@ -261,6 +261,23 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
                                  const float *controls, void *dlogits, double *partials,
                                  double *stats, void *stream);
 
+/* The loss backward above fused with the gradient of the readout that
+ * produced the logits, x = W h + b (pbg/core/tensor_ops.py:25-38, `linear`,
+ * whose weight and bias gradients autograd forms after the loss's dlogits,
+ * pbg/core/learner.py:2021-2077).  A == 8, bf16 logits and dlogits as in the
+ * vectorised path; hidden [N,d] bf16 (d = 64, 128 or 256, 16-byte aligned).
+ * Writes dlogits as pbg_ppo_categorical_backward does (same values) and
+ * dweight [8,d] = sum_r dlogits[r,:]^T hidden[r,:], dbias [8] = sum_r
+ * dlogits[r,:] in fp32, summed from the bf16 dlogits.  partials: caller
+ * scratch of pbg_ppo_readout_partials_size(N, 8, d) doubles, zero before the
+ * first call (the kernel leaves it cleared); stats as above. */
+int64_t pbg_ppo_readout_partials_size(int64_t N, int32_t A, int32_t d);
+int pbg_ppo_readout_backward(int64_t N, int32_t A, const void *logits, const uint8_t *mask,
+                             const int32_t *action, const float *old_logp, const float *adv,
+                             const float *weight, const float *controls, const void *hidden, int32_t d,
+                             void *dlogits, float *dweight, float *dbias, double *partials,
+                             double *stats, void *stream);
+
 /* Allocation-free variant of pbg_ppo_categorical_backward (no counterpart
  * in the reference).  For callers that cannot allocate device memory --
  * hosts that own all device memory through their own pool, bindings with no
