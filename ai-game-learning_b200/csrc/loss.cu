@@ -530,10 +530,10 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
 // second launch re-reading dlogits.
 //
 // Warps take 32-row chunks: lane l computes row l's dlogits (row8_backward),
-// then the warp walks the chunk's 32 hidden rows in groups of 4 or 8: lane l
+// then the warp walks the chunk's 32 hidden rows in groups of 2 or 8: lane l
 // holds columns [l*DC, l*DC + DC) of each row (one coalesced 2d-byte row per
-// warp load) and adds the row's dlogits, broadcast by shuffles, times its
-// columns into packed fp32 accumulators.  A CTA's warps add their partial sums
+// warp load) and adds the row's dlogits (staged once as fp32 in shared memory,
+// read back as broadcasts) times its columns into packed fp32 accumulators.  A CTA's warps add their partial sums
 // in warp order in shared memory; CTA partials go to caller scratch after the
 // loss statistics, and the last CTA adds them in CTA order (in double), so
 // the result does not depend on scheduling.
@@ -543,7 +543,7 @@ constexpr int RO_THREADS = 32 * RO_WARPS;
 // hidden rows loaded per batch, and the occupancy the register budget is set for
 template <int DC>
 __host__ __device__ constexpr int ro_group() {
-    return DC == 8 ? 4 : 8;
+    return DC == 8 ? 2 : 8;
 }
 
 template <int DC>
@@ -598,39 +598,56 @@ ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __r
     float rows_done = 0.0f;
     const int64_t chunks = (N + 31) / 32;
     const int64_t wstride = (int64_t)gridDim.x * RO_WARPS;
-    for (int64_t c = (int64_t)blockIdx.x * RO_WARPS + warp; c < chunks; c += wstride) {
+    constexpr int G = ro_group<DC>();
+    // Software pipeline: while a group of hidden rows is summed, the next group (or the next chunk's
+    // first group) and the next chunk's loss row are already loading.
+    auto load_group = [&](int64_t first, HV (&hv)[G]) {
+        #pragma unroll
+        for (int i = 0; i < G; ++i) {
+            const int64_t rr = first + i;
+            hv[i] = rr < N ? __ldcs(hidden + rr * 32 + lane) : HV{};
+        }
+    };
+    float* staged = ro_red + warp * 32 * 8;  // [32][8] fp32 dlogits of the warp's chunk
+    int64_t c = (int64_t)blockIdx.x * RO_WARPS + warp;
+    Row8 row;
+    HV cur[G];
+    if (c < chunks) {
+        if (c * 32 + lane < N) row = load_row8(c * 32 + lane, logits, mask, action, old_logp, adv, weight);
+        load_group(c * 32, cur);
+    }
+    for (; c < chunks; c += wstride) {
         const int64_t r = c * 32 + lane;
         uint4 out = make_uint4(0u, 0u, 0u, 0u);
         if (r < N) {
-            Row8 row = load_row8(r, logits, mask, action, old_logp, adv, weight);
             row8_backward(row, k, s, out);
             __stcs(dlogits + r, out);
             rows_done += 1.0f;
         }
+        const int64_t nc = c + wstride;
+        if (nc < chunks && nc * 32 + lane < N) row = load_row8(nc * 32 + lane, logits, mask, action, old_logp, adv, weight);
         {
+            // the row's dlogits as fp32, once, into the warp's staging rows (read back as broadcasts)
             const float2 d01 = bf2_to_f2(out.x), d23 = bf2_to_f2(out.y), d45 = bf2_to_f2(out.z),
                          d67 = bf2_to_f2(out.w);
             db[0] += d01.x; db[1] += d01.y; db[2] += d23.x; db[3] += d23.y;
             db[4] += d45.x; db[5] += d45.y; db[6] += d67.x; db[7] += d67.y;
+            float4* mine = reinterpret_cast<float4*>(staged + lane * 8);
+            mine[0] = make_float4(d01.x, d01.y, d23.x, d23.y);
+            mine[1] = make_float4(d45.x, d45.y, d67.x, d67.y);
         }
-        constexpr int G = ro_group<DC>();
+        __syncwarp();
         #pragma unroll 1
         for (int g = 0; g < 32; g += G) {
-            HV hv[G];
+            HV nxt[G];
+            if (g + G < 32) load_group(c * 32 + g + G, nxt);
+            else if (nc < chunks) load_group(nc * 32, nxt);
             #pragma unroll
             for (int i = 0; i < G; ++i) {
-                const int64_t rr = c * 32 + g + i;
-                hv[i] = rr < N ? __ldcs(hidden + rr * 32 + lane) : HV{};
-            }
-            #pragma unroll
-            for (int i = 0; i < G; ++i) {
-                const int src = g + i;
-                const float2 d01 = bf2_to_f2(__shfl_sync(0xffffffffu, out.x, src));
-                const float2 d23 = bf2_to_f2(__shfl_sync(0xffffffffu, out.y, src));
-                const float2 d45 = bf2_to_f2(__shfl_sync(0xffffffffu, out.z, src));
-                const float2 d67 = bf2_to_f2(__shfl_sync(0xffffffffu, out.w, src));
-                const float dl[8] = {d01.x, d01.y, d23.x, d23.y, d45.x, d45.y, d67.x, d67.y};
-                const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv[i]);
+                const float4 lo = reinterpret_cast<const float4*>(staged + (g + i) * 8)[0];
+                const float4 hi = reinterpret_cast<const float4*>(staged + (g + i) * 8)[1];
+                const float dl[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                const uint32_t* hw = reinterpret_cast<const uint32_t*>(&cur[i]);
                 float2 h[DC / 2];
                 #pragma unroll
                 for (int j = 0; j < DC / 2; ++j) h[j] = bf2_to_f2(hw[j]);
@@ -641,9 +658,14 @@ ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __r
                     for (int j = 0; j < DC / 2; ++j) acc[a][j] = __ffma2_rn(h[j], da, acc[a][j]);
                 }
             }
+            #pragma unroll
+            for (int i = 0; i < G; ++i) cur[i] = nxt[i];
         }
+        __syncwarp();  // every lane has read the staging rows before the next chunk rewrites them
     }
-    // this warp's partial sums, then the CTA's in warp order
+    // this warp's partial sums (over the staging rows: every warp is past its loop), then the CTA's
+    // in warp order
+    __syncthreads();
     float* mine = ro_red + warp * OUT;
     #pragma unroll
     for (int a = 0; a < 8; ++a) {
