@@ -33,6 +33,8 @@
 // the arrival counter.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "pbg_common.cuh"
 
 namespace pbg {
@@ -530,7 +532,7 @@ __global__ void __launch_bounds__(LOSS_BLOCK) ppo_generic_kernel(int64_t N, int 
 // second launch re-reading dlogits.
 //
 // Warps take 32-row chunks: lane l computes row l's dlogits (row8_backward),
-// then the warp walks the chunk's 32 hidden rows in groups of 2 or 8: lane l
+// then the warp walks the chunk's 32 hidden rows in groups of 4 or 8: lane l
 // holds columns [l*DC, l*DC + DC) of each row (one coalesced 2d-byte row per
 // warp load) and adds the row's dlogits (staged once as fp32 in shared memory,
 // read back as broadcasts) times its columns into packed fp32 accumulators.  A CTA's warps add their partial sums
@@ -543,7 +545,7 @@ constexpr int RO_THREADS = 32 * RO_WARPS;
 // hidden rows loaded per batch, and the occupancy the register budget is set for
 template <int DC>
 __host__ __device__ constexpr int ro_group() {
-    return DC == 8 ? 2 : 8;
+    return DC == 8 ? 4 : 8;
 }
 
 template <int DC>
@@ -563,7 +565,7 @@ struct HiddenVec<8> {
 
 template <int DC>
 __host__ __device__ constexpr int ro_min_blocks() {
-    return DC <= 2 ? 3 : 2;
+    return DC == 2 ? 3 : (DC == 4 ? 2 : 1);
 }
 
 template <int DC>
@@ -695,6 +697,239 @@ ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __r
     }
 }
 
+// Staged variant (d = 64 or 128, every stream 16-byte aligned): each warp keeps
+// its own ring of STAGES chunk stages in shared memory, filled by plain 1D bulk
+// copies (cp.async.bulk global -> shared, no tensor map, no multicast) that its
+// lane 0 issues STAGES chunks ahead, completing on the stage's mbarrier.  A
+// chunk's 32 hidden rows are contiguous in [N, d], so one copy brings all of
+// them, and six more bring the loss inputs; the loads no longer hold registers,
+// so the warp keeps ~3 chunks (28 KB at d = 128) in flight.  After a lane has
+// its loss row in registers, the stage's first 1,024 bytes (logits, mask,
+// action, old log pi) are reused as the fp32 dlogits staging rows.  Every wait
+// is bounded: one that runs out marks the launch failed (stats rows = -1),
+// lane 0 waits (bounded again) for its copies still in flight, and the warp
+// stops.  The rows after the last whole chunk go through direct loads.
+template <int DC>
+struct RoBulk {
+    static constexpr int D = 32 * DC;
+    static constexpr uint32_t HID = 32u * 2u * D;  // the chunk's hidden rows
+    static constexpr uint32_t LOGITS = HID, MASK = HID + 512, ACT = MASK + 256, OLD = ACT + 128, ADV = OLD + 128,
+                              WGT = ADV + 128, BYTES = WGT + 128;  // every offset a multiple of 16
+    static constexpr int STAGES = DC == 2 ? 4 : 3;
+    static constexpr size_t SMEM = (size_t)RO_WARPS * STAGES * BYTES;
+};
+
+struct RoArgs {
+    int64_t N;
+    const uint4* logits;
+    const uint2* mask;
+    const int32_t* action;
+    const float* old_logp;
+    const float* adv;
+    const float* weight;
+    const float* controls;
+    const unsigned char* hidden;
+    uint4* dlogits;
+    float* dweight;
+    float* dbias;
+    double* partials;
+    double* stats;
+};
+
+// dW += dl[row] (x) h[row] for the chunk's 32 rows: h rows from `hid` ([32][32] HV), fp32 dlogits
+// from `staged` ([32][8]).
+template <int DC>
+__device__ __forceinline__ void ro_accumulate(const typename HiddenVec<DC>::T* hid, const float* staged, int lane,
+                                              float2 (&acc)[8][DC / 2]) {
+    using HV = typename HiddenVec<DC>::T;
+    #pragma unroll 4
+    for (int r = 0; r < 32; ++r) {
+        const HV hv = hid[r * 32 + lane];
+        const float4 lo = reinterpret_cast<const float4*>(staged + r * 8)[0];
+        const float4 hi = reinterpret_cast<const float4*>(staged + r * 8)[1];
+        const float dl[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
+        float2 h[DC / 2];
+        #pragma unroll
+        for (int j = 0; j < DC / 2; ++j) h[j] = bf2_to_f2(hw[j]);
+        #pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            const float2 da = make_float2(dl[a], dl[a]);
+            #pragma unroll
+            for (int j = 0; j < DC / 2; ++j) acc[a][j] = __ffma2_rn(h[j], da, acc[a][j]);
+        }
+    }
+}
+
+__device__ __forceinline__ void ro_stage_dl(const uint4& out, float* staged, int lane, float (&db)[8]) {
+    const float2 d01 = bf2_to_f2(out.x), d23 = bf2_to_f2(out.y), d45 = bf2_to_f2(out.z), d67 = bf2_to_f2(out.w);
+    db[0] += d01.x; db[1] += d01.y; db[2] += d23.x; db[3] += d23.y;
+    db[4] += d45.x; db[5] += d45.y; db[6] += d67.x; db[7] += d67.y;
+    float4* mine = reinterpret_cast<float4*>(staged + lane * 8);
+    mine[0] = make_float4(d01.x, d01.y, d23.x, d23.y);
+    mine[1] = make_float4(d45.x, d45.y, d67.x, d67.y);
+}
+
+template <int DC>
+__global__ void __launch_bounds__(RO_THREADS, 1) ppo_readout_bulk_kernel(RoArgs a) {
+    using B = RoBulk<DC>;
+    using HV = typename HiddenVec<DC>::T;
+    constexpr int D = B::D, OUT = 8 * D + 8, S = B::STAGES;
+    extern __shared__ __align__(128) unsigned char ro_ring[];
+    __shared__ __align__(8) uint64_t full[RO_WARPS][S];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned char* ring = ro_ring + (size_t)warp * S * B::BYTES;
+    LossControls k = load_controls(a.controls);
+    RowStats s;
+    s.zero();
+    float2 acc[8][DC / 2];
+    float db[8];
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        db[q] = 0.0f;
+        #pragma unroll
+        for (int j = 0; j < DC / 2; ++j) acc[q][j] = make_float2(0.0f, 0.0f);
+    }
+    float rows_done = 0.0f;
+    const int64_t whole = a.N / 32;
+    const int64_t gw = (int64_t)blockIdx.x * RO_WARPS + warp;
+    const int64_t wstride = (int64_t)gridDim.x * RO_WARPS;
+    if (lane == 0) {
+        for (int st = 0; st < S; ++st) mbar_init(smem_u32(&full[warp][st]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    auto issue = [&](int64_t chunk, int st) {
+        const uint32_t dst = smem_u32(ring + (size_t)st * B::BYTES), bar = smem_u32(&full[warp][st]);
+        const int64_t r0 = chunk * 32;
+        // order this warp's earlier generic accesses to the stage before the copies overwrite it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bar, B::BYTES);
+        bulk_g2s(dst, a.hidden + r0 * 2 * D, B::HID, bar);
+        bulk_g2s(dst + B::LOGITS, a.logits + r0, 512, bar);
+        bulk_g2s(dst + B::MASK, a.mask + r0, 256, bar);
+        bulk_g2s(dst + B::ACT, a.action + r0, 128, bar);
+        bulk_g2s(dst + B::OLD, a.old_logp + r0, 128, bar);
+        bulk_g2s(dst + B::ADV, a.adv + r0, 128, bar);
+        bulk_g2s(dst + B::WGT, a.weight + r0, 128, bar);
+    };
+    int64_t issued = 0;  // chunks this warp has requested (lane 0's count; the same on every lane)
+    for (int st = 0; st < S; ++st) {
+        const int64_t chunk = gw + st * wstride;
+        if (chunk >= whole) break;
+        if (lane == 0) issue(chunk, st);
+        ++issued;
+    }
+    bool failed = false;
+    int64_t used = 0;
+    for (int64_t c = gw; c < whole; c += wstride, ++used) {
+        const int st = (int)(used % S);
+        const bool ok = mbar_wait_bounded(smem_u32(&full[warp][st]), (uint32_t)((used / S) & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+            failed = true;
+            break;
+        }
+        unsigned char* base = ring + (size_t)st * B::BYTES;
+        Row8 row;
+        row.logits = reinterpret_cast<const uint4*>(base + B::LOGITS)[lane];
+        row.mask = reinterpret_cast<const uint2*>(base + B::MASK)[lane];
+        row.act = reinterpret_cast<const int32_t*>(base + B::ACT)[lane];
+        row.old = reinterpret_cast<const float*>(base + B::OLD)[lane];
+        row.adv = reinterpret_cast<const float*>(base + B::ADV)[lane];
+        row.w = reinterpret_cast<const float*>(base + B::WGT)[lane];
+        __syncwarp();  // every lane holds its row: the logits .. old log pi bytes become the staging rows
+        uint4 out;
+        row8_backward(row, k, s, out);
+        __stcs(a.dlogits + c * 32 + lane, out);
+        rows_done += 1.0f;
+        float* staged = reinterpret_cast<float*>(base + B::LOGITS);
+        ro_stage_dl(out, staged, lane, db);
+        __syncwarp();
+        ro_accumulate<DC>(reinterpret_cast<const HV*>(base), staged, lane, acc);
+        __syncwarp();  // the stage is consumed
+        const int64_t next = c + S * wstride;
+        if (next < whole) {
+            if (lane == 0) issue(next, st);
+            ++issued;
+        }
+    }
+    if (failed) {
+        // copies of the chunks requested but not consumed may still be in flight
+        if (lane == 0)
+            for (int64_t m = used; m < issued; ++m)
+                mbar_wait_bounded(smem_u32(&full[warp][m % S]), (uint32_t)((m / S) & 1));
+        __syncwarp();
+    } else if (a.N % 32 && gw == whole % wstride) {
+        // the rows after the last whole chunk: direct loads, staged through this warp's first stage
+        const int64_t r = whole * 32 + lane;
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (r < a.N) {
+            Row8 row = load_row8(r, a.logits, a.mask, a.action, a.old_logp, a.adv, a.weight);
+            row8_backward(row, k, s, out);
+            __stcs(a.dlogits + r, out);
+            rows_done += 1.0f;
+        }
+        HV* hid = reinterpret_cast<HV*>(ring);
+        const HV* src = reinterpret_cast<const HV*>(a.hidden);
+        for (int rr = 0; rr < 32; ++rr)
+            hid[rr * 32 + lane] = whole * 32 + rr < a.N ? __ldcs(src + (whole * 32 + rr) * 32 + lane) : HV{};
+        float* staged = reinterpret_cast<float*>(ring + B::LOGITS);
+        ro_stage_dl(out, staged, lane, db);
+        __syncwarp();
+        ro_accumulate<DC>(hid, staged, lane, acc);
+    }
+    // every warp is past the ring: it now holds the warps' partial sums, then the CTA's in warp order
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(ro_ring);
+    float* mine = red + warp * OUT;
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        #pragma unroll
+        for (int j = 0; j < DC / 2; ++j)
+            *reinterpret_cast<float2*>(mine + q * D + lane * DC + 2 * j) = acc[q][j];
+        const float t = warp_sum(db[q]);
+        if (lane == 0) mine[8 * D + q] = t;
+    }
+    __syncthreads();
+    float* cta = reinterpret_cast<float*>(a.partials + 1 + (int64_t)gridDim.x * LOSS_STATS) + (int64_t)blockIdx.x * OUT;
+    for (int o = threadIdx.x; o < OUT; o += RO_THREADS) {
+        float v = 0.0f;
+        #pragma unroll
+        for (int w = 0; w < RO_WARPS; ++w) v += red[w * OUT + o];
+        cta[o] = v;
+    }
+    s.v[7] = rows_done;
+    if (block_stats<RO_THREADS>(s, a.partials, a.stats, __syncthreads_or(failed))) {
+        const float* all = reinterpret_cast<const float*>(a.partials + 1 + (int64_t)gridDim.x * LOSS_STATS);
+        for (int o = threadIdx.x; o < OUT; o += RO_THREADS) {
+            double v = 0.0;
+            for (unsigned b = 0; b < gridDim.x; ++b) v += (double)__ldcg(all + (int64_t)b * OUT + o);
+            if (o < 8 * D) a.dweight[o] = (float)v;
+            else a.dbias[o - 8 * D] = (float)v;
+        }
+    }
+}
+
+template <int DC>
+int readout_bulk_launch(const RoArgs& a, cudaStream_t s) {
+    static bool ready[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!ready[dev]) {
+        int rc = cuda_status(cudaFuncSetAttribute(ppo_readout_bulk_kernel<DC>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RoBulk<DC>::SMEM),
+                             "ppo_readout: shared-memory opt-in");
+        if (rc) return rc;
+        ready[dev] = true;
+    }
+    const int64_t whole = a.N / 32;
+    const int64_t need = (whole + RO_WARPS - 1) / RO_WARPS;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, sm_count()));
+    ppo_readout_bulk_kernel<DC><<<grid, RO_THREADS, RoBulk<DC>::SMEM, s>>>(a);
+    return PBG_OK;
+}
+
 template <int DC>
 int readout_grid_dc(int64_t N) {
     static int per_sm[64] = {0};
@@ -811,6 +1046,15 @@ int pbg_ppo_readout_backward(int64_t N, int32_t A, const void* logits, const uin
                            (uintptr_t)hidden % 16 == 0),
                 "ppo_readout: logits, dlogits and hidden must be 16-byte aligned, mask 8-byte aligned");
     cudaStream_t s = as_stream(stream);
+    const bool staged = N >= 32 && d <= 128 && (uintptr_t)mask % 16 == 0 && (uintptr_t)action % 16 == 0 &&
+                        (uintptr_t)old_logp % 16 == 0 && (uintptr_t)adv % 16 == 0 && (uintptr_t)weight % 16 == 0;
+    if (staged) {
+        RoArgs a{N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
+                 (const unsigned char*)hidden, (uint4*)dlogits, dweight, dbias, partials, stats};
+        const int rc = d == 64 ? readout_bulk_launch<2>(a, s) : readout_bulk_launch<4>(a, s);
+        if (rc) return rc;
+        return launch_status("ppo_readout_backward");
+    }
     const int grid = readout_grid(N > 0 ? N : 1, d);
     if (d == 64) {
         ppo_readout_kernel<2><<<grid, RO_THREADS, ro_smem<2>(), s>>>(

@@ -61,6 +61,24 @@ def test_readout_backward_matches_loss_and_torch(N, d):
         _check_readout(dl, hidden, dweight, dbias)
 
 
+def test_readout_backward_unaligned_row_streams():
+    """Per-row streams that are not 16-byte aligned take the direct-load kernel; same results."""
+
+    from pbg_b200.loss import FusedPPOBackward, FusedPPOReadoutBackward, LossConfig
+
+    N, d = 20_001, 128
+    logits, mask, action, old, adv, weight, hidden = _inputs(N + 1, d, 3)
+    logits, mask, hidden = logits[:N].contiguous(), mask[:N].contiguous(), hidden[:N].contiguous()
+    action, old, adv, weight = action[1:], old[1:], adv[1:], weight[1:]  # 4-byte offsets
+    assert action.data_ptr() % 16 != 0
+    want_d, want_s = FusedPPOBackward(N, 8, DEV, LossConfig())(logits, mask, action, old, adv, weight)
+    dl, dweight, dbias, stats = FusedPPOReadoutBackward(N, d, DEV)(logits, mask, action, old, adv, weight, hidden)
+    torch.cuda.synchronize()
+    assert torch.equal(dl, want_d)
+    np.testing.assert_allclose(stats.cpu().numpy()[[0, 6, 7]], want_s.cpu().numpy()[[0, 6, 7]], rtol=1e-5)
+    _check_readout(dl, hidden, dweight, dbias)
+
+
 def test_readout_backward_empty_batch_and_bad_arguments():
     from pbg_b200._native import lib, ptr
     from pbg_b200.loss import FusedPPOReadoutBackward
