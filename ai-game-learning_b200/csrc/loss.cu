@@ -697,13 +697,14 @@ ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __r
     }
 }
 
-// Staged variant (d = 64 or 128, every stream 16-byte aligned): each warp keeps
-// its own ring of STAGES chunk stages in shared memory, filled by plain 1D bulk
-// copies (cp.async.bulk global -> shared, no tensor map, no multicast) that its
-// lane 0 issues STAGES chunks ahead, completing on the stage's mbarrier.  A
+// Staged variant (d = 64 or 128, every stream 16-byte aligned): each of the 12
+// warps keeps its own ring of STAGES chunk stages in shared memory, filled by
+// plain 1D bulk copies (cp.async.bulk global -> shared, no tensor map, no
+// multicast) that its lane 0 issues STAGES chunks ahead, completing on the
+// stage's mbarrier.  A
 // chunk's 32 hidden rows are contiguous in [N, d], so one copy brings all of
 // them, and six more bring the loss inputs; the loads no longer hold registers,
-// so the warp keeps ~3 chunks (28 KB at d = 128) in flight.  After a lane has
+// so a CTA of 12 warps keeps up to 24 chunks (227 KB at d = 128) in flight.  After a lane has
 // its loss row in registers, the stage's first 1,024 bytes (logits, mask,
 // action, old log pi) are reused as the fp32 dlogits staging rows.  Every wait
 // is bounded: one that runs out marks the launch failed (stats rows = -1),
@@ -715,8 +716,10 @@ struct RoBulk {
     static constexpr uint32_t HID = 32u * 2u * D;  // the chunk's hidden rows
     static constexpr uint32_t LOGITS = HID, MASK = HID + 512, ACT = MASK + 256, OLD = ACT + 128, ADV = OLD + 128,
                               WGT = ADV + 128, BYTES = WGT + 128;  // every offset a multiple of 16
-    static constexpr int STAGES = DC == 2 ? 4 : 3;
-    static constexpr size_t SMEM = (size_t)RO_WARPS * STAGES * BYTES;
+    static constexpr int STAGES = DC == 2 ? 3 : 2;
+    static constexpr int WARPS = 12;
+    static constexpr int THREADS = 32 * WARPS;
+    static constexpr size_t SMEM = (size_t)WARPS * STAGES * BYTES;
 };
 
 struct RoArgs {
@@ -737,26 +740,29 @@ struct RoArgs {
 };
 
 // dW += dl[row] (x) h[row] for the chunk's 32 rows: h rows from `hid` ([32][32] HV), fp32 dlogits
-// from `staged` ([32][8]).
+// from `staged` ([32][8]).  acc[p][c] holds (dW[2p][col], dW[2p+1][col]) for the lane's column c: the
+// logit pairs come straight from the staged row, only the hidden value is duplicated per pair.
 template <int DC>
 __device__ __forceinline__ void ro_accumulate(const typename HiddenVec<DC>::T* hid, const float* staged, int lane,
-                                              float2 (&acc)[8][DC / 2]) {
+                                              float2 (&acc)[4][DC]) {
     using HV = typename HiddenVec<DC>::T;
     #pragma unroll 4
     for (int r = 0; r < 32; ++r) {
         const HV hv = hid[r * 32 + lane];
         const float4 lo = reinterpret_cast<const float4*>(staged + r * 8)[0];
         const float4 hi = reinterpret_cast<const float4*>(staged + r * 8)[1];
-        const float dl[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        const float2 dp[4] = {make_float2(lo.x, lo.y), make_float2(lo.z, lo.w), make_float2(hi.x, hi.y),
+                              make_float2(hi.z, hi.w)};
         const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
-        float2 h[DC / 2];
         #pragma unroll
-        for (int j = 0; j < DC / 2; ++j) h[j] = bf2_to_f2(hw[j]);
-        #pragma unroll
-        for (int a = 0; a < 8; ++a) {
-            const float2 da = make_float2(dl[a], dl[a]);
+        for (int j = 0; j < DC / 2; ++j) {
+            const float h0 = __uint_as_float(hw[j] << 16), h1 = __uint_as_float(hw[j] & 0xffff0000u);
+            const float2 hh0 = make_float2(h0, h0), hh1 = make_float2(h1, h1);
             #pragma unroll
-            for (int j = 0; j < DC / 2; ++j) acc[a][j] = __ffma2_rn(h[j], da, acc[a][j]);
+            for (int q = 0; q < 4; ++q) {
+                acc[q][2 * j] = __ffma2_rn(dp[q], hh0, acc[q][2 * j]);
+                acc[q][2 * j + 1] = __ffma2_rn(dp[q], hh1, acc[q][2 * j + 1]);
+            }
         }
     }
 }
@@ -771,29 +777,30 @@ __device__ __forceinline__ void ro_stage_dl(const uint4& out, float* staged, int
 }
 
 template <int DC>
-__global__ void __launch_bounds__(RO_THREADS, 1) ppo_readout_bulk_kernel(RoArgs a) {
+__global__ void __launch_bounds__(RoBulk<DC>::THREADS, 1) ppo_readout_bulk_kernel(RoArgs a) {
     using B = RoBulk<DC>;
     using HV = typename HiddenVec<DC>::T;
-    constexpr int D = B::D, OUT = 8 * D + 8, S = B::STAGES;
+    constexpr int D = B::D, OUT = 8 * D + 8, S = B::STAGES, W = B::WARPS;
     extern __shared__ __align__(128) unsigned char ro_ring[];
-    __shared__ __align__(8) uint64_t full[RO_WARPS][S];
+    __shared__ __align__(8) uint64_t full[W][S];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     unsigned char* ring = ro_ring + (size_t)warp * S * B::BYTES;
     LossControls k = load_controls(a.controls);
     RowStats s;
     s.zero();
-    float2 acc[8][DC / 2];
+    float2 acc[4][DC];
     float db[8];
     #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        db[q] = 0.0f;
+    for (int q = 0; q < 8; ++q) db[q] = 0.0f;
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
         #pragma unroll
-        for (int j = 0; j < DC / 2; ++j) acc[q][j] = make_float2(0.0f, 0.0f);
+        for (int j = 0; j < DC; ++j) acc[q][j] = make_float2(0.0f, 0.0f);
     }
     float rows_done = 0.0f;
     const int64_t whole = a.N / 32;
-    const int64_t gw = (int64_t)blockIdx.x * RO_WARPS + warp;
-    const int64_t wstride = (int64_t)gridDim.x * RO_WARPS;
+    const int64_t gw = (int64_t)blockIdx.x * W + warp;
+    const int64_t wstride = (int64_t)gridDim.x * W;
     if (lane == 0) {
         for (int st = 0; st < S; ++st) mbar_init(smem_u32(&full[warp][st]), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -883,25 +890,30 @@ __global__ void __launch_bounds__(RO_THREADS, 1) ppo_readout_bulk_kernel(RoArgs 
     float* red = reinterpret_cast<float*>(ro_ring);
     float* mine = red + warp * OUT;
     #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < 4; ++q) {
         #pragma unroll
-        for (int j = 0; j < DC / 2; ++j)
-            *reinterpret_cast<float2*>(mine + q * D + lane * DC + 2 * j) = acc[q][j];
+        for (int j = 0; j < DC; ++j) {
+            mine[(2 * q) * D + lane * DC + j] = acc[q][j].x;
+            mine[(2 * q + 1) * D + lane * DC + j] = acc[q][j].y;
+        }
+    }
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) {
         const float t = warp_sum(db[q]);
         if (lane == 0) mine[8 * D + q] = t;
     }
     __syncthreads();
     float* cta = reinterpret_cast<float*>(a.partials + 1 + (int64_t)gridDim.x * LOSS_STATS) + (int64_t)blockIdx.x * OUT;
-    for (int o = threadIdx.x; o < OUT; o += RO_THREADS) {
+    for (int o = threadIdx.x; o < OUT; o += B::THREADS) {
         float v = 0.0f;
         #pragma unroll
-        for (int w = 0; w < RO_WARPS; ++w) v += red[w * OUT + o];
+        for (int w = 0; w < W; ++w) v += red[w * OUT + o];
         cta[o] = v;
     }
     s.v[7] = rows_done;
-    if (block_stats<RO_THREADS>(s, a.partials, a.stats, __syncthreads_or(failed))) {
+    if (block_stats<B::THREADS>(s, a.partials, a.stats, __syncthreads_or(failed))) {
         const float* all = reinterpret_cast<const float*>(a.partials + 1 + (int64_t)gridDim.x * LOSS_STATS);
-        for (int o = threadIdx.x; o < OUT; o += RO_THREADS) {
+        for (int o = threadIdx.x; o < OUT; o += B::THREADS) {
             double v = 0.0;
             for (unsigned b = 0; b < gridDim.x; ++b) v += (double)__ldcg(all + (int64_t)b * OUT + o);
             if (o < 8 * D) a.dweight[o] = (float)v;
@@ -924,9 +936,9 @@ int readout_bulk_launch(const RoArgs& a, cudaStream_t s) {
         ready[dev] = true;
     }
     const int64_t whole = a.N / 32;
-    const int64_t need = (whole + RO_WARPS - 1) / RO_WARPS;
+    const int64_t need = (whole + RoBulk<DC>::WARPS - 1) / RoBulk<DC>::WARPS;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, sm_count()));
-    ppo_readout_bulk_kernel<DC><<<grid, RO_THREADS, RoBulk<DC>::SMEM, s>>>(a);
+    ppo_readout_bulk_kernel<DC><<<grid, RoBulk<DC>::THREADS, RoBulk<DC>::SMEM, s>>>(a);
     return PBG_OK;
 }
 
