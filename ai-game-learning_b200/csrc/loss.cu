@@ -697,8 +697,8 @@ ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __r
     }
 }
 
-// Staged variant (d = 64 or 128, every stream 16-byte aligned): each of the 12
-// warps keeps its own ring of STAGES chunk stages in shared memory, filled by
+// Staged variant (every stream 16-byte aligned): each warp (12 per CTA, 6 at
+// d = 256) keeps its own ring of STAGES chunk stages in shared memory, filled by
 // plain 1D bulk copies (cp.async.bulk global -> shared, no tensor map, no
 // multicast) that its lane 0 issues STAGES chunks ahead, completing on the
 // stage's mbarrier.  A
@@ -717,7 +717,7 @@ struct RoBulk {
     static constexpr uint32_t LOGITS = HID, MASK = HID + 512, ACT = MASK + 256, OLD = ACT + 128, ADV = OLD + 128,
                               WGT = ADV + 128, BYTES = WGT + 128;  // every offset a multiple of 16
     static constexpr int STAGES = DC == 2 ? 3 : 2;
-    static constexpr int WARPS = 12;
+    static constexpr int WARPS = DC == 8 ? 6 : 12;
     static constexpr int THREADS = 32 * WARPS;
     static constexpr size_t SMEM = (size_t)WARPS * STAGES * BYTES;
 };
@@ -922,6 +922,14 @@ __global__ void __launch_bounds__(RoBulk<DC>::THREADS, 1) ppo_readout_bulk_kerne
     }
 }
 
+// CTAs of the staged launch: one per SM at most, each with work for every warp where there is enough.
+template <int DC>
+int readout_bulk_grid(int64_t N) {
+    const int64_t whole = N / 32;
+    const int64_t need = (whole + RoBulk<DC>::WARPS - 1) / RoBulk<DC>::WARPS;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(need, sm_count()));
+}
+
 template <int DC>
 int readout_bulk_launch(const RoArgs& a, cudaStream_t s) {
     static bool ready[64] = {false};
@@ -935,10 +943,7 @@ int readout_bulk_launch(const RoArgs& a, cudaStream_t s) {
         if (rc) return rc;
         ready[dev] = true;
     }
-    const int64_t whole = a.N / 32;
-    const int64_t need = (whole + RoBulk<DC>::WARPS - 1) / RoBulk<DC>::WARPS;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, sm_count()));
-    ppo_readout_bulk_kernel<DC><<<grid, RoBulk<DC>::THREADS, RoBulk<DC>::SMEM, s>>>(a);
+    ppo_readout_bulk_kernel<DC><<<readout_bulk_grid<DC>(a.N), RoBulk<DC>::THREADS, RoBulk<DC>::SMEM, s>>>(a);
     return PBG_OK;
 }
 
@@ -1039,7 +1044,10 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
 
 int64_t pbg_ppo_readout_partials_size(int64_t N, int32_t A, int32_t d) {
     if (A != 8 || !(d == 64 || d == 128 || d == 256)) return -1;
-    const int64_t grid = readout_grid(N > 0 ? N : 1, d);
+    // the wider of the two launches (direct-load and staged) sizes the per-block partials
+    const int64_t n = N > 0 ? N : 1;
+    const int64_t staged = d == 64 ? readout_bulk_grid<2>(n) : d == 128 ? readout_bulk_grid<4>(n) : readout_bulk_grid<8>(n);
+    const int64_t grid = std::max<int64_t>(readout_grid(n, d), staged);
     const int64_t floats = grid * (8LL * d + 8);
     // counter/error slot, per-block statistics, then per-block dW/db partials (two floats per slot)
     return 1 + grid * LOSS_STATS + (floats + 1) / 2;
@@ -1058,12 +1066,14 @@ int pbg_ppo_readout_backward(int64_t N, int32_t A, const void* logits, const uin
                            (uintptr_t)hidden % 16 == 0),
                 "ppo_readout: logits, dlogits and hidden must be 16-byte aligned, mask 8-byte aligned");
     cudaStream_t s = as_stream(stream);
-    const bool staged = N >= 32 && d <= 128 && (uintptr_t)mask % 16 == 0 && (uintptr_t)action % 16 == 0 &&
+    const bool staged = N >= 32 && (uintptr_t)mask % 16 == 0 && (uintptr_t)action % 16 == 0 &&
                         (uintptr_t)old_logp % 16 == 0 && (uintptr_t)adv % 16 == 0 && (uintptr_t)weight % 16 == 0;
     if (staged) {
         RoArgs a{N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
                  (const unsigned char*)hidden, (uint4*)dlogits, dweight, dbias, partials, stats};
-        const int rc = d == 64 ? readout_bulk_launch<2>(a, s) : readout_bulk_launch<4>(a, s);
+        const int rc = d == 64    ? readout_bulk_launch<2>(a, s)
+                       : d == 128 ? readout_bulk_launch<4>(a, s)
+                                  : readout_bulk_launch<8>(a, s);
         if (rc) return rc;
         return launch_status("ppo_readout_backward");
     }

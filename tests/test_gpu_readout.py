@@ -41,7 +41,7 @@ def _check_readout(dl, hidden, dweight, dbias):
     assert torch.all((dbias.double() - ref_b).abs() <= 1e-5 * mag_b + 1e-30), "dbias differs"
 
 
-@pytest.mark.parametrize("N,d", [(4999, 64), (5000, 128), (300_001, 128), (70_000, 256), (33, 128)])
+@pytest.mark.parametrize("N,d", [(4999, 64), (5000, 128), (300_001, 128), (70_000, 256), (453, 256), (33, 128)])
 def test_readout_backward_matches_loss_and_torch(N, d):
     from pbg_b200.loss import FusedPPOBackward, FusedPPOReadoutBackward, LossConfig
 
@@ -61,12 +61,13 @@ def test_readout_backward_matches_loss_and_torch(N, d):
         _check_readout(dl, hidden, dweight, dbias)
 
 
-def test_readout_backward_unaligned_row_streams():
+@pytest.mark.parametrize("d", [128, 256])
+def test_readout_backward_unaligned_row_streams(d):
     """Per-row streams that are not 16-byte aligned take the direct-load kernel; same results."""
 
     from pbg_b200.loss import FusedPPOBackward, FusedPPOReadoutBackward, LossConfig
 
-    N, d = 20_001, 128
+    N = 20_001
     logits, mask, action, old, adv, weight, hidden = _inputs(N + 1, d, 3)
     logits, mask, hidden = logits[:N].contiguous(), mask[:N].contiguous(), hidden[:N].contiguous()
     action, old, adv, weight = action[1:], old[1:], adv[1:], weight[1:]  # 4-byte offsets
