@@ -734,7 +734,7 @@ def readout_component(device, rows=4_194_304, hidden=128, reps=10):
             "us": 1000.0 * ms, "decisions_per_s": rows / (ms / 1000.0),
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "bytes_per_row": per_row, "peak_kind": kind},
-            "kernel": "ppo_readout_kernel", "gpu_launches": 1}
+            "kernel": "ppo_readout_bulk_kernel", "gpu_launches": 1}
 
 
 def folded_component(device, rows=64):
