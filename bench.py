@@ -737,6 +737,37 @@ def readout_component(device, rows=4_194_304, hidden=128, reps=10):
             "kernel": "ppo_readout_bulk_kernel", "gpu_launches": 1}
 
 
+def optimizer_component(device, params=4_226_931, reps=10):
+    """The flat-buffer Adam step (pbg_b200.optim.FlatAdam, three launches: norm, finalise, apply) over the
+    cfg2 architecture's 4,226,931 fp32 parameters (16,907,724 B, model_storage_bytes / 4).  Algorithmic
+    bytes per parameter: 4 (gradient read by the norm pass) + 16 read + 16 written by the apply; each step
+    queued behind a device-side sleep."""
+
+    import torch
+    from pbg_b200.optim import FlatAdam
+
+    g = torch.Generator(device=device).manual_seed(9)
+    master = torch.randn(params, generator=g, device=device)
+    opt = FlatAdam(master, lr=1e-3, decay=0.01, clip=1.0)
+    grad = torch.randn(params, generator=g, device=device) * 1e-3
+
+    def step():
+        opt.grad.copy_(grad)
+        opt.step()
+
+    ms = _device_ms(device, step, reps)
+    copy_ms = _device_ms(device, lambda: opt.grad.copy_(grad), reps)
+    peak, kind = measured_peak()
+    step_ms = ms - copy_ms
+    gbs = 36 * params / (step_ms / 1000.0) / 1e9
+    return {"workload": f"flat AdamW step over {params} fp32 parameters (cfg2 architecture)", "us": 1000.0 * step_ms,
+            "note": "timed as (gradient refill + step) minus the refill alone; the 68 MB working set fits in the "
+                    "126 MB L2, so part of the traffic is L2 hits",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "bytes_per_param": 36, "peak_kind": kind},
+            "kernels": ["adam_norm_kernel", "adam_finalize_kernel", "adam_apply4_kernel"], "gpu_launches": 3}
+
+
 def folded_component(device, rows=64):
     """Multiway folded statistics (queued/folded.py): 6-max R13, four folded seats (all tight), flop
     boards, `rows` decisions; the finite-difference removal queries (1 + 52 + 1326 per decision) in
@@ -1083,6 +1114,7 @@ def main():
                                   "postflop_forward": postflop_forward_component(device),
                                   "posterior_sampler": posterior_component(device),
                                   "loss_readout": readout_component(device),
+                                  "optimizer_step": optimizer_component(device),
                                   "folded_statistics": folded_component(device),
                                   "branched_sampling": branching_component(device),
                                   "rollout_with_model": rollout_with_model_component(device)}

@@ -558,6 +558,29 @@ def test_adam_matches_reference_golden(gold):
     assert int(opt.step_count[0]) == 3
 
 
+def test_adam_vector_and_scalar_apply_agree():
+    """Aligned buffers take the four-per-thread apply, a master offset by one element the scalar one."""
+
+    from pbg_b200.optim import FlatAdam
+
+    n = 100_003
+    g = torch.Generator(device=DEV).manual_seed(4)
+    start = torch.randn(n + 1, generator=g, device=DEV)
+    grads = [torch.randn(n, generator=g, device=DEV) * 1e-2 for _ in range(3)]
+    aligned = FlatAdam(start[:n].clone(), lr=1e-3, decay=0.01, clip=0.5)
+    shifted_storage = torch.zeros(n + 1, device=DEV)
+    shifted_storage[1:] = start[:n]
+    shifted = FlatAdam(shifted_storage[1:], lr=1e-3, decay=0.01, clip=0.5)
+    assert shifted.master.data_ptr() % 16 != 0
+    for grad in grads:
+        for opt in (aligned, shifted):
+            opt.grad.copy_(grad)
+            opt.step()
+    torch.testing.assert_close(shifted.master, aligned.master, rtol=1e-6, atol=1e-9)
+    torch.testing.assert_close(shifted.first, aligned.first, rtol=1e-6, atol=1e-12)
+    torch.testing.assert_close(shifted.second, aligned.second, rtol=1e-6, atol=1e-15)
+
+
 def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
     """694,733 rows: 700 full 992-row tiles (several passes of the 4-stage ring per CTA) + 333 tail rows."""
 
