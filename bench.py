@@ -768,6 +768,37 @@ def optimizer_component(device, params=4_226_931, reps=10):
             "kernels": ["adam_norm_kernel", "adam_finalize_kernel", "adam_apply4_kernel"], "gpu_launches": 3}
 
 
+def showdown_component(device, hands=1_048_576, players=6, reps=10):
+    """Sampled settlement's showdown (poker_gpu_evaluator.evaluate_showdowns, the contract-v2 call
+    signature): `hands` 6-max R13 showdowns, every seat at stratum 0 except ~20 % folded (-1), seeded
+    distinct cards per hand; one launch per call, queued behind a device-side sleep."""
+
+    import numpy as np
+    import torch
+    import poker_gpu_evaluator as poker
+
+    rng = np.random.default_rng(12)
+    deal = np.argsort(rng.random((hands, 52), dtype=np.float32), axis=1)[:, : 5 + 2 * players]
+    board = torch.from_numpy(deal[:, :5].astype(np.uint8)).to(device)
+    lo = np.minimum(deal[:, 5::2], deal[:, 6::2])
+    hi = np.maximum(deal[:, 5::2], deal[:, 6::2])
+    combo = torch.from_numpy((lo * (103 - lo) // 2 + hi - lo - 1).astype(np.int32)).to(device)
+    level = np.where(rng.random((hands, players)) < 0.2, -1, 0).astype(np.int32)
+    level[:, 0] = 0
+    base = -rng.integers(1, 16, (hands, players)).astype(np.float32)
+    amount = np.zeros((hands, players), np.float32)
+    amount[:, 0] = -base.sum(1)
+    level, base, amount = (torch.from_numpy(x).to(device) for x in (level, base, amount))
+    ev = poker.bind(13)
+    ms = _device_ms(device, lambda: ev.evaluate_showdowns(board_cards=board, combo_ids=combo, stratum_level=level,
+                                                          payoff_baseline=base, stratum_amount=amount), reps)
+    return {"workload": f"{hands} {players}-max R13 showdowns (one stratum, ~20 % of seats folded)",
+            "us": 1000.0 * ms, "hands_per_s": hands / (ms / 1000.0),
+            "seat_hands_per_s": hands * players / (ms / 1000.0),
+            "bound": "integer issue (7-card evaluation per contending seat)", "kernel": "showdown_kernel",
+            "gpu_launches": 1}
+
+
 def folded_component(device, rows=64):
     """Multiway folded statistics (queued/folded.py): 6-max R13, four folded seats (all tight), flop
     boards, `rows` decisions; the finite-difference removal queries (1 + 52 + 1326 per decision) in
@@ -1115,6 +1146,7 @@ def main():
                                   "posterior_sampler": posterior_component(device),
                                   "loss_readout": readout_component(device),
                                   "optimizer_step": optimizer_component(device),
+                                  "showdown": showdown_component(device),
                                   "folded_statistics": folded_component(device),
                                   "branched_sampling": branching_component(device),
                                   "rollout_with_model": rollout_with_model_component(device)}
