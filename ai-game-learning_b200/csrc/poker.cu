@@ -648,10 +648,27 @@ __device__ __forceinline__ float selected_log_row(const RawRow& raw, const Legal
 }
 
 // Reach update: block per hand, thread per private row --------------------
+// The hand -> (cards, class) table is decoded once per block into shared
+// memory, and each thread's log-reach values are loaded before the policy rows
+// are evaluated (they do not depend on them), so their latency overlaps.
+constexpr int RC_THREADS = 256;
+constexpr int RC_MAXH = 1326;                                    // 52 cards
+constexpr int RC_CHUNKS = (RC_MAXH + RC_THREADS - 1) / RC_THREADS;  // private rows per thread
+
 template <int P>
-__global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, const int32_t* action,
-                             const int32_t* decision, float* log_reach) {
+__global__ void __launch_bounds__(RC_THREADS) reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol,
+                                                           const int32_t* action, const int32_t* decision,
+                                                           float* log_reach) {
     extern __shared__ float sel[];  // [H]
+    __shared__ uint16_t pair_s[RC_MAXH];  // (c0 - first) | (c1 - first) << 8
+    __shared__ uint8_t class_s[RC_MAXH];
+    for (int h = threadIdx.x; h < d.H; h += RC_THREADS) {
+        int c0, c1;
+        combo_cards(d.D, d.first, h, c0, c1);
+        pair_s[h] = (uint16_t)((c0 - d.first) | ((c1 - d.first) << 8));
+        class_s[h] = (uint8_t)combo_class(d.R, c0, c1);
+    }
+    __syncthreads();
     for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
         int a = decision[4 * b];
         if (a < 0) continue;  // hand was already terminal
@@ -663,7 +680,15 @@ __global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, con
         L.call_legal = (decision[4 * b + 3] >> 16) & 1;
         int act = action[b];
         int rows = street_before == 0 ? d.K : d.H;
-        for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+        float* reach = log_reach + (int64_t)b * P * d.H;
+        float held[RC_CHUNKS][P];
+        #pragma unroll
+        for (int k = 0; k < RC_CHUNKS; ++k) {
+            const int hnd = threadIdx.x + k * RC_THREADS;
+            #pragma unroll
+            for (int p = 0; p < P; ++p) held[k][p] = hnd < d.H ? reach[p * d.H + hnd] : 0.0f;
+        }
+        for (int r = threadIdx.x; r < rows; r += RC_THREADS) {
             sel[r] = selected_log_row(raw_row(pol, b * pol.rows + r), L, d.T, act);
         }
         __syncthreads();
@@ -673,15 +698,16 @@ __global__ void reach_kernel(Geo d, int64_t B, pbg_state st, pbg_policy pol, con
             int c = st.board[b * 5 + i];
             if (c != PAD_CARD) board_cards |= 1ULL << (c - d.first);
         }
-        float* reach = log_reach + (int64_t)b * P * d.H;
-        for (int hnd = threadIdx.x; hnd < d.H; hnd += blockDim.x) {
-            int c0, c1;
-            combo_cards(d.D, d.first, hnd, c0, c1);
-            int r = street_before == 0 ? combo_class(d.R, c0, c1) : hnd;
-            bool conflict = ((board_cards >> (c0 - d.first)) & 1ULL) || ((board_cards >> (c1 - d.first)) & 1ULL);
+        #pragma unroll
+        for (int k = 0; k < RC_CHUNKS; ++k) {
+            const int hnd = threadIdx.x + k * RC_THREADS;
+            if (hnd >= d.H) break;
+            const unsigned pc = pair_s[hnd];
+            const int r = street_before == 0 ? (int)class_s[hnd] : hnd;
+            const bool conflict = ((board_cards >> (pc & 0xffu)) | (board_cards >> (pc >> 8))) & 1ULL;
             #pragma unroll
             for (int p = 0; p < P; ++p) {
-                float v = reach[p * d.H + hnd];
+                float v = held[k][p];
                 if (p == a) v = __fadd_rn(v, sel[r]);
                 if (conflict) v = -INFINITY;
                 reach[p * d.H + hnd] = v;
@@ -1008,8 +1034,9 @@ int pbg_reach_update(pbg_geometry g, int64_t B, pbg_state st, pbg_policy pol, co
     PBG_REQUIRE(B >= 0 && state_ok(st) && action && decision && log_reach, "reach_update: bad arguments");
     PBG_REQUIRE(pol.rows >= d.H && pol.mixtures >= 1 && pol.mixtures <= 8, "reach_update: policy rows must be >= H");
     if (B == 0) return PBG_OK;
-    int blocks = stride_grid(B * 256, 256, 8);
-    PBG_DISPATCH_P(g.players, reach_kernel<PP><<<blocks, 256, d.H * sizeof(float), as_stream(stream)>>>(
+    int blocks = stride_grid(B * RC_THREADS, RC_THREADS, 8);
+    PBG_REQUIRE(d.H <= RC_MAXH, "reach_update: at most 52 cards");
+    PBG_DISPATCH_P(g.players, reach_kernel<PP><<<blocks, RC_THREADS, d.H * sizeof(float), as_stream(stream)>>>(
         d, B, st, pol, action, decision, log_reach));
     return launch_status("reach_update");
 }

@@ -46,12 +46,13 @@ def parse():
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
-                                                 "readout"),
+                                                 "readout", "reach"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
                         "the beta eigendecomposition of components.folded_statistics; posterior: one call of "
-                        "components.posterior_sampler; readout: one launch of components.loss_readout) "
+                        "components.posterior_sampler; readout: one launch of components.loss_readout; reach: "
+                        "one launch of components.reach_update) "
                         "between cudaProfilerStart/Stop (for ncu "
                         "--profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
@@ -799,6 +800,40 @@ def showdown_component(device, hands=1_048_576, players=6, reps=10):
             "gpu_launches": 1}
 
 
+def reach_component(device, hands=16_384, seed=0, reps=10):
+    """The reach update after a preflop decision (pbg_reach_update, hooks.py:1641-1703): `hands` HU 100bb
+    R13 hands after their first step, a seeded raw policy for every private row; per hand the 169 class
+    rows' log pi of the taken action (closed-form policy) and the [2, 1326] log-reach rows read and
+    written.  Each call queued behind a device-side sleep (the update is applied repeatedly in place)."""
+
+    import torch
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.rollout import RolloutStep
+
+    geometry = NLHEGeometry(2, 100.0, 13)
+    stepper = RolloutStep(geometry, seed=seed, iteration=0)
+    H, M = geometry.private_hands, 2
+    g = torch.Generator(device=device).manual_seed(seed + 3)
+    raw = {"type_logits": torch.randn((hands, H, 3), generator=g, device=device),
+           "omega": torch.softmax(torch.randn((hands, H, M), generator=g, device=device), -1),
+           "mu": torch.rand((hands, H, M), generator=g, device=device),
+           "s": torch.rand((hands, H, M), generator=g, device=device) * 0.3 + 0.02,
+           "iota": torch.rand((hands, H), generator=g, device=device) * 0.2}
+    arena = stepper.roots(hands, device=device)
+    stepper.step(arena, raw)
+    log_reach = torch.zeros((hands, 2, H), dtype=torch.float32, device=device)
+    ms = _device_ms(device, lambda: stepper.reach_update(arena, raw, log_reach), reps)
+    per_hand = 169 * (3 + 3 * M + 1) * 4 + 2 * 4 * 2 * H
+    peak, kind = measured_peak()
+    gbs = per_hand * hands / (ms / 1000.0) / 1e9
+    return {"workload": f"reach update after the first (preflop) decision, HU 100bb R13, {hands} hands",
+            "us": 1000.0 * ms, "hands_per_s": hands / (ms / 1000.0),
+            "policy_rows_per_s": 169 * hands / (ms / 1000.0),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "bytes_per_hand": per_hand, "peak_kind": kind},
+            "kernel": "reach_kernel", "gpu_launches": 1}
+
+
 def folded_component(device, rows=64):
     """Multiway folded statistics (queued/folded.py): 6-max R13, four folded seats (all tight), flop
     boards, `rows` decisions; the finite-difference removal queries (1 + 52 + 1326 per decision) in
@@ -950,7 +985,7 @@ def main():
         global PROFILE_ONE_FORWARD
         PROFILE_ONE_FORWARD = True
         name = {"folded": "folded_component", "posterior": "posterior_component",
-                "readout": "readout_component"}.get(
+                "readout": "readout_component", "reach": "reach_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         globals()[name](device)
         return
@@ -1147,6 +1182,7 @@ def main():
                                   "loss_readout": readout_component(device),
                                   "optimizer_step": optimizer_component(device),
                                   "showdown": showdown_component(device),
+                                  "reach_update": reach_component(device),
                                   "folded_statistics": folded_component(device),
                                   "branched_sampling": branching_component(device),
                                   "rollout_with_model": rollout_with_model_component(device)}
