@@ -46,13 +46,14 @@ def parse():
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
-                                                 "readout", "reach"),
+                                                 "readout", "reach", "showdown", "optimizer"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
                         "the beta eigendecomposition of components.folded_statistics; posterior: one call of "
                         "components.posterior_sampler; readout: one launch of components.loss_readout; reach: "
-                        "one launch of components.reach_update) "
+                        "one launch of components.reach_update; showdown / optimizer: one call of "
+                        "components.showdown / components.optimizer_step) "
                         "between cudaProfilerStart/Stop (for ncu "
                         "--profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
@@ -985,7 +986,8 @@ def main():
         global PROFILE_ONE_FORWARD
         PROFILE_ONE_FORWARD = True
         name = {"folded": "folded_component", "posterior": "posterior_component",
-                "readout": "readout_component", "reach": "reach_component"}.get(
+                "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
+                "optimizer": "optimizer_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         globals()[name](device)
         return
