@@ -4,9 +4,10 @@
 // unscale by the loss scale, global 2-norm and finiteness, norm clipping,
 // coupled or decoupled weight decay, bias-corrected moments, and the
 // all-or-nothing rule (a non-finite gradient leaves masters and moments
-// untouched and zeroes the gradient rows).  Three stream-ordered launches:
-// per-block sum of squares -> one-block finalise of the scalars -> apply
-// (four parameters per thread when the streams are 16-byte aligned).
+// untouched and zeroes the gradient rows).  Two stream-ordered launches:
+// per-block sum of squares, whose last block to finish computes the step's
+// scalars (norm, clip scale, bias corrections) -> apply (four parameters per
+// thread when the streams are 16-byte aligned).
 // Algorithmic traffic: 4 B per parameter for the norm pass, 32 B for the apply.
 // The dynamic fp16 loss-scale update (growth/backoff trackers) is not part
 // of this step: the scale is read from controls[6] as given.
@@ -16,43 +17,15 @@ namespace pbg {
 
 constexpr int ADAM_BLOCK = 256;
 
-__global__ void __launch_bounds__(ADAM_BLOCK) adam_norm_kernel(int64_t n, const float4* __restrict__ grad4,
-                                                                const float* __restrict__ grad,
-                                                                const float* controls, double* partials) {
-    float inv_scale = 1.0f / controls[6];
-    float ss = 0.0f;
-    float bad = 0.0f;
-    int64_t n4 = n / 4;
-    for (int64_t i = (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n4; i += (int64_t)gridDim.x * ADAM_BLOCK) {
-        float4 g = __ldcs(grad4 + i);
-        float a = g.x * inv_scale, b = g.y * inv_scale, c = g.z * inv_scale, d = g.w * inv_scale;
-        ss += a * a + b * b + c * c + d * d;
-        bad += (isfinite(a) && isfinite(b) && isfinite(c) && isfinite(d)) ? 0.0f : 1.0f;
-    }
-    for (int64_t i = 4 * n4 + (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n; i += (int64_t)gridDim.x * ADAM_BLOCK) {
-        float a = grad[i] * inv_scale;
-        ss += a * a;
-        bad += isfinite(a) ? 0.0f : 1.0f;
-    }
-    __shared__ float red[2][ADAM_BLOCK / 32];
-    float s1 = warp_sum(ss), s2 = warp_sum(bad);
-    if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = s1; red[1][threadIdx.x >> 5] = s2; }
-    __syncthreads();
-    if (threadIdx.x < 2) {
-        double acc = 0.0;
-        for (int w = 0; w < ADAM_BLOCK / 32; ++w) acc += (double)red[threadIdx.x][w];
-        partials[2 * (int64_t)blockIdx.x + threadIdx.x] = acc;
-    }
-}
-
 // report: [applied, finite, norm, clip_scale, step_after, c1, c2, unused]
-__global__ void adam_finalize_kernel(int blocks, const double* partials, const float* controls, int64_t* step,
-                                     double* report) {
+// Run by one block of ADAM_BLOCK threads.
+__device__ __forceinline__ void adam_finalize(int blocks, const double* partials, const float* controls,
+                                              int64_t* step, double* report) {
     __shared__ double red[2][ADAM_BLOCK];
     double ss = 0.0, bad = 0.0;
     for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        ss += partials[2 * (int64_t)b];
-        bad += partials[2 * (int64_t)b + 1];
+        ss += __ldcg(partials + 2 * (int64_t)b);
+        bad += __ldcg(partials + 2 * (int64_t)b + 1);
     }
     red[0][threadIdx.x] = ss;
     red[1][threadIdx.x] = bad;
@@ -83,6 +56,49 @@ __global__ void adam_finalize_kernel(int blocks, const double* partials, const f
         step[0] = t;
     }
 }
+
+__global__ void __launch_bounds__(ADAM_BLOCK) adam_norm_kernel(int64_t n, const float4* __restrict__ grad4,
+                                                                const float* __restrict__ grad,
+                                                                const float* controls, double* partials,
+                                                                int64_t* step, double* report) {
+    float inv_scale = 1.0f / controls[6];
+    float ss = 0.0f;
+    float bad = 0.0f;
+    int64_t n4 = n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n4; i += (int64_t)gridDim.x * ADAM_BLOCK) {
+        float4 g = __ldcs(grad4 + i);
+        float a = g.x * inv_scale, b = g.y * inv_scale, c = g.z * inv_scale, d = g.w * inv_scale;
+        ss += a * a + b * b + c * c + d * d;
+        bad += (isfinite(a) && isfinite(b) && isfinite(c) && isfinite(d)) ? 0.0f : 1.0f;
+    }
+    for (int64_t i = 4 * n4 + (int64_t)blockIdx.x * ADAM_BLOCK + threadIdx.x; i < n; i += (int64_t)gridDim.x * ADAM_BLOCK) {
+        float a = grad[i] * inv_scale;
+        ss += a * a;
+        bad += isfinite(a) ? 0.0f : 1.0f;
+    }
+    __shared__ float red[2][ADAM_BLOCK / 32];
+    float s1 = warp_sum(ss), s2 = warp_sum(bad);
+    if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = s1; red[1][threadIdx.x >> 5] = s2; }
+    __syncthreads();
+    if (threadIdx.x < 2) {
+        double acc = 0.0;
+        for (int w = 0; w < ADAM_BLOCK / 32; ++w) acc += (double)red[threadIdx.x][w];
+        partials[2 * (int64_t)blockIdx.x + threadIdx.x] = acc;
+    }
+    // the last block to arrive turns the per-block sums into the step's scalars (in block order, as a
+    // separate one-block launch would) and clears the arrival counter for the next step
+    __shared__ bool last;
+    unsigned int* counter = reinterpret_cast<unsigned int*>(partials + 2 * (int64_t)gridDim.x);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    adam_finalize(gridDim.x, partials, controls, step, report);
+    if (threadIdx.x == 0) *counter = 0u;
+}
+
 
 __global__ void __launch_bounds__(ADAM_BLOCK) adam_apply_kernel(int64_t n, float* __restrict__ master,
                                                                  float* __restrict__ grad, float* __restrict__ first,
@@ -190,7 +206,8 @@ using namespace pbg;
 
 extern "C" {
 
-int64_t pbg_adam_partials_size(int64_t n) { return 2 * (int64_t)adam_grid(n > 0 ? n : 1); }
+// per-block sums of squares and non-finite counts, then the arrival counter of the last-block finalise
+int64_t pbg_adam_partials_size(int64_t n) { return 2 * (int64_t)adam_grid(n > 0 ? n : 1) + 1; }
 
 int pbg_adam_step(int64_t n, float* master, float* grad, float* first, float* second, const float* controls,
                   int64_t* step, int32_t decoupled, double* partials, double* report, void* stream) {
@@ -199,11 +216,8 @@ int pbg_adam_step(int64_t n, float* master, float* grad, float* first, float* se
     PBG_REQUIRE(((uintptr_t)grad % 16) == 0, "adam_step: grad must be 16-byte aligned");
     cudaStream_t s = as_stream(stream);
     int grid = adam_grid(n > 0 ? n : 1);
-    adam_norm_kernel<<<grid, ADAM_BLOCK, 0, s>>>(n, (const float4*)grad, grad, controls, partials);
+    adam_norm_kernel<<<grid, ADAM_BLOCK, 0, s>>>(n, (const float4*)grad, grad, controls, partials, step, report);
     int rc = launch_status("adam_norm");
-    if (rc) return rc;
-    adam_finalize_kernel<<<1, ADAM_BLOCK, 0, s>>>(grid, partials, controls, step, report);
-    rc = launch_status("adam_finalize");
     if (rc) return rc;
     const bool vec = (uintptr_t)master % 16 == 0 && (uintptr_t)first % 16 == 0 && (uintptr_t)second % 16 == 0;
     if (n > 0 && vec)

@@ -740,7 +740,8 @@ def readout_component(device, rows=4_194_304, hidden=128, reps=10):
 
 
 def optimizer_component(device, params=4_226_931, reps=10):
-    """The flat-buffer Adam step (pbg_b200.optim.FlatAdam, three launches: norm, finalise, apply) over the
+    """The flat-buffer Adam step (pbg_b200.optim.FlatAdam, two launches: norm with the finalise in its last
+    block, then apply) over the
     cfg2 architecture's 4,226,931 fp32 parameters (16,907,724 B, model_storage_bytes / 4).  Algorithmic
     bytes per parameter: 4 (gradient read by the norm pass) + 16 read + 16 written by the apply; each step
     queued behind a device-side sleep."""
@@ -767,7 +768,7 @@ def optimizer_component(device, params=4_226_931, reps=10):
                     "126 MB L2, so part of the traffic is L2 hits",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "bytes_per_param": 36, "peak_kind": kind},
-            "kernels": ["adam_norm_kernel", "adam_finalize_kernel", "adam_apply4_kernel"], "gpu_launches": 3}
+            "kernels": ["adam_norm_kernel", "adam_apply4_kernel"], "gpu_launches": 2}
 
 
 def showdown_component(device, hands=1_048_576, players=6, reps=10):

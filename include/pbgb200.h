@@ -303,7 +303,8 @@ int pbg_ppo_categorical_backward_noalloc(int64_t N, int32_t A, int32_t dtype, co
  * master/grad/moment set of n parameters.  controls (device fp32[10]):
  * lr, beta1, beta2, eps, decay, clip, scale, growth, backoff, interval;
  * decoupled selects AdamW.  step (device int64[1]) advances when applied.
- * partials: caller scratch of pbg_adam_partials_size(n) doubles.
+ * partials: caller scratch of pbg_adam_partials_size(n) doubles, zero before
+ * the first call (the last slot is an arrival counter the step leaves cleared).
  * report (device double[4]): applied, finite, norm, clip scale. */
 int64_t pbg_adam_partials_size(int64_t n);
 int pbg_adam_step(int64_t n, float *master, float *grad, float *first, float *second,
