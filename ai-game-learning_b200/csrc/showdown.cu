@@ -2,7 +2,8 @@
 // signature (called at pbg/games/poker/queued/hooks.py:2277-2295).
 //
 // The reference delegates ranking to the external poker_gpu_evaluator; this
-// kernel ranks 7-card hands directly from rank counts and suit masks.  The
+// kernel ranks 7-card hands directly from rank-multiplicity bit planes and suit
+// masks (the board's built once per hand, each seat adding its hole cards).  The
 // category order of each deck is the rarity-consistent order of
 // pbg/games/poker/cards.py:37-74 (category_profile): categories sorted by
 // their exact five-card counts, equal counts in conventional order.  Within
@@ -70,31 +71,38 @@ __device__ __forceinline__ int next_rank(unsigned mask, int& cursor) {
     return r;
 }
 
-__device__ int64_t hand_value7(const int* cards, const Strength& S, int R) {
-    int rc[13];
-    #pragma unroll
-    for (int r = 0; r < 13; ++r) rc[r] = 0;
-    unsigned suit[4] = {0, 0, 0, 0};
-    unsigned ranks = 0;
-    #pragma unroll
-    for (int i = 0; i < 7; ++i) {
-        int r = cards[i] >> 2, s = cards[i] & 3;
-        rc[r]++;
-        suit[s] |= 1u << r;
-        ranks |= 1u << r;
+// Rank multiplicities as bit planes (ranks held at least once / twice / three / four times) and
+// the four suits' rank masks packed 16 bits apart: a card is added with a few register ops, so the
+// board's planes are built once per hand and each seat only adds its two hole cards.
+struct HandCounts {
+    unsigned ge1 = 0, ge2 = 0, ge3 = 0, ge4 = 0;
+    uint64_t suits = 0;
+
+    __device__ __forceinline__ void add(int card) {
+        const unsigned m = 1u << (card >> 2);
+        ge4 |= ge3 & m;
+        ge3 |= ge2 & m;
+        ge2 |= ge1 & m;
+        ge1 |= m;
+        suits |= (uint64_t)m << (16 * (card & 3));
     }
-    unsigned ge2 = 0, ge3 = 0, ge4 = 0;
-    #pragma unroll
-    for (int r = 0; r < 13; ++r) {
-        if (rc[r] >= 2) ge2 |= 1u << r;
-        if (rc[r] >= 3) ge3 |= 1u << r;
-        if (rc[r] >= 4) ge4 |= 1u << r;
-    }
+};
+
+__device__ int64_t hand_value(const HandCounts& h, const Strength& S, int R) {
+    const unsigned ranks = h.ge1, ge2 = h.ge2, ge3 = h.ge3, ge4 = h.ge4;
     int64_t best = -1;
     int flush_suit = -1;
-    for (int s = 0; s < 4; ++s) if (__popc(suit[s]) >= 5) flush_suit = s;
+    unsigned flush_mask = 0;
+    #pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const unsigned m = (unsigned)(h.suits >> (16 * s)) & 0x1FFFu;
+        if (__popc(m) >= 5) {
+            flush_suit = s;
+            flush_mask = m;
+        }
+    }
     if (flush_suit >= 0 && S.s[STRAIGHT_FLUSH] >= 0) {
-        int top = top_straight(suit[flush_suit], R);
+        int top = top_straight(flush_mask, R);
         if (top >= 0) best = max(best, pack(S.s[STRAIGHT_FLUSH], top, 0, 0, 0, 0));
     }
     if (ge4) {
@@ -110,7 +118,7 @@ __device__ int64_t hand_value7(const int* cards, const Strength& S, int R) {
     }
     if (flush_suit >= 0 && S.s[FLUSH] >= 0) {
         int cur = 12;
-        unsigned m = suit[flush_suit];
+        unsigned m = flush_mask;
         int a = next_rank(m, cur), b = next_rank(m, cur), c = next_rank(m, cur), d = next_rank(m, cur), e = next_rank(m, cur);
         best = max(best, pack(S.s[FLUSH], a, b, c, d, e));
     }
@@ -149,44 +157,79 @@ __device__ int64_t hand_value7(const int* cards, const Strength& S, int R) {
     return best;
 }
 
+__device__ __forceinline__ int64_t hand_value7(const int* cards, const Strength& S, int R) {
+    HandCounts h;
+    #pragma unroll
+    for (int i = 0; i < 7; ++i) h.add(cards[i]);
+    return hand_value(h, S, R);
+}
+
 __global__ void showdown_kernel(Strength S, int R, int D, int first, int64_t B, int P, int strata,
                                 const uint8_t* board, const int32_t* combo, const int32_t* level,
                                 const float* baseline, const float* amount, float* out) {
+    // seat loops run over the MAXP slots with an early exit, so the per-seat values stay in registers
     for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
         int64_t value[MAXP];
         int lev[MAXP];
-        int cards[7];
+        HandCounts on_board;
         bool board_ok = true;
         #pragma unroll
         for (int i = 0; i < 5; ++i) {
-            cards[i] = board[b * 5 + i];
-            board_ok &= cards[i] >= first && cards[i] < 52;
+            const int c = board[b * 5 + i];
+            board_ok &= c >= first && c < 52;
+            if (board_ok) on_board.add(c);
         }
         const int H = D * (D - 1) / 2;
-        for (int p = 0; p < P; ++p) {
+        #pragma unroll
+        for (int p = 0; p < MAXP; ++p) {
+            if (p >= P) break;
             value[p] = -1;
             lev[p] = level[b * P + p];
             int id = combo[b * P + p];
             // seats without a valid private combo or board take no share
             if (board_ok && id >= 0 && id < H && lev[p] >= 0) {
-                combo_cards(D, first, id, cards[5], cards[6]);
-                value[p] = hand_value7(cards, S, R);
+                int c0, c1;
+                combo_cards(D, first, id, c0, c1);
+                HandCounts h = on_board;
+                h.add(c0);
+                h.add(c1);
+                value[p] = hand_value(h, S, R);
             }
         }
         float acc[MAXP];
-        for (int p = 0; p < P; ++p) acc[p] = baseline[b * P + p];
+        #pragma unroll
+        for (int p = 0; p < MAXP; ++p) {
+            if (p >= P) break;
+            acc[p] = baseline[b * P + p];
+        }
         for (int k = 0; k < strata; ++k) {
             float amt = amount[b * strata + k];
             if (!(amt > 0.0f)) continue;
             int64_t best = -1;
-            for (int p = 0; p < P; ++p) if (value[p] >= 0 && lev[p] >= k && value[p] > best) best = value[p];
+            #pragma unroll
+            for (int p = 0; p < MAXP; ++p) {
+                if (p >= P) break;
+                if (value[p] >= 0 && lev[p] >= k && value[p] > best) best = value[p];
+            }
             if (best < 0) continue;
             int winners = 0;
-            for (int p = 0; p < P; ++p) winners += value[p] == best && lev[p] >= k;
+            #pragma unroll
+            for (int p = 0; p < MAXP; ++p) {
+                if (p >= P) break;
+                winners += value[p] == best && lev[p] >= k;
+            }
             float share = __fdiv_rn(amt, (float)winners);
-            for (int p = 0; p < P; ++p) if (value[p] == best && lev[p] >= k) acc[p] = __fadd_rn(acc[p], share);
+            #pragma unroll
+            for (int p = 0; p < MAXP; ++p) {
+                if (p >= P) break;
+                if (value[p] == best && lev[p] >= k) acc[p] = __fadd_rn(acc[p], share);
+            }
         }
-        for (int p = 0; p < P; ++p) out[b * P + p] = acc[p];
+        #pragma unroll
+        for (int p = 0; p < MAXP; ++p) {
+            if (p >= P) break;
+            out[b * P + p] = acc[p];
+        }
     }
 }
 
