@@ -13,9 +13,12 @@
 //                            lane draws every seat's hand for its attempt
 //                            (POSTERIOR key at draw = attempt, lane = seat;
 //                            target = min(u*mass, nextafter(mass, 0)); the
-//                            first CDF entry strictly above it by an 11-step
-//                            bisection, the seats' bisections interleaved so
-//                            their loads overlap) and tests the seats' cards for a
+//                            first CDF entry strictly above it: the bucket
+//                            from a 32-entry coarse level per seat (loaded
+//                            once per row, searched by shuffles), then a
+//                            bisection of at most 6 steps inside it, the
+//                            seats interleaved so their loads overlap) and
+//                            tests the seats' cards for a
 //                            collision; a ballot picks the first accepted
 //                            attempt of the round, rounds of 32 run until one
 //                            succeeds or max_attempts is spent.
@@ -96,7 +99,7 @@ posterior_cdf_kernel(Geo g, int64_t parents, const float* __restrict__ weights,
     }
 }
 
-__global__ void __launch_bounds__(128, 8) posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const float* __restrict__ cdf,
+__global__ void __launch_bounds__(128, 6) posterior_sample_kernel(Geo g, uint64_t ns, int64_t rows, const float* __restrict__ cdf,
                                         const float* __restrict__ mass, const int32_t* __restrict__ inherited,
                                         const int64_t* __restrict__ source, const int64_t* __restrict__ ordinal,
                                         const uint8_t* __restrict__ active, const int64_t* __restrict__ root,
@@ -123,6 +126,16 @@ __global__ void __launch_bounds__(128, 8) posterior_sample_kernel(Geo g, uint64_
             const int64_t ep = epoch ? epoch[r] : epoch_scalar;
             int accepted = -1;
             int32_t mine[MAXP];
+            // coarse level of every seat's CDF, loaded once per row: lane j holds the last entry of
+            // bucket j (G entries per bucket, 32 buckets cover the H entries)
+            const int G = (H + 31) >> 5;
+            float coarse[MAXP];
+#pragma unroll
+            for (int p = 0; p < MAXP; ++p) {
+                if (p >= P) break;
+                const int idx = (lane + 1) * G - 1;
+                coarse[p] = cdf[(src * P + p) * (int64_t)H + (idx < H - 1 ? idx : H - 1)];
+            }
             for (int base = 0; base < max_attempts && accepted < 0; base += 32) {
                 const int a = base + lane;
                 bool ok = a < max_attempts;
@@ -139,17 +152,37 @@ __global__ void __launch_bounds__(128, 8) posterior_sample_kernel(Geo g, uint64_
                     lo[p] = 0;
                     hi[p] = H;
                 }
+                // first bucket whose last entry is above the target (a search over the lanes' coarse
+                // entries: 33 outcomes, 6 halvings; every lane takes part in every shuffle)
 #pragma unroll
-                for (int step = 0; step < 11; ++step) {
+                for (int p = 0; p < MAXP; ++p) {
+                    if (p >= P) break;
+                    int j0 = 0, j1 = 32;
+#pragma unroll
+                    for (int step = 0; step < 6; ++step) {
+                        const int mid = (j0 + j1) >> 1;
+                        const float v = __shfl_sync(0xffffffffu, coarse[p], mid & 31);
+                        if (j0 < j1) {
+                            if (mid < 32 && v <= target[p]) j0 = mid + 1;
+                            else j1 = mid;
+                        }
+                    }
+                    // the entry lies in bucket j0 (none above the target: H, clamped below)
+                    lo[p] = j0 < 32 ? j0 * G : H;
+                    hi[p] = j0 < 32 ? min(j0 * G + G, H) : H;
+                }
+                // bisection inside the bucket (at most 42 entries at 52 cards: 6 steps), seats interleaved
+#pragma unroll
+                for (int step = 0; step < 6; ++step) {
 #pragma unroll
                     for (int p = 0; p < MAXP; ++p) {
                         if (p >= P) break;
-                        const float* c = cdf + (src * P + p) * (int64_t)H;
-                        const int mid = (lo[p] + hi[p]) >> 1;
-                        const int safe = mid < H - 1 ? mid : H - 1;
-                        const bool below = mid < H && c[safe] <= target[p];
-                        lo[p] = below ? mid + 1 : lo[p];
-                        hi[p] = below ? hi[p] : mid;
+                        if (lo[p] < hi[p]) {
+                            const float* c = cdf + (src * P + p) * (int64_t)H;
+                            const int mid = (lo[p] + hi[p]) >> 1;
+                            if (c[mid] <= target[p]) lo[p] = mid + 1;
+                            else hi[p] = mid;
+                        }
                     }
                 }
                 uint64_t held = 0;  // cards of the seats drawn so far; a repeat is a collision
