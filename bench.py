@@ -1166,7 +1166,7 @@ def main():
                                                      " (loss kernel)" + (", NCCL eager" if world > 1 else ""))},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": committed_traffic(N),
-                     "kernel": "ppo_bf16x8_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,
+                     "kernel": "ppo_bf16x8_bulk_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,
                      "algorithmic_bytes": algo_bytes},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps,
