@@ -697,8 +697,8 @@ ppo_readout_kernel(int64_t N, const uint4* __restrict__ logits, const uint2* __r
     }
 }
 
-// Staged variant (every stream 16-byte aligned): each warp (12 per CTA, 6 at
-// d = 256) keeps its own ring of STAGES chunk stages in shared memory, filled by
+// Staged variant (every stream 16-byte aligned): each warp (12 per CTA; 16 at
+// d = 64, 6 at d = 256) keeps its own ring of two chunk stages in shared memory, filled by
 // plain 1D bulk copies (cp.async.bulk global -> shared, no tensor map, no
 // multicast) that its lane 0 issues STAGES chunks ahead, completing on the
 // stage's mbarrier.  A
@@ -716,8 +716,8 @@ struct RoBulk {
     static constexpr uint32_t HID = 32u * 2u * D;  // the chunk's hidden rows
     static constexpr uint32_t LOGITS = HID, MASK = HID + 512, ACT = MASK + 256, OLD = ACT + 128, ADV = OLD + 128,
                               WGT = ADV + 128, BYTES = WGT + 128;  // every offset a multiple of 16
-    static constexpr int STAGES = DC == 2 ? 3 : 2;
-    static constexpr int WARPS = DC == 8 ? 6 : 12;
+    static constexpr int STAGES = 2;
+    static constexpr int WARPS = DC == 8 ? 6 : (DC == 2 ? 16 : 12);
     static constexpr int THREADS = 32 * WARPS;
     static constexpr size_t SMEM = (size_t)WARPS * STAGES * BYTES;
 };
