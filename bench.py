@@ -13,7 +13,8 @@ symmetric memory; NCCL when the fabric has no multicast).  Weak scaling: each
 rank owns its own rows.
 
 ``--impl reference`` times the CPU restatement of the same loss (the
-reference has no CPU path) on all host threads.
+reference has no CPU path, and its GPU path does not travel to the benchmark
+box) on all host threads.
 """
 
 from __future__ import annotations
