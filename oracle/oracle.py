@@ -503,6 +503,17 @@ def ppo_categorical(logits, mask, action, old_logp, adv, weight, *, clip=0.2, lo
     return d, sums
 
 
+def ppo_readout(logits, mask, action, old_logp, adv, weight, hidden, **loss_options):
+    """The loss gradient above carried through the readout that produced the logits, x = h W^T + b
+    (pbg/core/tensor_ops.py:25-38): dW = dlogits^T h and db = sum_r dlogits in float64.
+    Returns (dlogits, dW [A, d], db [A], sums)."""
+
+    d, sums = ppo_categorical(logits, mask, action, old_logp, adv, weight, **loss_options)
+    d64 = d.astype(np.float64)
+    h64 = np.ascontiguousarray(hidden, dtype=np.float64)
+    return d, d64.T @ h64, d64.sum(0), sums
+
+
 def adam(master, grad, first, second, controls, step, decoupled=True):
     """optimization.py:182-233 (adam_transition) for one lane, in place."""
 

@@ -80,6 +80,29 @@ def test_readout_backward_unaligned_row_streams(d):
     _check_readout(dl, hidden, dweight, dbias)
 
 
+def test_readout_backward_matches_the_oracle():
+    """Against the CPU restatement (double precision, from the un-rounded gradient): the kernel sums the
+    bf16 dlogits it writes, so the bar is the bf16 one, 2e-2 of the sum of the terms' magnitudes."""
+
+    import math
+
+    import oracle as O
+    from pbg_b200.loss import FusedPPOReadoutBackward, LossConfig
+
+    N, d = 5000, 128
+    logits, mask, action, old, adv, weight, hidden = _inputs(N, d, 21)
+    dl, dweight, dbias, stats = FusedPPOReadoutBackward(N, d, DEV, LossConfig(0.2, 1.5, 0.01))(
+        logits, mask, action, old, adv, weight, hidden)
+    torch.cuda.synchronize()
+    host = lambda t: t.detach().cpu().numpy()  # noqa: E731
+    ref_d, ref_w, ref_b, ref_s = O.ppo_readout(host(logits.float()), host(mask), host(action), host(old), host(adv),
+                                               host(weight), host(hidden.float()), log_cap=math.log(1.5))
+    mag_w = np.abs(ref_d).astype(np.float64).T @ np.abs(host(hidden.float())).astype(np.float64)
+    assert np.all(np.abs(host(dweight) - ref_w) <= 2e-2 * mag_w + 1e-30)
+    assert np.all(np.abs(host(dbias) - ref_b) <= 2e-2 * np.abs(ref_d).sum(0) + 1e-30)
+    np.testing.assert_allclose(host(stats)[[0, 6, 7]], ref_s[[0, 6, 7]], rtol=1e-4, atol=1e-9 * N)
+
+
 def test_readout_backward_empty_batch_and_bad_arguments():
     from pbg_b200._native import lib, ptr
     from pbg_b200.loss import FusedPPOReadoutBackward
