@@ -73,6 +73,7 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
                   const uint8_t* __restrict__ tight_mask, const float* __restrict__ base_cards,
                   float* __restrict__ phi_out, float* __restrict__ triple_out) {
     extern __shared__ float4 fd_smem4[];
+    __shared__ float fd_zero[FD_CPAD];  // the delta row of a slot that is not tight
     float* prob = reinterpret_cast<float*>(fd_smem4);                   // [P][H]
     float* marg = prob + players * hands;                                // [P][CPAD]
     uint16_t* comb = reinterpret_cast<uint16_t*>(marg + players * FD_CPAD);  // [H]: lo | hi << 8
@@ -102,6 +103,7 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
     }
     const float* src = probability + row * (int64_t)players * hands;
     for (int i = threadIdx.x; i < players * hands; i += FD_THREADS) prob[i] = src[i];
+    if (threadIdx.x < FD_CPAD) fd_zero[threadIdx.x] = 0.0f;
     for (int h = threadIdx.x; h < hands; h += FD_THREADS) {
         int lo = 0;
         while (fd_hand(lo + 1, lo + 2, cards) <= h && lo + 2 < cards) ++lo;
@@ -198,6 +200,16 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
             float ident[6], tri[6][2];
 #pragma unroll
             for (int i = 0; i < 6; ++i) ident[i] = tri[i][0] = tri[i][1] = 0.0f;
+            // per slot: its seat's probability row, and its delta row or the zero row when the slot is not
+            // tight (the loop then needs no selects).  Slots past the folder count read seat 0's row: the
+            // sums they feed are never used.
+            const float* prow[FD_DENSE];
+            const float* drow[FD_DENSE];
+#pragma unroll
+            for (int i = 0; i < FD_DENSE; ++i) {
+                prow[i] = prob + fseat[i] * hands;
+                drow[i] = (dtight >> i & 1u) ? delta + fseat[i] * FD_CPAD : fd_zero;
+            }
             for (int h = lane; h < hands; h += 32) {
                 const uint16_t pr = comb[h];
                 const int c1 = pr & 0xff, c2 = pr >> 8;
@@ -205,9 +217,9 @@ folded_phi_kernel(int players, int cards, int hands, int queries, int queries_pe
                 float ph[FD_DENSE], d1[FD_DENSE], d2[FD_DENSE];
 #pragma unroll
                 for (int i = 0; i < FD_DENSE; ++i) {
-                    ph[i] = i < folders ? prob[fseat[i] * hands + h] : 0.0f;
-                    d1[i] = (dtight >> i & 1u) ? delta[fseat[i] * FD_CPAD + c1] : 0.0f;
-                    d2[i] = (dtight >> i & 1u) ? delta[fseat[i] * FD_CPAD + c2] : 0.0f;
+                    ph[i] = prow[i][h];
+                    d1[i] = drow[i][c1];
+                    d2[i] = drow[i][c2];
                 }
 #pragma unroll
                 for (int s = 0; s < 6; ++s) {
