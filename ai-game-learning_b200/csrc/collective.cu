@@ -16,7 +16,10 @@
 // use disjoint slot ranges, which is enough for back-to-back calls: a peer can
 // only signal a slot again after this rank has cleared it (the intervening
 // barrier orders it).  Every wait is bounded; a wait that runs out sets
-// *error and the kernel returns without touching the buffer further.
+// *error and the kernel returns without touching the buffer further.  The
+// error word is sticky: a launch that finds it set returns at entry, before
+// signalling anyone, so slots left stale by a timed-out barrier are never
+// read by a later call (clear the pads and the word together to reuse them).
 #include "pbg_common.cuh"
 
 namespace pbg {
@@ -83,6 +86,7 @@ __device__ __forceinline__ void multimem_st(float* addr, const float4& v) {
 
 __global__ void __launch_bounds__(NVLS_THREADS) nvls_sum_kernel(int64_t n, float* mc, uint32_t* const* pads, int rank,
                                                                 int world, uint32_t* error) {
+    if (*reinterpret_cast<volatile uint32_t*>(error) != 0u) return;  // an earlier call failed: stay off
     if (!rank_barrier(pads, rank, world, 0, error)) return;
     const int64_t slice = n / world;  // multiple of 4 floats by contract
     const int64_t v0 = (int64_t)rank * slice / 4, vn = slice / 4;

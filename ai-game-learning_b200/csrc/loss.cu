@@ -1144,6 +1144,13 @@ extern "C" int pbg_ppo_categorical_backward_noalloc(int64_t N, int32_t A, int32_
                                                     const float* old_logp, const float* adv, const float* weight,
                                                     const float* controls, void* dlogits, double* stats,
                                                     void* stream) {
+    // Reject bad arguments before anything touches the shared array: a refused call must not
+    // queue a write that could race with another caller's launch.
+    PBG_REQUIRE(N >= 0 && A >= 1 && A <= LOSS_MAX_A, "ppo_noalloc: need N >= 0 and A in [1,32]");
+    PBG_REQUIRE(dtype == 0 || dtype == 1, "ppo_noalloc: dtype must be 0 (fp32) or 1 (bf16)");
+    PBG_REQUIRE(controls && stats, "ppo_noalloc: null controls or statistics");
+    PBG_REQUIRE(N == 0 || (logits && mask && action && old_logp && adv && weight && dlogits),
+                "ppo_noalloc: null argument");
     int grid = ppo_grid(N > 0 ? N : 1);
     if (grid > NOALLOC_MAX_BLOCKS) {
         set_error("ppo_noalloc: this launch needs statistics for %d blocks; the built-in scratch holds %d "

@@ -257,7 +257,9 @@ int pbg_posterior_sample_children(pbg_geometry geometry, int64_t parents, const 
     if (rc) return rc;
     const Geo g = derive(geometry);
     PBG_REQUIRE(parents >= 1 && rows >= 0 && max_attempts >= 1, "posterior: bad sizes");
-    PBG_REQUIRE(g.H <= 2047, "posterior: the 11-step search covers at most 2047 private hands");
+    // The hand search is a 32-entry coarse level (buckets of G = ceil(H / 32) hands) followed by at
+    // most 6 bisection steps inside one bucket, which covers buckets of up to 63 hands: H <= 2016.
+    PBG_REQUIRE(g.H <= 2016, "posterior: the coarse level plus 6 bisection steps covers at most 2016 private hands");
     PBG_REQUIRE(range_weights && board && inherited && workspace && min_failing && status,
                 "posterior: null pointer");
     PBG_REQUIRE(rows == 0 || (source && ordinal && active && root && path && profile && attempt_count && exhausted),

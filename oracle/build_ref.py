@@ -2,6 +2,10 @@
 
     python oracle/build_ref.py [--reference <pbg checkout>] [--force]
 
+The checkout is the ``--reference`` argument, else ``$PBG_REFERENCE``, else a
+directory named ``reference`` beside this repository; with none of them
+present nothing is built.
+
 The reference's native operators are single CUDA source files, each a torch
 extension with one entry point: pbg/core/csrc/layered_targets.cu
 (``run_layers``), alias_table.cu (``build_alias_table``) and
@@ -31,7 +35,8 @@ MODULES = {
     "ref_branching_metadata": os.path.join("pbg", "core", "csrc", "branching_metadata.cu"),
 }
 MODULE = "ref_layered_targets"
-DEFAULT_REFERENCE = os.environ.get("PBG_REFERENCE", "/root/reference")
+DEFAULT_REFERENCE = os.environ.get(
+    "PBG_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def target(module: str = MODULE) -> str:
