@@ -974,8 +974,203 @@ def gen_queued_model(out):
     out["config"] = np.array([cfg.max_history_tokens, cfg.max_players])
 
 
+def _poker_masks(gi, E):
+    with np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "poker.npz")) as data:
+        packed = data[f"g{gi}_masks"]
+    masks = np.unpackbits(packed, axis=-1)[..., :E].astype(bool).reshape(-1, E)
+    return masks[masks.any(1)]
+
+
+# (name, mask source, E, M, sigma rows, columns (1 = sampled, H = Rao-Blackwell), lanes, branched, reference raw)
+POKER_LOSS_CASES = (
+    ("s202", 3, 202, 2, 32, 1, 2, False, True),
+    ("s10", None, 10, 3, 16, 1, 1, False, False),
+    ("rb18", 0, 18, 2, 6, 120, 2, False, True),
+    ("br102", 5, 102, 2, 10, 1, 2, True, True),
+    ("brrb18", 0, 18, 2, 4, 120, 1, True, False),
+)
+
+
+def gen_poker_loss(out):
+    """The poker learner objective and its gradient from the reference's own loss program.
+
+    ``LearnerOperation.forward_loss`` (pbg/core/learner.py:1824-2159) with the
+    reference's composite policy (``PokerPolicyOperator.learner``,
+    pbg/games/poker/queued/policy.py:284-298) as the policy operation, given a
+    model evaluation whose raw fields, value and public heads are leaf tensors;
+    ``(total * lane_weight).sum().backward()`` (pbg/core/training.py:403 with
+    the objective weight times the loss scale per lane) gives the gradients.
+    Cases cover sampled and Rao-Blackwell private estimators, sequential and
+    branched (ragged action spans with trace/cost heads) batches, one and two
+    lanes with different controls, the clipped and MSE value objectives, the
+    negative-advantage log cap, the reference-KL term, and one row whose
+    mixture has no fp32 mass on its legal ticks (the uniform fallback).
+    """
+
+    import torch
+    from pbg.core.contracts import mode_schema
+    from pbg.core.learner import (BranchedLearnerBatch, BranchingLossConfig, LearnerOperation, LossConfig,
+                                  ModelEvaluation, SequentialLearnerBatch)
+    from pbg.games.poker.queued.policy import PokerLegality, PokerPolicyOperator
+
+    BranchedLearnerBatch.__post_init__ = lambda self: None  # learner.py:1127-1150 without the device test
+    rng = np.random.default_rng(2024)
+    op = PokerPolicyOperator()
+    out["cases"] = np.array([c[0] for c in POKER_LOSS_CASES])
+    for name, gi, E, M, S, W, lanes, branched, with_ref in POKER_LOSS_CASES:
+        if gi is None:
+            mask = rng.random((S, E)) < 0.6
+            mask[:, 1] = True
+            mask[1] = False
+            mask[1, 1] = True
+        else:
+            pool = _poker_masks(gi, E)
+            mask = pool[rng.choice(pool.shape[0], S, replace=pool.shape[0] < S)]
+        g = torch.Generator().manual_seed(int(rng.integers(0, 2**31)))
+        raw = _raw(rng, S, W, M)
+        if gi is None:
+            # every component far below the legal ticks with a narrow scale: the tick products
+            # underflow to zero in fp32, so the raise law is the uniform fallback
+            raw["mu"][2] = 0.0
+            raw["s"][2] = 0.005
+            mask[2] = False
+            mask[2, [1, E - 2, E - 1]] = True
+        ref_raw = None
+        if with_ref:
+            ref_raw = {k: v.clone() for k, v in raw.items()}
+            ref_raw["type_logits"] = ref_raw["type_logits"] + 0.3 * torch.randn(S, W, 3, generator=g)
+            ref_raw["mu"] = (ref_raw["mu"] + 0.1 * torch.randn(S, W, M, generator=g)).clamp(0.0, 1.0)
+            ref_raw["iota"] = (ref_raw["iota"] * 0.8).clamp(0.0, 1.0)
+        counts = rng.integers(1, 4, S) if branched else np.ones(S, np.int64)
+        if branched and lanes > 1:
+            # equal action rows per lane
+            half = S // lanes
+            counts[half:] = counts[:half][::-1]
+        A_rows = int(counts.sum())
+        ptr = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+        a2s = np.repeat(np.arange(S), counts)
+        action = np.array([rng.choice(np.nonzero(mask[s])[0]) for s in a2s], dtype=np.int32)
+        legality_sigma = PokerLegality(torch.arange(E, dtype=torch.int32)[None].expand(S, -1).contiguous(),
+                                       torch.from_numpy(mask))
+        with torch.no_grad():
+            p = op.probabilities(raw, legality_sigma)  # [S, W, E]
+            cur = torch.log(p[torch.from_numpy(a2s), :, torch.from_numpy(action).long()].clamp_min(1e-12))
+        old = (cur + 0.3 * torch.randn(A_rows, W, generator=g)).float()
+        far = rng.random(A_rows) < 0.3
+        old[torch.from_numpy(far)] += 1.5 * torch.randn(int(far.sum()), W, generator=g)
+        adv = torch.randn(A_rows, W, generator=g)
+        if W > 1:
+            post = torch.rand(A_rows, W, generator=g) * (torch.rand(A_rows, W, generator=g) > 0.3)
+        else:
+            post = torch.ones(A_rows, 1)
+        value = torch.randn(S, W, generator=g)
+        old_value = value + 0.3 * torch.randn(S, W, generator=g)
+        target = torch.randn(S, W, generator=g)
+        controls = torch.tensor([
+            [0.2, math.log(1.5), 0.5, 0.2, 0.01, 0.05 if with_ref else 0.0, 0.3 if branched else 0.0,
+             0.2 if branched else 0.0, 1.0e-8 if not branched else 1.0e-3, 1.0],
+            [0.25, math.inf, 0.7, 0.0, 0.02, 0.1 if with_ref else 0.0, 0.1 if branched else 0.0,
+             0.4 if branched else 0.0, 1.0e-8 if not branched else 1.0e-2, 0.0],
+        ], dtype=torch.float32)[:lanes]
+        lane_weight = torch.tensor([1.6, 0.5], dtype=torch.float32)[:lanes]
+
+        leaves = {k: v.detach().clone().requires_grad_() for k, v in raw.items()}
+        value_leaf = value.detach().clone().requires_grad_()
+        heads = {}
+        sigma = {"model_input": torch.arange(S, dtype=torch.float32)[:, None],
+                 "owner": torch.zeros(S, dtype=torch.int32), "old_value": old_value, "value_target": target}
+        if W == 1:
+            sigma["sampled_private_state"] = torch.zeros(S, 2, dtype=torch.int32)
+        if branched:
+            sigma["target_degree"] = torch.from_numpy(counts.astype(np.int32))
+            trace_pred = (torch.rand(S, generator=g) * 2 + 0.05).requires_grad_()
+            cost_pred = (torch.rand(S, generator=g) * 2 + 0.05).requires_grad_()
+            heads = {"trace": trace_pred, "cost": cost_pred}
+            sigma["trace_target"] = torch.rand(S, generator=g) * 2
+            sigma["cost_target"] = torch.rand(S, generator=g) * 2 + 0.01
+        action_fields = {"action": torch.from_numpy(action), "old_log_policy": old, "advantage_target": adv,
+                         "posterior": post}
+        if branched:
+            batch = BranchedLearnerBatch("post", torch.arange(S), torch.from_numpy(ptr), torch.arange(A_rows),
+                                         MappingProxyType(sigma), MappingProxyType(action_fields))
+        else:
+            fields = dict(sigma)
+            fields.update(action_fields)
+            batch = SequentialLearnerBatch("post", torch.arange(S), MappingProxyType(fields))
+
+        def policy(input_type, model_input, raw_rows, act, private, owner, reference):
+            rows = model_input[:, 0].long()
+            legality = PokerLegality(torch.arange(E, dtype=torch.int32)[None].expand(rows.numel(), -1).contiguous(),
+                                     torch.from_numpy(mask)[rows])
+            return op.learner(raw_rows, legality, act, private, owner, reference)
+
+        cfg = LossConfig(branching=BranchingLossConfig(0.3, 0.2, 1.0e-3) if branched else None)
+        estimator = "sampled" if W == 1 else "rao_blackwell"
+        rollout = "branched.fixed" if branched else "sequential"
+        learner = LearnerOperation(mode_schema("self_play", rollout, estimator), cfg, None, policy)
+        evaluation = ModelEvaluation(leaves, value_leaf, MappingProxyType(heads))
+        res = learner.forward_loss(batch, iteration=0, lane_count=lanes, loss_controls=controls,
+                                   evaluation=evaluation, reference_raw=ref_raw)
+        (res.total * lane_weight).sum().backward()
+        pre = f"pl_{name}_"
+        for k, v in raw.items():
+            out[pre + k] = _np(v)
+            out[pre + "grad_" + k] = _np(leaves[k].grad)
+            if ref_raw is not None:
+                out[pre + "ref_" + k] = _np(ref_raw[k])
+        out[pre + "mask"] = mask.astype(np.uint8)
+        out[pre + "action_ptr"] = ptr
+        out[pre + "action"] = action
+        out[pre + "old"] = _np(old)
+        out[pre + "adv"] = _np(adv)
+        out[pre + "post"] = _np(post)
+        out[pre + "value"] = _np(value)
+        out[pre + "old_value"] = _np(old_value)
+        out[pre + "target"] = _np(target)
+        out[pre + "grad_value"] = _np(value_leaf.grad)
+        out[pre + "controls"] = _np(controls)
+        out[pre + "lane_weight"] = _np(lane_weight)
+        out[pre + "meta"] = np.array([E, M, S, W, lanes, A_rows, int(branched), int(with_ref)], np.int64)
+        if branched:
+            for k in ("trace_target", "cost_target"):
+                out[pre + k] = _np(sigma[k])
+            out[pre + "trace_pred"] = _np(trace_pred)
+            out[pre + "cost_pred"] = _np(cost_pred)
+            out[pre + "grad_trace_pred"] = _np(trace_pred.grad)
+            out[pre + "grad_cost_pred"] = _np(cost_pred.grad)
+        out[pre + "result"] = np.stack([_np(getattr(res, f)) for f in res.__dataclass_fields__], 1)
+
+    # PokerPolicyOperator.learner itself (policy.py:284-298) with autograd: selected log pi, entropy and
+    # reference KL of [B, rows] policy rows and the raw-field gradients of a weighted sum of the three.
+    for name, gi, E, M, B, rows in (("pl202", 3, 202, 2, 12, 3), ("pl18", 0, 18, 3, 10, 5)):
+        pool = _poker_masks(gi, E)
+        mask = pool[rng.choice(pool.shape[0], B, replace=False)]
+        raw = _raw(rng, B, rows, M)
+        ref_raw = {k: v.clone() for k, v in raw.items()}
+        ref_raw["type_logits"] = ref_raw["type_logits"] + 0.5
+        ref_raw["mu"] = (ref_raw["mu"] * 0.7).clamp(0.0, 1.0)
+        leaves = {k: v.detach().clone().requires_grad_() for k, v in raw.items()}
+        action = np.array([rng.choice(np.nonzero(m)[0]) for m in mask], dtype=np.int32)
+        legality = PokerLegality(torch.arange(E, dtype=torch.int32)[None].expand(B, -1).contiguous(),
+                                 torch.from_numpy(mask))
+        ev = op.learner(leaves, legality, torch.from_numpy(action), None, None, ref_raw)
+        weights = [torch.randn(B, rows, generator=torch.Generator().manual_seed(7 + i)) for i in range(3)]
+        (ev.selected_log_policy * weights[0] + ev.entropy * weights[1] + ev.reference_kl * weights[2]).sum().backward()
+        pre = f"plr_{name}_"
+        out[pre + "mask"] = mask.astype(np.uint8)
+        out[pre + "action"] = action
+        for k in raw:
+            out[pre + k] = _np(raw[k])
+            out[pre + "ref_" + k] = _np(ref_raw[k])
+            out[pre + "grad_" + k] = _np(leaves[k].grad)
+        out[pre + "selected"] = _np(ev.selected_log_policy)
+        out[pre + "entropy"] = _np(ev.entropy)
+        out[pre + "kl"] = _np(ev.reference_kl)
+        out[pre + "weights"] = np.stack([_np(w) for w in weights])
+
+
 GENERATORS = {"posterior": gen_posterior, "preflop_model": gen_preflop_model, "postflop_model": gen_postflop_model,
-              "folded": gen_folded, "queued_model": gen_queued_model}
+              "folded": gen_folded, "queued_model": gen_queued_model, "poker_loss": gen_poker_loss}
 
 
 def main() -> None:
