@@ -66,7 +66,11 @@ class TargetChildren(ctypes.Structure):
     _fields_ = [(n, _P) for n in ("source_row", "source_type", "path", "multiplier")]
 
 
-G, S, Hs, L, Pol = Geometry, State, History, Leaf, Policy
+class PolicyGrad(ctypes.Structure):
+    _fields_ = [(n, _P) for n in ("type_logits", "omega", "mu", "scale", "iota")]
+
+
+G, S, Hs, L, Pol, PolG = Geometry, State, History, Leaf, Policy, PolicyGrad
 
 SIGNATURES: dict[str, tuple] = {
     "pbg_last_error": (ctypes.c_char_p, []),
@@ -94,6 +98,11 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_policy_selected_log_pi": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P]),
     "pbg_policy_entropy": (_I32, [_I64, _I32, Pol, _P, _P, _P]),
     "pbg_policy_sample_actor": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P, _P, _P]),
+    "pbg_learner_workspace_bytes": (_I64, [_I64, _I64, _I32]),
+    "pbg_poker_learner_objective": (_I32, [_I64, _I64, _I32, _I32, _I32, Pol, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                           _P, _P, _P, _P, _P, _P, _P, PolG, _P, _P, _P, _P, _P, _I64, _P]),
+    "pbg_policy_learner_forward": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_policy_learner_backward": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P, _P, _P, PolG, _P]),
     "pbg_rollout_step": (_I32, [G, _I64, S, Hs, _P, _P, _P, _I64, _I64, Pol, _P, _P, _P, _P, L, _P]),
     "pbg_reach_update": (_I32, [G, _I64, S, Pol, _P, _P, _P, _P]),
     "pbg_ppo_partials_size": (_I64, [_I64, _I32]),

@@ -2,7 +2,8 @@
 
 ``PokerPolicyOperator`` keeps the reference's entry points (probabilities,
 selected_log_pi, policy_reductions, sample_actor, learner); each runs one
-warp per policy row in libpbgb200.
+warp per policy row in libpbgb200.  ``learner`` and ``policy_reductions`` are
+differentiable in the raw fields, as the reference's autograd path is.
 """
 
 from __future__ import annotations
@@ -15,6 +16,7 @@ from torch import Tensor
 
 from . import _native as N
 from ._native import call, ptr, stream
+from .learner import policy_learner
 from .poker import CHECK_CALL, FOLD, RAISE_OFFSET, PokerLegality
 
 _FIELDS = ("type_logits", "omega", "mu", "s", "iota")
@@ -89,18 +91,11 @@ class PokerPolicyOperator:
 
     def policy_reductions(self, raw: Mapping[str, Tensor], legality: PokerLegality,
                           reference_raw: Mapping[str, Tensor] | None = None) -> tuple[Tensor, Tensor]:
-        pol, keep, rows = policy_struct(raw)
+        """policy.py:235-244; differentiable in ``raw`` (pbg_policy_learner_forward / _backward)."""
+
         mask = self._mask(legality)
-        B, E = mask.shape
-        entropy = torch.empty(B * rows, dtype=torch.float32, device=mask.device)
-        call("pbg_policy_entropy", B, E, pol, ptr(mask), ptr(entropy), stream(mask.device))
-        entropy = entropy.reshape(raw["type_logits"].shape[:-1])
-        if reference_raw is None:
-            return entropy, torch.zeros_like(entropy)
-        p = self.probabilities(raw, legality)
-        q = self.probabilities(reference_raw, legality)
-        logp = torch.log(p.clamp_min(self.epsilon))
-        kl = (p * (logp - torch.log(q.clamp_min(self.epsilon)))).sum(-1)
+        action = torch.ones(mask.shape[0], dtype=torch.int32, device=mask.device)  # check/call: always legal
+        _, entropy, kl = policy_learner(raw, mask, action, reference_raw)
         return entropy, kl
 
     def sample_actor(self, raw: Mapping[str, Tensor], legality: PokerLegality, actor_hand: Tensor,
@@ -118,10 +113,14 @@ class PokerPolicyOperator:
         return ActorSample(action, selected)
 
     def learner(self, raw, legality, action, sampled_private_state, owner, reference_raw) -> PolicyEvaluation:
+        """policy.py:284-298: selected log pi, entropy and reference KL in one pass per policy row,
+        differentiable in ``raw`` through libpbgb200's vector-Jacobian product."""
+
         del sampled_private_state, owner
-        selected = self.selected_log_pi(raw, legality, action)
-        entropy, kl = self.policy_reductions(raw, legality, reference_raw)
-        return PolicyEvaluation(selected, entropy, kl)
+        mask = self._mask(legality)
+        if action.shape != (mask.shape[0],):
+            raise PokerPolicyError("selected action must have shape [B]")
+        return PolicyEvaluation(*policy_learner(raw, mask, action, reference_raw))
 
 
 __all__ = ["CHECK_CALL", "FOLD", "RAISE_OFFSET", "ActorSample", "PokerLegality", "PokerPolicyError",

@@ -91,6 +91,15 @@ typedef struct {
     int32_t mixtures;         /* M in [1,8] */
 } pbg_policy;
 
+/* Gradients of the raw composite-policy fields, same layout as pbg_policy. */
+typedef struct {
+    float *type_logits; /* [B,rows,3] */
+    float *omega;       /* [B,rows,M] */
+    float *mu;          /* [B,rows,M] */
+    float *scale;       /* [B,rows,M] */
+    float *iota;        /* [B,rows] */
+} pbg_policy_grad;
+
 const char *pbg_last_error(void);
 int32_t pbg_abi_version(void);
 
@@ -208,6 +217,68 @@ int pbg_policy_entropy(int64_t B, int32_t E, pbg_policy pol, const uint8_t *mask
 int pbg_policy_sample_actor(int64_t B, int32_t E, pbg_policy pol, const uint8_t *mask,
                             const int32_t *hand, const int64_t *keys, int32_t *action,
                             float *selected_log, void *stream);
+
+/* PokerPolicyOperator.learner forward (pbg/games/poker/queued/policy.py:284-298):
+ * per policy row [B*rows] the selected log pi of action[b] (clamped at
+ * 1e-12), the entropy and KL(p || q) against reference fields of the same
+ * layout (kl = 0 when reference is NULL). */
+int pbg_policy_learner_forward(int64_t B, int32_t E, pbg_policy raw, const pbg_policy *reference,
+                               const uint8_t *mask, const int32_t *action, float *selected,
+                               float *entropy, float *kl, void *stream);
+
+/* Vector-Jacobian product of PokerPolicyOperator.learner
+ * (pbg/games/poker/queued/policy.py:284-298, the reference's autograd
+ * backward through its composite policy): upstream gradients of the
+ * selected log pi, entropy and reference KL [B*rows] (each may be NULL) ->
+ * gradients of the raw fields [B, rows, ...].  The reference fields enter
+ * the KL only (no gradient flows to them). */
+int pbg_policy_learner_backward(int64_t B, int32_t E, pbg_policy raw, const pbg_policy *reference,
+                                const uint8_t *mask, const int32_t *action,
+                                const float *g_selected, const float *g_entropy,
+                                const float *g_kl, pbg_policy_grad grad, void *stream);
+
+/* ------------------------------------------------- poker learner objective */
+
+/* Workspace bytes pbg_poker_learner_objective needs for S sigma rows, A
+ * action rows and `lanes` replica lanes (-1 for invalid sizes).  Zero the
+ * workspace once before its first use; every launch leaves it ready for the
+ * next. */
+int64_t pbg_learner_workspace_bytes(int64_t S, int64_t A, int32_t lanes);
+
+/* The poker learner objective of one physical batch and its gradient, one
+ * pass: LearnerOperation.forward_loss (pbg/core/learner.py:1824-2159) with the
+ * poker policy operation (pbg/games/poker/queued/policy.py:113-298 through
+ * hooks.py:2200-2246 PokerLearnerPolicy), then the backward of
+ * (total * lane_weight).sum() (pbg/core/training.py:403, lane_weight =
+ * objective weight x loss scale).  Replaces the autograd program the
+ * reference's learner runs between the model forward and the weight-gradient
+ * GEMMs.
+ *   raw        current raw fields [S, W, ...] (W = 1 sampled row, W = H
+ *              Rao-Blackwell hands); reference: same layout or NULL (no KL)
+ *   mask       [S, E] legal events of each sigma row (canonical ids 0..E-1)
+ *   action_ptr [S+1] ragged action spans (NULL: unit spans, A == S)
+ *   action [A]; old_log, advantage, posterior [A, W] (posterior NULL = 1
+ *              for W == 1); value, old_value, value_target [S, W]
+ *   trace/cost pred+target [S] (branched public heads) or all NULL
+ *   controls [lanes, 10] (learner.py:2162-2175 order); lane_weight [lanes]
+ * Writes grad (same layout as raw), d_value [S, W], d_trace / d_cost [S]
+ * and result [lanes, 10] in LossResult order (total, policy, value,
+ * entropy, reference_kl, approximate_kl, clip_fraction,
+ * negative_advantage_cap_fraction, negative_advantage_log_ratio_max,
+ * negative_advantage_influence_max).  Action spans must not cross lane
+ * boundaries (S/lanes sigma rows and A/lanes action rows per lane). */
+int pbg_poker_learner_objective(int64_t S, int64_t A, int32_t E, int32_t W, int32_t lanes,
+                                pbg_policy raw, const pbg_policy *reference,
+                                const uint8_t *mask, const int64_t *action_ptr,
+                                const int32_t *action, const float *old_log,
+                                const float *advantage, const float *posterior,
+                                const float *value, const float *old_value,
+                                const float *value_target, const float *trace_pred,
+                                const float *cost_pred, const float *trace_target,
+                                const float *cost_target, const float *controls,
+                                const float *lane_weight, pbg_policy_grad grad,
+                                float *d_value, float *d_trace, float *d_cost, float *result,
+                                void *workspace, int64_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------ fused rollout */
 
