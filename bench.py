@@ -12,9 +12,12 @@ gradient buffer of --params parameters (libpbgb200's NVLS multimem kernel on
 symmetric memory; NCCL when the fabric has no multicast).  Weak scaling: each
 rank owns its own rows.
 
-``--impl reference`` times the CPU restatement of the same loss (the
-reference has no CPU path, and its GPU path does not travel to the benchmark
-box) on all host threads.
+``--impl reference`` times the CPU restatement of the same loss on the same
+rows (the reference has no CPU execution path) on all host threads.  The
+reference's own PyTorch CUDA loss program, when the driver installed it under
+baseline/_ref, is timed inside the b200 arm on the same box and reported as
+``reference_torch_cuda`` (the comparator the north star names), with the
+speed-up of ``value`` and of ``e2e`` over it.
 """
 
 from __future__ import annotations
@@ -22,6 +25,7 @@ from __future__ import annotations
 import argparse
 import concurrent.futures as cf
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -231,7 +235,7 @@ def reference_arm(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    sample = host_sample(min(args.rows, 1 << 21), args.actions, 0)
+    sample = host_sample(args.rows, args.actions, 0)
     for _ in range(args.warmup):
         cpu_loss_rate(sample, seconds=0.0)
     rates = []
@@ -247,13 +251,229 @@ def reference_arm(args):
         "ms_per_step": 1000.0 * elapsed / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic",
-        "config": {"workload": "cfg5 loss microbench, CPU restatement (oracle port)", "rows_per_step": sample[0].shape[0],
-                   "actions": args.actions},
+        "config": {"workload": "cfg5 loss microbench: 4,194,304 decisions x 8 actions per step, fused PPO "
+                               "loss backward, CPU restatement (oracle port)",
+                   "rows_per_step": sample[0].shape[0], "actions": args.actions, "same_rows_as_b200_arm": True},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{sample[0].shape[0]} rows x {args.actions} actions per step, all host threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------- poker learner objective
+
+
+def _poker_loss_inputs(device, S, W, E, M=2, seed=11):
+    """A seeded learner batch on the device: raw fields with the model head's value ranges
+    (softmax omega, sigmoid mu / iota, softplus + 0.02 scale), a reference copy perturbed as
+    after one update, legal sets shaped as the game's (check/call always, fold when facing a bet
+    with probability 0.7, raise ticks one contiguous range ending at the all-in, none in 10% of
+    rows), legal taken actions, old log pi near the current one, N(0,1) advantages, posteriors
+    with 30% zeros (Rao-Blackwell), values and targets N(0,1)."""
+
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    T = E - 2
+    raw = {"type_logits": torch.randn(S, W, 3, device=device, generator=g) * 1.5,
+           "omega": torch.softmax(torch.randn(S, W, M, device=device, generator=g), -1),
+           "mu": torch.sigmoid(torch.randn(S, W, M, device=device, generator=g)),
+           "s": torch.nn.functional.softplus(torch.randn(S, W, M, device=device, generator=g)) + 0.02,
+           "iota": torch.sigmoid(torch.randn(S, W, device=device, generator=g))}
+    ref = {k: v.clone() for k, v in raw.items()}
+    ref["type_logits"] += 0.3 * torch.randn(S, W, 3, device=device, generator=g)
+    ref["mu"] = (ref["mu"] + 0.1 * torch.randn(S, W, M, device=device, generator=g)).clamp(0, 1)
+    mask = torch.zeros(S, E, dtype=torch.bool, device=device)
+    mask[:, 1] = True
+    mask[:, 0] = torch.rand(S, device=device, generator=g) < 0.7
+    lo = torch.randint(0, T, (S,), device=device, generator=g)
+    ticks = torch.arange(T, device=device)
+    raise_ok = (torch.rand(S, device=device, generator=g) >= 0.1)[:, None] & (ticks[None] >= lo[:, None])
+    mask[:, 2:] = raise_ok
+    legal_count = mask.sum(1)
+    pick = (torch.rand(S, device=device, generator=g) * legal_count).long()
+    action = (mask.cumsum(1) <= pick[:, None]).sum(1).to(torch.int32)
+    old = -1.5 + 0.5 * torch.randn(S, W, device=device, generator=g)
+    adv = torch.randn(S, W, device=device, generator=g)
+    post = torch.rand(S, W, device=device, generator=g) * (torch.rand(S, W, device=device, generator=g) > 0.3)
+    value = torch.randn(S, W, device=device, generator=g)
+    old_value = value + 0.3 * torch.randn(S, W, device=device, generator=g)
+    target = torch.randn(S, W, device=device, generator=g)
+    controls = torch.tensor([[0.2, math.log(1.5), 0.5, 0.2, 0.01, 0.05, 0.0, 0.0, 1e-8, 1.0]], device=device)
+    return dict(raw=raw, ref=ref, mask=mask, action=action, old=old, adv=adv, post=post if W > 1 else None,
+                value=value, old_value=old_value, target=target, controls=controls)
+
+
+def _events_ms(device, fn, reps):
+    import torch
+
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(device)
+    return a.elapsed_time(b) / reps
+
+
+def _reference_pbg():
+    """The reference package installed by the driver under baseline/_ref (None when absent)."""
+
+    path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "pbg")):
+        return None
+    if path not in sys.path:
+        sys.path.append(path)
+    try:
+        import pbg.core.learner  # noqa: F401
+        import pbg.games.poker.queued.policy  # noqa: F401
+    except Exception:  # the reference's own import failed on this box
+        return None
+    return path
+
+
+def _reference_poker_loss_ms(device, d, reps):
+    """The reference's own loss program on the same batch: pbg.core.learner.LearnerOperation.forward_loss
+    with pbg's PokerPolicyOperator.learner, then (total * weight).sum().backward() (training.py:403)."""
+
+    import torch
+    from pbg.core.contracts import mode_schema
+    from pbg.core.learner import LearnerOperation, LossConfig, ModelEvaluation, SequentialLearnerBatch
+    from pbg.games.poker.queued.policy import PokerLegality, PokerPolicyOperator
+
+    S, E = d["mask"].shape
+    W = d["raw"]["type_logits"].shape[1]
+    op = PokerPolicyOperator()
+    legality = PokerLegality(torch.arange(E, dtype=torch.int32, device=device)[None].expand(S, -1).contiguous(),
+                             d["mask"])
+
+    def policy(input_type, model_input, raw_rows, act, private, owner, reference):
+        return op.learner(raw_rows, legality, act, private, owner, reference)
+
+    fields = {"model_input": torch.zeros(S, 1, device=device), "owner": torch.zeros(S, dtype=torch.int32, device=device),
+              "action": d["action"], "old_log_policy": d["old"], "advantage_target": d["adv"],
+              "old_value": d["old_value"], "value_target": d["target"]}
+    if W == 1:
+        fields["sampled_private_state"] = torch.zeros(S, 2, dtype=torch.int32, device=device)
+    else:
+        fields["posterior"] = d["post"]
+    from types import MappingProxyType
+
+    batch = SequentialLearnerBatch("post", torch.arange(S, device=device), MappingProxyType(fields))
+    learner = LearnerOperation(mode_schema("self_play", "sequential", "sampled" if W == 1 else "rao_blackwell"),
+                               LossConfig(), None, policy)
+    leaves = {k: v.detach().clone().requires_grad_() for k, v in d["raw"].items()}
+    value = d["value"].detach().clone().requires_grad_()
+    weight = torch.ones(1, device=device)
+
+    def step():
+        for t in (*leaves.values(), value):
+            t.grad = None
+        res = learner.forward_loss(batch, iteration=0, lane_count=1, loss_controls=d["controls"],
+                                   evaluation=ModelEvaluation(leaves, value), reference_raw=d["ref"])
+        (res.total * weight).sum().backward()
+
+    return _events_ms(device, step, reps)
+
+
+def poker_loss_component(device, reps=10):
+    """The fused poker learner objective (pbg_poker_learner_objective) on a sampled cfg2-size batch and a
+    Rao-Blackwell batch over all 1,326 hands, beside the reference's own PyTorch CUDA loss program on the
+    same batches when the driver installed it."""
+
+    import torch
+    from pbg_b200.learner import PokerLearnerObjective
+
+    out = {}
+    obj = PokerLearnerObjective(device)
+    for name, S, W in (("sampled", 65_536, 1), ("rao_blackwell", 512, 1326)):
+        d = _poker_loss_inputs(device, S, W, 202)
+        lw = torch.ones(1, device=device)
+
+        def run():
+            obj(d["raw"], d["mask"], d["action"], d["old"], d["adv"], d["value"], d["old_value"], d["target"],
+                d["controls"], lw, posterior=d["post"], reference_raw=d["ref"])
+
+        ms = _events_ms(device, run, reps)
+        rows = S * W
+        # bytes: raw + reference fields (2 x 40 B at M = 2), gradient out (40 B), old/adv/post/value/targets
+        # and the value gradient (7 x 4 B), the mask row and action shared by a sigma row's columns
+        bytes_per_row = 40 + 40 + 40 + 28 + (202 + 4) / W
+        entry = {"workload": f"HU 100bb R13 (E = 202 events, M = 2), {S} sigma rows x {W} private column(s), "
+                             "reference KL, clipped value, one lane",
+                 "ms": ms, "sigma_rows_per_s": S / (ms / 1e3), "policy_rows_per_s": rows / (ms / 1e3),
+                 "hbm_gbs": rows * bytes_per_row / (ms / 1e3) / 1e9, "bytes_per_policy_row": bytes_per_row,
+                 "bound": "SFU / FP32 issue (2 x (T+1) logistic edges per component per row, forward and backward)",
+                 "kernel": "learner_objective_kernel", "gpu_launches": 1 if W == 1 else 2}
+        if _reference_pbg() is not None:
+            try:
+                ref_ms = _reference_poker_loss_ms(device, d, max(2, reps // 2))
+                entry["reference_torch_cuda_ms"] = ref_ms
+                entry["speedup_vs_reference_torch_cuda"] = ref_ms / ms
+            except torch.OutOfMemoryError:
+                entry["reference_torch_cuda_ms"] = "out of memory"
+        out[name] = entry
+        del d
+        torch.cuda.empty_cache()
+    return out
+
+
+def reference_torch_loss_component(device, inputs, reps=5):
+    """The reference's own PyTorch CUDA loss program on the cfg5 rows: pbg.core.learner.LearnerOperation
+    .forward_loss (sampled, sequential, unmodified, from baseline/_ref) over the same 4,194,304 x 8 bf16
+    logits, masks, actions, old log pi and advantages, with a categorical policy operation (masked
+    log-softmax selected log pi and entropy in torch, the math of the reference's game-neutral fixture
+    tests/categorical_policy_fixture.py), then (total * weight).sum().backward() for d logits."""
+
+    import torch
+    from types import MappingProxyType
+
+    from pbg.core.contracts import mode_schema
+    from pbg.core.learner import (EntropyLossConfig, LearnerOperation, LossConfig, ModelEvaluation,
+                                  PolicyEvaluation, SequentialLearnerBatch, ValueLossConfig)
+
+    logits, mask, action, old, adv, weight = inputs
+    N, A = logits.shape
+    legal = mask.bool()
+
+    def policy(input_type, model_input, raw, act, private, owner, reference):
+        x = raw["logits"].reshape(N, A).float().masked_fill(~legal, -torch.inf)
+        logp = torch.log_softmax(x, -1)
+        sel = logp.gather(1, act.long()[:, None]).squeeze(1)
+        prob = logp.exp()
+        ent = -(prob * torch.where(legal, logp, torch.zeros_like(logp))).sum(-1)
+        return PolicyEvaluation(sel, ent, torch.zeros_like(sel))
+
+    fields = MappingProxyType({
+        "model_input": torch.zeros(N, 1, device=device), "owner": torch.zeros(N, dtype=torch.int32, device=device),
+        "sampled_private_state": torch.zeros(N, 2, dtype=torch.int32, device=device), "action": action,
+        "old_log_policy": old[:, None], "old_value": torch.zeros(N, 1, device=device),
+        "value_target": torch.zeros(N, 1, device=device), "advantage_target": adv[:, None]})
+    batch = SequentialLearnerBatch("pre", torch.arange(N, device=device), fields)
+    cfg = LossConfig(policy_clip=0.2, value=ValueLossConfig(coefficient=0.0),
+                     entropy=EntropyLossConfig(coefficient=0.01))
+    learner = LearnerOperation(mode_schema("self_play", "sequential", "sampled"), cfg, None, policy,
+                               precision="bf16")
+    leaf = logits.detach().clone().requires_grad_()
+    value = torch.zeros(N, 1, device=device)
+    controls = learner.controls((cfg,), 0, device)
+
+    def step():
+        leaf.grad = None
+        res = learner.forward_loss(batch, iteration=0, lane_count=1, loss_controls=controls,
+                                   evaluation=ModelEvaluation({"logits": leaf[:, None, :]}, value))
+        res.total.sum().backward()
+
+    ms = _events_ms(device, step, reps)
+    del leaf
+    torch.cuda.empty_cache()
+    return {"workload": "cfg5 rows (4,194,304 x 8, bf16 logits): the reference's LearnerOperation.forward_loss "
+                        "+ backward on the device, inputs resident",
+            "ms_per_step": ms, "value": N / (ms / 1e3), "unit": UNIT, "source": "baseline/_ref (pbg, unmodified)"}
 
 
 # ----------------------------------------------------------- rollout component
@@ -1184,6 +1404,7 @@ def main():
                                   "postflop_forward": postflop_forward_component(device),
                                   "posterior_sampler": posterior_component(device),
                                   "loss_readout": readout_component(device),
+                                  "poker_loss": poker_loss_component(device),
                                   "optimizer_step": optimizer_component(device),
                                   "showdown": showdown_component(device),
                                   "reach_update": reach_component(device),
@@ -1192,6 +1413,11 @@ def main():
                                   "rollout_with_model": rollout_with_model_component(device)}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
+    if rank == 0 and world == 1 and _reference_pbg() is not None:
+        ref = reference_torch_loss_component(device, inputs)
+        ref["speedup_value"] = value / ref["value"]
+        ref["speedup_e2e"] = e2e_value / ref["value"]
+        line["reference_torch_cuda"] = ref
     if rank == 0 and world == 1:
         sample = host_sample(1 << 21, A, 0)
         rate, threads, rows, wall = cpu_loss_rate(sample, seconds=3.0)
