@@ -32,6 +32,8 @@
 // Statistics are accumulated per (warp, lane of the batch) in double in
 // shared memory, reduced per block in warp order and across blocks in block
 // order by the last block to arrive (deterministic for a given grid).
+#include <type_traits>
+
 #include "pbg_common.cuh"
 #include "policy.cuh"
 
@@ -65,88 +67,156 @@ struct LearnerArgs {
     float* result;  // [lanes,10]
 };
 
-// Forward of one row, keeping what the backward needs (lane chunk of C events).
+// ------------------------------------------------------------------ row math
+//
+// The learner's own forward of the composite policy (policy.py:113-204): the
+// same operations as warp_policy_row (policy.cuh), with every per-event
+// division replaced by a multiplication with a correctly rounded reciprocal
+// (__frcp_rn) and the edge spacing hoisted.  Results agree with the
+// rounding-for-rounding forward to a few ulp, far inside the learner's
+// tolerance; the rollout keeps the exact forward for its sampled actions.
+// Lanes hold CH consecutive events (CH a compile-time chunk >= ceil(E / 32)).
+
+struct Ticks {
+    int T, E, half;
+    float step;  // linspace(0, 1, T + 1) spacing
+};
+
+__device__ __forceinline__ Ticks make_ticks(int E) {
+    Ticks g;
+    g.E = E;
+    g.T = E - 2;
+    g.half = (g.T + 1) / 2;
+    g.step = __fdiv_rn(1.0f, (float)g.T);
+    return g;
+}
+
+// torch.linspace(0, 1, T+1)[i] in fp32 (two-sided formula)
+__device__ __forceinline__ float edge_at(const Ticks& g, int i) {
+    return i < g.half ? __fmul_rn((float)i, g.step) : __fsub_rn(1.0f, __fmul_rn(g.step, (float)(g.T - i)));
+}
+
+// sigma(z) and sigma(-z) from one exponential: sigma(-z) = e^{-z} sigma(z) (1 when e^{-z} overflows)
+__device__ __forceinline__ void sig_pair(float z, float& sig, float& sm) {
+    const float ex = expf(-z);
+    sig = __frcp_rn(1.0f + ex);
+    sm = isinf(ex) ? 1.0f : ex * sig;
+}
+
+// Per-component constants: 1/s, the tick width factor -expm1(-(1/T)/s) and the normaliser
+// sigma(z_T) sigma(-z_0) (-expm1(z_0 - z_T)).
+struct Comp {
+    float loc, inv_s, width, norm, inv_norm;
+};
+
+__device__ __forceinline__ Comp comp_setup(float mu, float s, const Ticks& g) {
+    Comp c;
+    c.loc = mu;
+    c.inv_s = __frcp_rn(s);
+    const float z0 = -mu * c.inv_s;
+    const float zT = (edge_at(g, g.T) - mu) * c.inv_s;
+    float sT, smT, s0, sm0;
+    sig_pair(zT, sT, smT);
+    sig_pair(z0, s0, sm0);
+    c.norm = sT * sm0 * -expm1f(z0 - zT);
+    c.inv_norm = __frcp_rn(fmaxf(c.norm, FLT_TINY));
+    c.width = -expm1f(-g.step * c.inv_s);
+    return c;
+}
+
+template <int CH>
 struct RowForward {
-    float p[CHUNK_MAX];     // probabilities, 0 where illegal
-    float mix[CHUNK_MAX];   // masked mixture on raise ticks
-    float cond[CHUNK_MAX];  // conditional raise probability
-    float rp[CHUNK_MAX];    // raise probability (1 - iota) cond + iota [all-in]
+    float p[CH];     // probabilities, 0 where illegal
+    float mix[CH];   // masked mixture on raise ticks
+    float cond[CH];  // conditional raise probability
+    float rp[CH];    // raise probability (1 - iota) cond + iota [all-in]
+    bool ok[CH];     // event legal
     float mass;
-    int all_in;             // highest legal raise tick, -1 when none
+    int all_in;      // highest legal raise tick, -1 when none
     bool facing;
 };
 
-// Same arithmetic as warp_policy_row (policy.cuh), rounding for rounding.
-template <class Legal>
-__device__ void policy_forward_ex(const RawRow& raw, const Legal& legal, int T, int E, int C, RowForward& f) {
+template <int CH>
+__device__ __forceinline__ float chunk_fetch(const float (&x)[CH], int e) {
     const int lane = threadIdx.x & 31;
-    const int e0 = lane * C;
+    float mine = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) f.mix[j] = 0.0f;
+    for (int j = 0; j < CH; ++j)
+        if (lane * CH + j == e) mine = x[j];
+    return __shfl_sync(0xffffffffu, mine, (e / CH) & 31);
+}
+
+template <int CH>
+__device__ void policy_forward_fast(const RawRow& raw, const MaskRow& legal, const Ticks& g, RowForward<CH>& f) {
+    const int lane = threadIdx.x & 31;
+    const int e0 = lane * CH;
+    #pragma unroll
+    for (int j = 0; j < CH; ++j) {
+        const int e = e0 + j;
+        f.ok[j] = e < g.E && legal(e);
+        f.mix[j] = 0.0f;
+    }
+    const int kk = e0 - 2 > 0 ? e0 - 2 : 0;
     for (int m = 0; m < raw.M; ++m) {
-        MixtureEdges mx_m = mixture_edges(raw.mu[m], raw.scale[m], T);
-        float tick[CHUNK_MAX];
+        const Comp c = comp_setup(raw.mu[m], raw.scale[m], g);
+        float sig, sm_prev;
+        sig_pair((edge_at(g, kk) - c.loc) * c.inv_s, sig, sm_prev);
+        float a[CH];
         float part = 0.0f;
-        const int k0 = e0 - 2;
-        float sig_unused, sm_prev;
-        edge_sigmoids(mx_m, k0 > 0 ? k0 : 0, T, sig_unused, sm_prev);
         #pragma unroll
-        for (int j = 0; j < CHUNK_MAX; ++j) {
-            tick[j] = 0.0f;
-            int e = e0 + j;
-            int k = e - 2;
-            if (j < C && k >= 0 && e < E) {
+        for (int j = 0; j < CH; ++j) {
+            const int e = e0 + j, k = e - 2;
+            a[j] = 0.0f;
+            if (k >= 0 && e < g.E) {
                 float sig_next, sm_next;
-                edge_sigmoids(mx_m, k + 1, T, sig_next, sm_next);
-                float v = fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev), mx_m.width), 0.0f);
-                tick[j] = __fmul_rn(v, mx_m.inv_norm);
-                part = __fadd_rn(part, tick[j]);
+                sig_pair((edge_at(g, k + 1) - c.loc) * c.inv_s, sig_next, sm_next);
+                a[j] = fmaxf(sig_next * sm_prev * c.width, 0.0f) * c.inv_norm;
+                part += a[j];
                 sm_prev = sm_next;
             }
         }
-        float total = fmaxf(warp_sum(part), FLT_TINY);
-        float om = raw.omega[m];
+        const float coef = raw.omega[m] * __frcp_rn(fmaxf(warp_sum(part), FLT_TINY));
         #pragma unroll
-        for (int j = 0; j < CHUNK_MAX; ++j) f.mix[j] = __fadd_rn(f.mix[j], __fmul_rn(om, __fdiv_rn(tick[j], total)));
+        for (int j = 0; j < CH; ++j) f.mix[j] += coef * a[j];
     }
     float part_mass = 0.0f;
     int part_count = 0, part_top = -1;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        int e = e0 + j;
-        bool ok = j < C && e >= 2 && e < E && legal(e);
-        if (!ok) f.mix[j] = 0.0f;
-        else {
-            part_mass = __fadd_rn(part_mass, f.mix[j]);
+    for (int j = 0; j < CH; ++j) {
+        const int e = e0 + j;
+        if (e >= 2 && f.ok[j]) {
+            part_mass += f.mix[j];
             ++part_count;
             part_top = e - 2;
+        } else {
+            f.mix[j] = 0.0f;
         }
     }
     f.mass = warp_sum(part_mass);
-    int count = __reduce_add_sync(0xffffffffu, part_count);
+    const int count = __reduce_add_sync(0xffffffffu, part_count);
     f.all_in = warp_max_int(part_top);
+    const float inv_mass = __frcp_rn(fmaxf(f.mass, POLICY_EPS));
+    const float uniform = __frcp_rn((float)max(count, 1));
     const float io = raw.iota;
     f.facing = legal(0);
     const float l0 = raw.logits[0], l1 = raw.logits[1], l2 = raw.logits[2];
-    float full[CHUNK_MAX];
+    float full[CH];
     float mx = -INFINITY;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        int e = e0 + j;
+    for (int j = 0; j < CH; ++j) {
+        const int e = e0 + j;
         full[j] = -INFINITY;
         f.cond[j] = 0.0f;
         f.rp[j] = 0.0f;
-        if (j < C && e < E && legal(e)) {
+        if (f.ok[j]) {
             if (e == 0) full[j] = l0;
             else if (e == 1) full[j] = f.facing ? l1 : l0;
             else {
-                float cond = f.mass > 0.0f ? __fdiv_rn(f.mix[j], fmaxf(f.mass, POLICY_EPS))
-                                           : __fdiv_rn(1.0f, (float)max(count, 1));
-                float atom = (e - 2) == f.all_in ? 1.0f : 0.0f;
-                float rp = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, io), cond), __fmul_rn(io, atom));
+                const float cond = f.mass > 0.0f ? f.mix[j] * inv_mass : uniform;
+                const float rp = (1.0f - io) * cond + (e - 2 == f.all_in ? io : 0.0f);
                 f.cond[j] = cond;
                 f.rp[j] = rp;
-                full[j] = rp > 0.0f ? __fadd_rn(l2, logf(fmaxf(rp, POLICY_EPS))) : -INFINITY;
+                full[j] = rp > 0.0f ? l2 + __logf(fmaxf(rp, POLICY_EPS)) : -INFINITY;
             }
             mx = fmaxf(mx, full[j]);
         }
@@ -154,102 +224,95 @@ __device__ void policy_forward_ex(const RawRow& raw, const Legal& legal, int T, 
     mx = warp_max(mx);
     float part_sum = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        int e = e0 + j;
-        f.p[j] = (j < C && e < E && legal(e)) ? expf(__fsub_rn(full[j], mx)) : 0.0f;
-        part_sum = __fadd_rn(part_sum, f.p[j]);
+    for (int j = 0; j < CH; ++j) {
+        f.p[j] = f.ok[j] ? expf(full[j] - mx) : 0.0f;
+        part_sum += f.p[j];
     }
-    float denom = warp_sum(part_sum);
+    const float inv_denom = __frcp_rn(warp_sum(part_sum));
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        int e = e0 + j;
-        f.p[j] = (j < C && e < E && legal(e)) ? __fdiv_rn(f.p[j], denom) : 0.0f;
-    }
+    for (int j = 0; j < CH; ++j) f.p[j] *= inv_denom;
 }
 
 // Backward of one mixture component: given d(total)/d(mixture_k) on the raise
-// ticks held by this lane (0 elsewhere), accumulate d omega_m, d mu_m, d s_m.
+// ticks held by this lane (0 elsewhere), add d omega_m, d mu_m, d s_m.
 // Recomputes the forward's tick masses a_k = v_k / max(N, tiny) and their sum.
-__device__ void component_backward(const RawRow& raw, int m, int T, int E, int C, const float (&dmix)[CHUNK_MAX],
-                                   float& d_om, float& d_mu, float& d_s) {
+template <int CH>
+__device__ void component_backward(const RawRow& raw, int m, const Ticks& g, const float (&dmix)[CH], float& d_om,
+                                   float& d_mu, float& d_s) {
     const int lane = threadIdx.x & 31;
-    const int e0 = lane * C;
-    const float loc = raw.mu[m], sc = raw.scale[m];
-    const MixtureEdges mx = mixture_edges(loc, sc, T);
-    const float z0 = __fdiv_rn(__fsub_rn(0.0f, loc), sc);
-    const float zT = __fdiv_rn(__fsub_rn(edge_of(T, T), loc), sc);
-    const float norm = __fmul_rn(__fmul_rn(sigmoid_f(zT), sigmoid_f(-z0)), -expm1f(__fsub_rn(z0, zT)));
-    float v[CHUNK_MAX], a[CHUNK_MAX], dlow[CHUNK_MAX], zlow[CHUNK_MAX];
+    const int e0 = lane * CH;
+    const Comp c = comp_setup(raw.mu[m], raw.scale[m], g);
+    float v[CH], a[CH], dlow[CH], zlow[CH];
     float dtop = 0.0f, ztop = 0.0f;  // sigma'(z_T) and z_T on the lane holding tick T-1
     float part = 0.0f;
-    const int k0 = e0 - 2;
+    const int kk = e0 - 2 > 0 ? e0 - 2 : 0;
+    float z_prev = (edge_at(g, kk) - c.loc) * c.inv_s;
     float sig_prev, sm_prev;
-    edge_sigmoids(mx, k0 > 0 ? k0 : 0, T, sig_prev, sm_prev);
+    sig_pair(z_prev, sig_prev, sm_prev);
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
+    for (int j = 0; j < CH; ++j) {
         v[j] = a[j] = dlow[j] = zlow[j] = 0.0f;
         const int e = e0 + j, k = e - 2;
-        if (j < C && k >= 0 && e < E) {
+        if (k >= 0 && e < g.E) {
+            const float z_next = (edge_at(g, k + 1) - c.loc) * c.inv_s;
             float sig_next, sm_next;
-            edge_sigmoids(mx, k + 1, T, sig_next, sm_next);
-            v[j] = fmaxf(__fmul_rn(__fmul_rn(sig_next, sm_prev), mx.width), 0.0f);
-            a[j] = __fmul_rn(v[j], mx.inv_norm);
-            part = __fadd_rn(part, a[j]);
+            sig_pair(z_next, sig_next, sm_next);
+            v[j] = fmaxf(sig_next * sm_prev * c.width, 0.0f);
+            a[j] = v[j] * c.inv_norm;
+            part += a[j];
             dlow[j] = sig_prev * sm_prev;  // sigma'(z_k)
-            zlow[j] = (edge_of(k, T) - loc) * mx.inv_scale;
-            if (k + 1 == T) {
+            zlow[j] = z_prev;
+            if (k + 1 == g.T) {
                 dtop = sig_next * sm_next;
-                ztop = (edge_of(T, T) - loc) * mx.inv_scale;
+                ztop = z_next;
             }
+            z_prev = z_next;
             sig_prev = sig_next;
             sm_prev = sm_next;
         }
     }
     const float total = warp_sum(part);
-    const float Sc = fmaxf(total, FLT_TINY);
+    const float inv_Sc = __frcp_rn(fmaxf(total, FLT_TINY));
     const float om = raw.omega[m];
     float pom = 0.0f, pq = 0.0f;
-    float ddl[CHUNK_MAX];
+    float ddl[CH];
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        const float dl = __fdiv_rn(a[j], Sc);
-        pom += dmix[j] * dl;
+    for (int j = 0; j < CH; ++j) {
+        pom += dmix[j] * a[j];
         ddl[j] = dmix[j] * om;
         pq += ddl[j] * a[j];
     }
-    d_om += warp_sum(pom);
+    d_om += warp_sum(pom) * inv_Sc;
     const float Q = warp_sum(pq);
-    const float qterm = total >= FLT_TINY ? Q / (Sc * Sc) : 0.0f;
-    float dc[CHUNK_MAX];
-    float pn = 0.0f, last = 0.0f;
+    const float qterm = total >= FLT_TINY ? Q * inv_Sc * inv_Sc : 0.0f;
+    float dc[CH];
+    float pn = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
+    for (int j = 0; j < CH; ++j) {
         const int e = e0 + j, k = e - 2;
         dc[j] = 0.0f;
-        if (j < C && k >= 0 && e < E) {
-            const float da = ddl[j] / Sc - qterm;
+        if (k >= 0 && e < g.E) {
+            const float da = ddl[j] * inv_Sc - qterm;
             pn += da * v[j];
-            dc[j] = da * mx.inv_norm;
+            dc[j] = da * c.inv_norm;
         }
-        if (j == C - 1) last = dc[j];
     }
     const float sn = warp_sum(pn);
-    const float dN = norm >= FLT_TINY ? -sn * mx.inv_norm * mx.inv_norm : 0.0f;
-    float carry = __shfl_up_sync(0xffffffffu, last, 1);  // dc of the tick just before this lane's chunk
+    const float dN = c.norm >= FLT_TINY ? -sn * c.inv_norm * c.inv_norm : 0.0f;
+    float carry = __shfl_up_sync(0xffffffffu, dc[CH - 1], 1);  // dc of the tick just before this lane's chunk
     if (lane == 0) carry = 0.0f;
     float sdz = 0.0f, szdz = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
+    for (int j = 0; j < CH; ++j) {
         const int e = e0 + j, k = e - 2;
-        const bool tick = j < C && k >= 0 && e < E;
-        if (tick) {
+        if (k >= 0 && e < g.E) {
             // edge k: lower edge of tick k, upper edge of tick k-1 (no tick before tick 0)
             const float before = k == 0 ? 0.0f : carry;
             float dz = (before - dc[j]) * dlow[j];
             if (k == 0) dz -= dN * dlow[j];
             sdz += dz;
             szdz += zlow[j] * dz;
-            if (k + 1 == T) {
+            if (k + 1 == g.T) {
                 const float dzT = (dc[j] + dN) * dtop;
                 sdz += dzT;
                 szdz += ztop * dzT;
@@ -257,8 +320,8 @@ __device__ void component_backward(const RawRow& raw, int m, int T, int E, int C
             carry = dc[j];
         }
     }
-    d_mu += -warp_sum(sdz) * mx.inv_scale;
-    d_s += -warp_sum(szdz) * mx.inv_scale;
+    d_mu += -warp_sum(sdz) * c.inv_s;
+    d_s += -warp_sum(szdz) * c.inv_s;
 }
 
 __device__ __forceinline__ float tie_share(float a, float b) { return a < b ? 1.0f : (a == b ? 0.5f : 0.0f); }
@@ -268,14 +331,13 @@ __device__ __forceinline__ float tie_share(float a, float b) { return a < b ? 1.
 // gives -(log max(p, eps) + [p >= eps]); KL sum p (log max(p, eps) - log max(q, eps))
 // gives log max(p, eps) - log max(q, eps) + [p >= eps].  Illegal events get 0
 // (the masked fill after the softmax).
-__device__ __forceinline__ void add_reduction_grads(const RowForward& f, const float (&logp)[CHUNK_MAX],
-                                                    const float (*logq)[CHUNK_MAX], const MaskRow& legal, int E,
-                                                    int C, float g_ent, float g_kl, float (&gp)[CHUNK_MAX]) {
-    const int lane = threadIdx.x & 31;
+template <int CH>
+__device__ __forceinline__ void add_reduction_grads(const RowForward<CH>& f, const float (&logp)[CH],
+                                                    const float (*logq)[CH], float g_ent, float g_kl,
+                                                    float (&gp)[CH]) {
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        const int e = lane * C + j;
-        if (j < C && e < E && legal(e)) {
+    for (int j = 0; j < CH; ++j) {
+        if (f.ok[j]) {
             const float ind = f.p[j] >= POLICY_EPS ? 1.0f : 0.0f;
             gp[j] += -g_ent * (logp[j] + ind);
             if (logq) gp[j] += g_kl * (logp[j] - (*logq)[j] + ind);
@@ -287,21 +349,22 @@ __device__ __forceinline__ void add_reduction_grads(const RowForward& f, const f
 
 // Composite backward of one policy row: given dL/dp on the legal events (gp),
 // write d type_logits, d omega, d mu, d s, d iota of row r.
-__device__ void policy_row_backward(const RawRow& raw, const RowForward& f, const float (&gp)[CHUNK_MAX],
-                                    const MaskRow& legal, int T, int E, int C, const pbg_policy_grad& grad,
-                                    int64_t r) {
+template <int CH>
+__device__ void policy_row_backward(const RawRow& raw, const RowForward<CH>& f, const float (&gp)[CH],
+                                    const Ticks& g, const pbg_policy_grad& grad, int64_t r) {
     const int lane = threadIdx.x & 31;
+    const int e0 = lane * CH;
     // masked softmax (selected logits -inf where illegal)
     float psg = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) psg += gp[j] * f.p[j];
+    for (int j = 0; j < CH; ++j) psg += gp[j] * f.p[j];
     const float sg = warp_sum(psg);
-    float dx[CHUNK_MAX];
+    float dx[CH];
     float pt0 = 0.0f, pt1 = 0.0f, pt2 = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        const int e = lane * C + j;
-        dx[j] = (j < C && e < E && legal(e)) ? f.p[j] * (gp[j] - sg) : 0.0f;
+    for (int j = 0; j < CH; ++j) {
+        const int e = e0 + j;
+        dx[j] = f.ok[j] ? f.p[j] * (gp[j] - sg) : 0.0f;
         if (e == 0) pt0 += dx[j];
         else if (e == 1) {
             if (f.facing) pt1 += dx[j];
@@ -311,15 +374,15 @@ __device__ void policy_row_backward(const RawRow& raw, const RowForward& f, cons
     const float dt0 = warp_sum(pt0), dt1 = warp_sum(pt1), dt2 = warp_sum(pt2);
     // raise logits l2 + log max(rp, eps) where rp > 0; rp = (1 - iota) cond + iota [all-in tick]
     const float io = raw.iota;
-    float dcond[CHUNK_MAX];
+    float dcond[CH];
     float pio = 0.0f, pdm = 0.0f;
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        const int e = lane * C + j;
+    for (int j = 0; j < CH; ++j) {
+        const int e = e0 + j;
         dcond[j] = 0.0f;
-        if (j < C && e >= 2 && e < E && legal(e)) {
+        if (e >= 2 && f.ok[j]) {
             const float rp = f.rp[j];
-            const float drp = (rp > 0.0f && rp >= POLICY_EPS) ? dx[j] / rp : 0.0f;
+            const float drp = (rp > 0.0f && rp >= POLICY_EPS) ? dx[j] * __frcp_rn(rp) : 0.0f;
             const float atom = (e - 2) == f.all_in ? 1.0f : 0.0f;
             pio += drp * (atom - f.cond[j]);
             dcond[j] = drp * (1.0f - io);
@@ -329,21 +392,21 @@ __device__ void policy_row_backward(const RawRow& raw, const RowForward& f, cons
     const float dio = warp_sum(pio);
     // cond = mixture / max(mass, eps) when mass > 0, else the uniform law (no gradient)
     const float mass = f.mass;
-    const float mc = fmaxf(mass, POLICY_EPS);
+    const float inv_mc = __frcp_rn(fmaxf(mass, POLICY_EPS));
     const float sdm = warp_sum(pdm);
-    const float dmass = mass >= POLICY_EPS ? -sdm / (mc * mc) : 0.0f;
-    float dmix[CHUNK_MAX];
+    const float dmass = mass >= POLICY_EPS ? -sdm * inv_mc * inv_mc : 0.0f;
+    float dmix[CH];
     #pragma unroll
-    for (int j = 0; j < CHUNK_MAX; ++j) {
-        const int e = lane * C + j;
-        dmix[j] = (mass > 0.0f && j < C && e >= 2 && e < E && legal(e)) ? dcond[j] / mc + dmass : 0.0f;
+    for (int j = 0; j < CH; ++j) {
+        const int e = e0 + j;
+        dmix[j] = (mass > 0.0f && e >= 2 && f.ok[j]) ? dcond[j] * inv_mc + dmass : 0.0f;
     }
     float* gom = grad.omega + r * raw.M;
     float* gmu = grad.mu + r * raw.M;
     float* gsc = grad.scale + r * raw.M;
     for (int m = 0; m < raw.M; ++m) {
         float dom = 0.0f, dmu = 0.0f, dsc = 0.0f;
-        component_backward(raw, m, T, E, C, dmix, dom, dmu, dsc);
+        component_backward<CH>(raw, m, g, dmix, dom, dmu, dsc);
         if (lane == 0) {
             gom[m] = dom;
             gmu[m] = dmu;
@@ -358,7 +421,18 @@ __device__ void policy_row_backward(const RawRow& raw, const RowForward& f, cons
     }
 }
 
-__global__ void __launch_bounds__(PL_THREADS) learner_objective_kernel(LearnerArgs g) {
+// probabilities only (the reference row of the KL term)
+template <int CH>
+__device__ __forceinline__ void policy_probs_fast(const RawRow& raw, const MaskRow& legal, const Ticks& g,
+                                                  float (&q)[CH]) {
+    RowForward<CH> f;
+    policy_forward_fast<CH>(raw, legal, g, f);
+    #pragma unroll
+    for (int j = 0; j < CH; ++j) q[j] = f.p[j];
+}
+
+template <int CH>
+__global__ void __launch_bounds__(PL_THREADS, 2) learner_objective_kernel(LearnerArgs g) {
     __shared__ double wst[PL_WARPS][PL_MAX_LANES][PL_STATS];
     __shared__ bool last_block;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -367,7 +441,8 @@ __global__ void __launch_bounds__(PL_THREADS) learner_objective_kernel(LearnerAr
         (&wst[0][0][0])[i] = st >= PL_SUMS ? -INFINITY : 0.0;
     }
     __syncthreads();
-    const int E = g.E, C = (E + 31) / 32, T = E - 2, W = g.W;
+    const Ticks tk = make_ticks(g.E);
+    const int W = g.W;
     const int64_t rpl = g.S / g.lanes, apl = g.A / g.lanes;
     const int64_t warps = (int64_t)gridDim.x * PL_WARPS;
     for (int64_t r = (int64_t)blockIdx.x * PL_WARPS + warp; r < g.rows; r += warps) {
@@ -376,29 +451,29 @@ __global__ void __launch_bounds__(PL_THREADS) learner_objective_kernel(LearnerAr
         const int ln = (int)(s / rpl);
         const float* ctl = g.controls + ln * 10;
         const float lw = g.lane_weight[ln] / (float)rpl;  // d (weighted total) / d (a sigma row's term)
-        MaskRow legal{g.mask + s * E};
+        MaskRow legal{g.mask + s * g.E};
         RawRow raw = raw_row(g.raw, r);
-        RowForward f;
-        policy_forward_ex(raw, legal, T, E, C, f);
-        float logp[CHUNK_MAX], gp[CHUNK_MAX];
+        RowForward<CH> f;
+        policy_forward_fast<CH>(raw, legal, tk, f);
+        float logp[CH], gp[CH];
         float pent = 0.0f;
         #pragma unroll
-        for (int j = 0; j < CHUNK_MAX; ++j) {
-            logp[j] = logf(fmaxf(f.p[j], POLICY_EPS));
+        for (int j = 0; j < CH; ++j) {
+            logp[j] = __logf(fmaxf(f.p[j], POLICY_EPS));
             pent += f.p[j] * logp[j];
             gp[j] = 0.0f;
         }
         const float entropy = -warp_sum(pent);
         float kl = 0.0f;
-        float logq[CHUNK_MAX];
+        float logq[CH];
         const bool with_ref = g.ref.type_logits != nullptr;
         if (with_ref) {
-            float q[CHUNK_MAX];
-            warp_policy_row(raw_row(g.ref, r), legal, T, E, C, q);
+            float q[CH];
+            policy_probs_fast<CH>(raw_row(g.ref, r), legal, tk, q);
             float pk = 0.0f;
             #pragma unroll
-            for (int j = 0; j < CHUNK_MAX; ++j) {
-                logq[j] = logf(fmaxf(q[j], POLICY_EPS));
+            for (int j = 0; j < CH; ++j) {
+                logq[j] = __logf(fmaxf(q[j], POLICY_EPS));
                 pk += f.p[j] * (logp[j] - logq[j]);
             }
             kl = warp_sum(pk);
@@ -415,8 +490,8 @@ __global__ void __launch_bounds__(PL_THREADS) learner_objective_kernel(LearnerAr
         for (int64_t i = a0; i < a1; ++i) {
             const float* actl = g.controls + (i / apl) * 10;
             const int act = g.action[i];
-            const float pa = warp_fetch(f.p, act, C);
-            const float cur = logf(fmaxf(pa, POLICY_EPS));
+            const float pa = chunk_fetch<CH>(f.p, act);
+            const float cur = __logf(fmaxf(pa, POLICY_EPS));
             const int64_t ic = i * W + c;
             const float post_raw = g.posterior ? g.posterior[ic] : 1.0f;
             const float post = g.inv_post ? post_raw * g.inv_post[i] : post_raw / fmaxf(post_raw, FLT_TINY);
@@ -444,15 +519,14 @@ __global__ void __launch_bounds__(PL_THREADS) learner_objective_kernel(LearnerAr
             const float dpr = neg ? nratio * tie_share(lr, cap) : ratio;
             const float dclip = (ratio >= 1.0f - clip && ratio <= 1.0f + clip) ? ratio : 0.0f;
             const float dcur = -lw * w * (tie_share(X, Y) * adv * dpr + tie_share(Y, X) * adv * dclip);
-            const float dpa = pa >= POLICY_EPS ? dcur / pa : 0.0f;
+            const float dpa = pa >= POLICY_EPS ? dcur * __frcp_rn(pa) : 0.0f;
             #pragma unroll
-            for (int j = 0; j < CHUNK_MAX; ++j)
-                if (lane * C + j == act) gp[j] += dpa;
+            for (int j = 0; j < CH; ++j)
+                if (lane * CH + j == act) gp[j] += dpa;
         }
         // ---- entropy (-c4) and KL (+c5) gradients, then the composite backward
-        add_reduction_grads(f, logp, with_ref ? &logq : nullptr, legal, E, C, -ctl[4] * lw * wsum,
-                            ctl[5] * lw * wsum, gp);
-        policy_row_backward(raw, f, gp, legal, T, E, C, g.grad, r);
+        add_reduction_grads<CH>(f, logp, with_ref ? &logq : nullptr, -ctl[4] * lw * wsum, ctl[5] * lw * wsum, gp);
+        policy_row_backward<CH>(raw, f, gp, tk, g.grad, r);
         // ---- value of this column under the sigma posterior: wsum (sum over the span of post / count)
         // normalised over the columns of the sigma row
         {
@@ -546,39 +620,40 @@ __global__ void __launch_bounds__(PL_THREADS) learner_objective_kernel(LearnerAr
 // PokerPolicyOperator.learner forward (policy.py:284-298) in one pass per
 // policy row: selected log pi (clamped at eps), entropy and, with reference
 // fields, KL(p || q).
-__global__ void __launch_bounds__(PL_THREADS) policy_learner_fwd_kernel(int64_t B, int E, pbg_policy raw,
+template <int CH>
+__global__ void __launch_bounds__(PL_THREADS, 2) policy_learner_fwd_kernel(int64_t B, int E, pbg_policy raw,
                                                                         pbg_policy ref, const uint8_t* mask,
                                                                         const int32_t* action, float* selected,
                                                                         float* entropy, float* kl) {
     const int lane = threadIdx.x & 31;
-    const int C = (E + 31) / 32, T = E - 2;
+    const Ticks tk = make_ticks(E);
     const int64_t rows = B * raw.rows;
     const int64_t warps = (int64_t)gridDim.x * PL_WARPS;
     for (int64_t r = ((int64_t)blockIdx.x * PL_THREADS + threadIdx.x) >> 5; r < rows; r += warps) {
         const int64_t b = r / raw.rows;
         MaskRow legal{mask + b * E};
-        float p[CHUNK_MAX];
-        warp_policy_row(raw_row(raw, r), legal, T, E, C, p);
-        float logp[CHUNK_MAX];
+        float p[CH];
+        policy_probs_fast<CH>(raw_row(raw, r), legal, tk, p);
+        float logp[CH];
         float pe = 0.0f;
         #pragma unroll
-        for (int j = 0; j < CHUNK_MAX; ++j) {
-            logp[j] = logf(fmaxf(p[j], POLICY_EPS));
+        for (int j = 0; j < CH; ++j) {
+            logp[j] = __logf(fmaxf(p[j], POLICY_EPS));
             pe += p[j] * logp[j];
         }
         const float ent = -warp_sum(pe);
         float k = 0.0f;
         if (ref.type_logits != nullptr) {
-            float q[CHUNK_MAX];
-            warp_policy_row(raw_row(ref, r), legal, T, E, C, q);
+            float q[CH];
+            policy_probs_fast<CH>(raw_row(ref, r), legal, tk, q);
             float pk = 0.0f;
             #pragma unroll
-            for (int j = 0; j < CHUNK_MAX; ++j) pk += p[j] * (logp[j] - logf(fmaxf(q[j], POLICY_EPS)));
+            for (int j = 0; j < CH; ++j) pk += p[j] * (logp[j] - __logf(fmaxf(q[j], POLICY_EPS)));
             k = warp_sum(pk);
         }
-        const float pa = warp_fetch(p, action[b], C);
+        const float pa = chunk_fetch<CH>(p, action[b]);
         if (lane == 0) {
-            selected[r] = logf(fmaxf(pa, POLICY_EPS));
+            selected[r] = __logf(fmaxf(pa, POLICY_EPS));
             entropy[r] = ent;
             kl[r] = k;
         }
@@ -589,45 +664,46 @@ __global__ void __launch_bounds__(PL_THREADS) policy_learner_fwd_kernel(int64_t 
 // upstream gradients of the selected log-probability, the entropy and the
 // reference KL of every policy row (B rows x `rows` columns, the action and
 // legality shared by a row's columns) -> gradients of the raw fields.
-__global__ void __launch_bounds__(PL_THREADS) policy_learner_vjp_kernel(int64_t B, int E, pbg_policy raw,
+template <int CH>
+__global__ void __launch_bounds__(PL_THREADS, 2) policy_learner_vjp_kernel(int64_t B, int E, pbg_policy raw,
                                                                         pbg_policy ref, const uint8_t* mask,
                                                                         const int32_t* action, const float* g_sel,
                                                                         const float* g_ent, const float* g_kl,
                                                                         pbg_policy_grad grad) {
     const int lane = threadIdx.x & 31;
-    const int C = (E + 31) / 32, T = E - 2;
+    const Ticks tk = make_ticks(E);
     const int64_t rows = B * raw.rows;
     const int64_t warps = (int64_t)gridDim.x * PL_WARPS;
     for (int64_t r = ((int64_t)blockIdx.x * PL_THREADS + threadIdx.x) >> 5; r < rows; r += warps) {
         const int64_t b = r / raw.rows;
         MaskRow legal{mask + b * E};
         RawRow rr = raw_row(raw, r);
-        RowForward f;
-        policy_forward_ex(rr, legal, T, E, C, f);
-        float logp[CHUNK_MAX], gp[CHUNK_MAX], logq[CHUNK_MAX];
+        RowForward<CH> f;
+        policy_forward_fast<CH>(rr, legal, tk, f);
+        float logp[CH], gp[CH], logq[CH];
         #pragma unroll
-        for (int j = 0; j < CHUNK_MAX; ++j) {
-            logp[j] = logf(fmaxf(f.p[j], POLICY_EPS));
+        for (int j = 0; j < CH; ++j) {
+            logp[j] = __logf(fmaxf(f.p[j], POLICY_EPS));
             gp[j] = 0.0f;
         }
         const bool with_ref = ref.type_logits != nullptr && g_kl != nullptr;
         if (with_ref) {
-            float q[CHUNK_MAX];
-            warp_policy_row(raw_row(ref, r), legal, T, E, C, q);
+            float q[CH];
+            policy_probs_fast<CH>(raw_row(ref, r), legal, tk, q);
             #pragma unroll
-            for (int j = 0; j < CHUNK_MAX; ++j) logq[j] = logf(fmaxf(q[j], POLICY_EPS));
+            for (int j = 0; j < CH; ++j) logq[j] = __logf(fmaxf(q[j], POLICY_EPS));
         }
         if (g_sel) {
             const int act = action[b];
-            const float pa = warp_fetch(f.p, act, C);
-            const float dpa = pa >= POLICY_EPS ? g_sel[r] / pa : 0.0f;
+            const float pa = chunk_fetch<CH>(f.p, act);
+            const float dpa = pa >= POLICY_EPS ? g_sel[r] * __frcp_rn(pa) : 0.0f;
             #pragma unroll
-            for (int j = 0; j < CHUNK_MAX; ++j)
-                if (lane * C + j == act) gp[j] += dpa;
+            for (int j = 0; j < CH; ++j)
+                if (lane * CH + j == act) gp[j] += dpa;
         }
-        add_reduction_grads(f, logp, with_ref ? &logq : nullptr, legal, E, C, g_ent ? g_ent[r] : 0.0f,
-                            with_ref ? g_kl[r] : 0.0f, gp);
-        policy_row_backward(rr, f, gp, legal, T, E, C, grad, r);
+        add_reduction_grads<CH>(f, logp, with_ref ? &logq : nullptr, g_ent ? g_ent[r] : 0.0f,
+                                with_ref ? g_kl[r] : 0.0f, gp);
+        policy_row_backward<CH>(rr, f, gp, tk, grad, r);
     }
 }
 
@@ -652,6 +728,16 @@ __global__ void __launch_bounds__(256) posterior_norm_kernel(int64_t S, int W, c
         vsum = warp_sum(vsum) / (float)(a1 - a0);
         if (lane == 0) inv_vpost[s] = 1.0f / fmaxf(vsum, FLT_TINY);
     }
+}
+
+// Chunk of events per lane: the smallest instantiated CH with 32 * CH >= E.
+template <class F>
+static void with_chunk(int E, F&& f) {
+    if (E <= 32) f(std::integral_constant<int, 1>{});
+    else if (E <= 64) f(std::integral_constant<int, 2>{});
+    else if (E <= 128) f(std::integral_constant<int, 4>{});
+    else if (E <= 224) f(std::integral_constant<int, 7>{});
+    else f(std::integral_constant<int, 9>{});
 }
 
 static int64_t stat_bytes(int32_t lanes) {
@@ -738,7 +824,7 @@ int pbg_poker_learner_objective(int64_t S, int64_t A, int32_t E, int32_t W, int3
         g.inv_vpost = norms + A;
         posterior_norm_kernel<<<stride_grid(S * 32, 256), 256, 0, st>>>(S, W, action_ptr, posterior, norms, norms + A);
     }
-    learner_objective_kernel<<<grid, PL_THREADS, 0, st>>>(g);
+    with_chunk(E, [&](auto ch) { learner_objective_kernel<decltype(ch)::value><<<grid, PL_THREADS, 0, st>>>(g); });
     return launch_status("poker_learner_objective");
 }
 
@@ -756,8 +842,11 @@ int pbg_policy_learner_forward(int64_t B, int32_t E, pbg_policy raw, const pbg_p
     if (B == 0) return PBG_OK;
     pbg_policy ref{};
     if (reference) ref = *reference;
-    policy_learner_fwd_kernel<<<stride_grid(B * raw.rows * 32, PL_THREADS), PL_THREADS, 0, as_stream(stream)>>>(
-        B, E, raw, ref, mask, action, selected, entropy, kl);
+    const int grid = stride_grid(B * raw.rows * 32, PL_THREADS);
+    with_chunk(E, [&](auto ch) {
+        policy_learner_fwd_kernel<decltype(ch)::value><<<grid, PL_THREADS, 0, as_stream(stream)>>>(
+            B, E, raw, ref, mask, action, selected, entropy, kl);
+    });
     return launch_status("policy_learner_forward");
 }
 
@@ -776,8 +865,11 @@ int pbg_policy_learner_backward(int64_t B, int32_t E, pbg_policy raw, const pbg_
     if (B == 0) return PBG_OK;
     pbg_policy ref{};
     if (reference) ref = *reference;
-    policy_learner_vjp_kernel<<<stride_grid(B * raw.rows * 32, PL_THREADS), PL_THREADS, 0, as_stream(stream)>>>(
-        B, E, raw, ref, mask, action, g_selected, g_entropy, g_kl, grad);
+    const int grid = stride_grid(B * raw.rows * 32, PL_THREADS);
+    with_chunk(E, [&](auto ch) {
+        policy_learner_vjp_kernel<decltype(ch)::value><<<grid, PL_THREADS, 0, as_stream(stream)>>>(
+            B, E, raw, ref, mask, action, g_selected, g_entropy, g_kl, grad);
+    });
     return launch_status("policy_learner_backward");
 }
 

@@ -51,14 +51,15 @@ def parse():
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
-                                                 "readout", "reach", "showdown", "optimizer"),
+                                                 "readout", "reach", "showdown", "optimizer", "poker_loss"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
                         "the beta eigendecomposition of components.folded_statistics; posterior: one call of "
                         "components.posterior_sampler; readout: one launch of components.loss_readout; reach: "
                         "one launch of components.reach_update; showdown / optimizer: one call of "
-                        "components.showdown / components.optimizer_step) "
+                        "components.showdown / components.optimizer_step; poker_loss: one launch of the "
+                        "sampled batch of components.poker_loss) "
                         "between cudaProfilerStart/Stop (for ncu "
                         "--profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
@@ -306,8 +307,20 @@ def _poker_loss_inputs(device, S, W, E, M=2, seed=11):
 
 
 def _events_ms(device, fn, reps):
+    """Mean CUDA-event time (ms) of `fn` after two warm-up calls.  With PROFILE_ONE_FORWARD: one call
+    between cudaProfilerStart/Stop after the warm-ups (no timing)."""
+
     import torch
 
+    if PROFILE_ONE_FORWARD:
+        fn()
+        fn()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.start()
+        fn()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.stop()
+        return float("nan")
     for _ in range(2):
         fn()
     torch.cuda.synchronize(device)
@@ -399,6 +412,8 @@ def poker_loss_component(device, reps=10):
                 d["controls"], lw, posterior=d["post"], reference_raw=d["ref"])
 
         ms = _events_ms(device, run, reps)
+        if PROFILE_ONE_FORWARD:
+            return {}
         rows = S * W
         # bytes: raw + reference fields (2 x 40 B at M = 2), gradient out (40 B), old/adv/post/value/targets
         # and the value gradient (7 x 4 B), the mask row and action shared by a sigma row's columns
@@ -1209,7 +1224,7 @@ def main():
         PROFILE_ONE_FORWARD = True
         name = {"folded": "folded_component", "posterior": "posterior_component",
                 "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
-                "optimizer": "optimizer_component"}.get(
+                "optimizer": "optimizer_component", "poker_loss": "poker_loss_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         globals()[name](device)
         return
