@@ -30,6 +30,7 @@ from __future__ import annotations
 
 import argparse
 import inspect
+import json
 import math
 import os
 import sys
@@ -520,11 +521,12 @@ def gen_posterior(out):
     out["cases"] = np.array(len(cases))
 
 
-def gen_preflop_model(out):
+def gen_preflop_model(out, config=None, ranks=None, batch=3, tokens=8):
     """preflop.py:472-693 (PreflopEncoder.forward) with shared.py's trunk and readout, fp32 on CPU.
 
     The reference's accelerator guards (tensor_ops._accelerator, MHA.forward's device check) are
-    lifted for this run only; weights come from tests/golden/model_params.py by name.
+    lifted for this run only; weights come from tests/golden/model_params.py by name.  ``config`` /
+    ``ranks`` default to model_params.CONFIG / RANKS; both are recorded in the fixture.
     """
 
     import inspect
@@ -544,21 +546,26 @@ def gen_preflop_model(out):
     tensor_ops._accelerator = lambda value: None
     source = textwrap.dedent(inspect.getsource(primitives.MHA.forward))
     guard = 'if q.device.type not in ("cuda", "mps"):'
-    assert guard in source, "reference MHA.forward changed shape"
-    namespace: dict = {}
-    exec(compile(source.replace(guard, "if False:"), primitives.__file__, "exec"), primitives.__dict__, namespace)
-    primitives.MHA.forward = namespace["forward"]
+    if guard in source:  # (a previous generator in this run may have lifted it already)
+        namespace: dict = {}
+        exec(compile(source.replace(guard, "if False:"), primitives.__file__, "exec"), primitives.__dict__,
+             namespace)
+        primitives.MHA.forward = namespace["forward"]
 
-    cfg = PokerModelConfig(**model_params.CONFIG)
-    geometry = DeckGeometry(model_params.RANKS)
+    config = dict(model_params.CONFIG if config is None else config)
+    ranks = model_params.RANKS if ranks is None else ranks
+    cfg = PokerModelConfig(**config)
+    geometry = DeckGeometry(ranks)
     shared = SharedPokerParameters(cfg, geometry.n_cards)
     encoder = PreflopEncoder(cfg, geometry)
+    out["config_json"] = np.array(json.dumps(config))
+    out["ranks"] = np.array(ranks)
     with torch.no_grad():
         for module in (shared, encoder):
             for name, param in module.named_parameters():
                 param.copy_(torch.from_numpy(model_params.parameter(name, tuple(param.shape))))
     g = torch.Generator().manual_seed(2024)
-    batch, players, tokens = 3, 2, 8
+    players = 2
     k = geometry.n_classes
     history = PackedPublicHistory(
         actor=torch.randint(-1, players, (batch, tokens), generator=g),
@@ -625,7 +632,7 @@ def gen_preflop_model(out):
     out["class_overlap_scalars"] = _np(encoder.class_overlap_scalars)
 
 
-def gen_postflop_model(out):
+def gen_postflop_model(out, config=None, ranks=None):
     """postflop.py:538-784 (PostflopEncoder.forward) with shared.py's trunk and readout, fp32 on CPU.
 
     Three seats (one folded, so the folder context is live), a flop or turn board, the compact
@@ -656,10 +663,14 @@ def gen_postflop_model(out):
         exec(compile(source.replace(guard, "if False:"), primitives.__file__, "exec"), primitives.__dict__, namespace)
         primitives.MHA.forward = namespace["forward"]
 
-    cfg = PokerModelConfig(**model_params.POSTFLOP_CONFIG)
-    geometry = DeckGeometry(model_params.RANKS)
+    config = dict(model_params.POSTFLOP_CONFIG if config is None else config)
+    ranks = model_params.RANKS if ranks is None else ranks
+    cfg = PokerModelConfig(**config)
+    geometry = DeckGeometry(ranks)
     shared = SharedPokerParameters(cfg, geometry.n_cards)
     encoder = PostflopEncoder(cfg, geometry)
+    out["config_json"] = np.array(json.dumps(config))
+    out["ranks"] = np.array(ranks)
     with torch.no_grad():
         for module in (shared, encoder):
             for name, param in module.named_parameters():
@@ -705,7 +716,7 @@ def gen_postflop_model(out):
         history=history,
     )
     ranges = torch.rand((batch, players, hands), generator=g)
-    rank = 3
+    rank = max(3, cfg.folder_beta_rank)  # the encoder reads folder_beta_rank eigenpairs
     eigvec = torch.randn((batch, deck, rank), generator=g)
     summary = {
         "hand_log_ratio": torch.randn((batch, hands), generator=g) * 0.3,
@@ -1169,8 +1180,33 @@ def gen_poker_loss(out):
         out[pre + "weights"] = np.stack([_np(w) for w in weights])
 
 
+# the cfg2 architecture (d 128, 2 layers, 4 heads, M = 2, class embedding 32, FFN 512)
+# and the reference's default network (PokerModelConfig defaults: d 256, 8 heads, 6 layers), at 13 ranks
+CFG2_MODEL = dict(d_model=128, n_heads=4, layers=2, m_raise=2, k_act=5, max_players=2, class_embedding_dim=32,
+                  ffn_hidden=512, max_history_tokens=110, folder_beta_rank=16)
+DEFAULT_MODEL = dict(max_players=2)
+
+
+def gen_preflop_model_r13(out):
+    gen_preflop_model(out, CFG2_MODEL, 13, batch=2, tokens=16)
+
+
+def gen_preflop_model_default(out):
+    gen_preflop_model(out, DEFAULT_MODEL, 13, batch=2, tokens=16)
+
+
+def gen_postflop_model_r13(out):
+    gen_postflop_model(out, dict(CFG2_MODEL, max_players=3), 13)
+
+
+def gen_postflop_model_default(out):
+    gen_postflop_model(out, dict(DEFAULT_MODEL, max_players=3), 13)
+
+
 GENERATORS = {"posterior": gen_posterior, "preflop_model": gen_preflop_model, "postflop_model": gen_postflop_model,
-              "folded": gen_folded, "queued_model": gen_queued_model, "poker_loss": gen_poker_loss}
+              "folded": gen_folded, "queued_model": gen_queued_model, "poker_loss": gen_poker_loss,
+              "preflop_model_r13": gen_preflop_model_r13, "preflop_model_default": gen_preflop_model_default,
+              "postflop_model_r13": gen_postflop_model_r13, "postflop_model_default": gen_postflop_model_default}
 
 
 def main() -> None:

@@ -581,6 +581,39 @@ def test_adam_vector_and_scalar_apply_agree():
     torch.testing.assert_close(shifted.second, aligned.second, rtol=1e-6, atol=1e-15)
 
 
+@pytest.mark.parametrize("dtype,N", [(torch.float32, 5000), (torch.bfloat16, 992 * 40 + 77)])
+def test_loss_scale_and_global_mass_normaliser(dtype, N):
+    """Non-default loss controls: the objective weight x loss scale (training.py:403; here 2.5) and the
+    global decision-mass normaliser of the global-Z variant (inv_count = 1 / sum of every rank's weights,
+    here the local sum x 3.7 as if three more ranks' mass were added).  Both scale the gradient and the
+    totals linearly; checked against the double-precision oracle with the same controls and against the
+    default-control launch scaled by hand.  The bf16 size runs the staged bulk kernel."""
+
+    from pbg_b200.loss import LossConfig, fused_ppo_backward
+
+    A = 8
+    logits, mask, action, old, adv, weight = _loss_inputs(N, A, 23)
+    x = cuda(logits).to(dtype)
+    xs = host(x.float())
+    scale, inv = 2.5, 1.0 / (3.7 * float(weight.astype(np.float64).sum()))
+    cfg = LossConfig(0.2, 1.5, 0.01)
+    d, stats = fused_ppo_backward(x, cuda(mask), cuda(action), cuda(old), cuda(adv), cuda(weight), cfg,
+                                  scale=scale, inv_count=inv)
+    ref_d, ref_s = O.ppo_categorical(xs, mask, action, old, adv, weight, log_cap=math.log(1.5), scale=scale,
+                                     inv_count=inv)
+    near = _boundary_rows(xs, mask, action, old, 0.2, math.log(1.5))
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    peak = float(np.abs(ref_d).max())
+    _assert_close_except_boundary(host(d.float()), ref_d, near, rtol=tol, atol=tol * peak)
+    np.testing.assert_allclose(host(stats)[[0, 1, 2]], ref_s[[0, 1, 2]], rtol=10 * tol, atol=1e-9 * N)
+    # linearity against the default controls (1 / N, scale 1)
+    d1, s1 = fused_ppo_backward(x, cuda(mask), cuda(action), cuda(old), cuda(adv), cuda(weight), cfg)
+    factor = scale * inv * N
+    ok = np.isclose(host(d.float()), host(d1.float()) * factor, rtol=tol, atol=tol * peak)
+    assert ok.mean() > 0.999
+    np.testing.assert_allclose(host(stats)[0], host(s1)[0] * factor, rtol=1e-4)
+
+
 def test_bulk_staged_path_wraps_the_ring_and_handles_the_tail():
     """694,733 rows: 700 full 992-row tiles (several passes of the 4-stage ring per CTA) + 333 tail rows."""
 

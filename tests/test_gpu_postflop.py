@@ -1,7 +1,8 @@
 """The compact postflop policy/value network on this build's kernels against the reference module itself.
 
-tests/golden/postflop_model.npz holds the reference PostflopEncoder's fp32 outputs (run on CPU by
-tests/golden/make_golden.py): three seats with one folded (so the folded-seat summary and the folder
+tests/golden/postflop_model*.npz hold the reference PostflopEncoder's fp32 outputs (run on CPU by
+tests/golden/make_golden.py) at three configurations (d128 / 2 layers at 4 ranks; the cfg2 network
+and the reference's default network at 13 ranks): three seats with one folded (so the folded-seat summary and the folder
 context are live), flop and turn boards, the board-compatible compact rows, random evaluator-summary
 fields and fold-line features, weights drawn by tests/golden/model_params.py from the parameter
 names.  This build runs the same weights in bf16 on the tensor cores (fp32 accumulation, fp32
@@ -31,11 +32,18 @@ def _params(d):
     return params
 
 
-def _model(params):
+def _model(params, d=None):
+    """The network of a fixture: its recorded configuration and rank count (the small default
+    fixture predates the record and uses model_params.POSTFLOP_CONFIG at model_params.RANKS)."""
+
+    import json
+
     import model_params
     from pbg_b200.postflop import PostflopModel
     from pbg_b200.preflop import PreflopConfig
 
+    if d is not None and "config_json" in d:
+        return PostflopModel(PreflopConfig(**json.loads(str(d["config_json"]))), int(d["ranks"]), params, DEV)
     return PostflopModel(PreflopConfig(**model_params.POSTFLOP_CONFIG), model_params.RANKS, params, DEV)
 
 
@@ -57,9 +65,14 @@ def _worst(raw, value, d):
     return diffs
 
 
-def test_postflop_forward_matches_reference_module(gold):
-    d = gold("postflop_model")
-    model = _model(_params(d))
+@pytest.mark.parametrize("fixture", ["postflop_model", "postflop_model_r13", "postflop_model_default"])
+def test_postflop_forward_matches_reference_module(gold, fixture):
+    """d128 / 2 layers at 4 ranks; the cfg2 network (d128, 2 layers, 4 heads, M = 2, FFN 512) and the
+    reference's default network (d256, 8 heads, 6 layers) at 13 ranks, whose 3 x ~1,176 compact rows per
+    decision run the attention kernel's multi-tile and tail paths."""
+
+    d = gold(fixture)
+    model = _model(_params(d), d)
     pub, ranges, masks = _inputs(d)
     raw, value = model.forward(pub, ranges, None, masks)
     torch.cuda.synchronize()

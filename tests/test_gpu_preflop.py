@@ -1,6 +1,7 @@
 """The preflop policy/value network on this build's kernels against the reference module itself.
 
-tests/golden/preflop_model.npz holds the reference PreflopEncoder's fp32 outputs (run on CPU by
+tests/golden/preflop_model*.npz hold the reference PreflopEncoder's fp32 outputs at three
+configurations (d128 / 2 layers at 4 ranks; the cfg2 network and the default network at 13 ranks) (run on CPU by
 tests/golden/make_golden.py) for seeded public batches and ranges, with weights drawn by
 tests/golden/model_params.py from the parameter names; this build runs the same weights in bf16
 on the tensor cores (fp32 accumulation, fp32 residual stream).  Tolerance: the bf16 bar, rtol and
@@ -21,6 +22,11 @@ sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
 
 
 def _model(d):
+    """The network of a fixture: its recorded configuration and rank count (the small default fixture
+    predates the record and uses model_params.CONFIG at model_params.RANKS)."""
+
+    import json
+
     import model_params
     from pbg_b200.preflop import PreflopConfig, PreflopModel
 
@@ -29,7 +35,11 @@ def _model(d):
         name, dims = str(item).split(":")
         shape = tuple(int(x) for x in dims.split(","))
         params[name] = torch.from_numpy(model_params.parameter(name, shape))
-    return PreflopModel(PreflopConfig(**model_params.CONFIG), model_params.RANKS, params, DEV), params
+    if "config_json" in d:
+        cfg, ranks = PreflopConfig(**json.loads(str(d["config_json"]))), int(d["ranks"])
+    else:
+        cfg, ranks = PreflopConfig(**model_params.CONFIG), model_params.RANKS
+    return PreflopModel(cfg, ranks, params, DEV), params
 
 
 def _pub(d):
@@ -38,8 +48,12 @@ def _pub(d):
     return pub
 
 
-def test_preflop_forward_matches_reference_module(gold):
-    d = gold("preflop_model")
+@pytest.mark.parametrize("fixture", ["preflop_model", "preflop_model_r13", "preflop_model_default"])
+def test_preflop_forward_matches_reference_module(gold, fixture):
+    """d128 / 2 layers at 4 ranks; the cfg2 network and the reference's default network (d256, 8 heads,
+    6 layers) at 13 ranks (169 class rows per seat, 2 x 169 + public + history + anchor tokens)."""
+
+    d = gold(fixture)
     model, _ = _model(d)
     raw, value = model.forward(_pub(d), torch.from_numpy(d["class_ranges"]).to(DEV),
                                torch.from_numpy(d["class_mask"]).to(DEV))
