@@ -84,6 +84,10 @@ __device__ __forceinline__ void multimem_st(float* addr, const float4& v) {
                  : "memory");
 }
 
+// Each thread walks its vectors of the rank's slice in rounds of NVLS_UNROLL, software-pipelined:
+// the multimem loads of round k+1 are issued before the multicast stores of round k, so this GPU's
+// outbound NVLink traffic (the switch gathering every copy for the reductions) overlaps its inbound
+// traffic (the switch delivering other ranks' reduced slices) instead of running as two phases.
 __global__ void __launch_bounds__(NVLS_THREADS) nvls_sum_kernel(int64_t n, float* mc, uint32_t* const* pads, int rank,
                                                                 int world, uint32_t* error) {
     if (*reinterpret_cast<volatile uint32_t*>(error) != 0u) return;  // an earlier call failed: stay off
@@ -91,16 +95,33 @@ __global__ void __launch_bounds__(NVLS_THREADS) nvls_sum_kernel(int64_t n, float
     const int64_t slice = n / world;  // multiple of 4 floats by contract
     const int64_t v0 = (int64_t)rank * slice / 4, vn = slice / 4;
     const int64_t stride = (int64_t)gridDim.x * NVLS_THREADS;
-    int64_t i = (int64_t)blockIdx.x * NVLS_THREADS + threadIdx.x;
     constexpr int U = NVLS_UNROLL;  // independent multimem loads in flight per thread
-    for (; i + (U - 1) * stride < vn; i += U * stride) {
-        float4 v[U];
-        #pragma unroll
-        for (int u = 0; u < U; ++u) v[u] = multimem_ld_reduce_add(mc + 4 * (v0 + i + u * stride));
-        #pragma unroll
-        for (int u = 0; u < U; ++u) multimem_st(mc + 4 * (v0 + i + u * stride), v[u]);
+    int64_t i = (int64_t)blockIdx.x * NVLS_THREADS + threadIdx.x;
+    float4 cur[U];
+    bool have[U];
+    #pragma unroll
+    for (int u = 0; u < U; ++u) {
+        have[u] = i + u * stride < vn;
+        if (have[u]) cur[u] = multimem_ld_reduce_add(mc + 4 * (v0 + i + u * stride));
     }
-    for (; i < vn; i += stride) multimem_st(mc + 4 * (v0 + i), multimem_ld_reduce_add(mc + 4 * (v0 + i)));
+    for (; i < vn; i += U * stride) {
+        const int64_t nx = i + U * stride;
+        float4 nxt[U];
+        bool nhave[U];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            nhave[u] = nx + u * stride < vn;
+            if (nhave[u]) nxt[u] = multimem_ld_reduce_add(mc + 4 * (v0 + nx + u * stride));
+        }
+        #pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (have[u]) multimem_st(mc + 4 * (v0 + i + u * stride), cur[u]);
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            cur[u] = nxt[u];
+            have[u] = nhave[u];
+        }
+    }
     __syncthreads();
     rank_barrier(pads, rank, world, 1, error);
 }
@@ -120,10 +141,10 @@ int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pa
     PBG_REQUIRE(n > 0 && n % (4 * world) == 0, "nvls_sum: n must be a positive multiple of 4*world");
     PBG_REQUIRE(multicast && signal_pads && error, "nvls_sum: null argument");
     PBG_REQUIRE(((uintptr_t)multicast % 16) == 0, "nvls_sum: multicast address must be 16-byte aligned");
-    // as many SMs issuing multimem requests as the slice allows (one float4 per thread
-    // at least), capped at one CTA per SM and by the barrier slots the pad holds
+    // as many SMs issuing multimem requests as the slice allows (one round of NVLS_UNROLL
+    // float4 per thread at least), capped at one CTA per SM and by the barrier slots the pad holds
     int64_t vn = n / world / 4;
-    int64_t want = (vn + NVLS_THREADS - 1) / NVLS_THREADS;
+    int64_t want = (vn + (int64_t)NVLS_THREADS * NVLS_UNROLL - 1) / ((int64_t)NVLS_THREADS * NVLS_UNROLL);
     int cap = sm_count() < NVLS_MAX_BLOCKS ? sm_count() : NVLS_MAX_BLOCKS;
     int64_t fit = pad_bytes / (2 * (int64_t)world * (int64_t)sizeof(uint32_t));  // barrier slots the pad holds
     PBG_REQUIRE(fit >= 1, "nvls_sum: signal pad of %lld bytes is too small", (long long)pad_bytes);

@@ -11,6 +11,8 @@ ranks is recovered as 1 - MAX(1 - active).
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 from torch import Tensor
@@ -176,6 +178,27 @@ class NVLSFlatSum:
                 self._host_error.copy_(self.error, non_blocking=True)
                 self._copied.record(s)
         return self.buffer
+
+    def sum_range_(self, start: int, count: int, stream=None) -> torch.Tensor:
+        """In-place SUM of ``buffer[start:start + count]`` (a bucket; both multiples of 4 * world).
+
+        Buckets go through the same signal pads, so launch them on ONE stream (in the same order on
+        every rank); a bucket may start while other work on this GPU is still running.
+        """
+
+        from ._native import call, ptr
+
+        if start % (4 * self.world) or count % (4 * self.world) or count <= 0 or start + count > self.numel:
+            raise ValueError("NVLS bucket bounds must be positive multiples of 4 * world_size inside the buffer")
+        s = torch.cuda.current_stream() if stream is None else stream
+        mc = ctypes.c_void_p(self.multicast.value + 4 * start)
+        call("pbg_nvls_allreduce_sum_f32", count, mc, self.pads, self.pad_bytes, self.rank, self.world,
+             ptr(self.error), ctypes_stream(s))
+        if not torch.cuda.is_current_stream_capturing():
+            with torch.cuda.stream(s):
+                self._host_error.copy_(self.error, non_blocking=True)
+                self._copied.record(s)
+        return self.buffer[start:start + count]
 
     def raise_if_failed(self) -> None:
         """Raise if an earlier sum_() reported a barrier timeout (no host sync).

@@ -7,10 +7,12 @@ with the lowest index forced legal in empty rows, the taken action drawn
 from the legal set with the counter RNG (LEARNER purpose), old log pi from
 logits + N(0,0.1), advantages N(0,1), decision-mass weights U(0,1).  One
 step = the fused masked log-softmax / clipped-ratio / entropy / dlogits
-kernel over all rows, then (N > 1) the SUM all-reduce of a flat fp32
-gradient buffer of --params parameters (libpbgb200's NVLS multimem kernel on
-symmetric memory; NCCL when the fabric has no multicast).  Weak scaling: each
-rank owns its own rows.
+kernel over all rows and (N > 1) the SUM all-reduce of a flat fp32 gradient
+buffer of --params parameters (libpbgb200's NVLS multimem kernel on symmetric
+memory from 4 ranks; NCCL at 2 ranks or when the fabric has no multicast).  At
+N > 1 the rows run as --buckets chunks and the SUM as as many buckets on a
+second stream, bucket k starting when chunk k is done, so the SUM overlaps the
+remaining loss.  Weak scaling: each rank owns its own rows.
 
 ``--impl reference`` times the CPU restatement of the same loss on the same
 rows (the reference has no CPU execution path) on all host threads.  The
@@ -50,6 +52,11 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--allreduce", choices=("auto", "nvls", "nccl"), default="auto",
+                   help="gradient SUM at N > 1: auto = libpbgb200's NVLS kernel from 4 ranks, NCCL below")
+    p.add_argument("--buckets", type=int, default=4,
+                   help="N > 1: the rows' loss runs as this many chunks, and the gradient SUM as as many buckets "
+                        "on a second stream, bucket k starting when chunk k's loss is done")
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
                                                  "readout", "reach", "showdown", "optimizer", "poker_loss"),
                    default=None,
@@ -1248,8 +1255,8 @@ def main():
         from pbg_b200.distributed import NVLSFlatSum
 
         try:
-            if world < 4:
-                raise RuntimeError("two ranks: NCCL ring")
+            if args.allreduce == "nccl" or (args.allreduce == "auto" and world < 4):
+                raise RuntimeError("NCCL ring (two ranks, or requested)")
             flat = NVLSFlatSum(args.params, device)
             grad = flat.buffer
             allreduce_kind = "NVLS multimem SUM (libpbgb200)"
@@ -1262,56 +1269,104 @@ def main():
     bound = op.bind(logits, mask, action, old, adv, weight, dlogits)
     bound.launch(stream)  # one-time device set-up happens outside any capture
     torch.cuda.synchronize(device)
-    # Steps are replayed from CUDA graphs over fixed buffers so host launch cost never gaps the
-    # device: one graph for the loss kernel and, at N > 1 with NVLS, one for the gradient SUM
-    # (NCCL, when used, stays eager).
+    # The loss kernel alone, replayed from a CUDA graph over fixed buffers (host launch cost never gaps
+    # the device): the whole step at N = 1, and the roofline timing at every N.
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         bound.launch()
+    torch.cuda.synchronize(device)
+    # N > 1: the loss runs as `buckets` row chunks and the flat gradient SUM as as many buckets on a
+    # second stream, bucket k starting when chunk k is done (the way a backward hands finished gradient
+    # buckets to the collective while it still computes), so the SUM overlaps the remaining loss.
+    buckets = max(1, args.buckets) if world > 1 else 1
+    if world > 1 and (N % buckets or args.params % (4 * world * buckets)):
+        buckets = 1
+    chunk_ops, chunk_binds = [], []
+    rows_b, params_b = N // buckets, args.params // buckets
+    if buckets > 1:
+        for k in range(buckets):
+            lo, hi = k * rows_b, (k + 1) * rows_b
+            chunk = FusedPPOBackward(rows_b, A, device, op.config)
+            chunk.set_controls(inv_count=1.0 / N)
+            chunk_ops.append(chunk)
+            chunk_binds.append(chunk.bind(logits[lo:hi], mask[lo:hi], action[lo:hi], old[lo:hi], adv[lo:hi],
+                                          weight[lo:hi], dlogits[lo:hi]))
+            chunk_binds[-1].launch(stream)
+    comm = torch.cuda.Stream(device) if world > 1 else None
+    done = [torch.cuda.Event() for _ in range(buckets)]
+
+    def overlapped_step():
+        main = torch.cuda.current_stream(device)
+        comm.wait_stream(main)
+        for k in range(buckets):
+            if buckets > 1:
+                chunk_binds[k].launch(main)
+            else:
+                bound.launch(main)
+            done[k].record(main)
+            comm.wait_event(done[k])
+            if flat is not None:
+                flat.sum_range_(k * params_b, params_b, comm)
+            else:
+                with torch.cuda.stream(comm):
+                    dist.all_reduce(grad[k * params_b:(k + 1) * params_b], op=dist.ReduceOp.SUM)
+        main.wait_stream(comm)
+
+    step_graph = None
+    if flat is not None:
+        overlapped_step()  # warm once outside capture
+        torch.cuda.synchronize(device)
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(step_graph):
+            overlapped_step()
     sum_graph = None
     if flat is not None:
-        flat.sum_(stream)  # warm once outside capture
-        torch.cuda.synchronize(device)
         sum_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(sum_graph):
             flat.sum_()
     torch.cuda.synchronize(device)
 
     def step(events=None):
-        if events is not None:
-            events[0].record(stream)
-        graph.replay()
-        if events is not None:
-            events[1].record(stream)
-        if world > 1:
-            if sum_graph is not None:
-                sum_graph.replay()
-            else:
-                dist.all_reduce(grad, op=dist.ReduceOp.SUM)
+        if world == 1:
+            graph.replay()
+        elif step_graph is not None:
+            step_graph.replay()
+        else:
+            overlapped_step()
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
-    kernel_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                     for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         time.sleep(0.3)
         torch.cuda.synchronize(device)
         start.record(stream)
         for i in range(args.steps):
-            step(kernel_events[i])
+            step()
         end.record(stream)
         torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
-    if float(op.stats[7]) != N:
-        raise RuntimeError("loss kernel reported a failed launch (stats rows != N)")
+    for chunk, rows in ([(c, rows_b) for c in chunk_ops] if buckets > 1 else [(op, N)]):
+        if float(chunk.stats[7]) != rows:
+            raise RuntimeError("loss kernel reported a failed launch (stats rows != rows)")
     if flat is not None:
         flat.check()
     elapsed_ms = start.elapsed_time(end)
+    # the loss kernel alone over all rows (its own events per launch, on the launching stream): the roofline
+    kernel_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                     for _ in range(args.steps)]
+    torch.cuda.synchronize(device)
+    for a, b in kernel_events:
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+    torch.cuda.synchronize(device)
+    if float(op.stats[7]) != N:
+        raise RuntimeError("loss kernel reported a failed launch (stats rows != N)")
     kernel_ms = sum(a.elapsed_time(b) for a, b in kernel_events) / args.steps
     if world > 1:
         t = torch.tensor([elapsed_ms, kernel_ms], device=device, dtype=torch.float64)
@@ -1398,14 +1453,17 @@ def main():
                    "rows_per_rank": N, "actions": A, "grad_params": args.params,
                    "allreduce": allreduce_kind,
                    "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}",
-                   "launch": "CUDA graph replay" + (" (loss kernel, then NVLS SUM kernel)" if flat is not None else
-                                                     " (loss kernel)" + (", NCCL eager" if world > 1 else ""))},
+                   "buckets": buckets,
+                   "launch": ("CUDA graph replay (loss kernel)" if world == 1 else
+                              f"{buckets} loss chunks on the main stream, {buckets} gradient-SUM buckets on a second "
+                              "stream, bucket k after chunk k" + (" (one CUDA graph)" if step_graph is not None
+                                                                   else " (eager, NCCL)"))},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": committed_traffic(N),
                      "kernel": "ppo_bf16x8_bulk_kernel", "kernel_ms": kernel_ms, "peak_kind": peak_kind,
                      "algorithmic_bytes": algo_bytes},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (1 if world == 1 else buckets * (2 if flat is not None else 1)),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -1442,7 +1500,7 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        del sum_graph, flat, grad
+        del step_graph, sum_graph, flat, grad
         torch.cuda.synchronize(device)
         dist.barrier()
         dist.destroy_process_group()

@@ -4,7 +4,8 @@ Runs as child processes (one per GPU, NCCL process group) at 2, 4 and 8 ranks,
 each case skipped when the machine has fewer GPUs.  Each rank fills the
 symmetric buffer with its own seeded gradient, sums it twice in a row through
 pbg_nvls_allreduce_sum_f32 and compares with NCCL on the same data and with a
-float64 sum of every rank's input.  At two ranks a + b is exact in either
+float64 sum of every rank's input, then sums a third gradient as four buckets
+launched back to back on a side stream (``NVLSFlatSum.sum_range_``).  At two ranks a + b is exact in either
 order, so the NVLS result must equal NCCL's bit for bit; at 4 and 8 ranks the
 switch and NCCL add in different orders, so both are held to the float64 sum
 within fp32 rounding of a W-term sum (rtol 4e-6 plus an absolute term scaled
@@ -68,6 +69,24 @@ def _worker(rank, world, port, queue):
                 "nccl_ok": bool((nccl_err <= bound).all()),
                 "nvls_max_err": float(nvls_err.max()),
             })
+        # four buckets summed one after another on a side stream (the bench's overlapped step)
+        inputs = [torch.randn(n, generator=torch.Generator(device=device).manual_seed(300 + r), device=device)
+                  for r in range(world)]
+        flat.buffer.copy_(inputs[rank])
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        q = n // 4
+        for k in range(4):
+            flat.sum_range_(k * q, q, side)
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        flat.check()
+        exact = torch.stack(inputs).double().sum(0)
+        scale = torch.stack(inputs).double().abs().sum(0)
+        bound = 4e-6 * exact.abs() + 2.0 * world * 2.0 ** -24 * scale
+        two_term = world != 2 or bool(torch.equal(flat.buffer, inputs[0] + inputs[1]))  # a + b: exact in fp32
+        results.append({"equal_nccl": two_term, "nvls_ok": bool(((flat.buffer.double() - exact).abs() <= bound).all()),
+                        "nccl_ok": True, "nvls_max_err": float((flat.buffer.double() - exact).abs().max())})
         # a set error word keeps every later launch off the buffer and the pads
         before = flat.buffer.clone()
         flat.error.fill_(1)
