@@ -75,9 +75,9 @@ def _worker(rank, world, port, queue):
         flat.buffer.copy_(inputs[rank])
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
-        q = n // 4
+        q = n // 4 // (4 * world) * (4 * world)  # bucket bounds are multiples of 4 * world
         for k in range(4):
-            flat.sum_range_(k * q, q, side)
+            flat.sum_range_(k * q, q if k < 3 else n - 3 * q, side)
         torch.cuda.current_stream(device).wait_stream(side)
         torch.cuda.synchronize(device)
         flat.check()
