@@ -135,8 +135,9 @@ extern "C" {
 // Signal-pad bytes one CTA needs per rank of the group (two barrier phases).
 int64_t pbg_nvls_signal_bytes(void) { return (int64_t)2 * NVLS_MAX_WORLD * sizeof(uint32_t); }
 
-int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pads, int64_t pad_bytes, int32_t rank,
-                               int32_t world, uint32_t* error, void* stream) {
+int pbg_nvls_allreduce_sum_f32_grid(int64_t n, void* multicast, const void* signal_pads, int64_t pad_bytes,
+                                    int32_t rank, int32_t world, uint32_t* error, int32_t max_ctas, void* stream) {
+    PBG_REQUIRE(max_ctas >= 0, "nvls_sum: max_ctas must be >= 0 (0 = no cap)");
     PBG_REQUIRE(world >= 2 && world <= NVLS_MAX_WORLD && rank >= 0 && rank < world, "nvls_sum: bad rank/world");
     PBG_REQUIRE(n > 0 && n % (4 * world) == 0, "nvls_sum: n must be a positive multiple of 4*world");
     PBG_REQUIRE(multicast && signal_pads && error, "nvls_sum: null argument");
@@ -149,11 +150,17 @@ int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pa
     int64_t fit = pad_bytes / (2 * (int64_t)world * (int64_t)sizeof(uint32_t));  // barrier slots the pad holds
     PBG_REQUIRE(fit >= 1, "nvls_sum: signal pad of %lld bytes is too small", (long long)pad_bytes);
     if (fit < cap) cap = (int)fit;
+    if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;  // leave SMs to concurrent work
     int blocks = (int)(want < cap ? want : cap);
     if (blocks < 1) blocks = 1;
     nvls_sum_kernel<<<blocks, NVLS_THREADS, 0, as_stream(stream)>>>(n, (float*)multicast, (uint32_t* const*)signal_pads,
                                                                     rank, world, error);
     return launch_status("nvls_allreduce_sum_f32");
+}
+
+int pbg_nvls_allreduce_sum_f32(int64_t n, void* multicast, const void* signal_pads, int64_t pad_bytes, int32_t rank,
+                               int32_t world, uint32_t* error, void* stream) {
+    return pbg_nvls_allreduce_sum_f32_grid(n, multicast, signal_pads, pad_bytes, rank, world, error, 0, stream);
 }
 
 }  // extern "C"

@@ -997,10 +997,11 @@ int64_t pbg_ppo_partials_size(int64_t N, int32_t A) {
     return 1 + (int64_t)ppo_grid(N > 0 ? N : 1) * LOSS_STATS;
 }
 
-int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void* logits, const uint8_t* mask,
-                                 const int32_t* action, const float* old_logp, const float* adv,
-                                 const float* weight, const float* controls, void* dlogits, double* partials,
-                                 double* stats, void* stream) {
+int pbg_ppo_categorical_backward_grid(int64_t N, int32_t A, int32_t dtype, const void* logits, const uint8_t* mask,
+                                      const int32_t* action, const float* old_logp, const float* adv,
+                                      const float* weight, const float* controls, void* dlogits, double* partials,
+                                      double* stats, int32_t max_ctas, void* stream) {
+    PBG_REQUIRE(max_ctas >= 0, "ppo: max_ctas must be >= 0 (0 = no cap)");
     PBG_REQUIRE(N >= 0 && A >= 1 && A <= LOSS_MAX_A, "ppo: need N >= 0 and A in [1,32]");
     PBG_REQUIRE(dtype == 0 || dtype == 1, "ppo: dtype must be 0 (fp32) or 1 (bf16)");
     PBG_REQUIRE(controls && partials && stats, "ppo: null controls or scratch");
@@ -1025,6 +1026,7 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
         }
         int64_t tiles = N / BULK_T;
         int bgrid = (int)(tiles < sm_count() ? tiles : sm_count());
+        if (max_ctas > 0 && bgrid > max_ctas) bgrid = max_ctas;  // leave SMs to concurrent work
         BulkArgs a{N, (const uint4*)logits, (const uint2*)mask, action, old_logp, adv, weight, controls,
                    (uint4*)dlogits, partials, stats};
         ppo_bf16x8_bulk_kernel<<<bgrid, BULK_THREADS, BULK_SMEM, s>>>(a);
@@ -1040,6 +1042,14 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
                                                               weight, controls, (float*)dlogits, partials, stats);
     }
     return launch_status("ppo_categorical_backward");
+}
+
+int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void* logits, const uint8_t* mask,
+                                 const int32_t* action, const float* old_logp, const float* adv,
+                                 const float* weight, const float* controls, void* dlogits, double* partials,
+                                 double* stats, void* stream) {
+    return pbg_ppo_categorical_backward_grid(N, A, dtype, logits, mask, action, old_logp, adv, weight, controls,
+                                             dlogits, partials, stats, 0, stream);
 }
 
 int64_t pbg_ppo_readout_partials_size(int64_t N, int32_t A, int32_t d) {

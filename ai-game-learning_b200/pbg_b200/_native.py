@@ -107,6 +107,8 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_reach_update": (_I32, [G, _I64, S, Pol, _P, _P, _P, _P]),
     "pbg_ppo_partials_size": (_I64, [_I64, _I32]),
     "pbg_ppo_categorical_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_ppo_categorical_backward_grid": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32,
+                                                 _P]),
     "pbg_ppo_categorical_backward_noalloc": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_ppo_readout_partials_size": (_I64, [_I64, _I32, _I32]),
     "pbg_ppo_readout_backward": (_I32, [_I64, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P]),
@@ -133,6 +135,7 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_layernorm": (_I32, [_I64, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _I32, _I64, _P]),
     "pbg_nvls_signal_bytes": (_I64, []),
     "pbg_nvls_allreduce_sum_f32": (_I32, [_I64, _P, _P, _I64, _I32, _I32, _P, _P]),
+    "pbg_nvls_allreduce_sum_f32_grid": (_I32, [_I64, _P, _P, _I64, _I32, _I32, _P, _I32, _P]),
     "pbg_adam_partials_size": (_I64, [_I64]),
     "pbg_adam_step": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P]),
 }

@@ -179,11 +179,12 @@ class NVLSFlatSum:
                 self._copied.record(s)
         return self.buffer
 
-    def sum_range_(self, start: int, count: int, stream=None) -> torch.Tensor:
+    def sum_range_(self, start: int, count: int, stream=None, max_ctas: int = 0) -> torch.Tensor:
         """In-place SUM of ``buffer[start:start + count]`` (a bucket; both multiples of 4 * world).
 
         Buckets go through the same signal pads, so launch them on ONE stream (in the same order on
-        every rank); a bucket may start while other work on this GPU is still running.
+        every rank); a bucket may start while other work on this GPU is still running.  ``max_ctas``
+        > 0 caps the kernel's grid, so it runs beside compute that holds the other SMs.
         """
 
         from ._native import call, ptr
@@ -192,8 +193,8 @@ class NVLSFlatSum:
             raise ValueError("NVLS bucket bounds must be positive multiples of 4 * world_size inside the buffer")
         s = torch.cuda.current_stream() if stream is None else stream
         mc = ctypes.c_void_p(self.multicast.value + 4 * start)
-        call("pbg_nvls_allreduce_sum_f32", count, mc, self.pads, self.pad_bytes, self.rank, self.world,
-             ptr(self.error), ctypes_stream(s))
+        call("pbg_nvls_allreduce_sum_f32_grid", count, mc, self.pads, self.pad_bytes, self.rank, self.world,
+             ptr(self.error), int(max_ctas), ctypes_stream(s))
         if not torch.cuda.is_current_stream_capturing():
             with torch.cuda.stream(s):
                 self._host_error.copy_(self.error, non_blocking=True)

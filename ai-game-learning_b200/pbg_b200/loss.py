@@ -72,10 +72,13 @@ class FusedPPOBackward:
              stream(logits.device))
         return dlogits, self.stats
 
-    def bind(self, logits, mask, action, old_logp, advantage, weight, dlogits) -> BoundPPOBackward:
+    def bind(self, logits, mask, action, old_logp, advantage, weight, dlogits, *, max_ctas: int = 0
+             ) -> BoundPPOBackward:
+        """``max_ctas`` > 0 caps the persistent kernel's grid (SMs left to a collective on another stream)."""
+
         if tuple(logits.shape) != (self.rows, self.actions) or dlogits.shape != logits.shape:
             raise ValueError("loss rows/actions differ from the admitted shape")
-        return BoundPPOBackward(self, logits, mask, action, old_logp, advantage, weight, dlogits)
+        return BoundPPOBackward(self, logits, mask, action, old_logp, advantage, weight, dlogits, max_ctas)
 
 
 class BoundPPOBackward:
@@ -87,7 +90,8 @@ class BoundPPOBackward:
     so one-time device set-up happens outside the capture).
     """
 
-    def __init__(self, op: "FusedPPOBackward", logits, mask, action, old_logp, advantage, weight, dlogits):
+    def __init__(self, op: "FusedPPOBackward", logits, mask, action, old_logp, advantage, weight, dlogits,
+                 max_ctas: int = 0):
         N, A = logits.shape
         tensors = (logits, mask.view(torch.uint8) if mask.dtype == torch.bool else mask, action, old_logp,
                    advantage, weight, op.controls, dlogits, op.partials, op.stats)
@@ -95,8 +99,9 @@ class BoundPPOBackward:
             if not (t.is_cuda and t.is_contiguous()):
                 raise ValueError("bound loss buffers must be contiguous CUDA tensors")
         self._keep = tensors
-        self._fn = lib().pbg_ppo_categorical_backward
-        self._args = (N, A, 1 if logits.dtype == torch.bfloat16 else 0, *(ctypes.c_void_p(t.data_ptr()) for t in tensors))
+        self._fn = lib().pbg_ppo_categorical_backward_grid
+        self._args = (N, A, 1 if logits.dtype == torch.bfloat16 else 0, *(ctypes.c_void_p(t.data_ptr()) for t in tensors),
+                      int(max_ctas))
         self.stats = op.stats
         self.dlogits = dlogits
 
@@ -104,7 +109,7 @@ class BoundPPOBackward:
         s = torch.cuda.current_stream() if stream is None else stream
         rc = self._fn(*self._args, ctypes.c_void_p(s.cuda_stream))
         if rc != 0:
-            check(rc, "pbg_ppo_categorical_backward")
+            check(rc, "pbg_ppo_categorical_backward_grid")
 
 
 class FusedPPOReadoutBackward:

@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--allreduce", choices=("auto", "nvls", "nccl"), default="auto",
                    help="gradient SUM at N > 1: auto = libpbgb200's NVLS kernel from 4 ranks, NCCL below")
+    p.add_argument("--comm-sms", type=int, default=16,
+                   help="N > 1 with buckets: SMs reserved for the gradient SUM (the loss kernel runs on the rest)")
     p.add_argument("--buckets", type=int, default=4,
                    help="N > 1: the rows' loss runs as this many chunks, and the gradient SUM as as many buckets "
                         "on a second stream, bucket k starting when chunk k's loss is done")
@@ -1283,6 +1285,11 @@ def main():
         buckets = 1
     chunk_ops, chunk_binds = [], []
     rows_b, params_b = N // buckets, args.params // buckets
+    # the persistent loss kernel holds every register of an SM, so nothing shares an SM it runs on:
+    # with buckets the SUM gets `comm_sms` SMs of its own and the loss chunks the rest
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    comm_ctas = max(1, min(args.comm_sms, sms // 2)) if buckets > 1 else 0
+    loss_ctas = sms - comm_ctas if buckets > 1 else 0
     if buckets > 1:
         for k in range(buckets):
             lo, hi = k * rows_b, (k + 1) * rows_b
@@ -1290,7 +1297,7 @@ def main():
             chunk.set_controls(inv_count=1.0 / N)
             chunk_ops.append(chunk)
             chunk_binds.append(chunk.bind(logits[lo:hi], mask[lo:hi], action[lo:hi], old[lo:hi], adv[lo:hi],
-                                          weight[lo:hi], dlogits[lo:hi]))
+                                          weight[lo:hi], dlogits[lo:hi], max_ctas=loss_ctas))
             chunk_binds[-1].launch(stream)
     comm = torch.cuda.Stream(device) if world > 1 else None
     done = [torch.cuda.Event() for _ in range(buckets)]
@@ -1306,7 +1313,7 @@ def main():
             done[k].record(main)
             comm.wait_event(done[k])
             if flat is not None:
-                flat.sum_range_(k * params_b, params_b, comm)
+                flat.sum_range_(k * params_b, params_b, comm, max_ctas=comm_ctas)
             else:
                 with torch.cuda.stream(comm):
                     dist.all_reduce(grad[k * params_b:(k + 1) * params_b], op=dist.ReduceOp.SUM)
@@ -1453,7 +1460,7 @@ def main():
                    "rows_per_rank": N, "actions": A, "grad_params": args.params,
                    "allreduce": allreduce_kind,
                    "l2": "inputs larger than L2 (235 MB per pass)", "parallelism": f"dp{world}",
-                   "buckets": buckets,
+                   "buckets": buckets, "comm_sms": comm_ctas,
                    "launch": ("CUDA graph replay (loss kernel)" if world == 1 else
                               f"{buckets} loss chunks on the main stream, {buckets} gradient-SUM buckets on a second "
                               "stream, bucket k after chunk k" + (" (one CUDA graph)" if step_graph is not None

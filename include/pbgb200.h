@@ -332,6 +332,16 @@ int pbg_ppo_categorical_backward(int64_t N, int32_t A, int32_t dtype, const void
                                  const float *controls, void *dlogits, double *partials,
                                  double *stats, void *stream);
 
+/* pbg_ppo_categorical_backward with the persistent kernel's grid capped at
+ * max_ctas thread blocks (0 = one per SM), so that a collective launched on
+ * another stream keeps SMs of its own while the loss runs.  The loss kernel
+ * fills every register of an SM, so nothing else shares an SM it holds. */
+int pbg_ppo_categorical_backward_grid(int64_t N, int32_t A, int32_t dtype, const void *logits,
+                                      const uint8_t *mask, const int32_t *action,
+                                      const float *old_logp, const float *adv, const float *weight,
+                                      const float *controls, void *dlogits, double *partials,
+                                      double *stats, int32_t max_ctas, void *stream);
+
 /* The loss backward above fused with the gradient of the readout that
  * produced the logits, x = W h + b (pbg/core/tensor_ops.py:25-38, `linear`,
  * whose weight and bias gradients autograd forms after the loss's dlogits,
@@ -599,6 +609,14 @@ int64_t pbg_nvls_signal_bytes(void); /* pad bytes one CTA uses per group of up t
 int pbg_nvls_allreduce_sum_f32(int64_t n, void *multicast, const void *signal_pads,
                                int64_t pad_bytes, int32_t rank, int32_t world, uint32_t *error,
                                void *stream);
+
+/* pbg_nvls_allreduce_sum_f32 on at most max_ctas thread blocks (0 = as many
+ * as the slice and the pad allow), for a SUM that overlaps compute on the
+ * remaining SMs.  A bucket of a larger buffer is summed by passing the
+ * multicast address of its first element and its length. */
+int pbg_nvls_allreduce_sum_f32_grid(int64_t n, void *multicast, const void *signal_pads,
+                                    int64_t pad_bytes, int32_t rank, int32_t world,
+                                    uint32_t *error, int32_t max_ctas, void *stream);
 
 #ifdef __cplusplus
 }
