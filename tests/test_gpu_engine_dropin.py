@@ -1,0 +1,80 @@
+"""The reference's own training engine with this build's kernels swapped in (pbg_b200.engine).
+
+The reference package (pbg, installed under baseline/_ref) runs one full
+iteration -- rollout, completion, targets, learner, optimizer step -- twice
+from the same seed in fresh processes (tests/engine_dropin_run.py): once
+unmodified and once after ``pbg_b200.engine.install()`` has routed its state
+machine, composite policy and layered targets to libpbgb200.  The drop-in
+must leave the engine's results where the reference puts them:
+
+* the same rollout: equal player-node, leaf, layer and edge counts (cards,
+  actions and chips are bit-exact by the parity tests; an action could only
+  differ at a near-tie of the sampler, which these counts would expose);
+* the same learner step: loss metrics within rtol 1e-4, and the flat
+  gradient the AdamW transition receives within rtol 1e-3 plus 1e-5 of its
+  largest entry.  The first AdamW step moves each parameter by +-lr times the
+  sign of its gradient, so parameters are compared where the sign is decided:
+  wherever the gradient exceeds 1e-3 of its largest entry they must agree to
+  1e-6; elsewhere (gradients at rounding level, such as an attention key bias,
+  whose gradient is zero by the softmax's shift invariance) they may differ
+  by at most 2 lr.
+
+Skipped when the reference package is not installed (its layered-targets
+extension is compiled from pbg/core/csrc/layered_targets.cu at run time, so
+the install must include the package's .cu files).
+"""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref", "pbg")
+# the reference JIT-compiles its layered-targets extension from the package's own CUDA source
+REF_TARGETS_SOURCE = os.path.join(REF, "core", "csrc", "layered_targets.cu")
+
+
+def _run(out, arm):
+    env = dict(os.environ, TORCH_CUDA_ARCH_LIST=os.environ.get("TORCH_CUDA_ARCH_LIST", "10.0"))
+    proc = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "engine_dropin_run.py"), out, arm, "16"],
+                          capture_output=True, text=True, timeout=900, env=env)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-6000:]
+    return torch.load(os.path.join(out, f"{arm}.pt"), weights_only=False)
+
+
+@pytest.mark.skipif(not os.path.isfile(REF_TARGETS_SOURCE),
+                    reason="the reference package (with its CUDA sources) is not installed under baseline/_ref")
+def test_reference_engine_runs_on_b200_kernels(tmp_path):
+    ref = _run(str(tmp_path), "reference")
+    b200 = _run(str(tmp_path), "b200")
+    assert b200["installed"] and any("PokerStateMachine" in name for name in b200["installed"])
+    for key in ("player_nodes", "leaves", "target_layers", "executed_edges", "presentations"):
+        assert [lane[key] for lane in b200["lanes"]] == [lane[key] for lane in ref["lanes"]], key
+    for lane_b, lane_r in zip(b200["lanes"], ref["lanes"], strict=True):
+        for loss_b, loss_r in zip(lane_b["losses"], lane_r["losses"], strict=True):
+            for name, value in loss_r.items():
+                assert abs(loss_b[name] - value) <= 1e-4 * abs(value) + 1e-6, (name, loss_b[name], value)
+    lr = 3.0e-4
+    assert len(b200["gradients"]) == len(ref["gradients"]) >= 1
+    for g_b, g_r in zip(b200["gradients"], ref["gradients"], strict=True):
+        scale = float(g_r.abs().max())
+        torch.testing.assert_close(g_b, g_r, rtol=1e-3, atol=1e-5 * scale)
+    g_r = ref["gradients"][0][0]
+    decided = g_r.abs() > 1e-3 * float(g_r.abs().max())
+    assert sum(n for _, n in ref["layout"]) == g_r.numel()
+    offset = 0
+    for name, n in ref["layout"]:
+        value = ref["state"][name]
+        assert torch.equal(b200["state0"][name], ref["state0"][name]), f"initial {name} differs"
+        sure = decided[offset:offset + n].reshape(value.shape)
+        diff = (b200["state"][name] - value).abs()
+        if bool(sure.any()):
+            assert float(diff[sure].max()) <= 1e-6, name
+        assert float(diff.max()) <= 2 * lr + 1e-6, name
+        offset += n
+    moved = max(float((ref["state"][n] - ref["state0"][n]).abs().max()) for n in ref["state"])
+    assert moved > 1e-5  # the optimizer step did change the model
