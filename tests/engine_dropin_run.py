@@ -1,6 +1,6 @@
 """One training iteration of the reference's own engine, optionally routed to libpbgb200.
 
-    python tests/engine_dropin_run.py <out_dir> <b200|reference> [roots] [repeats]
+    python tests/engine_dropin_run.py <out_dir> <reference|b200|b200_learner> [roots] [iterations] [program]
 
 Test infrastructure for tests/test_gpu_engine_dropin.py (run in a fresh process
 so that the two engines never share imported state).  It loads the reference
@@ -9,7 +9,7 @@ self-play run (sampled private estimator, sequential rollout, a small
 transformer), and runs ``pbg.runtime.TrainingSession.step`` once; with
 ``b200`` it first calls ``pbg_b200.engine.install()`` so that the state
 machine, the composite policy and the layered targets of that same engine run
-on this build's kernels.  The learner's tensor program runs eagerly in both
+on this build's kernels (``b200_learner``: the learner's loss program too).  The learner's tensor program runs eagerly in both
 (``tensor_program: eager``).  Writes <out_dir>/<arm>.pt with the model
 state before and after the optimizer step, the flat gradient rows each
 optimizer transition received, the loss metrics and the node counts.
@@ -74,10 +74,10 @@ def main() -> None:
     import torch
 
     handle = None
-    if arm == "b200":
+    if arm in ("b200", "b200_learner"):
         from pbg_b200 import engine
 
-        handle = engine.install()
+        handle = engine.install(learner=arm == "b200_learner")
     from pbg.config import load_config
     from pbg.runtime import TrainingSession
 
@@ -112,6 +112,9 @@ def main() -> None:
         torch.cuda.synchronize()
         walls.append(time.perf_counter() - t)
     state = {k: v.detach().cpu().clone() for k, v in session.modules.lane_module(0).state_dict().items()}
+    from pbg.core.learner import LearnerOperation
+
+    fused_calls = getattr(LearnerOperation.forward_loss, "fused_calls", 0)
     lanes = []
     for result in results:
         for lane in getattr(result, "results", (result,)):
@@ -121,8 +124,8 @@ def main() -> None:
                                                                   "executed_edges")})
             lanes[-1]["losses"] = [dict(loss) for loss in lane.learner.losses]
             lanes[-1]["presentations"] = lane.learner.statistical_presentations
-    torch.save({"state0": state0, "state": state, "lanes": lanes, "walls": walls, "gradients": gradients, "layout": layout,
-                "installed": None if handle is None else [f"{m.__name__}.{n}" for m, n, _ in handle.replaced]},
+    torch.save({"state0": state0, "state": state, "lanes": lanes, "walls": walls, "gradients": gradients, "layout": layout, "fused_calls": fused_calls,
+                "installed": None if handle is None else [f"{getattr(m, '__name__', m)}.{n}" for m, n, _ in handle.replaced]},
                os.path.join(out, f"{arm}.pt"))
     print(json.dumps({"arm": arm, "walls": walls, "lanes": lanes}, default=str)[:4000])
 

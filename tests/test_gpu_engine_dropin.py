@@ -48,10 +48,16 @@ def _run(out, arm):
 
 @pytest.mark.skipif(not os.path.isfile(REF_TARGETS_SOURCE),
                     reason="the reference package (with its CUDA sources) is not installed under baseline/_ref")
-def test_reference_engine_runs_on_b200_kernels(tmp_path):
+@pytest.mark.parametrize("arm", ["b200", "b200_learner"])
+def test_reference_engine_runs_on_b200_kernels(tmp_path, arm):
+    """b200: state machine, policy and targets swapped; b200_learner: the loss program as well
+    (``LearnerOperation.forward_loss`` -> one pbg_poker_learner_objective launch)."""
+
     ref = _run(str(tmp_path), "reference")
-    b200 = _run(str(tmp_path), "b200")
+    b200 = _run(str(tmp_path), arm)
     assert b200["installed"] and any("PokerStateMachine" in name for name in b200["installed"])
+    assert ("forward_loss" in " ".join(b200["installed"])) == (arm == "b200_learner")
+    assert (b200["fused_calls"] > 0) == (arm == "b200_learner")
     for key in ("player_nodes", "leaves", "target_layers", "executed_edges", "presentations"):
         assert [lane[key] for lane in b200["lanes"]] == [lane[key] for lane in ref["lanes"]], key
     for lane_b, lane_r in zip(b200["lanes"], ref["lanes"], strict=True):
