@@ -54,6 +54,14 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--engine-compare", action="store_true",
+                   help="time the reference's own training iteration (pbg.runtime.TrainingSession from baseline/_ref) "
+                        "unmodified and with pbg_b200.engine.install(learner=True), each in a fresh process, and "
+                        "print one JSON line (player nodes/s and learner presentations/s of both)")
+    p.add_argument("--engine-arm", choices=("reference", "reference_eager", "b200"), default=None,
+                   help=argparse.SUPPRESS)
+    p.add_argument("--engine-roots", type=int, default=4096)
+    p.add_argument("--engine-iterations", type=int, default=6)
     p.add_argument("--allreduce", choices=("auto", "nvls", "nccl"), default="auto",
                    help="gradient SUM at N > 1: auto = libpbgb200's NVLS kernel from 4 ranks, NCCL below")
     p.add_argument("--comm-sms", type=int, default=16,
@@ -500,6 +508,127 @@ def reference_torch_loss_component(device, inputs, reps=5):
     return {"workload": "cfg5 rows (4,194,304 x 8, bf16 logits): the reference's LearnerOperation.forward_loss "
                         "+ backward on the device, inputs resident",
             "ms_per_step": ms, "value": N / (ms / 1e3), "unit": UNIT, "source": "baseline/_ref (pbg, unmodified)"}
+
+
+# ----------------------------------------------------------- the reference's engine, with and without the drop-ins
+
+ENGINE_CONFIG = """kind: nlhe_run_v1
+scientific:
+  mode: {{training_regime: self_play, rollout_mode: sequential, private_estimator: sampled}}
+  game: {{players: 2, stack_bb: 8.0, rank_count: 4}}
+  model:
+    d_model: 64
+    n_heads: 4
+    layers: 2
+    raises: {{components: 2, minimum_scale: 0.02}}
+    class_embedding_dim: 8
+    ffn_hidden: 128
+    folder_beta_rank: 0
+    folder_line_dim: 8
+    epsilon: 1.0e-8
+  objective:
+    policy_clip: 0.2
+    value: {{kind: mse, coefficient: 0.5}}
+    entropy: {{kind: constant, coefficient: 0.01}}
+  optimizer: {{kind: adamw, learning_rate: 0.0003, beta1: 0.9, beta2: 0.999, epsilon: 1.0e-8, weight_decay: 0.0,
+              grad_clip: 1.0}}
+  schedule: {{batch_size: 1024, epochs: 1}}
+  lambda: 0.95
+run:
+  seed: 0
+  reproducibility: strict
+  utility: raw_bb
+  workload: {{roots: {roots}}}
+  execution:
+    device: cuda:0
+    precision: fp32
+    attention: sdpa
+    memory: {{reserve_bytes: 67108864}}
+    microbatch: auto
+    tensor_program: {{mode: {program}}}
+  iterations: {iterations}
+  checkpoint_every: 100000
+  output_dir: {out}
+"""
+
+
+def engine_arm(args):
+    """One arm of --engine-compare in this process: a TrainingSession of the config above, timed per iteration
+    (CUDA-synchronised wall clock: an iteration is host-scheduled work spanning many kernels)."""
+
+    import tempfile
+
+    import torch
+
+    sys.path.append(os.path.join(ROOT, "baseline", "_ref"))
+    if args.engine_arm == "b200":
+        from pbg_b200 import engine
+
+        engine.install(learner=True)
+    from pbg.config import load_config
+    from pbg.runtime import TrainingSession
+
+    out = tempfile.mkdtemp(prefix="engine-")
+    path = os.path.join(out, "cfg.yaml")
+    program = "captured" if args.engine_arm == "reference" else "eager"
+    with open(path, "w") as f:
+        f.write(ENGINE_CONFIG.format(roots=args.engine_roots, iterations=args.engine_iterations, program=program,
+                                     out=out))
+    session = TrainingSession(load_config(path), benchmark_telemetry=True)
+    rows = []
+    for _ in range(args.engine_iterations):
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        result = session.step()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t
+        lanes = [lane for lane in getattr(result, "results", (result,)) if lane is not None]
+        rows.append({"seconds": wall, "player_nodes": sum(int(lane.player_nodes) for lane in lanes),
+                     "presentations": sum(int(lane.learner.statistical_presentations) for lane in lanes)})
+        tele = getattr(lanes[0], "telemetry", None) if lanes else None
+        if tele is not None:
+            rows[-1]["telemetry"] = {"rollout_seconds": tele.rollout_seconds,
+                                     "model_inference_seconds": tele.model_inference_seconds,
+                                     "target_propagation_seconds": tele.target_propagation_seconds,
+                                     "host_synchronizations": tele.host_synchronizations,
+                                     "phases": {k: dict(v) for k, v in tele.phase_measurements.items()}}
+    print(json.dumps({"arm": args.engine_arm, "program": program, "iterations": rows}), flush=True)
+
+
+def engine_compare(args):
+    """Both arms in fresh processes; steady state = every iteration after the first two (compilation and
+    capture happen in the first iterations of the reference's captured tensor programs)."""
+
+    env = dict(os.environ, TORCH_CUDA_ARCH_LIST=os.environ.get("TORCH_CUDA_ARCH_LIST", "10.0"))
+    arms = {}
+    for arm in ("reference", "reference_eager", "b200"):
+        proc = subprocess.run([sys.executable, os.path.abspath(__file__), "--engine-arm", arm, "--engine-roots",
+                               str(args.engine_roots), "--engine-iterations", str(args.engine_iterations)],
+                              capture_output=True, text=True, env=env, timeout=1500)
+        lines = [line for line in proc.stdout.splitlines() if line.startswith("{")]
+        if proc.returncode != 0 or not lines:
+            arms[arm] = {"error": proc.stderr[-2000:]}
+            continue
+        data = json.loads(lines[-1])
+        steady = data["iterations"][2:] or data["iterations"]
+        seconds = sum(r["seconds"] for r in steady)
+        data["player_nodes_per_s"] = sum(r["player_nodes"] for r in steady) / seconds
+        data["learner_presentations_per_s"] = sum(r["presentations"] for r in steady) / seconds
+        data["seconds_per_iteration"] = seconds / len(steady)
+        arms[arm] = data
+    line = {"metric": "reference training iteration: player nodes/s and learner presentations/s",
+            "workload": f"pbg.runtime.TrainingSession, HU 8bb R4 self-play, sampled, {args.engine_roots} roots per "
+                        "iteration, transformer d64 / 2 layers, batch 1024, fp32; steady state after 2 iterations",
+            "reference": arms.get("reference"), "reference_eager": arms.get("reference_eager"),
+            "b200": arms.get("b200")}
+    ref, b200 = arms.get("reference", {}), arms.get("b200", {})
+    if "player_nodes_per_s" in ref and "player_nodes_per_s" in b200:
+        line["speedup_player_nodes"] = b200["player_nodes_per_s"] / ref["player_nodes_per_s"]
+        line["speedup_presentations"] = b200["learner_presentations_per_s"] / ref["learner_presentations_per_s"]
+    eager = arms.get("reference_eager", {})
+    if "player_nodes_per_s" in eager and "player_nodes_per_s" in b200:
+        line["speedup_vs_reference_eager"] = b200["player_nodes_per_s"] / eager["player_nodes_per_s"]
+    print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------- rollout component
@@ -1217,6 +1346,12 @@ def posterior_component(device, parents=4096, rows=16384, reps=10):
 
 def main():
     args = parse()
+    if args.engine_arm:
+        engine_arm(args)
+        return
+    if args.engine_compare:
+        engine_compare(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return
