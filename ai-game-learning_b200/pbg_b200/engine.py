@@ -29,10 +29,10 @@ reference's ``LossResult`` whose ``total`` backpropagates into the model.
 Other learners keep the reference's program.  ``uninstall(handle)`` restores
 the originals.
 
-The learner's tensor program must run eagerly
-(``run.execution.tensor_program.mode: eager``): the reference compiles that
-program with ``torch.compile(fullgraph=True)``, which cannot trace a call into
-a shared library.
+The kernels the learner's tensor program reaches (legality and the fused
+objective) are torch custom operators (pbg_b200.ops), so the reference's
+compiled and CUDA-graph-captured tensor programs (``tensor_program: captured``,
+its default) keep working with the drop-ins.
 """
 
 from __future__ import annotations
@@ -83,17 +83,14 @@ def _fused_forward_loss(original):
     """A LearnerOperation.forward_loss that runs the poker objective as one fused launch."""
 
     import torch
+    from pbg.core.contracts import PrivateEstimator
+    from pbg.core.learner import LossResult, _select_sampled_private
+    from pbg.games.poker.queued.hooks import PokerLearnerPolicy
 
-    from .learner import PokerLearnerObjective, poker_learner_loss
-
-    objectives: dict = {}
+    from .learner import poker_learner_loss
 
     def forward_loss(self, batch, *, iteration, reference_operation=None, reference_cache=None, lane_count=1,
                      loss_controls=None, evaluation=None, reference_raw=None):
-        from pbg.core.contracts import PrivateEstimator
-        from pbg.core.learner import LossResult, _select_sampled_private
-        from pbg.games.poker.queued.hooks import PokerLearnerPolicy
-
         policy = self.policy_operation
         if (not isinstance(policy, PokerLearnerPolicy) or evaluation is None or reference_operation is not None
                 or reference_cache is not None):
@@ -133,13 +130,8 @@ def _fused_forward_loss(original):
         if "trace_target" in sigma or "cost_target" in sigma:
             heads = dict(trace_pred=evaluation.public_heads["trace"], cost_pred=evaluation.public_heads["cost"],
                          trace_target=sigma["trace_target"], cost_target=sigma["cost_target"])
-        device = mask.device
-        objective = objectives.get(device)
-        if objective is None:
-            objective = objectives[device] = PokerLearnerObjective(device)
-        forward_loss.fused_calls += 1
         ptr = None if action_rows == rows and not heads else batch.action_ptr
-        result = poker_learner_loss(objective, raw, value.reshape(rows, width), mask=mask, action=action["action"],
+        result = poker_learner_loss(None, raw, value.reshape(rows, width), mask=mask, action=action["action"],
                                     old_log_policy=old.reshape(action_rows, width),
                                     advantage_target=adv.reshape(action_rows, width),
                                     old_value=old_value.reshape(rows, width), value_target=target.reshape(rows, width),
@@ -147,7 +139,6 @@ def _fused_forward_loss(original):
                                     **heads)
         return LossResult(*(getattr(result, name) for name in LossResult.__dataclass_fields__))
 
-    forward_loss.fused_calls = 0  # batches that took the fused path (the others kept the reference's program)
     return forward_loss
 
 

@@ -9,10 +9,11 @@ backward of ``(total * objective_weight * loss_scale).sum()``
 rows, value, entropy, reference KL, trace and cost heads, lane means, and the
 gradient of every raw policy field, the value and the public heads.
 
-``poker_learner_loss`` wraps the same launch as a ``torch.autograd.Function``
-whose backward scales the saved per-lane gradients by the upstream gradient of
-each lane's total, so the model's weight gradients follow from the usual
-``.backward()``.  ``policy_learner`` is the differentiable
+``poker_learner_loss`` runs the same launch as the ``pbg_b200::poker_learner_objective``
+operator (pbg_b200.ops), whose autograd formula scales the per-lane gradients
+it computed by the upstream gradient of each lane's total, so the model's
+weight gradients follow from the usual ``.backward()`` -- eagerly or inside a
+torch.compile'd, CUDA-graph-captured step.  ``policy_learner`` is the differentiable
 ``PokerPolicyOperator.learner`` (selected log pi, entropy, reference KL).
 
 Batch layout (the reference's names):
@@ -164,53 +165,37 @@ class PokerLearnerObjective:
         return LossResult.from_rows(result), out
 
 
-class _LearnerLossFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, objective, names, reference_raw, *tensors):
-        values = dict(zip(names, tensors, strict=True))
-        raw = {n: values[n] for n in _FIELDS}
-        kw = {k: values.get(k) for k in ("posterior", "action_ptr", "trace_pred", "cost_pred", "trace_target",
-                                          "cost_target")}
-        controls = values["controls"]
-        ones = torch.ones(controls.shape[0], dtype=torch.float32, device=controls.device)
-        result, grads = objective(raw, values["mask"], values["action"], values["old_log_policy"],
-                                  values["advantage_target"], values["value"], values["old_value"],
-                                  values["value_target"], controls, ones, reference_raw=reference_raw, **kw)
-        ctx.names = names
-        ctx.lanes, ctx.S = controls.shape[0], values["mask"].shape[0]
-        ctx.grads = grads
-        outs = tuple(getattr(result, f) for f in RESULT_FIELDS)
-        ctx.mark_non_differentiable(*outs[1:])
-        return outs
-
-    @staticmethod
-    def backward(ctx, g_total, *unused):
-        per_sigma = g_total.float().repeat_interleave(ctx.S // ctx.lanes)  # [S]
-        out = []
-        for name in ctx.names:
-            g = ctx.grads.get(name)
-            out.append(None if g is None else g * per_sigma.reshape((ctx.S,) + (1,) * (g.ndim - 1)))
-        return (None, None, None, *out)
-
-
-def poker_learner_loss(objective: PokerLearnerObjective, raw: Mapping[str, Tensor], value: Tensor, *,
+def poker_learner_loss(objective: "PokerLearnerObjective | None", raw: Mapping[str, Tensor], value: Tensor, *,
                        mask: Tensor, action: Tensor, old_log_policy: Tensor, advantage_target: Tensor,
                        old_value: Tensor, value_target: Tensor, controls: Tensor, posterior: Tensor | None = None,
                        action_ptr: Tensor | None = None, reference_raw: Mapping[str, Tensor] | None = None,
                        trace_pred: Tensor | None = None, cost_pred: Tensor | None = None,
                        trace_target: Tensor | None = None, cost_target: Tensor | None = None) -> LossResult:
     """Differentiable ``forward_loss``: a LossResult whose ``total`` [lanes] backpropagates into ``raw``,
-    ``value`` and the public heads (the other fields are statistics without gradient)."""
+    ``value`` and the public heads (the other fields are statistics without gradient).
 
-    tensors = {**raw, "value": value, "mask": mask, "action": action, "old_log_policy": old_log_policy,
-               "advantage_target": advantage_target, "old_value": old_value, "value_target": value_target,
-               "controls": controls}
-    for k, v in (("posterior", posterior), ("action_ptr", action_ptr), ("trace_pred", trace_pred),
-                 ("cost_pred", cost_pred), ("trace_target", trace_target), ("cost_target", cost_target)):
-        if v is not None:
-            tensors[k] = v
-    out = _LearnerLossFn.apply(objective, tuple(tensors), reference_raw, *tensors.values())
-    return LossResult(*out)
+    Runs the ``pbg_b200::poker_learner_objective`` operator, which torch.compile can trace and a CUDA
+    graph can capture; ``objective`` is accepted for symmetry with the non-autograd entry and unused."""
+
+    from .ops import poker_learner_objective as objective_op
+
+    del objective
+    S, E = mask.shape
+    if raw["type_logits"].ndim != 3:
+        raise LearnerError("raw fields must be [S, W, ...]")
+    W = raw["type_logits"].shape[1]
+    if action_ptr is None and action.shape[0] != S:
+        raise LearnerError("ragged learner batches need action_ptr")
+    if W > 1 and posterior is None:
+        raise LearnerError("Rao-Blackwell rows need the posterior")
+    ref = [None] * 5 if reference_raw is None else [reference_raw[n] for n in _FIELDS]
+    lanes = controls.shape[0]
+    ones = torch.ones(lanes, dtype=torch.float32, device=controls.device)
+    out = objective_op(*(raw[n] for n in _FIELDS), *ref, mask, action_ptr, action, old_log_policy, advantage_target,
+                       posterior, value, old_value, value_target, trace_pred, cost_pred, trace_target, cost_target,
+                       controls.float(), ones)
+    result = out[0]
+    return LossResult(result[:, 0], *(result[:, i].detach() for i in range(1, len(RESULT_FIELDS))))
 
 
 class _PolicyLearnerFn(torch.autograd.Function):

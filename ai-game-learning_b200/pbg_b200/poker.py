@@ -291,9 +291,13 @@ class PokerStateMachine:
         return out
 
     def legality(self, state: PokerState) -> PokerLegality:
+        """hooks.py:464-510, through the ``pbg_b200::legality`` operator (traceable by torch.compile)."""
+
+        from .ops import legality as legality_op
+
         E = self.geometry.events
-        mask = torch.empty((state.rows, E), dtype=torch.bool, device=state.device)
-        call("pbg_legality", self.geometry.c, state.rows, state.c(), ptr(mask), stream(state.device))
+        g = self.geometry
+        mask = legality_op(*(getattr(state, n) for n in STATE_FIELDS), g.players, g.stack_ticks, g.rank_count)
         ids = torch.arange(E, dtype=torch.int32, device=state.device)[None].expand(state.rows, -1).contiguous()
         return PokerLegality(ids, mask)
 

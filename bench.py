@@ -58,7 +58,7 @@ def parse():
                    help="time the reference's own training iteration (pbg.runtime.TrainingSession from baseline/_ref) "
                         "unmodified and with pbg_b200.engine.install(learner=True), each in a fresh process, and "
                         "print one JSON line (player nodes/s and learner presentations/s of both)")
-    p.add_argument("--engine-arm", choices=("reference", "reference_eager", "b200"), default=None,
+    p.add_argument("--engine-arm", choices=("reference", "reference_eager", "b200", "b200_eager"), default=None,
                    help=argparse.SUPPRESS)
     p.add_argument("--engine-roots", type=int, default=4096)
     p.add_argument("--engine-iterations", type=int, default=6)
@@ -561,7 +561,7 @@ def engine_arm(args):
     import torch
 
     sys.path.append(os.path.join(ROOT, "baseline", "_ref"))
-    if args.engine_arm == "b200":
+    if args.engine_arm.startswith("b200"):
         from pbg_b200 import engine
 
         engine.install(learner=True)
@@ -570,7 +570,7 @@ def engine_arm(args):
 
     out = tempfile.mkdtemp(prefix="engine-")
     path = os.path.join(out, "cfg.yaml")
-    program = "captured" if args.engine_arm == "reference" else "eager"
+    program = "eager" if args.engine_arm.endswith("_eager") else "captured"
     with open(path, "w") as f:
         f.write(ENGINE_CONFIG.format(roots=args.engine_roots, iterations=args.engine_iterations, program=program,
                                      out=out))
@@ -601,7 +601,7 @@ def engine_compare(args):
 
     env = dict(os.environ, TORCH_CUDA_ARCH_LIST=os.environ.get("TORCH_CUDA_ARCH_LIST", "10.0"))
     arms = {}
-    for arm in ("reference", "reference_eager", "b200"):
+    for arm in ("reference", "b200"):
         proc = subprocess.run([sys.executable, os.path.abspath(__file__), "--engine-arm", arm, "--engine-roots",
                                str(args.engine_roots), "--engine-iterations", str(args.engine_iterations)],
                               capture_output=True, text=True, env=env, timeout=1500)

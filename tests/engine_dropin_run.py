@@ -112,9 +112,11 @@ def main() -> None:
         torch.cuda.synchronize()
         walls.append(time.perf_counter() - t)
     state = {k: v.detach().cpu().clone() for k, v in session.modules.lane_module(0).state_dict().items()}
-    from pbg.core.learner import LearnerOperation
+    fused_calls = 0
+    if handle is not None:
+        from pbg_b200 import ops
 
-    fused_calls = getattr(LearnerOperation.forward_loss, "fused_calls", 0)
+        fused_calls = ops.CALLS["poker_learner_objective"]
     lanes = []
     for result in results:
         for lane in getattr(result, "results", (result,)):
