@@ -12,8 +12,14 @@ every hand.  ``FamilyRollout.step`` does the same on this build's pieces:
 ``QueuedPokerModel.rollout_operation`` (the tensor-core networks), and the
 fused ``RolloutStep.step`` / ``reach_update`` kernels, which read each hand's
 raw policy rows from one [B, H] buffer (class rows first for preflop hands).
-Grouping reads the hands' streets and statuses on the host once per step, as
-the reference's family scheduler does.
+
+The family codes stay on the device: a stable sort groups the live hands by
+family, and the only host read of a step is the per-family count vector
+(P + 2 integers), which sizes the model calls as the reference's family
+scheduler's sizes do.  The [B, H] raw buffers are allocated once per arena,
+and each family is evaluated in chunks of at most ``max_rows`` decisions so
+that a postflop call (thousands of tokens per decision) stays within memory
+at any batch size.
 """
 
 from __future__ import annotations
@@ -44,12 +50,30 @@ def tight_folder_mask(history: PokerHistory, status: Tensor) -> Tensor:
 class FamilyRollout:
     """Drive a rollout arena with a ``QueuedPokerModel`` evaluated per input family."""
 
-    def __init__(self, model: QueuedPokerModel, *, seed: int, iteration: int) -> None:
+    def __init__(self, model: QueuedPokerModel, *, seed: int, iteration: int,
+                 max_rows: dict | None = None) -> None:
         self.model = model
         self.geometry = model.geometry
         self.stepper = RolloutStep(self.geometry, seed=seed, iteration=iteration, with_history=True)
         self.machine = self.stepper.machine
         self.families: dict[str, int] = {}
+        self.max_rows = {"pre": 8192, "post": 1024, **(max_rows or {})}
+        self._raw: dict | None = None
+        self._raw_key = None
+
+    def _raw_buffers(self, rows: int, device) -> dict:
+        """[B, H] raw-policy buffers, allocated once per arena size (a neutral policy in every slot)."""
+
+        key = (rows, str(device))
+        if self._raw_key != key:
+            H, M = self.geometry.private_hands, self.model.cfg.m_raise
+            self._raw = {"type_logits": torch.zeros((rows, H, 3), device=device),
+                         "omega": torch.full((rows, H, M), 1.0 / M, device=device),
+                         "mu": torch.full((rows, H, M), 0.5, device=device),
+                         "s": torch.ones((rows, H, M), device=device),
+                         "iota": torch.full((rows, H), 0.5, device=device)}
+            self._raw_key = key
+        return self._raw
 
     def roots(self, rows: int, *, device, retry_epoch: int = 0, logical_base: int = 0,
               lane: int = 0) -> tuple[RolloutArena, Tensor]:
@@ -81,29 +105,31 @@ class FamilyRollout:
 
         g = self.geometry
         state = arena.state
-        live = ~state.terminal
-        street = state.street.to(torch.int64)
         live_seats = state.status.ne(FOLDED).sum(1)
-        code = torch.where(street.eq(0), torch.zeros_like(live_seats), live_seats)
-        code = torch.where(live, code, torch.full_like(code, -1)).cpu()
-        decisions = int((code >= 0).sum())
+        code = torch.where(state.street.eq(0), torch.zeros_like(live_seats), live_seats)
+        code = torch.where(~state.terminal, code, torch.full_like(code, -1))
+        counts = torch.bincount(code + 1, minlength=g.players + 2).cpu().tolist()  # the step's one host read
+        decisions = sum(counts[1:])
         if decisions == 0:
             return 0
-        B, H = arena.rows, g.private_hands
-        M = self.model.cfg.m_raise
-        device = state.device
-        raw = {"type_logits": torch.zeros((B, H, 3), device=device), "omega": torch.full((B, H, M), 1.0 / M, device=device),
-               "mu": torch.full((B, H, M), 0.5, device=device), "s": torch.ones((B, H, M), device=device),
-               "iota": torch.full((B, H), 0.5, device=device)}
-        for value in sorted(set(code.tolist()) - {-1}):
+        raw = self._raw_buffers(arena.rows, state.device)
+        order = torch.sort(code, stable=True).indices  # terminal hands first, then each family in index order
+        start = counts[0]
+        for value, count in enumerate(counts[1:]):
+            if count == 0:
+                continue
             kind = "pre" if value == 0 else f"post_{value}"
-            rows = torch.nonzero(code == value).flatten().to(device)
-            model_input, sub = self._family_rows(arena, kind, rows, log_reach)
-            evaluation = self.model.rollout_operation(kind, model_input, sub.combo_ids, sub.to_act.to(torch.int64))
-            for name in RAW_FIELDS:
-                field = evaluation.policy_raw[name].float()
-                raw[name][rows, : field.shape[1]] = field
-            self.families[kind] = self.families.get(kind, 0) + int(rows.numel())
+            chunk = self.max_rows["pre" if value == 0 else "post"]
+            family = order[start:start + count]
+            start += count
+            for lo in range(0, count, chunk):
+                rows = family[lo:lo + chunk]
+                model_input, sub = self._family_rows(arena, kind, rows, log_reach)
+                evaluation = self.model.rollout_operation(kind, model_input, sub.combo_ids, sub.to_act.to(torch.int64))
+                for name in RAW_FIELDS:
+                    field = evaluation.policy_raw[name]
+                    raw[name][rows, : field.shape[1]] = field.float()
+            self.families[kind] = self.families.get(kind, 0) + count
         self.stepper.step(arena, raw)
         self.stepper.reach_update(arena, raw, log_reach)
         return decisions

@@ -1015,7 +1015,7 @@ def _time_forward(device, forward, reps: int):
     return ms, eager_ms
 
 
-def rollout_with_model_component(device, hands=1024):
+def rollout_with_model_component(device, hands=65_536):
     """Family-scheduled rollout with the policy network in the loop (pbg_b200.family_rollout): HU 100bb
     R13 (cfg2), `hands` roots played to the end; every step groups the live hands by partition (preflop
     classes / postflop combos), encodes their retained rows, evaluates QueuedPokerModel with cfg2's
@@ -1047,7 +1047,10 @@ def rollout_with_model_component(device, hands=1024):
             total, steps = total + n, steps + 1
         return total, steps, roll.families
 
-    play()  # warm-up (bindings, first launches)
+    small = hands
+    hands = min(hands, 1024)
+    play()  # warm-up on a small arena (bindings, first launches)
+    hands = small
     torch.cuda.synchronize(device)
     t = time.perf_counter()
     decisions, steps, families = play()
