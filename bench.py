@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--actions", type=int, default=8)
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--profile-hands", type=int, default=4096,
+                   help="--profile-forward rollout_with_model: hands of the profiled rollout")
     p.add_argument("--engine-compare", action="store_true",
                    help="time the reference's own training iteration (pbg.runtime.TrainingSession from baseline/_ref) "
                         "unmodified and with pbg_b200.engine.install(learner=True), each in a fresh process, and "
@@ -70,7 +72,8 @@ def parse():
                    help="N > 1: the rows' loss runs as this many chunks, and the gradient SUM as as many buckets "
                         "on a second stream, bucket k starting when chunk k's loss is done")
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
-                                                 "readout", "reach", "showdown", "optimizer", "poker_loss"),
+                                                 "readout", "reach", "showdown", "optimizer", "poker_loss",
+                                                 "rollout_with_model"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
@@ -78,7 +81,8 @@ def parse():
                         "components.posterior_sampler; readout: one launch of components.loss_readout; reach: "
                         "one launch of components.reach_update; showdown / optimizer: one call of "
                         "components.showdown / components.optimizer_step; poker_loss: one launch of the "
-                        "sampled batch of components.poker_loss) "
+                        "sampled batch of components.poker_loss; rollout_with_model: one whole rollout of "
+                        "--profile-hands hands of components.rollout_with_model) "
                         "between cudaProfilerStart/Stop (for ncu "
                         "--profile-from-start off) after two warm-up runs, print nothing else, exit")
     return p.parse_args()
@@ -1051,6 +1055,13 @@ def rollout_with_model_component(device, hands=65_536):
     hands = min(hands, 1024)
     play()  # warm-up on a small arena (bindings, first launches)
     hands = small
+    if PROFILE_ONE_FORWARD:  # one whole rollout between cudaProfilerStart/Stop
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.start()
+        play()
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.stop()
+        return {}
     torch.cuda.synchronize(device)
     t = time.perf_counter()
     decisions, steps, families = play()
@@ -1373,9 +1384,13 @@ def main():
         PROFILE_ONE_FORWARD = True
         name = {"folded": "folded_component", "posterior": "posterior_component",
                 "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
-                "optimizer": "optimizer_component", "poker_loss": "poker_loss_component"}.get(
+                "optimizer": "optimizer_component", "poker_loss": "poker_loss_component",
+                "rollout_with_model": "rollout_with_model_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
-        globals()[name](device)
+        if name == "rollout_with_model_component":
+            rollout_with_model_component(device, hands=args.profile_hands)
+        else:
+            globals()[name](device)
         return
     if world > 1:
         import datetime
