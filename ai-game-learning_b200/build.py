@@ -22,7 +22,7 @@ OUT_DIR = os.path.join(HERE, "pbg_b200")
 LIB = os.path.join(OUT_DIR, "libpbgb200.so")
 BUILD = os.path.join(HERE, "_build")
 
-EXACT = ["common.cu", "poker.cu", "policy.cu", "showdown.cu", "targets.cu", "posterior.cu", "branching.cu",
+EXACT = ["common.cu", "poker.cu", "policy.cu", "showdown.cu", "completion.cu", "targets.cu", "posterior.cu", "branching.cu",
          "incidence.cu"]
 FAST = ["loss.cu", "learner.cu", "adam.cu", "collective.cu", "gemm.cu", "attention.cu", "layernorm.cu", "folded.cu", "eigh.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -61,8 +61,9 @@ __host__ __device__ __forceinline__ uint64_t scalar_hash(uint64_t v) {
     return (v ^ (v >> 31)) & M63;
 }
 
-// Namespace of (seed, iteration, purpose); computed once on the host.
-inline uint64_t rng_namespace(int64_t seed, int64_t iteration, int64_t purpose) {
+// Namespace of (seed, iteration, purpose): computed once on the host, or once per
+// row on the device where each row carries its own seed.
+__host__ __device__ __forceinline__ uint64_t rng_namespace(int64_t seed, int64_t iteration, int64_t purpose) {
     uint64_t ns = scalar_hash(((uint64_t)seed & M63) ^
                               (((uint64_t)iteration + 0x6A09E667F3BCC909ULL) & M63));
     return scalar_hash(ns ^ (((uint64_t)purpose + 0x5BE0CD19137E2179ULL) & M63));

@@ -3,159 +3,11 @@
 //
 // The reference delegates ranking to the external poker_gpu_evaluator; this
 // kernel ranks 7-card hands directly from rank-multiplicity bit planes and suit
-// masks (the board's built once per hand, each seat adding its hole cards).  The
-// category order of each deck is the rarity-consistent order of
-// pbg/games/poker/cards.py:37-74 (category_profile): categories sorted by
-// their exact five-card counts, equal counts in conventional order.  Within
-// a category the usual kicker order applies; tied winners share equally.
-#include "pbg_common.cuh"
+// masks (the board's built once per hand, each seat adding its hole cards),
+// with the category order and settlement of showdown.cuh.
+#include "showdown.cuh"
 
 namespace pbg {
-
-enum Cat { HIGH_CARD, PAIR, TWO_PAIR, TRIPS, STRAIGHT, FLUSH, FULL_HOUSE, QUADS, STRAIGHT_FLUSH, N_CAT };
-
-struct Strength {
-    int s[N_CAT];
-};
-
-static double comb_d(int n, int k) {
-    if (k < 0 || k > n) return 0.0;
-    double r = 1.0;
-    for (int i = 1; i <= k; ++i) r = r * (n - k + i) / i;
-    return r;
-}
-
-// Strength index of every category for a deck of R ranks (0 = weakest).
-static Strength category_strength(int R) {
-    double total = comb_d(4 * R, 5);
-    int seq = (R - 4 > 0 ? R - 4 : 0) + (R == 13 ? 1 : 0);
-    double cr5 = R >= 5 ? comb_d(R, 5) : 0.0;
-    double cnt[N_CAT];
-    cnt[HIGH_CARD] = total;
-    cnt[PAIR] = total - 1024.0 * cr5;
-    cnt[TWO_PAIR] = 144.0 * (R - 2) * comb_d(R, 2) + 24.0 * R * (R - 1);
-    cnt[TRIPS] = 64.0 * R * comb_d(R - 1, 2) + 28.0 * R * (R - 1);
-    cnt[STRAIGHT] = 1024.0 * seq;
-    cnt[FLUSH] = 4.0 * cr5;
-    cnt[FULL_HOUSE] = 24.0 * R * (R - 1);
-    cnt[QUADS] = 4.0 * R * (R - 1);
-    cnt[STRAIGHT_FLUSH] = 4.0 * seq;
-    Strength st;
-    for (int c = 0; c < N_CAT; ++c) {
-        int weaker = 0;
-        for (int o = 0; o < N_CAT; ++o) {
-            if (o == c || cnt[o] <= 0) continue;
-            if (cnt[o] > cnt[c] || (cnt[o] == cnt[c] && o < c)) ++weaker;
-        }
-        st.s[c] = cnt[c] > 0 ? weaker : -1;
-    }
-    return st;
-}
-
-__device__ __forceinline__ int top_straight(unsigned mask, int R) {
-    for (int top = 12; top >= 4; --top)
-        if (((mask >> (top - 4)) & 0x1Fu) == 0x1Fu) return top;
-    if (R == 13 && (mask & 0x100Fu) == 0x100Fu) return 3;  // A-2-3-4-5
-    return -1;
-}
-
-__device__ __forceinline__ int64_t pack(int strength, int t0, int t1, int t2, int t3, int t4) {
-    return ((((((int64_t)strength * 16 + t0) * 16 + t1) * 16 + t2) * 16 + t3) * 16) + t4;
-}
-
-// Highest set rank of mask below `below` (exclusive), or 0 when none.
-__device__ __forceinline__ int next_rank(unsigned mask, int& cursor) {
-    while (cursor >= 0 && !((mask >> cursor) & 1u)) --cursor;
-    int r = cursor >= 0 ? cursor : 0;
-    --cursor;
-    return r;
-}
-
-// Rank multiplicities as bit planes (ranks held at least once / twice / three / four times) and
-// the four suits' rank masks packed 16 bits apart: a card is added with a few register ops, so the
-// board's planes are built once per hand and each seat only adds its two hole cards.
-struct HandCounts {
-    unsigned ge1 = 0, ge2 = 0, ge3 = 0, ge4 = 0;
-    uint64_t suits = 0;
-
-    __device__ __forceinline__ void add(int card) {
-        const unsigned m = 1u << (card >> 2);
-        ge4 |= ge3 & m;
-        ge3 |= ge2 & m;
-        ge2 |= ge1 & m;
-        ge1 |= m;
-        suits |= (uint64_t)m << (16 * (card & 3));
-    }
-};
-
-__device__ int64_t hand_value(const HandCounts& h, const Strength& S, int R) {
-    const unsigned ranks = h.ge1, ge2 = h.ge2, ge3 = h.ge3, ge4 = h.ge4;
-    int64_t best = -1;
-    int flush_suit = -1;
-    unsigned flush_mask = 0;
-    #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const unsigned m = (unsigned)(h.suits >> (16 * s)) & 0x1FFFu;
-        if (__popc(m) >= 5) {
-            flush_suit = s;
-            flush_mask = m;
-        }
-    }
-    if (flush_suit >= 0 && S.s[STRAIGHT_FLUSH] >= 0) {
-        int top = top_straight(flush_mask, R);
-        if (top >= 0) best = max(best, pack(S.s[STRAIGHT_FLUSH], top, 0, 0, 0, 0));
-    }
-    if (ge4) {
-        int q = 31 - __clz(ge4);
-        unsigned rest = ranks & ~(1u << q);
-        int k = rest ? 31 - __clz(rest) : 0;
-        best = max(best, pack(S.s[QUADS], q, k, 0, 0, 0));
-    }
-    if (ge3) {
-        int t = 31 - __clz(ge3);
-        unsigned pairs = ge2 & ~(1u << t);
-        if (pairs) best = max(best, pack(S.s[FULL_HOUSE], t, 31 - __clz(pairs), 0, 0, 0));
-    }
-    if (flush_suit >= 0 && S.s[FLUSH] >= 0) {
-        int cur = 12;
-        unsigned m = flush_mask;
-        int a = next_rank(m, cur), b = next_rank(m, cur), c = next_rank(m, cur), d = next_rank(m, cur), e = next_rank(m, cur);
-        best = max(best, pack(S.s[FLUSH], a, b, c, d, e));
-    }
-    if (S.s[STRAIGHT] >= 0) {
-        int top = top_straight(ranks, R);
-        if (top >= 0) best = max(best, pack(S.s[STRAIGHT], top, 0, 0, 0, 0));
-    }
-    if (ge3) {
-        int t = 31 - __clz(ge3);
-        unsigned rest = ranks & ~(1u << t);
-        int cur = 12;
-        int a = next_rank(rest, cur), b = next_rank(rest, cur);
-        best = max(best, pack(S.s[TRIPS], t, a, b, 0, 0));
-    }
-    if (__popc(ge2) >= 2) {
-        int p1 = 31 - __clz(ge2);
-        unsigned others = ge2 & ~(1u << p1);
-        int p2 = 31 - __clz(others);
-        unsigned rest = ranks & ~(1u << p1) & ~(1u << p2);
-        int k = rest ? 31 - __clz(rest) : 0;
-        best = max(best, pack(S.s[TWO_PAIR], p1, p2, k, 0, 0));
-    }
-    if (ge2) {
-        int p = 31 - __clz(ge2);
-        unsigned rest = ranks & ~(1u << p);
-        int cur = 12;
-        int a = next_rank(rest, cur), b = next_rank(rest, cur), c = next_rank(rest, cur);
-        best = max(best, pack(S.s[PAIR], p, a, b, c, 0));
-    }
-    {
-        int cur = 12;
-        int a = next_rank(ranks, cur), b = next_rank(ranks, cur), c = next_rank(ranks, cur), d = next_rank(ranks, cur),
-            e = next_rank(ranks, cur);
-        best = max(best, pack(S.s[HIGH_CARD], a, b, c, d, e));
-    }
-    return best;
-}
 
 __device__ __forceinline__ int64_t hand_value7(const int* cards, const Strength& S, int R) {
     HandCounts h;
@@ -202,29 +54,7 @@ __global__ void showdown_kernel(Strength S, int R, int D, int first, int64_t B, 
             if (p >= P) break;
             acc[p] = baseline[b * P + p];
         }
-        for (int k = 0; k < strata; ++k) {
-            float amt = amount[b * strata + k];
-            if (!(amt > 0.0f)) continue;
-            int64_t best = -1;
-            #pragma unroll
-            for (int p = 0; p < MAXP; ++p) {
-                if (p >= P) break;
-                if (value[p] >= 0 && lev[p] >= k && value[p] > best) best = value[p];
-            }
-            if (best < 0) continue;
-            int winners = 0;
-            #pragma unroll
-            for (int p = 0; p < MAXP; ++p) {
-                if (p >= P) break;
-                winners += value[p] == best && lev[p] >= k;
-            }
-            float share = __fdiv_rn(amt, (float)winners);
-            #pragma unroll
-            for (int p = 0; p < MAXP; ++p) {
-                if (p >= P) break;
-                if (value[p] == best && lev[p] >= k) acc[p] = __fadd_rn(acc[p], share);
-            }
-        }
+        settle_strata(P, strata, value, lev, amount + b * strata, acc);
         #pragma unroll
         for (int p = 0; p < MAXP; ++p) {
             if (p >= P) break;

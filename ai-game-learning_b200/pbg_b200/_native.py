@@ -94,6 +94,8 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_direct_model_input": (_I32, [G, _I64, S, _I32, _P, Hs, _P, _I64, _P]),
     "pbg_evaluate_showdowns": (_I32, [_I32, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_hand_values": (_I32, [_I32, _I64, _P, _P, _P]),
+    "pbg_rb_complete": (_I32, [_I32, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_rb_complete_max_samples": (_I32, [_I32, _I32]),
     "pbg_policy_probabilities": (_I32, [_I64, _I32, Pol, _P, _P, _P]),
     "pbg_policy_selected_log_pi": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P]),
     "pbg_policy_entropy": (_I32, [_I64, _I32, Pol, _P, _P, _P]),

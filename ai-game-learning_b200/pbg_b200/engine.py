@@ -17,8 +17,10 @@ build's drop-ins, so every rollout step (legality, chip accounting, keyed
 chance, histories, leaves, model-input rows), every policy evaluation
 (sampling, selected log pi, the learner's differentiable policy operation) and
 every layered-target pass of the reference's own engine runs on the sm_100a
-kernels, while the engine, storage, scheduling and the showdown binding
-(``poker_gpu_evaluator``, already this build's module) stay the reference's.
+kernels, while the engine, storage, scheduling and the showdown and
+completion bindings stay the reference's (the evaluator they call,
+``poker_gpu_evaluator``, is this build's module: sampled showdowns and
+Rao-Blackwell leaf completion on the device).
 With ``learner=True`` the loss program of every learner whose policy
 operation is the poker one (``PokerLearnerPolicy``, hooks.py:2200-2246)
 becomes one launch of ``pbg_poker_learner_objective``: the adapter selects the
@@ -56,12 +58,6 @@ class EngineStateMachine(PokerStateMachine):
     def __init__(self, geometry) -> None:
         super().__init__(_geometry(geometry))
         self.reference_geometry = geometry
-
-    def rb_leaf(self, *args, **kwargs):
-        """hooks.py:1218-1271: Rao-Blackwell leaves go to the external evaluator's completion, which
-        this build does not provide; sampled settlement (``sampled_leaf``) is on the device."""
-
-        raise NotImplementedError("Rao-Blackwell leaf completion is not part of this build")
 
 
 class EnginePolicyOperator(PokerPolicyOperator):

@@ -360,6 +360,35 @@ class PokerStateMachine:
              N.Leaf(*(ptr(v) for v in leaf.values())), stream(state.device))
         return MappingProxyType(leaf)
 
+    def rb_leaf(self, state: PokerState, log_reach: Tensor, *, seed: Tensor, selected_player: Tensor | None = None):
+        """hooks.py:1218-1258: the contract-v2 completion inputs of Rao-Blackwell leaves.
+
+        The public pre-terminal board stays as it is (an early fold is not padded with dealt
+        cards, which would move it between the pre- and post-flop outputs); the stratum fields are
+        the sampled settlement's with the hand forced terminal; each seat's range weights are
+        exp(log_reach - its largest finite reach), non-finite reaches weighing 0."""
+
+        g = self.geometry
+        if (log_reach.shape != (state.rows, g.players, g.private_hands) or log_reach.dtype != torch.float32
+                or log_reach.device != state.device):
+            raise QueuedPokerError("RB leaf reaches must be CUDA FP32 [B,P,H]")
+        sampled = self.sampled_leaf(replace(state, terminal=torch.ones_like(state.terminal)))
+        finite = torch.isfinite(log_reach)
+        top = torch.where(finite, log_reach, -torch.inf).amax(-1, keepdim=True)
+        top = torch.where(torch.isfinite(top), top, 0.0)
+        weights = torch.where(finite, torch.exp(log_reach - top), 0.0)
+        leaf = {
+            "leaf_public_state": state.board_cards.contiguous(),
+            "stratum_level": sampled["stratum_level"],
+            "payoff_baseline": sampled["payoff_baseline"],
+            "stratum_amount": sampled["stratum_amount"],
+            "range_weights": weights.contiguous(),
+            "seed": seed.to(dtype=torch.int64, device=state.device).contiguous(),
+        }
+        if selected_player is not None:
+            leaf["trained_actor"] = selected_player.to(dtype=torch.int32, device=state.device).contiguous()
+        return MappingProxyType(leaf)
+
     def model_input_width(self, input_type: str) -> int:
         """hooks.py:138-169: retained row width of a partition."""
 

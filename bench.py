@@ -73,7 +73,7 @@ def parse():
                         "on a second stream, bucket k starting when chunk k's loss is done")
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
                                                  "readout", "reach", "showdown", "optimizer", "poker_loss",
-                                                 "rollout_with_model"),
+                                                 "rollout_with_model", "completion"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
@@ -1192,6 +1192,67 @@ def showdown_component(device, hands=1_048_576, players=6, reps=10):
             "gpu_launches": 1}
 
 
+def completion_component(device, leaves=4096, players=6, samples=(256, 1024), reps=5):
+    """Rao-Blackwell leaf completion (poker_gpu_evaluator.complete, the contract-v2 call of
+    RBCompletionBinding, hooks.py:2472-2477) at cfg3's geometry: `leaves` 6-max R13 leaf rows of
+    [6, 1326] fp32 range weights (preflop / flop / turn / river boards in turn, three strata, ~20 % of
+    seats folded), each sample count in `samples`.  One launch per call, queued behind a device-side
+    sleep.  The HBM floor per leaf is the range read plus the p_hat and v_hat writes; the CPU figure is
+    the C restatement (oracle) on one core over a few leaves of the same workload."""
+
+    import numpy as np
+    import torch
+    import poker_gpu_evaluator as poker
+
+    H = 1326
+    rng = np.random.default_rng(31)
+    board = np.full((leaves, 5), 255, np.uint8)
+    shown = np.array([0, 3, 4, 5])[np.arange(leaves) % 4]
+    cards = np.argsort(rng.random((leaves, 52), dtype=np.float32), axis=1)[:, :5]
+    board = np.where(np.arange(5)[None, :] < shown[:, None], cards, 255).astype(np.uint8)
+    w = np.exp(rng.normal(0.0, 1.5, (leaves, players, H))).astype(np.float32)
+    level = np.where(rng.random((leaves, players)) < 0.2, -1, rng.integers(0, 3, (leaves, players))).astype(np.int32)
+    level[:, :2] = np.maximum(level[:, :2], 0)
+    base = -rng.integers(1, 40, (leaves, players)).astype(np.float32) * 0.5
+    pot = -base.sum(1)
+    amount = np.stack([pot * 0.6, pot * 0.3, pot * 0.1], 1).astype(np.float32)
+    seed = rng.integers(0, 2**62, leaves, dtype=np.int64)
+    t = {k: torch.from_numpy(v).to(device) for k, v in
+         dict(board_cards=board, range_weights=w, stratum_level=level, payoff_baseline=base, stratum_amount=amount,
+              seed=seed).items()}
+    ev = poker.bind(13)
+    if PROFILE_ONE_FORWARD:
+        _device_ms(device, lambda: ev.complete(**t, n_samples=samples[0], validate=False))
+        return {}
+    peak, peak_kind = measured_peak()
+    algo = leaves * (players * H * 4 * 3 + 5 + players * 12 + 3 * 4 + 8 + 4)
+    out = {"workload": f"{leaves} {players}-max R13 leaves ([{players}, {H}] range weights; boards preflop / "
+                       "flop / turn / river in turn; 3 strata; ~20 % of seats folded)",
+           "kernel": "rb_complete_kernel", "gpu_launches": 1, "algorithmic_bytes": algo,
+           "bound": "instruction issue and shared-memory latency (per sample: 6 seat draws with "
+                    "inclusion-exclusion masses, the runout, 7-card evaluations) above the HBM floor"}
+    for n in samples:
+        ms = _device_ms(device, lambda: ev.complete(**t, n_samples=n, validate=False), reps)
+        gbs = algo / (ms / 1000.0) / 1e9
+        out[f"n{n}"] = {"us": 1000.0 * ms, "leaves_per_s": leaves / (ms / 1000.0),
+                        "samples_per_s": leaves * n / (ms / 1000.0), "hbm_gbs": gbs, "peak_gbs": peak,
+                        "frac": gbs / peak, "peak_kind": peak_kind}
+    try:
+        import time
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        k = 4
+        t0 = time.perf_counter()
+        O.rb_complete(13, board[:k], w[:k], level[:k], base[:k], amount[:k], samples[0], seed[:k])
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": k / dt, "unit": "leaves/s", "cores": 1, "kind": "port",
+                               "sample": f"{k} leaves at n_samples={samples[0]} through the C restatement"}
+    except Exception as exc:  # the oracle is optional on a box without a C compiler
+        out["cpu_baseline"] = {"unavailable": str(exc)[:200]}
+    return out
+
+
 def reach_component(device, hands=16_384, seed=0, reps=10):
     """The reach update after a preflop decision (pbg_reach_update, hooks.py:1641-1703): `hands` HU 100bb
     R13 hands after their first step, a seeded raw policy for every private row; per hand the 169 class
@@ -1385,7 +1446,7 @@ def main():
         name = {"folded": "folded_component", "posterior": "posterior_component",
                 "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
                 "optimizer": "optimizer_component", "poker_loss": "poker_loss_component",
-                "rollout_with_model": "rollout_with_model_component"}.get(
+                "rollout_with_model": "rollout_with_model_component", "completion": "completion_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         if name == "rollout_with_model_component":
             rollout_with_model_component(device, hands=args.profile_hands)
@@ -1642,6 +1703,7 @@ def main():
                                   "poker_loss": poker_loss_component(device),
                                   "optimizer_step": optimizer_component(device),
                                   "showdown": showdown_component(device),
+                                  "rb_completion": completion_component(device),
                                   "reach_update": reach_component(device),
                                   "folded_statistics": folded_component(device),
                                   "branched_sampling": branching_component(device),

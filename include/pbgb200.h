@@ -198,6 +198,30 @@ int pbg_evaluate_showdowns(int32_t rank_count, int64_t B, int32_t P, int32_t str
 int pbg_hand_values(int32_t rank_count, int64_t n, const int32_t *cards, int64_t *out,
                     void *stream);
 
+/* Contract-v2 `complete` / `complete_selected` of the external
+ * poker_gpu_evaluator, as called by RBCompletionBinding.leaf_to_layer_work
+ * (hooks.py:2472-2477, 2512) on PokerStateMachine.rb_leaf rows
+ * (hooks.py:1218-1258): the PreTerminalMC law of core_math.tex:664-684.
+ * Per leaf row f: board u8 [F,5] (255 = not dealt), range_weights f32
+ * [F,P,H], level i32 [F,P], baseline f32 [F,P], amount f32 [F,strata],
+ * seed i64 [F]; n_samples importance-weighted profiles (sequential over the
+ * seats), the missing board dealt uniformly, returns settled by strata.
+ * selected NULL: p_hat, v_hat f32 [F,P,H]; else selected i32 [F] and p_hat,
+ * v_hat f32 [F,H] (bit-identical to the dense slice).  n_eff f32 [F] (the
+ * effective sample size, <= n_samples).  *status (device, caller-zeroed):
+ * bit 1 an invalid board card or selected seat (the row publishes zeros),
+ * bit 2 a row without sample mass (n_eff = 0).  Deterministic. */
+int pbg_rb_complete(int32_t rank_count, int64_t F, int32_t P, int32_t strata, int32_t n_samples,
+                    const uint8_t *board, const float *range_weights, const int32_t *level,
+                    const float *baseline, const float *amount, const int64_t *seed,
+                    const int32_t *selected, float *p_hat, float *v_hat, float *n_eff,
+                    uint32_t *status, void *stream);
+
+/* Largest n_samples pbg_rb_complete accepts for this deck and seat count
+ * (one leaf's tables and sample records in one CTA's shared memory); 0 for
+ * an invalid geometry. */
+int32_t pbg_rb_complete_max_samples(int32_t rank_count, int32_t P);
+
 /* ------------------------------------------------------------- policy */
 
 /* policy.py:113-204 (PokerPolicyOperator.probabilities): out [B*rows,E];

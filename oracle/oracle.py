@@ -99,6 +99,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_sampled_leaf": (None, [G, _I64, S, _P, _P, _P, _P, _P]),
         "orc_hand_value7": (_I64, [_I32, _P]),
         "orc_evaluate_showdowns": (None, [_I32, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+        "orc_rb_complete": (_I32, [_I32, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
         "orc_policy_probabilities": (None, [_I64, _I32, _I32, _I64, _P, _P, _P, _P, _P, _P, _P]),
         "orc_ppo_categorical": (None, [_I64, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
         "orc_adam": (_I32, [_I64, _P, _P, _P, _P, _P, _P, _I32, _P]),
@@ -433,6 +434,30 @@ def evaluate_showdowns(rank_count, board_cards, combo_ids, stratum_level, payoff
     lib().orc_evaluate_showdowns(rank_count, B, P, amt.shape[1], _ptr(board), _ptr(combo), _ptr(level),
                                  _ptr(base), _ptr(amt), _ptr(out))
     return out
+
+
+def rb_complete(rank_count, board_cards, range_weights, stratum_level, payoff_baseline, stratum_amount, n_samples,
+                seed, selected_player=None):
+    """This build's estimator of the contract-v2 ``complete`` / ``complete_selected`` (hooks.py:2472-2477,
+    2512; law core_math.tex:664-684), restated on the host.  Parity with the external evaluator is
+    unpinned.  Returns (p_hat, v_hat, n_eff, status): [F,P,H] (or [F,H] with ``selected_player``)."""
+
+    board = np.ascontiguousarray(board_cards, dtype=np.uint8)
+    w = np.ascontiguousarray(range_weights, dtype=np.float32)
+    F, P, H = w.shape
+    level = np.ascontiguousarray(stratum_level, dtype=np.int32)
+    base = np.ascontiguousarray(payoff_baseline, dtype=np.float32)
+    amt = np.ascontiguousarray(stratum_amount, dtype=np.float32)
+    sd = np.ascontiguousarray(seed, dtype=np.int64).reshape(F)
+    sel = None if selected_player is None else np.ascontiguousarray(selected_player, dtype=np.int32).reshape(F)
+    shape = (F, P, H) if sel is None else (F, H)
+    p_hat = np.empty(shape, np.float32)
+    v_hat = np.empty(shape, np.float32)
+    n_eff = np.empty(F, np.float32)
+    status = lib().orc_rb_complete(int(rank_count), F, P, amt.shape[1], int(n_samples), _ptr(board), _ptr(w),
+                                   _ptr(level), _ptr(base), _ptr(amt), _ptr(sd), _ptr(sel), _ptr(p_hat),
+                                   _ptr(v_hat), _ptr(n_eff))
+    return p_hat, v_hat, n_eff, int(status)
 
 
 # ---------------------------------------------------------------- policy

@@ -1252,3 +1252,304 @@ int32_t orc_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *d
     }
     return 0;
 }
+
+/* ------------------------------------------------ Rao-Blackwell completion */
+
+/* Restatement of this build's estimator of the contract-v2 `complete` /
+ * `complete_selected` law (PreTerminalMC, docs/theory/core_math.tex:664-684,
+ * 1360-1380; called at pbg/games/poker/queued/hooks.py:2472-2477, 2512 on the
+ * rows of PokerStateMachine.rb_leaf, hooks.py:1218-1258).  The external
+ * evaluator's own implementation is not in the reference tree, so parity with
+ * it is unpinned; this function fixes the estimator the device kernel must
+ * reproduce bit for bit:
+ *   - range weights: non-positive, non-finite and board-conflicting hands
+ *     weigh 0;
+ *   - per seat, an fp32 CDF rounded from a double running sum whose 32
+ *     contiguous segments start from an inclusive Kogge-Stone scan of the
+ *     segment totals; Z = the double total; per-card masses summed in hand-id
+ *     order;
+ *   - sample i, seats in order: Z(dead) = (Z - sum of the dead cards' masses)
+ *     + sum of the weights of the dead-card pairs (inclusion-exclusion); the
+ *     weight multiplies by Z(dead)/Z; up to 16 CDF proposals (counter keys
+ *     (root i, path 0, draw attempt, lane seat) in the COMPLETION namespace of
+ *     the row's seed), the first disjoint from `dead` with positive weight
+ *     wins; else an exact scan of the restricted range (draw 16);
+ *   - missing board slots j dealt uniformly from the unused deck (path 1,
+ *     draw j); returns settled as evaluate_showdowns settles them;
+ *   - 64-bit fixed-point sums of q_i = rint(w_i 2^(Q-ew)) and
+ *     rint(w_i R 2^(Q-ew-er)), Q = 61 - ceil(log2 N), n_eff = W^2 / sum q^2
+ *     with sum q^2 reduced as 256 thread-strided partial sums, 32-lane
+ *     butterflies and warps in order.
+ * Returns the status bits (1: invalid board card or selected seat, 2: a row
+ * without sample mass). */
+
+#define RB_THREADS 256
+#define RB_ATTEMPTS 16
+
+static int rb_pair_id(int D, int a, int b) { return a * (2 * D - a - 1) / 2 + b - a - 1; }
+
+static int rb_ceil_log2(int n) {
+    int k = 0;
+    while ((1 << k) < n) ++k;
+    return k;
+}
+
+static int64_t rb_hand_value(int R, const int *strength, const int *cards7) {
+    int64_t best = -1;
+    int sub[5];
+    for (int a = 0; a < 7; ++a)
+        for (int b2 = a + 1; b2 < 7; ++b2) {
+            int n = 0;
+            for (int i = 0; i < 7; ++i) if (i != a && i != b2) sub[n++] = cards7[i];
+            int64_t v = five_value(sub, strength, R);
+            if (v > best) best = v;
+        }
+    return best;
+}
+
+int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t N, const uint8_t *board,
+                        const float *weights, const int32_t *level, const float *baseline, const float *amount,
+                        const int64_t *seed, const int32_t *selected, float *p_hat, float *v_hat, float *n_eff) {
+    const int D = 4 * R, first = 52 - D, H = D * (D - 1) / 2;
+    const uint64_t deck = (1ULL << D) - 1ULL;
+    int strength[N_CAT];
+    category_strength(R, strength);
+    int *hc = malloc(sizeof(int) * 2 * H);
+    float *wb = malloc(sizeof(float) * P * H), *cdf = malloc(sizeof(float) * P * H);
+    double *mass = malloc(sizeof(double) * P * D), *zd = malloc(sizeof(double) * P);
+    double *rw = malloc(sizeof(double) * N);
+    int *rh = malloc(sizeof(int) * N * P);
+    float *rr = malloc(sizeof(float) * N * P);
+    long long *pacc = malloc(sizeof(long long) * H), *vacc = malloc(sizeof(long long) * H);
+    int32_t status = 0;
+    for (int a = 0, id = 0; a < D; ++a)
+        for (int b = a + 1; b < D; ++b, ++id) {
+            hc[2 * id] = a;
+            hc[2 * id + 1] = b;
+        }
+    const int outputs = selected ? 1 : P;
+    for (int64_t f = 0; f < F; ++f) {
+        uint64_t bmask = 0;
+        int bc[5], bad = 0;
+        for (int j = 0; j < 5; ++j) {
+            int c = board[f * 5 + j];
+            bc[j] = c;
+            if (c == 255) continue;
+            if (c < first || c >= 52 || ((bmask >> (c - first)) & 1ULL)) bad = 1;
+            else bmask |= 1ULL << (c - first);
+        }
+        int sel = selected ? selected[f] : 0;
+        if (selected && (sel < 0 || sel >= P)) bad = 1;
+        if (bad) {
+            for (int64_t k = 0; k < (int64_t)outputs * H; ++k) {
+                p_hat[f * outputs * H + k] = 0.0f;
+                v_hat[f * outputs * H + k] = 0.0f;
+            }
+            n_eff[f] = 0.0f;
+            status |= 1;
+            continue;
+        }
+        for (int idx = 0; idx < P * H; ++idx) {
+            int h = idx % H;
+            float x = weights[f * P * H + idx];
+            int conflict = (int)(((bmask >> hc[2 * h]) | (bmask >> hc[2 * h + 1])) & 1ULL);
+            wb[idx] = (x > 0.0f && x <= FLT_MAX && !conflict) ? x : 0.0f;
+        }
+        for (int q = 0; q < P; ++q) {
+            const float *w = wb + q * H;
+            int seg = (H + 31) / 32;
+            double v[32], nv[32];
+            for (int l = 0; l < 32; ++l) {
+                int lo = l * seg < H ? l * seg : H, hi = lo + seg < H ? lo + seg : H;
+                double local = 0.0;
+                for (int h = lo; h < hi; ++h) local = local + (double)w[h];
+                v[l] = local;
+            }
+            for (int o = 1; o < 32; o <<= 1) {
+                for (int l = 0; l < 32; ++l) nv[l] = l >= o ? v[l - o] + v[l] : v[l];
+                memcpy(v, nv, sizeof v);
+            }
+            for (int l = 0; l < 32; ++l) {
+                int lo = l * seg < H ? l * seg : H, hi = lo + seg < H ? lo + seg : H;
+                double run = l ? v[l - 1] : 0.0;
+                for (int h = lo; h < hi; ++h) {
+                    run = run + (double)w[h];
+                    cdf[q * H + h] = (float)run;
+                }
+                if (l == 31) zd[q] = run;
+            }
+            for (int c = 0; c < D; ++c) {
+                double m = 0.0;
+                for (int a = 0; a < c; ++a) m = m + (double)w[rb_pair_id(D, a, c)];
+                for (int b = c + 1; b < D; ++b) m = m + (double)w[rb_pair_id(D, c, b)];
+                mass[q * D + c] = m;
+            }
+        }
+        const uint64_t ns = rng_namespace(seed[f], 0, 6 /* COMPLETION */);
+        for (int i = 0; i < N; ++i) {
+            double weight = 1.0;
+            uint64_t dead = 0;
+            int hand[6] = {0, 0, 0, 0, 0, 0};
+            for (int q = 0; q < P; ++q) {
+                const float *w = wb + q * H, *c = cdf + q * H;
+                const double *m = mass + q * D;
+                double z = zd[q], s1 = 0.0, s2 = 0.0;
+                for (uint64_t rest = dead; rest; rest &= rest - 1) {
+                    int a = __builtin_ctzll(rest);
+                    s1 = s1 + m[a];
+                    for (uint64_t r2 = rest & (rest - 1); r2; r2 &= r2 - 1)
+                        s2 = s2 + (double)w[rb_pair_id(D, a, __builtin_ctzll(r2))];
+                }
+                double zs = (z - s1) + s2;
+                if (!(z > 0.0) || !(zs > 0.0)) {
+                    weight = 0.0;
+                    break;
+                }
+                weight = weight * (zs / z);
+                int pick = -1;
+                float top = c[H - 1];
+                if (top > 0.0f) {
+                    float below = nextafterf(top, 0.0f);
+                    for (int a = 0; a < RB_ATTEMPTS; ++a) {
+                        float u = uniform_of(rng_key(ns, i, 0, a, q, 0));
+                        float t = u * top;
+                        if (t > below) t = below;
+                        int lo = 0, hi = H;
+                        while (lo < hi) {
+                            int mid = (lo + hi) >> 1;
+                            if (c[mid] > t) hi = mid;
+                            else lo = mid + 1;
+                        }
+                        if (lo >= H) lo = H - 1;
+                        int clash = (int)(((dead >> hc[2 * lo]) | (dead >> hc[2 * lo + 1])) & 1ULL);
+                        if (!clash && w[lo] > 0.0f) {
+                            pick = lo;
+                            break;
+                        }
+                    }
+                }
+                if (pick < 0) {
+                    double t = (double)uniform_of(rng_key(ns, i, 0, RB_ATTEMPTS, q, 0)) * zs;
+                    double run = 0.0;
+                    for (int h = 0; h < H; ++h) {
+                        float x = w[h];
+                        if (!(x > 0.0f)) continue;
+                        if (((dead >> hc[2 * h]) | (dead >> hc[2 * h + 1])) & 1ULL) continue;
+                        run = run + (double)x;
+                        pick = h;
+                        if (run > t) break;
+                    }
+                }
+                if (pick < 0) {
+                    weight = 0.0;
+                    break;
+                }
+                hand[q] = pick;
+                dead |= (1ULL << hc[2 * pick]) | (1ULL << hc[2 * pick + 1]);
+            }
+            float ret[6] = {0, 0, 0, 0, 0, 0};
+            if (weight > 0.0) {
+                uint64_t used = bmask | dead;
+                int cards[7];
+                for (int j = 0; j < 5; ++j) {
+                    int card = bc[j];
+                    if (card == 255) {
+                        uint64_t avail = deck & ~used;
+                        int n = __builtin_popcountll(avail);
+                        float u = uniform_of(rng_key(ns, i, 1, j, 0, 0));
+                        int k = (int)(u * (float)n);
+                        if (k >= n) k = n - 1;
+                        uint64_t r = avail;
+                        for (; k > 0; --k) r &= r - 1;
+                        int local = __builtin_ctzll(r);
+                        used |= 1ULL << local;
+                        card = local + first;
+                    }
+                    cards[j] = card;
+                }
+                int64_t value[6];
+                for (int p = 0; p < P; ++p) {
+                    value[p] = -1;
+                    if (level[f * P + p] >= 0) {
+                        cards[5] = hc[2 * hand[p]] + first;
+                        cards[6] = hc[2 * hand[p] + 1] + first;
+                        value[p] = rb_hand_value(R, strength, cards);
+                    }
+                    ret[p] = baseline[f * P + p];
+                }
+                for (int k = 0; k < strata; ++k) {
+                    float amt = amount[f * strata + k];
+                    if (!(amt > 0.0f)) continue;
+                    int64_t best = -1;
+                    for (int p = 0; p < P; ++p)
+                        if (value[p] >= 0 && level[f * P + p] >= k && value[p] > best) best = value[p];
+                    if (best < 0) continue;
+                    int winners = 0;
+                    for (int p = 0; p < P; ++p) winners += value[p] == best && level[f * P + p] >= k;
+                    float share = amt / (float)winners;
+                    for (int p = 0; p < P; ++p)
+                        if (value[p] == best && level[f * P + p] >= k) ret[p] += share;
+                }
+            }
+            rw[i] = weight;
+            for (int p = 0; p < P; ++p) {
+                rh[i * P + p] = hand[p];
+                rr[i * P + p] = ret[p];
+            }
+        }
+        double mw = 0.0, mr = 0.0;
+        for (int i = 0; i < N; ++i) {
+            if (!(rw[i] > 0.0)) continue;
+            mw = fmax(mw, rw[i]);
+            for (int p = 0; p < P; ++p) mr = fmax(mr, fabs((double)rr[i * P + p]));
+        }
+        int ew = 0, er = 0;
+        frexp(mw, &ew);
+        frexp(mr, &er);
+        const int Q = 61 - rb_ceil_log2(N);
+        long long W = 0;
+        double part[RB_THREADS];
+        for (int t = 0; t < RB_THREADS; ++t) {
+            double sq = 0.0;
+            for (int i = t; i < N; i += RB_THREADS) {
+                long long qi = llrint(ldexp(rw[i], Q - ew));
+                W += qi;
+                double qd = (double)qi;
+                sq = sq + qd * qd;
+            }
+            part[t] = sq;
+        }
+        double S2 = 0.0;
+        for (int wp = 0; wp < RB_THREADS / 32; ++wp) {
+            double v[32], nv[32];
+            memcpy(v, part + 32 * wp, sizeof v);
+            for (int o = 16; o > 0; o >>= 1) {
+                for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ o];
+                memcpy(v, nv, sizeof v);
+            }
+            S2 = S2 + v[0];
+        }
+        const double Wd = (double)W;
+        for (int o = 0; o < outputs; ++o) {
+            int p = selected ? sel : o;
+            memset(pacc, 0, sizeof(long long) * H);
+            memset(vacc, 0, sizeof(long long) * H);
+            for (int i = 0; i < N; ++i) {
+                double x = rw[i];
+                if (!(x > 0.0)) continue;
+                int h = rh[i * P + p];
+                pacc[h] += llrint(ldexp(x, Q - ew));
+                vacc[h] += llrint(ldexp(x * (double)rr[i * P + p], Q - ew - er));
+            }
+            float *po = p_hat + (f * outputs + o) * (int64_t)H, *vo = v_hat + (f * outputs + o) * (int64_t)H;
+            for (int h = 0; h < H; ++h) {
+                po[h] = W > 0 ? (float)((double)pacc[h] / Wd) : 0.0f;
+                vo[h] = pacc[h] != 0 ? (float)ldexp((double)vacc[h] / (double)pacc[h], er) : 0.0f;
+            }
+        }
+        n_eff[f] = W > 0 ? (float)fmin(Wd * Wd / S2, (double)N) : 0.0f;
+        if (W <= 0) status |= 2;
+    }
+    free(hc); free(wb); free(cdf); free(mass); free(zd); free(rw); free(rh); free(rr); free(pacc); free(vacc);
+    return status;
+}
