@@ -4,7 +4,9 @@
 // The reference delegates ranking to the external poker_gpu_evaluator; this
 // kernel ranks 7-card hands directly from rank-multiplicity bit planes and suit
 // masks (the board's built once per hand, each seat adding its hole cards),
-// with the category order and settlement of showdown.cuh.
+// with the category order and settlement of showdown.cuh; seats are compared
+// through hand_order, whose order is hand_value's (pbg_hand_values exports the
+// packed values themselves).
 #include "showdown.cuh"
 
 namespace pbg {
@@ -16,7 +18,7 @@ __device__ __forceinline__ int64_t hand_value7(const int* cards, const Strength&
     return hand_value(h, S, R);
 }
 
-__global__ void showdown_kernel(Strength S, int R, int D, int first, int64_t B, int P, int strata,
+__global__ void showdown_kernel(CategoryOrder O, int R, int D, int first, int64_t B, int P, int strata,
                                 const uint8_t* board, const int32_t* combo, const int32_t* level,
                                 const float* baseline, const float* amount, float* out) {
     // seat loops run over the MAXP slots with an early exit, so the per-seat values stay in registers
@@ -45,7 +47,7 @@ __global__ void showdown_kernel(Strength S, int R, int D, int first, int64_t B, 
                 HandCounts h = on_board;
                 h.add(c0);
                 h.add(c1);
-                value[p] = hand_value(h, S, R);
+                value[p] = hand_order(h, O, R);
             }
         }
         float acc[MAXP];
@@ -90,7 +92,7 @@ int pbg_evaluate_showdowns(int32_t rank_count, int64_t B, int32_t P, int32_t str
     PBG_REQUIRE(board && combo && level && baseline && amount && out, "evaluate_showdowns: null argument");
     if (B == 0) return PBG_OK;
     int D = 4 * rank_count;
-    showdown_kernel<<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(category_strength(rank_count), rank_count, D,
+    showdown_kernel<<<stride_grid(B, 128), 128, 0, as_stream(stream)>>>(category_order(rank_count), rank_count, D,
                                                                         52 - D, B, P, strata, board, combo, level,
                                                                         baseline, amount, out);
     return launch_status("evaluate_showdowns");

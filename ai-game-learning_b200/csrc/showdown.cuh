@@ -157,6 +157,94 @@ __device__ __forceinline__ int64_t hand_value(const HandCounts& h, const Strengt
 }
 
 
+// ---------------------------------------------------- order-equivalent values
+// Settlement needs only the order (and ties) of the seats' hands, so the
+// showdown and completion kernels rank with hand_order: for any two hands of
+// one deck its values compare exactly as hand_value's packed values do.  The
+// strongest category present decides (hand_value's maximum over all categories
+// is that one): every category's presence is set at its strength's bit and the
+// highest bit wins, without a data-dependent loop; its kickers are rank masks
+// (the k highest ranks of a set: equal-size masks compare as the descending
+// rank lists do).
+struct CategoryOrder {
+    unsigned bit[N_CAT];  // 1 << strength of each category present in the deck, 0 if absent
+};
+
+inline CategoryOrder category_order(int R) {
+    const Strength S = category_strength(R);
+    CategoryOrder o;
+    for (int c = 0; c < N_CAT; ++c) o.bit[c] = S.s[c] >= 0 ? 1u << S.s[c] : 0u;
+    return o;
+}
+
+// The k highest set bits of m (m holds at most seven ranks).
+__device__ __forceinline__ unsigned keep_top(unsigned m, int k) {
+    #pragma unroll
+    for (int r = 0; r < 6; ++r)
+        if (__popc(m) > k) m &= m - 1;
+    return m;
+}
+
+// Highest rank of a five-rank run in m (the wheel A-2-3-4-5 counts on the full deck), -1 if none.
+__device__ __forceinline__ int straight_top(unsigned m, int R) {
+    const unsigned run = m & (m >> 1) & (m >> 2) & (m >> 3) & (m >> 4);
+    if (run) return 35 - __clz(run);
+    return (R == 13 && (m & 0x100Fu) == 0x100Fu) ? 3 : -1;
+}
+
+__device__ __forceinline__ int64_t hand_order(const HandCounts& h, const CategoryOrder& O, int R) {
+    const unsigned ranks = h.ge1, ge2 = h.ge2, ge3 = h.ge3, ge4 = h.ge4;
+    unsigned flush = 0;
+    #pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const unsigned m = (unsigned)(h.suits >> (16 * s)) & 0x1FFFu;
+        if (__popc(m) >= 5) flush = m;
+    }
+    const int sf = flush ? straight_top(flush, R) : -1;
+    const int st = straight_top(ranks, R);
+    const int t = ge3 ? 31 - __clz(ge3) : 0;
+    const unsigned fh = ge3 ? (ge2 & ~(1u << t)) : 0u;
+    unsigned present = O.bit[HIGH_CARD];
+    if (ge2) present |= O.bit[PAIR];
+    if (__popc(ge2) >= 2) present |= O.bit[TWO_PAIR];
+    if (ge3) present |= O.bit[TRIPS];
+    if (st >= 0) present |= O.bit[STRAIGHT];
+    if (flush) present |= O.bit[FLUSH];
+    if (fh) present |= O.bit[FULL_HOUSE];
+    if (ge4) present |= O.bit[QUADS];
+    if (sf >= 0) present |= O.bit[STRAIGHT_FLUSH];
+    const int strength = 31 - __clz(present);
+    const unsigned top = 1u << strength;
+    unsigned a = 0, b = 0;
+    if (top == O.bit[STRAIGHT_FLUSH]) {
+        a = (unsigned)sf;
+    } else if (top == O.bit[QUADS]) {
+        const int q = 31 - __clz(ge4);
+        a = q;
+        b = keep_top(ranks & ~(1u << q), 1);
+    } else if (top == O.bit[FULL_HOUSE]) {
+        a = t;
+        b = 31 - __clz(fh);
+    } else if (top == O.bit[FLUSH]) {
+        b = keep_top(flush, 5);
+    } else if (top == O.bit[STRAIGHT]) {
+        a = (unsigned)st;
+    } else if (top == O.bit[TRIPS]) {
+        a = t;
+        b = keep_top(ranks & ~(1u << t), 2);
+    } else if (top == O.bit[TWO_PAIR]) {
+        a = keep_top(ge2, 2);
+        b = keep_top(ranks & ~a, 1);
+    } else if (top == O.bit[PAIR]) {
+        const int p = 31 - __clz(ge2);
+        a = p;
+        b = keep_top(ranks & ~(1u << p), 3);
+    } else {
+        b = keep_top(ranks, 5);
+    }
+    return ((int64_t)strength << 26) | ((int64_t)a << 13) | b;
+}
+
 // Chip settlement of one hand (the contract-v2 payoff: hooks.py:2252-2295): each
 // seat starts from its baseline; stratum k's amount goes in equal shares to the
 // strongest seats among those with level >= k and a valid hand (value >= 0).

@@ -1265,28 +1265,37 @@ int32_t orc_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *d
  *   - range weights: non-positive, non-finite and board-conflicting hands
  *     weigh 0;
  *   - per seat, an fp32 CDF rounded from a double running sum whose 32
- *     contiguous segments start from an inclusive Kogge-Stone scan of the
- *     segment totals; Z = the double total; per-card masses summed in hand-id
- *     order;
- *   - sample i, seats in order: Z(dead) = (Z - sum of the dead cards' masses)
- *     + sum of the weights of the dead-card pairs (inclusion-exclusion); the
- *     weight multiplies by Z(dead)/Z; up to 16 CDF proposals (counter keys
- *     (root i, path 0, draw attempt, lane seat) in the COMPLETION namespace of
- *     the row's seed), the first disjoint from `dead` with positive weight
- *     wins; else an exact scan of the restricted range (draw 16);
- *   - missing board slots j dealt uniformly from the unused deck (path 1,
- *     draw j); returns settled as evaluate_showdowns settles them;
+ *     contiguous segments (ceil(H/32) rounded up to 4 hands) start from an
+ *     inclusive Kogge-Stone scan of the segment totals; Z = the double total;
+ *     per-card masses summed in hand-id order;
+ *   - sample i (base key rng_key(root i) in the COMPLETION namespace of the
+ *     row's seed; draw `code` uses mix63(base + (code + 1) * 0x9E3779B97F4A7C15)),
+ *     seats q in order: Z(dead) = (Z - the dead cards' masses, seat by seat) +
+ *     (each earlier hand's own weight, then its four cross pairs with the hands
+ *     before it); the weight multiplies by Z(dead)/Z; up to 16 CDF proposals
+ *     (codes 32q + attempt), the first disjoint from `dead` with positive
+ *     weight wins; else an exact scan of the restricted range (code 32q + 16);
+ *   - missing board slots j dealt uniformly from the unused deck (code
+ *     1024 + j); returns settled as evaluate_showdowns settles them;
  *   - 64-bit fixed-point sums of q_i = rint(w_i 2^(Q-ew)) and
- *     rint(w_i R 2^(Q-ew-er)), Q = 61 - ceil(log2 N), n_eff = W^2 / sum q^2
- *     with sum q^2 reduced as 256 thread-strided partial sums, 32-lane
- *     butterflies and warps in order.
+ *     rint(w_i R 2^(Q-ew-er)), Q = 61 - ceil(log2 N); p_hat = sum q * (1/W),
+ *     v_hat = (sum m / sum q) 2^er; n_eff = W^2 / sum q^2 with sum q^2 reduced
+ *     as 256 thread-strided partial sums, 32-lane butterflies and warps in
+ *     order.
  * Returns the status bits (1: invalid board card or selected seat, 2: a row
  * without sample mass). */
 
 #define RB_THREADS 256
 #define RB_ATTEMPTS 16
 
-static int rb_pair_id(int D, int a, int b) { return a * (2 * D - a - 1) / 2 + b - a - 1; }
+static int rb_pair_id(int D, int a, int b) {
+    int lo = a < b ? a : b, hi = a < b ? b : a;
+    return lo * (2 * D - lo - 1) / 2 + hi - lo - 1;
+}
+
+static float rb_uniform(int64_t base, int code) {
+    return uniform_of(mix63((int64_t)(((uint64_t)base + (uint64_t)(code + 1) * 0x9E3779B97F4A7C15ULL) & M63)));
+}
 
 static int rb_ceil_log2(int n) {
     int k = 0;
@@ -1357,7 +1366,7 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
         }
         for (int q = 0; q < P; ++q) {
             const float *w = wb + q * H;
-            int seg = (H + 31) / 32;
+            int seg = (((H + 31) / 32) + 3) & ~3;
             double v[32], nv[32];
             for (int l = 0; l < 32; ++l) {
                 int lo = l * seg < H ? l * seg : H, hi = lo + seg < H ? lo + seg : H;
@@ -1387,18 +1396,26 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
         }
         const uint64_t ns = rng_namespace(seed[f], 0, 6 /* COMPLETION */);
         for (int i = 0; i < N; ++i) {
+            const int64_t key = rng_key(ns, i, 0, 0, 0, 0);
             double weight = 1.0;
             uint64_t dead = 0;
-            int hand[6] = {0, 0, 0, 0, 0, 0};
+            int hand[6] = {0, 0, 0, 0, 0, 0}, ca[6] = {0, 0, 0, 0, 0, 0}, cb[6] = {0, 0, 0, 0, 0, 0};
             for (int q = 0; q < P; ++q) {
                 const float *w = wb + q * H, *c = cdf + q * H;
                 const double *m = mass + q * D;
                 double z = zd[q], s1 = 0.0, s2 = 0.0;
-                for (uint64_t rest = dead; rest; rest &= rest - 1) {
-                    int a = __builtin_ctzll(rest);
-                    s1 = s1 + m[a];
-                    for (uint64_t r2 = rest & (rest - 1); r2; r2 &= r2 - 1)
-                        s2 = s2 + (double)w[rb_pair_id(D, a, __builtin_ctzll(r2))];
+                for (int j = 0; j < q; ++j) {
+                    s1 = s1 + m[ca[j]];
+                    s1 = s1 + m[cb[j]];
+                }
+                for (int j = 0; j < q; ++j) {
+                    s2 = s2 + (double)w[hand[j]];
+                    for (int k = 0; k < j; ++k) {
+                        s2 = s2 + (double)w[rb_pair_id(D, ca[k], ca[j])];
+                        s2 = s2 + (double)w[rb_pair_id(D, ca[k], cb[j])];
+                        s2 = s2 + (double)w[rb_pair_id(D, cb[k], ca[j])];
+                        s2 = s2 + (double)w[rb_pair_id(D, cb[k], cb[j])];
+                    }
                 }
                 double zs = (z - s1) + s2;
                 if (!(z > 0.0) || !(zs > 0.0)) {
@@ -1411,7 +1428,7 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
                 if (top > 0.0f) {
                     float below = nextafterf(top, 0.0f);
                     for (int a = 0; a < RB_ATTEMPTS; ++a) {
-                        float u = uniform_of(rng_key(ns, i, 0, a, q, 0));
+                        float u = rb_uniform(key, q * 32 + a);
                         float t = u * top;
                         if (t > below) t = below;
                         int lo = 0, hi = H;
@@ -1429,7 +1446,7 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
                     }
                 }
                 if (pick < 0) {
-                    double t = (double)uniform_of(rng_key(ns, i, 0, RB_ATTEMPTS, q, 0)) * zs;
+                    double t = (double)rb_uniform(key, q * 32 + RB_ATTEMPTS) * zs;
                     double run = 0.0;
                     for (int h = 0; h < H; ++h) {
                         float x = w[h];
@@ -1445,7 +1462,9 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
                     break;
                 }
                 hand[q] = pick;
-                dead |= (1ULL << hc[2 * pick]) | (1ULL << hc[2 * pick + 1]);
+                ca[q] = hc[2 * pick];
+                cb[q] = hc[2 * pick + 1];
+                dead |= (1ULL << ca[q]) | (1ULL << cb[q]);
             }
             float ret[6] = {0, 0, 0, 0, 0, 0};
             if (weight > 0.0) {
@@ -1456,7 +1475,7 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
                     if (card == 255) {
                         uint64_t avail = deck & ~used;
                         int n = __builtin_popcountll(avail);
-                        float u = uniform_of(rng_key(ns, i, 1, j, 0, 0));
+                        float u = rb_uniform(key, 1024 + j);
                         int k = (int)(u * (float)n);
                         if (k >= n) k = n - 1;
                         uint64_t r = avail;
@@ -1529,7 +1548,7 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
             }
             S2 = S2 + v[0];
         }
-        const double Wd = (double)W;
+        const double Wd = (double)W, invW = W > 0 ? 1.0 / Wd : 0.0;
         for (int o = 0; o < outputs; ++o) {
             int p = selected ? sel : o;
             memset(pacc, 0, sizeof(long long) * H);
@@ -1543,8 +1562,8 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
             }
             float *po = p_hat + (f * outputs + o) * (int64_t)H, *vo = v_hat + (f * outputs + o) * (int64_t)H;
             for (int h = 0; h < H; ++h) {
-                po[h] = W > 0 ? (float)((double)pacc[h] / Wd) : 0.0f;
-                vo[h] = pacc[h] != 0 ? (float)ldexp((double)vacc[h] / (double)pacc[h], er) : 0.0f;
+                po[h] = pacc[h] != 0 ? (float)((double)pacc[h] * invW) : 0.0f;
+                vo[h] = pacc[h] != 0 ? (float)(((double)vacc[h] / (double)pacc[h]) * ldexp(1.0, er)) : 0.0f;
             }
         }
         n_eff[f] = W > 0 ? (float)fmin(Wd * Wd / S2, (double)N) : 0.0f;
