@@ -59,6 +59,18 @@ class EngineStateMachine(PokerStateMachine):
         super().__init__(_geometry(geometry))
         self.reference_geometry = geometry
 
+    def combo_cards(self, combo_ids):
+        """hooks.py:1128-1143.  The reference also builds host-side tables with it (the Rao-Blackwell
+        target algebra, operations.py:593-595, passes a CPU arange): those ids are decoded by the
+        same kernel on the current CUDA device and the cards returned where the ids live."""
+
+        if combo_ids.is_cuda:
+            return super().combo_cards(combo_ids)
+        import torch
+
+        return super().combo_cards(combo_ids.to(torch.device("cuda", torch.cuda.current_device()))).to(
+            combo_ids.device)
+
 
 class EnginePolicyOperator(PokerPolicyOperator):
     """The device composite policy with the reference constructor's keyword (policy.py:139-142)."""

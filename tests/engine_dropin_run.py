@@ -1,12 +1,13 @@
 """One training iteration of the reference's own engine, optionally routed to libpbgb200.
 
     python tests/engine_dropin_run.py <out_dir> <reference|b200|b200_learner> [roots] [iterations] [program]
+                                      [sampled|rao_blackwell]
 
 Test infrastructure for tests/test_gpu_engine_dropin.py (run in a fresh process
 so that the two engines never share imported state).  It loads the reference
 package installed under baseline/_ref, builds a heads-up 8bb 4-rank
-self-play run (sampled private estimator, sequential rollout, a small
-transformer), and runs ``pbg.runtime.TrainingSession.step`` once; with
+self-play run (sampled private estimator, or Rao-Blackwell with evaluator
+completion of 64 samples per leaf; sequential rollout, a small transformer), and runs ``pbg.runtime.TrainingSession.step`` once; with
 ``b200`` it first calls ``pbg_b200.engine.install()`` so that the state
 machine, the composite policy and the layered targets of that same engine run
 on this build's kernels (``b200_learner``: the learner's loss program too).  The learner's tensor program runs eagerly in both
@@ -28,7 +29,7 @@ sys.path.append(os.path.join(ROOT, "baseline", "_ref"))
 
 CONFIG = """kind: nlhe_run_v1
 scientific:
-  mode: {{training_regime: self_play, rollout_mode: sequential, private_estimator: sampled}}
+  mode: {{training_regime: self_play, rollout_mode: sequential, private_estimator: {estimator}}}{completion}
   game: {{players: 2, stack_bb: 8.0, rank_count: 4}}
   model:
     d_model: 32
@@ -71,6 +72,8 @@ def main() -> None:
     roots = int(sys.argv[3]) if len(sys.argv) > 3 else 16
     iterations = int(sys.argv[4]) if len(sys.argv) > 4 else 1
     program = sys.argv[5] if len(sys.argv) > 5 else "eager"
+    estimator = sys.argv[6] if len(sys.argv) > 6 else "sampled"
+    completion = "\n  completion: {samples: 64}" if estimator == "rao_blackwell" else ""
     import torch
 
     handle = None
@@ -84,8 +87,8 @@ def main() -> None:
     os.makedirs(out, exist_ok=True)
     path = os.path.join(out, f"{arm}.yaml")
     with open(path, "w") as f:
-        f.write(CONFIG.format(roots=roots, iterations=iterations, program=program,
-                              out=os.path.join(out, f"run_{arm}")))
+        f.write(CONFIG.format(roots=roots, iterations=iterations, program=program, estimator=estimator,
+                              completion=completion, out=os.path.join(out, f"run_{arm}")))
     # record the flat gradient rows each optimizer transition receives (pbg/core/optimization.py:394-399)
     from pbg.core import optimization
 

@@ -2,7 +2,8 @@
 
 The reference package (pbg, installed under baseline/_ref) runs one full
 iteration -- rollout, completion, targets, learner, optimizer step -- twice
-from the same seed in fresh processes (tests/engine_dropin_run.py): once
+from the same seed in fresh processes (tests/engine_dropin_run.py), with the
+sampled and with the Rao-Blackwell private estimator: once
 unmodified and once after ``pbg_b200.engine.install()`` has routed its state
 machine, composite policy and layered targets to libpbgb200.  The drop-in
 must leave the engine's results where the reference puts them:
@@ -38,23 +39,27 @@ REF = os.path.join(ROOT, "baseline", "_ref", "pbg")
 REF_TARGETS_SOURCE = os.path.join(REF, "core", "csrc", "layered_targets.cu")
 
 
-def _run(out, arm):
+def _run(out, arm, estimator):
     env = dict(os.environ, TORCH_CUDA_ARCH_LIST=os.environ.get("TORCH_CUDA_ARCH_LIST", "10.0"))
-    proc = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "engine_dropin_run.py"), out, arm, "16"],
-                          capture_output=True, text=True, timeout=900, env=env)
+    proc = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "engine_dropin_run.py"), out, arm, "16", "1",
+                           "eager", estimator], capture_output=True, text=True, timeout=900, env=env)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-6000:]
     return torch.load(os.path.join(out, f"{arm}.pt"), weights_only=False)
 
 
 @pytest.mark.skipif(not os.path.isfile(REF_TARGETS_SOURCE),
                     reason="the reference package (with its CUDA sources) is not installed under baseline/_ref")
+@pytest.mark.parametrize("estimator", ["sampled", "rao_blackwell"])
 @pytest.mark.parametrize("arm", ["b200", "b200_learner"])
-def test_reference_engine_runs_on_b200_kernels(tmp_path, arm):
+def test_reference_engine_runs_on_b200_kernels(tmp_path, arm, estimator):
     """b200: state machine, policy and targets swapped; b200_learner: the loss program as well
-    (``LearnerOperation.forward_loss`` -> one pbg_poker_learner_objective launch)."""
+    (``LearnerOperation.forward_loss`` -> one pbg_poker_learner_objective launch).  With the
+    Rao-Blackwell estimator the leaves go through this build's ``rb_leaf`` and the reference's
+    completion binding, whose evaluator (``complete``, this build's module in both runs) draws 64
+    samples per leaf."""
 
-    ref = _run(str(tmp_path), "reference")
-    b200 = _run(str(tmp_path), arm)
+    ref = _run(str(tmp_path), "reference", estimator)
+    b200 = _run(str(tmp_path), arm, estimator)
     assert b200["installed"] and any("PokerStateMachine" in name for name in b200["installed"])
     assert ("forward_loss" in " ".join(b200["installed"])) == (arm == "b200_learner")
     assert (b200["fused_calls"] > 0) == (arm == "b200_learner")
