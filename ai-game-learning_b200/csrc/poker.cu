@@ -491,10 +491,11 @@ __global__ void combo_class_kernel(Geo d, int32_t* out) {
     }
 }
 
-// Fused sampled rollout step: one warp per hand ----------------------------
+// Fused sampled rollout step: one thread per hand ---------------------------
 struct StepArgs {
     Geo d;
     int64_t B;
+    const int32_t* list;   // work list mode: *list = live hands, list[1..] their indices (else NULL)
     pbg_state st;
     pbg_history hist;
     int64_t* root_path;
@@ -543,15 +544,20 @@ __device__ __forceinline__ void warp_smallest3(uint64_t ns, int64_t root, int64_
 // consecutive hands, so every state column is read and written coalesced.
 // The loop is warp-uniform: hands that must deal a street are dealt by the
 // whole warp (warp_smallest3), one hand at a time.
+//
+// Work list mode (A.list): a compaction pass has already written the outputs of
+// the terminal hands and listed the live ones, so every lane of a warp owns a
+// live hand and late steps, where few hands are left, run dense warps.
 template <int P>
 __global__ void __launch_bounds__(128) rollout_step_kernel(StepArgs A) {
     const Geo& d = A.d;
     const int lane = threadIdx.x & 31;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t base = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); base < A.B; base += stride) {
-        const int64_t b = base + lane;
-        const bool valid = b < A.B;
-        const bool live = valid && !A.st.terminal[b];
+    const int64_t n = A.list ? (int64_t)A.list[0] : A.B;
+    for (int64_t base = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); base < n; base += stride) {
+        const bool valid = base + lane < n;
+        const int64_t b = A.list ? (valid ? (int64_t)A.list[1 + base + lane] : 0) : base + lane;
+        const bool live = valid && (A.list || !A.st.terminal[b]);
         if (valid && !live) {
             A.action[b] = -1;
             A.selected[b] = 0.0f;
@@ -636,6 +642,36 @@ __global__ void __launch_bounds__(128) rollout_step_kernel(StepArgs A) {
         }
         if (A.new_leaf) A.new_leaf[b] = h.terminal;
         if (h.terminal) write_leaf(h, d.D, d.first, A.leaf, b);
+    }
+}
+
+// Work list of a rollout step: the terminal hands get the step's "no decision"
+// outputs (action -1, no leaf), the live ones are appended to list[1..] with one
+// atomic per warp (list order does not matter: every draw is addressed by the
+// hand's own root and path).  list[0] must be 0 on entry.
+__global__ void __launch_bounds__(256) rollout_list_kernel(int64_t B, const uint8_t* terminal, int32_t* action,
+                                                           float* selected, int32_t* decision, uint8_t* new_leaf,
+                                                           int32_t* list) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t base = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); base < B;
+         base += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = base + lane;
+        const bool valid = b < B;
+        const bool live = valid && !terminal[b];
+        if (valid && !live) {
+            action[b] = -1;
+            selected[b] = 0.0f;
+            if (new_leaf) new_leaf[b] = 0;
+            if (decision) {
+                decision[4 * b] = -1; decision[4 * b + 1] = -1; decision[4 * b + 2] = 1; decision[4 * b + 3] = 0;
+            }
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, live);
+        if (m == 0u) continue;
+        int start = 0;
+        if (lane == 0) start = atomicAdd(list, __popc(m));
+        start = __shfl_sync(0xffffffffu, start, 0);
+        if (live) list[1 + start + __popc(m & ((1u << lane) - 1u))] = (int32_t)b;
     }
 }
 
@@ -1001,10 +1037,10 @@ int pbg_combo_class(pbg_geometry g, int32_t* out, void* stream) {
     return launch_status("combo_class");
 }
 
-int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, int64_t* root_path,
-                     const int64_t* lane, const int64_t* retry_epoch, int64_t seed, int64_t iteration,
-                     pbg_policy pol, int32_t* action, float* selected_log, int32_t* decision, uint8_t* new_leaf,
-                     pbg_leaf leaf, void* stream) {
+static int rollout_step_impl(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, int64_t* root_path,
+                             const int64_t* lane, const int64_t* retry_epoch, int64_t seed, int64_t iteration,
+                             pbg_policy pol, int32_t* action, float* selected_log, int32_t* decision,
+                             uint8_t* new_leaf, pbg_leaf leaf, int32_t* worklist, void* stream) {
     int rc = check_geometry(g);
     if (rc) return rc;
     Geo d = derive(g);
@@ -1014,9 +1050,20 @@ int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, 
     PBG_REQUIRE(pol.rows == 1 || pol.rows >= d.H, "rollout_step: policy rows must be 1 or >= H (%d)", d.H);
     PBG_REQUIRE(leaf.board && leaf.combo && leaf.level && leaf.baseline && leaf.amount, "rollout_step: null leaf column");
     PBG_REQUIRE(hist.tokens == 0 || hist.mask, "rollout_step: history without mask");
+    PBG_REQUIRE(B <= INT32_MAX, "rollout_step: at most 2^31 - 1 hands");
     if (B == 0) return PBG_OK;
+    if (worklist) {
+        int err = cuda_status(cudaMemsetAsync(worklist, 0, sizeof(int32_t), as_stream(stream)), "rollout_step: list");
+        if (err) return err;
+        rollout_list_kernel<<<stride_grid(B, 256, 8), 256, 0, as_stream(stream)>>>(B, st.terminal, action,
+                                                                                   selected_log, decision, new_leaf,
+                                                                                   worklist);
+        err = launch_status("rollout_step: list");
+        if (err) return err;
+    }
     StepArgs A;
-    A.d = d; A.B = B; A.st = st; A.hist = hist; A.root_path = root_path; A.lane = lane; A.retry = retry_epoch;
+    A.d = d; A.B = B; A.list = worklist; A.st = st; A.hist = hist; A.root_path = root_path; A.lane = lane;
+    A.retry = retry_epoch;
     A.ns_action = rng_namespace(seed, iteration, ACTION);
     A.ns_chance = rng_namespace(seed, iteration, CHANCE);
     A.pol = pol; A.action = action; A.selected = selected_log; A.decision = decision; A.new_leaf = new_leaf;
@@ -1024,6 +1071,23 @@ int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, 
     const int block = 128;
     PBG_DISPATCH_P(g.players, rollout_step_kernel<PP><<<stride_grid(B, block, 16), block, 0, as_stream(stream)>>>(A));
     return launch_status("rollout_step");
+}
+
+int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, int64_t* root_path,
+                     const int64_t* lane, const int64_t* retry_epoch, int64_t seed, int64_t iteration,
+                     pbg_policy pol, int32_t* action, float* selected_log, int32_t* decision, uint8_t* new_leaf,
+                     pbg_leaf leaf, void* stream) {
+    return rollout_step_impl(g, B, st, hist, root_path, lane, retry_epoch, seed, iteration, pol, action,
+                             selected_log, decision, new_leaf, leaf, nullptr, stream);
+}
+
+int pbg_rollout_step_listed(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist, int64_t* root_path,
+                            const int64_t* lane, const int64_t* retry_epoch, int64_t seed, int64_t iteration,
+                            pbg_policy pol, int32_t* action, float* selected_log, int32_t* decision,
+                            uint8_t* new_leaf, pbg_leaf leaf, int32_t* worklist, void* stream) {
+    PBG_REQUIRE(worklist, "rollout_step_listed: null work list");
+    return rollout_step_impl(g, B, st, hist, root_path, lane, retry_epoch, seed, iteration, pol, action,
+                             selected_log, decision, new_leaf, leaf, worklist, stream);
 }
 
 int pbg_reach_update(pbg_geometry g, int64_t B, pbg_state st, pbg_policy pol, const int32_t* action,

@@ -106,6 +106,7 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_policy_learner_forward": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_policy_learner_backward": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P, _P, _P, PolG, _P]),
     "pbg_rollout_step": (_I32, [G, _I64, S, Hs, _P, _P, _P, _I64, _I64, Pol, _P, _P, _P, _P, L, _P]),
+    "pbg_rollout_step_listed": (_I32, [G, _I64, S, Hs, _P, _P, _P, _I64, _I64, Pol, _P, _P, _P, _P, L, _P, _P]),
     "pbg_reach_update": (_I32, [G, _I64, S, Pol, _P, _P, _P, _P]),
     "pbg_ppo_partials_size": (_I64, [_I64, _I32]),
     "pbg_ppo_categorical_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),

@@ -42,6 +42,7 @@ class RolloutArena:
     new_leaf: Tensor       # [B] bool
     leaf: dict             # sampled_leaf columns
     history_length: Tensor  # [B] int32 tokens used (kept by the kernel)
+    worklist: Tensor | None = None  # [B+1] int32: the live hands of the current step (count first)
 
     @property
     def rows(self) -> int:
@@ -49,8 +50,13 @@ class RolloutArena:
 
 
 class RolloutStep:
-    def __init__(self, geometry: NLHEGeometry, *, seed: int, iteration: int, with_history: bool = True) -> None:
+    def __init__(self, geometry: NLHEGeometry, *, seed: int, iteration: int, with_history: bool = True,
+                 work_list: bool = False) -> None:
         self.geometry = geometry
+        # work_list: list the live hands first and step them in dense warps (pbg_rollout_step_listed).
+        # Same results; on the HU 100bb rollout it is slower than one thread per row (the extra pass
+        # and the gathered state cost more than the idle lanes of finished hands).
+        self.work_list = work_list
         self.machine = PokerStateMachine(geometry)
         self.seed = int(seed)
         self.iteration = int(iteration)
@@ -72,17 +78,25 @@ class RolloutStep:
             torch.zeros((rows, 4), dtype=torch.int32, device=device),
             torch.zeros(rows, dtype=torch.bool, device=device),
             self.machine._leaf_tensors(rows, device),
-            torch.zeros(rows, dtype=torch.int32, device=device))
+            torch.zeros(rows, dtype=torch.int32, device=device),
+            torch.zeros(rows + 1, dtype=torch.int32, device=device) if self.work_list else None)
 
     def step(self, arena: RolloutArena, raw) -> None:
-        """Advance every non-terminal hand by one player decision (in place)."""
+        """Advance every non-terminal hand by one player decision (in place).
+
+        With the arena's work list (``work_list=True``) the live hands are listed first and the step
+        runs dense warps over them (``pbg_rollout_step_listed``); the results are the same."""
 
         pol, keep, rows = policy_struct(raw)
         hist = arena.history.c(arena.history_length) if self.with_history else N.History(*([None] * 10), 0, None)
         leaf = N.Leaf(*(ptr(v) for v in arena.leaf.values()))
-        call("pbg_rollout_step", self.geometry.c, arena.rows, arena.state.c(), hist, ptr(arena.root_path),
-             ptr(arena.lane), ptr(arena.retry_epoch), self.seed, self.iteration, pol, ptr(arena.action),
-             ptr(arena.selected_log), ptr(arena.decision), ptr(arena.new_leaf), leaf, stream(arena.state.device))
+        args = (self.geometry.c, arena.rows, arena.state.c(), hist, ptr(arena.root_path), ptr(arena.lane),
+                ptr(arena.retry_epoch), self.seed, self.iteration, pol, ptr(arena.action), ptr(arena.selected_log),
+                ptr(arena.decision), ptr(arena.new_leaf), leaf)
+        if arena.worklist is not None:
+            call("pbg_rollout_step_listed", *args, ptr(arena.worklist), stream(arena.state.device))
+        else:
+            call("pbg_rollout_step", *args, stream(arena.state.device))
 
     def reach_update(self, arena: RolloutArena, raw, log_reach: Tensor) -> None:
         """hooks.py:1641-1703 for the decision just taken (in place)."""

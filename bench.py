@@ -692,7 +692,8 @@ def rollout_component(device, hands=65_536, seed=0):
     return {"workload": "fused rollout step, HU 100bb R13, 65,536 hands to terminal, raw policy at the actor row",
             "decisions": decisions, "steps": len(counts), "ms": total_ms,
             "decisions_per_s": decisions / (total_ms / 1000.0),
-            "first_step_us": 1000.0 * times[0],
+            "first_step_us": 1000.0 * times[0], "step_us": [round(1000.0 * t, 1) for t in times],
+            "live_hands": counts,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "bytes_per_decision": ROLLOUT_BYTES_HU,
                          "kernel": "rollout_step_kernel"},

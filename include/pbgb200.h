@@ -328,6 +328,17 @@ int pbg_rollout_step(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist,
                      float *selected_log, int32_t *decision, uint8_t *new_leaf, pbg_leaf leaf,
                      void *stream);
 
+/* pbg_rollout_step over a work list: a compaction pass writes the terminal
+ * hands' outputs (action -1, no leaf) and lists the live hands in
+ * worklist[1..] (worklist[0] = their count; B + 1 device int32, no other
+ * contract), then the step runs one thread per listed hand, so warps stay
+ * full when few hands are left.  Results are identical to pbg_rollout_step. */
+int pbg_rollout_step_listed(pbg_geometry g, int64_t B, pbg_state st, pbg_history hist,
+                            int64_t *root_path, const int64_t *lane, const int64_t *retry_epoch,
+                            int64_t seed, int64_t iteration, pbg_policy pol, int32_t *action,
+                            float *selected_log, int32_t *decision, uint8_t *new_leaf, pbg_leaf leaf,
+                            int32_t *worklist, void *stream);
+
 /* hooks.py:1641-1656 and 1688-1703: add the selected action's log policy of
  * every private hand to the actor's log-reach row, then mask hands whose
  * cards meet the (post-chance) board with -inf for every seat.

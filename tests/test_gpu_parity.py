@@ -252,6 +252,40 @@ def test_showdown_matches_oracle(ranks, players):
 # ------------------------------------------------------ fused rollout
 
 
+@pytest.mark.parametrize("players,ranks,stack", [(2, 13, 100.0), (6, 13, 50.0), (3, 4, 8.0)])
+def test_rollout_work_list_equals_dense_step(players, ranks, stack):
+    """pbg_rollout_step_listed (live hands listed, dense warps) and pbg_rollout_step (one thread per
+    row) leave identical arenas after every step of a full rollout."""
+
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.rollout import RolloutStep
+
+    geometry = NLHEGeometry(players, stack, ranks)
+    B = 3000
+    stepper = RolloutStep(geometry, seed=5, iteration=2, work_list=True)
+    listed = stepper.roots(B, device=DEV)
+    dense = stepper.roots(B, device=DEV)
+    dense.worklist = None
+    gen = torch.Generator().manual_seed(players)
+    for _ in range(400):
+        if bool(listed.state.terminal.all()):
+            break
+        raw = {k: v.to(DEV) for k, v in _random_raw(gen, (B, 1), 2).items()}
+        stepper.step(listed, raw)
+        stepper.step(dense, raw)
+        for name in ("action", "selected_log", "decision", "new_leaf", "root_path", "history_length"):
+            assert torch.equal(getattr(listed, name), getattr(dense, name)), name
+        for name in STATE_MAP:
+            assert torch.equal(getattr(listed.state, name), getattr(dense.state, name)), name
+        ended = listed.state.terminal.bool()  # leaf columns are written for the hands that ended
+        for k, v in listed.leaf.items():
+            assert torch.equal(v[ended], dense.leaf[k][ended]), k
+        for k, v in vars(listed.history).items():
+            if isinstance(v, torch.Tensor):
+                assert torch.equal(v, getattr(dense.history, k)), k
+    assert bool(dense.state.terminal.all())
+
+
 def _random_raw(gen, rows_shape, M):
     t = lambda *s: torch.randn(*s, generator=gen)
     return {
