@@ -510,17 +510,27 @@ struct StepArgs {
     pbg_leaf leaf;
 };
 
+// The address terms of a hand's CHANCE keys other than the draw: rng_key(ns, root, path, draw,
+// lane, epoch) = mix63((base + draw * C_draw) mod 2^63) with this base.
+__device__ __forceinline__ uint64_t chance_base(uint64_t ns, int64_t root, int64_t path, int64_t lane_id,
+                                                int64_t epoch) {
+    return (uint64_t)root * 0x1C69B3F74AC4AE35ULL + (uint64_t)path * 0x3C79AC492BA7B653ULL +
+           (uint64_t)lane_id * 0x4A7484AA6EA6E483ULL + (uint64_t)epoch * 0x2E1B21385C26C926ULL + ns;
+}
+constexpr uint64_t CHANCE_DRAW_MUL = 0x1F83D9ABFB41BD6BULL;
+
 // Three smallest (key, card) CHANCE keys among one hand's unused cards,
 // computed by a whole warp: lane l keys cards l and l+32, then three
 // shuffle-argmin rounds over (key, card) pairs (stable by card index).
-__device__ __forceinline__ void warp_smallest3(uint64_t ns, int64_t root, int64_t path, int64_t draw_base,
-                                               int64_t lane_id, int64_t epoch, uint64_t used, int D,
+__device__ __forceinline__ void warp_smallest3(uint64_t base, int64_t draw_base, uint64_t used, int D,
                                                int (&out)[3]) {
     const int lane = threadIdx.x & 31;
     int64_t k0 = INT64_MAX, k1 = INT64_MAX;
     int c0 = lane, c1 = lane + 32;
-    if (c0 < D && !((used >> c0) & 1ULL)) k0 = rng_key(ns, root, path, draw_base + c0, lane_id, epoch);
-    if (c1 < D && !((used >> c1) & 1ULL)) k1 = rng_key(ns, root, path, draw_base + c1, lane_id, epoch);
+    if (c0 < D && !((used >> c0) & 1ULL))
+        k0 = mix63((int64_t)((base + (uint64_t)(draw_base + c0) * CHANCE_DRAW_MUL) & M63));
+    if (c1 < D && !((used >> c1) & 1ULL))
+        k1 = mix63((int64_t)((base + (uint64_t)(draw_base + c1) * CHANCE_DRAW_MUL) & M63));
     if (c0 >= D) c0 = 64;
     if (c1 >= D) c1 = 64;
     #pragma unroll
@@ -540,10 +550,39 @@ __device__ __forceinline__ void warp_smallest3(uint64_t ns, int64_t root, int64_
     }
 }
 
+// The same three cards computed by one thread for its own hand: used when many
+// hands of a warp deal at once, where the warp-wide version would run once per hand.
+__device__ __forceinline__ void thread_smallest3(uint64_t base, int64_t draw_base, uint64_t used, int D,
+                                                 int (&out)[3]) {
+    int64_t bk[3] = {INT64_MAX, INT64_MAX, INT64_MAX};
+    int bi[3] = {64, 64, 64};
+    uint64_t acc = base + (uint64_t)draw_base * CHANCE_DRAW_MUL;
+    for (int c = 0; c < D; ++c, acc += CHANCE_DRAW_MUL) {
+        if ((used >> c) & 1ULL) continue;
+        const int64_t k = mix63((int64_t)(acc & M63));
+        if (k < bk[2]) {  // cards arrive in increasing order: equal keys keep the earlier card
+            if (k < bk[1]) {
+                bk[2] = bk[1]; bi[2] = bi[1];
+                if (k < bk[0]) {
+                    bk[1] = bk[0]; bi[1] = bi[0];
+                    bk[0] = k; bi[0] = c;
+                } else {
+                    bk[1] = k; bi[1] = c;
+                }
+            } else {
+                bk[2] = k; bi[2] = c;
+            }
+        }
+    }
+    out[0] = bi[0]; out[1] = bi[1]; out[2] = bi[2];
+}
+
 // Fused sampled rollout step: one thread per hand.  Consecutive threads own
 // consecutive hands, so every state column is read and written coalesced.
-// The loop is warp-uniform: hands that must deal a street are dealt by the
-// whole warp (warp_smallest3), one hand at a time.
+// The loop is warp-uniform: when a few hands of a warp must deal a street they
+// are dealt by the whole warp (warp_smallest3), one hand at a time; from
+// DEAL_PER_THREAD pending hands on, each deals its own (thread_smallest3).
+constexpr int DEAL_PER_THREAD = 6;
 //
 // Work list mode (A.list): a compaction pass has already written the outputs of
 // the terminal hands and listed the live ones, so every lane of a warp owns a
@@ -617,14 +656,18 @@ __global__ void __launch_bounds__(128) rollout_step_kernel(StepArgs A) {
                 used = h.used_cards(d.D, d.first);
             }
             int dealt[3] = {0, 1, 2};
-            while (pending) {
-                const int src = __ffs(pending) - 1;
-                pending &= pending - 1;
-                int out3[3];
-                warp_smallest3(A.ns_chance, __shfl_sync(0xffffffffu, root, src), __shfl_sync(0xffffffffu, path, src),
-                               (int64_t)gen * d.D, __shfl_sync(0xffffffffu, rl, src), __shfl_sync(0xffffffffu, re, src),
-                               __shfl_sync(0xffffffffu, used, src), d.D, out3);
-                if (lane == src) { dealt[0] = out3[0]; dealt[1] = out3[1]; dealt[2] = out3[2]; }
+            const uint64_t base = chance_base(A.ns_chance, root, path, rl, re);
+            if (__popc(pending) >= DEAL_PER_THREAD) {
+                if (needs) thread_smallest3(base, (int64_t)gen * d.D, used, d.D, dealt);
+            } else {
+                while (pending) {
+                    const int src = __ffs(pending) - 1;
+                    pending &= pending - 1;
+                    int out3[3];
+                    warp_smallest3(__shfl_sync(0xffffffffu, base, src), (int64_t)gen * d.D,
+                                   __shfl_sync(0xffffffffu, used, src), d.D, out3);
+                    if (lane == src) { dealt[0] = out3[0]; dealt[1] = out3[1]; dealt[2] = out3[2]; }
+                }
             }
             if (live) h.apply_deal(needs, dealt, d.first);
         }

@@ -73,7 +73,7 @@ def parse():
                         "on a second stream, bucket k starting when chunk k's loss is done")
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
                                                  "readout", "reach", "showdown", "optimizer", "poker_loss",
-                                                 "rollout_with_model", "completion"),
+                                                 "rollout_with_model", "completion", "rollout"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
@@ -460,6 +460,112 @@ def poker_loss_component(device, reps=10):
     return out
 
 
+def learner_step_component(device, rows=16_384, reps=20):
+    """The learner step the metric counts, at cfg1: HU 8bb R4 (E = 18, K = 16 class rows, M = 2), the fp32
+    preflop-class MLP (two hidden layers of 256, pbg_b200.mlp), `rows` sampled learner presentations:
+    forward, fused poker objective, backward and AdamW, replayed from a CUDA graph.  Beside it, when the
+    driver installed the reference, the same network in torch through the reference's own loss program
+    (LearnerOperation.forward_loss with its PokerPolicyOperator.learner), autograd and torch AdamW."""
+
+    import torch
+    from pbg_b200.mlp import MLPLearnerStep, PreflopMLP
+    from pbg_b200.poker import NLHEGeometry
+
+    geometry = NLHEGeometry(2, 8.0, 4)
+    model = PreflopMLP(geometry, device=device, seed=0)
+    step = MLPLearnerStep(model)
+    batch = _mlp_batch(device, geometry, rows)
+    for _ in range(3):
+        step(batch)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(batch)
+    ms = _device_ms(device, graph.replay, reps)
+    flops = 3 * 2 * rows * (model.inp * model.hidden + model.hidden ** 2 + model.hidden * model.out)
+    out = {"workload": f"cfg1 learner step: HU 8bb R4, fp32 MLP {model.inp}-256-256-{model.out} "
+                       f"({model.numel} parameters), {rows} sampled presentations, forward + fused objective + "
+                       "backward + AdamW (one CUDA graph)",
+           "ms": ms, "presentations_per_s": rows / (ms / 1e3), "gemm_tflops": flops / (ms / 1e3) / 1e12,
+           "parameters": model.numel, "kernels": "cuBLAS sgemm x 8, mlp bias/heads/bias-gradient kernels, "
+                                                 "learner_objective_kernel, adam"}
+    if _reference_pbg() is not None:
+        try:
+            ref_ms = _reference_mlp_step_ms(device, model, geometry, batch, reps=max(3, reps // 4))
+            out["reference_torch_cuda_ms"] = ref_ms
+            out["reference_presentations_per_s"] = rows / (ref_ms / 1e3)
+            out["speedup_vs_reference_torch_cuda"] = ref_ms / ms
+        except Exception as exc:  # noqa: BLE001 - reported, not fatal
+            out["reference_torch_cuda_ms"] = f"failed: {str(exc)[:200]}"
+    return out
+
+
+def _mlp_batch(device, geometry, S, seed=5):
+    import torch
+
+    d = _poker_loss_inputs(device, S, 1, geometry.events, seed=seed)
+    g = torch.Generator(device=device).manual_seed(seed + 1)
+    return {"model_input": torch.randn(S, geometry.preflop_model_input_width, device=device, generator=g),
+            "sampled_class": torch.randint(0, geometry.private_classes, (S,), device=device, generator=g),
+            "mask": d["mask"], "action": d["action"], "old_log_policy": d["old"], "advantage_target": d["adv"],
+            "old_value": d["old_value"], "value_target": d["target"], "controls": d["controls"],
+            "lane_weight": torch.ones(1, device=device)}
+
+
+def _reference_mlp_step_ms(device, model, geometry, batch, reps):
+    """The same learner step on the reference's PyTorch CUDA path: torch modules for the network (the
+    reference heads' activations), pbg's LearnerOperation.forward_loss with pbg's
+    PokerPolicyOperator.learner, (total * weight).sum().backward() (training.py:403), torch AdamW."""
+
+    import torch
+    from types import MappingProxyType
+
+    from pbg.core.contracts import mode_schema
+    from pbg.core.learner import LearnerOperation, LossConfig, ModelEvaluation, SequentialLearnerBatch
+    from pbg.games.poker.queued.policy import PokerLegality, PokerPolicyOperator
+
+    S = batch["model_input"].shape[0]
+    E = geometry.events
+    K, R, M = model.K, model.row, model.M
+    params = {k: v.detach().clone().requires_grad_() for k, v in model.params.items()}
+    opt = torch.optim.AdamW(list(params.values()), lr=3e-4, weight_decay=0.0)
+    op = PokerPolicyOperator()
+    legality = PokerLegality(torch.arange(E, dtype=torch.int32, device=device)[None].expand(S, -1).contiguous(),
+                             batch["mask"])
+
+    def policy(input_type, model_input, raw_rows, act, private, owner, reference):
+        return op.learner(raw_rows, legality, act, private, owner, reference)
+
+    fields = {"model_input": batch["model_input"], "owner": torch.zeros(S, dtype=torch.int32, device=device),
+              "action": batch["action"], "old_log_policy": batch["old_log_policy"],
+              "advantage_target": batch["advantage_target"], "old_value": batch["old_value"],
+              "value_target": batch["value_target"],
+              "sampled_private_state": torch.zeros(S, 2, dtype=torch.int32, device=device)}
+    ref_batch = SequentialLearnerBatch("pre", torch.arange(S, device=device), MappingProxyType(fields))
+    learner = LearnerOperation(mode_schema("self_play", "sequential", "sampled"), LossConfig(), None, policy)
+    rows = torch.arange(S, device=device)
+    cls = batch["sampled_class"].long()
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        x = batch["model_input"]
+        h1 = torch.relu(torch.nn.functional.linear(x, params["w1"], params["b1"]))
+        h2 = torch.relu(torch.nn.functional.linear(h1, params["w2"], params["b2"]))
+        z = torch.nn.functional.linear(h2, params["w3"], params["b3"])
+        r = z[:, :K * R].reshape(S, K, R)[rows, cls]
+        raw = {"type_logits": r[:, None, :3], "omega": torch.softmax(r[:, 3:3 + M], -1)[:, None],
+               "mu": torch.sigmoid(r[:, 3 + M:3 + 2 * M])[:, None],
+               "s": (torch.nn.functional.softplus(r[:, 3 + 2 * M:3 + 3 * M]) + model.s_min)[:, None],
+               "iota": torch.sigmoid(r[:, 3 + 3 * M])[:, None]}
+        value = z[rows, K * R + cls][:, None]
+        res = learner.forward_loss(ref_batch, iteration=0, lane_count=1, loss_controls=batch["controls"],
+                                   evaluation=ModelEvaluation(raw, value))
+        (res.total * batch["lane_weight"]).sum().backward()
+        opt.step()
+
+    return _events_ms(device, step, reps)
+
+
 def reference_torch_loss_component(device, inputs, reps=5):
     """The reference's own PyTorch CUDA loss program on the cfg5 rows: pbg.core.learner.LearnerOperation
     .forward_loss (sampled, sequential, unmodified, from baseline/_ref) over the same 4,194,304 x 8 bf16
@@ -663,12 +769,18 @@ def rollout_component(device, hands=65_536, seed=0):
            "iota": torch.rand((hands, 1), generator=g, device=device) * 0.2}
     counts = []
     arena = stepper.roots(hands, device=device)
+    if PROFILE_ONE_FORWARD:  # one eager rollout to terminal, every step a profiled launch
+        torch.cuda.profiler.start()
     for _ in range(400):
         active = int((~arena.state.terminal).sum())
         if active == 0:
             break
         counts.append(active)
         stepper.step(arena, raw)
+    if PROFILE_ONE_FORWARD:
+        torch.cuda.synchronize(device)
+        torch.cuda.profiler.stop()
+        return {}
     arena = stepper.roots(hands, device=device)
     stream = torch.cuda.current_stream(device)
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in counts]
@@ -1447,7 +1559,8 @@ def main():
         name = {"folded": "folded_component", "posterior": "posterior_component",
                 "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
                 "optimizer": "optimizer_component", "poker_loss": "poker_loss_component",
-                "rollout_with_model": "rollout_with_model_component", "completion": "completion_component"}.get(
+                "rollout_with_model": "rollout_with_model_component", "completion": "completion_component",
+                "rollout": "rollout_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         if name == "rollout_with_model_component":
             rollout_with_model_component(device, hands=args.profile_hands)
@@ -1705,6 +1818,7 @@ def main():
                                   "optimizer_step": optimizer_component(device),
                                   "showdown": showdown_component(device),
                                   "rb_completion": completion_component(device),
+                                  "learner_step_cfg1": learner_step_component(device),
                                   "reach_update": reach_component(device),
                                   "folded_statistics": folded_component(device),
                                   "branched_sampling": branching_component(device),
