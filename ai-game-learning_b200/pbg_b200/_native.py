@@ -96,6 +96,12 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_hand_values": (_I32, [_I32, _I64, _P, _P, _P]),
     "pbg_rb_complete": (_I32, [_I32, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_rb_complete_max_samples": (_I32, [_I32, _I32]),
+    "pbg_mlp_bias_relu": (_I32, [_I64, _I32, _P, _P, _P]),
+    "pbg_mlp_heads": (_I32, [_I64, _I32, _I32, ctypes.c_float, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_mlp_heads_backward": (_I32, [_I64, _I32, _I32, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                      _I64, _P]),
+    "pbg_mlp_bias_partials": (_I64, [_I64, _I32]),
+    "pbg_mlp_relu_backward_bias": (_I32, [_I64, _I32, _P, _P, _P, _P, _I64, _P]),
     "pbg_policy_probabilities": (_I32, [_I64, _I32, Pol, _P, _P, _P]),
     "pbg_policy_selected_log_pi": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P]),
     "pbg_policy_entropy": (_I32, [_I64, _I32, Pol, _P, _P, _P]),

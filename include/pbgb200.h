@@ -653,6 +653,39 @@ int pbg_nvls_allreduce_sum_f32_grid(int64_t n, void *multicast, const void *sign
                                     int64_t pad_bytes, int32_t rank, int32_t world,
                                     uint32_t *error, int32_t max_ctas, void *stream);
 
+/* ------------------------------------------------ cfg1 preflop-class MLP */
+
+/* The element-wise parts of the fp32 preflop-class MLP (two hidden layers,
+ * ReLU) that the reference's ModelOperation protocol admits
+ * (learner.py:324-350); its heads apply the reference head activations
+ * (model/heads.py:28-62).  Output row layout of the last dense map: per class
+ * row [type 3 | omega logits M | mu logits M | s pre M | iota logit], then
+ * the K values.  y [M,N] row-major. */
+int pbg_mlp_bias_relu(int64_t M, int32_t N, float *y, const float *bias, void *stream);
+
+/* Heads of the sampled class row cls[s] (z [S, ldz] before its bias):
+ * type_logits [S,3], omega/mu/scale [S,M], iota [S], value [S].  *status
+ * (device, caller-zeroed) gets bit 1 for a class id outside [0,K). */
+int pbg_mlp_heads(int64_t S, int32_t K, int32_t M, float s_min, const float *z, int64_t ldz,
+                  const float *bias, const int32_t *cls, float *type_logits, float *omega, float *mu,
+                  float *scale, float *iota, float *value, uint32_t *status, void *stream);
+
+/* Vector-Jacobian product of pbg_mlp_heads into dz [S, lddz] (zero outside
+ * the sampled row's columns). */
+int pbg_mlp_heads_backward(int64_t S, int32_t K, int32_t M, const float *z, int64_t ldz,
+                           const float *bias, const int32_t *cls, const float *omega, const float *mu,
+                           const float *iota, const float *d_type, const float *d_omega,
+                           const float *d_mu, const float *d_scale, const float *d_iota,
+                           const float *d_value, float *dz, int64_t lddz, void *stream);
+
+/* Floats of scratch pbg_mlp_relu_backward_bias needs for M rows of N columns. */
+int64_t pbg_mlp_bias_partials(int64_t M, int32_t N);
+
+/* dy *= (y > 0) (y may be NULL: no mask) and dbias[n] = sum_m dy[m,n], summed
+ * in blocks of 64 rows and the blocks in order (deterministic). */
+int pbg_mlp_relu_backward_bias(int64_t M, int32_t N, float *dy, const float *y, float *dbias,
+                               float *partial, int64_t partial_len, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
