@@ -30,8 +30,10 @@
 // cancellation between the two product-rule terms that autograd forms.
 //
 // Statistics are accumulated per (warp, lane of the batch) in double in
-// shared memory, reduced per block in warp order and across blocks in block
-// order by the last block to arrive (deterministic for a given grid).
+// shared memory, reduced per block in warp order and across blocks by the last
+// block to arrive: each statistic strided over several of its threads (block
+// b to thread b mod groups, in block order), then those threads in order
+// (deterministic for a given grid).
 #include <type_traits>
 
 #include "pbg_common.cuh"
@@ -47,6 +49,7 @@ enum { ST_POLICY, ST_VALUE, ST_ENTROPY, ST_REFERENCE, ST_APPROX, ST_CLIP, ST_CAP
 constexpr int PL_STATS = PL_SUMS + 2;  // + negative log-ratio max, negative influence max
 constexpr int PL_RESULT = 10;          // LossResult fields (learner.py:1739-1749)
 constexpr int PL_MAX_BLOCKS = 2048;    // grid cap: sizes the statistics workspace independently of the device
+static_assert(PL_MAX_LANES * PL_STATS <= PL_THREADS, "the last block reduces every statistic at once");
 
 struct LearnerArgs {
     int64_t S, A, rows;  // sigma rows, action rows, policy rows S*W
@@ -589,12 +592,26 @@ __global__ void __launch_bounds__(PL_THREADS, 2) learner_objective_kernel(Learne
     __syncthreads();
     if (!last_block) return;
     __threadfence();
+    // the last block: each of the n statistics is reduced by `groups` threads, thread (i, grp) over
+    // the blocks grp, grp + groups, ... in order, then the groups in order
+    __shared__ double red[PL_THREADS];
+    const int groups = PL_THREADS / n;  // n <= PL_MAX_LANES * PL_STATS < PL_THREADS
+    if ((int)threadIdx.x < groups * n) {
+        const int i = threadIdx.x % n, grp = threadIdx.x / n, k = i % PL_STATS;
+        double acc = k >= PL_SUMS ? -INFINITY : 0.0;
+        for (unsigned b = grp; b < gridDim.x; b += groups) {
+            const double v = __ldcg(g.partials + 1 + (int64_t)b * n + i);
+            acc = k >= PL_SUMS ? fmax(acc, v) : acc + v;
+        }
+        red[threadIdx.x] = acc;
+    }
+    __syncthreads();
     for (int l = threadIdx.x; l < g.lanes; l += PL_THREADS) {
         double acc[PL_STATS];
         for (int k = 0; k < PL_STATS; ++k) acc[k] = k >= PL_SUMS ? -INFINITY : 0.0;
-        for (unsigned b = 0; b < gridDim.x; ++b)
+        for (int grp = 0; grp < groups; ++grp)
             for (int k = 0; k < PL_STATS; ++k) {
-                const double v = __ldcg(g.partials + 1 + (int64_t)b * n + l * PL_STATS + k);
+                const double v = red[grp * n + l * PL_STATS + k];
                 acc[k] = k >= PL_SUMS ? fmax(acc[k], v) : acc[k] + v;
             }
         const float* ctl = g.controls + l * 10;

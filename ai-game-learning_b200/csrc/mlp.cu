@@ -10,7 +10,8 @@
 //                      s_min, iota = sigmoid; value the row's value column
 //   heads_backward     their vector-Jacobian product into the output row
 //   relu_backward_bias dy *= (y > 0) and the bias gradient as column sums in a
-//                      fixed order (row blocks, then the blocks in order)
+//                      fixed order (blocks of 32 rows in row order, the blocks'
+//                      sums strided over a warp's lanes, then a butterfly)
 //
 // The output row of the last dense map holds, for each of the K class rows,
 // [type 3 | omega logits M | mu logits M | s pre-activations M | iota logit]
@@ -24,7 +25,7 @@ namespace {
 
 constexpr int MLP_THREADS = 256;
 constexpr int MLP_MAXM = 8;
-constexpr int MLP_ROW_BLOCK = 64;  // rows per partial column sum
+constexpr int MLP_ROW_BLOCK = 32;  // rows per partial column sum (loaded all at once)
 
 __global__ void bias_relu_kernel(int64_t M, int N, float* __restrict__ y, const float* __restrict__ bias) {
     const int64_t n = M * N;
@@ -108,32 +109,44 @@ __global__ void heads_backward_kernel(int64_t S, int K, int M, const float* __re
     }
 }
 
-// Per block: the column sums of rows [r0, r0 + MLP_ROW_BLOCK) after the ReLU mask.
+// Per block: the column sums of rows [r0, r0 + MLP_ROW_BLOCK) after the ReLU mask; each thread
+// loads its column's 32 rows at once and adds them in row order.
 __global__ void relu_backward_partial_kernel(int64_t M, int N, float* __restrict__ dy, const float* __restrict__ y,
                                              float* __restrict__ partial) {
     const int64_t blocks = (M + MLP_ROW_BLOCK - 1) / MLP_ROW_BLOCK;
     for (int64_t blk = blockIdx.x; blk < blocks; blk += gridDim.x) {
-        const int64_t r0 = blk * MLP_ROW_BLOCK, r1 = min(r0 + MLP_ROW_BLOCK, M);
+        const int64_t r0 = blk * MLP_ROW_BLOCK;
+        const int rows = (int)min((int64_t)MLP_ROW_BLOCK, M - r0);
         for (int n = threadIdx.x; n < N; n += blockDim.x) {
+            float g[MLP_ROW_BLOCK];
+            bool keep[MLP_ROW_BLOCK];
+            #pragma unroll
+            for (int r = 0; r < MLP_ROW_BLOCK; ++r) {
+                g[r] = r < rows ? dy[(r0 + r) * N + n] : 0.0f;
+                keep[r] = r < rows && (!y || y[(r0 + r) * N + n] > 0.0f);
+            }
             float acc = 0.0f;
-            for (int64_t r = r0; r < r1; ++r) {
-                float g = dy[r * N + n];
-                if (y && !(y[r * N + n] > 0.0f)) {
-                    g = 0.0f;
-                    dy[r * N + n] = 0.0f;
-                }
-                acc += g;
+            #pragma unroll
+            for (int r = 0; r < MLP_ROW_BLOCK; ++r) {
+                if (r < rows && !keep[r]) dy[(r0 + r) * N + n] = 0.0f;
+                acc += keep[r] ? g[r] : 0.0f;
             }
             partial[blk * N + n] = acc;
         }
     }
 }
 
+// One warp per column: lane l adds the partials of blocks l, l + 32, ... in order, then a fixed
+// butterfly adds the lanes.
 __global__ void column_total_kernel(int64_t blocks, int N, const float* __restrict__ partial, float* __restrict__ out) {
-    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t n = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
         float acc = 0.0f;
-        for (int64_t b = 0; b < blocks; ++b) acc += partial[b * N + n];
-        out[n] = acc;
+        for (int64_t b = lane; b < blocks; b += 32) acc += partial[b * N + n];
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) out[n] = acc;
     }
 }
 
@@ -198,12 +211,11 @@ int pbg_mlp_relu_backward_bias(int64_t M, int32_t N, float* dy, const float* y, 
         return cuda_status(cudaMemsetAsync(dbias, 0, (size_t)N * sizeof(float), as_stream(stream)),
                            "mlp_relu_backward_bias: clear");
     }
-    const int grid = (int)(blocks < 8 * (int64_t)sm_count() ? blocks : 8 * (int64_t)sm_count());
+    const int grid = (int)(blocks < 16 * (int64_t)sm_count() ? blocks : 16 * (int64_t)sm_count());
     relu_backward_partial_kernel<<<grid, MLP_THREADS, 0, as_stream(stream)>>>(M, N, dy, y, partial);
     int err = launch_status("mlp_relu_backward_bias: partials");
     if (err) return err;
-    column_total_kernel<<<(N + MLP_THREADS - 1) / MLP_THREADS, MLP_THREADS, 0, as_stream(stream)>>>(blocks, N, partial,
-                                                                                                   dbias);
+    column_total_kernel<<<(N + 7) / 8, MLP_THREADS, 0, as_stream(stream)>>>(blocks, N, partial, dbias);
     return launch_status("mlp_relu_backward_bias: totals");
 }
 

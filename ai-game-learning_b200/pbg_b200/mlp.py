@@ -34,6 +34,26 @@ from .optim import FlatAdam
 from .poker import NLHEGeometry
 
 
+WGRAD_CHUNK = 512  # rows per partial weight gradient
+
+
+def _weight_gradient(dy: Tensor, x: Tensor, out: Tensor) -> None:
+    """out = dy^T x over S rows.  The output is small and the reduction long, so the rows are cut into
+    chunks of WGRAD_CHUNK whose partial products run as one batched GEMM (enough tiles for every SM),
+    then summed over the chunks (a fixed-order reduction); the remainder rows are added last."""
+
+    S = dy.shape[0]
+    chunks = S // WGRAD_CHUNK
+    if chunks < 2:
+        torch.mm(dy.t(), x, out=out)
+        return
+    rows = chunks * WGRAD_CHUNK
+    parts = torch.bmm(dy[:rows].view(chunks, WGRAD_CHUNK, -1).transpose(1, 2), x[:rows].view(chunks, WGRAD_CHUNK, -1))
+    torch.sum(parts, 0, out=out)
+    if rows < S:
+        out.addmm_(dy[rows:].t(), x[rows:])
+
+
 class PreflopMLP:
     """x [S, W_pre] -> ReLU(x W1^T + b1) -> ReLU(. W2^T + b2) -> . W3^T + b3 -> heads of the sampled row."""
 
@@ -118,15 +138,15 @@ class PreflopMLP:
         partial = torch.empty(int(N.lib().pbg_mlp_bias_partials(S, max(self.out, self.hidden))), device=dev)
         call("pbg_mlp_relu_backward_bias", S, self.out, ptr(dz), None, ptr(g["b3"]), ptr(partial), partial.numel(),
              stream(dev))
-        torch.mm(dz.t(), h2, out=g["w3"])
+        _weight_gradient(dz, h2, g["w3"])
         dh2 = torch.mm(dz, p["w3"])
         call("pbg_mlp_relu_backward_bias", S, self.hidden, ptr(dh2), ptr(h2), ptr(g["b2"]), ptr(partial),
              partial.numel(), stream(dev))
-        torch.mm(dh2.t(), h1, out=g["w2"])
+        _weight_gradient(dh2, h1, g["w2"])
         dh1 = torch.mm(dh2, p["w2"])
         call("pbg_mlp_relu_backward_bias", S, self.hidden, ptr(dh1), ptr(h1), ptr(g["b1"]), ptr(partial),
              partial.numel(), stream(dev))
-        torch.mm(dh1.t(), x, out=g["w1"])
+        _weight_gradient(dh1, x, g["w1"])
 
 
 class MLPLearnerStep:

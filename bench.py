@@ -73,7 +73,7 @@ def parse():
                         "on a second stream, bucket k starting when chunk k's loss is done")
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
                                                  "readout", "reach", "showdown", "optimizer", "poker_loss",
-                                                 "rollout_with_model", "completion", "rollout"),
+                                                 "rollout_with_model", "completion", "rollout", "learner_step"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
@@ -475,6 +475,9 @@ def learner_step_component(device, rows=16_384, reps=20):
     model = PreflopMLP(geometry, device=device, seed=0)
     step = MLPLearnerStep(model)
     batch = _mlp_batch(device, geometry, rows)
+    if PROFILE_ONE_FORWARD:  # one eager learner step between cudaProfilerStart/Stop
+        _device_ms(device, lambda: step(batch))
+        return {}
     for _ in range(3):
         step(batch)
     torch.cuda.synchronize(device)
@@ -1560,7 +1563,7 @@ def main():
                 "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
                 "optimizer": "optimizer_component", "poker_loss": "poker_loss_component",
                 "rollout_with_model": "rollout_with_model_component", "completion": "completion_component",
-                "rollout": "rollout_component"}.get(
+                "rollout": "rollout_component", "learner_step": "learner_step_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         if name == "rollout_with_model_component":
             rollout_with_model_component(device, hands=args.profile_hands)

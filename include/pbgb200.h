@@ -682,7 +682,8 @@ int pbg_mlp_heads_backward(int64_t S, int32_t K, int32_t M, const float *z, int6
 int64_t pbg_mlp_bias_partials(int64_t M, int32_t N);
 
 /* dy *= (y > 0) (y may be NULL: no mask) and dbias[n] = sum_m dy[m,n], summed
- * in blocks of 64 rows and the blocks in order (deterministic). */
+ * in blocks of 32 rows, the blocks' sums strided over 32 lanes and added by a
+ * fixed butterfly (deterministic). */
 int pbg_mlp_relu_backward_bias(int64_t M, int32_t N, float *dy, const float *y, float *dbias,
                                float *partial, int64_t partial_len, void *stream);
 
