@@ -64,6 +64,9 @@ def parse():
                    help=argparse.SUPPRESS)
     p.add_argument("--engine-roots", type=int, default=4096)
     p.add_argument("--engine-iterations", type=int, default=6)
+    p.add_argument("--learner-scaling", action="store_true",
+                   help="time the cfg1 learner step data-parallel instead: every rank a step over its own 16,384 "
+                        "presentations, the SUM of the real flat gradient (NCCL), then AdamW; one JSON line")
     p.add_argument("--allreduce", choices=("auto", "nvls", "nccl"), default="auto",
                    help="gradient SUM at N > 1: auto = libpbgb200's NVLS kernel from 4 ranks, NCCL below")
     p.add_argument("--comm-sms", type=int, default=16,
@@ -501,6 +504,61 @@ def learner_step_component(device, rows=16_384, reps=20):
         except Exception as exc:  # noqa: BLE001 - reported, not fatal
             out["reference_torch_cuda_ms"] = f"failed: {str(exc)[:200]}"
     return out
+
+
+def learner_scaling(args, device, world, rank, rows=16_384):
+    """cfg1 learner step, data parallel: each rank runs forward, objective and backward over its own
+    `rows` presentations (CUDA graph), the flat gradient (172,720 fp32) is SUM-all-reduced with NCCL,
+    then AdamW (CUDA graph).  Weak scaling; the step is timed with CUDA events, max over ranks."""
+
+    import torch
+    import torch.distributed as dist
+    from pbg_b200.mlp import MLPLearnerStep, PreflopMLP
+    from pbg_b200.poker import NLHEGeometry
+
+    geometry = NLHEGeometry(2, 8.0, 4)
+    model = PreflopMLP(geometry, device=device, seed=0)  # the same initial weights on every rank
+    step = MLPLearnerStep(model)
+    batch = _mlp_batch(device, geometry, rows, seed=5 + rank)
+    for _ in range(3):
+        step(batch)
+    torch.cuda.synchronize(device)
+    g_grad, g_adam = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_grad):
+        step.gradient(batch)
+    with torch.cuda.graph(g_adam):
+        step.adam.step()
+
+    def one():
+        g_grad.replay()
+        if world > 1:
+            dist.all_reduce(step.adam.grad)
+        g_adam.replay()
+
+    for _ in range(max(3, args.warmup)):
+        one()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        one()
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b) / args.steps
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    del g_grad, g_adam
+    if rank == 0:
+        ms = float(t)
+        print(json.dumps({"metric": "learner presentations/s (cfg1 learner step, data parallel)",
+                          "value": world * rows / (ms / 1e3), "unit": "presentations/s", "n_gpus": world,
+                          "steps": args.steps, "ms_per_step": ms, "scaling": "weak",
+                          "config": {"workload": f"HU 8bb R4, fp32 MLP ({model.numel} parameters), {rows} "
+                                                 "presentations per rank per step, NCCL SUM of the flat gradient"}}))
 
 
 def _mlp_batch(device, geometry, S, seed=5):
@@ -1573,6 +1631,11 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if args.learner_scaling:
+        learner_scaling(args, device, world, rank)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     N, A = args.rows, args.actions
     inputs = make_inputs(N, A, seed=rank, device=device)
     logits, mask, action, old, adv, weight = inputs
