@@ -583,12 +583,13 @@ __device__ __forceinline__ void thread_smallest3(uint64_t base, int64_t draw_bas
 // are dealt by the whole warp (warp_smallest3), one hand at a time; from
 // DEAL_PER_THREAD pending hands on, each deals its own (thread_smallest3).
 constexpr int DEAL_PER_THREAD = 6;
+constexpr int ROLLOUT_BLOCK = 128;  // 64 measured the same
 //
 // Work list mode (A.list): a compaction pass has already written the outputs of
 // the terminal hands and listed the live ones, so every lane of a warp owns a
 // live hand and late steps, where few hands are left, run dense warps.
 template <int P>
-__global__ void __launch_bounds__(128) rollout_step_kernel(StepArgs A) {
+__global__ void __launch_bounds__(ROLLOUT_BLOCK) rollout_step_kernel(StepArgs A) {
     const Geo& d = A.d;
     const int lane = threadIdx.x & 31;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -1111,7 +1112,7 @@ static int rollout_step_impl(pbg_geometry g, int64_t B, pbg_state st, pbg_histor
     A.ns_chance = rng_namespace(seed, iteration, CHANCE);
     A.pol = pol; A.action = action; A.selected = selected_log; A.decision = decision; A.new_leaf = new_leaf;
     A.leaf = leaf;
-    const int block = 128;
+    const int block = ROLLOUT_BLOCK;
     PBG_DISPATCH_P(g.players, rollout_step_kernel<PP><<<stride_grid(B, block, 16), block, 0, as_stream(stream)>>>(A));
     return launch_status("rollout_step");
 }
