@@ -105,10 +105,9 @@ class FamilyRollout:
 
         g = self.geometry
         state = arena.state
-        live_seats = state.status.ne(FOLDED).sum(1)
-        code = torch.where(state.street.eq(0), torch.zeros_like(live_seats), live_seats)
-        code = torch.where(~state.terminal, code, torch.full_like(code, -1))
-        counts = torch.bincount(code + 1, minlength=g.players + 2).cpu().tolist()  # the step's one host read
+        # family of each hand (hooks.py:456-462, pbg_input_type: pre 0, post_A A - 1), -1 once terminal
+        code = torch.where(state.terminal, -1, self.machine.input_type(state))
+        counts = torch.bincount(code + 1, minlength=g.players + 1).cpu().tolist()  # the step's one host read
         decisions = sum(counts[1:])
         if decisions == 0:
             return 0
@@ -118,7 +117,7 @@ class FamilyRollout:
         for value, count in enumerate(counts[1:]):
             if count == 0:
                 continue
-            kind = "pre" if value == 0 else f"post_{value}"
+            kind = "pre" if value == 0 else f"post_{value + 1}"
             chunk = self.max_rows["pre" if value == 0 else "post"]
             family = order[start:start + count]
             start += count

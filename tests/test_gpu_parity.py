@@ -252,6 +252,35 @@ def test_showdown_matches_oracle(ranks, players):
 # ------------------------------------------------------ fused rollout
 
 
+@pytest.mark.parametrize("players,ranks,stack", [(2, 13, 100.0), (6, 13, 20.0), (4, 9, 20.5)])
+def test_input_type_matches_oracle_along_rollouts(players, ranks, stack):
+    """hooks.py:456-462 (input_type: pre 0, post with A contenders A - 1) on every state of seeded
+    rollouts, against the oracle's restatement."""
+
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.rollout import RolloutStep
+
+    geometry = NLHEGeometry(players, stack, ranks)
+    om = O.Machine(O.Geometry(players, stack, ranks))
+    B = 2000
+    stepper = RolloutStep(geometry, seed=9, iteration=1)
+    arena = stepper.roots(B, device=DEV)
+    gen = torch.Generator().manual_seed(players + ranks)
+    seen = set()
+    for _ in range(400):
+        got = host(stepper.machine.input_type(arena.state))
+        cols = {STATE_MAP[k]: host(getattr(arena.state, k)) for k in STATE_MAP}
+        state = O.State(**{k: v.astype(getattr(O.State.empty(1, players), k).dtype) for k, v in cols.items()})
+        np.testing.assert_array_equal(got, om.input_type(state))
+        seen.update(np.unique(got[~cols["terminal"].astype(bool)]).tolist())
+        if bool(arena.state.terminal.all()):
+            break
+        stepper.step(arena, {k: v.to(DEV) for k, v in _random_raw(gen, (B, 1), 2).items()})
+    assert 0 in seen and 1 in seen
+    if players > 2:
+        assert max(seen) >= 2  # multiway postflop families occur
+
+
 @pytest.mark.parametrize("players,ranks,stack", [(2, 13, 100.0), (6, 13, 50.0), (3, 4, 8.0)])
 def test_rollout_work_list_equals_dense_step(players, ranks, stack):
     """pbg_rollout_step_listed (live hands listed, dense warps) and pbg_rollout_step (one thread per
