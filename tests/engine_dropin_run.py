@@ -1,7 +1,7 @@
 """One training iteration of the reference's own engine, optionally routed to libpbgb200.
 
     python tests/engine_dropin_run.py <out_dir> <reference|b200|b200_learner> [roots] [iterations] [program]
-                                      [sampled|rao_blackwell]
+                                      [sampled|rao_blackwell] [players stack_bb ranks]
 
 Test infrastructure for tests/test_gpu_engine_dropin.py (run in a fresh process
 so that the two engines never share imported state).  It loads the reference
@@ -30,7 +30,7 @@ sys.path.append(os.path.join(ROOT, "baseline", "_ref"))
 CONFIG = """kind: nlhe_run_v1
 scientific:
   mode: {{training_regime: self_play, rollout_mode: sequential, private_estimator: {estimator}}}{completion}
-  game: {{players: 2, stack_bb: 8.0, rank_count: 4}}
+  game: {{players: {players}, stack_bb: {stack}, rank_count: {ranks}}}
   model:
     d_model: 32
     n_heads: 4
@@ -38,7 +38,7 @@ scientific:
     raises: {{components: 2, minimum_scale: 0.02}}
     class_embedding_dim: 8
     ffn_hidden: 64
-    folder_beta_rank: 0
+    folder_beta_rank: {beta_rank}
     folder_line_dim: 8
     epsilon: 1.0e-8
   objective:
@@ -73,6 +73,9 @@ def main() -> None:
     iterations = int(sys.argv[4]) if len(sys.argv) > 4 else 1
     program = sys.argv[5] if len(sys.argv) > 5 else "eager"
     estimator = sys.argv[6] if len(sys.argv) > 6 else "sampled"
+    players = int(sys.argv[7]) if len(sys.argv) > 7 else 2
+    stack = float(sys.argv[8]) if len(sys.argv) > 8 else 8.0
+    ranks = int(sys.argv[9]) if len(sys.argv) > 9 else 4
     completion = "\n  completion: {samples: 64}" if estimator == "rao_blackwell" else ""
     import torch
 
@@ -88,7 +91,8 @@ def main() -> None:
     path = os.path.join(out, f"{arm}.yaml")
     with open(path, "w") as f:
         f.write(CONFIG.format(roots=roots, iterations=iterations, program=program, estimator=estimator,
-                              completion=completion, out=os.path.join(out, f"run_{arm}")))
+                              completion=completion, players=players, stack=stack, ranks=ranks,
+                              beta_rank=0 if players == 2 else 4, out=os.path.join(out, f"run_{arm}")))
     # record the flat gradient rows each optimizer transition receives (pbg/core/optimization.py:394-399)
     from pbg.core import optimization
 

@@ -39,27 +39,31 @@ REF = os.path.join(ROOT, "baseline", "_ref", "pbg")
 REF_TARGETS_SOURCE = os.path.join(REF, "core", "csrc", "layered_targets.cu")
 
 
-def _run(out, arm, estimator):
+def _run(out, arm, estimator, geometry=(2, 8.0, 4), roots=16):
     env = dict(os.environ, TORCH_CUDA_ARCH_LIST=os.environ.get("TORCH_CUDA_ARCH_LIST", "10.0"))
-    proc = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "engine_dropin_run.py"), out, arm, "16", "1",
-                           "eager", estimator], capture_output=True, text=True, timeout=900, env=env)
+    proc = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "engine_dropin_run.py"), out, arm, str(roots),
+                           "1", "eager", estimator, *(str(g) for g in geometry)],
+                          capture_output=True, text=True, timeout=900, env=env)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-6000:]
     return torch.load(os.path.join(out, f"{arm}.pt"), weights_only=False)
 
 
 @pytest.mark.skipif(not os.path.isfile(REF_TARGETS_SOURCE),
                     reason="the reference package (with its CUDA sources) is not installed under baseline/_ref")
-@pytest.mark.parametrize("estimator", ["sampled", "rao_blackwell"])
-@pytest.mark.parametrize("arm", ["b200", "b200_learner"])
-def test_reference_engine_runs_on_b200_kernels(tmp_path, arm, estimator):
+@pytest.mark.parametrize("arm,estimator,geometry,roots", [
+    ("b200", "sampled", (2, 8.0, 4), 16), ("b200_learner", "sampled", (2, 8.0, 4), 16),
+    ("b200", "rao_blackwell", (2, 8.0, 4), 16), ("b200_learner", "rao_blackwell", (2, 8.0, 4), 16),
+    ("b200_learner", "rao_blackwell", (6, 100.0, 13), 8),  # cfg3's geometry: 6-max, 100 bb, 13 ranks
+])
+def test_reference_engine_runs_on_b200_kernels(tmp_path, arm, estimator, geometry, roots):
     """b200: state machine, policy and targets swapped; b200_learner: the loss program as well
     (``LearnerOperation.forward_loss`` -> one pbg_poker_learner_objective launch).  With the
     Rao-Blackwell estimator the leaves go through this build's ``rb_leaf`` and the reference's
     completion binding, whose evaluator (``complete``, this build's module in both runs) draws 64
     samples per leaf."""
 
-    ref = _run(str(tmp_path), "reference", estimator)
-    b200 = _run(str(tmp_path), arm, estimator)
+    ref = _run(str(tmp_path), "reference", estimator, geometry, roots)
+    b200 = _run(str(tmp_path), arm, estimator, geometry, roots)
     assert b200["installed"] and any("PokerStateMachine" in name for name in b200["installed"])
     assert ("forward_loss" in " ".join(b200["installed"])) == (arm == "b200_learner")
     assert (b200["fused_calls"] > 0) == (arm == "b200_learner")
@@ -68,7 +72,10 @@ def test_reference_engine_runs_on_b200_kernels(tmp_path, arm, estimator):
     for lane_b, lane_r in zip(b200["lanes"], ref["lanes"], strict=True):
         for loss_b, loss_r in zip(lane_b["losses"], lane_r["losses"], strict=True):
             for name, value in loss_r.items():
-                assert abs(loss_b[name] - value) <= 1e-4 * abs(value) + 1e-6, (name, loss_b[name], value)
+                # the log-ratio diagnostics sit at rounding level on a first minibatch (old and new log pi
+                # agree to a few ulp of |log pi| ~ 5): an absolute 1e-5 there
+                atol = 1e-5 if name in ("approximate_kl", "negative_advantage_log_ratio_max") else 1e-6
+                assert abs(loss_b[name] - value) <= 1e-4 * abs(value) + atol, (name, loss_b[name], value)
     lr = 3.0e-4
     assert len(b200["gradients"]) == len(ref["gradients"]) >= 1
     for g_b, g_r in zip(b200["gradients"], ref["gradients"], strict=True):
