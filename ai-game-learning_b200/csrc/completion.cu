@@ -33,8 +33,9 @@
 // Estimates are reduced in 64-bit fixed point (integer sums are associative,
 // so the shared-memory atomics are deterministic): q_i = rint(w_i 2^(Q-e_w)),
 // m_i,p = rint(w_i R_i,p 2^(Q-e_w-e_R)) with 2^e_w > max w and 2^e_R > max|R|;
-// p_hat = sum q * (1 / W), W = sum q, and v_hat = 2^e_R * sum m / sum q over
-// the samples that drew hand h; n_eff = W^2 / sum q^2 (at most n_samples).
+// p_hat = float(sum q) * float(1 / W), W = sum q, and v_hat = float(sum m) *
+// rcp(float(sum q)) * 2^e_R over the samples that drew hand h (single precision
+// from the integer sums on); n_eff = W^2 / sum q^2 (at most n_samples).
 //
 // One persistent CTA per leaf row (256 threads, or 512 when the sample records
 // leave room for one CTA per SM only), all tables in shared memory: the hand ->
@@ -291,9 +292,10 @@ rb_complete_kernel(CategoryOrder O, int R, int D, int first, int64_t F, int P, i
         for (int idx = tid; idx < P * D; idx += T) {
             const int q = idx / D, c = idx - q * D;
             const float* w = wb + q * Hp;
-            // the hands holding c in increasing id: {a, c} for a < c, then {c, b} for b > c
+            // the hands holding c in increasing id, t = 0..D-2: {t, c} for t < c, then {c, t + 1}; four
+            // running sums (terms t = 0, 1, 2, 3 mod 4, each in order), then (s0 + s1) + (s2 + s3)
             const int row = c * (2 * D - c - 1) / 2 - c - 1;
-            double m = 0.0;
+            double part[4] = {0.0, 0.0, 0.0, 0.0};
             for (int t0 = 0; t0 < D - 1; t0 += 8) {
                 float x[8];
                 #pragma unroll
@@ -304,9 +306,9 @@ rb_complete_kernel(CategoryOrder O, int R, int D, int first, int64_t F, int P, i
                 }
                 #pragma unroll
                 for (int u = 0; u < 8; ++u)
-                    if (t0 + u < D - 1) m = __dadd_rn(m, (double)x[u]);
+                    if (t0 + u < D - 1) part[u & 3] = __dadd_rn(part[u & 3], (double)x[u]);
             }
-            mass[idx] = m;
+            mass[idx] = __dadd_rn(__dadd_rn(part[0], part[1]), __dadd_rn(part[2], part[3]));
         }
         __syncthreads();
         // ---- per seat: guide[k] = the first hand whose CDF exceeds (k / RB_GUIDE) * top, guide[RB_GUIDE] = H - 1
@@ -541,8 +543,8 @@ rb_complete_kernel(CategoryOrder O, int R, int D, int first, int64_t F, int P, i
             S2 = __dadd_rn(S2, red[3 * WARPS + k]);
         }
         const double Wd = (double)W;
-        const double invW = W > 0 ? __ddiv_rn(1.0, Wd) : 0.0;
-        const double scale_r = pow2(er);
+        const float inv_w = W > 0 ? __double2float_rn(__ddiv_rn(1.0, Wd)) : 0.0f;
+        const float scale_r = ldexpf(1.0f, min(er, 127));  // exact: |returns| < 2^er
 
         // ---- per published seat, `group` seats per pass: fixed-point occurrence and return sums
         //      ([4][H] words per seat: occurrence low/high, return low/high), then the estimates;
@@ -563,20 +565,24 @@ rb_complete_kernel(CategoryOrder O, int R, int D, int first, int64_t F, int P, i
                 }
             }
             __syncthreads();
-            for (int k = tid; k < g_end * H; k += T) {
-                const int g = k / H, h = k - g * H;
+            for (int g = 0; g < g_end; ++g) {
                 unsigned* a = accum + g * 4 * H;
-                const long long n = (long long)(((unsigned long long)a[H + h] << 32) | a[h]);
-                float pv = 0.0f, vv = 0.0f;
-                if (n != 0) {
-                    const long long m = (long long)(((unsigned long long)a[3 * H + h] << 32) | a[2 * H + h]);
-                    pv = __double2float_rn(__dmul_rn((double)n, invW));
-                    vv = __double2float_rn(__dmul_rn(__ddiv_rn((double)m, (double)n), scale_r));
-                    a[h] = a[H + h] = a[2 * H + h] = a[3 * H + h] = 0u;
+                float* po = p_hat + (f * outputs + o0 + g) * (int64_t)H;
+                float* vo = v_hat + (f * outputs + o0 + g) * (int64_t)H;
+                #pragma unroll 4
+                for (int h = tid; h < H; h += T) {
+                    const long long n = (long long)(((unsigned long long)a[H + h] << 32) | a[h]);
+                    float pv = 0.0f, vv = 0.0f;
+                    if (n != 0) {  // single precision from here: n and m rounded to float once each
+                        const long long m = (long long)(((unsigned long long)a[3 * H + h] << 32) | a[2 * H + h]);
+                        const float nf = __ll2float_rn(n), mf = __ll2float_rn(m);
+                        pv = __fmul_rn(nf, inv_w);
+                        vv = __fmul_rn(__fmul_rn(mf, __frcp_rn(nf)), scale_r);
+                        a[h] = a[H + h] = a[2 * H + h] = a[3 * H + h] = 0u;
+                    }
+                    __stcs(po + h, pv);
+                    __stcs(vo + h, vv);
                 }
-                const int64_t out = (f * outputs + o0 + g) * (int64_t)H + h;
-                __stcs(p_hat + out, pv);
-                __stcs(v_hat + out, vv);
             }
             __syncthreads();
         }

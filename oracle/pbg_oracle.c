@@ -1267,7 +1267,8 @@ int32_t orc_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *d
  *   - per seat, an fp32 CDF rounded from a double running sum whose 32
  *     contiguous segments (ceil(H/32) rounded up to 4 hands) start from an
  *     inclusive Kogge-Stone scan of the segment totals; Z = the double total;
- *     per-card masses summed in hand-id order;
+ *     per-card masses: the hands holding the card in hand-id order as four
+ *     running sums of every fourth term, then (s0 + s1) + (s2 + s3);
  *   - sample i (base key rng_key(root i) in the COMPLETION namespace of the
  *     row's seed; draw `code` uses mix63(base + (code + 1) * 0x9E3779B97F4A7C15)),
  *     seats q in order: Z(dead) = (Z - the dead cards' masses, seat by seat) +
@@ -1278,8 +1279,9 @@ int32_t orc_decision_log_mass(int64_t n, const int32_t *parent, const int32_t *d
  *   - missing board slots j dealt uniformly from the unused deck (code
  *     1024 + j); returns settled as evaluate_showdowns settles them;
  *   - 64-bit fixed-point sums of q_i = rint(w_i 2^(Q-ew)) and
- *     rint(w_i R 2^(Q-ew-er)), Q = 61 - ceil(log2 N); p_hat = sum q * (1/W),
- *     v_hat = (sum m / sum q) 2^er; n_eff = W^2 / sum q^2 with sum q^2 reduced
+ *     rint(w_i R 2^(Q-ew-er)), Q = 61 - ceil(log2 N); then in single precision
+ *     p_hat = float(sum q) * float(1/W), v_hat = float(sum m) * (1 / float(sum q))
+ *     * 2^er; n_eff = W^2 / sum q^2 with sum q^2 reduced
  *     as 256 thread-strided partial sums, 32-lane butterflies and warps in
  *     order.
  * Returns the status bits (1: invalid board card or selected seat, 2: a row
@@ -1388,10 +1390,12 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
                 if (l == 31) zd[q] = run;
             }
             for (int c = 0; c < D; ++c) {
-                double m = 0.0;
-                for (int a = 0; a < c; ++a) m = m + (double)w[rb_pair_id(D, a, c)];
-                for (int b = c + 1; b < D; ++b) m = m + (double)w[rb_pair_id(D, c, b)];
-                mass[q * D + c] = m;
+                double part[4] = {0.0, 0.0, 0.0, 0.0};
+                for (int t = 0; t < D - 1; ++t) {
+                    int id = t < c ? rb_pair_id(D, t, c) : rb_pair_id(D, c, t + 1);
+                    part[t & 3] = part[t & 3] + (double)w[id];
+                }
+                mass[q * D + c] = (part[0] + part[1]) + (part[2] + part[3]);
             }
         }
         const uint64_t ns = rng_namespace(seed[f], 0, 6 /* COMPLETION */);
@@ -1548,7 +1552,9 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
             }
             S2 = S2 + v[0];
         }
-        const double Wd = (double)W, invW = W > 0 ? 1.0 / Wd : 0.0;
+        const double Wd = (double)W;
+        const float inv_w = W > 0 ? (float)(1.0 / Wd) : 0.0f;
+        const float scale_r = ldexpf(1.0f, er < 127 ? er : 127);
         for (int o = 0; o < outputs; ++o) {
             int p = selected ? sel : o;
             memset(pacc, 0, sizeof(long long) * H);
@@ -1562,8 +1568,14 @@ int32_t orc_rb_complete(int32_t R, int64_t F, int32_t P, int32_t strata, int32_t
             }
             float *po = p_hat + (f * outputs + o) * (int64_t)H, *vo = v_hat + (f * outputs + o) * (int64_t)H;
             for (int h = 0; h < H; ++h) {
-                po[h] = pacc[h] != 0 ? (float)((double)pacc[h] * invW) : 0.0f;
-                vo[h] = pacc[h] != 0 ? (float)(((double)vacc[h] / (double)pacc[h]) * ldexp(1.0, er)) : 0.0f;
+                if (pacc[h] != 0) {
+                    float nf = (float)pacc[h], mf = (float)vacc[h];
+                    po[h] = nf * inv_w;
+                    vo[h] = (mf * (1.0f / nf)) * scale_r;
+                } else {
+                    po[h] = 0.0f;
+                    vo[h] = 0.0f;
+                }
             }
         }
         n_eff[f] = W > 0 ? (float)fmin(Wd * Wd / S2, (double)N) : 0.0f;
