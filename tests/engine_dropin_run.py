@@ -1,7 +1,7 @@
 """One training iteration of the reference's own engine, optionally routed to libpbgb200.
 
     python tests/engine_dropin_run.py <out_dir> <reference|b200|b200_learner> [roots] [iterations] [program]
-                                      [sampled|rao_blackwell] [players stack_bb ranks]
+                                      [sampled|rao_blackwell|branched_rao_blackwell] [players stack_bb ranks]
 
 Test infrastructure for tests/test_gpu_engine_dropin.py (run in a fresh process
 so that the two engines never share imported state).  It loads the reference
@@ -67,6 +67,53 @@ run:
 """
 
 
+BRANCHED = """kind: nlhe_run_v1
+scientific:
+  mode: {{training_regime: self_play, rollout_mode: branched.fixed, private_estimator: rao_blackwell}}
+  game: {{players: {players}, stack_bb: {stack}, rank_count: {ranks}}}
+  model:
+    d_model: 32
+    n_heads: 4
+    layers: 1
+    raises: {{components: 2, minimum_scale: 0.02}}
+    class_embedding_dim: 8
+    ffn_hidden: 64
+    folder_beta_rank: {beta_rank}
+    folder_line_dim: 8
+    epsilon: 1.0e-8
+  objective:
+    policy_clip: 0.2
+    value: {{kind: mse, coefficient: 0.5}}
+    entropy: {{kind: constant, coefficient: 0.01}}
+    branching: {{trace_coefficient: 0.1, cost_coefficient: 0.1, trace_epsilon: 1.0e-6}}
+  optimizer: {{kind: adamw, learning_rate: 0.0003, beta1: 0.9, beta2: 0.999, epsilon: 1.0e-8, weight_decay: 0.0,
+              grad_clip: 1.0}}
+  schedule: {{batch_size: 16, epochs: 1}}
+  lambda: 0.95
+  branching:
+    fixed_beta: {{player: 1.5, chance: 1.25}}
+    beta_max: 3
+    minimum_tree_size: 16
+    cost_safeguard: {{gamma_deviance_max: 0.2, p95_underprediction_max: 1.5, consecutive_iterations: 4}}
+  completion: {{samples: 16}}
+run:
+  seed: 20261202
+  reproducibility: strict
+  utility: raw_bb
+  workload: {{roots: {roots}, tree_nodes: 512}}
+  execution:
+    device: cuda:0
+    precision: fp32
+    attention: sdpa
+    memory: {{reserve_bytes: 67108864}}
+    microbatch: auto
+    tensor_program: {{mode: {program}}}
+  iterations: {iterations}
+  checkpoint_every: 1000
+  output_dir: {out}
+"""
+
+
 def main() -> None:
     out, arm = sys.argv[1], sys.argv[2]
     roots = int(sys.argv[3]) if len(sys.argv) > 3 else 16
@@ -90,7 +137,8 @@ def main() -> None:
     os.makedirs(out, exist_ok=True)
     path = os.path.join(out, f"{arm}.yaml")
     with open(path, "w") as f:
-        f.write(CONFIG.format(roots=roots, iterations=iterations, program=program, estimator=estimator,
+        template = BRANCHED if estimator == "branched_rao_blackwell" else CONFIG
+        f.write(template.format(roots=roots, iterations=iterations, program=program, estimator=estimator,
                               completion=completion, players=players, stack=stack, ranks=ranks,
                               beta_rank=0 if players == 2 else 4, out=os.path.join(out, f"run_{arm}")))
     # record the flat gradient rows each optimizer transition receives (pbg/core/optimization.py:394-399)
