@@ -26,7 +26,7 @@ from torch import Tensor
 from torch.nn import functional as F
 
 from .checks import _assert, input_errors, raise_input_errors
-from .preflop import FamilyModel, PolicyOutput, PreflopConfig
+from .preflop import FamilyModel, PolicyOutput, PreflopConfig, _affine_rows
 
 
 @dataclass
@@ -462,16 +462,17 @@ class PostflopModel(FamilyModel):
                                 torch.zeros_like(corrected))
         ex = lambda t: t[:, None].expand(-1, live, -1, -1)  # noqa: E731
         ones = torch.ones_like(compact_ranges)[..., None]
-        row = self.row_affine(torch.cat((compact_ranges[..., None], log_range[..., None], corrected[..., None],
-                                         ex(combo_emb), ex(geometry), ex(pressure), ones), -1)).float()
+        feats = torch.cat((compact_ranges[..., None], log_range[..., None], corrected[..., None],
+                           ex(combo_emb), ex(geometry), ex(pressure), ones), -1)
         seats = torch.arange(players, device=dev)[None].expand(batch, -1)
         button = pub.get("button")
         relative = torch.remainder(seats - button[:, None].long(), players) if button is not None else seats
         live_relative = relative.gather(1, live_ids)
         live_status = status.gather(1, live_ids)
-        row = row + p["seat_embedding.weight"][live_relative][:, :, None]
-        row = row + p["status_embedding.weight"][live_status][:, :, None]
-        row = row + p["actor_embedding.weight"][(live_ids == actor[:, None]).long()][:, :, None]
+        # each live seat's seat, status and actor embeddings, added to its q rows in the map's epilogue
+        seat_terms = (p["seat_embedding.weight"][live_relative] + p["status_embedding.weight"][live_status]
+                      + p["actor_embedding.weight"][(live_ids == actor[:, None]).long()])
+        row = _affine_rows(self.row_affine, feats, seat_terms, q)
         rows_k = live * q
         public, public_mask = self._public_tokens(pub, masks.fold_line_features, relative)
         actor_relative = relative.gather(1, actor[:, None]).squeeze(1)

@@ -142,6 +142,20 @@ def _padded(x: Tensor, width: int) -> Tensor:
     return x.contiguous()
 
 
+def _affine_rows(affine, feats: Tensor, seat_terms: Tensor, rows_per_seat: int) -> Tensor:
+    """affine(feats) + seat_terms broadcast over each seat's rows, in fp32: one map whose epilogue adds
+    the per-seat terms (residual row m // rows_per_seat) and writes fp32, where the map's width allows
+    it; otherwise the map, then the broadcast addition."""
+
+    lead = feats.shape[:-1]
+    if affine.np_ != affine.n:
+        return affine(feats).float() + seat_terms[..., None, :]
+    rows = _padded(feats, affine.kp)
+    terms = seat_terms.reshape(-1, affine.n).float().contiguous()
+    return affine.apply(rows, residual=terms, residual_group=rows_per_seat, out_dtype=torch.float32).view(
+        *lead, affine.n)
+
+
 def _cat_maps(first: Tensor, second: Tensor) -> Tensor:
     return torch.cat((first, second), dim=1)
 
@@ -464,11 +478,11 @@ class PreflopModel(FamilyModel):
         log_range = torch.log(ranges.clamp_min(cfg.eps))
         row_feature = torch.cat((ranges[..., None], log_range[..., None], size_feature[..., None], expanded_emb,
                                  expanded_geometry, torch.ones_like(ranges)[..., None]), -1)
-        row = self.class_row_affine(row_feature).float()
-        row = row + p["seat_embedding.weight"][relative][:, :, None]
-        row = row + p["status_embedding.weight"][status][:, :, None]
         actor_flag = (torch.arange(players, device=dev)[None] == actor[:, None]).long()
-        row = row + p["actor_embedding.weight"][actor_flag][:, :, None]
+        # each seat's seat, status and actor embeddings, added to its K class rows in the map's epilogue
+        seat_terms = (p["seat_embedding.weight"][relative] + p["status_embedding.weight"][status]
+                      + p["actor_embedding.weight"][actor_flag])
+        row = _affine_rows(self.class_row_affine, row_feature, seat_terms, K)
         row_flat = row.reshape(batch, players * K, d)
         public_token, public_mask = self._public_tokens(pub, seat_mask, relative)
         actor_relative = relative.gather(1, actor[:, None]).squeeze(1)
