@@ -109,10 +109,10 @@ class _Map:
     def __call__(self, x: Tensor, activation: str | None = None) -> Tensor:
         lead = x.shape[:-1]
         rows = x.reshape(-1, x.shape[-1])
-        if rows.dtype != torch.bfloat16:
-            rows = rows.to(torch.bfloat16)
         if rows.shape[1] != self.kp:  # already padded operands (width kp) pass straight through
-            rows = F.pad(rows, (0, self.kp - self.k))
+            rows = _padded(rows, self.kp)
+        elif rows.dtype != torch.bfloat16:
+            rows = rows.to(torch.bfloat16)
         y = linear(rows if rows.is_contiguous() else rows.contiguous(), self.weight, self.bias, activation)
         if self.np_ != self.n:
             y = y[:, : self.n]
@@ -134,12 +134,16 @@ class _Map:
 
 
 def _padded(x: Tensor, width: int) -> Tensor:
-    """x as a contiguous bf16 matrix zero-padded to ``width`` columns (the map's padded K)."""
+    """x as a contiguous bf16 matrix zero-padded to ``width`` columns (the map's padded K): one pass
+    that converts into the padded buffer, the pad columns filled alone."""
 
-    x = x.reshape(-1, x.shape[-1]).to(torch.bfloat16)
-    if x.shape[1] != width:
-        x = F.pad(x, (0, width - x.shape[1]))
-    return x.contiguous()
+    x = x.reshape(-1, x.shape[-1])
+    if x.shape[1] == width:
+        return x.to(torch.bfloat16).contiguous()
+    out = torch.empty((x.shape[0], width), dtype=torch.bfloat16, device=x.device)
+    out[:, : x.shape[1]] = x
+    out[:, x.shape[1]:] = 0
+    return out
 
 
 def _affine_rows(affine, feats: Tensor, seat_terms: Tensor, rows_per_seat: int) -> Tensor:
@@ -311,9 +315,13 @@ class FamilyModel:
         # FamilyFFN operand [LN(x_hat) | j | oc^2 | oc*oe | side] in one bf16 buffer, padded to the map's K;
         # the side features (fixed across layers) and the zero rows of non-row tokens are written once
         width = self.layers[0]["ffn_in"].kp if self.layers else 0
-        operand = torch.zeros((batch, length, width), dtype=torch.bfloat16, device=x.device)
+        operand = torch.empty((batch, length, width), dtype=torch.bfloat16, device=x.device)
         side_width = side.shape[-1]
         operand[:, :rows_k, 4 * d: 4 * d + side_width] = side.reshape(batch, rows_k, side_width)
+        # every layer writes LN(x_hat) into the first d columns of all tokens, and j, oc^2 and oc*oe into
+        # the next 3d of the row tokens: what stays zero is filled once, alone
+        operand[:, :rows_k, 4 * d + side_width:] = 0
+        operand[:, rows_k:, d:] = 0
         mass_rows = mass.reshape(-1).to(torch.float32).contiguous()
         scale_rows = identical_scale.to(torch.float32).contiguous()
         x = x.contiguous()
