@@ -24,7 +24,7 @@ BUILD = os.path.join(HERE, "_build")
 
 EXACT = ["common.cu", "poker.cu", "policy.cu", "showdown.cu", "completion.cu", "targets.cu", "posterior.cu", "branching.cu",
          "incidence.cu"]
-FAST = ["loss.cu", "learner.cu", "mlp.cu", "adam.cu", "collective.cu", "gemm.cu", "attention.cu", "layernorm.cu", "folded.cu", "eigh.cu"]
+FAST = ["loss.cu", "learner.cu", "mlp.cu", "model_backward.cu", "adam.cu", "collective.cu", "gemm.cu", "attention.cu", "layernorm.cu", "folded.cu", "eigh.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

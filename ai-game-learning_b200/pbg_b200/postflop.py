@@ -150,7 +150,7 @@ class PostflopModel(FamilyModel):
         lin, p = self._lin, self.p
 
         def ffn(name):
-            return (lin(name + ".w1"), lin(name + ".w2"), p[name + ".w1.weight"], p[name + ".w1.bias"])
+            return (lin(name + ".w1"), lin(name + ".w2"), name)
 
         self.combo_features = ffn("combo_features")
         self.folder_context = ffn("folder_context")

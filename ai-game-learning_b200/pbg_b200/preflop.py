@@ -17,7 +17,6 @@ them) and the small elementwise steps are torch operations on the device.
 from __future__ import annotations
 
 import ctypes
-import math
 from dataclasses import dataclass
 
 import torch
@@ -26,6 +25,7 @@ from torch.nn import functional as F
 
 from ._native import NativeError, call, ptr, rows_ptr, stream
 from .model import attention, linear, linear_ex
+from .model_train import attention_train, layernorm_train, linear_train, q_scale_of
 
 
 @dataclass(frozen=True)
@@ -90,21 +90,45 @@ class PolicyOutput:
     c: Tensor | None = None
 
 
-class _Map:
-    """A Linear bound for pbg_linear_bf16: bf16 weight padded to K % 64 == 0 and N % 128 == 0."""
+class _Binding:
+    """Mode shared by a model's maps: ``training`` routes every map through its autograd function."""
 
-    def __init__(self, weight: Tensor, bias: Tensor | None, device) -> None:
+    def __init__(self) -> None:
+        self.training = False
+
+
+class _Map:
+    """A Linear bound for pbg_linear_bf16: bf16 weight padded to K % 64 == 0 and N % 128 == 0.
+
+    ``source`` returns the map's fp32 (weight [n, k], bias [n] or None) from the model's parameters
+    (the concatenation or slice of them for fused maps); in training mode (``binding.training``) the
+    map runs as ``model_train.linear_train`` with those tensors as its autograd inputs, the padded bf16
+    copy refreshed from them at every call."""
+
+    def __init__(self, weight: Tensor, bias: Tensor | None, device, source=None, binding: _Binding | None = None) -> None:
         n, k = weight.shape
         self.n, self.k = n, k
         self.kp, self.np_ = -(-k // 64) * 64, -(-n // 128) * 128
         w = torch.zeros((self.np_, self.kp), dtype=torch.bfloat16, device=device)
-        w[:n, :k] = weight.to(device=device, dtype=torch.bfloat16)
+        w[:n, :k] = weight.detach().to(device=device, dtype=torch.bfloat16)
         self.weight = w
         self.bias = None
         if bias is not None:
             b = torch.zeros(self.np_, dtype=torch.float32, device=device)
-            b[:n] = bias.to(device=device, dtype=torch.float32)
+            b[:n] = bias.detach().to(device=device, dtype=torch.float32)
             self.bias = b
+        self.source = source
+        self.binding = binding
+
+    def refresh(self, weight: Tensor, bias: Tensor | None) -> None:
+        """Copy the fp32 weight / bias into the padded bf16 operand and fp32 bias."""
+
+        self.weight[: self.n, : self.k].copy_(weight.detach())
+        if self.bias is not None and bias is not None:
+            self.bias[: self.n].copy_(bias.detach())
+
+    def _training(self) -> bool:
+        return self.binding is not None and self.binding.training
 
     def __call__(self, x: Tensor, activation: str | None = None) -> Tensor:
         lead = x.shape[:-1]
@@ -113,6 +137,8 @@ class _Map:
             rows = _padded(rows, self.kp)
         elif rows.dtype != torch.bfloat16:
             rows = rows.to(torch.bfloat16)
+        if self._training():
+            return linear_train(self, rows, activation).reshape(*lead, self.n)
         y = linear(rows if rows.is_contiguous() else rows.contiguous(), self.weight, self.bias, activation)
         if self.np_ != self.n:
             y = y[:, : self.n]
@@ -128,6 +154,11 @@ class _Map:
             raise NativeError("map operand must be a [rows, padded in] matrix")
         if self.np_ != self.n and (residual is not None or out is not None):
             raise NativeError("a fused residual or output buffer needs an unpadded output width")
+        if self._training():
+            if out is not None:
+                raise NativeError("a map in training mode writes no caller buffer")
+            return linear_train(self, rows, activation, row_scale=row_scale, residual=residual,
+                                residual_group=residual_group, out_dtype=out_dtype)
         y = linear_ex(rows, self.weight, self.bias, activation, row_scale=row_scale, residual=residual,
                       residual_group=residual_group, out=out, out_dtype=out_dtype)
         return y if self.np_ == self.n else y[:, : self.n]
@@ -180,35 +211,40 @@ class FamilyModel:
         self.n_cards = 4 * rank_count
         p = {k: v.to(self.device, torch.float32) for k, v in params.items()}
         self.p = p
-        lin = lambda name, bias=True: _Map(p[name + ".weight"], p.get(name + ".bias") if bias else None, self.device)  # noqa: E731
+        self.binding = _Binding()
+        self._maps: list[_Map] = []
+
+        def lin(name, bias=True):
+            return self._map(p[name + ".weight"], p.get(name + ".bias") if bias else None,
+                             lambda: (self.p[name + ".weight"], self.p.get(name + ".bias") if bias else None))
+
         self._lin = lin
         self.layers = []
         for i in range(cfg.layers):
             inc = f"incidence_residuals.{i}"
             ffn = f"layer_ffns.{i}"
             mha = f"attentions.{i}"
-            theta = p[f"{mha}.theta"]
-            temperature = F.softplus(theta) + 0.5
+            parts = (f"{inc}.query.weight", f"{inc}.identical.weight", f"{inc}.own.weight")
+            halves = (f"{ffn}.common.weight", f"{ffn}.static.{self.family}.weight")
             self.layers.append({
-                "ln": (p[f"layer_norms.{i}.weight"], p[f"layer_norms.{i}.bias"]),
-                "inc_ln": (p[f"{inc}.norm.weight"], p[f"{inc}.norm.bias"]),
                 "source": lin(f"{inc}.source", False),
                 # query(n) + identical(other_equal) + own(own_card) as one map over [n | other_equal | own_card]
-                "inc_in": _Map(torch.cat((p[f"{inc}.query.weight"], p[f"{inc}.identical.weight"],
-                                          p[f"{inc}.own.weight"]), dim=1), p[f"{inc}.query.bias"], self.device),
+                "inc_in": self._map(torch.cat([p[n] for n in parts], dim=1), p[f"{inc}.query.bias"],
+                                    lambda parts=parts, inc=inc: (torch.cat([self.p[n] for n in parts], dim=1),
+                                                                  self.p[f"{inc}.query.bias"])),
                 "inc_out": lin(f"{inc}.output"),
                 "w_qkv": lin(f"{mha}.w_qkv"),
                 "w_o": lin(f"{mha}.w_o"),
-                "q_scale": (1.0 / (temperature * math.sqrt(32))).contiguous(),
                 # FamilyFFN (shared.py:19-33): common(x) + static[family](s) as one map over [x, s]
-                "ffn_in": _Map(_cat_maps(p[f"{ffn}.common.weight"], p[f"{ffn}.static.{self.family}.weight"]),
-                               p[f"{ffn}.common.bias"], self.device),
+                "ffn_in": self._map(_cat_maps(p[halves[0]], p[halves[1]]), p[f"{ffn}.common.bias"],
+                                    lambda halves=halves, ffn=ffn: (_cat_maps(self.p[halves[0]], self.p[halves[1]]),
+                                                                    self.p[f"{ffn}.common.bias"])),
                 "ffn_out": lin(f"{ffn}.output"),
             })
-        self.final_ln = (p["final_norm.weight"], p["final_norm.bias"])
+        self._bind_layer_parameters()
 
         def ffn(name):
-            return (lin(name + ".w1"), lin(name + ".w2"), p[name + ".w1.weight"], p[name + ".w1.bias"])
+            return (lin(name + ".w1"), lin(name + ".w2"), name)
 
         self.actor_seat_features = ffn("actor_seat_features")
         self.seat_features = ffn("seat_features")
@@ -225,10 +261,61 @@ class FamilyModel:
         self.branching = "branching_heads.public_features.w1.weight" in p
         self._factored: dict = {}
 
+    # ------------------------------------------------------------ parameters and modes
+    def _map(self, weight: Tensor, bias: Tensor | None, source) -> _Map:
+        m = _Map(weight, bias, self.device, source, self.binding)
+        self._maps.append(m)
+        return m
+
+    def _bind_layer_parameters(self) -> None:
+        """The LayerNorm pairs and head score scales of every layer, from the current parameters."""
+
+        p = self.p
+        for i, layer in enumerate(self.layers):
+            inc = f"incidence_residuals.{i}"
+            layer["ln"] = (p[f"layer_norms.{i}.weight"], p[f"layer_norms.{i}.bias"])
+            layer["inc_ln"] = (p[f"{inc}.norm.weight"], p[f"{inc}.norm.bias"])
+            layer["theta"] = p[f"attentions.{i}.theta"]
+            layer["q_scale"] = q_scale_of(p[f"attentions.{i}.theta"].detach()).contiguous()
+        self.final_ln = (p["final_norm.weight"], p["final_norm.bias"])
+
+    def bind_parameters(self, params: dict[str, Tensor]) -> None:
+        """Use ``params`` (this model's names, e.g. leaf views of a flat fp32 master) as the parameters."""
+
+        missing = sorted(set(self.p) - set(params))
+        if missing:
+            raise KeyError(f"parameters missing: {missing[:4]}")
+        self.p = {name: params[name] for name in self.p}
+        self._bind_layer_parameters()
+        self.sync_weights()
+
+    def sync_weights(self) -> None:
+        """Refresh every map's bf16 operand and the score scales from the current parameters (after an
+        optimizer step, before an inference-mode forward)."""
+
+        with torch.no_grad():
+            for m in self._maps:
+                if m.source is not None:
+                    m.refresh(*m.source())
+            for layer in self.layers:
+                layer["q_scale"] = q_scale_of(layer["theta"].detach()).contiguous()
+
+    def train(self, mode: bool = True) -> "FamilyModel":
+        """Training mode: every native step runs as an autograd function (model_train)."""
+
+        self.binding.training = bool(mode)
+        if not mode:
+            self.sync_weights()
+        return self
+
     # ------------------------------------------------------------ kernels
     def _ln(self, x: Tensor, gain_bias, out: Tensor | None = None) -> Tensor:
         """LayerNorm -> bf16, into `out` (rows of any stride, e.g. a slice of a wider operand) if given."""
 
+        if self.binding.training:
+            if out is not None:
+                raise NativeError("a LayerNorm in training mode writes no caller buffer")
+            return layernorm_train(x, gain_bias[0], gain_bias[1])
         d = x.shape[-1]
         rows = x.reshape(-1, d).contiguous()
         if out is None:
@@ -247,10 +334,13 @@ class FamilyModel:
         """primitives.py:62-71 forward_factored: the context projected once per decision."""
 
         split = rows.shape[-1]
-        key = (id(maps), split)
+        name = maps[2]
+        key = (name, split)
         if key not in self._factored:
-            w1, b1 = maps[2], maps[3]
-            self._factored[key] = (_Map(w1[:, :split], b1, self.device), _Map(w1[:, split:], None, self.device))
+            wn, bn = name + ".w1.weight", name + ".w1.bias"
+            w1, b1 = self.p[wn], self.p[bn]
+            self._factored[key] = (self._map(w1[:, :split], b1, lambda: (self.p[wn][:, :split], self.p[bn])),
+                                   self._map(w1[:, split:], None, lambda: (self.p[wn][:, split:], None)))
         row_map, ctx_map = self._factored[key]
         # the context projection is computed once per decision (fp32) and added to each of its rows in the
         # row map's epilogue, GELU fused there too
@@ -308,6 +398,9 @@ class FamilyModel:
         biased attention with the residual add fused into the output map, FamilyFFN over
         [LN(x_hat) | j, oc^2, oc*oe | side] with the residual add fused into its output map."""
 
+        if self.binding.training:
+            return self._trunk_train(x, players, rows_per_seat, mass, incidence, identical_scale, side, key_bias,
+                                     key_mask)
         cfg = self.cfg
         d = cfg.d_model
         batch, length, _ = x.shape
@@ -337,6 +430,65 @@ class FamilyModel:
             self._ln(x_hat, layer["ln"], flat[:, :d])
             hidden = layer["ffn_in"].apply(flat, "gelu")
             x = layer["ffn_out"].apply(hidden, residual=x_hat, out_dtype=torch.float32).view(batch, length, d)
+        return x
+
+    def _incidence_train(self, layer, x: Tensor, players: int, rows: int, mass: Tensor, incidence: Tensor,
+                         identical_scale: Tensor):
+        """``_incidence`` as autograd steps (incidence.py:30-84): the LayerNorm, the source map with the
+        row mass as its row scale, the fp32 card contractions and seat sums, the query/identical/own map
+        with oc as its pre-GELU residual and the output map.  Returns j [B * players * rows, d] and the
+        FamilyFFN features oc^2, oc * oe [B, players * rows, d] (bf16)."""
+
+        batch, length, d = x.shape
+        count = batch * players * rows
+        n = self._ln(x[:, : players * rows].reshape(count, d), layer["inc_ln"])
+        source = layer["source"].apply(n, row_scale=mass, out_dtype=torch.float32)
+        if incidence.dim() == 2:
+            blocks = source.view(batch * players, rows, d)
+            card_overlap = torch.matmul(incidence, torch.matmul(incidence.t(), blocks))
+        else:
+            blocks = source.view(batch, players, rows, d)
+            card_overlap = torch.matmul(incidence[:, None], torch.matmul(incidence.transpose(1, 2)[:, None], blocks))
+        source = source.view(batch, players, rows, d)
+        card_overlap = card_overlap.reshape(batch, players, rows, d)
+        same = source * identical_scale.float()[:, None, :, None]
+        other_equal = same.sum(1, keepdim=True) - same
+        other_card = (card_overlap.sum(1, keepdim=True) - card_overlap) - 2.0 * other_equal
+        own_card = card_overlap - 2.0 * same
+        operand = torch.cat((n, other_equal.reshape(count, d).to(torch.bfloat16),
+                             own_card.reshape(count, d).to(torch.bfloat16)), -1)
+        hidden = layer["inc_in"].apply(operand, "gelu", residual=other_card.reshape(count, d))
+        j = layer["inc_out"].apply(hidden)
+        square = (other_card * other_card).to(torch.bfloat16).view(batch, players * rows, d)
+        product = (other_card * other_equal).to(torch.bfloat16).view(batch, players * rows, d)
+        return j, square, product
+
+    def _trunk_train(self, x: Tensor, players: int, rows_per_seat: int, mass: Tensor, incidence: Tensor,
+                     identical_scale: Tensor, side: Tensor, key_bias: Tensor, key_mask: Tensor) -> Tensor:
+        """``_trunk`` as autograd steps: the same maps, LayerNorms and attention core, the FamilyFFN operand
+        assembled by concatenation instead of in place."""
+
+        cfg = self.cfg
+        d = cfg.d_model
+        batch, length, _ = x.shape
+        rows_k = players * rows_per_seat
+        side_rows = side.reshape(batch, rows_k, -1).to(torch.bfloat16)
+        mass_rows = mass.reshape(-1).detach().to(torch.float32).contiguous()
+        pad = torch.zeros((batch, length - rows_k, 3 * d + side_rows.shape[-1]), dtype=torch.bfloat16,
+                          device=x.device)
+        x = x.contiguous()
+        for layer in self.layers:
+            j, square, product = self._incidence_train(layer, x, players, rows_per_seat, mass_rows, incidence,
+                                                       identical_scale)
+            nx = self._ln(x, layer["ln"])
+            qkv = layer["w_qkv"](nx)
+            attended = attention_train(qkv, cfg.n_heads, q_scale_of(layer["theta"]), key_bias, key_mask)
+            x_hat = layer["w_o"].apply(attended.view(-1, d), residual=x.view(-1, d), out_dtype=torch.float32)
+            normed = self._ln(x_hat, layer["ln"]).view(batch, length, d)
+            extra = torch.cat((torch.cat((j.view(batch, rows_k, d), square, product, side_rows), -1), pad), 1)
+            hidden = layer["ffn_in"](torch.cat((normed, extra), -1), "gelu")
+            x = layer["ffn_out"].apply(hidden.view(batch * length, -1), residual=x_hat,
+                                       out_dtype=torch.float32).view(batch, length, d)
         return x
 
     def _head(self, head: "_Map", x: Tensor) -> Tensor:

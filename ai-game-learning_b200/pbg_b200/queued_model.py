@@ -87,12 +87,40 @@ class QueuedPokerModel:
             raise PokerModelError("model max_players does not cover all seats")
         self.geometry, self.cfg, self.device = geometry, config, torch.device(device)
         shared = _split(params, "shared.")
+        self._shared_names = frozenset(shared)
         self.pre = PreflopModel(config, geometry.rank_count, {**shared, **_split(params, "pre_encoder.")}, device)
         self.post = PostflopModel(config, geometry.rank_count, {**shared, **_split(params, "post_encoder.")}, device)
         self.machine = PokerStateMachine(geometry)
         self.combo_class = self.machine._combo_class(self.device)
         self.combo_cards = self.machine.combo_cards(
             torch.arange(geometry.private_hands, dtype=torch.int32, device=self.device)).to(torch.int64)
+
+    # ------------------------------------------------------------ training
+    def enable_training(self):
+        """Put both partition networks in training mode over ONE set of parameters: every parameter
+        (``shared.*``, ``pre_encoder.*``, ``post_encoder.*``) a leaf view of one flat fp32 master, the
+        shared ones the same leaves in both networks.  Returns the ``FlatParameters``."""
+
+        from .model_train import FlatParameters
+
+        def full(prefix: str, name: str) -> str:
+            return ("shared." if name in self._shared_names else prefix) + name
+
+        params = {full("pre_encoder.", n): v for n, v in self.pre.p.items()}
+        params.update({full("post_encoder.", n): v for n, v in self.post.p.items()})
+        flat = FlatParameters(params, self.device)
+        self.pre.bind_parameters({n: flat.leaves[full("pre_encoder.", n)] for n in self.pre.p})
+        self.post.bind_parameters({n: flat.leaves[full("post_encoder.", n)] for n in self.post.p})
+        self.pre.train()
+        self.post.train()
+        return flat
+
+    def eval(self) -> "QueuedPokerModel":
+        """Back to inference mode (the maps' bf16 operands refreshed from the current parameters)."""
+
+        self.pre.train(False)
+        self.post.train(False)
+        return self
 
     # ------------------------------------------------------------ input decoding
     def _state(self, input_type: str, model_input: Tensor) -> PokerState:

@@ -74,9 +74,12 @@ def parse():
     p.add_argument("--buckets", type=int, default=1,
                    help="N > 1: the rows' loss runs as this many chunks, and the gradient SUM as as many buckets "
                         "on a second stream, bucket k starting when chunk k's loss is done")
+    p.add_argument("--component", default=None,
+                   help="run one entry of the components object (its name there) and print it as one JSON line")
     p.add_argument("--profile-forward", choices=("preflop", "postflop", "attention", "folded", "posterior",
                                                  "readout", "reach", "showdown", "optimizer", "poker_loss",
-                                                 "rollout_with_model", "completion", "rollout", "learner_step"),
+                                                 "rollout_with_model", "completion", "rollout", "learner_step",
+                                                 "learner_step_cfg2"),
                    default=None,
                    help="run one eager forward of that component (attention: one attention-core launch at the "
                         "postflop sequence length, 48 x 2,406 tokens x 8 heads; folded: the removal queries and "
@@ -503,6 +506,170 @@ def learner_step_component(device, rows=16_384, reps=20):
             out["speedup_vs_reference_torch_cuda"] = ref_ms / ms
         except Exception as exc:  # noqa: BLE001 - reported, not fatal
             out["reference_torch_cuda_ms"] = f"failed: {str(exc)[:200]}"
+    return out
+
+
+def _cfg2_model(device):
+    """The cfg2 queued model: HU 100bb R13, d_model 128, 2 layers, 4 heads, class embedding 32, hidden 512,
+    M = 2 (random weights)."""
+
+    from pbg_b200.poker import NLHEGeometry
+    from pbg_b200.preflop import PreflopConfig
+    from pbg_b200.queued_model import QueuedPokerModel, parameter_shapes
+
+    geo = NLHEGeometry(2, 100.0, 13)
+    cfg = PreflopConfig(d_model=128, n_heads=4, layers=2, m_raise=2, k_act=5, max_players=2,
+                        class_embedding_dim=32, ffn_hidden=512, max_history_tokens=geo.history_tokens)
+    params = _random_params(parameter_shapes(cfg, 13), seed=29)
+    return QueuedPokerModel(geo, cfg, params, device), geo, cfg, params
+
+
+def _cfg2_learner_batches(device, model, pre_rows, post_rows, seed=41):
+    """Learner batches of retained rows from a seeded rollout of the cfg2 geometry: the preflop rows of
+    the roots and the heads-up postflop rows (post_2) of later steps, played by a fixed raw policy that
+    mostly calls; each row's legal set from the state machine with a legal taken action, the dealt
+    private hands as the sampled private state, the actor as owner, seeded old log policy, advantage,
+    values and targets."""
+
+    import torch
+    from pbg_b200.family_rollout import FamilyRollout
+
+    roll = FamilyRollout(model, seed=seed, iteration=3)
+    hands = max(pre_rows, 4 * post_rows)
+    arena, log_reach = roll.roots(hands, device=device)
+    raw = roll._raw_buffers(hands, device)
+    raw["type_logits"][..., 1] = 2.0  # mostly check/call, so that hands reach the flop
+    machine = roll.machine
+    found = {"pre": [], "post_2": []}
+    need = {"pre": pre_rows, "post_2": post_rows}
+    for _ in range(64):
+        state = arena.state
+        code = torch.where(state.terminal, -1, machine.input_type(state))
+        for kind, value in (("pre", 0), ("post_2", 1)):
+            have = sum(int(r.numel()) for r in found[kind][0::3]) if found[kind] else 0
+            if have < need[kind]:
+                rows = torch.nonzero(code == value).flatten()[: need[kind] - have]
+                if rows.numel():
+                    model_input, sub = roll._family_rows(arena, kind, rows, log_reach)
+                    found[kind] += [rows, model_input, sub]
+        if all((sum(int(r.numel()) for r in found[k][0::3]) if found[k] else 0) >= need[k] for k in need):
+            break
+        roll.stepper.step(arena, raw)
+        roll.stepper.reach_update(arena, raw, log_reach)
+    g = torch.Generator(device=device).manual_seed(seed)
+    batches = []
+    for kind in ("pre", "post_2"):
+        parts = found[kind]
+        model_input = torch.cat(parts[1::3])
+        subs = parts[2::3]
+        private = torch.cat([s.combo_ids for s in subs]).to(torch.int32)
+        owner = torch.cat([s.to_act for s in subs]).to(torch.int64)
+        mask = torch.cat([machine.legality(s).mask for s in subs])
+        S = model_input.shape[0]
+        pick = (torch.rand(S, device=device, generator=g) * mask.sum(1)).long()
+        action = (mask.cumsum(1) <= pick[:, None]).sum(1).to(torch.int32)
+        value = torch.randn(S, 1, device=device, generator=g)
+        batches.append({"input_type": kind, "model_input": model_input, "sampled_private_state": private,
+                        "owner": owner, "mask": mask, "action": action,
+                        "old_log_policy": -1.5 + 0.5 * torch.randn(S, 1, device=device, generator=g),
+                        "advantage_target": torch.randn(S, 1, device=device, generator=g),
+                        "old_value": value + 0.3 * torch.randn(S, 1, device=device, generator=g),
+                        "value_target": torch.randn(S, 1, device=device, generator=g),
+                        "controls": torch.tensor([[0.2, math.log(1.5), 0.5, 0.2, 0.01, 0.05, 0.0, 0.0, 1e-8, 1.0]],
+                                                 device=device),
+                        "lane_weight": torch.ones(1, device=device)})
+    return batches
+
+
+def _reference_cfg2_step_ms(device, cfg, params, batches, reps):
+    """The same learner step on the reference's PyTorch CUDA path: pbg's own QueuedPokerModel (SDPA
+    attention) with the same weights, its learner_operation and LearnerOperation.forward_loss under bf16
+    autocast (training.py:381-403), pbg's PokerPolicyOperator.learner, autograd, torch AdamW."""
+
+    import dataclasses
+    from types import MappingProxyType
+
+    import torch
+    from pbg.core.contracts import mode_schema
+    from pbg.core.learner import LearnerOperation, LossConfig, SequentialLearnerBatch
+    from pbg.games.poker.model.preflop import PokerModelConfig
+    from pbg.games.poker.queued.hooks import NLHEGeometry as RefGeometry
+    from pbg.games.poker.queued.model import QueuedPokerModel as RefModel
+    from pbg.games.poker.queued.policy import PokerLegality, PokerPolicyOperator
+
+    model = RefModel(RefGeometry(2, 100.0, 13), PokerModelConfig(**dataclasses.asdict(cfg))).to(device)
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            param.copy_(params[name].to(device))
+    opt = torch.optim.AdamW(list(model.parameters()), lr=3e-4, weight_decay=0.0)
+    op = PokerPolicyOperator()
+    prepared = []
+    for b in batches:
+        S, E = b["mask"].shape
+        legality = PokerLegality(torch.arange(E, dtype=torch.int32, device=device)[None].expand(S, -1).contiguous(),
+                                 b["mask"])
+
+        def policy(input_type, model_input, raw_rows, act, private, owner, reference, legality=legality):
+            return op.learner(raw_rows, legality, act, private, owner, reference)
+
+        fields = {k: b[k] for k in ("model_input", "owner", "action", "old_log_policy", "advantage_target",
+                                    "old_value", "value_target", "sampled_private_state")}
+        physical = SequentialLearnerBatch(b["input_type"], torch.arange(S, device=device), MappingProxyType(fields))
+        learner = LearnerOperation(mode_schema("self_play", "sequential", "sampled"), LossConfig(), None, policy)
+        prepared.append((b, physical, learner))
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        for b, physical, learner in prepared:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                evaluation = model.learner_operation(b["input_type"], b["model_input"], b["sampled_private_state"],
+                                                     b["owner"])
+                result = learner.forward_loss(physical, iteration=0, lane_count=1, loss_controls=b["controls"],
+                                              evaluation=evaluation)
+            (result.total * b["lane_weight"]).sum().backward()
+        opt.step()
+
+    return _events_ms(device, step, reps)
+
+
+def learner_step_cfg2_component(device, pre_rows=1024, post_rows=256, reps=3):
+    """The learner step the metric counts, at cfg2: HU 100bb R13 with the cfg2 attention network (d_model
+    128, 2 layers, 4 heads), `pre_rows` preflop and `post_rows` heads-up postflop learner presentations
+    (sampled private rows) from a seeded rollout: the training forward on this build's kernels, the fused
+    poker objective, the backward (pbg_b200.model_train) and AdamW.  Beside it, when the driver installed
+    the reference, the same step on the reference's own PyTorch CUDA path with the same weights."""
+
+    import torch
+    from pbg_b200.model_train import ModelLearnerStep
+
+    model, geo, cfg, params = _cfg2_model(device)
+    batches = _cfg2_learner_batches(device, model, pre_rows, post_rows)
+    step = ModelLearnerStep(model)
+    if PROFILE_ONE_FORWARD:
+        _device_ms(device, lambda: step(batches), 1)
+        return {}
+    step(batches)  # warm-up (bindings, first launches)
+    ms = _events_ms(device, lambda: step(batches), reps)
+    per_family = {}
+    for b in batches:
+        per_family[b["input_type"]] = _events_ms(device, lambda b=b: step.gradient([b]), reps)
+    rows = sum(b["model_input"].shape[0] for b in batches)
+    out = {"workload": f"cfg2 learner step: HU 100bb R13, cfg2 network (d_model 128, 2 layers, 4 heads, "
+                       f"{step.flat.numel} parameters), {pre_rows} preflop + {post_rows} postflop (post_2) "
+                       "sampled presentations, training forward + fused objective + backward + AdamW",
+           "ms": ms, "presentations_per_s": rows / (ms / 1e3), "parameters": step.flat.numel,
+           "forward_backward_ms_by_family": per_family,
+           "kernels": "linear_tcgen05_kernel, attention_kernel, layernorm, incidence / gelu / layernorm / attention-"
+                      "softmax backward kernels, cuBLAS bf16 GEMMs for dX, dW and the attention-backward products, "
+                      "learner_objective_kernel, adam"}
+    if _reference_pbg() is not None:
+        try:
+            ref_ms = _reference_cfg2_step_ms(device, cfg, params, batches, reps=reps)
+            out["reference_torch_cuda_ms"] = ref_ms
+            out["reference_presentations_per_s"] = rows / (ref_ms / 1e3)
+            out["speedup_vs_reference_torch_cuda"] = ref_ms / ms
+        except Exception as exc:  # noqa: BLE001 - reported, not fatal
+            out["reference_torch_cuda_ms"] = f"failed: {str(exc)[:300]}"
     return out
 
 
@@ -1593,6 +1760,17 @@ def posterior_component(device, parents=4096, rows=16384, reps=10):
 # ----------------------------------------------------------- device arm
 
 
+COMPONENTS = {"rollout_step": rollout_component, "layered_targets": targets_component,
+              "model_linear": model_linear_component, "model_attention": model_attention_component,
+              "preflop_forward": preflop_forward_component, "postflop_forward": postflop_forward_component,
+              "posterior_sampler": posterior_component, "loss_readout": readout_component,
+              "poker_loss": poker_loss_component, "optimizer_step": optimizer_component,
+              "showdown": showdown_component, "rb_completion": completion_component,
+              "learner_step_cfg1": learner_step_component, "learner_step_cfg2": learner_step_cfg2_component,
+              "reach_update": reach_component, "folded_statistics": folded_component,
+              "branched_sampling": branching_component, "rollout_with_model": rollout_with_model_component}
+
+
 def main():
     args = parse()
     if args.engine_arm:
@@ -1614,6 +1792,9 @@ def main():
     if args.profile_forward == "attention":
         profile_attention(device)
         return
+    if args.component:  # one component's entry, printed alone
+        print(json.dumps({args.component: COMPONENTS[args.component](device)}), flush=True)
+        return
     if args.profile_forward:
         global PROFILE_ONE_FORWARD
         PROFILE_ONE_FORWARD = True
@@ -1621,7 +1802,8 @@ def main():
                 "readout": "readout_component", "reach": "reach_component", "showdown": "showdown_component",
                 "optimizer": "optimizer_component", "poker_loss": "poker_loss_component",
                 "rollout_with_model": "rollout_with_model_component", "completion": "completion_component",
-                "rollout": "rollout_component", "learner_step": "learner_step_component"}.get(
+                "rollout": "rollout_component", "learner_step": "learner_step_component",
+                "learner_step_cfg2": "learner_step_cfg2_component"}.get(
             args.profile_forward, f"{args.profile_forward}_forward_component")
         if name == "rollout_with_model_component":
             rollout_with_model_component(device, hands=args.profile_hands)
@@ -1872,23 +2054,7 @@ def main():
     if rank == 0:
         line["components"] = {}
         if world == 1:  # single-GPU kernels of the path, measured once, outside the scaling runs
-            line["components"] = {"rollout_step": rollout_component(device),
-                                  "layered_targets": targets_component(device),
-                                  "model_linear": model_linear_component(device),
-                                  "model_attention": model_attention_component(device),
-                                  "preflop_forward": preflop_forward_component(device),
-                                  "postflop_forward": postflop_forward_component(device),
-                                  "posterior_sampler": posterior_component(device),
-                                  "loss_readout": readout_component(device),
-                                  "poker_loss": poker_loss_component(device),
-                                  "optimizer_step": optimizer_component(device),
-                                  "showdown": showdown_component(device),
-                                  "rb_completion": completion_component(device),
-                                  "learner_step_cfg1": learner_step_component(device),
-                                  "reach_update": reach_component(device),
-                                  "folded_statistics": folded_component(device),
-                                  "branched_sampling": branching_component(device),
-                                  "rollout_with_model": rollout_with_model_component(device)}
+            line["components"] = {name: fn(device) for name, fn in COMPONENTS.items()}
         if allreduce is not None:
             line["components"]["gradient_sum"] = allreduce
     if rank == 0 and world == 1 and _reference_pbg() is not None:

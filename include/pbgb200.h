@@ -687,6 +687,42 @@ int64_t pbg_mlp_bias_partials(int64_t M, int32_t N);
 int pbg_mlp_relu_backward_bias(int64_t M, int32_t N, float *dy, const float *y, float *dbias,
                                float *partial, int64_t partial_len, void *stream);
 
+/* ---- policy/value network backward (pbg/core/training.py:381-403 autograd
+ * through pbg/games/poker/model/primitives.py FFN / MHA and tensor_ops.py
+ * LayerNorm): the element-wise and row-wise steps between the library GEMMs.
+ */
+
+/* out[m, c] = dy[m, c] * GELU'(pre[m, c]) (exact erf GELU), bf16 out; pre f32,
+ * dy bf16 (dy_bf16 = 1) or f32; row strides in elements. */
+int pbg_gelu_backward(int64_t M, int32_t N, const float *pre, int64_t ldp, const void *dy, int32_t dy_bf16,
+                      int64_t ldd, void *out, int64_t ldo, void *stream);
+
+/* Floats of scratch pbg_layernorm_backward needs for `rows` rows of width d
+ * (-1 for a width it does not take: d a multiple of 32 up to 512). */
+int64_t pbg_layernorm_backward_partials(int64_t rows, int32_t d);
+
+/* Backward of y = (x - mean) / sqrt(var + eps) * gain + bias over rows of
+ * width d: dx (f32 or bf16) from x (f32 or bf16), gain (NULL = 1) and dy, and
+ * partial [blocks, 2d]: each block's column sums of dy * xhat (first d) and dy
+ * (next d), rows in a fixed order; the gain / bias gradients are the sums of
+ * the partial rows. */
+int pbg_layernorm_backward(int64_t rows, int32_t d, const void *x, int32_t x_bf16, int64_t ldx, const float *gain,
+                           float eps, const void *dy, int32_t dy_bf16, int64_t ldy, void *dx, int32_t dx_bf16,
+                           int64_t lddx, float *partial, int64_t partial_len, void *stream);
+
+/* The softmax part of the attention backward for rows = sequences x heads x
+ * len score rows (row r: sequence r / (heads len), head (r / len) % heads):
+ * score f32 [rows, len] raw content scores q.k, dprob f32 [rows, len] = dO V^T,
+ * key_bias f32 [sequences, len] (NULL = 0), key_mask u8 [sequences, len]
+ * (NULL = all present), q_scale f32 [heads].  Writes prob bf16 [rows, len] =
+ * softmax(score * q_scale + key_bias) over present keys (0 for absent keys and
+ * for a row without keys), dlogit bf16 [rows, len] = prob * (dprob - sum(prob
+ * dprob)) * q_scale, and scale_partial f32 [rows] = sum over the row of
+ * prob * (dprob - sum(prob dprob)) * score. */
+int pbg_attention_softmax_backward(int64_t rows, int32_t len, int32_t heads, const float *score, const float *dprob,
+                                   const float *key_bias, const uint8_t *key_mask, const float *q_scale, void *prob,
+                                   void *dlogit, float *scale_partial, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -521,6 +521,37 @@ def gen_posterior(out):
     out["cases"] = np.array(len(cases))
 
 
+def _gradient_sketch(out, modules, outputs):
+    """The reference's own autograd gradient of a seeded loss sum_f <c_f, output_f> (c_f ~ N(0, 1),
+    recorded as gcoef_<field>) with respect to every parameter of ``modules``, sketched per parameter
+    by its norm (gsk_norm) and its projections onto model_params.probe's vectors (gsk_proj)."""
+
+    import torch
+
+    import model_params
+
+    g = torch.Generator().manual_seed(4242)
+    loss = 0.0
+    for name, value in outputs.items():
+        c = torch.randn(value.shape, generator=g)
+        out["gcoef_" + name] = _np(c)
+        loss = loss + (c * value).sum()
+    params = [(n, q) for m in modules for n, q in m.named_parameters()]
+    for _, q in params:
+        q.grad = None
+    loss.backward()
+    names, norms, projections = [], [], []
+    for n, q in params:
+        grad = torch.zeros_like(q) if q.grad is None else q.grad
+        flat = grad.detach().reshape(-1).double().numpy()
+        names.append(n)
+        norms.append(float(np.linalg.norm(flat)))
+        projections.append(model_params.probe(n, tuple(q.shape)) @ flat)
+    out["gsk_names"] = np.array(names)
+    out["gsk_norm"] = np.array(norms)
+    out["gsk_proj"] = np.stack(projections)
+
+
 def gen_preflop_model(out, config=None, ranks=None, batch=3, tokens=8):
     """preflop.py:472-693 (PreflopEncoder.forward) with shared.py's trunk and readout, fp32 on CPU.
 
@@ -630,6 +661,8 @@ def gen_preflop_model(out, config=None, ranks=None, batch=3, tokens=8):
     out["class_sizes"] = _np(encoder.class_sizes)
     out["class_card_geometry"] = _np(encoder.class_card_geometry)
     out["class_overlap_scalars"] = _np(encoder.class_overlap_scalars)
+    result = encoder(shared, pub, ranges, None, masks)
+    _gradient_sketch(out, (shared, encoder), {**result.raw, "value": result.v})
 
 
 def gen_postflop_model(out, config=None, ranks=None):
@@ -756,6 +789,8 @@ def gen_postflop_model(out, config=None, ranks=None):
         for name, param in module.named_parameters():
             spec.append(name + ":" + ",".join(str(n) for n in param.shape))
     out["param_spec"] = np.array(spec)
+    result = encoder(shared, pub, ranges, None, masks)
+    _gradient_sketch(out, (shared, encoder), {**result.raw, "value": result.v})
 
 
 FOLDED_CASES = (
@@ -943,6 +978,7 @@ def gen_queued_model(out):
             kind = "pre" if street == 0 else f"post_{live}"
             groups.setdefault(kind, []).append((sub, sub_hist, i))
     out["partitions"] = np.array(sorted(groups))
+    learner_outputs: dict = {}
     for kind, items in sorted(groups.items()):
         items = items[:: max(1, len(items) // 12)][:12]
         st = hooks.PokerState(*(torch.stack([getattr(s, n)[i] for s, _, i in items]) for n in STATE_FIELDS))
@@ -980,6 +1016,12 @@ def gen_queued_model(out):
         for name, value in learner.policy_raw.items():
             out[tag + "_lraw_" + name] = _np(value)
         out[tag + "_lvalue"] = _np(learner.value)
+        learner = model.learner_operation(kind, rows_in, private, owner)  # with autograd, for the sketch
+        learner_outputs.update({f"{kind}__{name}": value for name, value in learner.policy_raw.items()})
+        learner_outputs[f"{kind}__value"] = learner.value
+    # one seeded loss over the learner rows of every partition: the shared parameters collect the
+    # gradient of both networks
+    _gradient_sketch(out, (model,), learner_outputs)
     spec = [name + ":" + ",".join(str(x) for x in param.shape) for name, param in model.named_parameters()]
     out["param_spec"] = np.array(spec)
     out["config"] = np.array([cfg.max_history_tokens, cfg.max_players])

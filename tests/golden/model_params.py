@@ -40,3 +40,15 @@ def parameter(name: str, shape: tuple[int, ...]) -> np.ndarray:
 
 # the postflop run has three seats (one folded), so the table holds up to three players
 POSTFLOP_CONFIG = dict(CONFIG, max_players=3)
+
+
+SKETCH_PROBES = 4
+
+
+def probe(name: str, shape: tuple[int, ...]) -> np.ndarray:
+    """Seeded N(0, I) probe vectors [SKETCH_PROBES, numel] of a parameter (float64): the projections of
+    its gradient onto them sketch the gradient (each projection's error is about the norm of the
+    gradient's error)."""
+
+    rng = np.random.default_rng(zlib.crc32(("probe:" + name).encode()))
+    return rng.standard_normal((SKETCH_PROBES, int(np.prod(shape))))
