@@ -157,6 +157,7 @@ struct AttnArgs {
     const uint8_t* key_mask;   // [batch, len] (nonzero = key present) or null
     const float* q_scale;      // [heads]: 1 / (temperature_h * sqrt(32))
     __nv_bfloat16* out;        // [batch, len, heads * 32]
+    float* lse;                // [batch, heads, len] base-2 log-sum-exp of each row's logits (+inf: no key), or null
     uint32_t* error;
 };
 
@@ -341,6 +342,7 @@ __global__ void __launch_bounds__(AttnPlan<T>::threads, 1) attention_kernel(Attn
             const int q = (qg * T + tile) * AT_BLOCK + r;
             if (q < A.len) {
                 const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                if (A.lse) A.lse[((int64_t)b * A.heads + h) * A.len + q] = l > 0.0f ? shift + log2f(l) : INFINITY;
                 uint32_t packed[16];
 #pragma unroll
                 for (int j = 0; j < AT_DH; j += 2) {
@@ -480,9 +482,19 @@ static int launch_attention(const AttnArgs& A, int64_t grid, cudaStream_t stream
 
 using namespace pbg;
 
+extern "C" int pbg_attention_bf16_lse(int32_t batch, int32_t len, int32_t heads, const void* qkv,
+                                      const float* key_bias, const uint8_t* key_mask, const float* q_scale, void* out,
+                                      float* lse, uint32_t* error, void* stream);
+
 extern "C" int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, const void* qkv, const float* key_bias,
                                   const uint8_t* key_mask, const float* q_scale, void* out, uint32_t* error,
                                   void* stream) {
+    return pbg_attention_bf16_lse(batch, len, heads, qkv, key_bias, key_mask, q_scale, out, nullptr, error, stream);
+}
+
+extern "C" int pbg_attention_bf16_lse(int32_t batch, int32_t len, int32_t heads, const void* qkv,
+                                      const float* key_bias, const uint8_t* key_mask, const float* q_scale, void* out,
+                                      float* lse, uint32_t* error, void* stream) {
     PBG_REQUIRE(batch >= 0 && len >= 0 && heads >= 1, "attention: bad shape");
     PBG_REQUIRE(qkv && q_scale && out && error, "attention: null pointer");
     PBG_REQUIRE(((uintptr_t)qkv % 16) == 0 && ((uintptr_t)out % 16) == 0, "attention: qkv and out must be 16-byte aligned");
@@ -504,6 +516,7 @@ extern "C" int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, con
     A.key_mask = key_mask;
     A.q_scale = q_scale;
     A.out = static_cast<__nv_bfloat16*>(out);
+    A.lse = lse;
     A.error = error;
     const int64_t grid = (int64_t)batch * heads * A.qgroups;
     PBG_REQUIRE(grid <= INT32_MAX, "attention: too many blocks");

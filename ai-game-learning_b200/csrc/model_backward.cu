@@ -1,9 +1,9 @@
 // The element-wise and row-wise parts of the policy/value network's backward
 // (pbg/games/poker/model/primitives.py FFN and MHA, pbg/core/tensor_ops.py
 // LayerNorm, as differentiated by torch autograd in the reference's learner
-// step, pbg/core/training.py:381-403).  The dense products of the backward
-// (dX = dY W, dW = dY^T X, and the four attention products) are library
-// GEMMs; these kernels sit between them.
+// step, pbg/core/training.py:381-403).  The dense maps' products (dX = dY W,
+// dW = dY^T X) are library GEMMs; these kernels sit between them, and the
+// attention backward is one fused pass of its own.
 //
 //   gelu_backward      dpre = dy * (Phi(pre) + pre * phi(pre)) for the exact
 //                      (erf) GELU, bf16 out: the operand of the map's dX / dW
@@ -12,15 +12,9 @@
 //                      dx = inv * (g dy - mean(g dy) - xhat mean(g dy xhat)),
 //                      and per-block column sums of dy * xhat (gain) and dy
 //                      (bias) in a fixed order (the host adds the blocks' rows)
-//   attention_softmax_backward
-//                      one CTA per score row (sequence, head, query): from the
-//                      raw content scores q.k and dP = dO V^T it recomputes the
-//                      row's softmax of s * scale_h + key_bias (absent keys
-//                      excluded; a row without keys is all zeros), writes P
-//                      (bf16, for dV = P^T dO), the logit gradient
-//                      dZ = P (dP - sum(P dP)) times scale_h (bf16, for
-//                      dQ = dZ K and dK = dZ^T Q), and the row's sum of
-//                      dZ * s (the gradient of the head's score scale)
+//   attention backward (fused, below): dQ, dK, dV and the score-scale
+//                      gradient from the forward's log-sum-exp, the scores
+//                      recomputed tile by tile on the tensor cores
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -33,7 +27,6 @@ namespace {
 constexpr int GB_THREADS = 256;
 constexpr int LNB_WARPS = 8;
 constexpr int LNB_MAX_PER_LANE = 16;  // d <= 512
-constexpr int ASB_THREADS = 256;
 
 __device__ __forceinline__ float load_f(const float* p) { return *p; }
 __device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
@@ -124,79 +117,304 @@ layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t
     }
 }
 
-template <bool MAX>
-__device__ __forceinline__ float block_reduce(float v, float* scratch) {
-    #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float u = __shfl_xor_sync(0xffffffffu, v, o);
-        v = MAX ? fmaxf(v, u) : v + u;
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();  // the previous reduction's readers are done with scratch
-    if (lane == 0) scratch[warp] = v;
-    __syncthreads();
-    float t = scratch[0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = MAX ? fmaxf(t, scratch[w]) : t + scratch[w];
-    return t;
+// ---------------------------------------------------------------- fused attention backward
+// FlashAttention-style: the scores never leave the chip.  With the forward's base-2 log-sum-exp
+// lse2 of every (sequence, head, query) row and delta = sum_d dO O of the row, for a query/key tile
+// pair: z2 = s * scale_h * log2(e) + bias * log2(e) (absent key: -inf), P = 2^(z2 - lse2),
+// dP = dO V^T, dZ = P (dP - delta) (the logit gradient), and with dS = dZ * scale_h:
+// dQ = dS K, dK = dS^T Q, dV = P^T dO; the head's scale gradient sums dZ * s.  Two kernels, no
+// atomics: one CTA per 64-query block computes dQ (looping over key blocks), one per 64-key block
+// dK and dV (looping over query blocks).  Each of the 4 warps owns 16 rows; the products run on
+// mma.sync m16n8k16 (bf16 operands, fp32 accumulation) with operand tiles staged in shared memory
+// row-major (stride 40 elements) and, for the products that contract over rows, transposed
+// (stride 72); both strides make every fragment read bank-conflict free.
+constexpr int AB_TILE = 64;
+constexpr int AB_LD = 40;
+constexpr int AB_LDT = 72;
+constexpr float AB_LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ void ab_mma(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(ASB_THREADS)
-attention_softmax_backward_kernel(int64_t rows, int L, int heads, const float* __restrict__ score,
-                                  const float* __restrict__ dprob, const float* __restrict__ key_bias,
-                                  const uint8_t* __restrict__ key_mask, const float* __restrict__ q_scale,
-                                  __nv_bfloat16* __restrict__ prob, __nv_bfloat16* __restrict__ dlogit,
-                                  float* __restrict__ scale_partial) {
-    __shared__ float scratch[ASB_THREADS / 32];
-    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-        const int64_t bh = r / L;
-        const int64_t b = bh / heads;
-        const int h = (int)(bh - b * heads);
-        const float scale = q_scale[h];
-        const float* s = score + r * (int64_t)L;
-        const float* dp = dprob + r * (int64_t)L;
-        const float* bias = key_bias ? key_bias + b * (int64_t)L : nullptr;
-        const uint8_t* mask = key_mask ? key_mask + b * (int64_t)L : nullptr;
-        __nv_bfloat16* pr = prob + r * (int64_t)L;
-        __nv_bfloat16* dz = dlogit + r * (int64_t)L;
-        float top = -INFINITY;
-        for (int j = threadIdx.x; j < L; j += blockDim.x) {
-            if (mask && !mask[j]) continue;
-            const float z = s[j] * scale + (bias ? bias[j] : 0.0f);
-            top = fmaxf(top, z);
+__device__ __forceinline__ uint32_t ab_pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float ab_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t ab_ld32(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// A fragments (two k-steps of 16 columns) of a warp's 16 rows x 32 columns of a row-major bf16
+// matrix in global memory (rows at or past `rows` read as zero)
+__device__ __forceinline__ void ab_rows_a(const __nv_bfloat16* base, int64_t ld, int row0, int rows, int g, int t,
+                                          uint32_t a[2][4]) {
+    const bool v0 = row0 + g < rows, v1 = row0 + g + 8 < rows;
+    const __nv_bfloat16* r0 = base + (int64_t)(row0 + g) * ld;
+    const __nv_bfloat16* r1 = base + (int64_t)(row0 + g + 8) * ld;
+#pragma unroll
+    for (int kt = 0; kt < 2; ++kt) {
+        a[kt][0] = v0 ? ab_ld32(r0 + 16 * kt + 2 * t) : 0u;
+        a[kt][1] = v1 ? ab_ld32(r1 + 16 * kt + 2 * t) : 0u;
+        a[kt][2] = v0 ? ab_ld32(r0 + 16 * kt + 2 * t + 8) : 0u;
+        a[kt][3] = v1 ? ab_ld32(r1 + 16 * kt + 2 * t + 8) : 0u;
+    }
+}
+
+// stage 64 rows x 32 columns (row r of the tile at base + (row0 + r) * ld) into `tile` (row-major,
+// stride AB_LD) and, when `trans` is given, its transpose (stride AB_LDT); absent rows are zero
+__device__ __forceinline__ void ab_stage(const __nv_bfloat16* base, int64_t ld, int row0, int rows,
+                                         __nv_bfloat16* tile, __nv_bfloat16* trans) {
+    const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
+    uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
+    if (row0 + r < rows) {
+        const uint4* src = reinterpret_cast<const uint4*>(base + (int64_t)(row0 + r) * ld + 16 * half);
+        v0 = src[0];
+        v1 = src[1];
+    }
+    uint4* dst = reinterpret_cast<uint4*>(tile + r * AB_LD + 16 * half);
+    dst[0] = v0;
+    dst[1] = v1;
+    if (trans) {
+        const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&v0);
+        const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&v1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            trans[(16 * half + e) * AB_LDT + r] = e0[e];
+            trans[(16 * half + 8 + e) * AB_LDT + r] = e1[e];
         }
-        top = block_reduce<true>(top, scratch);
-        if (top == -INFINITY) {  // no key: the forward's row is zero, so is every gradient
-            for (int j = threadIdx.x; j < L; j += blockDim.x) {
-                pr[j] = __float2bfloat16_rn(0.0f);
-                dz[j] = __float2bfloat16_rn(0.0f);
+    }
+}
+
+__device__ __forceinline__ float ab_key_term(const float* bias, const uint8_t* mask, int64_t at, bool present) {
+    if (!present || (mask && !mask[at])) return -INFINITY;
+    return bias ? bias[at] * AB_LOG2E : 0.0f;
+}
+
+struct AttnBackArgs {
+    int batch, len, heads;
+    const __nv_bfloat16* qkv;   // [batch, len, 3 * heads * 32]
+    const __nv_bfloat16* dout;  // [batch, len, heads * 32]
+    const float* lse;           // [batch, heads, len] base 2
+    const float* delta;         // [batch, heads, len]
+    const float* key_bias;      // [batch, len] or null
+    const uint8_t* key_mask;    // [batch, len] or null
+    const float* q_scale;       // [heads]
+    __nv_bfloat16* dqkv;        // [batch, len, 3 * heads * 32]
+    float* scale_partial;       // [batch, heads, len]
+};
+
+__global__ void __launch_bounds__(128) attention_delta_kernel(int64_t rows, int heads, const __nv_bfloat16* out,
+                                                              const __nv_bfloat16* dout, int len, float* delta) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows; i += (int64_t)gridDim.x * blockDim.x) {
+        // i = (b * len + q) * heads + h
+        const int h = (int)(i % heads);
+        const int64_t bq = i / heads;
+        const uint4* o = reinterpret_cast<const uint4*>(out + i * 32);
+        const uint4* g = reinterpret_cast<const uint4*>(dout + i * 32);
+        float acc = 0.0f;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const uint4 a = o[v], c = g[v];
+            const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+            const __nv_bfloat162* pc = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 fa = __bfloat1622float2(pa[e]), fc = __bfloat1622float2(pc[e]);
+                acc += fa.x * fc.x + fa.y * fc.y;
             }
-            if (threadIdx.x == 0) scale_partial[r] = 0.0f;
-            continue;
         }
-        float total = 0.0f;
-        for (int j = threadIdx.x; j < L; j += blockDim.x) {
-            if (mask && !mask[j]) continue;
-            total += expf(s[j] * scale + (bias ? bias[j] : 0.0f) - top);
+        const int64_t b = bq / len, q = bq - b * len;
+        delta[(b * heads + h) * len + q] = acc;
+    }
+}
+
+__global__ void __launch_bounds__(128) attention_dq_kernel(AttnBackArgs A) {
+    __shared__ __align__(16) __nv_bfloat16 ks[AB_TILE * AB_LD], vs[AB_TILE * AB_LD], kt[32 * AB_LDT];
+    __shared__ float kterm[AB_TILE];
+    const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    const int qb = blockIdx.x % qblocks;
+    const int h = (blockIdx.x / qblocks) % A.heads;
+    const int b = blockIdx.x / (qblocks * A.heads);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int d = A.heads * 32, width = 3 * d;
+    const int q0 = qb * AB_TILE + 16 * warp;
+    const float scale = A.q_scale[h], scale2 = scale * AB_LOG2E;
+    const __nv_bfloat16* seq = A.qkv + (int64_t)b * A.len * width + h * 32;
+    uint32_t qa[2][4], da[2][4];
+    ab_rows_a(seq, width, q0, A.len, g, t, qa);
+    ab_rows_a(A.dout + (int64_t)b * A.len * d + h * 32, d, q0, A.len, g, t, da);
+    const int64_t row_base = ((int64_t)b * A.heads + h) * A.len;
+    const bool v0 = q0 + g < A.len, v1 = q0 + g + 8 < A.len;
+    const float lse0 = v0 ? A.lse[row_base + q0 + g] : INFINITY, lse1 = v1 ? A.lse[row_base + q0 + g + 8] : INFINITY;
+    const float dl0 = v0 ? A.delta[row_base + q0 + g] : 0.0f, dl1 = v1 ? A.delta[row_base + q0 + g + 8] : 0.0f;
+    float dq[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.0f;
+    float th0 = 0.0f, th1 = 0.0f;
+    const int kblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    for (int kb = 0; kb < kblocks; ++kb) {
+        const int k0 = kb * AB_TILE;
+        __syncthreads();  // the previous block's tiles are consumed
+        ab_stage(seq + d, width, k0, A.len, ks, kt);
+        ab_stage(seq + 2 * d, width, k0, A.len, vs, nullptr);
+        if (threadIdx.x < AB_TILE)
+            kterm[threadIdx.x] = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k0 + threadIdx.x,
+                                             k0 + (int)threadIdx.x < A.len);
+        __syncthreads();
+        float s[8][4], dp[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+            dp[nt][0] = dp[nt][1] = dp[nt][2] = dp[nt][3] = 0.0f;
+            const __nv_bfloat16* kr = ks + (8 * nt + g) * AB_LD + 2 * t;
+            const __nv_bfloat16* vr = vs + (8 * nt + g) * AB_LD + 2 * t;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                ab_mma(s[nt], qa[k], ab_ld32(kr + 16 * k), ab_ld32(kr + 16 * k + 8));
+                ab_mma(dp[nt], da[k], ab_ld32(vr + 16 * k), ab_ld32(vr + 16 * k + 8));
+            }
         }
-        const float inv_total = 1.0f / block_reduce<false>(total, scratch);
-        float dot = 0.0f;
-        for (int j = threadIdx.x; j < L; j += blockDim.x) {
-            float p = 0.0f;
-            if (!mask || mask[j]) p = expf(s[j] * scale + (bias ? bias[j] : 0.0f) - top) * inv_total;
-            pr[j] = __float2bfloat16_rn(p);
-            dot += p * dp[j];
+        uint32_t dsa[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const float t0 = kterm[8 * nt + 2 * t], t1 = kterm[8 * nt + 2 * t + 1];
+            const float p0 = ab_exp2(fmaf(s[nt][0], scale2, t0) - lse0), p1 = ab_exp2(fmaf(s[nt][1], scale2, t1) - lse0);
+            const float p2 = ab_exp2(fmaf(s[nt][2], scale2, t0) - lse1), p3 = ab_exp2(fmaf(s[nt][3], scale2, t1) - lse1);
+            const float z0 = p0 * (dp[nt][0] - dl0), z1 = p1 * (dp[nt][1] - dl0);
+            const float z2 = p2 * (dp[nt][2] - dl1), z3 = p3 * (dp[nt][3] - dl1);
+            th0 += z0 * s[nt][0] + z1 * s[nt][1];
+            th1 += z2 * s[nt][2] + z3 * s[nt][3];
+            // C fragment of n-tile nt -> half of the A fragment of key step nt / 2
+            dsa[nt >> 1][(nt & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
+            dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
         }
-        dot = block_reduce<false>(dot, scratch);
-        float ds = 0.0f;
-        for (int j = threadIdx.x; j < L; j += blockDim.x) {
-            float g = 0.0f;
-            const float raw = s[j];
-            if (!mask || mask[j]) g = expf(raw * scale + (bias ? bias[j] : 0.0f) - top) * inv_total * (dp[j] - dot);
-            dz[j] = __float2bfloat16_rn(g * scale);
-            ds += g * raw;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const __nv_bfloat16* col = kt + (8 * nt + g) * AB_LDT + 16 * kk + 2 * t;
+                ab_mma(dq[nt], dsa[kk], ab_ld32(col), ab_ld32(col + 8));
+            }
         }
-        ds = block_reduce<false>(ds, scratch);
-        if (threadIdx.x == 0) scale_partial[r] = ds;
+    }
+    th0 += __shfl_xor_sync(0xffffffffu, th0, 1);
+    th0 += __shfl_xor_sync(0xffffffffu, th0, 2);
+    th1 += __shfl_xor_sync(0xffffffffu, th1, 1);
+    th1 += __shfl_xor_sync(0xffffffffu, th1, 2);
+    __nv_bfloat16* out = A.dqkv + (int64_t)b * A.len * width + h * 32;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+        if (v0) *reinterpret_cast<uint32_t*>(out + (int64_t)(q0 + g) * width + 8 * nt + 2 * t) = ab_pack(dq[nt][0], dq[nt][1]);
+        if (v1)
+            *reinterpret_cast<uint32_t*>(out + (int64_t)(q0 + g + 8) * width + 8 * nt + 2 * t) = ab_pack(dq[nt][2], dq[nt][3]);
+    }
+    if (t == 0) {
+        if (v0) A.scale_partial[row_base + q0 + g] = th0;
+        if (v1) A.scale_partial[row_base + q0 + g + 8] = th1;
+    }
+}
+
+__global__ void __launch_bounds__(128) attention_dkv_kernel(AttnBackArgs A) {
+    __shared__ __align__(16) __nv_bfloat16 qs[AB_TILE * AB_LD], gs[AB_TILE * AB_LD], qt[32 * AB_LDT],
+        gt[32 * AB_LDT];
+    __shared__ float lse_s[AB_TILE], delta_s[AB_TILE];
+    const int kblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    const int kb = blockIdx.x % kblocks;
+    const int h = (blockIdx.x / kblocks) % A.heads;
+    const int b = blockIdx.x / (kblocks * A.heads);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int d = A.heads * 32, width = 3 * d;
+    const int k0 = kb * AB_TILE + 16 * warp;
+    const float scale = A.q_scale[h], scale2 = scale * AB_LOG2E;
+    const __nv_bfloat16* seq = A.qkv + (int64_t)b * A.len * width + h * 32;
+    const __nv_bfloat16* grad = A.dout + (int64_t)b * A.len * d + h * 32;
+    uint32_t ka[2][4], va[2][4];
+    ab_rows_a(seq + d, width, k0, A.len, g, t, ka);
+    ab_rows_a(seq + 2 * d, width, k0, A.len, g, t, va);
+    const float kt0 = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k0 + g, k0 + g < A.len);
+    const float kt1 = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k0 + g + 8, k0 + g + 8 < A.len);
+    const int64_t row_base = ((int64_t)b * A.heads + h) * A.len;
+    float dk[4][4], dv[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        dk[i][0] = dk[i][1] = dk[i][2] = dk[i][3] = 0.0f;
+        dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.0f;
+    }
+    const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    for (int qb = 0; qb < qblocks; ++qb) {
+        const int q0 = qb * AB_TILE;
+        __syncthreads();
+        ab_stage(seq, width, q0, A.len, qs, qt);
+        ab_stage(grad, d, q0, A.len, gs, gt);
+        if (threadIdx.x < AB_TILE) {
+            const bool v = q0 + (int)threadIdx.x < A.len;
+            lse_s[threadIdx.x] = v ? A.lse[row_base + q0 + threadIdx.x] : INFINITY;
+            delta_s[threadIdx.x] = v ? A.delta[row_base + q0 + threadIdx.x] : 0.0f;
+        }
+        __syncthreads();
+        float s[8][4], dp[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+            dp[nt][0] = dp[nt][1] = dp[nt][2] = dp[nt][3] = 0.0f;
+            const __nv_bfloat16* qr = qs + (8 * nt + g) * AB_LD + 2 * t;
+            const __nv_bfloat16* gr = gs + (8 * nt + g) * AB_LD + 2 * t;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                ab_mma(s[nt], ka[k], ab_ld32(qr + 16 * k), ab_ld32(qr + 16 * k + 8));
+                ab_mma(dp[nt], va[k], ab_ld32(gr + 16 * k), ab_ld32(gr + 16 * k + 8));
+            }
+        }
+        uint32_t pa[4][4], dsa[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int c = 8 * nt + 2 * t;
+            const float l0 = lse_s[c], l1 = lse_s[c + 1], e0 = delta_s[c], e1 = delta_s[c + 1];
+            // rows: keys g (regs 0, 1) and g + 8 (regs 2, 3); columns: queries c, c + 1
+            const float p0 = ab_exp2(fmaf(s[nt][0], scale2, kt0) - l0), p1 = ab_exp2(fmaf(s[nt][1], scale2, kt0) - l1);
+            const float p2 = ab_exp2(fmaf(s[nt][2], scale2, kt1) - l0), p3 = ab_exp2(fmaf(s[nt][3], scale2, kt1) - l1);
+            const float z0 = p0 * (dp[nt][0] - e0), z1 = p1 * (dp[nt][1] - e1);
+            const float z2 = p2 * (dp[nt][2] - e0), z3 = p3 * (dp[nt][3] - e1);
+            pa[nt >> 1][(nt & 1) * 2] = ab_pack(p0, p1);
+            pa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(p2, p3);
+            dsa[nt >> 1][(nt & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
+            dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const __nv_bfloat16* gc = gt + (8 * nt + g) * AB_LDT + 16 * kk + 2 * t;
+                const __nv_bfloat16* qc = qt + (8 * nt + g) * AB_LDT + 16 * kk + 2 * t;
+                ab_mma(dv[nt], pa[kk], ab_ld32(gc), ab_ld32(gc + 8));
+                ab_mma(dk[nt], dsa[kk], ab_ld32(qc), ab_ld32(qc + 8));
+            }
+        }
+    }
+    __nv_bfloat16* out = A.dqkv + (int64_t)b * A.len * width + h * 32;
+    const bool v0 = k0 + g < A.len, v1 = k0 + g + 8 < A.len;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+        const int col = 8 * nt + 2 * t;
+        if (v0) {
+            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g) * width + d + col) = ab_pack(dk[nt][0], dk[nt][1]);
+            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g) * width + 2 * d + col) = ab_pack(dv[nt][0], dv[nt][1]);
+        }
+        if (v1) {
+            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g + 8) * width + d + col) = ab_pack(dk[nt][2], dk[nt][3]);
+            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g + 8) * width + 2 * d + col) =
+                ab_pack(dv[nt][2], dv[nt][3]);
+        }
     }
 }
 
@@ -266,20 +484,41 @@ int pbg_layernorm_backward(int64_t rows, int32_t d, const void* x, int32_t x_bf1
     return launch_status("layernorm_backward");
 }
 
-int pbg_attention_softmax_backward(int64_t rows, int32_t len, int32_t heads, const float* score, const float* dprob,
-                                   const float* key_bias, const uint8_t* key_mask, const float* q_scale, void* prob,
-                                   void* dlogit, float* scale_partial, void* stream) {
-    PBG_REQUIRE(rows >= 0 && len >= 1 && heads >= 1 && rows % ((int64_t)len * heads) == 0,
-                "attention_softmax_backward: rows must be sequences x heads x length");
-    PBG_REQUIRE(score && dprob && q_scale && prob && dlogit && scale_partial,
-                "attention_softmax_backward: null argument");
-    if (rows == 0) return PBG_OK;
-    const int64_t cap = 16 * (int64_t)sm_count();
-    const int grid = (int)(rows < cap ? rows : cap);
-    attention_softmax_backward_kernel<<<grid, ASB_THREADS, 0, as_stream(stream)>>>(
-        rows, len, heads, score, dprob, key_bias, key_mask, q_scale,
-        static_cast<__nv_bfloat16*>(prob), static_cast<__nv_bfloat16*>(dlogit), scale_partial);
-    return launch_status("attention_softmax_backward");
+int pbg_attention_backward(int32_t batch, int32_t len, int32_t heads, const void* qkv, const void* out,
+                           const void* dout, const float* lse, const float* key_bias, const uint8_t* key_mask,
+                           const float* q_scale, void* dqkv, float* delta, float* scale_partial, void* stream) {
+    PBG_REQUIRE(batch >= 0 && len >= 0 && heads >= 1, "attention_backward: bad shape");
+    PBG_REQUIRE(qkv && out && dout && lse && q_scale && dqkv && delta && scale_partial,
+                "attention_backward: null argument");
+    PBG_REQUIRE(((uintptr_t)qkv | (uintptr_t)out | (uintptr_t)dout | (uintptr_t)dqkv) % 16 == 0,
+                "attention_backward: qkv, out, dout and dqkv must be 16-byte aligned");
+    if (batch == 0 || len == 0) return PBG_OK;
+    cudaStream_t s = as_stream(stream);
+    const int64_t rows = (int64_t)batch * len * heads;
+    attention_delta_kernel<<<stride_grid(rows, 128), 128, 0, s>>>(rows, heads, static_cast<const __nv_bfloat16*>(out),
+                                                                  static_cast<const __nv_bfloat16*>(dout), len, delta);
+    int err = launch_status("attention_backward: delta");
+    if (err) return err;
+    AttnBackArgs A;
+    A.batch = batch;
+    A.len = len;
+    A.heads = heads;
+    A.qkv = static_cast<const __nv_bfloat16*>(qkv);
+    A.dout = static_cast<const __nv_bfloat16*>(dout);
+    A.lse = lse;
+    A.delta = delta;
+    A.key_bias = key_bias;
+    A.key_mask = key_mask;
+    A.q_scale = q_scale;
+    A.dqkv = static_cast<__nv_bfloat16*>(dqkv);
+    A.scale_partial = scale_partial;
+    const int64_t grid = (int64_t)batch * heads * ((len + AB_TILE - 1) / AB_TILE);
+    PBG_REQUIRE(grid <= INT32_MAX, "attention_backward: too many blocks");
+    attention_dq_kernel<<<(unsigned)grid, 128, 0, s>>>(A);
+    err = launch_status("attention_backward: dq");
+    if (err) return err;
+    attention_dkv_kernel<<<(unsigned)grid, 128, 0, s>>>(A);
+    return launch_status("attention_backward: dk dv");
 }
 
 }  // extern "C"

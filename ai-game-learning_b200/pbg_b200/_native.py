@@ -106,7 +106,8 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_layernorm_backward_partials": (_I64, [_I64, _I32]),
     "pbg_layernorm_backward": (_I32, [_I64, _I32, _P, _I32, _I64, _P, ctypes.c_float, _P, _I32, _I64, _P, _I32, _I64, _P, _I64,
                                       _P]),
-    "pbg_attention_softmax_backward": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_attention_backward": (_I32, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "pbg_attention_bf16_lse": (_I32, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_policy_probabilities": (_I32, [_I64, _I32, Pol, _P, _P, _P]),
     "pbg_policy_selected_log_pi": (_I32, [_I64, _I32, Pol, _P, _P, _P, _P]),
     "pbg_policy_entropy": (_I32, [_I64, _I32, Pol, _P, _P, _P]),

@@ -121,13 +121,14 @@ class FFN:
 
 
 def attention(qkv: Tensor, heads: int, q_scale: Tensor, key_bias: Tensor | None = None,
-              key_mask: Tensor | None = None) -> Tensor:
+              key_mask: Tensor | None = None, lse: Tensor | None = None) -> Tensor:
     """Self-attention core of primitives.py MHA for heads of width 32 (pbg_attention_bf16).
 
     ``qkv`` bf16 ``[B, L, 3 * heads * 32]`` (the fused in-projection's output),
     ``q_scale`` fp32 ``[heads]`` = 1 / (temperature * sqrt(32)), ``key_bias``
     fp32 ``[B, L]``, ``key_mask`` bool ``[B, L]``.  Returns merged heads, bf16
-    ``[B, L, heads * 32]``.
+    ``[B, L, heads * 32]``; with ``lse`` (fp32 ``[B, heads, L]``) also each
+    row's base-2 log-sum-exp of its logits (the backward's input).
     """
 
     if qkv.dtype != torch.bfloat16 or qkv.ndim != 3 or qkv.shape[2] != 3 * heads * 32:
@@ -143,8 +144,15 @@ def attention(qkv: Tensor, heads: int, q_scale: Tensor, key_bias: Tensor | None 
         raise NativeError("q_scale must hold one value per head")
     out = torch.empty((batch, length, heads * 32), dtype=torch.bfloat16, device=qkv.device)
     mask = None if key_mask is None else key_mask.contiguous().view(torch.uint8)
-    call("pbg_attention_bf16", batch, length, heads, ptr(qkv), ptr(None if key_bias is None else key_bias.contiguous()),
-         ptr(mask), ptr(scale), ptr(out), ptr(_error_word(qkv.device)), stream(qkv.device))
+    bias = None if key_bias is None else key_bias.contiguous()
+    if lse is None:
+        call("pbg_attention_bf16", batch, length, heads, ptr(qkv), ptr(bias), ptr(mask), ptr(scale), ptr(out),
+             ptr(_error_word(qkv.device)), stream(qkv.device))
+        return out
+    if lse.dtype != torch.float32 or lse.shape != (batch, heads, length) or not lse.is_contiguous():
+        raise NativeError("lse must be contiguous float32 [B, heads, L]")
+    call("pbg_attention_bf16_lse", batch, length, heads, ptr(qkv), ptr(bias), ptr(mask), ptr(scale), ptr(out),
+         ptr(lse), ptr(_error_word(qkv.device)), stream(qkv.device))
     return out
 
 

@@ -12,11 +12,10 @@ wrapped in an autograd function whose backward is written for it:
   ``pbg_gelu_backward``, then dX = dY W and dW = dY^T X as bf16 library GEMMs
   with fp32 accumulation (fp32 dW), the bias and residual gradients as sums;
 - ``_LayerNormFn`` (``pbg_layernorm``): ``pbg_layernorm_backward``;
-- ``_AttentionFn`` (``pbg_attention_bf16``): per chunk of sequences the raw
-  scores Q K^T (fp32) and dP = dO V^T recomputed as batched GEMMs,
-  ``pbg_attention_softmax_backward`` for P and the logit gradient, then
-  dV = P^T dO, dQ = dZ K and dK = dZ^T Q, and the gradient of each head's score
-  scale (so of the temperature parameter theta).
+- ``_AttentionFn`` (``pbg_attention_bf16_lse``, which also keeps each row's
+  log-sum-exp): ``pbg_attention_backward``, one fused pass that recomputes the
+  scores tile by tile on the tensor cores and gives dQ, dK, dV and the gradient
+  of each head's score scale (so of the temperature parameter theta).
 
 The key bias and mask of the attention and the row mass of the incidence map
 come from the learner rows' ranges, not from parameters, and get no gradient.
@@ -38,8 +37,6 @@ from torch import Tensor
 from . import _native as N
 from ._native import NativeError, call, ptr, stream
 from .model import attention, linear_ex
-
-ATTENTION_CHUNK_BYTES = 4 << 30  # score-space working set of one attention-backward chunk
 
 
 def _f32(t: Tensor) -> Tensor:
@@ -145,51 +142,28 @@ def layernorm_train(x: Tensor, gain: Tensor, bias: Tensor, eps: float = 1e-5) ->
 class _AttentionFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, q_scale, key_bias, key_mask, heads):
-        out = attention(qkv, heads, q_scale, key_bias, key_mask)
-        ctx.save_for_backward(qkv, q_scale, key_bias, key_mask)
+        B, L, _ = qkv.shape
+        lse = torch.empty((B, heads, L), dtype=torch.float32, device=qkv.device)
+        out = attention(qkv, heads, q_scale, key_bias, key_mask, lse=lse)
+        ctx.save_for_backward(qkv, q_scale, key_bias, key_mask, out, lse)
         ctx.heads = heads
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        qkv, q_scale, key_bias, key_mask = ctx.saved_tensors
+        qkv, q_scale, key_bias, key_mask, out, lse = ctx.saved_tensors
         H = ctx.heads
         B, L, _ = qkv.shape
         dev = qkv.device
-        heads5 = qkv.view(B, L, 3, H, 32)
-        do5 = dout.to(torch.bfloat16).view(B, L, H, 32)
+        dout = dout.to(torch.bfloat16).contiguous()
         dqkv = torch.empty_like(qkv)
-        d5 = dqkv.view(B, L, 3, H, 32)
-        scale = q_scale.detach().float().contiguous()
+        delta = torch.empty((B, H, L), dtype=torch.float32, device=dev)
+        partial = torch.empty((B, H, L), dtype=torch.float32, device=dev)
         bias = None if key_bias is None else key_bias.float().contiguous()
         mask = None if key_mask is None else key_mask.contiguous().view(torch.uint8)
-        dscale = torch.zeros(H, dtype=torch.float32, device=dev)
-        per_sequence = 12 * H * L * L  # f32 scores and dP, bf16 P and dZ
-        chunk = max(1, min(B, ATTENTION_CHUNK_BYTES // max(per_sequence, 1)))
-        for b0 in range(0, B, chunk):
-            b1 = min(B, b0 + chunk)
-            c = b1 - b0
-            q = heads5[b0:b1, :, 0].permute(0, 2, 1, 3).reshape(c * H, L, 32)
-            k = heads5[b0:b1, :, 1].permute(0, 2, 1, 3).reshape(c * H, L, 32)
-            v = heads5[b0:b1, :, 2].permute(0, 2, 1, 3).reshape(c * H, L, 32)
-            do = do5[b0:b1].permute(0, 2, 1, 3).reshape(c * H, L, 32)
-            score = torch.bmm(q, k.transpose(1, 2), out_dtype=torch.float32)
-            dprob = torch.bmm(do, v.transpose(1, 2), out_dtype=torch.float32)
-            prob = torch.empty((c * H, L, L), dtype=torch.bfloat16, device=dev)
-            dlogit = torch.empty_like(prob)
-            partial = torch.empty(c * H * L, dtype=torch.float32, device=dev)
-            call("pbg_attention_softmax_backward", c * H * L, L, H, ptr(score), ptr(dprob),
-                 ptr(None if bias is None else bias[b0:b1]), ptr(None if mask is None else mask[b0:b1]), ptr(scale),
-                 ptr(prob), ptr(dlogit), ptr(partial), stream(dev))
-            del score, dprob
-            dv = torch.bmm(prob.transpose(1, 2), do)
-            dq = torch.bmm(dlogit, k)
-            dk = torch.bmm(dlogit.transpose(1, 2), q)
-            d5[b0:b1, :, 0] = dq.view(c, H, L, 32).permute(0, 2, 1, 3)
-            d5[b0:b1, :, 1] = dk.view(c, H, L, 32).permute(0, 2, 1, 3)
-            d5[b0:b1, :, 2] = dv.view(c, H, L, 32).permute(0, 2, 1, 3)
-            dscale += partial.view(c, H, L).sum((0, 2))
-        return dqkv, dscale.to(q_scale.dtype), None, None, None
+        call("pbg_attention_backward", B, L, H, ptr(qkv), ptr(out), ptr(dout), ptr(lse), ptr(bias), ptr(mask),
+             ptr(q_scale.detach().float().contiguous()), ptr(dqkv), ptr(delta), ptr(partial), stream(dev))
+        return dqkv, partial.sum((0, 2)).to(q_scale.dtype), None, None, None
 
 
 def attention_train(qkv: Tensor, heads: int, q_scale: Tensor, key_bias: Tensor | None,

@@ -26,7 +26,7 @@ from torch import Tensor
 from torch.nn import functional as F
 
 from .checks import _assert, input_errors, raise_input_errors
-from .preflop import FamilyModel, PolicyOutput, PreflopConfig, _affine_rows
+from .preflop import FamilyModel, PolicyOutput, PreflopConfig, _affine_rows, lookup
 
 
 @dataclass
@@ -173,7 +173,7 @@ class PostflopModel(FamilyModel):
         """postflop.py:348-350: rank + suit embedding of global card ids (padding clamps to card 0)."""
 
         safe = cards.clamp(0, 51).long()
-        return self.p["rank_embedding.weight"][safe // 4] + self.p["suit_embedding.weight"][safe % 4]
+        return lookup(self.p["rank_embedding.weight"], safe // 4) + lookup(self.p["suit_embedding.weight"], safe % 4)
 
     def _combo_embedding(self, ids: Tensor, supplied: Tensor | None) -> Tensor:
         """postflop.py:352-365."""
@@ -394,8 +394,8 @@ class PostflopModel(FamilyModel):
         scalars = torch.cat([g.float() for g in groups], 1)
         type_ids = torch.cat([torch.full((n,), k, dtype=torch.long, device=dev) for n, k in kinds])
         token = (scalars[..., None] * p["public_scalar_affine.weight"][:, 0] + p["public_scalar_affine.bias"]
-                 + p["public_type_embedding.weight"][type_ids])
-        seat_pos = p["seat_embedding.weight"][relative]
+                 + lookup(p["public_type_embedding.weight"], type_ids))
+        seat_pos = lookup(p["seat_embedding.weight"], relative)
         rest = scalars.shape[1] - 1 - 2 * players
         zeros = torch.zeros((batch, 1, d), device=dev)
         token = token + torch.cat((zeros, seat_pos, seat_pos, zeros.expand(-1, rest, -1)), 1)
@@ -414,11 +414,11 @@ class PostflopModel(FamilyModel):
             numeric = torch.stack([h[k].float() for k in ("amount", "pot_before", "call_amount", "current_bet",
                                                           "min_raise_to", "max_raise_to")], -1)
             ht = numeric @ p["history_numeric_affine.weight"].T + p["history_numeric_affine.bias"]
-            ht = ht + p["history_action_embedding.weight"][h["action"].clamp(0, 3).long()]
-            ht = ht + p["history_street_embedding.weight"][h["street"].clamp(0, 3).long()]
-            ht = ht + p["history_position_embedding.weight"][torch.arange(h["mask"].shape[1], device=dev)][None]
+            ht = ht + lookup(p["history_action_embedding.weight"], h["action"].clamp(0, 3).long())
+            ht = ht + lookup(p["history_street_embedding.weight"], h["street"].clamp(0, 3).long())
+            ht = ht + p["history_position_embedding.weight"][: h["mask"].shape[1]][None]
             actor = h["actor"].clamp(0, players - 1).long()
-            ht = ht + p["seat_embedding.weight"][relative.gather(1, actor)] * (h["actor"] >= 0)[..., None]
+            ht = ht + lookup(p["seat_embedding.weight"], relative.gather(1, actor)) * (h["actor"] >= 0)[..., None]
             tokens = torch.cat((tokens, ht), 1)
             valid = torch.cat((valid, h["mask"].bool()), 1)
         return tokens, valid
@@ -470,13 +470,13 @@ class PostflopModel(FamilyModel):
         live_relative = relative.gather(1, live_ids)
         live_status = status.gather(1, live_ids)
         # each live seat's seat, status and actor embeddings, added to its q rows in the map's epilogue
-        seat_terms = (p["seat_embedding.weight"][live_relative] + p["status_embedding.weight"][live_status]
-                      + p["actor_embedding.weight"][(live_ids == actor[:, None]).long()])
+        seat_terms = (lookup(p["seat_embedding.weight"], live_relative) + lookup(p["status_embedding.weight"], live_status)
+                      + lookup(p["actor_embedding.weight"], (live_ids == actor[:, None]).long()))
         row = _affine_rows(self.row_affine, feats, seat_terms, q)
         rows_k = live * q
         public, public_mask = self._public_tokens(pub, masks.fold_line_features, relative)
         actor_relative = relative.gather(1, actor[:, None]).squeeze(1)
-        anchors = p["anchor_tokens"][None] + p["anchor_seat_embedding.weight"][actor_relative][:, None]
+        anchors = p["anchor_tokens"][None] + lookup(p["anchor_seat_embedding.weight"], actor_relative)[:, None]
         x = torch.cat((row.reshape(batch, rows_k, d), public, anchors), 1)
         key_mask = torch.cat((compact_mask.reshape(batch, -1), public_mask,
                               torch.ones((batch, cfg.k_act), dtype=torch.bool, device=dev)), 1)

@@ -177,6 +177,17 @@ def _padded(x: Tensor, width: int) -> Tensor:
     return out
 
 
+def lookup(table: Tensor, index: Tensor) -> Tensor:
+    """``table[index]``: rows of an embedding table.  While the table takes a gradient this is the one-hot
+    product ``one_hot(index) @ table`` (exact in fp32: one nonzero term per output), so that its backward is
+    a GEMM rather than an index scatter serialised over the many repeats of a few table rows."""
+
+    if table.requires_grad and torch.is_grad_enabled():
+        rows = F.one_hot(index.reshape(-1), table.shape[0]).to(table.dtype) @ table
+        return rows.view(*index.shape, table.shape[1])
+    return table[index]
+
+
 def _affine_rows(affine, feats: Tensor, seat_terms: Tensor, rows_per_seat: int) -> Tensor:
     """affine(feats) + seat_terms broadcast over each seat's rows, in fp32: one map whose epilogue adds
     the per-seat terms (residual row m // rows_per_seat) and writes fp32, where the map's width allows
@@ -579,8 +590,8 @@ class PreflopModel(FamilyModel):
         scalars = torch.cat(groups, 1)
         type_ids = torch.cat([torch.full((n,), k, dtype=torch.long, device=dev) for n, k in kinds])
         w = p["public_scalar_affine.weight"][:, 0]
-        token = scalars[..., None] * w + p["public_scalar_affine.bias"] + p["public_type_embedding.weight"][type_ids]
-        seat_pos = p["seat_embedding.weight"][relative_seats]
+        token = scalars[..., None] * w + p["public_scalar_affine.bias"] + lookup(p["public_type_embedding.weight"], type_ids)
+        seat_pos = lookup(p["seat_embedding.weight"], relative_seats)
         rest = scalars.shape[1] - 1 - 2 * players
         zeros = lambda n: torch.zeros((batch, n, self.cfg.d_model), device=dev)  # noqa: E731
         token = token + torch.cat((zeros(1), seat_pos, seat_pos, zeros(rest)), 1)
@@ -591,11 +602,11 @@ class PreflopModel(FamilyModel):
             numeric = torch.stack([h[k].float() for k in ("amount", "pot_before", "call_amount", "current_bet",
                                                           "min_raise_to", "max_raise_to")], -1)
             ht = numeric @ p["history_numeric_affine.weight"].T + p["history_numeric_affine.bias"]
-            ht = ht + p["history_action_embedding.weight"][h["action"].clamp(0, 3).long()]
-            ht = ht + p["history_street_embedding.weight"][h["street"].clamp(0, 3).long()]
-            ht = ht + p["history_position_embedding.weight"][torch.arange(h["mask"].shape[1], device=dev)][None]
+            ht = ht + lookup(p["history_action_embedding.weight"], h["action"].clamp(0, 3).long())
+            ht = ht + lookup(p["history_street_embedding.weight"], h["street"].clamp(0, 3).long())
+            ht = ht + p["history_position_embedding.weight"][: h["mask"].shape[1]][None]
             actor = h["actor"].clamp(0, players - 1).long()
-            ht = ht + p["seat_embedding.weight"][relative_seats.gather(1, actor)] * (h["actor"] >= 0)[..., None]
+            ht = ht + lookup(p["seat_embedding.weight"], relative_seats.gather(1, actor)) * (h["actor"] >= 0)[..., None]
             token = torch.cat((token, ht), 1)
             valid = torch.cat((valid, h["mask"].bool()), 1)
         mean = (token * valid[..., None]).sum(1) / valid.sum(1, keepdim=True)
@@ -629,8 +640,7 @@ class PreflopModel(FamilyModel):
         seat_ids = torch.arange(players, device=dev)[None].expand(batch, -1)
         button = pub.get("button")
         relative = torch.remainder(seat_ids - button[:, None].long(), players) if button is not None else seat_ids
-        class_ids = torch.arange(K, device=dev)
-        class_emb = p["class_embedding.weight"][class_ids][None].expand(batch, -1, -1)
+        class_emb = p["class_embedding.weight"][None].expand(batch, -1, -1)  # every class row, in class order
         expanded_emb = class_emb[:, None].expand(-1, players, -1, -1)
         size_feature = (self.class_sizes / 12.0)[None, None].expand(batch, players, -1)
         geometry = torch.cat((self.class_card_geometry, self.class_overlap_scalars), -1)
@@ -640,13 +650,13 @@ class PreflopModel(FamilyModel):
                                  expanded_geometry, torch.ones_like(ranges)[..., None]), -1)
         actor_flag = (torch.arange(players, device=dev)[None] == actor[:, None]).long()
         # each seat's seat, status and actor embeddings, added to its K class rows in the map's epilogue
-        seat_terms = (p["seat_embedding.weight"][relative] + p["status_embedding.weight"][status]
-                      + p["actor_embedding.weight"][actor_flag])
+        seat_terms = (lookup(p["seat_embedding.weight"], relative) + lookup(p["status_embedding.weight"], status)
+                      + lookup(p["actor_embedding.weight"], actor_flag))
         row = _affine_rows(self.class_row_affine, row_feature, seat_terms, K)
         row_flat = row.reshape(batch, players * K, d)
         public_token, public_mask = self._public_tokens(pub, seat_mask, relative)
         actor_relative = relative.gather(1, actor[:, None]).squeeze(1)
-        anchors = p["anchor_tokens"][None] + p["anchor_seat_embedding.weight"][actor_relative][:, None]
+        anchors = p["anchor_tokens"][None] + lookup(p["anchor_seat_embedding.weight"], actor_relative)[:, None]
         x = torch.cat((row_flat, public_token, anchors), 1)
         length = x.shape[1]
         key_mask = torch.cat((cmask.reshape(batch, players * K), public_mask,
@@ -739,4 +749,5 @@ def parameter_shapes(cfg: PreflopConfig, rank_count: int) -> dict[str, tuple[int
     return shapes
 
 
-__all__ = ["FamilyModel", "PolicyOutput", "PreflopConfig", "PreflopModel", "class_geometry", "parameter_shapes"]
+__all__ = ["FamilyModel", "PolicyOutput", "PreflopConfig", "PreflopModel", "class_geometry", "lookup",
+           "parameter_shapes"]

@@ -591,6 +591,12 @@ int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void *x, int64_t ldx, c
  * pbg_linear_bf16. */
 int pbg_attention_bf16(int32_t batch, int32_t len, int32_t heads, const void *qkv, const float *key_bias,
                        const uint8_t *key_mask, const float *q_scale, void *out, uint32_t *error, void *stream);
+/* pbg_attention_bf16 that also writes each row's base-2 log-sum-exp of its
+ * logits, lse f32 [batch, heads, len] (+inf for a row without keys): the
+ * input of pbg_attention_backward. */
+int pbg_attention_bf16_lse(int32_t batch, int32_t len, int32_t heads, const void *qkv, const float *key_bias,
+                           const uint8_t *key_mask, const float *q_scale, void *out, float *lse, uint32_t *error,
+                           void *stream);
 
 /* pbg/core/tensor_ops.py:70-81 (LayerNorm over the last dimension, d <= 1024):
  * y = (x - mean) / sqrt(var + eps) * gain + bias, fp32 statistics; x and y
@@ -710,18 +716,18 @@ int pbg_layernorm_backward(int64_t rows, int32_t d, const void *x, int32_t x_bf1
                            float eps, const void *dy, int32_t dy_bf16, int64_t ldy, void *dx, int32_t dx_bf16,
                            int64_t lddx, float *partial, int64_t partial_len, void *stream);
 
-/* The softmax part of the attention backward for rows = sequences x heads x
- * len score rows (row r: sequence r / (heads len), head (r / len) % heads):
- * score f32 [rows, len] raw content scores q.k, dprob f32 [rows, len] = dO V^T,
- * key_bias f32 [sequences, len] (NULL = 0), key_mask u8 [sequences, len]
- * (NULL = all present), q_scale f32 [heads].  Writes prob bf16 [rows, len] =
- * softmax(score * q_scale + key_bias) over present keys (0 for absent keys and
- * for a row without keys), dlogit bf16 [rows, len] = prob * (dprob - sum(prob
- * dprob)) * q_scale, and scale_partial f32 [rows] = sum over the row of
- * prob * (dprob - sum(prob dprob)) * score. */
-int pbg_attention_softmax_backward(int64_t rows, int32_t len, int32_t heads, const float *score, const float *dprob,
-                                   const float *key_bias, const uint8_t *key_mask, const float *q_scale, void *prob,
-                                   void *dlogit, float *scale_partial, void *stream);
+/* Backward of pbg_attention_bf16 (fused: the scores are recomputed tile by
+ * tile and never stored): from qkv, the forward's output `out` and its base-2
+ * log-sum-exp `lse` [batch, heads, len] (pbg_attention_bf16_lse), the output
+ * gradient dout bf16 [batch, len, heads * 32], the same key_bias / key_mask /
+ * q_scale, writes dqkv bf16 [batch, len, 3 * heads * 32] (dQ | dK | dV) and
+ * scale_partial f32 [batch, heads, len]: per query row the sum over keys of
+ * dZ * (q.k), dZ the gradient of the row's logits (the head's q_scale
+ * gradient is the sum over the head's rows).  delta f32 [batch, heads, len]
+ * is scratch.  qkv, out, dout and dqkv 16-byte aligned. */
+int pbg_attention_backward(int32_t batch, int32_t len, int32_t heads, const void *qkv, const void *out,
+                           const void *dout, const float *lse, const float *key_bias, const uint8_t *key_mask,
+                           const float *q_scale, void *dqkv, float *delta, float *scale_partial, void *stream);
 
 #ifdef __cplusplus
 }
