@@ -170,23 +170,29 @@ __device__ __forceinline__ void ab_rows_a(const __nv_bfloat16* base, int64_t ld,
     }
 }
 
-// stage 64 rows x 32 columns (row r of the tile at base + (row0 + r) * ld) into `tile` (row-major,
-// stride AB_LD) and, when `trans` is given, its transpose (stride AB_LDT); absent rows are zero
-__device__ __forceinline__ void ab_stage(const __nv_bfloat16* base, int64_t ld, int row0, int rows,
-                                         __nv_bfloat16* tile, __nv_bfloat16* trans) {
+// A tile of 64 rows x 32 columns (row r at base + (row0 + r) * ld; absent rows zero) moves through
+// registers: ab_fetch loads this thread's 16 columns of one row, ab_put stores them into `tile`
+// (row-major, stride AB_LD) and, when `trans` is given, into its transpose (stride AB_LDT).  The
+// kernels fetch the next tile before computing on the current one, so its load latency overlaps
+// the tensor-core work.
+__device__ __forceinline__ void ab_fetch(const __nv_bfloat16* base, int64_t ld, int row0, int rows, uint4 v[2]) {
     const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
-    uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
+    v[0] = v[1] = make_uint4(0u, 0u, 0u, 0u);
     if (row0 + r < rows) {
         const uint4* src = reinterpret_cast<const uint4*>(base + (int64_t)(row0 + r) * ld + 16 * half);
-        v0 = src[0];
-        v1 = src[1];
+        v[0] = src[0];
+        v[1] = src[1];
     }
+}
+
+__device__ __forceinline__ void ab_put(const uint4 v[2], __nv_bfloat16* tile, __nv_bfloat16* trans) {
+    const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
     uint4* dst = reinterpret_cast<uint4*>(tile + r * AB_LD + 16 * half);
-    dst[0] = v0;
-    dst[1] = v1;
+    dst[0] = v[0];
+    dst[1] = v[1];
     if (trans) {
-        const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&v0);
-        const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&v1);
+        const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&v[0]);
+        const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&v[1]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             trans[(16 * half + e) * AB_LDT + r] = e0[e];
@@ -238,7 +244,7 @@ __global__ void __launch_bounds__(128) attention_delta_kernel(int64_t rows, int 
     }
 }
 
-__global__ void __launch_bounds__(128) attention_dq_kernel(AttnBackArgs A) {
+__global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
     __shared__ __align__(16) __nv_bfloat16 ks[AB_TILE * AB_LD], vs[AB_TILE * AB_LD], kt[32 * AB_LDT];
     __shared__ float kterm[AB_TILE];
     const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
@@ -262,15 +268,26 @@ __global__ void __launch_bounds__(128) attention_dq_kernel(AttnBackArgs A) {
     for (int i = 0; i < 4; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.0f;
     float th0 = 0.0f, th1 = 0.0f;
     const int kblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    uint4 kv[2], vv[2];
+    float term = 0.0f;
+    ab_fetch(seq + d, width, 0, A.len, kv);
+    ab_fetch(seq + 2 * d, width, 0, A.len, vv);
+    if (threadIdx.x < AB_TILE)
+        term = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + threadIdx.x, (int)threadIdx.x < A.len);
     for (int kb = 0; kb < kblocks; ++kb) {
-        const int k0 = kb * AB_TILE;
         __syncthreads();  // the previous block's tiles are consumed
-        ab_stage(seq + d, width, k0, A.len, ks, kt);
-        ab_stage(seq + 2 * d, width, k0, A.len, vs, nullptr);
-        if (threadIdx.x < AB_TILE)
-            kterm[threadIdx.x] = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k0 + threadIdx.x,
-                                             k0 + (int)threadIdx.x < A.len);
+        ab_put(kv, ks, kt);
+        ab_put(vv, vs, nullptr);
+        if (threadIdx.x < AB_TILE) kterm[threadIdx.x] = term;
         __syncthreads();
+        if (kb + 1 < kblocks) {  // the next block's rows, in flight during this block's products
+            const int k1 = (kb + 1) * AB_TILE;
+            ab_fetch(seq + d, width, k1, A.len, kv);
+            ab_fetch(seq + 2 * d, width, k1, A.len, vv);
+            if (threadIdx.x < AB_TILE)
+                term = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k1 + threadIdx.x,
+                                   k1 + (int)threadIdx.x < A.len);
+        }
         float s[8][4], dp[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
@@ -324,7 +341,7 @@ __global__ void __launch_bounds__(128) attention_dq_kernel(AttnBackArgs A) {
     }
 }
 
-__global__ void __launch_bounds__(128) attention_dkv_kernel(AttnBackArgs A) {
+__global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
     __shared__ __align__(16) __nv_bfloat16 qs[AB_TILE * AB_LD], gs[AB_TILE * AB_LD], qt[32 * AB_LDT],
         gt[32 * AB_LDT];
     __shared__ float lse_s[AB_TILE], delta_s[AB_TILE];
@@ -351,17 +368,31 @@ __global__ void __launch_bounds__(128) attention_dkv_kernel(AttnBackArgs A) {
         dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.0f;
     }
     const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    uint4 qv[2], gv[2];
+    float lv = INFINITY, dv_ = 0.0f;
+    ab_fetch(seq, width, 0, A.len, qv);
+    ab_fetch(grad, d, 0, A.len, gv);
+    if (threadIdx.x < AB_TILE && (int)threadIdx.x < A.len) {
+        lv = A.lse[row_base + threadIdx.x];
+        dv_ = A.delta[row_base + threadIdx.x];
+    }
     for (int qb = 0; qb < qblocks; ++qb) {
-        const int q0 = qb * AB_TILE;
         __syncthreads();
-        ab_stage(seq, width, q0, A.len, qs, qt);
-        ab_stage(grad, d, q0, A.len, gs, gt);
+        ab_put(qv, qs, qt);
+        ab_put(gv, gs, gt);
         if (threadIdx.x < AB_TILE) {
-            const bool v = q0 + (int)threadIdx.x < A.len;
-            lse_s[threadIdx.x] = v ? A.lse[row_base + q0 + threadIdx.x] : INFINITY;
-            delta_s[threadIdx.x] = v ? A.delta[row_base + q0 + threadIdx.x] : 0.0f;
+            lse_s[threadIdx.x] = lv;
+            delta_s[threadIdx.x] = dv_;
         }
         __syncthreads();
+        if (qb + 1 < qblocks) {  // the next block's rows, in flight during this block's products
+            const int q1 = (qb + 1) * AB_TILE;
+            ab_fetch(seq, width, q1, A.len, qv);
+            ab_fetch(grad, d, q1, A.len, gv);
+            const bool v = threadIdx.x < AB_TILE && q1 + (int)threadIdx.x < A.len;
+            lv = v ? A.lse[row_base + q1 + threadIdx.x] : INFINITY;
+            dv_ = v ? A.delta[row_base + q1 + threadIdx.x] : 0.0f;
+        }
         float s[8][4], dp[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
