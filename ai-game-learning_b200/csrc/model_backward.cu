@@ -154,6 +154,17 @@ __device__ __forceinline__ float ab_exp2(float x) {
 
 __device__ __forceinline__ uint32_t ab_ld32(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// four 8x8 bf16 matrices from shared memory; lane l gives the address of row l % 8 of matrix l / 8
+// and receives, of each matrix i, the pair (row l / 4, columns 2 (l % 4) + {0, 1}) in r[i]: with the
+// rows of a tile as the MMA's n index and 8 consecutive k per matrix, r[0..1] and r[2..3] are the
+// B fragments of two consecutive k steps of 16
+__device__ __forceinline__ void ab_ldm4(uint32_t r[4], const __nv_bfloat16* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p))
+                 : "memory");
+}
+
 // A fragments (two k-steps of 16 columns) of a warp's 16 rows x 32 columns of a row-major bf16
 // matrix in global memory (rows at or past `rows` read as zero)
 __device__ __forceinline__ void ab_rows_a(const __nv_bfloat16* base, int64_t ld, int row0, int rows, int g, int t,
@@ -289,16 +300,18 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
                                    k1 + (int)threadIdx.x < A.len);
         }
         float s[8][4], dp[8][4];
+        const int lrow = lane & 7, lmat = lane >> 3;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
             dp[nt][0] = dp[nt][1] = dp[nt][2] = dp[nt][3] = 0.0f;
-            const __nv_bfloat16* kr = ks + (8 * nt + g) * AB_LD + 2 * t;
-            const __nv_bfloat16* vr = vs + (8 * nt + g) * AB_LD + 2 * t;
+            uint32_t kb4[4], vb4[4];
+            ab_ldm4(kb4, ks + (8 * nt + lrow) * AB_LD + 8 * lmat);
+            ab_ldm4(vb4, vs + (8 * nt + lrow) * AB_LD + 8 * lmat);
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                ab_mma(s[nt], qa[k], ab_ld32(kr + 16 * k), ab_ld32(kr + 16 * k + 8));
-                ab_mma(dp[nt], da[k], ab_ld32(vr + 16 * k), ab_ld32(vr + 16 * k + 8));
+                ab_mma(s[nt], qa[k], kb4[2 * k], kb4[2 * k + 1]);
+                ab_mma(dp[nt], da[k], vb4[2 * k], vb4[2 * k + 1]);
             }
         }
         uint32_t dsa[4][4];
@@ -316,11 +329,13 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
             dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
         }
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; kk += 2) {
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt) {
-                const __nv_bfloat16* col = kt + (8 * nt + g) * AB_LDT + 16 * kk + 2 * t;
-                ab_mma(dq[nt], dsa[kk], ab_ld32(col), ab_ld32(col + 8));
+                uint32_t b4[4];
+                ab_ldm4(b4, kt + (8 * nt + lrow) * AB_LDT + 16 * kk + 8 * lmat);
+                ab_mma(dq[nt], dsa[kk], b4[0], b4[1]);
+                ab_mma(dq[nt], dsa[kk + 1], b4[2], b4[3]);
             }
         }
     }
@@ -394,16 +409,18 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
             dv_ = v ? A.delta[row_base + q1 + threadIdx.x] : 0.0f;
         }
         float s[8][4], dp[8][4];
+        const int lrow = lane & 7, lmat = lane >> 3;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
             dp[nt][0] = dp[nt][1] = dp[nt][2] = dp[nt][3] = 0.0f;
-            const __nv_bfloat16* qr = qs + (8 * nt + g) * AB_LD + 2 * t;
-            const __nv_bfloat16* gr = gs + (8 * nt + g) * AB_LD + 2 * t;
+            uint32_t qb4[4], gb4[4];
+            ab_ldm4(qb4, qs + (8 * nt + lrow) * AB_LD + 8 * lmat);
+            ab_ldm4(gb4, gs + (8 * nt + lrow) * AB_LD + 8 * lmat);
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                ab_mma(s[nt], ka[k], ab_ld32(qr + 16 * k), ab_ld32(qr + 16 * k + 8));
-                ab_mma(dp[nt], va[k], ab_ld32(gr + 16 * k), ab_ld32(gr + 16 * k + 8));
+                ab_mma(s[nt], ka[k], qb4[2 * k], qb4[2 * k + 1]);
+                ab_mma(dp[nt], va[k], gb4[2 * k], gb4[2 * k + 1]);
             }
         }
         uint32_t pa[4][4], dsa[4][4];
@@ -422,13 +439,16 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
             dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
         }
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; kk += 2) {
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt) {
-                const __nv_bfloat16* gc = gt + (8 * nt + g) * AB_LDT + 16 * kk + 2 * t;
-                const __nv_bfloat16* qc = qt + (8 * nt + g) * AB_LDT + 16 * kk + 2 * t;
-                ab_mma(dv[nt], pa[kk], ab_ld32(gc), ab_ld32(gc + 8));
-                ab_mma(dk[nt], dsa[kk], ab_ld32(qc), ab_ld32(qc + 8));
+                uint32_t gb4[4], qb4[4];
+                ab_ldm4(gb4, gt + (8 * nt + lrow) * AB_LDT + 16 * kk + 8 * lmat);
+                ab_ldm4(qb4, qt + (8 * nt + lrow) * AB_LDT + 16 * kk + 8 * lmat);
+                ab_mma(dv[nt], pa[kk], gb4[0], gb4[1]);
+                ab_mma(dv[nt], pa[kk + 1], gb4[2], gb4[3]);
+                ab_mma(dk[nt], dsa[kk], qb4[0], qb4[1]);
+                ab_mma(dk[nt], dsa[kk + 1], qb4[2], qb4[3]);
             }
         }
     }

@@ -80,7 +80,7 @@ class _LinearFn(torch.autograd.Function):
         dw = None
         if ctx.needs_input_grad[1]:
             dw = torch.mm(operand.t(), x, out_dtype=torch.float32)[:, : m.k]
-        db = _f32(dpre).sum(0) if ctx.has_b and ctx.needs_input_grad[2] else None
+        db = dpre.sum(0, dtype=torch.float32) if ctx.has_b and ctx.needs_input_grad[2] else None
         dres = None
         if residual is not None and ctx.needs_input_grad[3]:
             dres = _f32(dpre)

@@ -485,8 +485,12 @@ class FamilyModel:
         rows_k = players * rows_per_seat
         side_rows = side.reshape(batch, rows_k, -1).to(torch.bfloat16)
         mass_rows = mass.reshape(-1).detach().to(torch.float32).contiguous()
-        pad = torch.zeros((batch, length - rows_k, 3 * d + side_rows.shape[-1]), dtype=torch.bfloat16,
-                          device=x.device)
+        # the FamilyFFN operand is assembled at the map's padded width: the columns after
+        # [LN(x_hat) | j | oc^2 | oc*oe | side] and the row-only columns of the other tokens are zero
+        width = self.layers[0]["ffn_in"].kp if self.layers else 0
+        tail = width - 4 * d - side_rows.shape[-1]
+        side_rows = torch.cat((side_rows, side_rows.new_zeros((batch, rows_k, tail))), -1) if tail else side_rows
+        pad = torch.zeros((batch, length - rows_k, width - d), dtype=torch.bfloat16, device=x.device)
         x = x.contiguous()
         for layer in self.layers:
             j, square, product = self._incidence_train(layer, x, players, rows_per_seat, mass_rows, incidence,
@@ -497,9 +501,8 @@ class FamilyModel:
             x_hat = layer["w_o"].apply(attended.view(-1, d), residual=x.view(-1, d), out_dtype=torch.float32)
             normed = self._ln(x_hat, layer["ln"]).view(batch, length, d)
             extra = torch.cat((torch.cat((j.view(batch, rows_k, d), square, product, side_rows), -1), pad), 1)
-            hidden = layer["ffn_in"](torch.cat((normed, extra), -1), "gelu")
-            x = layer["ffn_out"].apply(hidden.view(batch * length, -1), residual=x_hat,
-                                       out_dtype=torch.float32).view(batch, length, d)
+            hidden = layer["ffn_in"].apply(torch.cat((normed, extra), -1).view(batch * length, width), "gelu")
+            x = layer["ffn_out"].apply(hidden, residual=x_hat, out_dtype=torch.float32).view(batch, length, d)
         return x
 
     def _head(self, head: "_Map", x: Tensor) -> Tensor:
