@@ -26,7 +26,7 @@ namespace {
 
 constexpr int GB_THREADS = 256;
 constexpr int LNB_WARPS = 8;
-constexpr int LNB_MAX_PER_LANE = 16;  // d <= 512
+constexpr int LNB_MAX_WIDTH = 512;
 
 __device__ __forceinline__ float load_f(const float* p) { return *p; }
 __device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
@@ -50,12 +50,14 @@ __global__ void gelu_backward_kernel(int64_t M, int N, const float* __restrict__
     }
 }
 
-template <typename In, typename DY, typename Out>
+// PER: the columns a lane holds (d <= 32 PER)
+template <int PER, typename In, typename DY, typename Out>
 __global__ void __launch_bounds__(LNB_WARPS * 32)
 layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t ldx, const float* __restrict__ gain,
                           float eps, const DY* __restrict__ dy, int64_t ldy, Out* __restrict__ dx, int64_t lddx,
                           float* __restrict__ partial) {
-    __shared__ float red[LNB_WARPS][2 * 32 * LNB_MAX_PER_LANE];
+    constexpr int LNB_MAX_PER_LANE = PER;
+    __shared__ float red[LNB_WARPS][2 * 32 * PER];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per = d >> 5;
     float acc_g[LNB_MAX_PER_LANE], acc_b[LNB_MAX_PER_LANE];
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
 
 int layernorm_backward_grid(int64_t rows) {
     const int64_t need = (rows + LNB_WARPS - 1) / LNB_WARPS;
-    const int64_t cap = 4 * (int64_t)sm_count();
+    const int64_t cap = 8 * (int64_t)sm_count();
     return (int)(need < cap ? (need > 0 ? need : 1) : cap);
 }
 
@@ -499,25 +501,34 @@ int pbg_gelu_backward(int64_t M, int32_t N, const float* pre, int64_t ldp, const
 }
 
 int64_t pbg_layernorm_backward_partials(int64_t rows, int32_t d) {
-    if (rows < 0 || d < 32 || d % 32 || d > 32 * LNB_MAX_PER_LANE) return -1;
+    if (rows < 0 || d < 32 || d % 32 || d > LNB_MAX_WIDTH) return -1;
     return (int64_t)layernorm_backward_grid(rows) * 2 * d;
 }
 
 int pbg_layernorm_backward(int64_t rows, int32_t d, const void* x, int32_t x_bf16, int64_t ldx, const float* gain,
                            float eps, const void* dy, int32_t dy_bf16, int64_t ldy, void* dx, int32_t dx_bf16,
                            int64_t lddx, float* partial, int64_t partial_len, void* stream) {
-    PBG_REQUIRE(rows >= 0 && d >= 32 && d % 32 == 0 && d <= 32 * LNB_MAX_PER_LANE,
-                "layernorm_backward: width %d must be a multiple of 32 up to %d", (int)d, 32 * LNB_MAX_PER_LANE);
+    PBG_REQUIRE(rows >= 0 && d >= 32 && d % 32 == 0 && d <= LNB_MAX_WIDTH,
+                "layernorm_backward: width %d must be a multiple of 32 up to %d", (int)d, LNB_MAX_WIDTH);
     PBG_REQUIRE(x && dy && dx && partial && ldx >= d && ldy >= d && lddx >= d, "layernorm_backward: bad arguments");
     const int grid = layernorm_backward_grid(rows);
     PBG_REQUIRE(partial_len >= (int64_t)grid * 2 * d, "layernorm_backward: partials hold %lld floats, need %lld",
                 (long long)partial_len, (long long)grid * 2 * d);
     cudaStream_t s = as_stream(stream);
     const dim3 block(LNB_WARPS * 32);
-#define PBG_LNB(IN, DYT, OUT)                                                                                     \
-    layernorm_backward_kernel<IN, DYT, OUT><<<grid, block, 0, s>>>(rows, d, static_cast<const IN*>(x), ldx, gain, \
-                                                                   eps, static_cast<const DYT*>(dy), ldy,         \
-                                                                   static_cast<OUT*>(dx), lddx, partial)
+#define PBG_LNB_PER(PER, IN, DYT, OUT)                                                                    \
+    layernorm_backward_kernel<PER, IN, DYT, OUT><<<grid, block, 0, s>>>(                                   \
+        rows, d, static_cast<const IN*>(x), ldx, gain, eps, static_cast<const DYT*>(dy), ldy, static_cast<OUT*>(dx), \
+        lddx, partial)
+#define PBG_LNB(IN, DYT, OUT)                  \
+    do {                                       \
+        if (d <= 128)                          \
+            PBG_LNB_PER(4, IN, DYT, OUT);      \
+        else if (d <= 256)                     \
+            PBG_LNB_PER(8, IN, DYT, OUT);      \
+        else                                   \
+            PBG_LNB_PER(16, IN, DYT, OUT);     \
+    } while (0)
     if (x_bf16) {
         if (dy_bf16) {
             if (dx_bf16) PBG_LNB(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16); else PBG_LNB(__nv_bfloat16, __nv_bfloat16, float);
@@ -532,6 +543,7 @@ int pbg_layernorm_backward(int64_t rows, int32_t d, const void* x, int32_t x_bf1
         }
     }
 #undef PBG_LNB
+#undef PBG_LNB_PER
     return launch_status("layernorm_backward");
 }
 
