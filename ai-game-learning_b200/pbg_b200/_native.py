@@ -144,6 +144,7 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_layernorm_rows": (_I32, [_I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P, ctypes.c_float, _P, _I32, _I64,
                                   _I64, _P]),
     "pbg_scatter_rows_bf16": (_I32, [_I64, _I32, _I64, _P, _P, _I64, _I64, _P]),
+    "pbg_incidence_combine_backward": (_I32, [_I64, _I32, _I64, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pbg_incidence_combine": (_I32, [_I64, _I32, _I64, _I32, _P, _P, _P, _P, _I64, _I32, _I32, _P, _P, _I64, _I64,
                                      _I32, _I32, _P]),
     "pbg_attention_bf16": (_I32, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),

@@ -175,6 +175,44 @@ def attention_train(qkv: Tensor, heads: int, q_scale: Tensor, key_bias: Tensor |
     return _AttentionFn.apply(qkv.contiguous(), q_scale, kb, km, heads)
 
 
+class _IncidenceCombineFn(torch.autograd.Function):
+    """incidence.py:57-70 after the card contractions (``pbg_incidence_combine``): from source and
+    overlap [B, P, R, d] (fp32) and the identical-row scale [B, R], the rows [oe | own] (bf16), oc
+    (fp32) and the FamilyFFN features [oc^2 | oc * oe] (bf16), rows (b * P + p) * R + r; the backward
+    is ``pbg_incidence_combine_backward``."""
+
+    @staticmethod
+    def forward(ctx, source, overlap, identical_scale):
+        B, P, R, d = source.shape
+        count, dev = B * P * R, source.device
+        pair = torch.empty((count, 2 * d), dtype=torch.bfloat16, device=dev)
+        other_card = torch.empty((count, d), dtype=torch.float32, device=dev)
+        ffn = torch.empty((count, 2 * d), dtype=torch.bfloat16, device=dev)
+        call("pbg_incidence_combine", B, P, R, d, ptr(source), ptr(overlap), ptr(identical_scale), ptr(pair), 2 * d, 0,
+             d, ptr(other_card), ptr(ffn), P * R * 2 * d, 2 * d, 0, d, stream(dev))
+        ctx.save_for_backward(source, overlap, identical_scale)
+        return pair, other_card, ffn
+
+    @staticmethod
+    def backward(ctx, g_pair, g_other_card, g_ffn):
+        source, overlap, identical_scale = ctx.saved_tensors
+        B, P, R, d = source.shape
+        d_source, d_overlap = torch.empty_like(source), torch.empty_like(source)
+        flat = lambda g, dtype: None if g is None else g.to(dtype).contiguous()  # noqa: E731
+        g_pair, g_other_card, g_ffn = flat(g_pair, torch.bfloat16), flat(g_other_card, torch.float32), flat(
+            g_ffn, torch.bfloat16)
+        call("pbg_incidence_combine_backward", B, P, R, d, ptr(source), ptr(overlap), ptr(identical_scale), ptr(g_pair),
+             ptr(g_other_card), ptr(g_ffn), ptr(d_source), ptr(d_overlap), stream(source.device))
+        return d_source, d_overlap, None
+
+
+def incidence_combine_train(source: Tensor, overlap: Tensor, identical_scale: Tensor):
+    """Differentiable ``pbg_incidence_combine``: ([oe | own] bf16, oc fp32, [oc^2 | oc oe] bf16) rows."""
+
+    return _IncidenceCombineFn.apply(source.contiguous(), overlap.contiguous(),
+                                     identical_scale.detach().float().contiguous())
+
+
 def q_scale_of(theta: Tensor) -> Tensor:
     """primitives.py MHA: the score scale 1 / ((softplus(theta) + 0.5) sqrt(32)) of each head."""
 

@@ -25,7 +25,7 @@ from torch.nn import functional as F
 
 from ._native import NativeError, call, ptr, rows_ptr, stream
 from .model import attention, linear, linear_ex
-from .model_train import attention_train, layernorm_train, linear_train, q_scale_of
+from .model_train import attention_train, incidence_combine_train, layernorm_train, linear_train, q_scale_of
 
 
 @dataclass(frozen=True)
@@ -171,6 +171,8 @@ def _padded(x: Tensor, width: int) -> Tensor:
     x = x.reshape(-1, x.shape[-1])
     if x.shape[1] == width:
         return x.to(torch.bfloat16).contiguous()
+    if x.requires_grad and torch.is_grad_enabled():  # training: a pad whose backward is a slice, not a copy
+        return F.pad(x.to(torch.bfloat16), (0, width - x.shape[1]))
     out = torch.empty((x.shape[0], width), dtype=torch.bfloat16, device=x.device)
     out[:, : x.shape[1]] = x
     out[:, x.shape[1]:] = 0
@@ -446,9 +448,9 @@ class FamilyModel:
     def _incidence_train(self, layer, x: Tensor, players: int, rows: int, mass: Tensor, incidence: Tensor,
                          identical_scale: Tensor):
         """``_incidence`` as autograd steps (incidence.py:30-84): the LayerNorm, the source map with the
-        row mass as its row scale, the fp32 card contractions and seat sums, the query/identical/own map
-        with oc as its pre-GELU residual and the output map.  Returns j [B * players * rows, d] and the
-        FamilyFFN features oc^2, oc * oe [B, players * rows, d] (bf16)."""
+        row mass as its row scale, the fp32 card contractions, the seat sums (``incidence_combine_train``),
+        the query/identical/own map with oc as its pre-GELU residual and the output map.  Returns j
+        [B * players * rows, d] and the FamilyFFN features [oc^2 | oc * oe] [B, players * rows, 2d] (bf16)."""
 
         batch, length, d = x.shape
         count = batch * players * rows
@@ -460,19 +462,12 @@ class FamilyModel:
         else:
             blocks = source.view(batch, players, rows, d)
             card_overlap = torch.matmul(incidence[:, None], torch.matmul(incidence.transpose(1, 2)[:, None], blocks))
-        source = source.view(batch, players, rows, d)
-        card_overlap = card_overlap.reshape(batch, players, rows, d)
-        same = source * identical_scale.float()[:, None, :, None]
-        other_equal = same.sum(1, keepdim=True) - same
-        other_card = (card_overlap.sum(1, keepdim=True) - card_overlap) - 2.0 * other_equal
-        own_card = card_overlap - 2.0 * same
-        operand = torch.cat((n, other_equal.reshape(count, d).to(torch.bfloat16),
-                             own_card.reshape(count, d).to(torch.bfloat16)), -1)
-        hidden = layer["inc_in"].apply(operand, "gelu", residual=other_card.reshape(count, d))
+        pair, other_card, features = incidence_combine_train(source.view(batch, players, rows, d),
+                                                             card_overlap.reshape(batch, players, rows, d),
+                                                             identical_scale)
+        hidden = layer["inc_in"].apply(torch.cat((n, pair), -1), "gelu", residual=other_card)
         j = layer["inc_out"].apply(hidden)
-        square = (other_card * other_card).to(torch.bfloat16).view(batch, players * rows, d)
-        product = (other_card * other_equal).to(torch.bfloat16).view(batch, players * rows, d)
-        return j, square, product
+        return j, features.view(batch, players * rows, 2 * d)
 
     def _trunk_train(self, x: Tensor, players: int, rows_per_seat: int, mass: Tensor, incidence: Tensor,
                      identical_scale: Tensor, side: Tensor, key_bias: Tensor, key_mask: Tensor) -> Tensor:
@@ -493,14 +488,14 @@ class FamilyModel:
         pad = torch.zeros((batch, length - rows_k, width - d), dtype=torch.bfloat16, device=x.device)
         x = x.contiguous()
         for layer in self.layers:
-            j, square, product = self._incidence_train(layer, x, players, rows_per_seat, mass_rows, incidence,
-                                                       identical_scale)
+            j, features = self._incidence_train(layer, x, players, rows_per_seat, mass_rows, incidence,
+                                                identical_scale)
             nx = self._ln(x, layer["ln"])
             qkv = layer["w_qkv"](nx)
             attended = attention_train(qkv, cfg.n_heads, q_scale_of(layer["theta"]), key_bias, key_mask)
             x_hat = layer["w_o"].apply(attended.view(-1, d), residual=x.view(-1, d), out_dtype=torch.float32)
             normed = self._ln(x_hat, layer["ln"]).view(batch, length, d)
-            extra = torch.cat((torch.cat((j.view(batch, rows_k, d), square, product, side_rows), -1), pad), 1)
+            extra = torch.cat((torch.cat((j.view(batch, rows_k, d), features, side_rows), -1), pad), 1)
             hidden = layer["ffn_in"].apply(torch.cat((normed, extra), -1).view(batch * length, width), "gelu")
             x = layer["ffn_out"].apply(hidden, residual=x_hat, out_dtype=torch.float32).view(batch, length, d)
         return x

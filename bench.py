@@ -55,7 +55,8 @@ def parse():
     p.add_argument("--params", type=int, default=4_194_304)
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--profile-hands", type=int, default=4096,
-                   help="--profile-forward rollout_with_model: hands of the profiled rollout")
+                   help="--profile-forward rollout_with_model: hands of the profiled rollout; learner_step_cfg2: "
+                        "H / 4 preflop and H / 16 postflop presentations")
     p.add_argument("--engine-compare", action="store_true",
                    help="time the reference's own training iteration (pbg.runtime.TrainingSession from baseline/_ref) "
                         "unmodified and with pbg_b200.engine.install(learner=True), each in a fresh process, and "
@@ -64,9 +65,10 @@ def parse():
                    help=argparse.SUPPRESS)
     p.add_argument("--engine-roots", type=int, default=4096)
     p.add_argument("--engine-iterations", type=int, default=6)
-    p.add_argument("--learner-scaling", action="store_true",
-                   help="time the cfg1 learner step data-parallel instead: every rank a step over its own 16,384 "
-                        "presentations, the SUM of the real flat gradient (NCCL), then AdamW; one JSON line")
+    p.add_argument("--learner-scaling", nargs="?", const="cfg1", choices=("cfg1", "cfg2"), default=None,
+                   help="time a learner step data-parallel instead: every rank a step over its own presentations "
+                        "(cfg1: 16,384 for the MLP; cfg2: 1,024 preflop + 256 postflop for the attention "
+                        "network), the SUM of the real flat gradient (NCCL), then AdamW; one JSON line")
     p.add_argument("--allreduce", choices=("auto", "nvls", "nccl"), default="auto",
                    help="gradient SUM at N > 1: auto = libpbgb200's NVLS kernel from 4 ranks, NCCL below")
     p.add_argument("--comm-sms", type=int, default=16,
@@ -725,6 +727,54 @@ def learner_scaling(args, device, world, rank, rows=16_384):
                           "value": world * rows / (ms / 1e3), "unit": "presentations/s", "n_gpus": world,
                           "steps": args.steps, "ms_per_step": ms, "scaling": "weak",
                           "config": {"workload": f"HU 8bb R4, fp32 MLP ({model.numel} parameters), {rows} "
+                                                 "presentations per rank per step, NCCL SUM of the flat gradient"}}))
+
+
+def learner_scaling_cfg2(args, device, world, rank, pre_rows=1024, post_rows=256):
+    """cfg2 learner step, data parallel: each rank runs the training forward, fused objective and backward
+    of the attention network over its own presentations (`pre_rows` preflop + `post_rows` postflop from a
+    rollout seeded by the rank), the flat gradient (4,226,931 fp32) is SUM-all-reduced with NCCL, then
+    AdamW.  Weak scaling; timed with CUDA events, max over ranks."""
+
+    import torch
+    import torch.distributed as dist
+    from pbg_b200.model_train import ModelLearnerStep
+
+    model, _, _, _ = _cfg2_model(device)  # the same initial weights on every rank
+    batches = _cfg2_learner_batches(device, model, pre_rows, post_rows, seed=41 + rank)
+    step = ModelLearnerStep(model)
+
+    def one():
+        step.gradient(batches)
+        if world > 1:
+            dist.all_reduce(step.adam.grad)
+        step.adam.step()
+
+    for _ in range(max(3, args.warmup)):
+        one()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    steps = min(args.steps, 10)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b) / steps
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    if rank == 0:
+        ms = float(t)
+        rows = pre_rows + post_rows
+        print(json.dumps({"metric": "learner presentations/s (cfg2 learner step, data parallel)",
+                          "value": world * rows / (ms / 1e3), "unit": "presentations/s", "n_gpus": world,
+                          "steps": steps, "ms_per_step": ms, "scaling": "weak",
+                          "config": {"workload": f"HU 100bb R13, cfg2 attention network ({step.flat.numel} "
+                                                 f"parameters), {pre_rows} preflop + {post_rows} postflop "
                                                  "presentations per rank per step, NCCL SUM of the flat gradient"}}))
 
 
@@ -1807,12 +1857,19 @@ def main():
             args.profile_forward, f"{args.profile_forward}_forward_component")
         if name == "rollout_with_model_component":
             rollout_with_model_component(device, hands=args.profile_hands)
+        elif name == "learner_step_cfg2_component":  # --profile-hands H: H / 4 preflop + H / 16 postflop rows
+            learner_step_cfg2_component(device, pre_rows=args.profile_hands // 4, post_rows=args.profile_hands // 16)
         else:
             globals()[name](device)
         return
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if args.learner_scaling == "cfg2":
+        learner_scaling_cfg2(args, device, world, rank)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.learner_scaling:
         learner_scaling(args, device, world, rank)
         if world > 1:

@@ -635,6 +635,14 @@ int pbg_incidence_combine(int64_t batch, int32_t players, int64_t rows, int32_t 
                           const float *overlap, const float *identical_scale, void *inc, int64_t ld_inc,
                           int32_t col_equal, int32_t col_own, float *other_card, void *ffn, int64_t ffn_batch_stride,
                           int64_t ld_ffn, int32_t col_square, int32_t col_product, void *stream);
+/* Backward of pbg_incidence_combine for outputs laid out per row
+ * (b * P + p) * R + r: g_pair bf16 [rows, 2d] (the gradients of oe | own),
+ * g_other_card f32 [rows, d], g_ffn bf16 [rows, 2d] (of oc*oc | oc*oe); any
+ * may be NULL (zero).  Writes d_source and d_overlap f32 [B, P, R, d]. */
+int pbg_incidence_combine_backward(int64_t batch, int32_t players, int64_t rows, int32_t d, const float *source,
+                                   const float *overlap, const float *identical_scale, const void *g_pair,
+                                   const float *g_other_card, const void *g_ffn, float *d_source, float *d_overlap,
+                                   void *stream);
 
 /* ---------------------------------------------------------- collective */
 

@@ -118,6 +118,39 @@ def test_attention_backward_matches_torch(length):
     assert float(got_qkv[2].abs().max()) == 0.0
 
 
+@pytest.mark.parametrize("players,rows,shared_scale", [(2, 169, True), (3, 300, False)])
+def test_incidence_combine_backward_matches_torch(players, rows, shared_scale):
+    """incidence.py:57-70 seat sums: [oe | own], oc and [oc^2 | oc oe] and their backward against torch fp32
+    autograd of the same formulas (bf16 outputs rounded as the kernel's)."""
+
+    from pbg_b200.model_train import incidence_combine_train
+
+    g = torch.Generator(device=DEV).manual_seed(6)
+    B, d = 4, 128
+    source = torch.randn(B, players, rows, d, device=DEV, generator=g).requires_grad_()
+    overlap = torch.randn(B, players, rows, d, device=DEV, generator=g).requires_grad_()
+    scale = (torch.rand(rows, device=DEV, generator=g) + 0.1)[None].expand(B, -1) if shared_scale else \
+        torch.ones(B, rows, device=DEV)
+    pair, oc, feats = incidence_combine_train(source, overlap, scale)
+    c1, c2, c3 = (torch.randn(t.shape, device=DEV, generator=g) for t in (pair, oc, feats))
+    ((pair.float() * c1).sum() + (oc * c2).sum() + (feats.float() * c3).sum()).backward()
+    got = [source.grad.clone(), overlap.grad.clone()]
+    source.grad, overlap.grad = None, None
+    same = source * scale[:, None, :, None]
+    oe = same.sum(1, keepdim=True) - same
+    occ = (overlap.sum(1, keepdim=True) - overlap) - 2.0 * oe
+    own = overlap - 2.0 * same
+    count = B * players * rows
+    ref_pair = torch.cat((oe.reshape(count, d), own.reshape(count, d)), -1)
+    ref_feats = torch.cat(((occ * occ).reshape(count, d), (occ * oe).reshape(count, d)), -1)
+    _close(pair.float().detach(), ref_pair.detach())
+    _close(oc.detach(), occ.reshape(count, d).detach(), tol=1e-5)
+    _close(feats.float().detach(), ref_feats.detach())
+    ((ref_pair * _bf(c1)).sum() + (occ.reshape(count, d) * c2).sum() + (ref_feats * _bf(c3)).sum()).backward()
+    _close(got[0], source.grad, tol=1e-4)
+    _close(got[1], overlap.grad, tol=1e-4)
+
+
 def _sketch_check(model_params, d, leaves):
     names = [str(n) for n in d["gsk_names"]]
     norms, projections = d["gsk_norm"], d["gsk_proj"]
