@@ -128,11 +128,10 @@ layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t
 // atomics: one CTA per 64-query block computes dQ (looping over key blocks), one per 64-key block
 // dK and dV (looping over query blocks).  Each of the 4 warps owns 16 rows; the products run on
 // mma.sync m16n8k16 (bf16 operands, fp32 accumulation) with operand tiles staged in shared memory
-// row-major (stride 40 elements) and, for the products that contract over rows, transposed
-// (stride 72); both strides make every fragment read bank-conflict free.
+// row-major at a stride of 40 elements, which makes every ldmatrix read bank-conflict free; the
+// products that contract over a tile's rows read it with ldmatrix.trans.
 constexpr int AB_TILE = 64;
 constexpr int AB_LD = 40;
-constexpr int AB_LDT = 72;
 constexpr float AB_LOG2E = 1.4426950408889634f;
 
 __device__ __forceinline__ void ab_mma(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
@@ -160,6 +159,15 @@ __device__ __forceinline__ uint32_t ab_ld32(const __nv_bfloat16* p) { return *re
 // and receives, of each matrix i, the pair (row l / 4, columns 2 (l % 4) + {0, 1}) in r[i]: with the
 // rows of a tile as the MMA's n index and 8 consecutive k per matrix, r[0..1] and r[2..3] are the
 // B fragments of two consecutive k steps of 16
+// the same four matrices transposed: lane l receives (rows 2 (l % 4) + {0, 1}, column l / 4), the B
+// fragment of an MMA whose k index runs along the stored rows (a row-major [k][n] tile)
+__device__ __forceinline__ void ab_ldm4t(uint32_t r[4], const __nv_bfloat16* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p))
+                 : "memory");
+}
+
 __device__ __forceinline__ void ab_ldm4(uint32_t r[4], const __nv_bfloat16* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -185,9 +193,8 @@ __device__ __forceinline__ void ab_rows_a(const __nv_bfloat16* base, int64_t ld,
 
 // A tile of 64 rows x 32 columns (row r at base + (row0 + r) * ld; absent rows zero) moves through
 // registers: ab_fetch loads this thread's 16 columns of one row, ab_put stores them into `tile`
-// (row-major, stride AB_LD) and, when `trans` is given, into its transpose (stride AB_LDT).  The
-// kernels fetch the next tile before computing on the current one, so its load latency overlaps
-// the tensor-core work.
+// (row-major, stride AB_LD).  The kernels fetch the next tile before computing on the current one,
+// so its load latency overlaps the tensor-core work.
 __device__ __forceinline__ void ab_fetch(const __nv_bfloat16* base, int64_t ld, int row0, int rows, uint4 v[2]) {
     const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
     v[0] = v[1] = make_uint4(0u, 0u, 0u, 0u);
@@ -198,20 +205,11 @@ __device__ __forceinline__ void ab_fetch(const __nv_bfloat16* base, int64_t ld, 
     }
 }
 
-__device__ __forceinline__ void ab_put(const uint4 v[2], __nv_bfloat16* tile, __nv_bfloat16* trans) {
+__device__ __forceinline__ void ab_put(const uint4 v[2], __nv_bfloat16* tile) {
     const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
     uint4* dst = reinterpret_cast<uint4*>(tile + r * AB_LD + 16 * half);
     dst[0] = v[0];
     dst[1] = v[1];
-    if (trans) {
-        const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&v[0]);
-        const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&v[1]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            trans[(16 * half + e) * AB_LDT + r] = e0[e];
-            trans[(16 * half + 8 + e) * AB_LDT + r] = e1[e];
-        }
-    }
 }
 
 __device__ __forceinline__ float ab_key_term(const float* bias, const uint8_t* mask, int64_t at, bool present) {
@@ -258,8 +256,8 @@ __global__ void __launch_bounds__(128) attention_delta_kernel(int64_t rows, int 
 }
 
 __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
-    __shared__ __align__(16) __nv_bfloat16 ks[AB_TILE * AB_LD], vs[AB_TILE * AB_LD], kt[32 * AB_LDT];
-    __shared__ float kterm[AB_TILE];
+    __shared__ __align__(16) __nv_bfloat16 ks[AB_TILE * AB_LD], vs[AB_TILE * AB_LD];
+    __shared__ __align__(8) float kterm[AB_TILE];
     const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
     const int qb = blockIdx.x % qblocks;
     const int h = (blockIdx.x / qblocks) % A.heads;
@@ -289,8 +287,8 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
         term = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + threadIdx.x, (int)threadIdx.x < A.len);
     for (int kb = 0; kb < kblocks; ++kb) {
         __syncthreads();  // the previous block's tiles are consumed
-        ab_put(kv, ks, kt);
-        ab_put(vv, vs, nullptr);
+        ab_put(kv, ks);
+        ab_put(vv, vs);
         if (threadIdx.x < AB_TILE) kterm[threadIdx.x] = term;
         __syncthreads();
         if (kb + 1 < kblocks) {  // the next block's rows, in flight during this block's products
@@ -319,7 +317,8 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
         uint32_t dsa[4][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-            const float t0 = kterm[8 * nt + 2 * t], t1 = kterm[8 * nt + 2 * t + 1];
+            const float2 tp = *reinterpret_cast<const float2*>(kterm + 8 * nt + 2 * t);
+            const float t0 = tp.x, t1 = tp.y;
             const float p0 = ab_exp2(fmaf(s[nt][0], scale2, t0) - lse0), p1 = ab_exp2(fmaf(s[nt][1], scale2, t1) - lse0);
             const float p2 = ab_exp2(fmaf(s[nt][2], scale2, t0) - lse1), p3 = ab_exp2(fmaf(s[nt][3], scale2, t1) - lse1);
             const float z0 = p0 * (dp[nt][0] - dl0), z1 = p1 * (dp[nt][1] - dl0);
@@ -330,14 +329,15 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
             dsa[nt >> 1][(nt & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
             dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
         }
+        // dQ += dS K: the k index (keys) runs along the rows of the K tile
 #pragma unroll
-        for (int kk = 0; kk < 4; kk += 2) {
+        for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
+            for (int nt = 0; nt < 4; nt += 2) {
                 uint32_t b4[4];
-                ab_ldm4(b4, kt + (8 * nt + lrow) * AB_LDT + 16 * kk + 8 * lmat);
+                ab_ldm4t(b4, ks + (16 * kk + 8 * (lmat & 1) + lrow) * AB_LD + 8 * (nt + (lmat >> 1)));
                 ab_mma(dq[nt], dsa[kk], b4[0], b4[1]);
-                ab_mma(dq[nt], dsa[kk + 1], b4[2], b4[3]);
+                ab_mma(dq[nt + 1], dsa[kk], b4[2], b4[3]);
             }
         }
     }
@@ -359,9 +359,8 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
 }
 
 __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
-    __shared__ __align__(16) __nv_bfloat16 qs[AB_TILE * AB_LD], gs[AB_TILE * AB_LD], qt[32 * AB_LDT],
-        gt[32 * AB_LDT];
-    __shared__ float lse_s[AB_TILE], delta_s[AB_TILE];
+    __shared__ __align__(16) __nv_bfloat16 qs[AB_TILE * AB_LD], gs[AB_TILE * AB_LD];
+    __shared__ __align__(8) float lse_s[AB_TILE], delta_s[AB_TILE];
     const int kblocks = (A.len + AB_TILE - 1) / AB_TILE;
     const int kb = blockIdx.x % kblocks;
     const int h = (blockIdx.x / kblocks) % A.heads;
@@ -395,8 +394,8 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
     }
     for (int qb = 0; qb < qblocks; ++qb) {
         __syncthreads();
-        ab_put(qv, qs, qt);
-        ab_put(gv, gs, gt);
+        ab_put(qv, qs);
+        ab_put(gv, gs);
         if (threadIdx.x < AB_TILE) {
             lse_s[threadIdx.x] = lv;
             delta_s[threadIdx.x] = dv_;
@@ -429,7 +428,9 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             const int c = 8 * nt + 2 * t;
-            const float l0 = lse_s[c], l1 = lse_s[c + 1], e0 = delta_s[c], e1 = delta_s[c + 1];
+            const float2 lp = *reinterpret_cast<const float2*>(lse_s + c);
+            const float2 ep = *reinterpret_cast<const float2*>(delta_s + c);
+            const float l0 = lp.x, l1 = lp.y, e0 = ep.x, e1 = ep.y;
             // rows: keys g (regs 0, 1) and g + 8 (regs 2, 3); columns: queries c, c + 1
             const float p0 = ab_exp2(fmaf(s[nt][0], scale2, kt0) - l0), p1 = ab_exp2(fmaf(s[nt][1], scale2, kt0) - l1);
             const float p2 = ab_exp2(fmaf(s[nt][2], scale2, kt1) - l0), p3 = ab_exp2(fmaf(s[nt][3], scale2, kt1) - l1);
@@ -440,17 +441,19 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
             dsa[nt >> 1][(nt & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
             dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
         }
+        // dV += P^T dO and dK += dS^T Q: the k index (queries) runs along the rows of the dO and Q tiles
 #pragma unroll
-        for (int kk = 0; kk < 4; kk += 2) {
+        for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
+            for (int nt = 0; nt < 4; nt += 2) {
+                const int at = (16 * kk + 8 * (lmat & 1) + lrow) * AB_LD + 8 * (nt + (lmat >> 1));
                 uint32_t gb4[4], qb4[4];
-                ab_ldm4(gb4, gt + (8 * nt + lrow) * AB_LDT + 16 * kk + 8 * lmat);
-                ab_ldm4(qb4, qt + (8 * nt + lrow) * AB_LDT + 16 * kk + 8 * lmat);
+                ab_ldm4t(gb4, gs + at);
+                ab_ldm4t(qb4, qs + at);
                 ab_mma(dv[nt], pa[kk], gb4[0], gb4[1]);
-                ab_mma(dv[nt], pa[kk + 1], gb4[2], gb4[3]);
+                ab_mma(dv[nt + 1], pa[kk], gb4[2], gb4[3]);
                 ab_mma(dk[nt], dsa[kk], qb4[0], qb4[1]);
-                ab_mma(dk[nt], dsa[kk + 1], qb4[2], qb4[3]);
+                ab_mma(dk[nt + 1], dsa[kk], qb4[2], qb4[3]);
             }
         }
     }
