@@ -661,8 +661,9 @@ def learner_step_cfg2_component(device, pre_rows=1024, post_rows=256, reps=3):
                        "sampled presentations, training forward + fused objective + backward + AdamW",
            "ms": ms, "presentations_per_s": rows / (ms / 1e3), "parameters": step.flat.numel,
            "forward_backward_ms_by_family": per_family,
-           "kernels": "linear_tcgen05_kernel, attention_kernel, layernorm, incidence / gelu / layernorm / attention-"
-                      "softmax backward kernels, cuBLAS bf16 GEMMs for dX, dW and the attention-backward products, "
+           "kernels": "linear_tcgen05_kernel, attention_kernel (with log-sum-exp), layernorm, incidence_combine; "
+                      "backward: attention_dq_kernel + attention_dkv_kernel (fused), gelu / layernorm / "
+                      "incidence-combine backward kernels, cuBLAS bf16 GEMMs for the maps' dX and dW; "
                       "learner_objective_kernel, adam"}
     if _reference_pbg() is not None:
         try:
