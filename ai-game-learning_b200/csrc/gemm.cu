@@ -60,7 +60,9 @@ struct GemmArgs {
     const float* row_scale;  // [M] or null
     const float* residual;   // fp32, row m at residual + (m / res_div) * ldr, or null
     int64_t ldr, res_div;
-    int act;                 // 0 none, 1 gelu
+    const __nv_bfloat16* grad;  // act 2: bf16 [M, N] row stride ldg, the gradient of the GELU's output
+    int64_t ldg;
+    int act;                 // 0 none, 1 gelu, 2 GELU backward: grad * GELU'(pre-activation)
     int out_f32;             // 0 bf16, 1 fp32
     uint32_t* error;
 };
@@ -173,6 +175,11 @@ __device__ __forceinline__ float gm_erf(float x) {
 // is absolute: relative to the output it stays below 1e-4 for x >= -3; further out the output is
 // below 1e-5 in magnitude and the deviation below 1e-6.
 __device__ __forceinline__ float gm_gelu(float x) { return 0.5f * x * (1.0f + gm_erf(x * 0.70710678118654752f)); }
+
+// GELU's derivative, erf form: Phi(x) + x phi(x)
+__device__ __forceinline__ float gm_gelu_grad(float x) {
+    return 0.5f * (1.0f + gm_erf(x * 0.70710678118654752f)) + x * 0.39894228040143268f * __expf(-0.5f * x * x);
+}
 
 // activation and bf16 packing of one thread's 32 finished columns (two at a time: few live registers)
 template <int ACT>
@@ -369,6 +376,20 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                         }
                     }
                 }
+                if (G.act == 2) {  // the gradient through the GELU: grad * GELU'(pre-activation); 0 past M
+                    const uint4* g4 = reinterpret_cast<const uint4*>(G.grad + row * G.ldg + col_base + c);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint4 raw = live ? __ldg(g4 + q) : make_uint4(0u, 0u, 0u, 0u);
+                        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 g = __bfloat1622float2(h[e]);
+                            v[8 * q + 2 * e] = g.x * gm_gelu_grad(v[8 * q + 2 * e]);
+                            v[8 * q + 2 * e + 1] = g.y * gm_gelu_grad(v[8 * q + 2 * e + 1]);
+                        }
+                    }
+                }
                 const int y0 = m_blk * GM_BM + quad * 32;
                 const bool gelu = G.act == 1;
                 if (!G.out_f32) {
@@ -451,13 +472,37 @@ using namespace pbg;
 
 extern "C" {
 
+static int linear_launch(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, const void* w,
+                         const float* bias, const float* row_scale, const float* residual, int64_t ldr,
+                         int64_t residual_row_div, const void* grad, int64_t ldg, void* y, int64_t ldy, int32_t y_f32,
+                         int32_t activation, uint32_t* error, void* stream);
+
 int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, const void* w, const float* bias,
                   const float* row_scale, const float* residual, int64_t ldr, int64_t residual_row_div, void* y,
                   int64_t ldy, int32_t y_f32, int32_t activation, uint32_t* error, void* stream) {
+    PBG_REQUIRE(activation == 0 || activation == 1, "linear: activation must be 0 (none) or 1 (gelu)");
+    return linear_launch(M, N, K, x, ldx, w, bias, row_scale, residual, ldr, residual_row_div, nullptr, 0, y, ldy,
+                         y_f32, activation, error, stream);
+}
+
+int pbg_linear_gelu_backward(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, const void* w,
+                             const float* bias, const float* row_scale, const float* residual, int64_t ldr,
+                             int64_t residual_row_div, const void* dy, int64_t ldd, void* out, int64_t ldo,
+                             uint32_t* error, void* stream) {
+    PBG_REQUIRE(dy && ldd >= N && ldd % 8 == 0 && ((uintptr_t)dy % 16) == 0,
+                "linear_gelu_backward: dy must be 16-byte aligned with a row stride >= N and a multiple of 8");
+    return linear_launch(M, N, K, x, ldx, w, bias, row_scale, residual, ldr, residual_row_div, dy, ldd, out, ldo, 0, 2,
+                         error, stream);
+}
+
+static int linear_launch(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, const void* w,
+                         const float* bias, const float* row_scale, const float* residual, int64_t ldr,
+                         int64_t residual_row_div, const void* grad, int64_t ldg, void* y, int64_t ldy, int32_t y_f32,
+                         int32_t activation, uint32_t* error, void* stream) {
     PBG_REQUIRE(M >= 0 && N > 0 && K > 0, "linear: bad shape");
     PBG_REQUIRE(K % GM_BK == 0, "linear: K must be a multiple of %d", GM_BK);
     PBG_REQUIRE(N % 128 == 0, "linear: N must be a multiple of 128");
-    PBG_REQUIRE(activation == 0 || activation == 1, "linear: activation must be 0 (none) or 1 (gelu)");
+    PBG_REQUIRE(activation != 2 || (grad && y_f32 == 0), "linear: the GELU backward takes a gradient, bf16 out");
     PBG_REQUIRE(y_f32 == 0 || y_f32 == 1, "linear: y_f32 must be 0 (bf16) or 1 (fp32)");
     PBG_REQUIRE(x && w && y && error, "linear: null pointer");
     PBG_REQUIRE(ldx >= K && (ldx * 2) % 16 == 0, "linear: x row stride must be >= K and a multiple of 8");
@@ -495,6 +540,8 @@ int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void* x, int64_t ldx, c
     G.residual = residual;
     G.ldr = ldr;
     G.res_div = residual_row_div >= 1 ? residual_row_div : 1;
+    G.grad = static_cast<const __nv_bfloat16*>(grad);
+    G.ldg = ldg;
     G.act = activation;
     G.out_f32 = y_f32;
     G.error = error;

@@ -140,6 +140,8 @@ SIGNATURES: dict[str, tuple] = {
     "pbg_layered_targets": (_I32, [_P, _I32, TargetNodes, TargetChildren, TargetTables, _I32, _I32, _I32, _I32,
                                    _I32, _I32, ctypes.c_float, _I32, _I32, _P, _P, _P]),
     "pbg_linear_bf16": (_I32, [_I64, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
+    "pbg_linear_gelu_backward": (_I32, [_I64, _I32, _I32, _P, _I64, _P, _P, _P, _P, _I64, _I64, _P, _I64, _P, _I64, _P,
+                                        _P]),
     "pbg_linear_ex": (_I32, [_I64, _I32, _I32, _P, _I64, _P, _P, _P, _P, _I64, _I64, _P, _I64, _I32, _I32, _P, _P]),
     "pbg_layernorm_rows": (_I32, [_I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P, ctypes.c_float, _P, _I32, _I64,
                                   _I64, _P]),

@@ -7,15 +7,18 @@ autograd and the optimizer.  Here the forward is the same tensor-core network
 (``PreflopModel`` / ``PostflopModel`` in training mode) with each native step
 wrapped in an autograd function whose backward is written for it:
 
-- ``_LinearFn`` (``pbg_linear_ex``: ``act(x W^T * s + b + r)``): the GELU
-  pre-activation recomputed by the same kernel, its derivative on
-  ``pbg_gelu_backward``, then dX = dY W and dW = dY^T X as bf16 library GEMMs
-  with fp32 accumulation (fp32 dW), the bias and residual gradients as sums;
+- ``_LinearFn`` (``pbg_linear_ex``: ``act(x W^T * s + b + r)``): for a GELU
+  map the same tcgen05 kernel recomputes the pre-activation and writes
+  dY = dy * GELU'(pre) from its epilogue (``pbg_linear_gelu_backward``), then
+  dX = dY W and dW = dY^T X as bf16 library GEMMs with fp32 accumulation (fp32
+  dW), the bias and residual gradients as sums;
 - ``_LayerNormFn`` (``pbg_layernorm``): ``pbg_layernorm_backward``;
 - ``_AttentionFn`` (``pbg_attention_bf16_lse``, which also keeps each row's
   log-sum-exp): ``pbg_attention_backward``, one fused pass that recomputes the
   scores tile by tile on the tensor cores and gives dQ, dK, dV and the gradient
-  of each head's score scale (so of the temperature parameter theta).
+  of each head's score scale (so of the temperature parameter theta);
+- ``_IncidenceCombineFn`` (``pbg_incidence_combine``, the incidence residual's
+  seat sums): ``pbg_incidence_combine_backward``.
 
 The key bias and mask of the attention and the row mass of the incidence map
 come from the learner rows' ranges, not from parameters, and get no gradient.
@@ -36,7 +39,7 @@ from torch import Tensor
 
 from . import _native as N
 from ._native import NativeError, call, ptr, stream
-from .model import attention, linear_ex
+from .model import _error_word, attention, linear_ex
 
 
 def _f32(t: Tensor) -> Tensor:
@@ -64,7 +67,14 @@ class _LinearFn(torch.autograd.Function):
         m = ctx.m
         M, n = x.shape[0], m.n
         dev = x.device
-        if ctx.activation == "gelu":
+        if ctx.activation == "gelu" and m.np_ == n and dy.dtype == torch.bfloat16:
+            # the map recomputed with dy * GELU'(pre-activation) in its epilogue: bf16 out, no fp32 round trip
+            dy = dy.contiguous()
+            dpre = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
+            call("pbg_linear_gelu_backward", M, n, x.shape[1], ptr(x), x.stride(0), ptr(m.weight), ptr(m.bias),
+                 ptr(row_scale), ptr(residual), 0 if residual is None else residual.stride(0), ctx.group, ptr(dy), n,
+                 ptr(dpre), n, ptr(_error_word(dev)), stream(dev))
+        elif ctx.activation == "gelu":
             pre = linear_ex(x, m.weight, m.bias, None, row_scale=row_scale, residual=residual,
                             residual_group=ctx.group, out_dtype=torch.float32)
             dy = dy.contiguous()

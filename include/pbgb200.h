@@ -579,6 +579,14 @@ int pbg_linear_bf16(int64_t M, int32_t N, int32_t K, const void *x, const void *
 int pbg_linear_ex(int64_t M, int32_t N, int32_t K, const void *x, int64_t ldx, const void *w, const float *bias,
                   const float *row_scale, const float *residual, int64_t ldr, int64_t residual_row_div, void *y,
                   int64_t ldy, int32_t y_f32, int32_t activation, uint32_t *error, void *stream);
+/* The gradient through a GELU map of pbg_linear_ex, recomputing its pre-activation on the tensor
+ * cores: out = dy * GELU'(x . w^T * row_scale + bias + residual), bf16 [M, N] (row stride ldo), with dy
+ * bf16 [M, N] (row stride ldd, a multiple of 8; 16-byte aligned).  The other arguments and rules are
+ * pbg_linear_ex's. */
+int pbg_linear_gelu_backward(int64_t M, int32_t N, int32_t K, const void *x, int64_t ldx, const void *w,
+                             const float *bias, const float *row_scale, const float *residual, int64_t ldr,
+                             int64_t residual_row_div, const void *dy, int64_t ldd, void *out, int64_t ldo,
+                             uint32_t *error, void *stream);
 
 /* pbg/games/poker/model/primitives.py:63-283 (MHA, self-attention, heads of
  * width 32): out[b, q, h] = softmax_k((q_h / temperature_h) . k_h / sqrt(32)

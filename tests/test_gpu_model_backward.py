@@ -39,9 +39,13 @@ def _close(got, ref, tol=2e-2):
     assert err <= tol * scale, f"max error {err:.3e} vs scale {scale:.3e}"
 
 
-@pytest.mark.parametrize("activation,group,scaled", [(None, 1, False), ("gelu", 1, False), ("gelu", 4, False),
-                                                     (None, 1, True)])
-def test_linear_backward_matches_torch(activation, group, scaled):
+@pytest.mark.parametrize("activation,group,scaled,out_dtype", [
+    (None, 1, False, torch.float32), ("gelu", 1, False, torch.float32), ("gelu", 4, False, torch.float32),
+    (None, 1, True, torch.float32), ("gelu", 1, False, torch.bfloat16), ("gelu", 4, True, torch.bfloat16)])
+def test_linear_backward_matches_torch(activation, group, scaled, out_dtype):
+    """bf16 outputs of a GELU map take the fused path (pbg_linear_gelu_backward: the pre-activation
+    recomputed with dy * GELU' in the epilogue); fp32 outputs the recompute + pbg_gelu_backward path."""
+
     from pbg_b200.preflop import _Binding, _Map, _padded
 
     g = torch.Generator(device=DEV).manual_seed(3)
@@ -55,9 +59,9 @@ def test_linear_backward_matches_torch(activation, group, scaled):
     binding.training = True
     m = _Map(w, b, DEV, source=lambda: (w, b), binding=binding)
     y = m.apply(_padded(x, m.kp), activation, row_scale=scale, residual=res, residual_group=group,
-                out_dtype=torch.float32)
+                out_dtype=out_dtype)
     c = torch.randn(M, Nn, device=DEV, generator=g)
-    (y * c).sum().backward()
+    (y.float() * c).sum().backward()
     got = [t.grad.clone() for t in (x, w, b, res)]
     for t in (x, w, b, res):
         t.grad = None
@@ -66,7 +70,7 @@ def test_linear_backward_matches_torch(activation, group, scaled):
         pre = pre * scale[:, None]
     pre = pre + b + res.repeat_interleave(group, 0)
     ref = F.gelu(pre) if activation == "gelu" else pre
-    (ref * c).sum().backward()
+    (ref * (c if out_dtype == torch.float32 else _bf(c))).sum().backward()
     for a, t in zip(got, (x, w, b, res)):
         _close(a, t.grad)
 
