@@ -7,7 +7,9 @@
 //
 //   gelu_backward      dpre = dy * (Phi(pre) + pre * phi(pre)) for the exact
 //                      (erf) GELU, bf16 out: the operand of the map's dX / dW
-//                      products
+//                      products (for maps with an fp32 output; a bf16-output
+//                      map gets dpre from its GEMM's epilogue,
+//                      pbg_linear_gelu_backward)
 //   layernorm_backward warp per row: the statistics recomputed from the row,
 //                      dx = inv * (g dy - mean(g dy) - xhat mean(g dy xhat)),
 //                      and per-block column sums of dy * xhat (gain) and dy
@@ -56,21 +58,20 @@ __global__ void __launch_bounds__(LNB_WARPS * 32)
 layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t ldx, const float* __restrict__ gain,
                           float eps, const DY* __restrict__ dy, int64_t ldy, Out* __restrict__ dx, int64_t lddx,
                           float* __restrict__ partial) {
-    constexpr int LNB_MAX_PER_LANE = PER;
     __shared__ float red[LNB_WARPS][2 * 32 * PER];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per = d >> 5;
-    float acc_g[LNB_MAX_PER_LANE], acc_b[LNB_MAX_PER_LANE];
+    float acc_g[PER], acc_b[PER];
     #pragma unroll
-    for (int i = 0; i < LNB_MAX_PER_LANE; ++i) acc_g[i] = acc_b[i] = 0.0f;
+    for (int i = 0; i < PER; ++i) acc_g[i] = acc_b[i] = 0.0f;
     const int64_t warps = (int64_t)gridDim.x * LNB_WARPS;
     for (int64_t r = (int64_t)blockIdx.x * LNB_WARPS + warp; r < rows; r += warps) {
         const In* xr = x + r * ldx;
         const DY* dr = dy + r * ldy;
-        float v[LNB_MAX_PER_LANE], g[LNB_MAX_PER_LANE];
+        float v[PER], g[PER];
         float sum = 0.0f;
         #pragma unroll
-        for (int i = 0; i < LNB_MAX_PER_LANE; ++i) {
+        for (int i = 0; i < PER; ++i) {
             if (i < per) {
                 v[i] = load_f(xr + lane + 32 * i);
                 sum += v[i];
@@ -79,12 +80,12 @@ layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t
         const float mean = warp_sum(sum) / (float)d;
         float sq = 0.0f;
         #pragma unroll
-        for (int i = 0; i < LNB_MAX_PER_LANE; ++i)
+        for (int i = 0; i < PER; ++i)
             if (i < per) sq += (v[i] - mean) * (v[i] - mean);
         const float inv = rsqrtf(warp_sum(sq) / (float)d + eps);
         float s1 = 0.0f, s2 = 0.0f;
         #pragma unroll
-        for (int i = 0; i < LNB_MAX_PER_LANE; ++i) {
+        for (int i = 0; i < PER; ++i) {
             if (i < per) {
                 const int c = lane + 32 * i;
                 const float t = load_f(dr + c);
@@ -101,11 +102,11 @@ layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t
         s2 = warp_sum(s2) / (float)d;
         Out* out = dx + r * lddx;
         #pragma unroll
-        for (int i = 0; i < LNB_MAX_PER_LANE; ++i)
+        for (int i = 0; i < PER; ++i)
             if (i < per) store_f(out + lane + 32 * i, inv * (g[i] - s1 - v[i] * s2));
     }
     #pragma unroll
-    for (int i = 0; i < LNB_MAX_PER_LANE; ++i) {
+    for (int i = 0; i < PER; ++i) {
         if (i < per) {
             red[warp][lane + 32 * i] = acc_g[i];
             red[warp][d + lane + 32 * i] = acc_b[i];
