@@ -134,6 +134,7 @@ layernorm_backward_kernel(int64_t rows, int d, const In* __restrict__ x, int64_t
 constexpr int AB_TILE = 64;
 constexpr int AB_LD = 40;
 constexpr float AB_LOG2E = 1.4426950408889634f;
+constexpr int AB_DKV_BLOCKS = 2;  // 16-key row blocks per warp in the dK/dV kernel
 
 __device__ __forceinline__ void ab_mma(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -359,31 +360,42 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
     }
 }
 
-__global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
+// RB row blocks of 16 keys per warp (4 * 16 * RB keys per CTA): every B fragment read from shared
+// memory feeds RB products, which divides the kernel's shared-memory traffic per pair by RB (it is
+// bound by that traffic); the queries of a tile are taken in two halves of 32 to bound registers
+template <int RB>
+__global__ void __launch_bounds__(128, RB == 1 ? 4 : 2) attention_dkv_kernel(AttnBackArgs A) {
     __shared__ __align__(16) __nv_bfloat16 qs[AB_TILE * AB_LD], gs[AB_TILE * AB_LD];
     __shared__ __align__(8) float lse_s[AB_TILE], delta_s[AB_TILE];
-    const int kblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    constexpr int KEYS = 64 * RB;  // keys per CTA
+    const int kblocks = (A.len + KEYS - 1) / KEYS;
     const int kb = blockIdx.x % kblocks;
     const int h = (blockIdx.x / kblocks) % A.heads;
     const int b = blockIdx.x / (kblocks * A.heads);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int lrow = lane & 7, lmat = lane >> 3;
     const int d = A.heads * 32, width = 3 * d;
-    const int k0 = kb * AB_TILE + 16 * warp;
+    const int k0 = kb * KEYS + 16 * RB * warp;  // row block r: keys k0 + 16 r + {g, g + 8}
     const float scale = A.q_scale[h], scale2 = scale * AB_LOG2E;
     const __nv_bfloat16* seq = A.qkv + (int64_t)b * A.len * width + h * 32;
     const __nv_bfloat16* grad = A.dout + (int64_t)b * A.len * d + h * 32;
-    uint32_t ka[2][4], va[2][4];
-    ab_rows_a(seq + d, width, k0, A.len, g, t, ka);
-    ab_rows_a(seq + 2 * d, width, k0, A.len, g, t, va);
-    const float kt0 = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k0 + g, k0 + g < A.len);
-    const float kt1 = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k0 + g + 8, k0 + g + 8 < A.len);
-    const int64_t row_base = ((int64_t)b * A.heads + h) * A.len;
-    float dk[4][4], dv[4][4];
+    uint32_t ka[RB][2][4], va[RB][2][4];
+    float kt0[RB], kt1[RB];
+    float dk[RB][4][4], dv[RB][4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        dk[i][0] = dk[i][1] = dk[i][2] = dk[i][3] = 0.0f;
-        dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.0f;
+    for (int r = 0; r < RB; ++r) {
+        const int kr = k0 + 16 * r;
+        ab_rows_a(seq + d, width, kr, A.len, g, t, ka[r]);
+        ab_rows_a(seq + 2 * d, width, kr, A.len, g, t, va[r]);
+        kt0[r] = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + kr + g, kr + g < A.len);
+        kt1[r] = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + kr + g + 8, kr + g + 8 < A.len);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            dk[r][i][0] = dk[r][i][1] = dk[r][i][2] = dk[r][i][3] = 0.0f;
+            dv[r][i][0] = dv[r][i][1] = dv[r][i][2] = dv[r][i][3] = 0.0f;
+        }
     }
+    const int64_t row_base = ((int64_t)b * A.heads + h) * A.len;
     const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
     uint4 qv[2], gv[2];
     float lv = INFINITY, dv_ = 0.0f;
@@ -410,67 +422,88 @@ __global__ void __launch_bounds__(128, 4) attention_dkv_kernel(AttnBackArgs A) {
             lv = v ? A.lse[row_base + q1 + threadIdx.x] : INFINITY;
             dv_ = v ? A.delta[row_base + q1 + threadIdx.x] : 0.0f;
         }
-        float s[8][4], dp[8][4];
-        const int lrow = lane & 7, lmat = lane >> 3;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-            dp[nt][0] = dp[nt][1] = dp[nt][2] = dp[nt][3] = 0.0f;
-            uint32_t qb4[4], gb4[4];
-            ab_ldm4(qb4, qs + (8 * nt + lrow) * AB_LD + 8 * lmat);
-            ab_ldm4(gb4, gs + (8 * nt + lrow) * AB_LD + 8 * lmat);
+        for (int half = 0; half < 2; ++half) {  // queries 32 half .. 32 half + 31
+            float s[RB][4][4], dp[RB][4][4];
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                ab_mma(s[nt], ka[k], qb4[2 * k], qb4[2 * k + 1]);
-                ab_mma(dp[nt], va[k], gb4[2 * k], gb4[2 * k + 1]);
+            for (int j = 0; j < 4; ++j) {
+                const int nt = 4 * half + j;
+                uint32_t qb4[4], gb4[4];
+                ab_ldm4(qb4, qs + (8 * nt + lrow) * AB_LD + 8 * lmat);
+                ab_ldm4(gb4, gs + (8 * nt + lrow) * AB_LD + 8 * lmat);
+#pragma unroll
+                for (int r = 0; r < RB; ++r) {
+                    s[r][j][0] = s[r][j][1] = s[r][j][2] = s[r][j][3] = 0.0f;
+                    dp[r][j][0] = dp[r][j][1] = dp[r][j][2] = dp[r][j][3] = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        ab_mma(s[r][j], ka[r][k], qb4[2 * k], qb4[2 * k + 1]);
+                        ab_mma(dp[r][j], va[r][k], gb4[2 * k], gb4[2 * k + 1]);
+                    }
+                }
             }
-        }
-        uint32_t pa[4][4], dsa[4][4];
+            uint32_t pa[RB][2][4], dsa[RB][2][4];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const int c = 8 * nt + 2 * t;
-            const float2 lp = *reinterpret_cast<const float2*>(lse_s + c);
-            const float2 ep = *reinterpret_cast<const float2*>(delta_s + c);
-            const float l0 = lp.x, l1 = lp.y, e0 = ep.x, e1 = ep.y;
-            // rows: keys g (regs 0, 1) and g + 8 (regs 2, 3); columns: queries c, c + 1
-            const float p0 = ab_exp2(fmaf(s[nt][0], scale2, kt0) - l0), p1 = ab_exp2(fmaf(s[nt][1], scale2, kt0) - l1);
-            const float p2 = ab_exp2(fmaf(s[nt][2], scale2, kt1) - l0), p3 = ab_exp2(fmaf(s[nt][3], scale2, kt1) - l1);
-            const float z0 = p0 * (dp[nt][0] - e0), z1 = p1 * (dp[nt][1] - e1);
-            const float z2 = p2 * (dp[nt][2] - e0), z3 = p3 * (dp[nt][3] - e1);
-            pa[nt >> 1][(nt & 1) * 2] = ab_pack(p0, p1);
-            pa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(p2, p3);
-            dsa[nt >> 1][(nt & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
-            dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
-        }
-        // dV += P^T dO and dK += dS^T Q: the k index (queries) runs along the rows of the dO and Q tiles
+            for (int j = 0; j < 4; ++j) {
+                const int c = 8 * (4 * half + j) + 2 * t;
+                const float2 lp = *reinterpret_cast<const float2*>(lse_s + c);
+                const float2 ep = *reinterpret_cast<const float2*>(delta_s + c);
+                const float l0 = lp.x, l1 = lp.y, e0 = ep.x, e1 = ep.y;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+                for (int r = 0; r < RB; ++r) {
+                    // rows: keys g (regs 0, 1) and g + 8 (regs 2, 3) of block r; columns: queries c, c + 1
+                    const float p0 = ab_exp2(fmaf(s[r][j][0], scale2, kt0[r]) - l0);
+                    const float p1 = ab_exp2(fmaf(s[r][j][1], scale2, kt0[r]) - l1);
+                    const float p2 = ab_exp2(fmaf(s[r][j][2], scale2, kt1[r]) - l0);
+                    const float p3 = ab_exp2(fmaf(s[r][j][3], scale2, kt1[r]) - l1);
+                    const float z0 = p0 * (dp[r][j][0] - e0), z1 = p1 * (dp[r][j][1] - e1);
+                    const float z2 = p2 * (dp[r][j][2] - e0), z3 = p3 * (dp[r][j][3] - e1);
+                    pa[r][j >> 1][(j & 1) * 2] = ab_pack(p0, p1);
+                    pa[r][j >> 1][(j & 1) * 2 + 1] = ab_pack(p2, p3);
+                    dsa[r][j >> 1][(j & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
+                    dsa[r][j >> 1][(j & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
+                }
+            }
+            // dV += P^T dO and dK += dS^T Q: the k index (queries) runs along the rows of the dO and Q tiles
 #pragma unroll
-            for (int nt = 0; nt < 4; nt += 2) {
-                const int at = (16 * kk + 8 * (lmat & 1) + lrow) * AB_LD + 8 * (nt + (lmat >> 1));
-                uint32_t gb4[4], qb4[4];
-                ab_ldm4t(gb4, gs + at);
-                ab_ldm4t(qb4, qs + at);
-                ab_mma(dv[nt], pa[kk], gb4[0], gb4[1]);
-                ab_mma(dv[nt + 1], pa[kk], gb4[2], gb4[3]);
-                ab_mma(dk[nt], dsa[kk], qb4[0], qb4[1]);
-                ab_mma(dk[nt + 1], dsa[kk], qb4[2], qb4[3]);
+            for (int kl = 0; kl < 2; ++kl) {
+                const int kk = 2 * half + kl;
+#pragma unroll
+                for (int nt = 0; nt < 4; nt += 2) {
+                    const int at = (16 * kk + 8 * (lmat & 1) + lrow) * AB_LD + 8 * (nt + (lmat >> 1));
+                    uint32_t gb4[4], qb4[4];
+                    ab_ldm4t(gb4, gs + at);
+                    ab_ldm4t(qb4, qs + at);
+#pragma unroll
+                    for (int r = 0; r < RB; ++r) {
+                        ab_mma(dv[r][nt], pa[r][kl], gb4[0], gb4[1]);
+                        ab_mma(dv[r][nt + 1], pa[r][kl], gb4[2], gb4[3]);
+                        ab_mma(dk[r][nt], dsa[r][kl], qb4[0], qb4[1]);
+                        ab_mma(dk[r][nt + 1], dsa[r][kl], qb4[2], qb4[3]);
+                    }
+                }
             }
         }
     }
     __nv_bfloat16* out = A.dqkv + (int64_t)b * A.len * width + h * 32;
-    const bool v0 = k0 + g < A.len, v1 = k0 + g + 8 < A.len;
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-        const int col = 8 * nt + 2 * t;
-        if (v0) {
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g) * width + d + col) = ab_pack(dk[nt][0], dk[nt][1]);
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g) * width + 2 * d + col) = ab_pack(dv[nt][0], dv[nt][1]);
-        }
-        if (v1) {
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g + 8) * width + d + col) = ab_pack(dk[nt][2], dk[nt][3]);
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(k0 + g + 8) * width + 2 * d + col) =
-                ab_pack(dv[nt][2], dv[nt][3]);
+    for (int r = 0; r < RB; ++r) {
+        const int kr = k0 + 16 * r;
+        const bool v0 = kr + g < A.len, v1 = kr + g + 8 < A.len;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            const int col = 8 * nt + 2 * t;
+            if (v0) {
+                *reinterpret_cast<uint32_t*>(out + (int64_t)(kr + g) * width + d + col) = ab_pack(dk[r][nt][0], dk[r][nt][1]);
+                *reinterpret_cast<uint32_t*>(out + (int64_t)(kr + g) * width + 2 * d + col) =
+                    ab_pack(dv[r][nt][0], dv[r][nt][1]);
+            }
+            if (v1) {
+                *reinterpret_cast<uint32_t*>(out + (int64_t)(kr + g + 8) * width + d + col) =
+                    ab_pack(dk[r][nt][2], dk[r][nt][3]);
+                *reinterpret_cast<uint32_t*>(out + (int64_t)(kr + g + 8) * width + 2 * d + col) =
+                    ab_pack(dv[r][nt][2], dv[r][nt][3]);
+            }
         }
     }
 }
@@ -584,7 +617,8 @@ int pbg_attention_backward(int32_t batch, int32_t len, int32_t heads, const void
     attention_dq_kernel<<<(unsigned)grid, 128, 0, s>>>(A);
     err = launch_status("attention_backward: dq");
     if (err) return err;
-    attention_dkv_kernel<<<(unsigned)grid, 128, 0, s>>>(A);
+    const int64_t grid_kv = (int64_t)batch * heads * ((len + 64 * AB_DKV_BLOCKS - 1) / (64 * AB_DKV_BLOCKS));
+    attention_dkv_kernel<AB_DKV_BLOCKS><<<(unsigned)grid_kv, 128, 0, s>>>(A);
     return launch_status("attention_backward: dk dv");
 }
 
