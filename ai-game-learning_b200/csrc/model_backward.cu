@@ -135,6 +135,7 @@ constexpr int AB_TILE = 64;
 constexpr int AB_LD = 40;
 constexpr float AB_LOG2E = 1.4426950408889634f;
 constexpr int AB_DKV_BLOCKS = 2;  // 16-key row blocks per warp in the dK/dV kernel
+constexpr int AB_DQ_BLOCKS = 2;   // 16-query row blocks per warp in the dQ kernel
 
 __device__ __forceinline__ void ab_mma(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -257,29 +258,41 @@ __global__ void __launch_bounds__(128) attention_delta_kernel(int64_t rows, int 
     }
 }
 
-__global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
+// RB row blocks of 16 queries per warp (4 * 16 * RB queries per CTA), as in the dK/dV kernel: every
+// K / V fragment read from shared memory feeds RB products; keys taken in two halves of 32
+template <int RB>
+__global__ void __launch_bounds__(128, RB == 1 ? 4 : 2) attention_dq_kernel(AttnBackArgs A) {
     __shared__ __align__(16) __nv_bfloat16 ks[AB_TILE * AB_LD], vs[AB_TILE * AB_LD];
     __shared__ __align__(8) float kterm[AB_TILE];
-    const int qblocks = (A.len + AB_TILE - 1) / AB_TILE;
+    constexpr int QUERIES = 64 * RB;  // queries per CTA
+    const int qblocks = (A.len + QUERIES - 1) / QUERIES;
     const int qb = blockIdx.x % qblocks;
     const int h = (blockIdx.x / qblocks) % A.heads;
     const int b = blockIdx.x / (qblocks * A.heads);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int lrow = lane & 7, lmat = lane >> 3;
     const int d = A.heads * 32, width = 3 * d;
-    const int q0 = qb * AB_TILE + 16 * warp;
+    const int q0 = qb * QUERIES + 16 * RB * warp;  // row block r: queries q0 + 16 r + {g, g + 8}
     const float scale = A.q_scale[h], scale2 = scale * AB_LOG2E;
     const __nv_bfloat16* seq = A.qkv + (int64_t)b * A.len * width + h * 32;
-    uint32_t qa[2][4], da[2][4];
-    ab_rows_a(seq, width, q0, A.len, g, t, qa);
-    ab_rows_a(A.dout + (int64_t)b * A.len * d + h * 32, d, q0, A.len, g, t, da);
     const int64_t row_base = ((int64_t)b * A.heads + h) * A.len;
-    const bool v0 = q0 + g < A.len, v1 = q0 + g + 8 < A.len;
-    const float lse0 = v0 ? A.lse[row_base + q0 + g] : INFINITY, lse1 = v1 ? A.lse[row_base + q0 + g + 8] : INFINITY;
-    const float dl0 = v0 ? A.delta[row_base + q0 + g] : 0.0f, dl1 = v1 ? A.delta[row_base + q0 + g + 8] : 0.0f;
-    float dq[4][4];
+    uint32_t qa[RB][2][4], da[RB][2][4];
+    float lse0[RB], lse1[RB], dl0[RB], dl1[RB], th0[RB], th1[RB];
+    float dq[RB][4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.0f;
-    float th0 = 0.0f, th1 = 0.0f;
+    for (int r = 0; r < RB; ++r) {
+        const int qr = q0 + 16 * r;
+        ab_rows_a(seq, width, qr, A.len, g, t, qa[r]);
+        ab_rows_a(A.dout + (int64_t)b * A.len * d + h * 32, d, qr, A.len, g, t, da[r]);
+        const bool v0 = qr + g < A.len, v1 = qr + g + 8 < A.len;
+        lse0[r] = v0 ? A.lse[row_base + qr + g] : INFINITY;
+        lse1[r] = v1 ? A.lse[row_base + qr + g + 8] : INFINITY;
+        dl0[r] = v0 ? A.delta[row_base + qr + g] : 0.0f;
+        dl1[r] = v1 ? A.delta[row_base + qr + g + 8] : 0.0f;
+        th0[r] = th1[r] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dq[r][i][0] = dq[r][i][1] = dq[r][i][2] = dq[r][i][3] = 0.0f;
+    }
     const int kblocks = (A.len + AB_TILE - 1) / AB_TILE;
     uint4 kv[2], vv[2];
     float term = 0.0f;
@@ -301,62 +314,86 @@ __global__ void __launch_bounds__(128, 4) attention_dq_kernel(AttnBackArgs A) {
                 term = ab_key_term(A.key_bias, A.key_mask, (int64_t)b * A.len + k1 + threadIdx.x,
                                    k1 + (int)threadIdx.x < A.len);
         }
-        float s[8][4], dp[8][4];
-        const int lrow = lane & 7, lmat = lane >> 3;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-            dp[nt][0] = dp[nt][1] = dp[nt][2] = dp[nt][3] = 0.0f;
-            uint32_t kb4[4], vb4[4];
-            ab_ldm4(kb4, ks + (8 * nt + lrow) * AB_LD + 8 * lmat);
-            ab_ldm4(vb4, vs + (8 * nt + lrow) * AB_LD + 8 * lmat);
+        for (int half = 0; half < 2; ++half) {  // keys 32 half .. 32 half + 31 of the block
+            float s[RB][4][4], dp[RB][4][4];
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                ab_mma(s[nt], qa[k], kb4[2 * k], kb4[2 * k + 1]);
-                ab_mma(dp[nt], da[k], vb4[2 * k], vb4[2 * k + 1]);
+            for (int j = 0; j < 4; ++j) {
+                const int nt = 4 * half + j;
+                uint32_t kb4[4], vb4[4];
+                ab_ldm4(kb4, ks + (8 * nt + lrow) * AB_LD + 8 * lmat);
+                ab_ldm4(vb4, vs + (8 * nt + lrow) * AB_LD + 8 * lmat);
+#pragma unroll
+                for (int r = 0; r < RB; ++r) {
+                    s[r][j][0] = s[r][j][1] = s[r][j][2] = s[r][j][3] = 0.0f;
+                    dp[r][j][0] = dp[r][j][1] = dp[r][j][2] = dp[r][j][3] = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        ab_mma(s[r][j], qa[r][k], kb4[2 * k], kb4[2 * k + 1]);
+                        ab_mma(dp[r][j], da[r][k], vb4[2 * k], vb4[2 * k + 1]);
+                    }
+                }
             }
-        }
-        uint32_t dsa[4][4];
+            uint32_t dsa[RB][2][4];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const float2 tp = *reinterpret_cast<const float2*>(kterm + 8 * nt + 2 * t);
-            const float t0 = tp.x, t1 = tp.y;
-            const float p0 = ab_exp2(fmaf(s[nt][0], scale2, t0) - lse0), p1 = ab_exp2(fmaf(s[nt][1], scale2, t1) - lse0);
-            const float p2 = ab_exp2(fmaf(s[nt][2], scale2, t0) - lse1), p3 = ab_exp2(fmaf(s[nt][3], scale2, t1) - lse1);
-            const float z0 = p0 * (dp[nt][0] - dl0), z1 = p1 * (dp[nt][1] - dl0);
-            const float z2 = p2 * (dp[nt][2] - dl1), z3 = p3 * (dp[nt][3] - dl1);
-            th0 += z0 * s[nt][0] + z1 * s[nt][1];
-            th1 += z2 * s[nt][2] + z3 * s[nt][3];
-            // C fragment of n-tile nt -> half of the A fragment of key step nt / 2
-            dsa[nt >> 1][(nt & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
-            dsa[nt >> 1][(nt & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
-        }
-        // dQ += dS K: the k index (keys) runs along the rows of the K tile
+            for (int j = 0; j < 4; ++j) {
+                const float2 tp = *reinterpret_cast<const float2*>(kterm + 8 * (4 * half + j) + 2 * t);
+                const float t0 = tp.x, t1 = tp.y;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+                for (int r = 0; r < RB; ++r) {
+                    const float p0 = ab_exp2(fmaf(s[r][j][0], scale2, t0) - lse0[r]);
+                    const float p1 = ab_exp2(fmaf(s[r][j][1], scale2, t1) - lse0[r]);
+                    const float p2 = ab_exp2(fmaf(s[r][j][2], scale2, t0) - lse1[r]);
+                    const float p3 = ab_exp2(fmaf(s[r][j][3], scale2, t1) - lse1[r]);
+                    const float z0 = p0 * (dp[r][j][0] - dl0[r]), z1 = p1 * (dp[r][j][1] - dl0[r]);
+                    const float z2 = p2 * (dp[r][j][2] - dl1[r]), z3 = p3 * (dp[r][j][3] - dl1[r]);
+                    th0[r] += z0 * s[r][j][0] + z1 * s[r][j][1];
+                    th1[r] += z2 * s[r][j][2] + z3 * s[r][j][3];
+                    // C fragment of n-tile j -> half of the A fragment of key step j / 2
+                    dsa[r][j >> 1][(j & 1) * 2] = ab_pack(z0 * scale, z1 * scale);
+                    dsa[r][j >> 1][(j & 1) * 2 + 1] = ab_pack(z2 * scale, z3 * scale);
+                }
+            }
+            // dQ += dS K: the k index (keys) runs along the rows of the K tile
 #pragma unroll
-            for (int nt = 0; nt < 4; nt += 2) {
-                uint32_t b4[4];
-                ab_ldm4t(b4, ks + (16 * kk + 8 * (lmat & 1) + lrow) * AB_LD + 8 * (nt + (lmat >> 1)));
-                ab_mma(dq[nt], dsa[kk], b4[0], b4[1]);
-                ab_mma(dq[nt + 1], dsa[kk], b4[2], b4[3]);
+            for (int kl = 0; kl < 2; ++kl) {
+                const int kk = 2 * half + kl;
+#pragma unroll
+                for (int nt = 0; nt < 4; nt += 2) {
+                    uint32_t b4[4];
+                    ab_ldm4t(b4, ks + (16 * kk + 8 * (lmat & 1) + lrow) * AB_LD + 8 * (nt + (lmat >> 1)));
+#pragma unroll
+                    for (int r = 0; r < RB; ++r) {
+                        ab_mma(dq[r][nt], dsa[r][kl], b4[0], b4[1]);
+                        ab_mma(dq[r][nt + 1], dsa[r][kl], b4[2], b4[3]);
+                    }
+                }
             }
         }
     }
-    th0 += __shfl_xor_sync(0xffffffffu, th0, 1);
-    th0 += __shfl_xor_sync(0xffffffffu, th0, 2);
-    th1 += __shfl_xor_sync(0xffffffffu, th1, 1);
-    th1 += __shfl_xor_sync(0xffffffffu, th1, 2);
     __nv_bfloat16* out = A.dqkv + (int64_t)b * A.len * width + h * 32;
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-        if (v0) *reinterpret_cast<uint32_t*>(out + (int64_t)(q0 + g) * width + 8 * nt + 2 * t) = ab_pack(dq[nt][0], dq[nt][1]);
-        if (v1)
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(q0 + g + 8) * width + 8 * nt + 2 * t) = ab_pack(dq[nt][2], dq[nt][3]);
-    }
-    if (t == 0) {
-        if (v0) A.scale_partial[row_base + q0 + g] = th0;
-        if (v1) A.scale_partial[row_base + q0 + g + 8] = th1;
+    for (int r = 0; r < RB; ++r) {
+        float a = th0[r], c = th1[r];
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        c += __shfl_xor_sync(0xffffffffu, c, 1);
+        c += __shfl_xor_sync(0xffffffffu, c, 2);
+        const int qr = q0 + 16 * r;
+        const bool v0 = qr + g < A.len, v1 = qr + g + 8 < A.len;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            if (v0)
+                *reinterpret_cast<uint32_t*>(out + (int64_t)(qr + g) * width + 8 * nt + 2 * t) =
+                    ab_pack(dq[r][nt][0], dq[r][nt][1]);
+            if (v1)
+                *reinterpret_cast<uint32_t*>(out + (int64_t)(qr + g + 8) * width + 8 * nt + 2 * t) =
+                    ab_pack(dq[r][nt][2], dq[r][nt][3]);
+        }
+        if (t == 0) {
+            if (v0) A.scale_partial[row_base + qr + g] = a;
+            if (v1) A.scale_partial[row_base + qr + g + 8] = c;
+        }
     }
 }
 
@@ -614,7 +651,8 @@ int pbg_attention_backward(int32_t batch, int32_t len, int32_t heads, const void
     A.scale_partial = scale_partial;
     const int64_t grid = (int64_t)batch * heads * ((len + AB_TILE - 1) / AB_TILE);
     PBG_REQUIRE(grid <= INT32_MAX, "attention_backward: too many blocks");
-    attention_dq_kernel<<<(unsigned)grid, 128, 0, s>>>(A);
+    const int64_t grid_q = (int64_t)batch * heads * ((len + 64 * AB_DQ_BLOCKS - 1) / (64 * AB_DQ_BLOCKS));
+    attention_dq_kernel<AB_DQ_BLOCKS><<<(unsigned)grid_q, 128, 0, s>>>(A);
     err = launch_status("attention_backward: dq");
     if (err) return err;
     const int64_t grid_kv = (int64_t)batch * heads * ((len + 64 * AB_DKV_BLOCKS - 1) / (64 * AB_DKV_BLOCKS));
