@@ -292,8 +292,10 @@ class ModelLearnerStep:
         self.objective = PokerLearnerObjective(self.flat.master.device)
 
     def gradient(self, batches: list) -> list:
-        """Forward, objective and backward of every batch; the flat gradient lands in ``self.adam.grad``."""
+        """Forward, objective and backward of every batch; the flat gradient lands in ``self.adam.grad``,
+        cleared first (the AdamW transition leaves the clipped gradient there, and autograd adds into it)."""
 
+        self.adam.grad.zero_()
         results = []
         for b in batches:
             evaluation = self.model.learner_operation(b["input_type"], b["model_input"], b["sampled_private_state"],

@@ -321,3 +321,10 @@ def test_model_learner_step_accumulates_families_and_steps(gold):
     torch.cuda.synchronize()
     assert bool(torch.isfinite(report).all())
     assert float((step.flat.master - before).abs().max()) > 0
+    # each step's gradient starts from zero: the transition leaves the clipped gradient in the buffer
+    step.adam.step()
+    first = step.gradient([pre])
+    g1 = step.adam.grad.clone()
+    step.gradient([pre])
+    torch.testing.assert_close(step.adam.grad, g1, rtol=1e-5, atol=1e-7 * float(g1.abs().max()))
+    assert all(bool(torch.isfinite(r.total).all()) for r in first)
