@@ -12,6 +12,11 @@ inputs with GELU in its epilogue.  The residual stream stays fp32; the
 token assembly (embeddings, the 1- and 6-wide affine maps of the scalars),
 the incidence mass reductions (fp32 batched GEMMs, as the reference keeps
 them) and the small elementwise steps are torch operations on the device.
+
+In training mode (``FamilyModel.train()``, after ``bind_parameters`` with leaf
+tensors) the same forward runs with every native step as an autograd function
+of ``pbg_b200.model_train`` (the learner step's backward); embedding rows are
+then one-hot products (``lookup``) so that their gradients are GEMMs.
 """
 
 from __future__ import annotations
